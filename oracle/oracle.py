@@ -1,0 +1,243 @@
+"""ctypes view of the CPU oracle (libmsoracle.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, ``__graft_entry__.smoke()`` and the
+``cpu_baseline`` / ``--impl reference`` legs of bench.py, as the checker or the
+timed CPU restatement of the reference.  The product never imports it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libmsoracle.so")
+_lib = None
+
+F32, F16, Q8_0, Q4_K, Q6_K, MXFP4 = 0, 1, 8, 12, 14, 39
+
+_fp = C.POINTER(C.c_float)
+_i32p = C.POINTER(C.c_int32)
+_vp = C.c_void_p
+
+
+class MoeLayer(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("inter", C.c_int), ("n_experts", C.c_int), ("top_k", C.c_int),
+                ("gate_q", C.c_int), ("up_q", C.c_int), ("down_q", C.c_int),
+                ("gate", _vp), ("up", _vp), ("down", _vp),
+                ("gate_bias", _fp), ("up_bias", _fp), ("down_bias", _fp),
+                ("router_w", _fp), ("router_b", _fp),
+                ("oai_swiglu", C.c_int), ("norm_topk_prob", C.c_int)]
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (g++ only; no reference sources involved)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = C.CDLL(_LIB_PATH)
+        L.orc_fp16_to_f32.restype = C.c_float
+        L.orc_fp16_to_f32.argtypes = [C.c_uint16]
+        L.orc_e8m0_to_f32_half.restype = C.c_float
+        L.orc_e8m0_to_f32_half.argtypes = [C.c_uint8]
+        L.orc_dequantize.argtypes = [C.c_int, _vp, C.c_int64, _fp]
+        L.orc_mxfp4_matvec_mul.argtypes = [_vp, _fp, C.c_int64, C.c_int64, _fp]
+        L.orc_gemv.argtypes = [C.c_int, _vp, C.c_int64, C.c_int64, _fp, _fp]
+        L.orc_q8_0_gemv.argtypes = [_vp, C.c_int64, C.c_int64, _fp, _fp, C.c_int]
+        L.orc_quantize_q8_0.argtypes = [_fp, C.c_int64, _vp]
+        L.orc_rms_norm.argtypes = [_fp, _fp, _fp, C.c_int64, C.c_int64, C.c_float]
+        L.orc_rope_tables.argtypes = [C.c_int, C.c_int, C.c_double, _fp, _fp]
+        L.orc_swiglu_oai.argtypes = [_fp, _fp, _fp, C.c_int64, C.c_float, C.c_float]
+        L.orc_silu_and_mul.argtypes = [_fp, _fp, _fp, C.c_int64]
+        L.orc_top_k_routing.argtypes = [_fp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _i32p, _fp]
+        L.orc_moe_forward.argtypes = [C.POINTER(MoeLayer), _fp, C.c_int, _fp, _i32p, _fp]
+        L.orc_model_open.restype = _vp
+        L.orc_model_open.argtypes = [C.c_char_p, C.c_int, C.c_char_p, C.c_int]
+        L.orc_model_set_attn_mode.argtypes = [_vp, C.c_int]
+        L.orc_model_set_threads.argtypes = [_vp, C.c_int]
+        L.orc_model_forward.argtypes = [_vp, _i32p, C.c_int, _fp]
+        L.orc_model_generate.argtypes = [_vp, _i32p, C.c_int, C.c_int, _i32p]
+        L.orc_model_vocab.argtypes = [_vp]
+        L.orc_model_hidden.argtypes = [_vp]
+        L.orc_model_seq_len.argtypes = [_vp]
+        L.orc_model_clear_cache.argtypes = [_vp]
+        L.orc_model_last_hidden.argtypes = [_vp, _fp]
+        L.orc_model_last_routing.argtypes = [_vp, _i32p, _fp]
+        L.orc_model_destroy.argtypes = [_vp]
+        _lib = L
+    return _lib
+
+
+def _f(a: np.ndarray):
+    return a.ctypes.data_as(_fp)
+
+
+def _i(a: np.ndarray):
+    return a.ctypes.data_as(_i32p)
+
+
+def dequantize(qtype: int, blocks: np.ndarray, n: int) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    b = np.ascontiguousarray(blocks)
+    if lib().orc_dequantize(qtype, b.ctypes.data, n, _f(out)) != 0:
+        raise ValueError(f"unsupported qtype {qtype}")
+    return out
+
+
+def gemv(qtype: int, w: np.ndarray, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
+    y = np.empty(rows, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w)
+    lib().orc_gemv(qtype, w.ctypes.data, rows, cols, _f(x), _f(y))
+    return y
+
+
+def mxfp4_matvec_mul(w: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    y = np.empty(rows, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w)
+    lib().orc_mxfp4_matvec_mul(w.ctypes.data, _f(x), rows, cols, _f(y))
+    return y
+
+
+def q8_0_gemv(w: np.ndarray, rows: int, cols: int, x: np.ndarray, mode: int = 1) -> np.ndarray:
+    y = np.empty(rows, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w)
+    lib().orc_q8_0_gemv(w.ctypes.data, rows, cols, _f(x), _f(y), mode)
+    return y
+
+
+def quantize_q8_0(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.size // 32 * 34, dtype=np.uint8)
+    lib().orc_quantize_q8_0(_f(x), x.size, out.ctypes.data)
+    return out
+
+
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    y = np.empty_like(x)
+    dim = x.shape[-1]
+    lib().orc_rms_norm(_f(x), _f(w), _f(y), x.size // dim, dim, eps)
+    return y
+
+
+def rope_tables(rot_dim: int, max_seq: int, theta: float):
+    c = np.empty((max_seq, rot_dim // 2), dtype=np.float32)
+    s = np.empty_like(c)
+    lib().orc_rope_tables(rot_dim, max_seq, theta, _f(c), _f(s))
+    return c, s
+
+
+def swiglu_oai(g, u, alpha=1.702, limit=7.0):
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    u = np.ascontiguousarray(u, dtype=np.float32)
+    o = np.empty_like(g)
+    lib().orc_swiglu_oai(_f(g), _f(u), _f(o), g.size, alpha, limit)
+    return o
+
+
+def silu_and_mul(g, u):
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    u = np.ascontiguousarray(u, dtype=np.float32)
+    o = np.empty_like(g)
+    lib().orc_silu_and_mul(_f(g), _f(u), _f(o), g.size)
+    return o
+
+
+def top_k_routing(logits: np.ndarray, k: int, normalize: bool, softmax_weight: bool):
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    if logits.ndim == 1:
+        logits = logits[None]
+    n, e = logits.shape
+    idx = np.empty((n, k), dtype=np.int32)
+    w = np.empty((n, k), dtype=np.float32)
+    lib().orc_top_k_routing(_f(logits), n, e, k, int(normalize), int(softmax_weight), _i(idx), _f(w))
+    return idx, w
+
+
+def moe_forward(layer: dict, x: np.ndarray):
+    """One MoE FFN layer on the default CPU path.  ``layer`` holds numpy arrays:
+    gate/up/down (raw stacked blocks), *_bias, router_w, router_b, and ints."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n_tok = x.size // layer["hidden"]
+    keep = []
+
+    def ptr(a, fp=False):
+        if a is None:
+            return None if not fp else _fp()
+        a = np.ascontiguousarray(a)
+        keep.append(a)
+        return a.ctypes.data_as(_fp) if fp else a.ctypes.data
+
+    L = MoeLayer(layer["hidden"], layer["inter"], layer["n_experts"], layer["top_k"],
+                 layer["gate_q"], layer["up_q"], layer["down_q"],
+                 ptr(layer["gate"]), ptr(layer["up"]), ptr(layer["down"]),
+                 ptr(layer.get("gate_bias"), True), ptr(layer.get("up_bias"), True),
+                 ptr(layer.get("down_bias"), True), ptr(layer["router_w"], True),
+                 ptr(layer.get("router_b"), True), int(layer["oai_swiglu"]), int(layer["norm_topk_prob"]))
+    out = np.empty((n_tok, layer["hidden"]), dtype=np.float32)
+    idx = np.empty((n_tok, layer["top_k"]), dtype=np.int32)
+    w = np.empty((n_tok, layer["top_k"]), dtype=np.float32)
+    lib().orc_moe_forward(C.byref(L), _f(x), n_tok, _f(out), _i(idx), _f(w))
+    return out, idx, w
+
+
+class Model:
+    """Whole-model oracle over a GGUF file (engine.rs forward/generate)."""
+
+    def __init__(self, path: str, max_seq_len: int = 4096, attn_mode: int = 1, threads: int = 0):
+        err = C.create_string_buffer(512)
+        self.h = lib().orc_model_open(path.encode(), max_seq_len, err, 512)
+        if not self.h:
+            raise RuntimeError(err.value.decode())
+        lib().orc_model_set_attn_mode(self.h, attn_mode)
+        if threads:
+            lib().orc_model_set_threads(self.h, threads)
+        self.vocab = lib().orc_model_vocab(self.h)
+        self.hidden = lib().orc_model_hidden(self.h)
+
+    def forward(self, tokens) -> np.ndarray:
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        logits = np.empty(self.vocab, dtype=np.float32)
+        rc = lib().orc_model_forward(self.h, _i(t), t.size, _f(logits))
+        if rc != 0:
+            raise RuntimeError(f"oracle forward failed ({rc})")
+        return logits
+
+    def generate(self, prompt, max_new: int) -> np.ndarray:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(max_new, dtype=np.int32)
+        n = lib().orc_model_generate(self.h, _i(p), p.size, max_new, _i(out))
+        if n < 0:
+            raise RuntimeError("oracle generate failed")
+        return out[:n]
+
+    def last_hidden(self) -> np.ndarray:
+        o = np.empty(self.hidden, dtype=np.float32)
+        lib().orc_model_last_hidden(self.h, _f(o))
+        return o
+
+    def clear_cache(self):
+        lib().orc_model_clear_cache(self.h)
+
+    def close(self):
+        if self.h:
+            lib().orc_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
