@@ -1,0 +1,176 @@
+/*
+ * moestream_cuda.h — C ABI of the moe-stream B200 (sm_100a) backend.
+ *
+ * This library replaces the Metal compute backend of moe-stream-core for the quantized
+ * MoE decode step.  Each entry point names the reference function or call site it stands
+ * in for (paths relative to the moe-stream repository, moe-stream-core/src/...).  All
+ * arguments are plain pointers and sizes; "d_" pointers are device memory (allocate them
+ * with ms_malloc or any CUDA allocator on the context's device), other pointers are host
+ * memory.  Every call returns an ms_status; no C++ exception crosses this boundary.  A
+ * context is not thread-safe: use it from one host thread, as the reference Engine is used
+ * from its single engine thread (moe-stream-server/src/engine_handle.rs:88-93).
+ */
+#ifndef MOESTREAM_CUDA_H
+#define MOESTREAM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MS_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define MS_API __attribute__((visibility("default")))
+#else
+#define MS_API
+#endif
+
+/* Status codes (the Rust shim maps them to candle_core::Error::Msg with ms_last_error()). */
+typedef enum ms_status {
+  MS_OK = 0,
+  MS_ERR_INVALID_ARG = 1,
+  MS_ERR_OOM = 2,
+  MS_ERR_CUDA = 3,
+  MS_ERR_NCCL = 4,
+  MS_ERR_TIMEOUT = 5,          /* a device-side bounded wait expired (see ms_ctx_error_flags) */
+  MS_ERR_UNSUPPORTED_QTYPE = 6,
+  MS_ERR_SHAPE = 7,
+  MS_ERR_IO = 8,
+  MS_ERR_FORMAT = 9,           /* malformed GGUF */
+  MS_ERR_STATE = 10,           /* call out of order (e.g. step before finalize) */
+  MS_ERR_DEVICE_INDEX = 11     /* a token / expert index outside its table was seen on the device */
+} ms_status;
+
+/* GGML tensor type ids, as gguf/reader.rs:38-65 (GgmlQuantType). */
+typedef enum ms_qtype {
+  MS_Q_F32 = 0,
+  MS_Q_F16 = 1,
+  MS_Q_Q8_0 = 8,
+  MS_Q_Q4_K = 12,
+  MS_Q_Q6_K = 14,
+  MS_Q_MXFP4 = 39
+} ms_qtype;
+
+/* Architecture switches the reference derives from general.architecture (layer.rs:774). */
+typedef enum ms_arch {
+  MS_ARCH_GPT_OSS = 0,   /* OAI SwiGLU (clamp 7, alpha 1.702), softmax over the selected top-k */
+  MS_ARCH_QWEN_MOE = 1   /* SiLU*up, softmax over all experts then top-k (+renormalise) */
+} ms_arch;
+
+typedef struct ms_ctx ms_ctx;
+typedef struct ms_model ms_model;
+
+MS_API int ms_abi_version(void);
+MS_API const char* ms_status_string(ms_status s);
+
+/* ---- context (replaces Device::new_metal, engine.rs:277-298) ---- */
+MS_API ms_status ms_ctx_create(int device, ms_ctx** out);
+MS_API ms_status ms_ctx_destroy(ms_ctx* ctx);
+/* Enqueue work on a caller-owned cudaStream_t (NULL restores the context's own stream). */
+MS_API ms_status ms_ctx_set_stream(ms_ctx* ctx, void* cuda_stream);
+/* Wait for the stream; reports MS_ERR_TIMEOUT / MS_ERR_DEVICE_INDEX raised by device code. */
+MS_API ms_status ms_sync(ms_ctx* ctx);
+MS_API const char* ms_last_error(const ms_ctx* ctx);
+/* Device error word (bit 0/1: wait timeouts, bit 2: bad index, bit 3: bad shape); clear if nonzero. */
+MS_API ms_status ms_ctx_error_flags(ms_ctx* ctx, uint32_t* flags, int clear);
+MS_API int ms_ctx_sm_count(const ms_ctx* ctx);
+
+/* ---- device memory (so an FFI caller needs no CUDA runtime of its own) ---- */
+MS_API ms_status ms_malloc(ms_ctx* ctx, size_t bytes, void** d_ptr);
+MS_API ms_status ms_free(ms_ctx* ctx, void* d_ptr);
+MS_API ms_status ms_memcpy_h2d(ms_ctx* ctx, void* d_dst, const void* src, size_t bytes);   /* synchronous */
+MS_API ms_status ms_memcpy_d2h(ms_ctx* ctx, void* dst, const void* d_src, size_t bytes);   /* synchronous */
+
+/* ---- kernels on device pointers (the metal/mod.rs seam, one entry per dispatch) ---- */
+
+/* Block dequantization to f32, bit-exact with gguf/dequant.rs (dequantize_mxfp4 605-628,
+ * dequantize_q4k 218-262, dequantize_q6k 335-378, dequantize_q80 511-531, f16 37-41). */
+MS_API ms_status ms_dequantize(ms_ctx* ctx, int qtype, const void* d_blocks, int64_t n_elements, float* d_out);
+
+/* y = x * rsqrt(mean(x^2) + eps) * w per row; replaces fused_rms_norm_metal (metal/mod.rs:290-371). */
+MS_API ms_status ms_rms_norm(ms_ctx* ctx, const float* d_x, const float* d_w, float* d_y, int rows, int dim, float eps);
+
+/* y = W x (+bias) for one token, W [rows, cols] in native blocks.  Replaces
+ * mxfp4_matmul_metal_gpu (metal/mod.rs:896-962) for MXFP4 (W allocation padded to 16 rows),
+ * quantized_attn_matmul_metal_gpu_batched (metal/mod.rs:1123-1141) for Q8_0 (activation quantized
+ * to Q8_0 as the CPU QMatMul path does), and the dense f16/f32 matmuls. */
+MS_API ms_status ms_gemv(ms_ctx* ctx, int qtype, const void* d_w, int rows, int cols, const float* d_x,
+                  const float* d_bias, float* d_y);
+
+/* RMSNorm + router GEMV + bias + dummy-expert mask + top-k + routing weights for one token.
+ * Replaces softmax_topk_kernel's dispatch (metal/mod.rs:1560-1602) and layer.rs:806-837,
+ * 1016-1027, 2346-2403.  d_mask may be NULL (1 = dummy expert).  Ties pick the lower index. */
+MS_API ms_status ms_router_topk(ms_ctx* ctx, const float* d_h, const float* d_norm_w, float eps, const float* d_router_w,
+                         const float* d_router_b, const uint8_t* d_mask, int hidden, int n_experts, int top_k,
+                         int arch, int norm_topk_prob, float* d_xn, float* d_logits, int32_t* d_idx, float* d_wts);
+
+/* One-token MXFP4 expert FFN with weighted combine into the residual stream:
+ * d_h += sum over selected experts e (ascending id) of w_e * (Wd_e act_e + bd_e),
+ * act_e = SwiGLU(Wg_e x + bg_e, Wu_e x + bu_e).  Replaces gpu_routed_moe_forward_metal
+ * (metal/mod.rs:1512-1677: mxfp4_fused_gate_up_swiglu_f32 + mxfp4_fused_down_accum_f32).
+ * Weights are the stacked GGUF tensors blk.N.ffn_{gate,up,down}_exps in native layout;
+ * biases may be NULL.  Uses device scratch owned by the context. */
+MS_API ms_status ms_moe_mxfp4_decode(ms_ctx* ctx, const void* d_gate, const void* d_up, const void* d_down,
+                              const float* d_gate_b, const float* d_up_b, const float* d_down_b, int hidden,
+                              int inter, int n_experts, int top_k, int arch, const float* d_x, const int32_t* d_idx,
+                              const float* d_wts, float* d_h);
+
+/* ---- model: the Engine surface (engine.rs open_with_device / preload_weights / forward /
+ *      generate / clear_cache) ---- */
+typedef struct ms_model_config {
+  int arch;             /* ms_arch */
+  int hidden, layers, heads, kv_heads, head_dim, rot_dim;
+  int experts, top_k, inter, vocab;
+  float rope_theta, eps;
+  int sliding_window;   /* > 0: even layers attend to the last `sliding_window` positions */
+  int norm_topk_prob;
+  int max_seq_len;      /* RoPE table and KV capacity */
+  int ep_rank, ep_size; /* expert parallel placement (single GPU: 0, 1) */
+  int attn_splits;      /* split-K factor of decode attention, 0 = automatic */
+} ms_model_config;
+
+/* Create an empty model; then ms_model_set_tensor for every tensor and ms_model_finalize. */
+MS_API ms_status ms_model_create(ms_ctx* ctx, const ms_model_config* cfg, ms_model** out);
+/* Upload one GGUF-named tensor in its native block layout (no re-quantization).  dims are in
+ * PyTorch order ([n_exp, rows, cols] for stacked experts).  Replaces preload_gates /
+ * preload_attention / preload_experts_gpu (engine.rs:606-667, 674-921, 1079-1369). */
+MS_API ms_status ms_model_set_tensor(ms_model* m, const char* name, int qtype, int n_dims, const int64_t* dims,
+                              const void* host_data, size_t bytes);
+MS_API ms_status ms_model_finalize(ms_model* m);
+/* Parse a GGUF file (reader.rs:259-368, config.rs:253-434) and upload everything. */
+MS_API ms_status ms_model_open_gguf(ms_ctx* ctx, const char* path, int max_seq_len, int ep_rank, int ep_size,
+                             ms_model** out);
+MS_API ms_status ms_model_get_config(const ms_model* m, ms_model_config* cfg);
+MS_API ms_status ms_model_destroy(ms_model* m);
+
+/* Run n tokens through the model at the current position (engine.rs:1869-2006); writes the
+ * last position's logits [vocab] to host memory when logits != NULL. */
+MS_API ms_status ms_model_forward(ms_model* m, const int32_t* tokens, int n_tokens, float* logits);
+/* One decode step with host buffers: token in, greedy next token out (argmax, lowest id on ties). */
+MS_API ms_status ms_model_decode_step(ms_model* m, int32_t token, int32_t* next_token);
+/* Greedy generation (engine.rs:2011-2118): clears the cache, prefill, max_new tokens out. */
+MS_API ms_status ms_model_generate(ms_model* m, const int32_t* prompt, int n_prompt, int max_new, int32_t* out,
+                            int* n_out);
+/* n greedy steps entirely on the device, each feeding the previous argmax (no host copies). */
+MS_API ms_status ms_model_decode_steps_device(ms_model* m, int n_steps);
+/* tokens fed to the model since the last clear (device log), up to max */
+MS_API ms_status ms_model_token_log(ms_model* m, int32_t* out, int max, int* n);
+MS_API ms_status ms_model_clear_cache(ms_model* m);   /* engine.rs:2402-2408 */
+MS_API ms_status ms_model_seq_len(const ms_model* m, int* n);
+/* Diagnostics for parity tests: residual stream after the last layer of the last step [hidden],
+ * routed experts of the last step for one layer [top_k], logits of the last step [vocab]. */
+MS_API ms_status ms_model_last_hidden(ms_model* m, float* out);
+MS_API ms_status ms_model_last_routing(ms_model* m, int layer, int32_t* idx, float* wts);
+MS_API ms_status ms_model_last_logits(ms_model* m, float* out);
+/* 1 (default): replay each step as a captured CUDA graph; 0: plain stream launches. */
+MS_API ms_status ms_model_set_graph(ms_model* m, int enable);
+/* Kernel launches per decode step (for launch accounting). */
+MS_API int ms_model_kernels_per_step(const ms_model* m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOESTREAM_CUDA_H */

@@ -1,0 +1,107 @@
+"""ctypes binding of libmoestream_cuda.so (the C ABI declared in include/moestream_cuda.h).
+
+There is no fallback: if the CUDA library is missing or cannot be loaded, every entry
+point raises.  Build it with ``python -m moe_stream_b200.build``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "libmoestream_cuda.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "moestream_cuda.h")
+
+MS_OK = 0
+STATUS = {0: "ok", 1: "invalid argument", 2: "out of device memory", 3: "CUDA error", 4: "NCCL error",
+          5: "device wait timed out", 6: "unsupported tensor type", 7: "shape mismatch", 8: "I/O error",
+          9: "malformed GGUF", 10: "call out of order", 11: "out-of-range index seen on the device"}
+
+ARCH_GPT_OSS, ARCH_QWEN_MOE = 0, 1
+
+
+class MsError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+class ModelConfig(C.Structure):
+    _fields_ = [("arch", C.c_int), ("hidden", C.c_int), ("layers", C.c_int), ("heads", C.c_int),
+                ("kv_heads", C.c_int), ("head_dim", C.c_int), ("rot_dim", C.c_int), ("experts", C.c_int),
+                ("top_k", C.c_int), ("inter", C.c_int), ("vocab", C.c_int), ("rope_theta", C.c_float),
+                ("eps", C.c_float), ("sliding_window", C.c_int), ("norm_topk_prob", C.c_int),
+                ("max_seq_len", C.c_int), ("ep_rank", C.c_int), ("ep_size", C.c_int), ("attn_splits", C.c_int)]
+
+
+_lib = None
+_vp, _i, _f = C.c_void_p, C.c_int, C.c_float
+_ip = C.POINTER(C.c_int32)
+_fp = C.POINTER(C.c_float)
+
+# name -> (restype, argtypes)
+_SIGS = {
+    "ms_abi_version": (C.c_int, []),
+    "ms_status_string": (C.c_char_p, [C.c_int]),
+    "ms_ctx_create": (C.c_int, [C.c_int, C.POINTER(_vp)]),
+    "ms_ctx_destroy": (C.c_int, [_vp]),
+    "ms_ctx_set_stream": (C.c_int, [_vp, _vp]),
+    "ms_sync": (C.c_int, [_vp]),
+    "ms_last_error": (C.c_char_p, [_vp]),
+    "ms_ctx_error_flags": (C.c_int, [_vp, C.POINTER(C.c_uint32), C.c_int]),
+    "ms_ctx_sm_count": (C.c_int, [_vp]),
+    "ms_malloc": (C.c_int, [_vp, C.c_size_t, C.POINTER(_vp)]),
+    "ms_free": (C.c_int, [_vp, _vp]),
+    "ms_memcpy_h2d": (C.c_int, [_vp, _vp, _vp, C.c_size_t]),
+    "ms_memcpy_d2h": (C.c_int, [_vp, _vp, _vp, C.c_size_t]),
+    "ms_dequantize": (C.c_int, [_vp, _i, _vp, C.c_int64, _vp]),
+    "ms_rms_norm": (C.c_int, [_vp, _vp, _vp, _vp, _i, _i, _f]),
+    "ms_gemv": (C.c_int, [_vp, _i, _vp, _i, _i, _vp, _vp, _vp]),
+    "ms_router_topk": (C.c_int, [_vp, _vp, _vp, _f, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "ms_moe_mxfp4_decode": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "ms_model_create": (C.c_int, [_vp, C.POINTER(ModelConfig), C.POINTER(_vp)]),
+    "ms_model_set_tensor": (C.c_int, [_vp, C.c_char_p, _i, _i, C.POINTER(C.c_int64), _vp, C.c_size_t]),
+    "ms_model_finalize": (C.c_int, [_vp]),
+    "ms_model_open_gguf": (C.c_int, [_vp, C.c_char_p, _i, _i, _i, C.POINTER(_vp)]),
+    "ms_model_get_config": (C.c_int, [_vp, C.POINTER(ModelConfig)]),
+    "ms_model_destroy": (C.c_int, [_vp]),
+    "ms_model_forward": (C.c_int, [_vp, _ip, _i, _fp]),
+    "ms_model_decode_step": (C.c_int, [_vp, C.c_int32, _ip]),
+    "ms_model_generate": (C.c_int, [_vp, _ip, _i, _i, _ip, C.POINTER(C.c_int)]),
+    "ms_model_decode_steps_device": (C.c_int, [_vp, _i]),
+    "ms_model_token_log": (C.c_int, [_vp, _ip, _i, C.POINTER(C.c_int)]),
+    "ms_model_clear_cache": (C.c_int, [_vp]),
+    "ms_model_seq_len": (C.c_int, [_vp, C.POINTER(C.c_int)]),
+    "ms_model_last_hidden": (C.c_int, [_vp, _fp]),
+    "ms_model_last_routing": (C.c_int, [_vp, _i, _ip, _fp]),
+    "ms_model_last_logits": (C.c_int, [_vp, _fp]),
+    "ms_model_set_graph": (C.c_int, [_vp, _i]),
+    "ms_model_kernels_per_step": (C.c_int, [_vp]),
+}
+
+
+def header_symbols() -> list:
+    """Every function the public header declares."""
+    src = open(HEADER).read()
+    return re.findall(r"^MS_API\s+[\w\s\*]+?\b(ms_\w+)\s*\(", src, flags=re.M)
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise OSError(f"{LIB_PATH} is missing: build it with `python -m moe_stream_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(status: int, ctx=None) -> None:
+    if status != MS_OK:
+        msg = lib().ms_last_error(ctx).decode() if ctx else ""
+        raise MsError(status, msg)

@@ -1,0 +1,164 @@
+// kernels.h — host-side launch interface of the moe-stream B200 kernels.
+// Every argument is a plain device pointer or size; no torch types.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ms {
+
+// ---- device error word bits (the host reads them through ms_ctx_error_flags) ----
+enum : uint32_t {
+  EF_TIMEOUT_FULL = 1u << 0,    // consumer waited too long for a stage to land
+  EF_TIMEOUT_EMPTY = 1u << 1,   // producer waited too long for a stage to drain
+  EF_BAD_INDEX = 1u << 2,       // an expert / token index outside its table was skipped
+  EF_BAD_SHAPE = 1u << 3,
+};
+
+enum QType : int { Q_F32 = 0, Q_F16 = 1, Q_Q8_0 = 8, Q_Q4_K = 12, Q_Q6_K = 14, Q_MXFP4 = 39 };
+
+// bytes of one row of `cols` elements in GGML block layout; -1 when not representable
+int64_t row_bytes(int qtype, int64_t cols);
+
+struct DevCtx {
+  int sm_count = 148;
+  uint32_t* err = nullptr;  // device error word
+};
+
+// ---- generic / test ops ----
+cudaError_t launch_dequantize(const DevCtx& c, int qtype, const void* blocks, int64_t n, float* out, cudaStream_t s);
+cudaError_t launch_rms_norm(const DevCtx& c, const float* x, const float* w, float* y, int rows, int dim, float eps,
+                            cudaStream_t s);
+
+// y[r] = W[r,:] . x  (+bias[r]) (+residual: y[r] += y_in[r]);  MXFP4 / F16 / F32 weights.
+struct GemvArgs {
+  int qtype = Q_MXFP4;
+  const void* w = nullptr;
+  int rows = 0, cols = 0;
+  const float* x = nullptr;
+  const float* bias = nullptr;
+  float* y = nullptr;
+  int accumulate = 0;          // y[r] += result
+};
+cudaError_t launch_gemv(const DevCtx& c, const GemvArgs& a, cudaStream_t s);
+
+// Q8_0 projection with the activation quantized to Q8_0 blocks (candle QMatMul numerics).
+// Optional RMSNorm of x first (norm_w != null); optional residual add into `residual`.
+struct Q8GemvArgs {
+  const uint8_t* w = nullptr;  // [rows, cols] Q8_0
+  int rows = 0, cols = 0;
+  const float* x = nullptr;
+  const float* norm_w = nullptr;
+  float eps = 1e-5f;
+  const float* bias = nullptr;
+  float* y = nullptr;          // output (ignored when residual != null)
+  float* residual = nullptr;   // residual[r] += W x + bias
+  int exact = 0;               // 1: f32 activations (no quantization), for the exact-mode oracle
+};
+cudaError_t launch_q8_gemv(const DevCtx& c, const Q8GemvArgs& a, cudaStream_t s);
+
+// ---- MoE ----
+// RMSNorm(h)*gamma -> xn, router logits = xn W^T + b (+ -inf mask) -> top-k + weights.
+struct RouterArgs {
+  const float* h = nullptr;       // [H] residual stream (nullptr: x is already normed, read xn)
+  const float* norm_w = nullptr;  // [H]
+  float eps = 1e-5f;
+  float* xn = nullptr;            // [H] output (input when h == nullptr)
+  const float* w = nullptr;       // [E, H] f32
+  const float* b = nullptr;       // [E] or null
+  const uint8_t* mask = nullptr;  // [E] 1 = dummy expert (masked to -inf) or null
+  float* logits = nullptr;        // [E] scratch/output
+  int* idx = nullptr;             // [K]
+  float* wts = nullptr;           // [K]
+  uint32_t* counter = nullptr;    // 1 word scratch, zero-initialised, self-resetting
+  int H = 0, E = 0, K = 0;
+  int softmax_weight = 1;         // GPT-OSS: softmax over the selected k logits
+  int normalize = 0;              // renormalise top-k probabilities (norm_topk_prob)
+};
+cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s);
+
+// Fused expert FFN for one token over MXFP4 experts: act = SwiGLU(Wg x + bg, Wu x + bu),
+// y_e = Wd act + bd, h += sum over selected experts (ascending expert id) of w_e * y_e.
+struct MoeArgs {
+  const float* x = nullptr;        // [H] normed input
+  const int* idx = nullptr;        // [K] selected expert ids
+  const float* wts = nullptr;      // [K] routing weights
+  const uint8_t* gate = nullptr;   // [E_local, I, H] MXFP4 (native blocks)
+  const uint8_t* up = nullptr;     // [E_local, I, H]
+  const uint8_t* down = nullptr;   // [E_local, H, I]
+  const float* gate_b = nullptr;   // [E_local, I] or null
+  const float* up_b = nullptr;
+  const float* down_b = nullptr;   // [E_local, H] or null
+  float* act = nullptr;            // [K, I] scratch
+  float* partial = nullptr;        // [K, H] scratch
+  uint32_t* tile_cnt = nullptr;    // [H/16] scratch counters, zero-initialised, self-resetting
+  float* h = nullptr;              // [H] residual stream: h += moe(x)   (when out == null)
+  float* out = nullptr;            // [H] if set: out = moe(x) (no residual), for EP partial sums
+  int H = 0, I = 0, K = 0;
+  int expert_base = 0, n_local = 0;  // experts [base, base+n_local) live on this device
+  int oai_swiglu = 1;
+};
+cudaError_t launch_moe_mxfp4(const DevCtx& c, const MoeArgs& a, cudaStream_t s);
+// plain MXFP4 GEMV through the same streaming machinery: y = W x (+bias) (+= when accumulate)
+cudaError_t launch_mxfp4_gemv(const DevCtx& c, const uint8_t* w, int rows, int cols, const float* x,
+                              const float* bias, float* y, int accumulate, cudaStream_t s);
+
+// ---- attention (decode, one token) ----
+struct AttnArgs {
+  const float* qkv = nullptr;      // [nh*hd + 2*nkv*hd] projections (+bias), before RoPE
+  const float* q_norm = nullptr;   // [hd] QK-RMSNorm weights or null
+  const float* k_norm = nullptr;
+  float eps = 1e-6f;
+  const float* cos_t = nullptr;    // [max_seq][rot/2]
+  const float* sin_t = nullptr;
+  int rot = 0;                     // rotary dims (<= hd)
+  const int* pos = nullptr;        // device: position of this token
+  float* kc = nullptr;             // [nkv][cap][hd] f32 cache
+  float* vc = nullptr;
+  int cap = 0;                     // cache slots (== window for sliding-window layers: ring)
+  int window = 0;                  // 0: full attention
+  const float* sinks = nullptr;    // [nh] or null
+  float* part = nullptr;           // scratch [nkv][S][rep][hd + 2]
+  uint32_t* cnt = nullptr;         // [nkv] zero-initialised, self-resetting
+  float* out = nullptr;            // [nh*hd]
+  int nh = 0, nkv = 0, hd = 0, S = 0;
+  float scale = 1.0f;
+};
+cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s);
+
+// ---- LM head / f16 GEMV ----
+// logits = W (RMSNorm(h)*norm_w if norm_w) (+bias); argmax (lowest index on ties) into *key.
+struct LmHeadArgs {
+  const uint16_t* w = nullptr;     // [V, H] f16
+  const float* x = nullptr;        // [H]
+  const float* norm_w = nullptr;   // final norm weights or null (x used as is)
+  float eps = 1e-5f;
+  const float* bias = nullptr;
+  float* logits = nullptr;         // [V] or null
+  unsigned long long* key = nullptr;  // argmax key (value, index) or null; caller zeroes it
+  int V = 0, H = 0;
+  int accumulate = 0;
+};
+cudaError_t launch_lmhead(const DevCtx& c, const LmHeadArgs& a, cudaStream_t s);
+int argmax_from_key(unsigned long long key);
+
+// f32 weights, y = W x (+bias)
+cudaError_t launch_gemv_f32(const DevCtx& c, const float* w, int rows, int cols, const float* x,
+                            const float* bias, float* y, int accumulate, cudaStream_t s);
+
+// ---- step plumbing ----
+struct StepState {
+  int token_in;            // host-provided token
+  int use_argmax;          // 1: take the token from the previous step's argmax key
+  int pos;                 // position being written this step
+  int n_ctx;               // tokens in the cache
+  int max_seq;
+  int last_token;
+  unsigned long long key;  // argmax of this step
+  int n_log;               // tokens appended to the log
+  int pad;
+};
+// token -> embedding row (f16 or f32 table) -> h; advances pos; resets the argmax key
+cudaError_t launch_embed(const DevCtx& c, StepState* st, const void* table, int table_q, int H, int vocab,
+                         float* h, int* token_log, cudaStream_t s);
+
+}  // namespace ms

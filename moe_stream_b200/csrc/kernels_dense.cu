@@ -1,0 +1,697 @@
+// kernels_dense.cu — Q8_0 projections, decode attention, LM head, norms, dequant (sm_100a).
+//
+// Reference semantics (moe-stream-core/src):
+//   RMSNorm ......................... ops/norm.rs:16-37
+//   Q8_0 projection on CPU (candle QMatMul: activation quantized to Q8_0, int8 block dot)
+//                                     ... model/layer.rs:566-572, 722-730; block format gguf/dequant.rs:511-531
+//   QK-norm, RoPE, KV append, SDPA with sinks / sliding window / GQA
+//                                     ... model/layer.rs:643-692, ops/attention.rs:49-120, 178-280,
+//                                         model/kv_cache.rs:37-60, config.rs:463-465
+//   embedding + final norm + LM head + greedy argmax ... model/engine.rs:1877, 1963-1987, 2069-2077
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ms {
+
+int64_t row_bytes(int q, int64_t cols) {
+  switch (q) {
+    case Q_F32: return cols * 4;
+    case Q_F16: return cols * 2;
+    case Q_Q8_0: return cols % 32 ? -1 : cols / 32 * 34;
+    case Q_Q4_K: return cols % 256 ? -1 : cols / 256 * 144;
+    case Q_Q6_K: return cols % 256 ? -1 : cols / 256 * 210;
+    case Q_MXFP4: return cols % 32 ? -1 : cols / 32 * 17;
+  }
+  return -1;
+}
+
+namespace {
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int w = 0; w < nw; ++w) t += red[w];
+  return t;
+}
+
+// ============================ dequant (bit-exact) ============================
+__device__ __forceinline__ float e8m0_half(uint32_t e) {
+  return e < 2 ? __uint_as_float(0x00200000u << e) : __uint_as_float((e - 1u) << 23);
+}
+__constant__ float kMx[16] = {0.0f, 1.0f, 2.0f, 3.0f, 4.0f, 6.0f, 8.0f, 12.0f,
+                              -0.0f, -1.0f, -2.0f, -3.0f, -4.0f, -6.0f, -8.0f, -12.0f};
+
+__global__ void dequant_kernel(int q, const uint8_t* __restrict__ src, int64_t n, float* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  switch (q) {
+    case Q_F32: out[i] = reinterpret_cast<const float*>(src)[i]; break;
+    case Q_F16: out[i] = __half2float(reinterpret_cast<const __half*>(src)[i]); break;
+    case Q_MXFP4: {   // dequant.rs:605-628
+      const uint8_t* b = src + (i >> 5) * 17;
+      const int j = (int)(i & 31);
+      const uint8_t byte = b[1 + (j & 15)];
+      out[i] = kMx[j < 16 ? (byte & 0xf) : (byte >> 4)] * e8m0_half(b[0]);
+      break;
+    }
+    case Q_Q8_0: {    // dequant.rs:511-531
+      const uint8_t* b = src + (i >> 5) * 34;
+      const float d = __half2float(__ushort_as_half((uint16_t)(b[0] | (b[1] << 8))));
+      out[i] = d * (float)(int8_t)b[2 + (i & 31)];
+      break;
+    }
+    case Q_Q4_K: {    // dequant.rs:199-262
+      const uint8_t* b = src + (i >> 8) * 144;
+      const int e = (int)(i & 255), j = e >> 6, hi = (e >> 5) & 1, l = e & 31, is = 2 * j + hi;
+      const float d = __half2float(__ushort_as_half((uint16_t)(b[0] | (b[1] << 8))));
+      const float dmin = __half2float(__ushort_as_half((uint16_t)(b[2] | (b[3] << 8))));
+      const uint8_t* sc = b + 4;
+      uint32_t s, m;
+      if (is < 4) { s = sc[is] & 63; m = sc[is + 4] & 63; }
+      else { s = (sc[is + 4] & 0xf) | ((sc[is - 4] >> 6) << 4); m = (sc[is + 4] >> 4) | ((sc[is] >> 6) << 4); }
+      const uint8_t qb = b[16 + j * 32 + l];
+      const float qv = (float)(hi ? (qb >> 4) : (qb & 0xf));
+      out[i] = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)s), qv), __fmul_rn(dmin, (float)m));
+      break;
+    }
+    case Q_Q6_K: {    // dequant.rs:335-378
+      const uint8_t* b = src + (i >> 8) * 210;
+      const int e = (int)(i & 255), half = e >> 7, r = e & 127, quad = r >> 5, l = r & 31;
+      const uint8_t* ql = b + half * 64;
+      const uint8_t* qh = b + 128 + half * 32;
+      const int8_t* sc = reinterpret_cast<const int8_t*>(b + 192);
+      const float d = __half2float(__ushort_as_half((uint16_t)(b[208] | (b[209] << 8))));
+      int qv;
+      if (quad == 0) qv = ((ql[l] & 0xf) | ((qh[l] & 3) << 4)) - 32;
+      else if (quad == 1) qv = ((ql[l + 32] & 0xf) | (((qh[l] >> 2) & 3) << 4)) - 32;
+      else if (quad == 2) qv = ((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+      else qv = ((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+      const int is = half * 8 + l / 16 + 2 * quad;
+      out[i] = __fmul_rn(__fmul_rn(d, (float)sc[is]), (float)qv);
+      break;
+    }
+  }
+}
+
+// ============================ RMSNorm ============================
+__global__ void rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ y,
+                                int dim, float eps) {
+  __shared__ float red[32];
+  const float* xr = x + (size_t)blockIdx.x * dim;
+  float* yr = y + (size_t)blockIdx.x * dim;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) ss += xr[i] * xr[i];
+  ss = block_sum(ss, red);
+  const float inv = 1.0f / sqrtf(ss / (float)dim + eps);
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) yr[i] = (xr[i] * inv) * w[i];
+}
+
+// ============================ Q8_0 projection ============================
+// Persistent CTA per SM: one producer thread bulk-copies row groups (<= 8 rows, 16-byte
+// aligned) into a ring of stages; 8 consumer warps each take one row of a stage.  Lane l
+// owns activation blocks l, l+32, ... whose int8 codes stay in registers; a row block is
+// 34 bytes (f16 d + 32 int8) at a 2-byte aligned offset, read with aligned words and a
+// 16-bit funnel shift, dotted with __dp4a.  Block sums follow candle's Q8_0 vec_dot:
+// (float)sum_i * d_w * d_x accumulated in f32.
+constexpr int kQW = 8;
+constexpr int kQThreads = (kQW + 1) * 32;
+constexpr int kQMaxStages = 8;
+
+struct Q8Params {
+  const uint8_t* w;
+  int rows, cols, rb, unit_rows, n_units, stage_rows, stage_bytes, ns;
+  const float* x;
+  const float* norm_w;
+  float eps;
+  const float* bias;
+  float* y;
+  float* residual;
+  uint32_t* err;
+};
+
+template <int NBL>
+__global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* stages = smem;
+  int8_t* xq = reinterpret_cast<int8_t*>(smem + (size_t)p.ns * p.stage_bytes);   // [cols]
+  float* xd = reinterpret_cast<float*>(xq + ((p.cols + 15) & ~15));                // [nb]
+  float* xf = xd + ((p.cols / 32 + 3) & ~3);                                       // [cols]
+  uint64_t* full = reinterpret_cast<uint64_t*>(xf + p.cols);
+  uint64_t* empty = full + kQMaxStages;
+  __shared__ float red[32];
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = p.cols / 32;
+  // contiguous row range of this CTA, in units that keep every copy 16-byte aligned
+  const int u0 = (int)((int64_t)blockIdx.x * p.n_units / gridDim.x);
+  const int u1 = (int)((int64_t)(blockIdx.x + 1) * p.n_units / gridDim.x);
+  const int r_begin = u0 * p.unit_rows, r_end = min(u1 * p.unit_rows, p.rows);
+  const int n_stage = (r_end - r_begin + p.stage_rows - 1) / p.stage_rows;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < p.ns; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kQW); }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kQW) {
+    // producer: weights do not depend on the previous kernel, start streaming before the wait
+    if (lane == 0 && n_stage > 0) {
+      const uint64_t pol = policy_evict_first();
+      int issued = 0;
+      for (int j = 0; j < n_stage; ++j) {
+        const int s = j % p.ns, n = j / p.ns;
+        if (n > 0 && !mbar_wait(&empty[s], (uint32_t)((n - 1) & 1), p.err, EF_TIMEOUT_EMPTY)) break;
+        const int r0 = r_begin + j * p.stage_rows;
+        const int nr = min(p.stage_rows, r_end - r0);
+        const uint32_t bytes = (uint32_t)(((int64_t)nr * p.rb + 15) & ~15ll);
+        mbar_expect_tx(&full[s], bytes);
+        bulk_g2s_stream(stages + (size_t)s * p.stage_bytes, p.w + (int64_t)r0 * p.rb, bytes, &full[s], pol);
+        ++issued;
+      }
+      for (int j = max(0, issued - p.ns); j < issued; ++j)
+        mbar_wait(&full[j % p.ns], (uint32_t)((j / p.ns) & 1), p.err, EF_TIMEOUT_FULL);
+    }
+    // the producer warp still joins the block-wide prologue barriers below? no: consumers use
+    // named barrier 1 only, so the producer may leave now.
+    return;
+  }
+
+  // ---- consumer prologue: (RMSNorm) + Q8_0 quantization of the activation ----
+  pdl_wait_prior();
+  const int nct = kQW * 32;
+  float inv = 1.f;
+  if (p.norm_w) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < p.cols; i += nct) { const float v = p.x[i]; ss += v * v; }
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    named_bar(1, nct);
+    float t = 0.f;
+    for (int w = 0; w < kQW; ++w) t += red[w];
+    inv = 1.0f / sqrtf(t / (float)p.cols + p.eps);
+  }
+  for (int i = threadIdx.x; i < p.cols; i += nct) xf[i] = p.norm_w ? (p.x[i] * inv) * p.norm_w[i] : p.x[i];
+  named_bar(1, nct);
+  for (int b = warp; b < nb; b += kQW) {   // one warp per 32-element block
+    const float v = xf[32 * b + lane];
+    const float amax = warp_max(fabsf(v));
+    const float d = amax / 127.0f;
+    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+    xq[32 * b + lane] = (int8_t)roundf(v * id);
+    if (lane == 0) xd[b] = __half2float(__float2half_rn(d));
+  }
+  named_bar(1, nct);
+  int xr[NBL][8];
+  float xdr[NBL];
+#pragma unroll
+  for (int i = 0; i < NBL; ++i) {
+    const int b = lane + 32 * i;
+    xdr[i] = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) xr[i][k] = 0;
+    if (b < nb) {
+      const int4* q4 = reinterpret_cast<const int4*>(xq + 32 * b);
+      const int4 a0 = q4[0], a1 = q4[1];
+      xr[i][0] = a0.x; xr[i][1] = a0.y; xr[i][2] = a0.z; xr[i][3] = a0.w;
+      xr[i][4] = a1.x; xr[i][5] = a1.y; xr[i][6] = a1.z; xr[i][7] = a1.w;
+      xdr[i] = xd[b];
+    }
+  }
+
+  for (int j = 0; j < n_stage; ++j) {
+    const int s = j % p.ns, n = j / p.ns;
+    const int r0 = r_begin + j * p.stage_rows;
+    const int nr = min(p.stage_rows, r_end - r0);
+    const bool ok = mbar_wait(&full[s], (uint32_t)(n & 1), p.err, EF_TIMEOUT_FULL);
+    if (!ok) { if (lane == 0) atomicExch(&abort_flag, 1); }
+    float acc = 0.f;
+    if (ok && warp < nr) {
+      const uint8_t* row = stages + (size_t)s * p.stage_bytes + (size_t)warp * p.rb;
+#pragma unroll
+      for (int i = 0; i < NBL; ++i) {
+        const int b = lane + 32 * i;
+        if (b < nb) {
+          const uint32_t off = 34u * b;
+          const uint16_t dw = *reinterpret_cast<const uint16_t*>(row + off);
+          const uint32_t qa = (off + 2) & ~3u, sh = ((off + 2) & 3u) * 8u;
+          const uint32_t* wp = reinterpret_cast<const uint32_t*>(row + qa);
+          uint32_t wd[9];
+#pragma unroll
+          for (int k = 0; k < 9; ++k) wd[k] = wp[k];
+          int sumi = 0;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) sumi = __dp4a((int)__funnelshift_r(wd[k], wd[k + 1], sh), xr[i][k], sumi);
+          acc += (float)sumi * h2f_bits(dw) * xdr[i];
+        }
+      }
+    }
+    __syncwarp();
+    if (ok && lane == 0) mbar_arrive(&empty[s]);
+    acc = warp_sum(acc);
+    if (ok && warp < nr && lane == 0) {
+      const int r = r0 + warp;
+      const float v = acc + (p.bias ? p.bias[r] : 0.f);
+      if (p.residual) p.residual[r] = p.residual[r] + v;
+      else p.y[r] = v;
+    }
+    if (!ok) break;
+  }
+}
+
+template <int NBL>
+cudaError_t launch_q8(const DevCtx& c, const Q8Params& p, cudaStream_t s) {
+  const size_t smem = (size_t)p.ns * p.stage_bytes + ((p.cols + 15) & ~15) + ((p.cols / 32 + 3) & ~3) * 4 +
+                      (size_t)p.cols * 4 + 2 * kQMaxStages * 8 + 16;
+  cudaError_t e = cudaFuncSetAttribute(q8_gemv_kernel<NBL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)min(c.sm_count, p.n_units));
+  cfg.blockDim = dim3(kQThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, q8_gemv_kernel<NBL>, p);
+}
+
+// ============================ attention (decode) ============================
+constexpr int kAT = 32;        // positions per tile
+constexpr int kAThreads = 128;
+
+__device__ __forceinline__ void rope_inplace(float* v, int rot, const float* c, const float* s) {
+  // ops/attention.rs:96-118: half-rotate over the first `rot` dims
+  const int half = rot / 2;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float x1 = v[i], x2 = v[i + half];
+    v[i] = __fsub_rn(__fmul_rn(x1, c[i]), __fmul_rn(x2, s[i]));
+    v[i + half] = __fadd_rn(__fmul_rn(x2, c[i]), __fmul_rn(x1, s[i]));
+  }
+}
+
+// per-head RMSNorm over hd by one warp (layer.rs:643-650)
+__device__ __forceinline__ void head_norm_warp(float* v, const float* w, int hd, float eps, int lane) {
+  float ss = 0.f;
+  for (int i = lane; i < hd; i += 32) ss += v[i] * v[i];
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / (float)hd + eps);
+  __syncwarp();
+  for (int i = lane; i < hd; i += 32) v[i] = (v[i] * inv) * w[i];
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint32_t* err) {
+  extern __shared__ __align__(16) float sm[];
+  const int rep = a.nh / a.nkv, hd = a.hd, hdp = hd + 1;
+  float* qs = sm;                          // [rep][hd]
+  float* kt = qs + rep * hd;               // [kAT][hd+1]
+  float* vt = kt + kAT * hdp;              // [kAT][hd]
+  float* sc = vt + kAT * hd;               // [rep][kAT]
+  float* os = sc + rep * kAT;              // [rep][hd]
+  float* ml = os + rep * hd;               // [rep][2] running max, sum
+  float* corr = ml + 2 * rep;              // [rep]
+  float* kn = corr + rep;                  // [hd] new k
+  float* vn = kn + hd;                     // [hd] new v
+  __shared__ uint32_t last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+  const int kh = blockIdx.y, sidx = blockIdx.x, S = gridDim.x;
+  pdl_wait_prior();
+  const int pos = *a.pos;
+  const int lo = a.window ? max(0, pos - a.window + 1) : 0;
+  const int n = pos - lo + 1;
+  const int chunk = (n + S - 1) / S;
+  const int p0 = lo + sidx * chunk, p1 = min(p0 + chunk, pos + 1);
+  const bool has_new = (p0 < p1) && (p1 == pos + 1);
+  const int half = a.rot / 2;
+  const float* cs = a.cos_t + (size_t)pos * half;
+  const float* sn = a.sin_t + (size_t)pos * half;
+
+  // q heads of this kv group (+ QK-norm, RoPE)
+  for (int i = threadIdx.x; i < rep * hd; i += blockDim.x) qs[i] = a.qkv[(size_t)kh * rep * hd + i];
+  for (int i = threadIdx.x; i < rep * 2; i += blockDim.x) ml[i] = (i & 1) ? 0.f : -INFINITY;
+  for (int i = threadIdx.x; i < rep * hd; i += blockDim.x) os[i] = 0.f;
+  if (has_new) {
+    const float* kq = a.qkv + (size_t)a.nh * hd + (size_t)kh * hd;
+    const float* vq = a.qkv + (size_t)a.nh * hd + (size_t)a.nkv * hd + (size_t)kh * hd;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) { kn[i] = kq[i]; vn[i] = vq[i]; }
+  }
+  __syncthreads();
+  if (a.q_norm) {
+    for (int h = warp; h < rep; h += nwarp) head_norm_warp(qs + h * hd, a.q_norm, hd, a.eps, lane);
+    if (has_new && warp == 0) head_norm_warp(kn, a.k_norm, hd, a.eps, lane);
+    __syncthreads();
+  }
+  for (int h = 0; h < rep; ++h) rope_inplace(qs + h * hd, a.rot, cs, sn);
+  if (has_new) rope_inplace(kn, a.rot, cs, sn);
+  __syncthreads();
+  if (has_new) {   // kv_cache.rs:37-60 append (ring slot for sliding-window layers)
+    const int slot = a.window ? pos % a.cap : pos;
+    float* kd = a.kc + ((size_t)kh * a.cap + slot) * hd;
+    float* vd = a.vc + ((size_t)kh * a.cap + slot) * hd;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) { kd[i] = kn[i]; vd[i] = vn[i]; }
+  }
+
+  for (int t0 = p0; t0 < p1; t0 += kAT) {
+    const int tn = min(kAT, p1 - t0);
+    for (int i = threadIdx.x; i < tn * hd; i += blockDim.x) {
+      const int j = i / hd, d = i - j * hd, p = t0 + j;
+      float kv, vv;
+      if (p == pos) { kv = kn[d]; vv = vn[d]; }
+      else {
+        const int slot = a.window ? p % a.cap : p;
+        kv = a.kc[((size_t)kh * a.cap + slot) * hd + d];
+        vv = a.vc[((size_t)kh * a.cap + slot) * hd + d];
+      }
+      kt[j * hdp + d] = kv;
+      vt[j * hd + d] = vv;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < rep * kAT; i += blockDim.x) {
+      const int h = i / kAT, j = i - h * kAT;
+      float s = -INFINITY;
+      if (j < tn) {
+        const float* q = qs + h * hd;
+        const float* k = kt + j * hdp;
+        float dot = 0.f;
+        for (int d = 0; d < hd; ++d) dot = fmaf(q[d], k[d], dot);
+        s = dot * a.scale;
+      }
+      sc[i] = s;
+    }
+    __syncthreads();
+    for (int h = warp; h < rep; h += nwarp) {   // online softmax update per head
+      const float v = lane < kAT ? sc[h * kAT + lane] : -INFINITY;
+      const float tm = warp_max(v);
+      const float m_old = ml[2 * h], m_new = fmaxf(m_old, tm);
+      const float pexp = (v == -INFINITY) ? 0.f : expf(v - m_new);
+      const float psum = warp_sum(pexp);
+      const float cr = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
+      if (lane < kAT) sc[h * kAT + lane] = pexp;
+      if (lane == 0) { ml[2 * h] = m_new; ml[2 * h + 1] = ml[2 * h + 1] * cr + psum; corr[h] = cr; }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < rep * hd; i += blockDim.x) {
+      const int h = i / hd, d = i - h * hd;
+      float o = os[i] * corr[h];
+      const float* pp = sc + h * kAT;
+      for (int j = 0; j < tn; ++j) o = fmaf(pp[j], vt[j * hd + d], o);
+      os[i] = o;
+    }
+    __syncthreads();
+  }
+  // partial (m, l, o) of this split
+  float* part = a.part + ((size_t)kh * S + sidx) * rep * (hd + 2);
+  for (int i = threadIdx.x; i < rep * hd; i += blockDim.x) {
+    const int h = i / hd, d = i - h * hd;
+    part[h * (hd + 2) + 2 + d] = os[i];
+  }
+  for (int h = threadIdx.x; h < rep; h += blockDim.x) {
+    part[h * (hd + 2)] = ml[2 * h];
+    part[h * (hd + 2) + 1] = ml[2 * h + 1];
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = (atomicAdd(&a.cnt[kh], 1u) == (uint32_t)S - 1) ? 1u : 0u;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // merge the splits of this kv group (+ attention sink in the denominator)
+  const float* gp = a.part + (size_t)kh * S * rep * (hd + 2);
+  for (int h = warp; h < rep; h += nwarp) {
+    const int hq = kh * rep + h;
+    float M = -INFINITY;
+    for (int s = lane; s < S; s += 32) M = fmaxf(M, __ldcg(&gp[((size_t)s * rep + h) * (hd + 2)]));
+    M = warp_max(M);
+    float sink = 0.f;
+    if (a.sinks) { sink = a.sinks[hq]; M = 0.5f * ((M + sink) + fabsf(M - sink)); }
+    float L = 0.f;
+    for (int s = lane; s < S; s += 32) {
+      const float m = __ldcg(&gp[((size_t)s * rep + h) * (hd + 2)]);
+      if (m != -INFINITY) L += __ldcg(&gp[((size_t)s * rep + h) * (hd + 2) + 1]) * expf(m - M);
+    }
+    L = warp_sum(L);
+    if (a.sinks) L += expf(sink - M);
+    const float invL = 1.0f / L;
+    for (int d = lane; d < hd; d += 32) {
+      float o = 0.f;
+      for (int s = 0; s < S; ++s) {
+        const float m = __ldcg(&gp[((size_t)s * rep + h) * (hd + 2)]);
+        if (m != -INFINITY) o += __ldcg(&gp[((size_t)s * rep + h) * (hd + 2) + 2 + d]) * expf(m - M);
+      }
+      a.out[(size_t)hq * hd + d] = o * invL;
+    }
+  }
+  if (threadIdx.x == 0) a.cnt[kh] = 0u;
+}
+
+// ============================ LM head (f16) + argmax ============================
+// Warp per row, 16-byte streaming loads; x (after the final RMSNorm) in registers.
+constexpr int kLWarps = 8;
+constexpr int kLMaxChunks = 16;   // H <= 16*32*8 = 4096
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+  uint32_t b = __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)b << 32) | (uint32_t)(0xffffffffu - (uint32_t)idx);
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(kLWarps * 32, 1) lmhead_kernel(LmHeadArgs a) {
+  extern __shared__ __align__(16) float xs[];
+  __shared__ float red[kLWarps];
+  __shared__ unsigned long long bestk[kLWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait_prior();
+  float inv = 1.f;
+  if (a.norm_w) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < a.H; i += blockDim.x) ss += a.x[i] * a.x[i];
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float t = 0.f;
+    for (int w = 0; w < kLWarps; ++w) t += red[w];
+    inv = 1.0f / sqrtf(t / (float)a.H + a.eps);
+  }
+  for (int i = threadIdx.x; i < a.H; i += blockDim.x) xs[i] = a.norm_w ? (a.x[i] * inv) * a.norm_w[i] : a.x[i];
+  __syncthreads();
+  const int nch = a.H / 8;
+  float xr[NCH][8];
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) {
+    const int ch = lane + 32 * i;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) xr[i][k] = (ch < nch) ? xs[8 * ch + k] : 0.f;
+  }
+  const int rows_per = (a.V + gridDim.x - 1) / gridDim.x;
+  const int rb = blockIdx.x * rows_per, re = min(a.V, rb + rows_per);
+  unsigned long long best = 0ull;
+  for (int r = rb + warp; r < re; r += kLWarps) {
+    const uint4* wr = reinterpret_cast<const uint4*>(a.w + (size_t)r * a.H);
+    uint4 wv[NCH];
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+      const int ch = lane + 32 * i;
+      if (ch < nch) wv[i] = __ldcs(wr + ch);
+      else wv[i] = make_uint4(0, 0, 0, 0);
+    }
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+      const uint32_t u[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[k]));
+        acc = fmaf(f.x, xr[i][2 * k], acc);
+        acc = fmaf(f.y, xr[i][2 * k + 1], acc);
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      float v = acc + (a.bias ? a.bias[r] : 0.f);
+      if (a.logits) { if (a.accumulate) v += a.logits[r]; a.logits[r] = v; }
+      if (v == v) { const unsigned long long k = argmax_key(v, r); best = k > best ? k : best; }
+    }
+  }
+  if (lane == 0) bestk[warp] = best;
+  __syncthreads();
+  if (threadIdx.x == 0 && a.key) {
+    unsigned long long b = 0ull;
+    for (int w = 0; w < kLWarps; ++w) b = bestk[w] > b ? bestk[w] : b;
+    if (b) atomicMax(a.key, b);
+  }
+}
+
+// ============================ f32 GEMV ============================
+__global__ void gemv_f32_kernel(const float* __restrict__ w, int rows, int cols, const float* __restrict__ x,
+                                const float* __restrict__ bias, float* __restrict__ y, int accumulate) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float* wr = w + (size_t)warp * cols;
+  float acc = 0.f;
+  for (int i = lane; i < cols; i += 32) acc = fmaf(wr[i], x[i], acc);
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    float v = acc + (bias ? bias[warp] : 0.f);
+    y[warp] = accumulate ? y[warp] + v : v;
+  }
+}
+
+// ============================ embedding / step start ============================
+__global__ void embed_kernel(StepState* st, const void* table, int q, int H, int vocab, float* h, int* log,
+                             uint32_t* err) {
+  __shared__ int tok_s;
+  pdl_wait_prior();
+  if (threadIdx.x == 0) {
+    int tok = st->token_in;
+    if (st->use_argmax) {
+      const unsigned long long k = st->key;
+      tok = (int)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
+      if (k == 0ull) tok = 0;
+    }
+    if (tok < 0 || tok >= vocab) { atomicOr(err, EF_BAD_INDEX); tok = 0; }
+    int pos = st->n_ctx;
+    if (pos >= st->max_seq) { atomicOr(err, EF_BAD_SHAPE); pos = st->max_seq - 1; }
+    st->pos = pos;
+    st->n_ctx = pos + 1;
+    st->last_token = tok;
+    st->key = 0ull;
+    if (log && st->n_log < st->max_seq) log[st->n_log] = tok;
+    st->n_log = st->n_log + 1;
+    tok_s = tok;
+  }
+  __syncthreads();
+  const int tok = tok_s;
+  for (int i = threadIdx.x; i < H; i += blockDim.x)
+    h[i] = (q == Q_F16) ? __half2float(reinterpret_cast<const __half*>(table)[(size_t)tok * H + i])
+                        : reinterpret_cast<const float*>(table)[(size_t)tok * H + i];
+}
+
+template <class Kern, class... Args>
+cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+}  // namespace
+
+cudaError_t launch_dequantize(const DevCtx& c, int q, const void* blocks, int64_t n, float* out, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  const int bs = 256;
+  dequant_kernel<<<(unsigned)((n + bs - 1) / bs), bs, 0, s>>>(q, (const uint8_t*)blocks, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rms_norm(const DevCtx& c, const float* x, const float* w, float* y, int rows, int dim, float eps,
+                            cudaStream_t s) {
+  rms_norm_kernel<<<rows, 256, 0, s>>>(x, w, y, dim, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_q8_gemv(const DevCtx& c, const Q8GemvArgs& a, cudaStream_t s) {
+  if (a.exact || a.cols % 32 || a.rows <= 0) return cudaErrorInvalidValue;
+  Q8Params p = {};
+  p.w = a.w; p.rows = a.rows; p.cols = a.cols; p.rb = a.cols / 32 * 34;
+  int u = 1;
+  while ((int64_t)u * p.rb % 16) u *= 2;
+  p.unit_rows = u;                              // smallest row count whose bytes are a multiple of 16
+  p.n_units = (a.rows + u - 1) / u;
+  p.stage_rows = kQW;                           // one row per consumer warp
+  if (p.stage_rows % u) p.stage_rows = u;       // (u <= 16; rows per stage must keep alignment)
+  p.stage_bytes = (int)((((int64_t)p.stage_rows * p.rb) + 15) & ~15ll);
+  p.ns = (int)((180 * 1024) / p.stage_bytes);
+  p.ns = p.ns > 6 ? 6 : (p.ns < 2 ? 2 : p.ns);
+  p.x = a.x; p.norm_w = a.norm_w; p.eps = a.eps; p.bias = a.bias; p.y = a.y; p.residual = a.residual;
+  p.err = c.err;
+  const int nbl = (a.cols / 32 + 31) / 32;
+  if (p.stage_rows > kQW) return cudaErrorInvalidValue;
+  if (nbl <= 1) return launch_q8<1>(c, p, s);
+  if (nbl <= 2) return launch_q8<2>(c, p, s);
+  if (nbl <= 3) return launch_q8<3>(c, p, s);
+  if (nbl <= 4) return launch_q8<4>(c, p, s);
+  if (nbl <= 8) return launch_q8<8>(c, p, s);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s) {
+  if (a.nkv <= 0 || a.nh % a.nkv || a.hd % 4 || a.S <= 0 || a.rot > a.hd || a.rot % 2) return cudaErrorInvalidValue;
+  const int rep = a.nh / a.nkv, hd = a.hd;
+  const size_t smem = sizeof(float) * ((size_t)rep * hd + kAT * (hd + 1) + kAT * hd + rep * kAT + rep * hd +
+                                       3 * rep + 2 * hd);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_pdl(attn_decode_kernel, dim3((unsigned)a.S, (unsigned)a.nkv), dim3(kAThreads), smem, s, a, c.err);
+}
+
+cudaError_t launch_lmhead(const DevCtx& c, const LmHeadArgs& a, cudaStream_t s) {
+  if (a.H % 8 || a.H > kLMaxChunks * 256) return cudaErrorInvalidValue;
+  const int nch = (a.H / 8 + 31) / 32;
+  const size_t smem = (size_t)a.H * sizeof(float);
+  const dim3 grid((unsigned)min(2 * c.sm_count, (a.V + kLWarps - 1) / kLWarps)), block(kLWarps * 32);
+  if (nch <= 4) return launch_pdl(lmhead_kernel<4>, grid, block, smem, s, a);
+  if (nch <= 8) return launch_pdl(lmhead_kernel<8>, grid, block, smem, s, a);
+  if (nch <= 12) return launch_pdl(lmhead_kernel<12>, grid, block, smem, s, a);
+  return launch_pdl(lmhead_kernel<16>, grid, block, smem, s, a);
+}
+
+int argmax_from_key(unsigned long long key) { return (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull)); }
+
+cudaError_t launch_gemv_f32(const DevCtx& c, const float* w, int rows, int cols, const float* x, const float* bias,
+                            float* y, int accumulate, cudaStream_t s) {
+  const int warps_per = 8;
+  gemv_f32_kernel<<<(rows + warps_per - 1) / warps_per, warps_per * 32, 0, s>>>(w, rows, cols, x, bias, y,
+                                                                                accumulate);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_embed(const DevCtx& c, StepState* st, const void* table, int table_q, int H, int vocab, float* h,
+                         int* token_log, cudaStream_t s) {
+  return launch_pdl(embed_kernel, dim3(1), dim3(256), 0, s, st, table, table_q, H, vocab, h, token_log, c.err);
+}
+
+cudaError_t launch_gemv(const DevCtx& c, const GemvArgs& a, cudaStream_t s) {
+  switch (a.qtype) {
+    case Q_MXFP4:
+      return launch_mxfp4_gemv(c, (const uint8_t*)a.w, a.rows, a.cols, a.x, a.bias, a.y, a.accumulate, s);
+    case Q_F16: {
+      LmHeadArgs l;
+      l.w = (const uint16_t*)a.w; l.x = a.x; l.bias = a.bias; l.logits = a.y; l.V = a.rows; l.H = a.cols;
+      l.accumulate = a.accumulate;
+      return launch_lmhead(c, l, s);
+    }
+    case Q_F32:
+      return launch_gemv_f32(c, (const float*)a.w, a.rows, a.cols, a.x, a.bias, a.y, a.accumulate, s);
+    case Q_Q8_0: {
+      if (a.accumulate) return cudaErrorInvalidValue;
+      Q8GemvArgs q;
+      q.w = (const uint8_t*)a.w; q.rows = a.rows; q.cols = a.cols; q.x = a.x; q.bias = a.bias; q.y = a.y;
+      return launch_q8_gemv(c, q, s);
+    }
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace ms

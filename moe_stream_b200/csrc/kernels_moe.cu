@@ -1,0 +1,503 @@
+// kernels_moe.cu — router top-k and the fused MXFP4 expert FFN for decode (sm_100a).
+//
+// Reference semantics (moe-stream-core/src):
+//   router + bias + dummy mask + top-k/softmax ... model/layer.rs:806-837, 1016-1027, 2346-2403
+//   expert FFN, OAI SwiGLU, ascending-expert combine ... model/layer.rs:1797-1847, ops/activation.rs:25-38
+//   MXFP4 block decode ... gguf/dequant.rs:580-628
+//
+// Expert FFN design (one token, memory bound): a persistent grid of one CTA per SM
+// streams expert weight tiles in their native 17-byte MXFP4 blocks through a ring of
+// shared-memory stages filled by 1-D bulk async copies (one producer thread, mbarrier
+// completion).  Eight consumer warps decode the e2m1 codes in registers with
+// cvt.rn.f16x2.e2m1x2 and feed mma.sync m16n8k16 (f16 in, f32 accumulate).  The
+// activation vector is pre-split per 32-element block into f16 hi + lo parts after an
+// exact power-of-two prescale, so each block dot is exact to ~2^-22 relative; the e8m0
+// block scale and the prescale are re-applied in f32 per (row, block).  Column 0 of the
+// MMA carries x_hi and column 1 carries x_lo.
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ms {
+namespace {
+
+constexpr int kCW = 8;                    // consumer warps
+constexpr int kThreads = (kCW + 1) * 32;  // + one producer warp
+constexpr int kMaxK = 16;                 // max experts per token
+constexpr int kMaxStages = 8;
+
+enum { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_PLAIN = 2 };
+
+struct PhaseParams {
+  int mode;
+  const uint8_t* w0;       // gate (GATEUP) or down (DOWN), stacked [E_local, rows, cols]
+  const uint8_t* w1;       // up (GATEUP)
+  int64_t expert_stride;   // bytes per expert matrix
+  int rb;                  // bytes per streamed row
+  int cols;                // reduction length (H for GATEUP, I for DOWN)
+  int rows;                // rows per expert matrix (I for GATEUP, H for DOWN)
+  int tile_rows;           // rows of the matrix per item: 8 (GATEUP: +8 up rows) or 16 (DOWN)
+  int n_tiles;
+  int stage_bytes;
+  int ns;
+  const float* x;          // GATEUP: [cols] normed hidden; DOWN: act [K, cols]
+  const int* idx;
+  const float* wts;
+  const float* bias0;      // gate_b or down_b
+  const float* bias1;      // up_b
+  float* act;              // GATEUP output [K, I]
+  float* partial;          // DOWN scratch [K, H]
+  uint32_t* tile_cnt;
+  float* h;
+  float* out;
+  int K;
+  int expert_base, n_local;
+  int oai;
+  int accumulate;          // PLAIN: y += W x
+  uint32_t* err;
+};
+
+struct SlotInfo {
+  int n;                   // local slots
+  int slot[kMaxK];         // global slot index (0..K-1), ordered by ascending expert id
+  int expert[kMaxK];       // local expert index
+};
+
+// one (row pair) x (32-column block): A rows = (row0, row1) of the thread's MMA rows.
+__device__ __forceinline__ void mx_block(const uint8_t* st, uint32_t off0, uint32_t off1, const uint32_t (&bf)[4],
+                                         int kb, int c, float& acc0, float& acc1) {
+  const uint32_t w0 = lds_u32_unaligned(st, off0 + 1 + 4 * c);
+  const uint32_t w1 = lds_u32_unaligned(st, off1 + 1 + 4 * c);
+  const int e0 = st[off0], e1 = st[off1];
+  uint32_t a[4];
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  a[0] = e2m1x2_to_f16x2(w0);
+  a[1] = e2m1x2_to_f16x2(w1);
+  a[2] = e2m1x2_to_f16x2(w0 >> 8);
+  a[3] = e2m1x2_to_f16x2(w1 >> 8);
+  mma_f16_16816(d, a, bf[0], bf[1]);
+  a[0] = e2m1x2_to_f16x2(w0 >> 16);
+  a[1] = e2m1x2_to_f16x2(w1 >> 16);
+  a[2] = e2m1x2_to_f16x2(w0 >> 24);
+  a[3] = e2m1x2_to_f16x2(w1 >> 24);
+  mma_f16_16816(d, a, bf[2], bf[3]);
+  // weight = e2m1 * 2^(E-127); x = x' * 2^kb  ->  scale 2^(E-127+kb): exponent field E+kb
+  const int f0 = min(max(e0 + kb, 0), 255), f1 = min(max(e1 + kb, 0), 255);
+  acc0 = fmaf(__uint_as_float((uint32_t)f0 << 23), d[0] + d[1], acc0);
+  acc1 = fmaf(__uint_as_float((uint32_t)f1 << 23), d[2] + d[3], acc1);
+}
+
+// B fragments of the activation vector for the K-blocks this warp owns.
+template <int NBW>
+__device__ __forceinline__ void build_bfrag(const float* __restrict__ x, int nb, int warp, int lane,
+                                            uint32_t (&bf)[NBW][4], int (&kb)[NBW]) {
+  const int c = lane & 3, n = lane >> 2;
+#pragma unroll
+  for (int i = 0; i < NBW; ++i) {
+    const int b = warp + kCW * i;
+    bf[i][0] = bf[i][1] = bf[i][2] = bf[i][3] = 0u;
+    kb[i] = 0;
+    if (b < nb) {
+      const float v = x[32 * b + lane];
+      const float m = warp_max(fabsf(v));
+      const int ef = (int)((__float_as_uint(m) >> 23) & 0xffu);
+      const int k = (m > 0.f) ? (ef - 126) : 0;              // m * 2^-k in [0.5, 1)
+      kb[i] = k;
+      const float sc = __uint_as_float((uint32_t)(127 - k) << 23);
+      if (n < 2) {
+        const float4 lo4 = *reinterpret_cast<const float4*>(x + 32 * b + 4 * c);
+        const float4 hi4 = *reinterpret_cast<const float4*>(x + 32 * b + 16 + 4 * c);
+        const float va[4] = {lo4.x, lo4.y, lo4.z, lo4.w};
+        const float vb[4] = {hi4.x, hi4.y, hi4.z, hi4.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float a = va[q] * sc, bb = vb[q] * sc;
+          __half ah = __float2half_rn(a), bh = __float2half_rn(bb);
+          if (n == 1) {
+            ah = __float2half_rn(a - __half2float(ah));
+            bh = __float2half_rn(bb - __half2float(bh));
+          }
+          bf[i][q] = pack_half2(ah, bh);
+        }
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ float swiglu_oai(float g, float u) {
+  const float gc = fminf(g, 7.0f);
+  const float uc = fminf(fmaxf(u, -7.0f), 7.0f);
+  const float sig = 1.0f / (expf(-(gc * 1.702f)) + 1.0f);
+  return (gc * sig) * (uc + 1.0f);
+}
+__device__ __forceinline__ float silu_mul(float g, float u) { return (g / (1.0f + expf(-g))) * u; }
+
+template <int NBW>
+__global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* stages = smem;
+  float* red = reinterpret_cast<float*>(smem + (size_t)p.ns * p.stage_bytes);  // [2][kCW][16]
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * kCW * 16);
+  uint64_t* empty = full + kMaxStages;
+  SlotInfo* si = reinterpret_cast<SlotInfo*>(empty + kMaxStages);
+  int* abort_flag = reinterpret_cast<int*>(si + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  pdl_wait_prior();
+  if (threadIdx.x == 0) {
+    // local slots ordered by ascending expert id (the reference's accumulation order)
+    int n = 0;
+    if (p.mode == MODE_PLAIN) { si->expert[0] = 0; si->slot[0] = 0; n = 1; }
+    for (int k = 0; k < p.K && p.mode != MODE_PLAIN; ++k) {
+      const int e = p.idx[k] - p.expert_base;
+      if (e < 0 || e >= p.n_local) {
+        if (p.n_local == 0 || p.idx[k] < 0) atomicOr(p.err, EF_BAD_INDEX);
+        continue;
+      }
+      int j = n++;
+      while (j > 0 && si->expert[j - 1] > e) {
+        si->expert[j] = si->expert[j - 1];
+        si->slot[j] = si->slot[j - 1];
+        --j;
+      }
+      si->expert[j] = e;
+      si->slot[j] = k;
+    }
+    si->n = n;
+    *abort_flag = 0;
+    for (int s = 0; s < p.ns; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kCW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const int n_items = si->n * p.n_tiles;
+  const int begin = (int)((int64_t)blockIdx.x * n_items / gridDim.x);
+  const int end = (int)((int64_t)(blockIdx.x + 1) * n_items / gridDim.x);
+  const int my_n = end - begin;
+  if (my_n <= 0) return;
+
+  if (warp == kCW) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      const uint32_t half_bytes = (uint32_t)(p.tile_rows * p.rb);
+      int issued = 0;
+      for (int j = 0; j < my_n; ++j) {
+        const int s = j % p.ns, n = j / p.ns;
+        if (n > 0 && !mbar_wait(&empty[s], (uint32_t)((n - 1) & 1), p.err, EF_TIMEOUT_EMPTY)) break;
+        const int item = begin + j;
+        const int ls = item / p.n_tiles, t = item % p.n_tiles;
+        const int64_t base = (int64_t)si->expert[ls] * p.expert_stride + (int64_t)t * half_bytes;
+        uint8_t* dst = stages + (size_t)s * p.stage_bytes;
+        mbar_expect_tx(&full[s], (uint32_t)p.stage_bytes);
+        bulk_g2s_stream(dst, p.w0 + base, half_bytes, &full[s], pol);
+        if (p.mode == MODE_GATEUP) bulk_g2s_stream(dst + half_bytes, p.w1 + base, half_bytes, &full[s], pol);
+        ++issued;
+      }
+      // make sure no copy into this CTA's shared memory is still in flight at exit
+      for (int j = max(0, issued - p.ns); j < issued; ++j)
+        mbar_wait(&full[j % p.ns], (uint32_t)((j / p.ns) & 1), p.err, EF_TIMEOUT_FULL);
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int nb = p.cols / 32;
+  const int c = lane & 3, g = lane >> 2;
+  uint32_t bf[NBW][4];
+  int kb[NBW];
+  int cur_slot = -1;
+  for (int j = 0; j < my_n; ++j) {
+    const int s = j % p.ns, n = j / p.ns;
+    const int item = begin + j;
+    const int ls = item / p.n_tiles, t = item % p.n_tiles;
+    const int slot = si->slot[ls];
+    const int x_slot = (p.mode == MODE_GATEUP) ? 0 : slot;
+    if (x_slot != cur_slot) {
+      build_bfrag<NBW>(p.x + (size_t)x_slot * (p.mode == MODE_GATEUP ? 0 : p.cols), nb, warp, lane, bf, kb);
+      cur_slot = x_slot;
+    }
+    float acc0 = 0.f, acc1 = 0.f;
+    const bool ok = mbar_wait(&full[s], (uint32_t)(n & 1), p.err, EF_TIMEOUT_FULL);
+    if (ok) {
+      const uint8_t* st = stages + (size_t)s * p.stage_bytes;
+      const uint32_t row0 = (uint32_t)g * p.rb;
+      const uint32_t row1 = (p.mode == MODE_GATEUP) ? (uint32_t)(8 + g) * p.rb : (uint32_t)(g + 8) * p.rb;
+#pragma unroll
+      for (int i = 0; i < NBW; ++i) {
+        const int b = warp + kCW * i;
+        if (b < nb) mx_block(st, row0 + 17u * b, row1 + 17u * b, bf[i], kb[i], c, acc0, acc1);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    } else if (lane == 0) {
+      atomicExch(abort_flag, 1);
+    }
+    float* rb = red + (j & 1) * kCW * 16 + warp * 16;
+    if (c == 0) {
+      rb[g] = acc0;
+      rb[g + 8] = acc1;
+    }
+    named_bar(1, kCW * 32);
+    if (*abort_flag) break;
+    if (warp == 0 && lane < 16) {
+      const float* r0 = red + (j & 1) * kCW * 16;
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kCW; ++w) sum += r0[w * 16 + lane];
+      const int e = si->expert[ls];
+      if (p.mode == MODE_GATEUP) {
+        // lanes 0..7: gate rows, lanes 8..15: up rows of the same 8 output rows
+        const int r = t * 8 + (lane & 7);
+        const float* bias = lane < 8 ? p.bias0 : p.bias1;
+        if (bias) sum += bias[(size_t)e * p.rows + r];
+        const float other = __shfl_down_sync(0x0000ffffu, sum, 8);
+        if (lane < 8) p.act[(size_t)slot * p.rows + r] = p.oai ? swiglu_oai(sum, other) : silu_mul(sum, other);
+      } else if (p.mode == MODE_PLAIN) {
+        const int r = t * 16 + lane;
+        if (r < p.rows) {
+          if (p.bias0) sum += p.bias0[r];
+          p.out[r] = p.accumulate ? p.out[r] + sum : sum;
+        }
+      } else {
+        const int r = t * 16 + lane;
+        if (p.bias0) sum += p.bias0[(size_t)e * p.rows + r];
+        p.partial[(size_t)slot * p.rows + r] = sum;
+        __threadfence();
+        uint32_t old = 0;
+        if (lane == 0) old = atomicAdd(&p.tile_cnt[t], 1u);
+        old = __shfl_sync(0x0000ffffu, old, 0);
+        if (old == (uint32_t)(si->n - 1)) {
+          __threadfence();
+          float acc = 0.f;
+          for (int q = 0; q < si->n; ++q) {
+            const int sl = si->slot[q];
+            acc += __ldcg(&p.partial[(size_t)sl * p.rows + r]) * p.wts[sl];
+          }
+          if (p.out) p.out[r] = acc;
+          else p.h[r] = p.h[r] + acc;
+          if (lane == 0) p.tile_cnt[t] = 0u;
+        }
+      }
+    }
+  }
+}
+
+// ---------------- router: RMSNorm + GEMV + bias + mask + top-k + softmax ----------------
+constexpr int kRouterWarps = 8;
+
+__global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a, uint32_t* err) {
+  __shared__ float red[kRouterWarps];
+  __shared__ float inv_s;
+  __shared__ uint32_t last;
+  extern __shared__ float xs[];   // [H]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait_prior();
+  if (a.h) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < a.H; i += blockDim.x) ss += a.h[i] * a.h[i];
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int w = 0; w < kRouterWarps; ++w) t += red[w];
+      inv_s = 1.0f / sqrtf(t / (float)a.H + a.eps);
+    }
+    __syncthreads();
+    const float inv = inv_s;
+    for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
+      const float v = (a.h[i] * inv) * a.norm_w[i];
+      xs[i] = v;
+      if (blockIdx.x == 0) a.xn[i] = v;
+    }
+  } else {
+    for (int i = threadIdx.x; i < a.H; i += blockDim.x) xs[i] = a.xn[i];
+  }
+  __syncthreads();
+  const int e = blockIdx.x * kRouterWarps + warp;
+  if (e < a.E) {
+    const float* wr = a.w + (size_t)e * a.H;
+    float acc = 0.f;
+    for (int i = lane * 4; i < a.H; i += 128) {
+      const float4 w4 = __ldcs(reinterpret_cast<const float4*>(wr + i));
+      acc += w4.x * xs[i] + w4.y * xs[i + 1] + w4.z * xs[i + 2] + w4.w * xs[i + 3];
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      float v = acc + (a.b ? a.b[e] : 0.f);
+      if (a.mask && a.mask[e]) v = -INFINITY;
+      a.logits[e] = v;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = (atomicAdd(a.counter, 1u) == gridDim.x - 1) ? 1u : 0u;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // ---- top-k on the last CTA (ties -> lower index, as a stable descending sort) ----
+  __shared__ float sel_v[kMaxK];
+  __shared__ int sel_i[kMaxK];
+  __shared__ float bv[kRouterWarps];
+  __shared__ int bi[kRouterWarps];
+  float* lg = xs;   // reuse: [E] logits
+  for (int i = threadIdx.x; i < a.E; i += blockDim.x) lg[i] = __ldcg(&a.logits[i]);
+  __syncthreads();
+  for (int k = 0; k < a.K; ++k) {
+    float best = -INFINITY;
+    int bidx = 0x7fffffff;
+    for (int i = threadIdx.x; i < a.E; i += blockDim.x) {
+      const float v = lg[i];
+      bool taken = false;
+      for (int q = 0; q < k; ++q) taken |= (sel_i[q] == i);
+      if (taken) continue;
+      if (v > best || (v == best && i < bidx) || (bidx == 0x7fffffff && !(v == v))) { best = v; bidx = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+      if (ov > best || (ov == best && oi < bidx)) { best = ov; bidx = oi; }
+    }
+    if (lane == 0) { bv[warp] = best; bi[warp] = bidx; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float bb = bv[0]; int ii = bi[0];
+      for (int w = 1; w < kRouterWarps; ++w)
+        if (bv[w] > bb || (bv[w] == bb && bi[w] < ii)) { bb = bv[w]; ii = bi[w]; }
+      if (ii == 0x7fffffff) { ii = 0; atomicOr(err, EF_BAD_INDEX); }
+      sel_v[k] = bb; sel_i[k] = ii;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    float w[kMaxK];
+    if (a.softmax_weight) {              // layer.rs:2361-2372
+      float mx = -INFINITY;
+      for (int k = 0; k < a.K; ++k) mx = fmaxf(mx, sel_v[k]);
+      float sum = 0.f;
+      for (int k = 0; k < a.K; ++k) { w[k] = expf(sel_v[k] - mx); }
+      for (int k = 0; k < a.K; ++k) sum += w[k];
+      for (int k = 0; k < a.K; ++k) w[k] = w[k] / sum;
+    } else {                              // layer.rs:2374-2394
+      float mx = -INFINITY;
+      for (int i = 0; i < a.E; ++i) mx = fmaxf(mx, lg[i]);
+      float sum = 0.f;
+      for (int i = 0; i < a.E; ++i) sum += expf(lg[i] - mx);
+      float ts = 0.f;
+      for (int k = 0; k < a.K; ++k) { w[k] = expf(sel_v[k] - mx) / sum; }
+      for (int k = 0; k < a.K; ++k) ts += w[k];
+      if (a.normalize) for (int k = 0; k < a.K; ++k) w[k] = w[k] / ts;
+    }
+    for (int k = 0; k < a.K; ++k) { a.idx[k] = sel_i[k]; a.wts[k] = w[k]; }
+    *a.counter = 0u;
+  }
+}
+
+template <int NBW>
+cudaError_t launch_phase(const DevCtx& c, const PhaseParams& p, cudaStream_t s) {
+  const size_t smem = (size_t)p.ns * p.stage_bytes + 2 * kCW * 16 * sizeof(float) + 2 * kMaxStages * 8 +
+                      sizeof(SlotInfo) + 16;
+  cudaError_t e = cudaFuncSetAttribute(moe_mxfp4_phase_kernel<NBW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)c.sm_count);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, moe_mxfp4_phase_kernel<NBW>, p);
+}
+
+cudaError_t dispatch_phase(const DevCtx& c, const PhaseParams& p, cudaStream_t s) {
+  const int nbw = (p.cols / 32 + kCW - 1) / kCW;
+  if (nbw <= 1) return launch_phase<1>(c, p, s);
+  if (nbw <= 2) return launch_phase<2>(c, p, s);
+  if (nbw <= 4) return launch_phase<4>(c, p, s);
+  if (nbw <= 8) return launch_phase<8>(c, p, s);
+  if (nbw <= 12) return launch_phase<12>(c, p, s);
+  if (nbw <= 16) return launch_phase<16>(c, p, s);
+  return cudaErrorInvalidValue;
+}
+
+int pick_stages(int stage_bytes) {
+  int ns = (int)((200 * 1024) / stage_bytes);
+  return ns < 2 ? 2 : (ns > 6 ? 6 : ns);
+}
+
+}  // namespace
+
+cudaError_t launch_mxfp4_gemv(const DevCtx& c, const uint8_t* w, int rows, int cols, const float* x,
+                              const float* bias, float* y, int accumulate, cudaStream_t s) {
+  // rows are streamed in 16-row tiles; the weight allocation must be padded to a whole tile
+  if (cols % 32 || rows <= 0) return cudaErrorInvalidValue;
+  const int rb = cols / 32 * 17;
+  if ((16 * rb) % 16) return cudaErrorInvalidValue;
+  PhaseParams p = {};
+  p.mode = MODE_PLAIN; p.w0 = w; p.expert_stride = 0; p.rb = rb; p.cols = cols; p.rows = rows;
+  p.tile_rows = 16; p.n_tiles = (rows + 15) / 16; p.stage_bytes = 16 * rb; p.ns = pick_stages(p.stage_bytes);
+  p.x = x; p.bias0 = bias; p.out = y; p.accumulate = accumulate; p.K = 1; p.err = c.err;
+  return dispatch_phase(c, p, s);
+}
+
+size_t moe_mxfp4_smem_bytes(int H, int I) {
+  const int rbg = H / 32 * 17;
+  return (size_t)pick_stages(16 * rbg) * 16 * rbg;
+}
+
+cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s) {
+  if (a.K < 1 || a.K > kMaxK || a.K > a.E || a.H % 4 || !a.counter) return cudaErrorInvalidValue;
+  const int grid = (a.E + kRouterWarps - 1) / kRouterWarps;
+  const size_t smem = (size_t)(a.H > a.E ? a.H : a.E) * sizeof(float);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kRouterWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaLaunchKernelEx(&cfg, router_kernel, a, c.err);
+}
+
+cudaError_t launch_moe_mxfp4(const DevCtx& c, const MoeArgs& a, cudaStream_t s) {
+  if (a.K < 1 || a.K > kMaxK || a.H % 64 || a.I % 32 || a.n_local < 0) return cudaErrorInvalidValue;
+  const int rbg = a.H / 32 * 17;   // gate/up row bytes
+  const int rbd = a.I / 32 * 17;   // down row bytes
+  PhaseParams p = {};
+  p.K = a.K; p.idx = a.idx; p.wts = a.wts; p.expert_base = a.expert_base; p.n_local = a.n_local;
+  p.oai = a.oai_swiglu; p.err = c.err;
+  // phase 1: gate + up + activation
+  p.mode = MODE_GATEUP; p.w0 = a.gate; p.w1 = a.up; p.expert_stride = (int64_t)a.I * rbg; p.rb = rbg;
+  p.cols = a.H; p.rows = a.I; p.tile_rows = 8; p.n_tiles = a.I / 8; p.stage_bytes = 16 * rbg;
+  p.ns = pick_stages(p.stage_bytes); p.x = a.x; p.bias0 = a.gate_b; p.bias1 = a.up_b; p.act = a.act;
+  if ((8 * rbg) % 16 || p.expert_stride % 16) return cudaErrorInvalidValue;
+  cudaError_t e = dispatch_phase(c, p, s);
+  if (e != cudaSuccess) return e;
+  // phase 2: down + weighted combine (+ residual)
+  p.mode = MODE_DOWN; p.w0 = a.down; p.w1 = nullptr; p.expert_stride = (int64_t)a.H * rbd; p.rb = rbd;
+  p.cols = a.I; p.rows = a.H; p.tile_rows = 16; p.n_tiles = a.H / 16; p.stage_bytes = 16 * rbd;
+  p.ns = pick_stages(p.stage_bytes); p.x = a.act; p.bias0 = a.down_b; p.bias1 = nullptr;
+  p.partial = a.partial; p.tile_cnt = a.tile_cnt; p.h = a.h; p.out = a.out;
+  if ((16 * rbd) % 16 || p.expert_stride % 16) return cudaErrorInvalidValue;
+  return dispatch_phase(c, p, s);
+}
+
+}  // namespace ms

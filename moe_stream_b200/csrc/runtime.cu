@@ -1,0 +1,963 @@
+// runtime.cu — host runtime and C ABI of the moe-stream B200 backend.
+//
+// Holds the context (device, stream, device error word, scratch), the model (weights
+// uploaded in their native GGUF block layout, f32 KV cache, RoPE tables, per-step
+// scratch), the GGUF loader, and the per-token decode step, which is captured once as a
+// CUDA graph and replayed.  Reference call sites are cited per function.
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "../../include/moestream_cuda.h"
+#include "kernels.h"
+
+using namespace ms;
+
+struct ms_ctx {
+  int device = 0;
+  cudaStream_t own = nullptr, stream = nullptr;
+  DevCtx dc;
+  std::string err;
+  // scratch for the standalone kernel entry points
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  uint32_t* counters = nullptr;   // zero-initialised, self-resetting
+  size_t n_counters = 0;
+};
+
+namespace {
+
+ms_status fail(ms_ctx* c, ms_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (c) c->err = buf;
+  return s;
+}
+
+ms_status cuda_fail(ms_ctx* c, cudaError_t e, const char* what) {
+  return fail(c, e == cudaErrorMemoryAllocation ? MS_ERR_OOM : MS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define MS_CUDA(ctx, call)                                      \
+  do {                                                          \
+    cudaError_t e_ = (call);                                    \
+    if (e_ != cudaSuccess) return cuda_fail((ctx), e_, #call);  \
+  } while (0)
+
+ms_status check_dev_flags(ms_ctx* c) {
+  uint32_t f = 0;
+  MS_CUDA(c, cudaMemcpy(&f, c->dc.err, 4, cudaMemcpyDeviceToHost));
+  if (!f) return MS_OK;
+  cudaMemset(c->dc.err, 0, 4);
+  if (f & (EF_TIMEOUT_FULL | EF_TIMEOUT_EMPTY))
+    return fail(c, MS_ERR_TIMEOUT, "device wait timed out (flags 0x%x)", f);
+  return fail(c, MS_ERR_DEVICE_INDEX, "device saw an out-of-range index or shape (flags 0x%x)", f);
+}
+
+ms_status ensure_scratch(ms_ctx* c, size_t bytes, size_t counters) {
+  if (bytes > c->scratch_bytes) {
+    if (c->scratch) cudaFree(c->scratch);
+    c->scratch = nullptr;
+    c->scratch_bytes = 0;
+    MS_CUDA(c, cudaMalloc(&c->scratch, bytes));
+    c->scratch_bytes = bytes;
+  }
+  if (counters > c->n_counters) {
+    if (c->counters) cudaFree(c->counters);
+    c->counters = nullptr;
+    c->n_counters = 0;
+    MS_CUDA(c, cudaMalloc(&c->counters, counters * 4));
+    MS_CUDA(c, cudaMemset(c->counters, 0, counters * 4));
+    c->n_counters = counters;
+  }
+  return MS_OK;
+}
+
+int64_t raw_bytes(int q, int64_t n_elements) {
+  switch (q) {
+    case Q_F32: return n_elements * 4;
+    case Q_F16: return n_elements * 2;
+    case Q_Q8_0: return (n_elements + 31) / 32 * 34;
+    case Q_Q4_K: return (n_elements + 255) / 256 * 144;
+    case Q_Q6_K: return (n_elements + 255) / 256 * 210;
+    case Q_MXFP4: return (n_elements + 31) / 32 * 17;
+  }
+  return -1;
+}
+
+}  // namespace
+
+// =====================================================================================
+// model
+// =====================================================================================
+struct LayerW {
+  float* attn_norm = nullptr;
+  float* post_norm = nullptr;
+  uint8_t* wqkv = nullptr;
+  float* bqkv = nullptr;
+  uint8_t* wo = nullptr;
+  float* bo = nullptr;
+  float* sinks = nullptr;
+  float* qn = nullptr;
+  float* kn = nullptr;
+  float* router_w = nullptr;
+  float* router_b = nullptr;
+  uint8_t* mask = nullptr;
+  uint8_t* gate = nullptr;
+  uint8_t* up = nullptr;
+  uint8_t* down = nullptr;
+  float* gate_b = nullptr;
+  float* up_b = nullptr;
+  float* down_b = nullptr;
+  int gate_q = -1, up_q = -1, down_q = -1, attn_q = -1;
+  float* kc = nullptr;
+  float* vc = nullptr;
+  int cap = 0, window = 0;
+  int* idx = nullptr;
+  float* wts = nullptr;
+  int qkv_parts = 0, bqkv_parts = 0;
+};
+
+struct ms_model {
+  ms_ctx* ctx = nullptr;
+  ms_model_config cfg{};
+  std::vector<LayerW> L;
+  void* embd = nullptr;
+  int embd_q = -1;
+  uint16_t* out_w = nullptr;
+  float* out_norm = nullptr;
+  float* out_b = nullptr;
+  float* cos_t = nullptr;
+  float* sin_t = nullptr;
+  // per-step scratch
+  float *h = nullptr, *qkv = nullptr, *attn_out = nullptr, *xn = nullptr, *router_logits = nullptr;
+  float *act = nullptr, *partial = nullptr, *logits = nullptr, *attn_part = nullptr;
+  uint32_t *router_cnt = nullptr, *tile_cnt = nullptr, *attn_cnt = nullptr;
+  StepState* st = nullptr;
+  int* token_log = nullptr;
+  int expert_base = 0, n_local = 0;
+  int splits_full = 0, splits_swa = 0;
+  std::vector<void*> allocs;
+  std::set<std::string> seen;
+  cudaGraphExec_t graph = nullptr;
+  bool use_graph = true;
+  bool finalized = false;
+  int seq = 0;
+  int* h_tok = nullptr;             // pinned token staging [max_seq + 1]
+  StepState* h_st = nullptr;        // pinned
+  int kernels_per_step = 0;
+
+  template <class T>
+  ms_status alloc(T** p, size_t bytes, bool zero = true) {
+    void* q = nullptr;
+    cudaError_t e = cudaMalloc(&q, bytes ? bytes : 16);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMalloc");
+    if (zero) cudaMemset(q, 0, bytes ? bytes : 16);
+    allocs.push_back(q);
+    *p = reinterpret_cast<T*>(q);
+    return MS_OK;
+  }
+};
+
+namespace {
+
+int q_dim(const ms_model_config& c) { return c.heads * c.head_dim; }
+int kv_dim(const ms_model_config& c) { return c.kv_heads * c.head_dim; }
+
+ms_status upload(ms_model* m, void* dst, const void* src, size_t bytes) {
+  cudaError_t e = cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(m->ctx, e, "upload");
+  return MS_OK;
+}
+
+// f32 vector tensor [n]
+ms_status set_vec(ms_model* m, float** slot, const char* name, int q, int64_t n, int64_t want, const void* data) {
+  if (q != Q_F32) return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: expected F32", name);
+  if (n != want) return fail(m->ctx, MS_ERR_SHAPE, "%s: %lld elements, expected %lld", name, (long long)n, (long long)want);
+  ms_status s = m->alloc(slot, (size_t)n * 4);
+  if (s != MS_OK) return s;
+  return upload(m, *slot, data, (size_t)n * 4);
+}
+
+// weight allocations are padded so 16-row streaming tiles never read past the end
+size_t padded(size_t bytes) { return (bytes + 16 * 4352 + 255) & ~(size_t)255; }
+
+ms_status set_layer_tensor(ms_model* m, int li, const std::string& t, int q, const std::vector<int64_t>& dims,
+                           const void* data, size_t bytes) {
+  const ms_model_config& c = m->cfg;
+  LayerW& Lw = m->L[li];
+  const char* nm = t.c_str();
+  int64_t n = 1;
+  for (auto d : dims) n *= d;
+  const int H = c.hidden, Dq = q_dim(c), Dkv = kv_dim(c);
+  if (raw_bytes(q, n) < 0) return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: qtype %d", nm, q);
+  if ((int64_t)bytes < raw_bytes(q, n)) return fail(m->ctx, MS_ERR_SHAPE, "%s: %zu bytes < %lld", nm, bytes, (long long)raw_bytes(q, n));
+  if (t == "attn_norm.weight") return set_vec(m, &Lw.attn_norm, nm, q, n, H, data);
+  if (t == "post_attention_norm.weight" || t == "ffn_norm.weight") return set_vec(m, &Lw.post_norm, nm, q, n, H, data);
+  if (t == "attn_sinks.weight") return set_vec(m, &Lw.sinks, nm, q, n, c.heads, data);
+  if (t == "attn_q_norm.weight") return set_vec(m, &Lw.qn, nm, q, n, c.head_dim, data);
+  if (t == "attn_k_norm.weight") return set_vec(m, &Lw.kn, nm, q, n, c.head_dim, data);
+  if (t == "attn_output.bias") return set_vec(m, &Lw.bo, nm, q, n, H, data);
+  if (t == "ffn_gate_inp.bias") return set_vec(m, &Lw.router_b, nm, q, n, c.experts, data);
+  if (t == "attn_q.weight" || t == "attn_k.weight" || t == "attn_v.weight") {
+    // q, k, v rows are concatenated into one [Dq + 2 Dkv, H] projection (row layout unchanged)
+    const int rows = t == "attn_q.weight" ? Dq : Dkv;
+    const int off = t == "attn_q.weight" ? 0 : (t == "attn_k.weight" ? Dq : Dq + Dkv);
+    if (dims.size() != 2 || dims[0] != rows || dims[1] != H) return fail(m->ctx, MS_ERR_SHAPE, "%s: bad shape", nm);
+    if (q != Q_Q8_0) return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: attention projections must be Q8_0", nm);
+    if (Lw.attn_q >= 0 && Lw.attn_q != q) return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: mixed qtypes", nm);
+    Lw.attn_q = q;
+    const int64_t rb = row_bytes(q, H);
+    if (!Lw.wqkv) {
+      ms_status s = m->alloc(&Lw.wqkv, padded((size_t)(Dq + 2 * Dkv) * rb));
+      if (s != MS_OK) return s;
+    }
+    ++Lw.qkv_parts;
+    return upload(m, Lw.wqkv + (size_t)off * rb, data, (size_t)rows * rb);
+  }
+  if (t == "attn_q.bias" || t == "attn_k.bias" || t == "attn_v.bias") {
+    const int rows = t == "attn_q.bias" ? Dq : Dkv;
+    const int off = t == "attn_q.bias" ? 0 : (t == "attn_k.bias" ? Dq : Dq + Dkv);
+    if (q != Q_F32 || n != rows) return fail(m->ctx, MS_ERR_SHAPE, "%s: bad bias", nm);
+    if (!Lw.bqkv) {
+      ms_status s = m->alloc(&Lw.bqkv, (size_t)(Dq + 2 * Dkv) * 4);
+      if (s != MS_OK) return s;
+    }
+    ++Lw.bqkv_parts;
+    return upload(m, Lw.bqkv + off, data, (size_t)rows * 4);
+  }
+  if (t == "attn_output.weight") {
+    if (dims.size() != 2 || dims[0] != H || dims[1] != Dq) return fail(m->ctx, MS_ERR_SHAPE, "%s: bad shape", nm);
+    if (q != Q_Q8_0) return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: must be Q8_0", nm);
+    ms_status s = m->alloc(&Lw.wo, padded(bytes));
+    if (s != MS_OK) return s;
+    return upload(m, Lw.wo, data, (size_t)raw_bytes(q, n));
+  }
+  if (t == "ffn_gate_inp.weight") {
+    if (q != Q_F32 || dims.size() != 2 || dims[0] != c.experts || dims[1] != H)
+      return fail(m->ctx, MS_ERR_SHAPE, "%s: expected F32 [%d, %d]", nm, c.experts, H);
+    ms_status s = set_vec(m, &Lw.router_w, nm, q, n, (int64_t)c.experts * H, data);
+    if (s != MS_OK) return s;
+    // engine.rs:628-652: a router row constant within 1e-6 marks a dummy (padded) expert
+    std::vector<uint8_t> mask(c.experts, 0);
+    const float* w = (const float*)data;
+    for (int e = 0; e < c.experts; ++e) {
+      const float* r = w + (size_t)e * H;
+      bool uni = true;
+      for (int i = 0; i < H && uni; ++i) uni = std::fabs(r[i] - r[0]) < 1e-6f;
+      mask[e] = uni ? 1 : 0;
+    }
+    s = m->alloc(&Lw.mask, c.experts);
+    if (s != MS_OK) return s;
+    return upload(m, Lw.mask, mask.data(), c.experts);
+  }
+  // stacked experts: keep only this rank's contiguous slice [base, base + n_local)
+  struct { const char* name; uint8_t** w; float** b; int* qt; int rows, cols; } ex[3] = {
+      {"ffn_gate_exps", &Lw.gate, &Lw.gate_b, &Lw.gate_q, c.inter, H},
+      {"ffn_up_exps", &Lw.up, &Lw.up_b, &Lw.up_q, c.inter, H},
+      {"ffn_down_exps", &Lw.down, &Lw.down_b, &Lw.down_q, H, c.inter}};
+  for (auto& x : ex) {
+    const std::string wn = std::string(x.name) + ".weight", bn = std::string(x.name) + ".bias";
+    if (t == wn) {
+      if (dims.size() != 3 || dims[0] != c.experts || dims[1] != x.rows || dims[2] != x.cols)
+        return fail(m->ctx, MS_ERR_SHAPE, "%s: expected [%d, %d, %d]", nm, c.experts, x.rows, x.cols);
+      if (q != Q_MXFP4) return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: expert qtype %d not supported yet", nm, q);
+      const int64_t per = raw_bytes(q, (int64_t)x.rows * x.cols);
+      ms_status s = m->alloc(x.w, padded((size_t)per * m->n_local));
+      if (s != MS_OK) return s;
+      *x.qt = q;
+      return upload(m, *x.w, (const uint8_t*)data + per * m->expert_base, (size_t)per * m->n_local);
+    }
+    if (t == bn) {
+      if (q != Q_F32 || n != (int64_t)c.experts * x.rows) return fail(m->ctx, MS_ERR_SHAPE, "%s: bad bias", nm);
+      ms_status s = m->alloc(x.b, (size_t)x.rows * m->n_local * 4);
+      if (s != MS_OK) return s;
+      return upload(m, *x.b, (const float*)data + (size_t)x.rows * m->expert_base, (size_t)x.rows * m->n_local * 4);
+    }
+  }
+  return MS_OK;   // tensors outside the decode path are ignored (as the reference ignores them)
+}
+
+// ops/attention.rs:9-34 evaluated on the host exactly as the reference does (f64 pow, f32 tables)
+void rope_tables(int rot, int max_seq, double theta, std::vector<float>& cs, std::vector<float>& sn) {
+  const int half = rot / 2;
+  std::vector<float> inv(half);
+  for (int i = 0; i < half; ++i) inv[i] = 1.0f / (float)std::pow(theta, 2.0 * (double)i / (double)rot);
+  cs.resize((size_t)max_seq * half);
+  sn.resize(cs.size());
+  for (int p = 0; p < max_seq; ++p)
+    for (int i = 0; i < half; ++i) {
+      const float f = (float)p * inv[i];
+      cs[(size_t)p * half + i] = std::cos(f);
+      sn[(size_t)p * half + i] = std::sin(f);
+    }
+}
+
+ms_status enqueue_step(ms_model* m, cudaStream_t s) {
+  const ms_model_config& c = m->cfg;
+  const DevCtx& dc = m->ctx->dc;
+  const int H = c.hidden, Dq = q_dim(c), Dkv = kv_dim(c);
+  int nk = 0;
+#define LAUNCH(call)                                                       \
+  do {                                                                     \
+    cudaError_t e_ = (call);                                               \
+    if (e_ != cudaSuccess) return cuda_fail(m->ctx, e_, #call);           \
+    ++nk;                                                                  \
+  } while (0)
+  LAUNCH(launch_embed(dc, m->st, m->embd, m->embd_q, H, c.vocab, m->h, m->token_log, s));
+  for (int li = 0; li < c.layers; ++li) {
+    LayerW& Lw = m->L[li];
+    Q8GemvArgs qa;
+    qa.w = Lw.wqkv; qa.rows = Dq + 2 * Dkv; qa.cols = H; qa.x = m->h; qa.norm_w = Lw.attn_norm; qa.eps = c.eps;
+    qa.bias = Lw.bqkv; qa.y = m->qkv;
+    LAUNCH(launch_q8_gemv(dc, qa, s));
+    AttnArgs aa;
+    aa.qkv = m->qkv; aa.q_norm = Lw.qn; aa.k_norm = Lw.kn; aa.eps = c.eps; aa.cos_t = m->cos_t; aa.sin_t = m->sin_t;
+    aa.rot = c.rot_dim; aa.pos = &m->st->pos; aa.kc = Lw.kc; aa.vc = Lw.vc; aa.cap = Lw.cap; aa.window = Lw.window;
+    aa.sinks = Lw.sinks; aa.part = m->attn_part; aa.cnt = m->attn_cnt; aa.out = m->attn_out; aa.nh = c.heads;
+    aa.nkv = c.kv_heads; aa.hd = c.head_dim; aa.S = Lw.window ? m->splits_swa : m->splits_full;
+    aa.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
+    LAUNCH(launch_attention(dc, aa, s));
+    Q8GemvArgs oa;
+    oa.w = Lw.wo; oa.rows = H; oa.cols = Dq; oa.x = m->attn_out; oa.bias = Lw.bo; oa.residual = m->h;
+    LAUNCH(launch_q8_gemv(dc, oa, s));
+    RouterArgs ra;
+    ra.h = m->h; ra.norm_w = Lw.post_norm; ra.eps = c.eps; ra.xn = m->xn; ra.w = Lw.router_w; ra.b = Lw.router_b;
+    ra.mask = Lw.mask; ra.logits = m->router_logits; ra.idx = Lw.idx; ra.wts = Lw.wts; ra.counter = m->router_cnt;
+    ra.H = H; ra.E = c.experts; ra.K = c.top_k; ra.softmax_weight = c.arch == MS_ARCH_GPT_OSS;
+    ra.normalize = c.norm_topk_prob;
+    LAUNCH(launch_router(dc, ra, s));
+    MoeArgs ma;
+    ma.x = m->xn; ma.idx = Lw.idx; ma.wts = Lw.wts; ma.gate = Lw.gate; ma.up = Lw.up; ma.down = Lw.down;
+    ma.gate_b = Lw.gate_b; ma.up_b = Lw.up_b; ma.down_b = Lw.down_b; ma.act = m->act; ma.partial = m->partial;
+    ma.tile_cnt = m->tile_cnt; ma.h = m->h; ma.H = H; ma.I = c.inter; ma.K = c.top_k;
+    ma.expert_base = m->expert_base; ma.n_local = m->n_local; ma.oai_swiglu = c.arch == MS_ARCH_GPT_OSS;
+    LAUNCH(launch_moe_mxfp4(dc, ma, s));
+    ++nk;   // two kernels (gate/up, down)
+  }
+  LmHeadArgs la;
+  la.w = m->out_w; la.x = m->h; la.norm_w = m->out_norm; la.eps = c.eps; la.bias = m->out_b; la.logits = m->logits;
+  la.key = &m->st->key; la.V = c.vocab; la.H = H;
+  LAUNCH(launch_lmhead(dc, la, s));
+#undef LAUNCH
+  m->kernels_per_step = nk;
+  return MS_OK;
+}
+
+ms_status run_step(ms_model* m) {
+  cudaStream_t s = m->ctx->stream;
+  if (!m->use_graph) return enqueue_step(m, s);
+  if (!m->graph) {
+    cudaGraph_t g = nullptr;
+    MS_CUDA(m->ctx, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    ms_status st = enqueue_step(m, s);
+    cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (st != MS_OK) { if (g) cudaGraphDestroy(g); return st; }
+    if (e != cudaSuccess) return cuda_fail(m->ctx, e, "cudaStreamEndCapture");
+    e = cudaGraphInstantiate(&m->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) { m->graph = nullptr; return cuda_fail(m->ctx, e, "cudaGraphInstantiate"); }
+  }
+  MS_CUDA(m->ctx, cudaGraphLaunch(m->graph, s));
+  return MS_OK;
+}
+
+ms_status set_feed(ms_model* m, int use_argmax) {
+  // StepState.use_argmax lives at a fixed offset; one small async copy from pinned memory
+  // constants 0 / 1 live in the pinned staging tail, so pending copies never see a rewrite
+  const int* src = &m->h_tok[m->cfg.max_seq_len + 2 + (use_argmax ? 1 : 0)];
+  MS_CUDA(m->ctx, cudaMemcpyAsync(&m->st->use_argmax, src, sizeof(int), cudaMemcpyHostToDevice, m->ctx->stream));
+  return MS_OK;
+}
+
+// ---------------- GGUF (reader.rs:259-368) ----------------
+struct GgufMeta { int type = 0; int64_t i = 0; double f = 0; std::string s; };
+struct GgufT { int q; std::vector<int64_t> shape; uint64_t off; int64_t nbytes; };
+
+struct GgufParser {
+  const uint8_t* b; size_t n, pos = 0; bool ok = true;
+  bool need(size_t k) { if (pos + k > n) { ok = false; return false; } return true; }
+  template <class T> T rd() { T v{}; if (need(sizeof(T))) { memcpy(&v, b + pos, sizeof(T)); pos += sizeof(T); } return v; }
+  std::string str() { uint64_t k = rd<uint64_t>(); if (!need(k)) return {}; std::string s((const char*)b + pos, k); pos += k; return s; }
+  void val(int t, GgufMeta* v, int depth = 0) {
+    v->type = t;
+    switch (t) {
+      case 0: v->i = rd<uint8_t>(); break;
+      case 1: v->i = rd<int8_t>(); break;
+      case 2: v->i = rd<uint16_t>(); break;
+      case 3: v->i = rd<int16_t>(); break;
+      case 4: v->i = rd<uint32_t>(); break;
+      case 5: v->i = rd<int32_t>(); break;
+      case 6: v->f = rd<float>(); v->i = (int64_t)v->f; break;
+      case 7: v->i = rd<uint8_t>(); break;
+      case 8: v->s = str(); break;
+      case 9: {
+        int et = (int)rd<uint32_t>(); uint64_t k = rd<uint64_t>();
+        if (depth > 4 || k > (1ull << 28)) { ok = false; return; }
+        GgufMeta tmp;
+        for (uint64_t j = 0; j < k && ok; ++j) val(et, &tmp, depth + 1);
+        break;
+      }
+      case 10: v->i = (int64_t)rd<uint64_t>(); break;
+      case 11: v->i = rd<int64_t>(); break;
+      case 12: v->f = rd<double>(); v->i = (int64_t)v->f; break;
+      default: ok = false;
+    }
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+int ms_abi_version(void) { return MS_ABI_VERSION; }
+
+const char* ms_status_string(ms_status s) {
+  switch (s) {
+    case MS_OK: return "ok";
+    case MS_ERR_INVALID_ARG: return "invalid argument";
+    case MS_ERR_OOM: return "out of device memory";
+    case MS_ERR_CUDA: return "CUDA error";
+    case MS_ERR_NCCL: return "NCCL error";
+    case MS_ERR_TIMEOUT: return "device wait timed out";
+    case MS_ERR_UNSUPPORTED_QTYPE: return "unsupported tensor type";
+    case MS_ERR_SHAPE: return "shape mismatch";
+    case MS_ERR_IO: return "I/O error";
+    case MS_ERR_FORMAT: return "malformed GGUF";
+    case MS_ERR_STATE: return "call out of order";
+    case MS_ERR_DEVICE_INDEX: return "out-of-range index seen on the device";
+  }
+  return "unknown status";
+}
+
+ms_status ms_ctx_create(int device, ms_ctx** out) {
+  if (!out) return MS_ERR_INVALID_ARG;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return MS_ERR_INVALID_ARG;
+  auto* c = new ms_ctx();
+  c->device = device;
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&c->dc.sm_count, cudaDevAttrMultiProcessorCount, device);
+  if (e == cudaSuccess) e = cudaMalloc(&c->dc.err, 16);
+  if (e == cudaSuccess) e = cudaMemset(c->dc.err, 0, 16);
+  if (e != cudaSuccess) { delete c; return MS_ERR_CUDA; }
+  c->stream = c->own;
+  *out = c;
+  return MS_OK;
+}
+
+ms_status ms_ctx_destroy(ms_ctx* c) {
+  if (!c) return MS_ERR_INVALID_ARG;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  if (c->scratch) cudaFree(c->scratch);
+  if (c->counters) cudaFree(c->counters);
+  if (c->dc.err) cudaFree(c->dc.err);
+  if (c->own) cudaStreamDestroy(c->own);
+  delete c;
+  return MS_OK;
+}
+
+ms_status ms_ctx_set_stream(ms_ctx* c, void* stream) {
+  if (!c) return MS_ERR_INVALID_ARG;
+  c->stream = stream ? (cudaStream_t)stream : c->own;
+  return MS_OK;
+}
+
+ms_status ms_sync(ms_ctx* c) {
+  if (!c) return MS_ERR_INVALID_ARG;
+  MS_CUDA(c, cudaStreamSynchronize(c->stream));
+  return check_dev_flags(c);
+}
+
+const char* ms_last_error(const ms_ctx* c) { return c ? c->err.c_str() : "null context"; }
+
+ms_status ms_ctx_error_flags(ms_ctx* c, uint32_t* flags, int clear) {
+  if (!c || !flags) return MS_ERR_INVALID_ARG;
+  MS_CUDA(c, cudaMemcpy(flags, c->dc.err, 4, cudaMemcpyDeviceToHost));
+  if (clear && *flags) MS_CUDA(c, cudaMemset(c->dc.err, 0, 4));
+  return MS_OK;
+}
+
+int ms_ctx_sm_count(const ms_ctx* c) { return c ? c->dc.sm_count : 0; }
+
+ms_status ms_malloc(ms_ctx* c, size_t bytes, void** p) {
+  if (!c || !p) return MS_ERR_INVALID_ARG;
+  MS_CUDA(c, cudaMalloc(p, bytes ? bytes : 16));
+  return MS_OK;
+}
+ms_status ms_free(ms_ctx* c, void* p) {
+  if (!c) return MS_ERR_INVALID_ARG;
+  MS_CUDA(c, cudaFree(p));
+  return MS_OK;
+}
+ms_status ms_memcpy_h2d(ms_ctx* c, void* d, const void* s, size_t n) {
+  if (!c) return MS_ERR_INVALID_ARG;
+  MS_CUDA(c, cudaMemcpyAsync(d, s, n, cudaMemcpyHostToDevice, c->stream));
+  MS_CUDA(c, cudaStreamSynchronize(c->stream));
+  return MS_OK;
+}
+ms_status ms_memcpy_d2h(ms_ctx* c, void* d, const void* s, size_t n) {
+  if (!c) return MS_ERR_INVALID_ARG;
+  MS_CUDA(c, cudaMemcpyAsync(d, s, n, cudaMemcpyDeviceToHost, c->stream));
+  MS_CUDA(c, cudaStreamSynchronize(c->stream));
+  return MS_OK;
+}
+
+ms_status ms_dequantize(ms_ctx* c, int q, const void* d_blocks, int64_t n, float* d_out) {
+  if (!c || !d_blocks || !d_out || n < 0) return MS_ERR_INVALID_ARG;
+  if (raw_bytes(q, 1) < 0) return fail(c, MS_ERR_UNSUPPORTED_QTYPE, "qtype %d", q);
+  MS_CUDA(c, launch_dequantize(c->dc, q, d_blocks, n, d_out, c->stream));
+  return MS_OK;
+}
+
+ms_status ms_rms_norm(ms_ctx* c, const float* x, const float* w, float* y, int rows, int dim, float eps) {
+  if (!c || !x || !w || !y || rows <= 0 || dim <= 0) return MS_ERR_INVALID_ARG;
+  MS_CUDA(c, launch_rms_norm(c->dc, x, w, y, rows, dim, eps, c->stream));
+  return MS_OK;
+}
+
+ms_status ms_gemv(ms_ctx* c, int q, const void* w, int rows, int cols, const float* x, const float* bias, float* y) {
+  if (!c || !w || !x || !y || rows <= 0 || cols <= 0) return MS_ERR_INVALID_ARG;
+  if (q != Q_MXFP4 && q != Q_Q8_0 && q != Q_F16 && q != Q_F32) return fail(c, MS_ERR_UNSUPPORTED_QTYPE, "gemv qtype %d", q);
+  if (row_bytes(q, cols) < 0) return fail(c, MS_ERR_SHAPE, "cols %d not a whole number of blocks", cols);
+  GemvArgs a;
+  a.qtype = q; a.w = w; a.rows = rows; a.cols = cols; a.x = x; a.bias = bias; a.y = y;
+  cudaError_t e = launch_gemv(c->dc, a, c->stream);
+  if (e == cudaErrorInvalidValue) return fail(c, MS_ERR_SHAPE, "gemv: unsupported shape %dx%d", rows, cols);
+  if (e != cudaSuccess) return cuda_fail(c, e, "gemv");
+  return MS_OK;
+}
+
+ms_status ms_router_topk(ms_ctx* c, const float* h, const float* nw, float eps, const float* rw, const float* rb,
+                         const uint8_t* mask, int H, int E, int K, int arch, int norm_topk, float* xn, float* logits,
+                         int32_t* idx, float* wts) {
+  if (!c || !rw || !xn || !logits || !idx || !wts || (h && !nw) || H <= 0 || E <= 0 || K <= 0 || K > E || K > 16)
+    return MS_ERR_INVALID_ARG;
+  ms_status s = ensure_scratch(c, 16, 64);
+  if (s != MS_OK) return s;
+  RouterArgs a;
+  a.h = h; a.norm_w = nw; a.eps = eps; a.xn = xn; a.w = rw; a.b = rb; a.mask = mask; a.logits = logits; a.idx = idx;
+  a.wts = wts; a.counter = c->counters; a.H = H; a.E = E; a.K = K; a.softmax_weight = arch == MS_ARCH_GPT_OSS;
+  a.normalize = norm_topk;
+  MS_CUDA(c, launch_router(c->dc, a, c->stream));
+  return MS_OK;
+}
+
+ms_status ms_moe_mxfp4_decode(ms_ctx* c, const void* gate, const void* up, const void* down, const float* gb,
+                              const float* ub, const float* db, int H, int I, int E, int K, int arch, const float* x,
+                              const int32_t* idx, const float* wts, float* h) {
+  if (!c || !gate || !up || !down || !x || !idx || !wts || !h || K <= 0 || K > 16 || E <= 0) return MS_ERR_INVALID_ARG;
+  if (H % 64 || I % 32) return fail(c, MS_ERR_SHAPE, "moe: hidden %% 64 and inter %% 32 required");
+  const size_t act_b = (size_t)K * I * 4, part_b = (size_t)K * H * 4;
+  ms_status s = ensure_scratch(c, act_b + part_b + 256, 64 + H / 16);
+  if (s != MS_OK) return s;
+  MoeArgs a;
+  a.x = x; a.idx = idx; a.wts = wts; a.gate = (const uint8_t*)gate; a.up = (const uint8_t*)up;
+  a.down = (const uint8_t*)down; a.gate_b = gb; a.up_b = ub; a.down_b = db;
+  a.act = (float*)c->scratch; a.partial = (float*)((char*)c->scratch + ((act_b + 255) & ~(size_t)255));
+  a.tile_cnt = c->counters + 64; a.h = h; a.H = H; a.I = I; a.K = K; a.expert_base = 0; a.n_local = E;
+  a.oai_swiglu = arch == MS_ARCH_GPT_OSS;
+  cudaError_t e = launch_moe_mxfp4(c->dc, a, c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "moe_mxfp4");
+  return MS_OK;
+}
+
+// ---------------------------------------------------------------------------------
+ms_status ms_model_create(ms_ctx* c, const ms_model_config* cfg, ms_model** out) {
+  if (!c || !cfg || !out) return MS_ERR_INVALID_ARG;
+  *out = nullptr;
+  const ms_model_config& k = *cfg;
+  if (k.hidden <= 0 || k.layers <= 0 || k.heads <= 0 || k.kv_heads <= 0 || k.heads % k.kv_heads || k.head_dim <= 0 ||
+      k.experts <= 0 || k.top_k <= 0 || k.top_k > 16 || k.top_k > k.experts || k.inter <= 0 || k.vocab <= 0 ||
+      k.max_seq_len <= 0 || k.rot_dim <= 0 || k.rot_dim > k.head_dim || k.rot_dim % 2 || k.ep_size <= 0 ||
+      k.ep_rank < 0 || k.ep_rank >= k.ep_size || k.experts % k.ep_size)
+    return fail(c, MS_ERR_INVALID_ARG, "invalid model config");
+  if (k.hidden % 64 || k.inter % 32) return fail(c, MS_ERR_SHAPE, "hidden %% 64 and inter %% 32 required");
+  auto* m = new ms_model();
+  m->ctx = c;
+  m->cfg = k;
+  m->L.resize(k.layers);
+  m->n_local = k.experts / k.ep_size;
+  m->expert_base = k.ep_rank * m->n_local;
+  *out = m;
+  return MS_OK;
+}
+
+ms_status ms_model_set_tensor(ms_model* m, const char* name, int q, int nd, const int64_t* dims, const void* data,
+                              size_t bytes) {
+  if (!m || !name || !dims || nd <= 0 || nd > 4 || !data) return MS_ERR_INVALID_ARG;
+  if (m->finalized) return fail(m->ctx, MS_ERR_STATE, "set_tensor after finalize");
+  cudaSetDevice(m->ctx->device);
+  std::vector<int64_t> d(dims, dims + nd);
+  int64_t n = 1;
+  for (auto x : d) n *= x;
+  const std::string nm(name);
+  const ms_model_config& c = m->cfg;
+  m->seen.insert(nm);
+  if (raw_bytes(q, n) < 0) return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: qtype %d", name, q);
+  if ((int64_t)bytes < raw_bytes(q, n)) return fail(m->ctx, MS_ERR_SHAPE, "%s: short buffer", name);
+  if (nm == "token_embd.weight") {
+    if (nd != 2 || d[0] != c.vocab || d[1] != c.hidden || (q != Q_F16 && q != Q_F32))
+      return fail(m->ctx, MS_ERR_SHAPE, "%s: expected F16/F32 [%d, %d]", name, c.vocab, c.hidden);
+    ms_status s = m->alloc(&m->embd, (size_t)raw_bytes(q, n), false);
+    if (s != MS_OK) return s;
+    m->embd_q = q;
+    return upload(m, m->embd, data, (size_t)raw_bytes(q, n));
+  }
+  if (nm == "output.weight") {
+    if (nd != 2 || d[0] != c.vocab || d[1] != c.hidden) return fail(m->ctx, MS_ERR_SHAPE, "%s: bad shape", name);
+    if (q != Q_F16) return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: LM head must be F16", name);
+    ms_status s = m->alloc(&m->out_w, (size_t)raw_bytes(q, n), false);
+    if (s != MS_OK) return s;
+    return upload(m, m->out_w, data, (size_t)raw_bytes(q, n));
+  }
+  if (nm == "output_norm.weight") return set_vec(m, &m->out_norm, name, q, n, c.hidden, data);
+  if (nm == "output.bias") return set_vec(m, &m->out_b, name, q, n, c.vocab, data);
+  int li = -1, off = 0;
+  if (sscanf(name, "blk.%d.%n", &li, &off) == 1 && off > 0) {
+    if (li < 0 || li >= c.layers) return fail(m->ctx, MS_ERR_SHAPE, "%s: layer out of range", name);
+    return set_layer_tensor(m, li, std::string(name + off), q, d, data, bytes);
+  }
+  return MS_OK;
+}
+
+ms_status ms_model_finalize(ms_model* m) {
+  if (!m) return MS_ERR_INVALID_ARG;
+  if (m->finalized) return MS_OK;
+  cudaSetDevice(m->ctx->device);
+  const ms_model_config& c = m->cfg;
+  if (!m->embd || !m->out_w || !m->out_norm) return fail(m->ctx, MS_ERR_STATE, "missing token_embd/output/output_norm");
+  for (int li = 0; li < c.layers; ++li) {
+    LayerW& Lw = m->L[li];
+    if (!Lw.attn_norm || !Lw.post_norm || Lw.qkv_parts != 3 || !Lw.wo || !Lw.router_w || !Lw.gate || !Lw.up || !Lw.down)
+      return fail(m->ctx, MS_ERR_STATE, "layer %d: missing tensors", li);
+    if (Lw.bqkv_parts != 0 && Lw.bqkv_parts != 3) return fail(m->ctx, MS_ERR_STATE, "layer %d: partial qkv bias", li);
+    if ((Lw.qn == nullptr) != (Lw.kn == nullptr)) return fail(m->ctx, MS_ERR_STATE, "layer %d: q/k norm mismatch", li);
+    Lw.window = (c.sliding_window > 0 && li % 2 == 0) ? c.sliding_window : 0;   // config.rs:463-465
+    Lw.cap = Lw.window ? std::min(Lw.window, c.max_seq_len) : c.max_seq_len;
+    if (Lw.window) Lw.cap = Lw.window;
+    const size_t kvb = (size_t)c.kv_heads * Lw.cap * c.head_dim * 4;
+    ms_status s = m->alloc(&Lw.kc, kvb, false);
+    if (s == MS_OK) s = m->alloc(&Lw.vc, kvb, false);
+    if (s == MS_OK) s = m->alloc(&Lw.idx, 16 * 4);
+    if (s == MS_OK) s = m->alloc(&Lw.wts, 16 * 4);
+    if (s != MS_OK) return s;
+  }
+  const int H = c.hidden, Dq = q_dim(c), Dkv = kv_dim(c), rep = c.heads / c.kv_heads;
+  int S = c.attn_splits;
+  if (S <= 0) { S = (2 * m->ctx->dc.sm_count + c.kv_heads - 1) / c.kv_heads; if (S > 64) S = 64; }
+  m->splits_full = S;
+  m->splits_swa = c.sliding_window > 0 ? std::max(1, std::min(S, (c.sliding_window + 31) / 32)) : S;
+  ms_status s = MS_OK;
+  s = s ? s : m->alloc(&m->h, (size_t)H * 4);
+  s = s ? s : m->alloc(&m->qkv, (size_t)(Dq + 2 * Dkv) * 4);
+  s = s ? s : m->alloc(&m->attn_out, (size_t)Dq * 4);
+  s = s ? s : m->alloc(&m->xn, (size_t)H * 4);
+  s = s ? s : m->alloc(&m->router_logits, (size_t)c.experts * 4);
+  s = s ? s : m->alloc(&m->act, (size_t)c.top_k * c.inter * 4);
+  s = s ? s : m->alloc(&m->partial, (size_t)c.top_k * H * 4);
+  s = s ? s : m->alloc(&m->logits, (size_t)c.vocab * 4);
+  s = s ? s : m->alloc(&m->attn_part, (size_t)c.kv_heads * S * rep * (c.head_dim + 2) * 4);
+  s = s ? s : m->alloc(&m->router_cnt, 16);
+  s = s ? s : m->alloc(&m->tile_cnt, (size_t)(H / 16 + 16) * 4);
+  s = s ? s : m->alloc(&m->attn_cnt, (size_t)(c.kv_heads + 16) * 4);
+  s = s ? s : m->alloc(&m->st, sizeof(StepState));
+  s = s ? s : m->alloc(&m->token_log, (size_t)(c.max_seq_len + 1) * 4);
+  if (s != MS_OK) return s;
+  std::vector<float> cs, sn;
+  rope_tables(c.rot_dim, c.max_seq_len, (double)c.rope_theta, cs, sn);
+  s = m->alloc(&m->cos_t, cs.size() * 4, false);
+  s = s ? s : m->alloc(&m->sin_t, sn.size() * 4, false);
+  if (s != MS_OK) return s;
+  s = upload(m, m->cos_t, cs.data(), cs.size() * 4);
+  s = s ? s : upload(m, m->sin_t, sn.data(), sn.size() * 4);
+  if (s != MS_OK) return s;
+  MS_CUDA(m->ctx, cudaMallocHost(&m->h_tok, (size_t)(c.max_seq_len + 4) * 4));
+  m->h_tok[c.max_seq_len + 2] = 0;
+  m->h_tok[c.max_seq_len + 3] = 1;
+  MS_CUDA(m->ctx, cudaMallocHost(&m->h_st, sizeof(StepState)));
+  memset(m->h_st, 0, sizeof(StepState));
+  m->h_st->max_seq = c.max_seq_len;
+  MS_CUDA(m->ctx, cudaMemcpy(m->st, m->h_st, sizeof(StepState), cudaMemcpyHostToDevice));
+  m->finalized = true;
+  return MS_OK;
+}
+
+ms_status ms_model_destroy(ms_model* m) {
+  if (!m) return MS_ERR_INVALID_ARG;
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  if (m->graph) cudaGraphExecDestroy(m->graph);
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->h_tok) cudaFreeHost(m->h_tok);
+  if (m->h_st) cudaFreeHost(m->h_st);
+  delete m;
+  return MS_OK;
+}
+
+ms_status ms_model_get_config(const ms_model* m, ms_model_config* cfg) {
+  if (!m || !cfg) return MS_ERR_INVALID_ARG;
+  *cfg = m->cfg;
+  return MS_OK;
+}
+
+ms_status ms_model_set_graph(ms_model* m, int enable) {
+  if (!m) return MS_ERR_INVALID_ARG;
+  m->use_graph = enable != 0;
+  return MS_OK;
+}
+
+int ms_model_kernels_per_step(const ms_model* m) { return m ? m->kernels_per_step : 0; }
+
+ms_status ms_model_clear_cache(ms_model* m) {
+  if (!m || !m->finalized) return MS_ERR_STATE;
+  MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+  memset(m->h_st, 0, sizeof(StepState));
+  m->h_st->max_seq = m->cfg.max_seq_len;
+  MS_CUDA(m->ctx, cudaMemcpy(m->st, m->h_st, sizeof(StepState), cudaMemcpyHostToDevice));
+  m->seq = 0;
+  return MS_OK;
+}
+
+ms_status ms_model_seq_len(const ms_model* m, int* n) {
+  if (!m || !n) return MS_ERR_INVALID_ARG;
+  *n = m->seq;
+  return MS_OK;
+}
+
+ms_status ms_model_forward(ms_model* m, const int32_t* tokens, int n, float* logits) {
+  if (!m || !tokens || n <= 0) return MS_ERR_INVALID_ARG;
+  if (!m->finalized) return fail(m->ctx, MS_ERR_STATE, "forward before finalize");
+  if (m->seq + n > m->cfg.max_seq_len) return fail(m->ctx, MS_ERR_SHAPE, "sequence exceeds max_seq_len");
+  cudaSetDevice(m->ctx->device);
+  cudaStream_t s = m->ctx->stream;
+  MS_CUDA(m->ctx, cudaStreamSynchronize(s));   // pinned staging is reused below
+  for (int i = 0; i < n; ++i) {
+    if (tokens[i] < 0 || tokens[i] >= m->cfg.vocab) return fail(m->ctx, MS_ERR_INVALID_ARG, "token %d out of range", tokens[i]);
+    m->h_tok[i] = tokens[i];
+  }
+  ms_status st = set_feed(m, 0);
+  if (st != MS_OK) return st;
+  for (int i = 0; i < n; ++i) {
+    MS_CUDA(m->ctx, cudaMemcpyAsync(&m->st->token_in, &m->h_tok[i], 4, cudaMemcpyHostToDevice, s));
+    st = run_step(m);
+    if (st != MS_OK) return st;
+  }
+  m->seq += n;
+  if (logits) MS_CUDA(m->ctx, cudaMemcpyAsync(logits, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, s));
+  return ms_sync(m->ctx);
+}
+
+ms_status ms_model_decode_step(ms_model* m, int32_t token, int32_t* next) {
+  if (!m || !next) return MS_ERR_INVALID_ARG;
+  if (!m->finalized) return fail(m->ctx, MS_ERR_STATE, "decode before finalize");
+  if (m->seq + 1 > m->cfg.max_seq_len) return fail(m->ctx, MS_ERR_SHAPE, "sequence exceeds max_seq_len");
+  if (token < 0 || token >= m->cfg.vocab) return fail(m->ctx, MS_ERR_INVALID_ARG, "token out of range");
+  cudaSetDevice(m->ctx->device);
+  cudaStream_t s = m->ctx->stream;
+  MS_CUDA(m->ctx, cudaStreamSynchronize(s));
+  m->h_tok[0] = token;
+  ms_status st = set_feed(m, 0);
+  if (st != MS_OK) return st;
+  MS_CUDA(m->ctx, cudaMemcpyAsync(&m->st->token_in, &m->h_tok[0], 4, cudaMemcpyHostToDevice, s));
+  st = run_step(m);
+  if (st != MS_OK) return st;
+  MS_CUDA(m->ctx, cudaMemcpyAsync(&m->h_st->key, &m->st->key, 8, cudaMemcpyDeviceToHost, s));
+  st = ms_sync(m->ctx);
+  if (st != MS_OK) return st;
+  m->seq += 1;
+  *next = argmax_from_key(m->h_st->key);
+  return MS_OK;
+}
+
+ms_status ms_model_decode_steps_device(ms_model* m, int n) {
+  if (!m || n < 0) return MS_ERR_INVALID_ARG;
+  if (!m->finalized) return fail(m->ctx, MS_ERR_STATE, "decode before finalize");
+  if (m->seq + n > m->cfg.max_seq_len) return fail(m->ctx, MS_ERR_SHAPE, "sequence exceeds max_seq_len");
+  cudaSetDevice(m->ctx->device);
+  ms_status st = set_feed(m, 1);
+  if (st != MS_OK) return st;
+  for (int i = 0; i < n; ++i) {
+    st = run_step(m);
+    if (st != MS_OK) return st;
+  }
+  m->seq += n;
+  return MS_OK;
+}
+
+ms_status ms_model_token_log(ms_model* m, int32_t* out, int max, int* n) {
+  if (!m || !out || !n) return MS_ERR_INVALID_ARG;
+  MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+  StepState st;
+  MS_CUDA(m->ctx, cudaMemcpy(&st, m->st, sizeof st, cudaMemcpyDeviceToHost));
+  const int k = std::min(std::min(st.n_log, max), m->cfg.max_seq_len);
+  if (k > 0) MS_CUDA(m->ctx, cudaMemcpy(out, m->token_log, (size_t)k * 4, cudaMemcpyDeviceToHost));
+  *n = k;
+  return MS_OK;
+}
+
+ms_status ms_model_generate(ms_model* m, const int32_t* prompt, int n_prompt, int max_new, int32_t* out, int* n_out) {
+  if (!m || !prompt || n_prompt <= 0 || max_new <= 0 || !out) return MS_ERR_INVALID_ARG;
+  if (n_prompt + max_new - 1 > m->cfg.max_seq_len) return fail(m->ctx, MS_ERR_SHAPE, "sequence exceeds max_seq_len");
+  ms_status st = ms_model_clear_cache(m);
+  if (st != MS_OK) return st;
+  st = ms_model_forward(m, prompt, n_prompt, nullptr);   // prefill (engine.rs:2022-2025)
+  if (st != MS_OK) return st;
+  st = ms_model_decode_steps_device(m, max_new - 1);      // decode loop (engine.rs:2051-2096)
+  if (st != MS_OK) return st;
+  MS_CUDA(m->ctx, cudaMemcpyAsync(&m->h_st->key, &m->st->key, 8, cudaMemcpyDeviceToHost, m->ctx->stream));
+  st = ms_sync(m->ctx);
+  if (st != MS_OK) return st;
+  std::vector<int32_t> log(n_prompt + max_new);
+  int k = 0;
+  st = ms_model_token_log(m, log.data(), (int)log.size(), &k);
+  if (st != MS_OK) return st;
+  int w = 0;
+  for (int i = n_prompt; i < k && w < max_new - 1; ++i) out[w++] = log[i];
+  out[w++] = argmax_from_key(m->h_st->key);
+  if (n_out) *n_out = w;
+  return MS_OK;
+}
+
+ms_status ms_model_last_hidden(ms_model* m, float* out) {
+  if (!m || !out) return MS_ERR_INVALID_ARG;
+  MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+  MS_CUDA(m->ctx, cudaMemcpy(out, m->h, (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost));
+  return MS_OK;
+}
+
+ms_status ms_model_last_routing(ms_model* m, int layer, int32_t* idx, float* wts) {
+  if (!m || !idx || !wts || layer < 0 || layer >= m->cfg.layers) return MS_ERR_INVALID_ARG;
+  MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+  MS_CUDA(m->ctx, cudaMemcpy(idx, m->L[layer].idx, (size_t)m->cfg.top_k * 4, cudaMemcpyDeviceToHost));
+  MS_CUDA(m->ctx, cudaMemcpy(wts, m->L[layer].wts, (size_t)m->cfg.top_k * 4, cudaMemcpyDeviceToHost));
+  return MS_OK;
+}
+
+ms_status ms_model_last_logits(ms_model* m, float* out) {
+  if (!m || !out) return MS_ERR_INVALID_ARG;
+  MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+  MS_CUDA(m->ctx, cudaMemcpy(out, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost));
+  return MS_OK;
+}
+
+ms_status ms_model_open_gguf(ms_ctx* c, const char* path, int max_seq_len, int ep_rank, int ep_size, ms_model** out) {
+  if (!c || !path || !out || max_seq_len <= 0) return MS_ERR_INVALID_ARG;
+  *out = nullptr;
+  int fd = ::open(path, O_RDONLY);
+  if (fd < 0) return fail(c, MS_ERR_IO, "cannot open %s", path);
+  struct stat sb;
+  fstat(fd, &sb);
+  const size_t size = (size_t)sb.st_size;
+  void* map = mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+  ::close(fd);
+  if (map == MAP_FAILED) return fail(c, MS_ERR_IO, "mmap failed");
+  struct Unmap { void* p; size_t n; ~Unmap() { munmap(p, n); } } um{map, size};
+  GgufParser P{(const uint8_t*)map, size};
+  if (P.rd<uint32_t>() != 0x46554747u) return fail(c, MS_ERR_FORMAT, "invalid GGUF magic");
+  const uint32_t ver = P.rd<uint32_t>();
+  if (ver < 2 || ver > 3) return fail(c, MS_ERR_FORMAT, "unsupported GGUF version %u", ver);
+  const uint64_t nt = P.rd<uint64_t>(), nm = P.rd<uint64_t>();
+  if (nt > 1000000 || nm > 1000000) return fail(c, MS_ERR_FORMAT, "absurd tensor/metadata counts");
+  std::map<std::string, GgufMeta> meta;
+  for (uint64_t i = 0; i < nm && P.ok; ++i) {
+    std::string k = P.str();
+    GgufMeta v;
+    P.val((int)P.rd<uint32_t>(), &v);
+    meta[k] = v;
+  }
+  std::vector<std::pair<std::string, GgufT>> ts;
+  for (uint64_t i = 0; i < nt && P.ok; ++i) {
+    std::string name = P.str();
+    const uint32_t nd = P.rd<uint32_t>();
+    if (nd > 8) return fail(c, MS_ERR_FORMAT, "tensor %s: too many dims", name.c_str());
+    GgufT t;
+    std::vector<uint64_t> g(nd);
+    for (uint32_t j = 0; j < nd; ++j) g[j] = P.rd<uint64_t>();
+    for (int j = (int)nd - 1; j >= 0; --j) t.shape.push_back((int64_t)g[j]);   // TensorInfo::pt_shape
+    t.q = (int)P.rd<uint32_t>();
+    t.off = P.rd<uint64_t>();
+    int64_t n = 1;
+    for (auto x : t.shape) n *= x;
+    t.nbytes = raw_bytes(t.q, n);
+    ts.push_back({name, t});
+  }
+  if (!P.ok) return fail(c, MS_ERR_FORMAT, "truncated GGUF header");
+  uint64_t align = 32;
+  auto ai = meta.find("general.alignment");
+  if (ai != meta.end() && ai->second.i > 0) align = (uint64_t)ai->second.i;
+  const uint64_t start = (P.pos + align - 1) / align * align;
+  auto gi = [&](const std::string& k, int64_t d) { auto it = meta.find(k); return it == meta.end() ? d : it->second.i; };
+  auto gf = [&](const std::string& k, double d) {
+    auto it = meta.find(k);
+    if (it == meta.end()) return d;
+    return (it->second.type == 6 || it->second.type == 12) ? it->second.f : (double)it->second.i;
+  };
+  auto gs = [&](const std::string& k, const std::string& d) { auto it = meta.find(k); return it == meta.end() ? d : it->second.s; };
+  std::map<std::string, GgufT> tm(ts.begin(), ts.end());
+  // config.rs:253-434 keys and defaults
+  const std::string a = gs("general.architecture", "qwen2moe");
+  if (tm.count("blk.0.ssm_a") || tm.count("blk.0.ssm_conv1d.weight"))
+    return fail(c, MS_ERR_UNSUPPORTED_QTYPE, "DeltaNet hybrid models are not supported by this build");
+  ms_model_config cfg{};
+  cfg.arch = a == "gpt-oss" ? MS_ARCH_GPT_OSS : MS_ARCH_QWEN_MOE;
+  cfg.hidden = (int)gi(a + ".embedding_length", 2048);
+  cfg.layers = (int)gi(a + ".block_count", 48);
+  cfg.heads = (int)gi(a + ".attention.head_count", 16);
+  cfg.kv_heads = (int)gi(a + ".attention.head_count_kv", 2);
+  cfg.head_dim = (int)gi(a + ".attention.key_length", cfg.hidden / cfg.heads);
+  cfg.experts = (int)gi(a + ".expert_count", 128);
+  cfg.top_k = (int)gi(a + ".expert_used_count", 8);
+  cfg.rope_theta = (float)gf(a + ".rope.freq_base", 1000000.0);
+  cfg.eps = (float)gf(a + ".attention.layer_norm_rms_epsilon", 1e-6);
+  auto te = tm.find("token_embd.weight");
+  cfg.vocab = (int)gi(a + ".vocab_size", te != tm.end() ? te->second.shape[0] : 151936);
+  auto ge = tm.find("blk.0.ffn_gate_exps.weight");
+  cfg.inter = (int)gi(a + ".expert_feed_forward_length", ge != tm.end() && ge->second.shape.size() >= 3 ? ge->second.shape[1] : 768);
+  cfg.sliding_window = (int)gi(a + ".attention.sliding_window", 0);
+  double prf = gf(a + ".rope.partial_rotary_factor", -1.0);
+  if (prf < 0) {
+    const int64_t dc = gi(a + ".rope.dimension_count", -1);
+    prf = dc >= 0 ? (double)((float)dc / (float)cfg.head_dim) : 1.0;
+  }
+  cfg.rot_dim = (int)((float)cfg.head_dim * (float)prf);
+  const std::string name = gs("general.name", "");
+  cfg.norm_topk_prob = !(name.find("Qwen1.5") != std::string::npos || name.find("Qwen2") != std::string::npos);
+  cfg.max_seq_len = max_seq_len;
+  cfg.ep_rank = ep_rank;
+  cfg.ep_size = ep_size;
+  ms_model* m = nullptr;
+  ms_status s = ms_model_create(c, &cfg, &m);
+  if (s != MS_OK) return s;
+  for (auto& kv : ts) {
+    const GgufT& t = kv.second;
+    if (t.nbytes < 0) continue;   // types outside the decode path are not indexed
+    if (start + t.off + (uint64_t)t.nbytes > size) { ms_model_destroy(m); return fail(c, MS_ERR_FORMAT, "%s: out of bounds", kv.first.c_str()); }
+    s = ms_model_set_tensor(m, kv.first.c_str(), t.q, (int)t.shape.size(), t.shape.data(),
+                            (const uint8_t*)map + start + t.off, (size_t)t.nbytes);
+    if (s != MS_OK) { ms_model_destroy(m); return s; }
+  }
+  s = ms_model_finalize(m);
+  if (s != MS_OK) { ms_model_destroy(m); return s; }
+  *out = m;
+  return MS_OK;
+}
+
+}  // extern "C"

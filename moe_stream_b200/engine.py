@@ -1,0 +1,275 @@
+"""Python host API mirroring moe-stream-core's Engine and its Metal kernel seam.
+
+``Context`` wraps ``ms_ctx`` and exposes the per-dispatch kernels (the functions of
+moe-stream-core/src/metal/mod.rs the CUDA backend replaces) on device pointers, so they
+can be driven with torch CUDA tensors.  ``Engine`` wraps ``ms_model`` with the reference
+Engine's surface (model/engine.rs: ``open_with_device`` 277-598, ``preload_weights`` 1551,
+``forward`` 1869-2006, ``generate`` 2011-2118, ``clear_cache`` 2402).  All compute runs in
+the CUDA library; nothing here computes on the CPU.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import gguf as G
+from ._lib import ARCH_GPT_OSS, ARCH_QWEN_MOE, ModelConfig, check, lib
+
+
+def _ptr(t) -> int:
+    """Device pointer of a torch tensor / raw int / None."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+class Context:
+    """One GPU (``Device::new_cuda``); not thread-safe, like the reference Engine."""
+
+    def __init__(self, device: int = 0, stream=None):
+        h = C.c_void_p()
+        check(lib().ms_ctx_create(device, C.byref(h)))
+        self.h = h
+        self.device = device
+        if stream is not None:
+            self.set_stream(stream)
+
+    def set_stream(self, stream) -> None:
+        """Enqueue on a caller stream (a torch.cuda.Stream or raw cudaStream_t int)."""
+        s = getattr(stream, "cuda_stream", stream)
+        check(lib().ms_ctx_set_stream(self.h, s), self.h)
+
+    def sync(self) -> None:
+        check(lib().ms_sync(self.h), self.h)
+
+    def error_flags(self, clear: bool = True) -> int:
+        f = C.c_uint32()
+        check(lib().ms_ctx_error_flags(self.h, C.byref(f), int(clear)), self.h)
+        return f.value
+
+    @property
+    def sm_count(self) -> int:
+        return lib().ms_ctx_sm_count(self.h)
+
+    # ---- metal/mod.rs seam ----
+    def dequantize(self, qtype: int, blocks, n: int, out) -> None:
+        check(lib().ms_dequantize(self.h, qtype, _ptr(blocks), n, _ptr(out)), self.h)
+
+    def rms_norm(self, x, w, y, rows: int, dim: int, eps: float) -> None:
+        check(lib().ms_rms_norm(self.h, _ptr(x), _ptr(w), _ptr(y), rows, dim, eps), self.h)
+
+    def gemv(self, qtype: int, w, rows: int, cols: int, x, y, bias=None) -> None:
+        check(lib().ms_gemv(self.h, qtype, _ptr(w), rows, cols, _ptr(x), _ptr(bias), _ptr(y)), self.h)
+
+    def router_topk(self, h, norm_w, eps, router_w, router_b, mask, hidden, n_experts, top_k, arch,
+                    norm_topk_prob, xn, logits, idx, wts) -> None:
+        check(lib().ms_router_topk(self.h, _ptr(h), _ptr(norm_w), eps, _ptr(router_w), _ptr(router_b), _ptr(mask),
+                                   hidden, n_experts, top_k, arch, int(norm_topk_prob), _ptr(xn), _ptr(logits),
+                                   _ptr(idx), _ptr(wts)), self.h)
+
+    def moe_mxfp4_decode(self, gate, up, down, gate_b, up_b, down_b, hidden, inter, n_experts, top_k, arch,
+                         x, idx, wts, h) -> None:
+        check(lib().ms_moe_mxfp4_decode(self.h, _ptr(gate), _ptr(up), _ptr(down), _ptr(gate_b), _ptr(up_b),
+                                        _ptr(down_b), hidden, inter, n_experts, top_k, arch, _ptr(x), _ptr(idx),
+                                        _ptr(wts), _ptr(h)), self.h)
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            lib().ms_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def config_from_model(m: G.Model, max_seq_len: int, ep_rank: int = 0, ep_size: int = 1) -> ModelConfig:
+    """config.rs:253-434 for an in-memory GGUF model (same keys and defaults as the file loader)."""
+    meta = {k: v for k, (_, v) in m.metadata.items()}
+    a = meta.get("general.architecture", "qwen2moe")
+    gi = lambda k, d: int(meta.get(f"{a}.{k}", d))
+    gf = lambda k, d: float(meta.get(f"{a}.{k}", d))
+    c = ModelConfig()
+    c.arch = ARCH_GPT_OSS if a == "gpt-oss" else ARCH_QWEN_MOE
+    c.hidden = gi("embedding_length", 2048)
+    c.layers = gi("block_count", 48)
+    c.heads = gi("attention.head_count", 16)
+    c.kv_heads = gi("attention.head_count_kv", 2)
+    c.head_dim = gi("attention.key_length", c.hidden // c.heads)
+    c.experts = gi("expert_count", 128)
+    c.top_k = gi("expert_used_count", 8)
+    c.inter = gi("expert_feed_forward_length", 768)
+    c.vocab = gi("vocab_size", m.tensors["token_embd.weight"].shape[0] if "token_embd.weight" in m.tensors else 151936)
+    c.rope_theta = gf("rope.freq_base", 1e6)
+    c.eps = gf("attention.layer_norm_rms_epsilon", 1e-6)
+    c.sliding_window = gi("attention.sliding_window", 0)
+    c.rot_dim = c.head_dim
+    name = meta.get("general.name", "")
+    c.norm_topk_prob = int(not ("Qwen1.5" in name or "Qwen2" in name))
+    c.max_seq_len = max_seq_len
+    c.ep_rank, c.ep_size = ep_rank, ep_size
+    c.attn_splits = 0
+    return c
+
+
+class Engine:
+    """GPU-resident engine over one GGUF model (the reference's GpuResident mode)."""
+
+    def __init__(self, handle: C.c_void_p, ctx: Context):
+        self.h = handle
+        self.ctx = ctx
+        cfg = ModelConfig()
+        check(lib().ms_model_get_config(self.h, C.byref(cfg)), ctx.h)
+        self.config = cfg
+
+    # engine.rs:277 open_with_device
+    @classmethod
+    def open(cls, path: str, max_seq_len: int = 4096, device: int = 0, ep_rank: int = 0, ep_size: int = 1,
+             ctx: Optional[Context] = None) -> "Engine":
+        ctx = ctx or Context(device)
+        h = C.c_void_p()
+        check(lib().ms_model_open_gguf(ctx.h, path.encode(), max_seq_len, ep_rank, ep_size, C.byref(h)), ctx.h)
+        return cls(h, ctx)
+
+    @classmethod
+    def from_model(cls, m: G.Model, max_seq_len: int = 4096, device: int = 0, ep_rank: int = 0, ep_size: int = 1,
+                   ctx: Optional[Context] = None, attn_splits: int = 0) -> "Engine":
+        """Upload an in-memory GGUF model (native block layouts) without writing a file."""
+        ctx = ctx or Context(device)
+        cfg = config_from_model(m, max_seq_len, ep_rank, ep_size)
+        cfg.attn_splits = attn_splits
+        h = C.c_void_p()
+        check(lib().ms_model_create(ctx.h, C.byref(cfg), C.byref(h)), ctx.h)
+        try:
+            for name, t in m.tensors.items():
+                raw = t.raw()
+                dims = (C.c_int64 * len(t.shape))(*t.shape)
+                check(lib().ms_model_set_tensor(h, name.encode(), t.qtype, len(t.shape), dims, raw.ctypes.data,
+                                                raw.size), ctx.h)
+            check(lib().ms_model_finalize(h), ctx.h)
+        except Exception:
+            lib().ms_model_destroy(h)
+            raise
+        return cls(h, ctx)
+
+    @classmethod
+    def from_spec(cls, spec, seed: int = 0, max_seq_len: int = 4096, device: int = 0, ep_rank: int = 0,
+                  ep_size: int = 1, ctx: Optional[Context] = None, attn_splits: int = 0,
+                  progress=None) -> "Engine":
+        """Generate a seeded synthetic model tensor by tensor and upload each as it is made,
+        so host memory holds one tensor at a time (the benchmark's 13 GB GPT-OSS shape)."""
+        from . import synth
+        ctx = ctx or Context(device)
+        meta = G.Model()
+        for k, (vt, v) in synth.metadata(spec).items():
+            meta.add_meta(k, vt, v)
+        cfg = config_from_model(meta, max_seq_len, ep_rank, ep_size)
+        cfg.attn_splits = attn_splits
+        h = C.c_void_p()
+        check(lib().ms_model_create(ctx.h, C.byref(cfg), C.byref(h)), ctx.h)
+        try:
+            for name, q, shape, gen in synth.tensor_defs(spec):
+                raw = np.ascontiguousarray(gen(synth.tensor_rng(seed, name))).view(np.uint8).reshape(-1)
+                dims = (C.c_int64 * len(shape))(*shape)
+                check(lib().ms_model_set_tensor(h, name.encode(), q, len(shape), dims, raw.ctypes.data, raw.size),
+                      ctx.h)
+                if progress:
+                    progress(name)
+                del raw
+            check(lib().ms_model_finalize(h), ctx.h)
+        except Exception:
+            lib().ms_model_destroy(h)
+            raise
+        return cls(h, ctx)
+
+    def preload_weights(self) -> None:
+        """Weights are uploaded to HBM at open; nothing to preload (engine.rs:1551)."""
+
+    def warmup_gpu(self) -> None:
+        """The decode step is captured as a CUDA graph on its first run (engine.rs:1683)."""
+
+    def forward(self, tokens: Sequence[int]) -> np.ndarray:
+        """Tokens at the current position; returns the last position's logits (engine.rs:1869)."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.empty(self.config.vocab, dtype=np.float32)
+        check(lib().ms_model_forward(self.h, t.ctypes.data_as(C.POINTER(C.c_int32)), t.size,
+                                     out.ctypes.data_as(C.POINTER(C.c_float))), self.ctx.h)
+        return out
+
+    def decode_step(self, token: int) -> int:
+        nxt = C.c_int32()
+        check(lib().ms_model_decode_step(self.h, int(token), C.byref(nxt)), self.ctx.h)
+        return nxt.value
+
+    def generate(self, prompt: Sequence[int], max_new_tokens: int) -> list:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(max_new_tokens, dtype=np.int32)
+        n = C.c_int()
+        check(lib().ms_model_generate(self.h, p.ctypes.data_as(C.POINTER(C.c_int32)), p.size, max_new_tokens,
+                                      out.ctypes.data_as(C.POINTER(C.c_int32)), C.byref(n)), self.ctx.h)
+        return out[:n.value].tolist()
+
+    def decode_steps_device(self, n: int) -> None:
+        check(lib().ms_model_decode_steps_device(self.h, n), self.ctx.h)
+
+    def token_log(self) -> list:
+        cap = self.config.max_seq_len
+        out = np.empty(cap, dtype=np.int32)
+        n = C.c_int()
+        check(lib().ms_model_token_log(self.h, out.ctypes.data_as(C.POINTER(C.c_int32)), cap, C.byref(n)),
+              self.ctx.h)
+        return out[:n.value].tolist()
+
+    def clear_cache(self) -> None:
+        check(lib().ms_model_clear_cache(self.h), self.ctx.h)
+
+    @property
+    def seq_len(self) -> int:
+        n = C.c_int()
+        check(lib().ms_model_seq_len(self.h, C.byref(n)), self.ctx.h)
+        return n.value
+
+    def last_hidden(self) -> np.ndarray:
+        o = np.empty(self.config.hidden, dtype=np.float32)
+        check(lib().ms_model_last_hidden(self.h, o.ctypes.data_as(C.POINTER(C.c_float))), self.ctx.h)
+        return o
+
+    def last_routing(self, layer: int):
+        k = self.config.top_k
+        idx = np.empty(k, dtype=np.int32)
+        w = np.empty(k, dtype=np.float32)
+        check(lib().ms_model_last_routing(self.h, layer, idx.ctypes.data_as(C.POINTER(C.c_int32)),
+                                          w.ctypes.data_as(C.POINTER(C.c_float))), self.ctx.h)
+        return idx, w
+
+    def last_logits(self) -> np.ndarray:
+        o = np.empty(self.config.vocab, dtype=np.float32)
+        check(lib().ms_model_last_logits(self.h, o.ctypes.data_as(C.POINTER(C.c_float))), self.ctx.h)
+        return o
+
+    def set_graph(self, enable: bool) -> None:
+        check(lib().ms_model_set_graph(self.h, int(enable)), self.ctx.h)
+
+    @property
+    def kernels_per_step(self) -> int:
+        return lib().ms_model_kernels_per_step(self.h)
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            lib().ms_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+__all__ = ["Context", "Engine", "config_from_model", "ARCH_GPT_OSS", "ARCH_QWEN_MOE"]

@@ -88,7 +88,8 @@ def tensor_rng(seed: int, name: str) -> np.random.Generator:
 
 
 def _bytes(rng: np.random.Generator, n: int) -> np.ndarray:
-    return np.frombuffer(rng.bytes(n), dtype=np.uint8).copy()
+    """n uniform bytes from the generator's raw 64-bit stream (fast path for GB-sized tensors)."""
+    return rng.bit_generator.random_raw((n + 7) // 8).view(np.uint8)[:n].copy()
 
 
 def rand_mxfp4(rng, n_elements: int, e_lo: int = 119, e_hi: int = 123) -> np.ndarray:
@@ -106,12 +107,9 @@ def quantize_q8_0(x: np.ndarray) -> np.ndarray:
     d = (amax / np.float32(127.0)).astype(np.float32)
     with np.errstate(divide="ignore"):
         idv = np.where(d != 0, np.float32(1.0) / d, np.float32(0.0)).astype(np.float32)
-    q = np.round(x * idv[:, None]).astype(np.int8)   # round-half-to-even differs from roundf only at .5 ties
-    # ties at exactly .5 are measure-zero for Gaussian data; ggml rounds them away from zero:
-    frac = x * idv[:, None]
-    tie = np.abs(frac - np.trunc(frac)) == 0.5
-    if tie.any():
-        q = np.where(tie, (np.trunc(frac) + np.sign(frac)).astype(np.int8), q)
+    v = x * idv[:, None]
+    # roundf (half away from zero): |v| <= 127, so v + 0.5*sign(v) is exact in f32
+    q = np.trunc(v + np.copysign(np.float32(0.5), v)).astype(np.int8)
     out = np.empty((x.shape[0], 34), dtype=np.uint8)
     out[:, 0:2] = d.astype(np.float16).view(np.uint8).reshape(-1, 2)
     out[:, 2:] = q.view(np.uint8)
@@ -143,8 +141,19 @@ def rand_normal_f32(rng, n: int, std: float) -> np.ndarray:
     return rng.standard_normal(n, dtype=np.float32) * np.float32(std)
 
 
+_F16_NORMAL_TABLE = {}
+
+
 def rand_normal_f16(rng, n: int, std: float) -> np.ndarray:
-    return (rng.standard_normal(n, dtype=np.float32) * np.float32(std)).astype(np.float16)
+    """~N(0, std) in f16 by inverse-CDF sampling of 16-bit uniforms (fast for the 1.2 GB
+    embedding / LM head tables; f16 itself is coarser than the 65536 quantile levels)."""
+    tab = _F16_NORMAL_TABLE.get(std)
+    if tab is None:
+        from scipy.special import ndtri
+        u = (np.arange(65536, dtype=np.float64) + 0.5) / 65536.0
+        tab = (ndtri(u) * std).astype(np.float16)
+        _F16_NORMAL_TABLE[std] = tab
+    return tab[_bytes(rng, 2 * n).view(np.uint16)]
 
 
 def _rand_quant(rng, qtype: int, n: int) -> np.ndarray:

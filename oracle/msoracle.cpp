@@ -767,6 +767,26 @@ void orc_model_last_routing(const orc_model* m, int32_t* idx, float* w) {
   std::memcpy(idx, m->last_idx.data(), m->last_idx.size() * 4); std::memcpy(w, m->last_w.data(), m->last_w.size() * 4);
 }
 
+// engine.rs:1963-1987: final RMSNorm + LM head (f16 weights converted exactly to f32)
+static void lm_head(orc_model* m, const float* hidden, float* logits) {
+  const int H = m->hidden;
+  const int th = m->threads ? m->threads : hw_threads();
+  std::vector<float> last(H);
+  rms_norm(hidden, m->out_norm, last.data(), 1, H, m->eps);
+  const int64_t rb = raw_size(m->out->qtype, H);
+  parallel_for(m->vocab, th, [&](int64_t b, int64_t e) {
+    std::vector<float> row(H);
+    for (int64_t r = b; r < e; ++r) {
+      dequant(m->out->qtype, m->out->data + r * rb, H, row.data());
+      float acc = 0.0f;
+      for (int i = 0; i < H; ++i) acc += last[i] * row[i];
+      logits[r] = m->out_bias ? acc + m->out_bias[r] : acc;
+    }
+  });
+}
+
+void orc_model_lm_head(orc_model* m, const float* hidden, float* logits) { lm_head(m, hidden, logits); }
+
 // engine.rs:1869-2006
 int orc_model_forward(orc_model* m, const int32_t* tokens, int n, float* logits) {
   if (n <= 0 || m->seq + n > m->max_seq) return -1;
@@ -792,22 +812,8 @@ int orc_model_forward(orc_model* m, const int32_t* tokens, int n, float* logits)
     std::memcpy(&m->last_w[(size_t)li * K], &w[(size_t)(n - 1) * K], K * 4);
   }
   m->seq += n;
-  // final norm + LM head (f16 weights converted exactly to f32; last position only is needed)
-  std::vector<float> last(H);
-  rms_norm(&h[(size_t)(n - 1) * H], m->out_norm, last.data(), 1, H, m->eps);
   m->last_hidden.assign(h.end() - H, h.end());
-  if (logits) {
-    const int64_t rb = raw_size(m->out->qtype, H);
-    parallel_for(m->vocab, th, [&](int64_t b, int64_t e) {
-      std::vector<float> row(H);
-      for (int64_t r = b; r < e; ++r) {
-        dequant(m->out->qtype, m->out->data + r * rb, H, row.data());
-        float acc = 0.0f;
-        for (int i = 0; i < H; ++i) acc += last[i] * row[i];
-        logits[r] = m->out_bias ? acc + m->out_bias[r] : acc;
-      }
-    });
-  }
+  if (logits) lm_head(m, m->last_hidden.data(), logits);
   return 0;
 }
 

@@ -88,6 +88,8 @@ void orc_model_clear_cache(orc_model* m);
 void orc_model_last_hidden(const orc_model* m, float* out);
 /* routed experts of the last position per layer [layers*k] */
 void orc_model_last_routing(const orc_model* m, int32_t* idx, float* w);
+/* final norm + LM head of one hidden vector [hidden] -> logits [vocab] (timing / tests) */
+void orc_model_lm_head(orc_model* m, const float* hidden, float* logits);
 void orc_model_destroy(orc_model* m);
 
 #ifdef __cplusplus

@@ -71,6 +71,7 @@ def lib():
         L.orc_model_clear_cache.argtypes = [_vp]
         L.orc_model_last_hidden.argtypes = [_vp, _fp]
         L.orc_model_last_routing.argtypes = [_vp, _i32p, _fp]
+        L.orc_model_lm_head.argtypes = [_vp, _fp, _fp]
         L.orc_model_destroy.argtypes = [_vp]
         _lib = L
     return _lib
@@ -227,6 +228,12 @@ class Model:
         o = np.empty(self.hidden, dtype=np.float32)
         lib().orc_model_last_hidden(self.h, _f(o))
         return o
+
+    def lm_head(self, hidden: np.ndarray) -> np.ndarray:
+        hidden = np.ascontiguousarray(hidden, dtype=np.float32)
+        out = np.empty(self.vocab, dtype=np.float32)
+        lib().orc_model_lm_head(self.h, _f(hidden), _f(out))
+        return out
 
     def clear_cache(self):
         lib().orc_model_clear_cache(self.h)
