@@ -221,19 +221,21 @@ def run_ours(args):
     from moe_stream_b200.engine import Context, Engine
 
     spec = synth.GPT_OSS_20B
-    max_seq = PROMPT + args.warmup + 2 * args.steps + 64
+    prompt_len = args.prompt
+    max_seq = prompt_len + args.warmup + 2 * args.steps + 64
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     t0 = time.time()
     ctx = Context(local)
+    ctx.set_stream(stream)
     eng = Engine.from_spec(spec, seed=0, max_seq_len=max_seq, ctx=ctx)
     log(f"[rank {rank}] model generated + uploaded in {time.time() - t0:.1f}s")
-    prompt = synth.prompt_ids(spec, PROMPT, seed=0)
+    prompt = synth.prompt_ids(spec, prompt_len, seed=0)
     t0 = time.time()
     eng.forward(prompt)
-    log(f"[rank {rank}] prefill {PROMPT} tokens (one decode step per token) in {time.time() - t0:.1f}s")
+    log(f"[rank {rank}] prefill {prompt_len} tokens (one decode step per token) in {time.time() - t0:.1f}s")
 
     # ---- device-resident decode: warmup, then K timed steps ----
-    ctx.set_stream(torch.cuda.current_stream())
-    stream = torch.cuda.current_stream()
     eng.decode_steps_device(args.warmup)
     torch.cuda.synchronize()
     if ws > 1:
@@ -255,12 +257,14 @@ def run_ours(args):
     ctx.sync()
 
     # ---- end to end through the C ABI with host buffers ----
-    tok = eng.decode_step(int(prompt[-1]))
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        tok = eng.decode_step(tok)
-    e2e_s = time.perf_counter() - t0
+    e2e_s = float("nan")
+    if not args.no_e2e:
+        tok = eng.decode_step(int(prompt[-1]))
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            tok = eng.decode_step(tok)
+        e2e_s = time.perf_counter() - t0
     if ws > 1:
         t = torch.tensor([e2e_s], device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -268,9 +272,9 @@ def run_ours(args):
     eng.close()
 
     # ---- roofline of the dominant kernel pair (MXFP4 expert FFN) ----
-    moe_ms, moe_launches = moe_roofline(torch, ctx)
+    moe_ms, moe_launches = moe_roofline(torch, ctx) if not args.no_roofline else (float("nan"), 0)
     peak, peak_kind = peaks()
-    achieved = MOE_BYTES / (moe_ms * 1e-3) / 1e9
+    achieved = MOE_BYTES / (moe_ms * 1e-3) / 1e9 if moe_ms == moe_ms else float("nan")
     traffic = None
     tp = os.path.join(ROOT, "profiles", "moe_mxfp4_traffic.json")
     if os.path.exists(tp):
@@ -290,9 +294,9 @@ def run_ours(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "f32 (MXFP4/Q8_0/f16 weights, f32 activations and KV)",
         "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
         "config": {"workload": "GPT-OSS-20B-shaped MXFP4 greedy decode, bs1, after a 2048-token prompt",
-                   "model": "gpt-oss-20b-shaped", "global_batch": ws, "seq_len": PROMPT, "parallelism": f"replicas{ws}",
+                   "model": "gpt-oss-20b-shaped", "global_batch": ws, "seq_len": prompt_len, "parallelism": f"replicas{ws}",
                    "l2": "no flush: each step streams ~3.1 GB of weights (> 126 MB L2)"},
-        "e2e": {"value": round(ws * args.steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 + 4,
+        "e2e": {"value": round(ws * args.steps / e2e_s, 2) if e2e_s == e2e_s else None, "unit": "tok/s", "h2d_bytes_per_step": 4 + 4,
                 "d2h_bytes_per_step": 8},
         "roofline": {"kernel": "moe_mxfp4 gate_up+down (config-0 shape, one token-layer)", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -308,6 +312,16 @@ def run_ours(args):
         torch.distributed.destroy_process_group()
 
 
+def run_case_moe(args):
+    """Small profiling case: the config-0 MoE layer (gate/up + down kernels) only, ~1.7 GB."""
+    import torch
+    from moe_stream_b200.engine import Context
+    ctx = Context(0)
+    ms, _ = moe_roofline(torch, ctx, iters=max(1, args.steps))
+    print(json.dumps({"case": "moe-layer", "us_per_launch_pair": round(ms * 1000, 2),
+                      "achieved_gbs": round(MOE_BYTES / (ms * 1e-3) / 1e9, 1)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -316,10 +330,16 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--steps-ref", type=int, default=3, help="timed tokens of the CPU sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--no-roofline", action="store_true", help="skip the expert-FFN roofline leg")
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (default 2048)")
+    ap.add_argument("--case", default=None, choices=[None, "moe-layer"], help="small profiling case")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.case == "moe-layer":
+        run_case_moe(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -69,8 +69,10 @@ MS_API const char* ms_status_string(ms_status s);
 /* ---- context (replaces Device::new_metal, engine.rs:277-298) ---- */
 MS_API ms_status ms_ctx_create(int device, ms_ctx** out);
 MS_API ms_status ms_ctx_destroy(ms_ctx* ctx);
-/* Enqueue work on a caller-owned cudaStream_t (NULL restores the context's own stream). */
+/* Enqueue work on a caller-owned cudaStream_t (NULL = the legacy default stream). */
 MS_API ms_status ms_ctx_set_stream(ms_ctx* ctx, void* cuda_stream);
+/* Enqueue work on the context's own non-blocking stream (the default after ms_ctx_create). */
+MS_API ms_status ms_ctx_use_own_stream(ms_ctx* ctx);
 /* Wait for the stream; reports MS_ERR_TIMEOUT / MS_ERR_DEVICE_INDEX raised by device code. */
 MS_API ms_status ms_sync(ms_ctx* ctx);
 MS_API const char* ms_last_error(const ms_ctx* ctx);

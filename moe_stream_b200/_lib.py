@@ -47,6 +47,7 @@ _SIGS = {
     "ms_ctx_create": (C.c_int, [C.c_int, C.POINTER(_vp)]),
     "ms_ctx_destroy": (C.c_int, [_vp]),
     "ms_ctx_set_stream": (C.c_int, [_vp, _vp]),
+    "ms_ctx_use_own_stream": (C.c_int, [_vp]),
     "ms_sync": (C.c_int, [_vp]),
     "ms_last_error": (C.c_char_p, [_vp]),
     "ms_ctx_error_flags": (C.c_int, [_vp, C.POINTER(C.c_uint32), C.c_int]),

@@ -362,10 +362,14 @@ ms_status run_step(ms_model* m) {
   cudaStream_t s = m->ctx->stream;
   if (!m->use_graph) return enqueue_step(m, s);
   if (!m->graph) {
+    // capture on the context's private stream (the caller's stream may be the legacy default
+    // stream, which cannot be captured); the graph is then launched on the caller's stream
     cudaGraph_t g = nullptr;
-    MS_CUDA(m->ctx, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-    ms_status st = enqueue_step(m, s);
-    cudaError_t e = cudaStreamEndCapture(s, &g);
+    cudaStream_t cs = m->ctx->own;
+    MS_CUDA(m->ctx, cudaStreamSynchronize(s));
+    MS_CUDA(m->ctx, cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    ms_status st = enqueue_step(m, cs);
+    cudaError_t e = cudaStreamEndCapture(cs, &g);
     if (st != MS_OK) { if (g) cudaGraphDestroy(g); return st; }
     if (e != cudaSuccess) return cuda_fail(m->ctx, e, "cudaStreamEndCapture");
     e = cudaGraphInstantiate(&m->graph, g, 0);
@@ -476,7 +480,13 @@ ms_status ms_ctx_destroy(ms_ctx* c) {
 
 ms_status ms_ctx_set_stream(ms_ctx* c, void* stream) {
   if (!c) return MS_ERR_INVALID_ARG;
-  c->stream = stream ? (cudaStream_t)stream : c->own;
+  c->stream = stream ? (cudaStream_t)stream : cudaStreamLegacy;   // NULL: the legacy default stream
+  return MS_OK;
+}
+
+ms_status ms_ctx_use_own_stream(ms_ctx* c) {
+  if (!c) return MS_ERR_INVALID_ARG;
+  c->stream = c->own;
   return MS_OK;
 }
 
