@@ -117,13 +117,23 @@ __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
   return out;
 }
 
+// the four bytes of w (byte i = e2m1 pair i) -> four f16x2 registers
+__device__ __forceinline__ void e2m1x8_to_f16x2x4(uint32_t w, uint32_t& o0, uint32_t& o1, uint32_t& o2,
+                                                  uint32_t& o3) {
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}\n"
+      : "=r"(o0), "=r"(o1), "=r"(o2), "=r"(o3)
+      : "r"(w));
+}
+
 __device__ __forceinline__ uint32_t pack_half2(__half lo, __half hi) {
   return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
 }
 
 // D += A(16x16, f16, row) * B(16x8, f16, col); f32 accumulators.
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

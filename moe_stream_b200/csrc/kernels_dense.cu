@@ -10,6 +10,8 @@
 //   embedding + final norm + LM head + greedy argmax ... model/engine.rs:1877, 1963-1987, 2069-2077
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -199,15 +201,41 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
     for (int w = 0; w < kQW; ++w) t += red[w];
     inv = 1.0f / sqrtf(t / (float)p.cols + p.eps);
   }
-  for (int i = threadIdx.x; i < p.cols; i += nct) xf[i] = p.norm_w ? (p.x[i] * inv) * p.norm_w[i] : p.x[i];
-  named_bar(1, nct);
-  for (int b = warp; b < nb; b += kQW) {   // one warp per 32-element block
-    const float v = xf[32 * b + lane];
-    const float amax = warp_max(fabsf(v));
+  // one thread per 32-element block: (RMSNorm) -> Q8_0 (d = amax/127 as f16, q = roundf(x/d))
+  for (int b = threadIdx.x; b < nb; b += nct) {
+    float v[32];
+    const float4* x4 = reinterpret_cast<const float4*>(p.x + 32 * b);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float4 t = x4[k];
+      v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
+    }
+    if (p.norm_w) {
+      const float4* w4 = reinterpret_cast<const float4*>(p.norm_w + 32 * b);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float4 t = w4[k];
+        v[4 * k] = (v[4 * k] * inv) * t.x; v[4 * k + 1] = (v[4 * k + 1] * inv) * t.y;
+        v[4 * k + 2] = (v[4 * k + 2] * inv) * t.z; v[4 * k + 3] = (v[4 * k + 3] * inv) * t.w;
+      }
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) amax = fmaxf(amax, fabsf(v[k]));
     const float d = amax / 127.0f;
     const float id = d != 0.0f ? 1.0f / d : 0.0f;
-    xq[32 * b + lane] = (int8_t)roundf(v * id);
-    if (lane == 0) xd[b] = __half2float(__float2half_rn(d));
+    int qw[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      uint32_t u = 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) u |= ((uint32_t)(uint8_t)(int8_t)roundf(v[4 * k + q] * id)) << (8 * q);
+      qw[k] = (int)u;
+    }
+    int4* dst = reinterpret_cast<int4*>(xq + 32 * b);
+    dst[0] = make_int4(qw[0], qw[1], qw[2], qw[3]);
+    dst[1] = make_int4(qw[4], qw[5], qw[6], qw[7]);
+    xd[b] = __half2float(__float2half_rn(d));
   }
   named_bar(1, nct);
   int xr[NBL][8];
@@ -365,17 +393,18 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
 
   for (int t0 = p0; t0 < p1; t0 += kAT) {
     const int tn = min(kAT, p1 - t0);
-    for (int i = threadIdx.x; i < tn * hd; i += blockDim.x) {
-      const int j = i / hd, d = i - j * hd, p = t0 + j;
-      float kv, vv;
-      if (p == pos) { kv = kn[d]; vv = vn[d]; }
+    const int hd4 = hd / 4;
+    for (int i = threadIdx.x; i < tn * hd4; i += blockDim.x) {
+      const int j = i / hd4, d = (i - j * hd4) * 4, p = t0 + j;
+      float4 kv, vv;
+      if (p == pos) { kv = make_float4(kn[d], kn[d + 1], kn[d + 2], kn[d + 3]); vv = make_float4(vn[d], vn[d + 1], vn[d + 2], vn[d + 3]); }
       else {
         const int slot = a.window ? p % a.cap : p;
-        kv = a.kc[((size_t)kh * a.cap + slot) * hd + d];
-        vv = a.vc[((size_t)kh * a.cap + slot) * hd + d];
+        kv = *reinterpret_cast<const float4*>(a.kc + ((size_t)kh * a.cap + slot) * hd + d);
+        vv = *reinterpret_cast<const float4*>(a.vc + ((size_t)kh * a.cap + slot) * hd + d);
       }
-      kt[j * hdp + d] = kv;
-      vt[j * hd + d] = vv;
+      kt[j * hdp + d] = kv.x; kt[j * hdp + d + 1] = kv.y; kt[j * hdp + d + 2] = kv.z; kt[j * hdp + d + 3] = kv.w;
+      *reinterpret_cast<float4*>(vt + j * hd + d) = vv;
     }
     __syncthreads();
     for (int i = threadIdx.x; i < rep * kAT; i += blockDim.x) {
@@ -427,31 +456,46 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
   __syncthreads();
   if (!last) return;
   __threadfence();
-  // merge the splits of this kv group (+ attention sink in the denominator)
+  // merge the splits of this kv group (+ attention sink in the denominator): stage every
+  // split's (m, l) in shared memory, form per-split weights, then a parallel weighted sum
   const float* gp = a.part + (size_t)kh * S * rep * (hd + 2);
-  for (int h = warp; h < rep; h += nwarp) {
-    const int hq = kh * rep + h;
+  float* wsm = sm;                      // [S][rep] split weights (reuses the tile area)
+  float* hm = sm + S * rep;             // [rep] merged max
+  float* hinv = hm + rep;               // [rep] 1 / denominator
+  for (int i = threadIdx.x; i < S * rep; i += blockDim.x) wsm[i] = __ldcg(&gp[(size_t)i * (hd + 2)]);
+  __syncthreads();
+  for (int h = threadIdx.x; h < rep; h += blockDim.x) {
     float M = -INFINITY;
-    for (int s = lane; s < S; s += 32) M = fmaxf(M, __ldcg(&gp[((size_t)s * rep + h) * (hd + 2)]));
-    M = warp_max(M);
+    for (int s = 0; s < S; ++s) M = fmaxf(M, wsm[s * rep + h]);
     float sink = 0.f;
-    if (a.sinks) { sink = a.sinks[hq]; M = 0.5f * ((M + sink) + fabsf(M - sink)); }
+    if (a.sinks) { sink = a.sinks[kh * rep + h]; M = 0.5f * ((M + sink) + fabsf(M - sink)); }
     float L = 0.f;
-    for (int s = lane; s < S; s += 32) {
-      const float m = __ldcg(&gp[((size_t)s * rep + h) * (hd + 2)]);
+    for (int s = 0; s < S; ++s) {
+      const float m = wsm[s * rep + h];
       if (m != -INFINITY) L += __ldcg(&gp[((size_t)s * rep + h) * (hd + 2) + 1]) * expf(m - M);
     }
-    L = warp_sum(L);
     if (a.sinks) L += expf(sink - M);
-    const float invL = 1.0f / L;
-    for (int d = lane; d < hd; d += 32) {
-      float o = 0.f;
-      for (int s = 0; s < S; ++s) {
-        const float m = __ldcg(&gp[((size_t)s * rep + h) * (hd + 2)]);
-        if (m != -INFINITY) o += __ldcg(&gp[((size_t)s * rep + h) * (hd + 2) + 2 + d]) * expf(m - M);
-      }
-      a.out[(size_t)hq * hd + d] = o * invL;
+    hm[h] = M;
+    hinv[h] = 1.0f / L;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < S * rep; i += blockDim.x) {
+    const int h = i % rep;
+    const float m = wsm[i];
+    wsm[i] = (m == -INFINITY) ? 0.f : expf(m - hm[h]) * hinv[h];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < rep * hd; i += blockDim.x) {
+    const int h = i / hd, d = i - h * hd;
+    const float* src = gp + (size_t)h * (hd + 2) + 2 + d;
+    float o0 = 0.f, o1 = 0.f;
+    int s = 0;
+    for (; s + 1 < S; s += 2) {
+      o0 = fmaf(wsm[s * rep + h], __ldcg(src + (size_t)s * rep * (hd + 2)), o0);
+      o1 = fmaf(wsm[(s + 1) * rep + h], __ldcg(src + (size_t)(s + 1) * rep * (hd + 2)), o1);
     }
+    if (s < S) o0 = fmaf(wsm[s * rep + h], __ldcg(src + (size_t)s * rep * (hd + 2)), o0);
+    a.out[(size_t)(kh * rep + h) * hd + d] = o0 + o1;
   }
   if (threadIdx.x == 0) a.cnt[kh] = 0u;
 }
@@ -637,8 +681,9 @@ cudaError_t launch_q8_gemv(const DevCtx& c, const Q8GemvArgs& a, cudaStream_t s)
 cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s) {
   if (a.nkv <= 0 || a.nh % a.nkv || a.hd % 4 || a.S <= 0 || a.rot > a.hd || a.rot % 2) return cudaErrorInvalidValue;
   const int rep = a.nh / a.nkv, hd = a.hd;
-  const size_t smem = sizeof(float) * ((size_t)rep * hd + kAT * (hd + 1) + kAT * hd + rep * kAT + rep * hd +
-                                       3 * rep + 2 * hd);
+  size_t smem = sizeof(float) * ((size_t)rep * hd + kAT * (hd + 1) + kAT * hd + rep * kAT + rep * hd +
+                                 3 * rep + 2 * hd);
+  smem = std::max(smem, sizeof(float) * ((size_t)a.S * rep + 2 * rep));
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;

@@ -22,22 +22,23 @@
 namespace ms {
 namespace {
 
-constexpr int kCW = 8;                    // consumer warps
+constexpr int kCW = 16;                   // consumer warps
 constexpr int kThreads = (kCW + 1) * 32;  // + one producer warp
 constexpr int kMaxK = 16;                 // max experts per token
 constexpr int kMaxStages = 8;
+constexpr int kRedRows = 32;              // per-warp partial sums per item (RT=2 gate/up: 16 gate + 16 up)
 
 enum { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_PLAIN = 2 };
 
 struct PhaseParams {
   int mode;
-  const uint8_t* w0;       // gate (GATEUP) or down (DOWN), stacked [E_local, rows, cols]
+  const uint8_t* w0;       // gate (GATEUP) or down (DOWN/PLAIN), stacked [E_local, rows, cols]
   const uint8_t* w1;       // up (GATEUP)
   int64_t expert_stride;   // bytes per expert matrix
   int rb;                  // bytes per streamed row
   int cols;                // reduction length (H for GATEUP, I for DOWN)
   int rows;                // rows per expert matrix (I for GATEUP, H for DOWN)
-  int tile_rows;           // rows of the matrix per item: 8 (GATEUP: +8 up rows) or 16 (DOWN)
+  int tile_rows;           // output rows per item (16)
   int n_tiles;
   int stage_bytes;
   int ns;
@@ -64,46 +65,45 @@ struct SlotInfo {
   int expert[kMaxK];       // local expert index
 };
 
-// one (row pair) x (32-column block): A rows = (row0, row1) of the thread's MMA rows.
+// One 32-column block of two MMA rows (row0, row1 of this thread): A from the e2m1 codes of
+// both rows, B = the block's (x_hi, x_lo) fragments; the block dot is scaled by 2^(E-127+kb).
 __device__ __forceinline__ void mx_block(const uint8_t* st, uint32_t off0, uint32_t off1, const uint32_t (&bf)[4],
-                                         int kb, int c, float& acc0, float& acc1) {
+                                         int kbs, int c, float& acc0, float& acc1) {
   const uint32_t w0 = lds_u32_unaligned(st, off0 + 1 + 4 * c);
   const uint32_t w1 = lds_u32_unaligned(st, off1 + 1 + 4 * c);
   const int e0 = st[off0], e1 = st[off1];
-  uint32_t a[4];
+  uint32_t a0[4], a1[4];
+  uint32_t g0, g1, g2, g3, u0, u1, u2, u3;
+  e2m1x8_to_f16x2x4(w0, g0, g1, g2, g3);
+  e2m1x8_to_f16x2x4(w1, u0, u1, u2, u3);
+  a0[0] = g0; a0[1] = u0; a0[2] = g1; a0[3] = u1;
+  a1[0] = g2; a1[1] = u2; a1[2] = g3; a1[3] = u3;
   float d[4] = {0.f, 0.f, 0.f, 0.f};
-  a[0] = e2m1x2_to_f16x2(w0);
-  a[1] = e2m1x2_to_f16x2(w1);
-  a[2] = e2m1x2_to_f16x2(w0 >> 8);
-  a[3] = e2m1x2_to_f16x2(w1 >> 8);
-  mma_f16_16816(d, a, bf[0], bf[1]);
-  a[0] = e2m1x2_to_f16x2(w0 >> 16);
-  a[1] = e2m1x2_to_f16x2(w1 >> 16);
-  a[2] = e2m1x2_to_f16x2(w0 >> 24);
-  a[3] = e2m1x2_to_f16x2(w1 >> 24);
-  mma_f16_16816(d, a, bf[2], bf[3]);
-  // weight = e2m1 * 2^(E-127); x = x' * 2^kb  ->  scale 2^(E-127+kb): exponent field E+kb
-  const int f0 = min(max(e0 + kb, 0), 255), f1 = min(max(e1 + kb, 0), 255);
-  acc0 = fmaf(__uint_as_float((uint32_t)f0 << 23), d[0] + d[1], acc0);
-  acc1 = fmaf(__uint_as_float((uint32_t)f1 << 23), d[2] + d[3], acc1);
+  mma_f16_16816(d, a0, bf[0], bf[1]);
+  mma_f16_16816(d, a1, bf[2], bf[3]);
+  // weight = e2m1 * 2^(E-127); x = x' * 2^kb: scale bits = (E + kb) << 23 (kbs = kb << 23)
+  const float s0 = __int_as_float(max(e0 * 8388608 + kbs, 0));
+  const float s1 = __int_as_float(max(e1 * 8388608 + kbs, 0));
+  acc0 = fmaf(s0, d[0] + d[1], acc0);
+  acc1 = fmaf(s1, d[2] + d[3], acc1);
 }
 
 // B fragments of the activation vector for the K-blocks this warp owns.
 template <int NBW>
 __device__ __forceinline__ void build_bfrag(const float* __restrict__ x, int nb, int warp, int lane,
-                                            uint32_t (&bf)[NBW][4], int (&kb)[NBW]) {
+                                            uint32_t (&bf)[NBW][4], int (&kbs)[NBW]) {
   const int c = lane & 3, n = lane >> 2;
 #pragma unroll
   for (int i = 0; i < NBW; ++i) {
     const int b = warp + kCW * i;
     bf[i][0] = bf[i][1] = bf[i][2] = bf[i][3] = 0u;
-    kb[i] = 0;
+    kbs[i] = 0;
     if (b < nb) {
       const float v = x[32 * b + lane];
       const float m = warp_max(fabsf(v));
       const int ef = (int)((__float_as_uint(m) >> 23) & 0xffu);
       const int k = (m > 0.f) ? (ef - 126) : 0;              // m * 2^-k in [0.5, 1)
-      kb[i] = k;
+      kbs[i] = k * 8388608;
       const float sc = __uint_as_float((uint32_t)(127 - k) << 23);
       if (n < 2) {
         const float4 lo4 = *reinterpret_cast<const float4*>(x + 32 * b + 4 * c);
@@ -133,14 +133,72 @@ __device__ __forceinline__ float swiglu_oai(float g, float u) {
 }
 __device__ __forceinline__ float silu_mul(float g, float u) { return (g / (1.0f + expf(-g))) * u; }
 
-template <int NBW>
+// Epilogue of one item, run by the last consumer warp to finish it.
+__device__ __forceinline__ void item_epilogue(const PhaseParams& p, const SlotInfo* si, const float* red, int ls,
+                                              int t, int lane) {
+  const int slot = si->slot[ls], e = si->expert[ls];
+  if (p.mode == MODE_GATEUP) {
+    // red[w][0..15] gate rows, red[w][16..31] up rows of output rows t*16 + 0..15
+    const int r = t * 16 + (lane & 15);
+    float sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCW; ++w) sum += red[w * kRedRows + lane];
+    const float* bias = lane < 16 ? p.bias0 : p.bias1;
+    if (bias) sum += bias[(size_t)e * p.rows + r];
+    const float up = __shfl_down_sync(0xffffffffu, sum, 16);
+    if (lane < 16) p.act[(size_t)slot * p.rows + r] = p.oai ? swiglu_oai(sum, up) : silu_mul(sum, up);
+    return;
+  }
+  float sum = 0.f;
+  if (lane < 16) {
+#pragma unroll
+    for (int w = 0; w < kCW; ++w) sum += red[w * kRedRows + lane];
+  }
+  const int r = t * 16 + lane;
+  if (p.mode == MODE_PLAIN) {
+    if (lane < 16 && r < p.rows) {
+      if (p.bias0) sum += p.bias0[r];
+      p.out[r] = p.accumulate ? p.out[r] + sum : sum;
+    }
+    return;
+  }
+  // DOWN: per-slot partial rows; the last CTA to finish a tile combines the slots in
+  // ascending expert order (layer.rs:1797-1847) and adds into the residual stream.
+  if (lane < 16) {
+    if (p.bias0) sum += p.bias0[(size_t)e * p.rows + r];
+    p.partial[(size_t)slot * p.rows + r] = sum;
+  }
+  __threadfence();
+  __syncwarp();
+  uint32_t old = 0;
+  if (lane == 0) old = atomicAdd(&p.tile_cnt[t], 1u);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  if (old == (uint32_t)(si->n - 1)) {
+    __threadfence();
+    if (lane < 16) {
+      float acc = 0.f;
+      for (int q = 0; q < si->n; ++q) {
+        const int sl = si->slot[q];
+        acc += __ldcg(&p.partial[(size_t)sl * p.rows + r]) * p.wts[sl];
+      }
+      if (p.out) p.out[r] = acc;
+      else p.h[r] = p.h[r] + acc;
+    }
+    if (lane == 0) p.tile_cnt[t] = 0u;
+  }
+}
+
+// RT = MMA row tiles per item: 2 for GATEUP (16 gate + 16 up rows), 1 for DOWN / PLAIN (16 rows).
+template <int NBW, int RT>
 __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
-  float* red = reinterpret_cast<float*>(smem + (size_t)p.ns * p.stage_bytes);  // [2][kCW][16]
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * kCW * 16);
+  const int nrb = p.ns + 1;   // reduction buffers: warps run at most ns items apart
+  float* red = reinterpret_cast<float*>(smem + (size_t)p.ns * p.stage_bytes);       // [nrb][kCW][kRedRows]
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + (size_t)nrb * kCW * kRedRows);
   uint64_t* empty = full + kMaxStages;
-  SlotInfo* si = reinterpret_cast<SlotInfo*>(empty + kMaxStages);
+  uint32_t* red_cnt = reinterpret_cast<uint32_t*>(empty + kMaxStages);                // [kMaxStages + 1]
+  SlotInfo* si = reinterpret_cast<SlotInfo*>(red_cnt + kMaxStages + 1);
   int* abort_flag = reinterpret_cast<int*>(si + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -167,6 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
     }
     si->n = n;
     *abort_flag = 0;
+    for (int b = 0; b <= kMaxStages; ++b) red_cnt[b] = 0u;
     for (int s = 0; s < p.ns; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kCW);
@@ -185,18 +244,18 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
     // ---------------- producer ----------------
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
-      const uint32_t half_bytes = (uint32_t)(p.tile_rows * p.rb);
+      const uint32_t part_bytes = (uint32_t)(p.tile_rows * p.rb);
       int issued = 0;
       for (int j = 0; j < my_n; ++j) {
         const int s = j % p.ns, n = j / p.ns;
         if (n > 0 && !mbar_wait(&empty[s], (uint32_t)((n - 1) & 1), p.err, EF_TIMEOUT_EMPTY)) break;
         const int item = begin + j;
         const int ls = item / p.n_tiles, t = item % p.n_tiles;
-        const int64_t base = (int64_t)si->expert[ls] * p.expert_stride + (int64_t)t * half_bytes;
+        const int64_t base = (int64_t)si->expert[ls] * p.expert_stride + (int64_t)t * part_bytes;
         uint8_t* dst = stages + (size_t)s * p.stage_bytes;
         mbar_expect_tx(&full[s], (uint32_t)p.stage_bytes);
-        bulk_g2s_stream(dst, p.w0 + base, half_bytes, &full[s], pol);
-        if (p.mode == MODE_GATEUP) bulk_g2s_stream(dst + half_bytes, p.w1 + base, half_bytes, &full[s], pol);
+        bulk_g2s_stream(dst, p.w0 + base, part_bytes, &full[s], pol);
+        if (p.mode == MODE_GATEUP) bulk_g2s_stream(dst + part_bytes, p.w1 + base, part_bytes, &full[s], pol);
         ++issued;
       }
       // make sure no copy into this CTA's shared memory is still in flight at exit
@@ -210,154 +269,181 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
   const int nb = p.cols / 32;
   const int c = lane & 3, g = lane >> 2;
   uint32_t bf[NBW][4];
-  int kb[NBW];
+  int kbs[NBW];
+  // this thread's two MMA rows per row tile (byte offsets of row starts in the stage)
+  uint32_t off0[RT], off1[RT];
+#pragma unroll
+  for (int q = 0; q < RT; ++q) {
+    if (p.mode == MODE_GATEUP) {
+      off0[q] = (uint32_t)(8 * q + g) * p.rb;           // gate row
+      off1[q] = (uint32_t)(16 + 8 * q + g) * p.rb;      // up row of the same output row
+    } else {
+      off0[q] = (uint32_t)(16 * q + g) * p.rb;
+      off1[q] = (uint32_t)(16 * q + g + 8) * p.rb;
+    }
+  }
   int cur_slot = -1;
   for (int j = 0; j < my_n; ++j) {
+    if (*reinterpret_cast<volatile int*>(abort_flag)) break;
     const int s = j % p.ns, n = j / p.ns;
     const int item = begin + j;
     const int ls = item / p.n_tiles, t = item % p.n_tiles;
-    const int slot = si->slot[ls];
-    const int x_slot = (p.mode == MODE_GATEUP) ? 0 : slot;
+    const int x_slot = (p.mode == MODE_GATEUP) ? 0 : si->slot[ls];
     if (x_slot != cur_slot) {
-      build_bfrag<NBW>(p.x + (size_t)x_slot * (p.mode == MODE_GATEUP ? 0 : p.cols), nb, warp, lane, bf, kb);
+      build_bfrag<NBW>(p.x + (size_t)x_slot * (p.mode == MODE_GATEUP ? 0 : p.cols), nb, warp, lane, bf, kbs);
       cur_slot = x_slot;
     }
-    float acc0 = 0.f, acc1 = 0.f;
-    const bool ok = mbar_wait(&full[s], (uint32_t)(n & 1), p.err, EF_TIMEOUT_FULL);
-    if (ok) {
-      const uint8_t* st = stages + (size_t)s * p.stage_bytes;
-      const uint32_t row0 = (uint32_t)g * p.rb;
-      const uint32_t row1 = (p.mode == MODE_GATEUP) ? (uint32_t)(8 + g) * p.rb : (uint32_t)(g + 8) * p.rb;
+    float acc0[RT], acc1[RT];
 #pragma unroll
-      for (int i = 0; i < NBW; ++i) {
-        const int b = warp + kCW * i;
-        if (b < nb) mx_block(st, row0 + 17u * b, row1 + 17u * b, bf[i], kb[i], c, acc0, acc1);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-    } else if (lane == 0) {
-      atomicExch(abort_flag, 1);
+    for (int q = 0; q < RT; ++q) acc0[q] = acc1[q] = 0.f;
+    if (!mbar_wait(&full[s], (uint32_t)(n & 1), p.err, EF_TIMEOUT_FULL)) {
+      if (lane == 0) atomicExch(abort_flag, 1);
+      break;
     }
-    float* rb = red + (j & 1) * kCW * 16 + warp * 16;
+    const uint8_t* st = stages + (size_t)s * p.stage_bytes;
+#pragma unroll
+    for (int i = 0; i < NBW; ++i) {
+      const int b = warp + kCW * i;
+      if (b < nb) {
+#pragma unroll
+        for (int q = 0; q < RT; ++q) mx_block(st, off0[q] + 17u * b, off1[q] + 17u * b, bf[i], kbs[i], c, acc0[q], acc1[q]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);   // stage data no longer needed by this warp
+    // partial sums -> reduction buffer; the last warp to arrive runs the item's epilogue
+    const int rbuf = j % nrb;
+    float* rw = red + ((size_t)rbuf * kCW + warp) * kRedRows;
     if (c == 0) {
-      rb[g] = acc0;
-      rb[g + 8] = acc1;
-    }
-    named_bar(1, kCW * 32);
-    if (*abort_flag) break;
-    if (warp == 0 && lane < 16) {
-      const float* r0 = red + (j & 1) * kCW * 16;
-      float sum = 0.f;
 #pragma unroll
-      for (int w = 0; w < kCW; ++w) sum += r0[w * 16 + lane];
-      const int e = si->expert[ls];
-      if (p.mode == MODE_GATEUP) {
-        // lanes 0..7: gate rows, lanes 8..15: up rows of the same 8 output rows
-        const int r = t * 8 + (lane & 7);
-        const float* bias = lane < 8 ? p.bias0 : p.bias1;
-        if (bias) sum += bias[(size_t)e * p.rows + r];
-        const float other = __shfl_down_sync(0x0000ffffu, sum, 8);
-        if (lane < 8) p.act[(size_t)slot * p.rows + r] = p.oai ? swiglu_oai(sum, other) : silu_mul(sum, other);
-      } else if (p.mode == MODE_PLAIN) {
-        const int r = t * 16 + lane;
-        if (r < p.rows) {
-          if (p.bias0) sum += p.bias0[r];
-          p.out[r] = p.accumulate ? p.out[r] + sum : sum;
-        }
-      } else {
-        const int r = t * 16 + lane;
-        if (p.bias0) sum += p.bias0[(size_t)e * p.rows + r];
-        p.partial[(size_t)slot * p.rows + r] = sum;
-        __threadfence();
-        uint32_t old = 0;
-        if (lane == 0) old = atomicAdd(&p.tile_cnt[t], 1u);
-        old = __shfl_sync(0x0000ffffu, old, 0);
-        if (old == (uint32_t)(si->n - 1)) {
-          __threadfence();
-          float acc = 0.f;
-          for (int q = 0; q < si->n; ++q) {
-            const int sl = si->slot[q];
-            acc += __ldcg(&p.partial[(size_t)sl * p.rows + r]) * p.wts[sl];
-          }
-          if (p.out) p.out[r] = acc;
-          else p.h[r] = p.h[r] + acc;
-          if (lane == 0) p.tile_cnt[t] = 0u;
-        }
+      for (int q = 0; q < RT; ++q) {
+        if (p.mode == MODE_GATEUP) { rw[8 * q + g] = acc0[q]; rw[16 + 8 * q + g] = acc1[q]; }
+        else { rw[16 * q + g] = acc0[q]; rw[16 * q + g + 8] = acc1[q]; }
       }
+    }
+    __syncwarp();
+    uint32_t old = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      old = atomicAdd(&red_cnt[rbuf], 1u);
+    }
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old == kCW - 1) {
+      __threadfence_block();
+      item_epilogue(p, si, red + (size_t)rbuf * kCW * kRedRows, ls, t, lane);
+      __syncwarp();
+      if (lane == 0) red_cnt[rbuf] = 0u;
     }
   }
 }
 
-// ---------------- router: RMSNorm + GEMV + bias + mask + top-k + softmax ----------------
-constexpr int kRouterWarps = 8;
+template <int NBW, int RT>
+cudaError_t launch_phase(const DevCtx& c, const PhaseParams& p, cudaStream_t s) {
+  const size_t smem = (size_t)p.ns * p.stage_bytes + (size_t)(p.ns + 1) * kCW * kRedRows * sizeof(float) +
+                      2 * kMaxStages * 8 + (kMaxStages + 1) * 4 + sizeof(SlotInfo) + 16;
+  cudaError_t e = cudaFuncSetAttribute(moe_mxfp4_phase_kernel<NBW, RT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)c.sm_count);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, moe_mxfp4_phase_kernel<NBW, RT>, p);
+}
 
-__global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a, uint32_t* err) {
-  __shared__ float red[kRouterWarps];
-  __shared__ float inv_s;
-  __shared__ uint32_t last;
-  extern __shared__ float xs[];   // [H]
+template <int RT>
+cudaError_t dispatch_nbw(const DevCtx& c, const PhaseParams& p, cudaStream_t s) {
+  const int nbw = (p.cols / 32 + kCW - 1) / kCW;
+  if (nbw <= 1) return launch_phase<1, RT>(c, p, s);
+  if (nbw <= 2) return launch_phase<2, RT>(c, p, s);
+  if (nbw <= 4) return launch_phase<4, RT>(c, p, s);
+  if (nbw <= 6) return launch_phase<6, RT>(c, p, s);
+  if (nbw <= 8) return launch_phase<8, RT>(c, p, s);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t dispatch_phase(const DevCtx& c, const PhaseParams& p, cudaStream_t s) {
+  return p.mode == MODE_GATEUP ? dispatch_nbw<2>(c, p, s) : dispatch_nbw<1>(c, p, s);
+}
+
+int pick_stages(int stage_bytes) {
+  int ns = (int)((192 * 1024) / stage_bytes);
+  return ns < 2 ? 2 : (ns > 6 ? 6 : ns);
+}
+
+// ---------------- router: RMSNorm + GEMV + bias + mask + top-k + softmax ----------------
+// One CTA per expert row: each recomputes the RMSNorm of h (L2-resident), dots its router row
+// and writes one logit; the last CTA to finish selects the top-k and the routing weights.
+constexpr int kRouterThreads = 256;
+constexpr int kRouterMaxE = 1024;
+
+__device__ __forceinline__ float router_block_sum(float v, float* red) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  v = warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kRouterThreads / 32; ++w) t += red[w];
+  __syncthreads();
+  return t;
+}
+
+__global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, uint32_t* err) {
+  __shared__ float red[kRouterThreads / 32];
+  __shared__ uint32_t last;
+  __shared__ float lg[kRouterMaxE];
+  __shared__ float sel_v[kMaxK];
+  __shared__ int sel_i[kMaxK];
+  __shared__ float bv[kRouterThreads / 32];
+  __shared__ int bi[kRouterThreads / 32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x;
   pdl_wait_prior();
+  const float* wr = a.w + (size_t)e * a.H;
+  float dot = 0.f;
   if (a.h) {
     float ss = 0.f;
-    for (int i = threadIdx.x; i < a.H; i += blockDim.x) ss += a.h[i] * a.h[i];
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float t = 0.f;
-      for (int w = 0; w < kRouterWarps; ++w) t += red[w];
-      inv_s = 1.0f / sqrtf(t / (float)a.H + a.eps);
-    }
-    __syncthreads();
-    const float inv = inv_s;
-    for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
+    for (int i = threadIdx.x; i < a.H; i += kRouterThreads) { const float v = a.h[i]; ss += v * v; }
+    ss = router_block_sum(ss, red);
+    const float inv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
+    for (int i = threadIdx.x; i < a.H; i += kRouterThreads) {
       const float v = (a.h[i] * inv) * a.norm_w[i];
-      xs[i] = v;
-      if (blockIdx.x == 0) a.xn[i] = v;
+      if (e == 0) a.xn[i] = v;
+      dot = fmaf(v, __ldcs(wr + i), dot);
     }
   } else {
-    for (int i = threadIdx.x; i < a.H; i += blockDim.x) xs[i] = a.xn[i];
+    for (int i = threadIdx.x; i < a.H; i += kRouterThreads) dot = fmaf(a.xn[i], __ldcs(wr + i), dot);
   }
-  __syncthreads();
-  const int e = blockIdx.x * kRouterWarps + warp;
-  if (e < a.E) {
-    const float* wr = a.w + (size_t)e * a.H;
-    float acc = 0.f;
-    for (int i = lane * 4; i < a.H; i += 128) {
-      const float4 w4 = __ldcs(reinterpret_cast<const float4*>(wr + i));
-      acc += w4.x * xs[i] + w4.y * xs[i + 1] + w4.z * xs[i + 2] + w4.w * xs[i + 3];
-    }
-    acc = warp_sum(acc);
-    if (lane == 0) {
-      float v = acc + (a.b ? a.b[e] : 0.f);
-      if (a.mask && a.mask[e]) v = -INFINITY;
-      a.logits[e] = v;
-    }
+  dot = router_block_sum(dot, red);
+  if (threadIdx.x == 0) {
+    float v = dot + (a.b ? a.b[e] : 0.f);
+    if (a.mask && a.mask[e]) v = -INFINITY;
+    a.logits[e] = v;
+    __threadfence();
+    last = (atomicAdd(a.counter, 1u) == gridDim.x - 1) ? 1u : 0u;
   }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) last = (atomicAdd(a.counter, 1u) == gridDim.x - 1) ? 1u : 0u;
   __syncthreads();
   if (!last) return;
   __threadfence();
   // ---- top-k on the last CTA (ties -> lower index, as a stable descending sort) ----
-  __shared__ float sel_v[kMaxK];
-  __shared__ int sel_i[kMaxK];
-  __shared__ float bv[kRouterWarps];
-  __shared__ int bi[kRouterWarps];
-  float* lg = xs;   // reuse: [E] logits
-  for (int i = threadIdx.x; i < a.E; i += blockDim.x) lg[i] = __ldcg(&a.logits[i]);
+  for (int i = threadIdx.x; i < a.E; i += kRouterThreads) lg[i] = __ldcg(&a.logits[i]);
   __syncthreads();
   for (int k = 0; k < a.K; ++k) {
     float best = -INFINITY;
     int bidx = 0x7fffffff;
-    for (int i = threadIdx.x; i < a.E; i += blockDim.x) {
+    for (int i = threadIdx.x; i < a.E; i += kRouterThreads) {
       const float v = lg[i];
       bool taken = false;
       for (int q = 0; q < k; ++q) taken |= (sel_i[q] == i);
       if (taken) continue;
-      if (v > best || (v == best && i < bidx) || (bidx == 0x7fffffff && !(v == v))) { best = v; bidx = i; }
+      if (v > best || (v == best && i < bidx)) { best = v; bidx = i; }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -369,7 +455,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a,
     __syncthreads();
     if (threadIdx.x == 0) {
       float bb = bv[0]; int ii = bi[0];
-      for (int w = 1; w < kRouterWarps; ++w)
+      for (int w = 1; w < kRouterThreads / 32; ++w)
         if (bv[w] > bb || (bv[w] == bb && bi[w] < ii)) { bb = bv[w]; ii = bi[w]; }
       if (ii == 0x7fffffff) { ii = 0; atomicOr(err, EF_BAD_INDEX); }
       sel_v[k] = bb; sel_i[k] = ii;
@@ -400,42 +486,6 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a,
   }
 }
 
-template <int NBW>
-cudaError_t launch_phase(const DevCtx& c, const PhaseParams& p, cudaStream_t s) {
-  const size_t smem = (size_t)p.ns * p.stage_bytes + 2 * kCW * 16 * sizeof(float) + 2 * kMaxStages * 8 +
-                      sizeof(SlotInfo) + 16;
-  cudaError_t e = cudaFuncSetAttribute(moe_mxfp4_phase_kernel<NBW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-  if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)c.sm_count);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, moe_mxfp4_phase_kernel<NBW>, p);
-}
-
-cudaError_t dispatch_phase(const DevCtx& c, const PhaseParams& p, cudaStream_t s) {
-  const int nbw = (p.cols / 32 + kCW - 1) / kCW;
-  if (nbw <= 1) return launch_phase<1>(c, p, s);
-  if (nbw <= 2) return launch_phase<2>(c, p, s);
-  if (nbw <= 4) return launch_phase<4>(c, p, s);
-  if (nbw <= 8) return launch_phase<8>(c, p, s);
-  if (nbw <= 12) return launch_phase<12>(c, p, s);
-  if (nbw <= 16) return launch_phase<16>(c, p, s);
-  return cudaErrorInvalidValue;
-}
-
-int pick_stages(int stage_bytes) {
-  int ns = (int)((200 * 1024) / stage_bytes);
-  return ns < 2 ? 2 : (ns > 6 ? 6 : ns);
-}
-
 }  // namespace
 
 cudaError_t launch_mxfp4_gemv(const DevCtx& c, const uint8_t* w, int rows, int cols, const float* x,
@@ -457,23 +507,17 @@ size_t moe_mxfp4_smem_bytes(int H, int I) {
 }
 
 cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s) {
-  if (a.K < 1 || a.K > kMaxK || a.K > a.E || a.H % 4 || !a.counter) return cudaErrorInvalidValue;
-  const int grid = (a.E + kRouterWarps - 1) / kRouterWarps;
-  const size_t smem = (size_t)(a.H > a.E ? a.H : a.E) * sizeof(float);
+  if (a.K < 1 || a.K > kMaxK || a.K > a.E || a.E > kRouterMaxE || !a.counter) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3(kRouterWarps * 32);
-  cfg.dynamicSmemBytes = smem;
+  cfg.gridDim = dim3((unsigned)a.E);
+  cfg.blockDim = dim3(kRouterThreads);
+  cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-  }
   return cudaLaunchKernelEx(&cfg, router_kernel, a, c.err);
 }
 
@@ -486,9 +530,9 @@ cudaError_t launch_moe_mxfp4(const DevCtx& c, const MoeArgs& a, cudaStream_t s) 
   p.oai = a.oai_swiglu; p.err = c.err;
   // phase 1: gate + up + activation
   p.mode = MODE_GATEUP; p.w0 = a.gate; p.w1 = a.up; p.expert_stride = (int64_t)a.I * rbg; p.rb = rbg;
-  p.cols = a.H; p.rows = a.I; p.tile_rows = 8; p.n_tiles = a.I / 8; p.stage_bytes = 16 * rbg;
+  p.cols = a.H; p.rows = a.I; p.tile_rows = 16; p.n_tiles = a.I / 16; p.stage_bytes = 32 * rbg;
   p.ns = pick_stages(p.stage_bytes); p.x = a.x; p.bias0 = a.gate_b; p.bias1 = a.up_b; p.act = a.act;
-  if ((8 * rbg) % 16 || p.expert_stride % 16) return cudaErrorInvalidValue;
+  if ((16 * rbg) % 16 || p.expert_stride % 16 || a.I % 16 || a.H % 16) return cudaErrorInvalidValue;
   cudaError_t e = dispatch_phase(c, p, s);
   if (e != cudaSuccess) return e;
   // phase 2: down + weighted combine (+ residual)
