@@ -120,6 +120,21 @@ MS_API ms_status ms_moe_mxfp4_decode(ms_ctx* ctx, const void* d_gate, const void
                               int inter, int n_experts, int top_k, int arch, const float* d_x, const int32_t* d_idx,
                               const float* d_wts, float* d_h);
 
+/* Allocation-free variant of ms_moe_mxfp4_decode, for callers that cannot allocate device
+ * memory when they run the MoE step (a fixed memory pool owns the whole budget, or the
+ * step runs where cudaMalloc is not allowed).  No counterpart in the reference: the Metal
+ * path allocates its routing buffers up front.  Same arguments and result as
+ * ms_moe_mxfp4_decode; the scratch lives in one fixed device array of 513 KiB that every
+ * GPU loading this library keeps until exit, so top_k <= 16, hidden <= 4096 and
+ * inter <= 4096 (larger sizes return MS_ERR_SHAPE).  The first call on a device looks up
+ * the array's device address; make that first call before any stream capture.  Every call
+ * shares the array: calls that overlap on the GPU (other streams or contexts on the same
+ * device) race and must be serialised by the caller. */
+MS_API ms_status ms_moe_mxfp4_decode_noalloc(ms_ctx* ctx, const void* d_gate, const void* d_up, const void* d_down,
+                                             const float* d_gate_b, const float* d_up_b, const float* d_down_b,
+                                             int hidden, int inter, int n_experts, int top_k, int arch,
+                                             const float* d_x, const int32_t* d_idx, const float* d_wts, float* d_h);
+
 /* ---- model: the Engine surface (engine.rs open_with_device / preload_weights / forward /
  *      generate / clear_cache) ---- */
 typedef struct ms_model_config {

@@ -15,6 +15,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <set>
 #include <string>
 #include <vector>
@@ -971,3 +972,75 @@ ms_status ms_model_open_gguf(ms_ctx* c, const char* path, int max_seq_len, int e
 }
 
 }  // extern "C"
+
+// =====================================================================================
+// Allocation-free variant of ms_moe_mxfp4_decode.
+//
+// Some callers cannot allocate device memory at the time they run the MoE step: a
+// caller that has handed its whole memory budget to a fixed-size pool, a real-time
+// loop that must not enter the CUDA allocator, or a host that replays the step from
+// a context where cudaMalloc is forbidden.  For them this entry point keeps the FFN's
+// scratch (per-slot activations, per-slot partial outputs and per-tile arrival
+// counters) in one file-scope device array instead of context-owned cudaMalloc'd
+// memory.  Every GPU that loads this library holds the array until the process exits.
+// =====================================================================================
+namespace {
+
+constexpr int kNoAllocMaxTopK = 16;      // experts per token
+constexpr int kNoAllocMaxDim = 4096;     // max hidden size and max expert intermediate size
+constexpr size_t kNoAllocActFloats = (size_t)kNoAllocMaxTopK * kNoAllocMaxDim;
+constexpr size_t kNoAllocPartFloats = (size_t)kNoAllocMaxTopK * kNoAllocMaxDim;
+constexpr size_t kNoAllocCounters = kNoAllocMaxDim / 16;
+constexpr size_t kNoAllocFloats = kNoAllocActFloats + kNoAllocPartFloats + kNoAllocCounters;
+
+// act [K*I] | partial [K*H] | tile counters [H/16] (as uint32): 513 KiB per device
+static __device__ __align__(256) float g_moe_noalloc_scratch[kNoAllocFloats];
+
+constexpr int kNoAllocMaxDevices = 64;
+float* g_noalloc_addr[kNoAllocMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// once per device, with that device current: the device address of the array (the
+// array's name in host code is only a host-side stand-in and must not reach a kernel)
+ms_status noalloc_setup(ms_ctx* c, float** out) {
+  if (c->device < 0 || c->device >= kNoAllocMaxDevices) return fail(c, MS_ERR_INVALID_ARG, "device index too large");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[c->device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_moe_noalloc_scratch);
+    if (e != cudaSuccess || !p) return cuda_fail(c, e == cudaSuccess ? cudaErrorInvalidSymbol : e, "cudaGetSymbolAddress");
+    g_noalloc_addr[c->device] = (float*)p;
+  }
+  *out = g_noalloc_addr[c->device];
+  return MS_OK;
+}
+
+}  // namespace
+
+extern "C" ms_status ms_moe_mxfp4_decode_noalloc(ms_ctx* c, const void* gate, const void* up, const void* down,
+                                                 const float* gb, const float* ub, const float* db, int H, int I,
+                                                 int E, int K, int arch, const float* x, const int32_t* idx,
+                                                 const float* wts, float* h) {
+  if (!c || !gate || !up || !down || !x || !idx || !wts || !h || K <= 0 || E <= 0) return MS_ERR_INVALID_ARG;
+  if (K > kNoAllocMaxTopK || H > kNoAllocMaxDim || I > kNoAllocMaxDim)
+    return fail(c, MS_ERR_SHAPE, "moe noalloc: top_k %d / hidden %d / inter %d exceed the fixed scratch "
+                "(top_k <= %d, hidden <= %d, inter <= %d)", K, H, I, kNoAllocMaxTopK, kNoAllocMaxDim, kNoAllocMaxDim);
+  if (H % 64 || I % 32) return fail(c, MS_ERR_SHAPE, "moe: hidden %% 64 and inter %% 32 required");
+  cudaError_t e = cudaSetDevice(c->device);
+  if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
+  float* base = nullptr;
+  ms_status s = noalloc_setup(c, &base);
+  if (s != MS_OK) return s;
+  uint32_t* cnt = reinterpret_cast<uint32_t*>(base + kNoAllocActFloats + kNoAllocPartFloats);
+  // the array keeps the previous call's contents; the arrival counters must start at zero
+  e = cudaMemsetAsync(cnt, 0, (size_t)(H / 16) * sizeof(uint32_t), c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "cudaMemsetAsync");
+  MoeArgs a;
+  a.x = x; a.idx = idx; a.wts = wts; a.gate = (const uint8_t*)gate; a.up = (const uint8_t*)up;
+  a.down = (const uint8_t*)down; a.gate_b = gb; a.up_b = ub; a.down_b = db;
+  a.act = base; a.partial = base + kNoAllocActFloats; a.tile_cnt = cnt; a.h = h;
+  a.H = H; a.I = I; a.K = K; a.expert_base = 0; a.n_local = E; a.oai_swiglu = arch == MS_ARCH_GPT_OSS;
+  e = launch_moe_mxfp4(c->dc, a, c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "moe_mxfp4 (noalloc)");
+  return MS_OK;
+}

@@ -77,6 +77,13 @@ class Context:
                                         _ptr(down_b), hidden, inter, n_experts, top_k, arch, _ptr(x), _ptr(idx),
                                         _ptr(wts), _ptr(h)), self.h)
 
+    def moe_mxfp4_decode_noalloc(self, gate, up, down, gate_b, up_b, down_b, hidden, inter, n_experts, top_k,
+                                 arch, x, idx, wts, h) -> None:
+        """Same as moe_mxfp4_decode, with its scratch in the library's fixed device array."""
+        check(lib().ms_moe_mxfp4_decode_noalloc(self.h, _ptr(gate), _ptr(up), _ptr(down), _ptr(gate_b),
+                                                _ptr(up_b), _ptr(down_b), hidden, inter, n_experts, top_k, arch,
+                                                _ptr(x), _ptr(idx), _ptr(wts), _ptr(h)), self.h)
+
     def close(self) -> None:
         if getattr(self, "h", None):
             lib().ms_ctx_destroy(self.h)
