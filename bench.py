@@ -13,8 +13,10 @@ needed between steps.
   cpu_baseline  C++ restatement of the reference CPU path (oracle/), bounded sample
 
 --impl reference times that CPU restatement alone (the Rust reference does not build here).
-Under torchrun (N > 1) every rank decodes its own replica (expert-parallel sharding is not in
-this build yet); value is the sum over ranks, timed as the max over ranks.
+Under torchrun (N > 1) the default --mode ep splits the experts evenly over the ranks and all
+ranks decode one sequence together (NCCL all-reduce of each layer's MoE output, "strong"
+scaling); --mode replicas runs one independent sequence per rank ("weak" scaling, value summed).
+Times are the max over ranks.
 """
 from __future__ import annotations
 
@@ -221,6 +223,9 @@ def run_ours(args):
     from moe_stream_b200.engine import Context, Engine
 
     spec = synth.GPT_OSS_20B
+    if args.layers:
+        from dataclasses import replace
+        spec = replace(spec, layers=args.layers)   # profiling cases only: fewer layers, same shapes
     prompt_len = args.prompt
     max_seq = prompt_len + args.warmup + 2 * args.steps + 64
     stream = torch.cuda.Stream()
@@ -228,7 +233,13 @@ def run_ours(args):
     t0 = time.time()
     ctx = Context(local)
     ctx.set_stream(stream)
-    eng = Engine.from_spec(spec, seed=0, max_seq_len=max_seq, ctx=ctx)
+    ep = ws > 1 and args.mode == "ep"
+    eng = Engine.from_spec(spec, seed=0, max_seq_len=max_seq, ctx=ctx,
+                           ep_rank=rank if ep else 0, ep_size=ws if ep else 1)
+    if ep:
+        uid = [Engine.nccl_unique_id(ctx) if rank == 0 else None]
+        torch.distributed.broadcast_object_list(uid, src=0)
+        eng.init_ep(uid[0])
     log(f"[rank {rank}] model generated + uploaded in {time.time() - t0:.1f}s")
     prompt = synth.prompt_ids(spec, prompt_len, seed=0)
     t0 = time.time()
@@ -287,16 +298,18 @@ def run_ours(args):
                "sample": r["sample"]}
     if rank != 0:
         return
-    value = ws * args.steps / (ms * 1e-3)
+    streams = 1 if ep else ws          # expert parallel: all ranks decode one sequence together
+    value = streams * args.steps / (ms * 1e-3)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (MXFP4/Q8_0/f16 weights, f32 activations and KV)",
+        "scaling": "strong" if ep else "weak", "vs_baseline": None, "dtype": "f32 (MXFP4/Q8_0/f16 weights, f32 activations and KV)",
         "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
         "config": {"workload": "GPT-OSS-20B-shaped MXFP4 greedy decode, bs1, after a 2048-token prompt",
-                   "model": "gpt-oss-20b-shaped", "global_batch": ws, "seq_len": prompt_len, "parallelism": f"replicas{ws}",
+                   "model": "gpt-oss-20b-shaped", "global_batch": streams, "seq_len": prompt_len,
+                   "parallelism": (f"ep{ws}" if ep else f"replicas{ws}"),
                    "l2": "no flush: each step streams ~3.1 GB of weights (> 126 MB L2)"},
-        "e2e": {"value": round(ws * args.steps / e2e_s, 2) if e2e_s == e2e_s else None, "unit": "tok/s", "h2d_bytes_per_step": 4 + 4,
+        "e2e": {"value": round(streams * args.steps / e2e_s, 2) if e2e_s == e2e_s else None, "unit": "tok/s", "h2d_bytes_per_step": 4 + 4,
                 "d2h_bytes_per_step": 8},
         "roofline": {"kernel": "moe_mxfp4 gate_up+down (config-0 shape, one token-layer)", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -333,6 +346,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-roofline", action="store_true", help="skip the expert-FFN roofline leg")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (default 2048)")
+    ap.add_argument("--layers", type=int, default=0, help="profiling only: override the layer count")
+    ap.add_argument("--mode", default="ep", choices=["ep", "replicas"],
+                    help="N > 1: expert parallel over one sequence (default) or N independent replicas")
     ap.add_argument("--case", default=None, choices=[None, "moe-layer"], help="small profiling case")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -157,6 +157,13 @@ MS_API ms_status ms_model_create(ms_ctx* ctx, const ms_model_config* cfg, ms_mod
 MS_API ms_status ms_model_set_tensor(ms_model* m, const char* name, int qtype, int n_dims, const int64_t* dims,
                               const void* host_data, size_t bytes);
 MS_API ms_status ms_model_finalize(ms_model* m);
+/* Expert parallelism (no counterpart in the reference, which runs on one device): a model
+ * created with ep_size > 1 holds experts [ep_rank*E/ep_size, (ep_rank+1)*E/ep_size) and sums
+ * each layer's MoE output over the group with an NCCL all-reduce inside the decode step.
+ * Rank 0 calls ms_nccl_unique_id, the caller broadcasts the 128 bytes to every rank, and
+ * each rank calls ms_model_init_ep before its first forward. */
+MS_API ms_status ms_nccl_unique_id(ms_ctx* ctx, void* out, size_t bytes);
+MS_API ms_status ms_model_init_ep(ms_model* m, const void* unique_id, size_t bytes);
 /* Parse a GGUF file (reader.rs:259-368, config.rs:253-434) and upload everything. */
 MS_API ms_status ms_model_open_gguf(ms_ctx* ctx, const char* path, int max_seq_len, int ep_rank, int ep_size,
                              ms_model** out);

@@ -63,6 +63,8 @@ _SIGS = {
     "ms_moe_mxfp4_decode": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "ms_moe_mxfp4_decode_noalloc": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp,
                                               _vp, _vp]),
+    "ms_nccl_unique_id": (C.c_int, [_vp, _vp, C.c_size_t]),
+    "ms_model_init_ep": (C.c_int, [_vp, _vp, C.c_size_t]),
     "ms_model_create": (C.c_int, [_vp, C.POINTER(ModelConfig), C.POINTER(_vp)]),
     "ms_model_set_tensor": (C.c_int, [_vp, C.c_char_p, _i, _i, C.POINTER(C.c_int64), _vp, C.c_size_t]),
     "ms_model_finalize": (C.c_int, [_vp]),

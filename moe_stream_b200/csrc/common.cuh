@@ -140,6 +140,41 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// ---- pending MoE combine (see PendingCombine in kernels.h) ----
+struct CombineOrder {
+  int n;
+  int slot[16];
+  float w[16];
+};
+
+// single thread: local slots ordered by ascending expert id
+__device__ __forceinline__ void combine_order(const PendingCombine& pc, CombineOrder* co) {
+  int n = 0;
+  if (pc.partial) {
+    for (int k = 0; k < pc.K; ++k) {
+      const int e = pc.idx[k] - pc.expert_base;
+      if (e < 0 || e >= pc.n_local) continue;
+      int j = n++;
+      while (j > 0 && pc.idx[co->slot[j - 1]] - pc.expert_base > e) {
+        co->slot[j] = co->slot[j - 1];
+        co->w[j] = co->w[j - 1];
+        --j;
+      }
+      co->slot[j] = k;
+      co->w[j] = pc.wts[k];
+    }
+  }
+  co->n = n;
+}
+
+// moe_out[r], accumulated from zero in ascending expert order as the reference does
+__device__ __forceinline__ float combine_at(const PendingCombine& pc, const CombineOrder& co, int H, int r) {
+  if (pc.dense) return pc.dense[r];
+  float acc = 0.f;
+  for (int q = 0; q < co.n; ++q) acc += pc.partial[(size_t)co.slot[q] * H + r] * co.w[q];
+  return acc;
+}
+
 // Programmatic dependent launch: let the next kernel start its prologue early /
 // wait for the previous kernel's memory to be visible.
 __device__ __forceinline__ void pdl_launch_dependents() {

@@ -29,6 +29,20 @@ cudaError_t launch_dequantize(const DevCtx& c, int qtype, const void* blocks, in
 cudaError_t launch_rms_norm(const DevCtx& c, const float* x, const float* w, float* y, int rows, int dim, float eps,
                             cudaStream_t s);
 
+// A MoE combine not yet applied to the residual stream: the stream's value is
+// h[r] + sum over local slots, in ascending expert id, of partial[slot][r] * wts[slot]
+// (layer.rs:1797-1847 accumulation order; hidden = residual + moe_out, layer.rs:494),
+// or h[r] + dense[r] when the expert-parallel all-reduce already summed it.
+struct PendingCombine {
+  const float* dense = nullptr;    // [H] summed MoE output, or null
+  const float* partial = nullptr;  // [K, H] per-slot expert outputs (bias included)
+  const int* idx = nullptr;        // [K] expert ids
+  const float* wts = nullptr;      // [K] routing weights
+  int K = 0;
+  int expert_base = 0, n_local = 0;
+  __host__ __device__ bool active() const { return dense != nullptr || partial != nullptr; }
+};
+
 // y[r] = W[r,:] . x  (+bias[r]) (+residual: y[r] += y_in[r]);  MXFP4 / F16 / F32 weights.
 struct GemvArgs {
   int qtype = Q_MXFP4;
@@ -53,6 +67,8 @@ struct Q8GemvArgs {
   float* y = nullptr;          // output (ignored when residual != null)
   float* residual = nullptr;   // residual[r] += W x + bias
   int exact = 0;               // 1: f32 activations (no quantization), for the exact-mode oracle
+  PendingCombine x_pend;       // applied to x before use (x is a residual stream)
+  PendingCombine res_pend;     // applied to residual before the add
 };
 cudaError_t launch_q8_gemv(const DevCtx& c, const Q8GemvArgs& a, cudaStream_t s);
 
@@ -96,8 +112,12 @@ struct MoeArgs {
   int H = 0, I = 0, K = 0;
   int expert_base = 0, n_local = 0;  // experts [base, base+n_local) live on this device
   int oai_swiglu = 1;
+  int defer_combine = 0;           // 1: leave the combine pending (consumers apply it); no h / out update
 };
 cudaError_t launch_moe_mxfp4(const DevCtx& c, const MoeArgs& a, cudaStream_t s);
+// the combine as its own kernel: h[r] += comb(r), or out[r] = comb(r) when out != null
+cudaError_t launch_moe_combine(const DevCtx& c, const PendingCombine& pc, int H, float* h, float* out,
+                               cudaStream_t s);
 // plain MXFP4 GEMV through the same streaming machinery: y = W x (+bias) (+= when accumulate)
 cudaError_t launch_mxfp4_gemv(const DevCtx& c, const uint8_t* w, int rows, int cols, const float* x,
                               const float* bias, float* y, int accumulate, cudaStream_t s);
@@ -137,6 +157,8 @@ struct LmHeadArgs {
   unsigned long long* key = nullptr;  // argmax key (value, index) or null; caller zeroes it
   int V = 0, H = 0;
   int accumulate = 0;
+  PendingCombine x_pend;              // applied to x first
+  float* x_out = nullptr;             // effective x (before the norm) written by CTA 0, or null
 };
 cudaError_t launch_lmhead(const DevCtx& c, const LmHeadArgs& a, cudaStream_t s);
 int argmax_from_key(unsigned long long key);

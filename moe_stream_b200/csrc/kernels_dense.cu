@@ -134,6 +134,7 @@ struct Q8Params {
   const float* bias;
   float* y;
   float* residual;
+  PendingCombine x_pend, res_pend;
   uint32_t* err;
 };
 
@@ -190,10 +191,21 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
   // ---- consumer prologue: (RMSNorm) + Q8_0 quantization of the activation ----
   pdl_wait_prior();
   const int nct = kQW * 32;
+  __shared__ CombineOrder xco, rco;
+  if (threadIdx.x == 0) {
+    xco.n = 0; rco.n = 0;
+    if (p.x_pend.active()) combine_order(p.x_pend, &xco);
+    if (p.res_pend.active()) combine_order(p.res_pend, &rco);
+  }
+  named_bar(1, nct);
+  const bool xp = p.x_pend.active();
   float inv = 1.f;
   if (p.norm_w) {
     float ss = 0.f;
-    for (int i = threadIdx.x; i < p.cols; i += nct) { const float v = p.x[i]; ss += v * v; }
+    for (int i = threadIdx.x; i < p.cols; i += nct) {
+      const float v = xp ? p.x[i] + combine_at(p.x_pend, xco, p.cols, i) : p.x[i];
+      ss += v * v;
+    }
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
     named_bar(1, nct);
@@ -209,6 +221,10 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
     for (int k = 0; k < 8; ++k) {
       const float4 t = x4[k];
       v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
+    }
+    if (xp) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = v[k] + combine_at(p.x_pend, xco, p.cols, 32 * b + k);
     }
     if (p.norm_w) {
       const float4* w4 = reinterpret_cast<const float4*>(p.norm_w + 32 * b);
@@ -264,14 +280,17 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
     float acc = 0.f;
     if (ok && warp < nr) {
       const uint8_t* row = stages + (size_t)s * p.stage_bytes + (size_t)warp * p.rb;
+      // block b = lane + 32 i starts at 34 b; 34 * 32 = 1088 is a multiple of 4, so the
+      // alignment of this lane's codes is the same for all of its blocks in the row
+      const uint32_t off_l = (uint32_t)warp * p.rb + 34u * lane;
+      const uint32_t qa_l = (off_l + 2) & ~3u, sh = ((off_l + 2) & 3u) * 8u;
+      const uint8_t* sbase = stages + (size_t)s * p.stage_bytes;
 #pragma unroll
       for (int i = 0; i < NBL; ++i) {
         const int b = lane + 32 * i;
         if (b < nb) {
-          const uint32_t off = 34u * b;
-          const uint16_t dw = *reinterpret_cast<const uint16_t*>(row + off);
-          const uint32_t qa = (off + 2) & ~3u, sh = ((off + 2) & 3u) * 8u;
-          const uint32_t* wp = reinterpret_cast<const uint32_t*>(row + qa);
+          const uint16_t dw = *reinterpret_cast<const uint16_t*>(row + 34u * lane + 1088u * i);
+          const uint32_t* wp = reinterpret_cast<const uint32_t*>(sbase + qa_l + 1088u * i);
           uint32_t wd[9];
 #pragma unroll
           for (int k = 0; k < 9; ++k) wd[k] = wp[k];
@@ -288,8 +307,12 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
     if (ok && warp < nr && lane == 0) {
       const int r = r0 + warp;
       const float v = acc + (p.bias ? p.bias[r] : 0.f);
-      if (p.residual) p.residual[r] = p.residual[r] + v;
-      else p.y[r] = v;
+      if (p.residual) {
+        const float base = p.res_pend.active() ? p.residual[r] + combine_at(p.res_pend, rco, p.rows, r) : p.residual[r];
+        p.residual[r] = base + v;
+      } else {
+        p.y[r] = v;
+      }
     }
     if (!ok) break;
   }
@@ -315,7 +338,7 @@ cudaError_t launch_q8(const DevCtx& c, const Q8Params& p, cudaStream_t s) {
 }
 
 // ============================ attention (decode) ============================
-constexpr int kAT = 32;        // positions per tile
+constexpr int kAT = 64;        // positions per tile
 constexpr int kAThreads = 128;
 
 __device__ __forceinline__ void rope_inplace(float* v, int rot, const float* c, const float* s) {
@@ -421,13 +444,21 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
     }
     __syncthreads();
     for (int h = warp; h < rep; h += nwarp) {   // online softmax update per head
-      const float v = lane < kAT ? sc[h * kAT + lane] : -INFINITY;
-      const float tm = warp_max(v);
+      float v[kAT / 32];
+      float tm = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < kAT / 32; ++u) { v[u] = sc[h * kAT + 32 * u + lane]; tm = fmaxf(tm, v[u]); }
+      tm = warp_max(tm);
       const float m_old = ml[2 * h], m_new = fmaxf(m_old, tm);
-      const float pexp = (v == -INFINITY) ? 0.f : expf(v - m_new);
-      const float psum = warp_sum(pexp);
+      float ps = 0.f;
+#pragma unroll
+      for (int u = 0; u < kAT / 32; ++u) {
+        const float pexp = (v[u] == -INFINITY) ? 0.f : expf(v[u] - m_new);
+        sc[h * kAT + 32 * u + lane] = pexp;
+        ps += pexp;
+      }
+      const float psum = warp_sum(ps);
       const float cr = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-      if (lane < kAT) sc[h * kAT + lane] = pexp;
       if (lane == 0) { ml[2 * h] = m_new; ml[2 * h + 1] = ml[2 * h + 1] * cr + psum; corr[h] = cr; }
     }
     __syncthreads();
@@ -488,14 +519,18 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
   for (int i = threadIdx.x; i < rep * hd; i += blockDim.x) {
     const int h = i / hd, d = i - h * hd;
     const float* src = gp + (size_t)h * (hd + 2) + 2 + d;
-    float o0 = 0.f, o1 = 0.f;
+    const size_t stride = (size_t)rep * (hd + 2);
+    float o = 0.f;
     int s = 0;
-    for (; s + 1 < S; s += 2) {
-      o0 = fmaf(wsm[s * rep + h], __ldcg(src + (size_t)s * rep * (hd + 2)), o0);
-      o1 = fmaf(wsm[(s + 1) * rep + h], __ldcg(src + (size_t)(s + 1) * rep * (hd + 2)), o1);
+    for (; s + 8 <= S; s += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldcg(src + (size_t)(s + u) * stride);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o = fmaf(wsm[(s + u) * rep + h], v[u], o);
     }
-    if (s < S) o0 = fmaf(wsm[s * rep + h], __ldcg(src + (size_t)s * rep * (hd + 2)), o0);
-    a.out[(size_t)(kh * rep + h) * hd + d] = o0 + o1;
+    for (; s < S; ++s) o = fmaf(wsm[s * rep + h], __ldcg(src + (size_t)s * stride), o);
+    a.out[(size_t)(kh * rep + h) * hd + d] = o;
   }
   if (threadIdx.x == 0) a.cnt[kh] = 0u;
 }
@@ -516,12 +551,21 @@ __global__ void __launch_bounds__(kLWarps * 32, 1) lmhead_kernel(LmHeadArgs a) {
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[kLWarps];
   __shared__ unsigned long long bestk[kLWarps];
+  __shared__ CombineOrder co;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_wait_prior();
+  if (threadIdx.x == 0) { co.n = 0; if (a.x_pend.active()) combine_order(a.x_pend, &co); }
+  __syncthreads();
+  for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
+    const float v = a.x_pend.active() ? a.x[i] + combine_at(a.x_pend, co, a.H, i) : a.x[i];
+    xs[i] = v;
+    if (a.x_out && blockIdx.x == 0) a.x_out[i] = v;
+  }
+  __syncthreads();
   float inv = 1.f;
   if (a.norm_w) {
     float ss = 0.f;
-    for (int i = threadIdx.x; i < a.H; i += blockDim.x) ss += a.x[i] * a.x[i];
+    for (int i = threadIdx.x; i < a.H; i += blockDim.x) ss += xs[i] * xs[i];
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
     __syncthreads();
@@ -529,7 +573,8 @@ __global__ void __launch_bounds__(kLWarps * 32, 1) lmhead_kernel(LmHeadArgs a) {
     for (int w = 0; w < kLWarps; ++w) t += red[w];
     inv = 1.0f / sqrtf(t / (float)a.H + a.eps);
   }
-  for (int i = threadIdx.x; i < a.H; i += blockDim.x) xs[i] = a.norm_w ? (a.x[i] * inv) * a.norm_w[i] : a.x[i];
+  __syncthreads();
+  for (int i = threadIdx.x; i < a.H; i += blockDim.x) xs[i] = a.norm_w ? (xs[i] * inv) * a.norm_w[i] : xs[i];
   __syncthreads();
   const int nch = a.H / 8;
   float xr[NCH][8];
@@ -667,6 +712,7 @@ cudaError_t launch_q8_gemv(const DevCtx& c, const Q8GemvArgs& a, cudaStream_t s)
   p.ns = (int)((180 * 1024) / p.stage_bytes);
   p.ns = p.ns > 6 ? 6 : (p.ns < 2 ? 2 : p.ns);
   p.x = a.x; p.norm_w = a.norm_w; p.eps = a.eps; p.bias = a.bias; p.y = a.y; p.residual = a.residual;
+  p.x_pend = a.x_pend; p.res_pend = a.res_pend;
   p.err = c.err;
   const int nbl = (a.cols / 32 + 31) / 32;
   if (p.stage_rows > kQW) return cudaErrorInvalidValue;

@@ -65,13 +65,15 @@ struct SlotInfo {
   int expert[kMaxK];       // local expert index
 };
 
-// One 32-column block of two MMA rows (row0, row1 of this thread): A from the e2m1 codes of
-// both rows, B = the block's (x_hi, x_lo) fragments; the block dot is scaled by 2^(E-127+kb).
-__device__ __forceinline__ void mx_block(const uint8_t* st, uint32_t off0, uint32_t off1, const uint32_t (&bf)[4],
-                                         int kbs, int c, float& acc0, float& acc1) {
-  const uint32_t w0 = lds_u32_unaligned(st, off0 + 1 + 4 * c);
-  const uint32_t w1 = lds_u32_unaligned(st, off1 + 1 + 4 * c);
-  const int e0 = st[off0], e1 = st[off1];
+// One 32-column block of two MMA rows of this thread.  p0/p1: the rows' block starts in shared
+// memory; w0/w1: 4-byte-aligned address of the word holding the thread's first code byte, with
+// funnel shift sh0/sh1 (bits); the caller precomputes them so all loads use immediate offsets.
+__device__ __forceinline__ void mx_block(const uint8_t* p0, const uint8_t* p1, const uint32_t* w0p,
+                                         const uint32_t* w1p, uint32_t sh0, uint32_t sh1, const uint32_t (&bf)[4],
+                                         int kbs, float& acc0, float& acc1) {
+  const uint32_t w0 = __funnelshift_r(w0p[0], w0p[1], sh0);
+  const uint32_t w1 = __funnelshift_r(w1p[0], w1p[1], sh1);
+  const int e0 = *p0, e1 = *p1;
   uint32_t a0[4], a1[4];
   uint32_t g0, g1, g2, g3, u0, u1, u2, u3;
   e2m1x8_to_f16x2x4(w0, g0, g1, g2, g3);
@@ -162,29 +164,11 @@ __device__ __forceinline__ void item_epilogue(const PhaseParams& p, const SlotIn
     }
     return;
   }
-  // DOWN: per-slot partial rows; the last CTA to finish a tile combines the slots in
-  // ascending expert order (layer.rs:1797-1847) and adds into the residual stream.
+  // DOWN: per-slot expert output rows (bias included); the weighted combine in ascending expert
+  // order happens in the consumer of the residual stream (PendingCombine) or moe_combine_kernel.
   if (lane < 16) {
     if (p.bias0) sum += p.bias0[(size_t)e * p.rows + r];
     p.partial[(size_t)slot * p.rows + r] = sum;
-  }
-  __threadfence();
-  __syncwarp();
-  uint32_t old = 0;
-  if (lane == 0) old = atomicAdd(&p.tile_cnt[t], 1u);
-  old = __shfl_sync(0xffffffffu, old, 0);
-  if (old == (uint32_t)(si->n - 1)) {
-    __threadfence();
-    if (lane < 16) {
-      float acc = 0.f;
-      for (int q = 0; q < si->n; ++q) {
-        const int sl = si->slot[q];
-        acc += __ldcg(&p.partial[(size_t)sl * p.rows + r]) * p.wts[sl];
-      }
-      if (p.out) p.out[r] = acc;
-      else p.h[r] = p.h[r] + acc;
-    }
-    if (lane == 0) p.tile_cnt[t] = 0u;
   }
 }
 
@@ -282,6 +266,17 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
       off1[q] = (uint32_t)(16 * q + g + 8) * p.rb;
     }
   }
+  // Block b = warp + kCW*i of a row starts at row + 17*b; kCW*17 = 272 bytes is a multiple of 4,
+  // so the alignment of the thread's code bytes is the same for all its blocks.
+  uint32_t bs0[RT], bs1[RT], wa0[RT], wa1[RT], sh0[RT], sh1[RT];
+#pragma unroll
+  for (int q = 0; q < RT; ++q) {
+    bs0[q] = off0[q] + 17u * warp;
+    bs1[q] = off1[q] + 17u * warp;
+    const uint32_t c0 = bs0[q] + 1 + 4 * c, c1 = bs1[q] + 1 + 4 * c;
+    wa0[q] = c0 & ~3u; sh0[q] = (c0 & 3u) * 8u;
+    wa1[q] = c1 & ~3u; sh1[q] = (c1 & 3u) * 8u;
+  }
   int cur_slot = -1;
   for (int j = 0; j < my_n; ++j) {
     if (*reinterpret_cast<volatile int*>(abort_flag)) break;
@@ -306,7 +301,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
       const int b = warp + kCW * i;
       if (b < nb) {
 #pragma unroll
-        for (int q = 0; q < RT; ++q) mx_block(st, off0[q] + 17u * b, off1[q] + 17u * b, bf[i], kbs[i], c, acc0[q], acc1[q]);
+        for (int q = 0; q < RT; ++q)
+          mx_block(st + bs0[q] + kCW * 17 * i, st + bs1[q] + kCW * 17 * i,
+                   reinterpret_cast<const uint32_t*>(st + wa0[q] + kCW * 17 * i),
+                   reinterpret_cast<const uint32_t*>(st + wa1[q] + kCW * 17 * i), sh0[q], sh1[q], bf[i], kbs[i],
+                   acc0[q], acc1[q]);
       }
     }
     __syncwarp();
@@ -506,6 +505,32 @@ size_t moe_mxfp4_smem_bytes(int H, int I) {
   return (size_t)pick_stages(16 * rbg) * 16 * rbg;
 }
 
+__global__ void moe_combine_kernel(PendingCombine pc, int H, float* h, float* out) {
+  __shared__ CombineOrder co;
+  pdl_wait_prior();
+  if (threadIdx.x == 0) combine_order(pc, &co);
+  __syncthreads();
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < H; r += gridDim.x * blockDim.x) {
+    const float v = combine_at(pc, co, H, r);
+    if (out) out[r] = v;
+    else h[r] = h[r] + v;
+  }
+}
+
+cudaError_t launch_moe_combine(const DevCtx& c, const PendingCombine& pc, int H, float* h, float* out,
+                               cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((H + 255) / 256));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, moe_combine_kernel, pc, H, h, out);
+}
+
 cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s) {
   if (a.K < 1 || a.K > kMaxK || a.K > a.E || a.E > kRouterMaxE || !a.counter) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
@@ -541,7 +566,12 @@ cudaError_t launch_moe_mxfp4(const DevCtx& c, const MoeArgs& a, cudaStream_t s) 
   p.ns = pick_stages(p.stage_bytes); p.x = a.act; p.bias0 = a.down_b; p.bias1 = nullptr;
   p.partial = a.partial; p.tile_cnt = a.tile_cnt; p.h = a.h; p.out = a.out;
   if ((16 * rbd) % 16 || p.expert_stride % 16) return cudaErrorInvalidValue;
-  return dispatch_phase(c, p, s);
+  e = dispatch_phase(c, p, s);
+  if (e != cudaSuccess || a.defer_combine) return e;
+  PendingCombine pc;
+  pc.partial = a.partial; pc.idx = a.idx; pc.wts = a.wts; pc.K = a.K; pc.expert_base = a.expert_base;
+  pc.n_local = a.n_local;
+  return launch_moe_combine(c, pc, a.H, a.h, a.out, s);
 }
 
 }  // namespace ms

@@ -5,7 +5,9 @@
 // scratch), the GGUF loader, and the per-token decode step, which is captured once as a
 // CUDA graph and replayed.  Reference call sites are cited per function.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 #include <fcntl.h>
+#include <nccl.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
 #include <unistd.h>
@@ -133,8 +135,38 @@ struct LayerW {
   int qkv_parts = 0, bqkv_parts = 0;
 };
 
+// NCCL is resolved at run time (dlopen), so a process that already loaded libnccl (torch does)
+// shares that copy and single-GPU users need no NCCL at all.
+struct NcclApi {
+  bool ok = false;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+static NcclApi* nccl_api() {
+  static NcclApi api;
+  static bool tried = false;
+  if (tried) return api.ok ? &api : nullptr;
+  tried = true;
+  void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+  if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+  if (!h) return nullptr;
+  api.get_unique_id = (decltype(api.get_unique_id))dlsym(h, "ncclGetUniqueId");
+  api.comm_init_rank = (decltype(api.comm_init_rank))dlsym(h, "ncclCommInitRank");
+  api.all_reduce = (decltype(api.all_reduce))dlsym(h, "ncclAllReduce");
+  api.comm_destroy = (decltype(api.comm_destroy))dlsym(h, "ncclCommDestroy");
+  api.error_string = (decltype(api.error_string))dlsym(h, "ncclGetErrorString");
+  api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.comm_destroy && api.error_string;
+  return api.ok ? &api : nullptr;
+}
+
 struct ms_model {
   ms_ctx* ctx = nullptr;
+  ncclComm_t comm = nullptr;        // expert-parallel communicator (ep_size > 1)
+  float* moe_out = nullptr;         // [H] local MoE output, all-reduced across the EP group
   ms_model_config cfg{};
   std::vector<LayerW> L;
   void* embd = nullptr;
@@ -146,7 +178,7 @@ struct ms_model {
   float* sin_t = nullptr;
   // per-step scratch
   float *h = nullptr, *qkv = nullptr, *attn_out = nullptr, *xn = nullptr, *router_logits = nullptr;
-  float *act = nullptr, *partial = nullptr, *logits = nullptr, *attn_part = nullptr;
+  float *act = nullptr, *partial = nullptr, *logits = nullptr, *attn_part = nullptr, *h_last = nullptr;
   uint32_t *router_cnt = nullptr, *tile_cnt = nullptr, *attn_cnt = nullptr;
   StepState* st = nullptr;
   int* token_log = nullptr;
@@ -320,11 +352,14 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     ++nk;                                                                  \
   } while (0)
   LAUNCH(launch_embed(dc, m->st, m->embd, m->embd_q, H, c.vocab, m->h, m->token_log, s));
+  // the previous layer's MoE output stays pending: its consumers (this layer's QKV prologue and
+  // O-projection epilogue, or the LM head) add it to the residual stream
+  PendingCombine pend;
   for (int li = 0; li < c.layers; ++li) {
     LayerW& Lw = m->L[li];
     Q8GemvArgs qa;
     qa.w = Lw.wqkv; qa.rows = Dq + 2 * Dkv; qa.cols = H; qa.x = m->h; qa.norm_w = Lw.attn_norm; qa.eps = c.eps;
-    qa.bias = Lw.bqkv; qa.y = m->qkv;
+    qa.bias = Lw.bqkv; qa.y = m->qkv; qa.x_pend = pend;
     LAUNCH(launch_q8_gemv(dc, qa, s));
     AttnArgs aa;
     aa.qkv = m->qkv; aa.q_norm = Lw.qn; aa.k_norm = Lw.kn; aa.eps = c.eps; aa.cos_t = m->cos_t; aa.sin_t = m->sin_t;
@@ -335,6 +370,7 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     LAUNCH(launch_attention(dc, aa, s));
     Q8GemvArgs oa;
     oa.w = Lw.wo; oa.rows = H; oa.cols = Dq; oa.x = m->attn_out; oa.bias = Lw.bo; oa.residual = m->h;
+    oa.res_pend = pend;
     LAUNCH(launch_q8_gemv(dc, oa, s));
     RouterArgs ra;
     ra.h = m->h; ra.norm_w = Lw.post_norm; ra.eps = c.eps; ra.xn = m->xn; ra.w = Lw.router_w; ra.b = Lw.router_b;
@@ -347,12 +383,27 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     ma.gate_b = Lw.gate_b; ma.up_b = Lw.up_b; ma.down_b = Lw.down_b; ma.act = m->act; ma.partial = m->partial;
     ma.tile_cnt = m->tile_cnt; ma.h = m->h; ma.H = H; ma.I = c.inter; ma.K = c.top_k;
     ma.expert_base = m->expert_base; ma.n_local = m->n_local; ma.oai_swiglu = c.arch == MS_ARCH_GPT_OSS;
-    LAUNCH(launch_moe_mxfp4(dc, ma, s));
-    ++nk;   // two kernels (gate/up, down)
+    pend = PendingCombine();
+    if (c.ep_size > 1) {
+      // expert parallel: combine the local experts into moe_out, sum it over the EP group,
+      // and let the consumers add the summed vector to the residual stream
+      ma.defer_combine = 0; ma.out = m->moe_out;
+      LAUNCH(launch_moe_mxfp4(dc, ma, s));
+      nk += 2;   // gate/up, down, combine
+      NcclApi* api = nccl_api();
+      ncclResult_t r = api->all_reduce(m->moe_out, m->moe_out, (size_t)H, ncclFloat32, ncclSum, m->comm, s);
+      if (r != ncclSuccess) return fail(m->ctx, MS_ERR_NCCL, "ncclAllReduce: %s", api->error_string(r));
+      pend.dense = m->moe_out;
+    } else {
+      // single device: a small combine kernel adds the experts (ascending id) into h
+      ma.defer_combine = 0;
+      LAUNCH(launch_moe_mxfp4(dc, ma, s));
+      nk += 2;   // gate/up, down, combine
+    }
   }
   LmHeadArgs la;
   la.w = m->out_w; la.x = m->h; la.norm_w = m->out_norm; la.eps = c.eps; la.bias = m->out_b; la.logits = m->logits;
-  la.key = &m->st->key; la.V = c.vocab; la.H = H;
+  la.key = &m->st->key; la.V = c.vocab; la.H = H; la.x_pend = pend; la.x_out = m->h_last;
   LAUNCH(launch_lmhead(dc, la, s));
 #undef LAUNCH
   m->kernels_per_step = nk;
@@ -361,6 +412,7 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
 
 ms_status run_step(ms_model* m) {
   cudaStream_t s = m->ctx->stream;
+  if (m->cfg.ep_size > 1 && !m->comm) return fail(m->ctx, MS_ERR_STATE, "expert-parallel model: call ms_model_init_ep first");
   if (!m->use_graph) return enqueue_step(m, s);
   if (!m->graph) {
     // capture on the context's private stream (the caller's stream may be the legacy default
@@ -678,6 +730,8 @@ ms_status ms_model_finalize(ms_model* m) {
   m->splits_swa = c.sliding_window > 0 ? std::max(1, std::min(S, (c.sliding_window + 31) / 32)) : S;
   ms_status s = MS_OK;
   s = s ? s : m->alloc(&m->h, (size_t)H * 4);
+  s = s ? s : m->alloc(&m->h_last, (size_t)H * 4);
+  s = s ? s : m->alloc(&m->moe_out, (size_t)H * 4);
   s = s ? s : m->alloc(&m->qkv, (size_t)(Dq + 2 * Dkv) * 4);
   s = s ? s : m->alloc(&m->attn_out, (size_t)Dq * 4);
   s = s ? s : m->alloc(&m->xn, (size_t)H * 4);
@@ -716,6 +770,7 @@ ms_status ms_model_destroy(ms_model* m) {
   cudaSetDevice(m->ctx->device);
   cudaStreamSynchronize(m->ctx->stream);
   if (m->graph) cudaGraphExecDestroy(m->graph);
+  if (m->comm) nccl_api()->comm_destroy(m->comm);
   for (void* p : m->allocs) cudaFree(p);
   if (m->h_tok) cudaFreeHost(m->h_tok);
   if (m->h_st) cudaFreeHost(m->h_st);
@@ -850,7 +905,7 @@ ms_status ms_model_generate(ms_model* m, const int32_t* prompt, int n_prompt, in
 ms_status ms_model_last_hidden(ms_model* m, float* out) {
   if (!m || !out) return MS_ERR_INVALID_ARG;
   MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
-  MS_CUDA(m->ctx, cudaMemcpy(out, m->h, (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost));
+  MS_CUDA(m->ctx, cudaMemcpy(out, m->h_last, (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost));
   return MS_OK;
 }
 
@@ -866,6 +921,32 @@ ms_status ms_model_last_logits(ms_model* m, float* out) {
   if (!m || !out) return MS_ERR_INVALID_ARG;
   MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
   MS_CUDA(m->ctx, cudaMemcpy(out, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost));
+  return MS_OK;
+}
+
+ms_status ms_nccl_unique_id(ms_ctx* c, void* out, size_t bytes) {
+  if (!c || !out || bytes < sizeof(ncclUniqueId)) return MS_ERR_INVALID_ARG;
+  NcclApi* api = nccl_api();
+  if (!api) return fail(c, MS_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  ncclUniqueId id;
+  ncclResult_t r = api->get_unique_id(&id);
+  if (r != ncclSuccess) return fail(c, MS_ERR_NCCL, "ncclGetUniqueId: %s", api->error_string(r));
+  memcpy(out, &id, sizeof id);
+  return MS_OK;
+}
+
+ms_status ms_model_init_ep(ms_model* m, const void* unique_id, size_t bytes) {
+  if (!m || !unique_id || bytes < sizeof(ncclUniqueId)) return MS_ERR_INVALID_ARG;
+  if (m->cfg.ep_size <= 1) return MS_OK;
+  if (m->comm) return fail(m->ctx, MS_ERR_STATE, "expert-parallel group already initialised");
+  NcclApi* api = nccl_api();
+  if (!api) return fail(m->ctx, MS_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  cudaSetDevice(m->ctx->device);
+  ncclUniqueId id;
+  memcpy(&id, unique_id, sizeof id);
+  ncclResult_t r = api->comm_init_rank(&m->comm, m->cfg.ep_size, id, m->cfg.ep_rank);
+  if (r != ncclSuccess) { m->comm = nullptr; return fail(m->ctx, MS_ERR_NCCL, "ncclCommInitRank: %s", api->error_string(r)); }
+  if (m->graph) { cudaGraphExecDestroy(m->graph); m->graph = nullptr; }
   return MS_OK;
 }
 

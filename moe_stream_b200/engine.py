@@ -195,6 +195,18 @@ class Engine:
             raise
         return cls(h, ctx)
 
+    @staticmethod
+    def nccl_unique_id(ctx: Context) -> bytes:
+        """128-byte NCCL id for an expert-parallel group (rank 0 makes it, every rank receives it)."""
+        buf = (C.c_uint8 * 128)()
+        check(lib().ms_nccl_unique_id(ctx.h, buf, 128), ctx.h)
+        return bytes(buf)
+
+    def init_ep(self, unique_id: bytes) -> None:
+        """Join the expert-parallel group (all-reduce of each layer's MoE output)."""
+        buf = (C.c_uint8 * 128).from_buffer_copy(unique_id[:128])
+        check(lib().ms_model_init_ep(self.h, buf, 128), self.ctx.h)
+
     def preload_weights(self) -> None:
         """Weights are uploaded to HBM at open; nothing to preload (engine.rs:1551)."""
 

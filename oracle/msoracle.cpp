@@ -354,7 +354,7 @@ void rope_apply(float* x, int rot_dim, const float* c, const float* s) {
 // ---------------------------------------------------------------------------
 // MoE FFN (layer.rs:756-1895, default f32 path)
 int moe_forward(const orc_moe_layer* L, const float* x, int n_tok, float* out, int32_t* idx_out, float* w_out,
-                const std::vector<int>* dummies, int threads) {
+                const std::vector<int>* dummies, int threads, int e_begin = 0, int e_end = 1 << 30) {
   const int H = L->hidden, I = L->inter, E = L->n_experts, K = L->top_k;
   std::vector<float> logits((size_t)n_tok * E);
   matmul_xwt(x, n_tok, L->router_w, E, H, logits.data(), threads);       // layer.rs:818-820
@@ -376,6 +376,7 @@ int moe_forward(const orc_moe_layer* L, const float* x, int n_tok, float* out, i
   std::vector<float> Wg((size_t)I * H), Wu((size_t)I * H), Wd((size_t)H * I);
   for (auto& kv : assign) {   // std::map iterates in ascending expert order (layer.rs:1797)
     const int e = kv.first; const auto& as = kv.second;
+    if (e < e_begin || e >= e_end) continue;   // expert-parallel restriction (test decomposition)
     dequant_matrix(L->gate_q, (const uint8_t*)L->gate + e * gsz, I, H, Wg.data(), threads);  // layer.rs:1750-1762
     dequant_matrix(L->up_q, (const uint8_t*)L->up + e * usz, I, H, Wu.data(), threads);
     dequant_matrix(L->down_q, (const uint8_t*)L->down + e * dsz, H, I, Wd.data(), threads);
@@ -661,6 +662,9 @@ int orc_gemv(int qtype, const void* w, int64_t rows, int64_t cols, const float* 
 void orc_q8_0_gemv(const uint8_t* w, int64_t rows, int64_t cols, const float* x, float* y, int mode) {
   if (mode == 1) { q8_0_gemv_actq(w, rows, cols, x, y, hw_threads()); return; }
   orc_gemv(ORC_Q8_0, w, rows, cols, x, y);
+}
+int orc_moe_forward_range(const orc_moe_layer* L, const float* x, int n_tok, float* out, int e_begin, int e_end) {
+  return moe_forward(L, x, n_tok, out, nullptr, nullptr, nullptr, hw_threads(), e_begin, e_end);
 }
 void orc_sdpa(const float* q, const float* k, const float* v, int nh, int nkv, int seq_q, int seq_k, int hd,
               double scale, int causal, const float* sinks, int sliding_window, float* out) {

@@ -68,6 +68,9 @@ typedef struct {
 int orc_moe_forward(const orc_moe_layer* L, const float* x, int n_tok, float* out,
                     int32_t* idx_out /* [n_tok*k] or NULL */, float* w_out /* or NULL */);
 
+/* the same layer restricted to experts [e_begin, e_end) (routing over all experts) */
+int orc_moe_forward_range(const orc_moe_layer* L, const float* x, int n_tok, float* out, int e_begin, int e_end);
+
 /* ---- whole model (engine.rs:1869-2118) ---- */
 typedef struct orc_model orc_model;
 /* open a GGUF file (reader.rs:259-368, config.rs:253-434) */

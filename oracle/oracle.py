@@ -59,6 +59,7 @@ def lib():
         L.orc_silu_and_mul.argtypes = [_fp, _fp, _fp, C.c_int64]
         L.orc_top_k_routing.argtypes = [_fp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _i32p, _fp]
         L.orc_moe_forward.argtypes = [C.POINTER(MoeLayer), _fp, C.c_int, _fp, _i32p, _fp]
+        L.orc_moe_forward_range.argtypes = [C.POINTER(MoeLayer), _fp, C.c_int, _fp, C.c_int, C.c_int]
         L.orc_model_open.restype = _vp
         L.orc_model_open.argtypes = [C.c_char_p, C.c_int, C.c_char_p, C.c_int]
         L.orc_model_set_attn_mode.argtypes = [_vp, C.c_int]
@@ -167,7 +168,7 @@ def top_k_routing(logits: np.ndarray, k: int, normalize: bool, softmax_weight: b
     return idx, w
 
 
-def moe_forward(layer: dict, x: np.ndarray):
+def moe_forward(layer: dict, x: np.ndarray, expert_range=None):
     """One MoE FFN layer on the default CPU path.  ``layer`` holds numpy arrays:
     gate/up/down (raw stacked blocks), *_bias, router_w, router_b, and ints."""
     x = np.ascontiguousarray(x, dtype=np.float32)
@@ -190,6 +191,9 @@ def moe_forward(layer: dict, x: np.ndarray):
     out = np.empty((n_tok, layer["hidden"]), dtype=np.float32)
     idx = np.empty((n_tok, layer["top_k"]), dtype=np.int32)
     w = np.empty((n_tok, layer["top_k"]), dtype=np.float32)
+    if expert_range is not None:
+        lib().orc_moe_forward_range(C.byref(L), _f(x), n_tok, _f(out), int(expert_range[0]), int(expert_range[1]))
+        return out, None, None
     lib().orc_moe_forward(C.byref(L), _f(x), n_tok, _f(out), _i(idx), _f(w))
     return out, idx, w
 

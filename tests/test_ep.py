@@ -1,0 +1,101 @@
+"""Expert parallelism.
+
+CPU (gloo, world size 2): the decomposition the CUDA path uses — each rank combines only its
+contiguous expert slice [rank*E/N, (rank+1)*E/N), then a sum all-reduce — reproduces the
+single-device MoE layer (oracle, routing over all experts on every rank).
+
+GPU (2 devices): a tiny GPT-OSS-shaped model split over two ranks through the C ABI
+(ms_model_init_ep + in-graph NCCL all-reduce) decodes the same greedy tokens as one device.
+"""
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+
+from moe_stream_b200 import synth
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _layer(spec, seed):
+    m = synth.build_model(spec, seed)
+    t = lambda n: m.tensors["blk.0." + n]
+    f = lambda n: t(n).data.astype(np.float32)
+    return dict(hidden=spec.hidden, inter=spec.inter, n_experts=spec.experts, top_k=spec.top_k,
+                gate_q=spec.expert_gate_q, up_q=spec.expert_gate_q, down_q=spec.expert_down_q,
+                gate=t("ffn_gate_exps.weight").raw(), up=t("ffn_up_exps.weight").raw(),
+                down=t("ffn_down_exps.weight").raw(), gate_bias=f("ffn_gate_exps.bias"),
+                up_bias=f("ffn_up_exps.bias"), down_bias=f("ffn_down_exps.bias"),
+                router_w=f("ffn_gate_inp.weight"), router_b=f("ffn_gate_inp.bias"), oai_swiglu=1, norm_topk_prob=1)
+
+
+def _cpu_rank(rank, world, port, out_path):
+    import torch
+    import torch.distributed as dist
+    from oracle import oracle
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    spec = synth.TINY_GPT_OSS
+    L = _layer(spec, 4)
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((3, spec.hidden)).astype(np.float32)
+    per = spec.experts // world
+    local, _, _ = oracle.moe_forward(L, x, expert_range=(rank * per, (rank + 1) * per))
+    t = torch.from_numpy(local.copy())
+    dist.all_reduce(t)
+    if rank == 0:
+        np.save(out_path, t.numpy())
+    dist.destroy_process_group()
+
+
+def test_ep_decomposition_gloo(orc, tmp_path):
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "ep.npy")
+    mp.spawn(_cpu_rank, args=(2, _free_port(), out), nprocs=2, join=True)
+    spec = synth.TINY_GPT_OSS
+    L = _layer(spec, 4)
+    x = np.random.default_rng(8).standard_normal((3, spec.hidden)).astype(np.float32)
+    full, _, _ = orc.moe_forward(L, x)
+    got = np.load(out)
+    assert np.abs(got - full).max() / np.abs(full).max() < 1e-5
+
+
+def _gpu_rank(rank, world, port, path, prompt, out_dir):
+    import torch
+    import torch.distributed as dist
+    from moe_stream_b200.engine import Context, Engine
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    ctx = Context(rank)
+    eng = Engine.open(path, max_seq_len=256, ep_rank=rank, ep_size=world, ctx=ctx)
+    uid = [Engine.nccl_unique_id(ctx) if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    eng.init_ep(uid[0])
+    toks = eng.generate(prompt, 16)
+    np.save(os.path.join(out_dir, f"tok{rank}.npy"), np.array(toks, np.int32))
+    eng.close()
+    ctx.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_ep_two_gpus_greedy_tokens(tmp_path):
+    import torch
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    f = np.load(os.path.join(GOLD, "tiny_models.npz"))
+    path = str(tmp_path / "tiny.gguf")
+    synth.write_model(path, synth.TINY_GPT_OSS, seed=7)
+    mp.spawn(_gpu_rank, args=(2, _free_port(), path, f["tiny_gpt_oss_prompt"], str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        assert np.load(str(tmp_path / f"tok{r}.npy")).tolist() == f["tiny_gpt_oss_tokens"].tolist()
