@@ -266,7 +266,6 @@ def run_ours(args):
         torch.distributed.barrier()
     kps = eng.kernels_per_step
     ctx.sync()
-
     # ---- end to end through the C ABI with host buffers ----
     e2e_s = float("nan")
     if not args.no_e2e:
@@ -280,6 +279,16 @@ def run_ours(args):
         t = torch.tensor([e2e_s], device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         e2e_s = float(t.item())
+    # per-class device time of one step: each kernel class's launches alone in a PDL-chained graph
+    # (overwrites activations and KV cache, so it runs after the timed and end-to-end decodes)
+    breakdown = None
+    if not ep and not args.no_profile:
+        us = eng.profile_step()
+        names = ["embed", "qkv_q8", "attention", "o_q8", "router", "moe_gate_up", "moe_down", "resid_norm_q8",
+                 "lm_head"]
+        breakdown = {names[i] if len(us) == len(names) else f"class{i}": round(v, 1) for i, v in enumerate(us)}
+        breakdown["sum_us"] = round(sum(us), 1)
+        log(f"[rank {rank}] per-step kernel-class us: {breakdown}")
     eng.close()
 
     # ---- roofline of the dominant kernel pair (MXFP4 expert FFN) ----
@@ -317,6 +326,7 @@ def run_ours(args):
                      "us_per_launch_pair": round(moe_ms * 1000, 2), "traffic": traffic},
         "gpu_launches": kps * args.steps,
         "kernels_per_step": kps,
+        "kernel_us_per_step": breakdown,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
     }
@@ -345,6 +355,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-roofline", action="store_true", help="skip the expert-FFN roofline leg")
+    ap.add_argument("--no-profile", action="store_true", help="skip the per-kernel-class breakdown")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (default 2048)")
     ap.add_argument("--layers", type=int, default=0, help="profiling only: override the layer count")
     ap.add_argument("--mode", default="ep", choices=["ep", "replicas"],

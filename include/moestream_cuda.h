@@ -68,6 +68,7 @@ MS_API const char* ms_status_string(ms_status s);
 
 /* ---- context (replaces Device::new_metal, engine.rs:277-298) ---- */
 MS_API ms_status ms_ctx_create(int device, ms_ctx** out);
+/* Also destroys any model of this context that is still open (its handle becomes invalid). */
 MS_API ms_status ms_ctx_destroy(ms_ctx* ctx);
 /* Enqueue work on a caller-owned cudaStream_t (NULL = the legacy default stream). */
 MS_API ms_status ms_ctx_set_stream(ms_ctx* ctx, void* cuda_stream);
@@ -96,7 +97,8 @@ MS_API ms_status ms_dequantize(ms_ctx* ctx, int qtype, const void* d_blocks, int
 MS_API ms_status ms_rms_norm(ms_ctx* ctx, const float* d_x, const float* d_w, float* d_y, int rows, int dim, float eps);
 
 /* y = W x (+bias) for one token, W [rows, cols] in native blocks.  Replaces
- * mxfp4_matmul_metal_gpu (metal/mod.rs:896-962) for MXFP4 (W allocation padded to 16 rows),
+ * mxfp4_matmul_metal_gpu (metal/mod.rs:896-962) for MXFP4 and the CPU QMatMul / dequant matmul
+ * of Q4_K and Q6_K (model/layer.rs:1516-1748; W allocation padded to 16 rows),
  * quantized_attn_matmul_metal_gpu_batched (metal/mod.rs:1123-1141) for Q8_0 (activation quantized
  * to Q8_0 as the CPU QMatMul path does), and the dense f16/f32 matmuls. */
 MS_API ms_status ms_gemv(ms_ctx* ctx, int qtype, const void* d_w, int rows, int cols, const float* d_x,
@@ -191,6 +193,12 @@ MS_API ms_status ms_model_last_routing(ms_model* m, int layer, int32_t* idx, flo
 MS_API ms_status ms_model_last_logits(ms_model* m, float* out);
 /* 1 (default): replay each step as a captured CUDA graph; 0: plain stream launches. */
 MS_API ms_status ms_model_set_graph(ms_model* m, int enable);
+/* Tracing (single device, after at least one decode step): the decode step's launches grouped by
+ * class -- 0 = embedding, 1..P = the P kernels of a layer by their position in it, P+1 = LM head --
+ * and each class's launches of one step captured alone into a PDL-chained graph and timed over
+ * ten launches: us[c] = device microseconds per step spent on class c.  The runs overwrite the
+ * model's activations and KV cache: call ms_model_clear_cache before decoding again. */
+MS_API ms_status ms_model_profile_step(ms_model* m, float* us, int max, int* n);
 /* Kernel launches per decode step (for launch accounting). */
 MS_API int ms_model_kernels_per_step(const ms_model* m);
 

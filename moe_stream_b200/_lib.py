@@ -83,6 +83,7 @@ _SIGS = {
     "ms_model_last_logits": (C.c_int, [_vp, _fp]),
     "ms_model_set_graph": (C.c_int, [_vp, _i]),
     "ms_model_kernels_per_step": (C.c_int, [_vp]),
+    "ms_model_profile_step": (C.c_int, [_vp, _fp, _i, C.POINTER(C.c_int)]),
 }
 
 

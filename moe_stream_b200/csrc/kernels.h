@@ -67,8 +67,8 @@ struct Q8GemvArgs {
   float* y = nullptr;          // output (ignored when residual != null)
   float* residual = nullptr;   // residual[r] += W x + bias
   int exact = 0;               // 1: f32 activations (no quantization), for the exact-mode oracle
-  PendingCombine x_pend;       // applied to x before use (x is a residual stream)
-  PendingCombine res_pend;     // applied to residual before the add
+  const int8_t* xq_in = nullptr;  // activation already quantized by its producer: int8 codes [cols]
+  const float* xd_in = nullptr;   // and block scales [cols / 32]; x / norm_w are then unused
 };
 cudaError_t launch_q8_gemv(const DevCtx& c, const Q8GemvArgs& a, cudaStream_t s);
 
@@ -98,7 +98,9 @@ struct MoeArgs {
   const float* x = nullptr;        // [H] normed input
   const int* idx = nullptr;        // [K] selected expert ids
   const float* wts = nullptr;      // [K] routing weights
-  const uint8_t* gate = nullptr;   // [E_local, I, H] MXFP4 (native blocks)
+  int gate_q = Q_MXFP4;            // qtype of gate/up: MXFP4 or Q4_K
+  int down_q = Q_MXFP4;            // qtype of down: MXFP4 or Q6_K (or Q4_K)
+  const uint8_t* gate = nullptr;   // [E_local, I, H] native blocks
   const uint8_t* up = nullptr;     // [E_local, I, H]
   const uint8_t* down = nullptr;   // [E_local, H, I]
   const float* gate_b = nullptr;   // [E_local, I] or null
@@ -118,8 +120,8 @@ cudaError_t launch_moe_mxfp4(const DevCtx& c, const MoeArgs& a, cudaStream_t s);
 // the combine as its own kernel: h[r] += comb(r), or out[r] = comb(r) when out != null
 cudaError_t launch_moe_combine(const DevCtx& c, const PendingCombine& pc, int H, float* h, float* out,
                                cudaStream_t s);
-// plain MXFP4 GEMV through the same streaming machinery: y = W x (+bias) (+= when accumulate)
-cudaError_t launch_mxfp4_gemv(const DevCtx& c, const uint8_t* w, int rows, int cols, const float* x,
+// plain MXFP4 / Q4_K / Q6_K GEMV through the same streaming machinery: y = W x (+bias) (+= when accumulate)
+cudaError_t launch_block_gemv(const DevCtx& c, int qtype, const uint8_t* w, int rows, int cols, const float* x,
                               const float* bias, float* y, int accumulate, cudaStream_t s);
 
 // ---- attention (decode, one token) ----
@@ -140,10 +142,14 @@ struct AttnArgs {
   float* part = nullptr;           // scratch [nkv][S][rep][hd + 2]
   uint32_t* cnt = nullptr;         // [nkv] zero-initialised, self-resetting
   float* out = nullptr;            // [nh*hd]
+  int8_t* oq = nullptr;            // optional Q8_0 codes of out [nh*hd] (for the O-projection)
+  float* od = nullptr;             // and their block scales [nh*hd/32]
   int nh = 0, nkv = 0, hd = 0, S = 0;
   float scale = 1.0f;
 };
 cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s);
+// splits (grid.x) needed to cover `range` attended positions (128 positions per split)
+int attn_splits(int range);
 
 // ---- LM head / f16 GEMV ----
 // logits = W (RMSNorm(h)*norm_w if norm_w) (+bias); argmax (lowest index on ties) into *key.
@@ -157,7 +163,6 @@ struct LmHeadArgs {
   unsigned long long* key = nullptr;  // argmax key (value, index) or null; caller zeroes it
   int V = 0, H = 0;
   int accumulate = 0;
-  PendingCombine x_pend;              // applied to x first
   float* x_out = nullptr;             // effective x (before the norm) written by CTA 0, or null
 };
 cudaError_t launch_lmhead(const DevCtx& c, const LmHeadArgs& a, cudaStream_t s);
@@ -181,6 +186,10 @@ struct StepState {
 };
 // token -> embedding row (f16 or f32 table) -> h; advances pos; resets the argmax key
 cudaError_t launch_embed(const DevCtx& c, StepState* st, const void* table, int table_q, int H, int vocab,
-                         float* h, int* token_log, cudaStream_t s);
+                         float* h, int* token_log, cudaStream_t s, const float* norm_w = nullptr, float eps = 0.f,
+                         int8_t* xq = nullptr, float* xd = nullptr);
+// h += MoE output, then (norm_w set) RMSNorm + Q8_0 quantization of h for the next projection
+cudaError_t launch_resid_norm_q8(const DevCtx& c, const PendingCombine& pc, float* h, int H, const float* norm_w,
+                                 float eps, int8_t* xq, float* xd, cudaStream_t s);
 
 }  // namespace ms

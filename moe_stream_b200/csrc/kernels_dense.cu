@@ -121,6 +121,52 @@ __global__ void rms_norm_kernel(const float* __restrict__ x, const float* __rest
 // 34 bytes (f16 d + 32 int8) at a 2-byte aligned offset, read with aligned words and a
 // 16-bit funnel shift, dotted with __dp4a.  Block sums follow candle's Q8_0 vec_dot:
 // (float)sum_i * d_w * d_x accumulated in f32.
+// Q8_0 quantization of one 32-element block as candle's BlockQ8_0::from_float does:
+// d = amax / 127 (stored as f16), q = roundf(x / d) with the unrounded f32 d.
+__device__ __forceinline__ void quantize_q8_block(const float (&v)[32], int8_t* q, float* d_out) {
+  float amax = 0.f;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) amax = fmaxf(amax, fabsf(v[k]));
+  const float d = amax / 127.0f;
+  const float id = d != 0.0f ? 1.0f / d : 0.0f;
+  int qw[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    uint32_t u = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) u |= ((uint32_t)(uint8_t)(int8_t)roundf(v[4 * k + j] * id)) << (8 * j);
+    qw[k] = (int)u;
+  }
+  int4* dst = reinterpret_cast<int4*>(q);
+  dst[0] = make_int4(qw[0], qw[1], qw[2], qw[3]);
+  dst[1] = make_int4(qw[4], qw[5], qw[6], qw[7]);
+  *d_out = __half2float(__float2half_rn(d));
+}
+
+// Whole-CTA RMSNorm (weights w) of xs[0..H) in shared memory, then Q8_0 quantization into
+// xq / xd (one thread per 32-element block).  red: >= 32 floats of shared scratch.
+__device__ __forceinline__ void cta_rmsnorm_q8(const float* xs, int H, const float* w, float eps, int8_t* xq,
+                                               float* xd, float* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) ss += xs[i] * xs[i];
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float t = 0.f;
+  for (int k = 0; k < nw; ++k) t += red[k];
+  const float inv = 1.0f / sqrtf(t / (float)H + eps);
+  for (int b = threadIdx.x; b < H / 32; b += blockDim.x) {
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      const int kk = (k + lane) & 31;   // rotate the start so lanes hit different banks
+      v[kk] = (xs[32 * b + kk] * inv) * w[32 * b + kk];
+    }
+    quantize_q8_block(v, xq + 32 * b, &xd[b]);
+  }
+}
+
 constexpr int kQW = 8;
 constexpr int kQThreads = (kQW + 1) * 32;
 constexpr int kQMaxStages = 8;
@@ -134,7 +180,8 @@ struct Q8Params {
   const float* bias;
   float* y;
   float* residual;
-  PendingCombine x_pend, res_pend;
+  const int8_t* xq_in;
+  const float* xd_in;
   uint32_t* err;
 };
 
@@ -188,72 +235,47 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
     return;
   }
 
-  // ---- consumer prologue: (RMSNorm) + Q8_0 quantization of the activation ----
+  // ---- consumer prologue: the activation's Q8_0 blocks in registers.  They come quantized
+  // from the producing kernel (xq_in / xd_in), or are made here: (RMSNorm) + Q8_0 quantization.
   pdl_wait_prior();
   const int nct = kQW * 32;
-  __shared__ CombineOrder xco, rco;
-  if (threadIdx.x == 0) {
-    xco.n = 0; rco.n = 0;
-    if (p.x_pend.active()) combine_order(p.x_pend, &xco);
-    if (p.res_pend.active()) combine_order(p.res_pend, &rco);
-  }
-  named_bar(1, nct);
-  const bool xp = p.x_pend.active();
-  float inv = 1.f;
-  if (p.norm_w) {
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < p.cols; i += nct) {
-      const float v = xp ? p.x[i] + combine_at(p.x_pend, xco, p.cols, i) : p.x[i];
-      ss += v * v;
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
-    named_bar(1, nct);
-    float t = 0.f;
-    for (int w = 0; w < kQW; ++w) t += red[w];
-    inv = 1.0f / sqrtf(t / (float)p.cols + p.eps);
-  }
-  // one thread per 32-element block: (RMSNorm) -> Q8_0 (d = amax/127 as f16, q = roundf(x/d))
-  for (int b = threadIdx.x; b < nb; b += nct) {
-    float v[32];
-    const float4* x4 = reinterpret_cast<const float4*>(p.x + 32 * b);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float4 t = x4[k];
-      v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
-    }
-    if (xp) {
-#pragma unroll
-      for (int k = 0; k < 32; ++k) v[k] = v[k] + combine_at(p.x_pend, xco, p.cols, 32 * b + k);
-    }
+  const int8_t* xqs = p.xq_in;
+  const float* xds = p.xd_in;
+  if (!xqs) {
+    float inv = 1.f;
     if (p.norm_w) {
-      const float4* w4 = reinterpret_cast<const float4*>(p.norm_w + 32 * b);
+      float ss = 0.f;
+      for (int i = threadIdx.x; i < p.cols; i += nct) { const float v = p.x[i]; ss += v * v; }
+      ss = warp_sum(ss);
+      if (lane == 0) red[warp] = ss;
+      named_bar(1, nct);
+      float t = 0.f;
+      for (int w = 0; w < kQW; ++w) t += red[w];
+      inv = 1.0f / sqrtf(t / (float)p.cols + p.eps);
+    }
+    for (int b = threadIdx.x; b < nb; b += nct) {
+      float v[32];
+      const float4* x4 = reinterpret_cast<const float4*>(p.x + 32 * b);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const float4 t = w4[k];
-        v[4 * k] = (v[4 * k] * inv) * t.x; v[4 * k + 1] = (v[4 * k + 1] * inv) * t.y;
-        v[4 * k + 2] = (v[4 * k + 2] * inv) * t.z; v[4 * k + 3] = (v[4 * k + 3] * inv) * t.w;
+        const float4 t = x4[k];
+        v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
       }
+      if (p.norm_w) {
+        const float4* w4 = reinterpret_cast<const float4*>(p.norm_w + 32 * b);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float4 t = w4[k];
+          v[4 * k] = (v[4 * k] * inv) * t.x; v[4 * k + 1] = (v[4 * k + 1] * inv) * t.y;
+          v[4 * k + 2] = (v[4 * k + 2] * inv) * t.z; v[4 * k + 3] = (v[4 * k + 3] * inv) * t.w;
+        }
+      }
+      quantize_q8_block(v, xq + 32 * b, &xd[b]);
     }
-    float amax = 0.f;
-#pragma unroll
-    for (int k = 0; k < 32; ++k) amax = fmaxf(amax, fabsf(v[k]));
-    const float d = amax / 127.0f;
-    const float id = d != 0.0f ? 1.0f / d : 0.0f;
-    int qw[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      uint32_t u = 0;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) u |= ((uint32_t)(uint8_t)(int8_t)roundf(v[4 * k + q] * id)) << (8 * q);
-      qw[k] = (int)u;
-    }
-    int4* dst = reinterpret_cast<int4*>(xq + 32 * b);
-    dst[0] = make_int4(qw[0], qw[1], qw[2], qw[3]);
-    dst[1] = make_int4(qw[4], qw[5], qw[6], qw[7]);
-    xd[b] = __half2float(__float2half_rn(d));
+    named_bar(1, nct);
+    xqs = xq;
+    xds = xd;
   }
-  named_bar(1, nct);
   int xr[NBL][8];
   float xdr[NBL];
 #pragma unroll
@@ -263,11 +285,11 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) xr[i][k] = 0;
     if (b < nb) {
-      const int4* q4 = reinterpret_cast<const int4*>(xq + 32 * b);
+      const int4* q4 = reinterpret_cast<const int4*>(xqs + 32 * b);
       const int4 a0 = q4[0], a1 = q4[1];
       xr[i][0] = a0.x; xr[i][1] = a0.y; xr[i][2] = a0.z; xr[i][3] = a0.w;
       xr[i][4] = a1.x; xr[i][5] = a1.y; xr[i][6] = a1.z; xr[i][7] = a1.w;
-      xdr[i] = xd[b];
+      xdr[i] = xds[b];
     }
   }
 
@@ -307,12 +329,8 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
     if (ok && warp < nr && lane == 0) {
       const int r = r0 + warp;
       const float v = acc + (p.bias ? p.bias[r] : 0.f);
-      if (p.residual) {
-        const float base = p.res_pend.active() ? p.residual[r] + combine_at(p.res_pend, rco, p.rows, r) : p.residual[r];
-        p.residual[r] = base + v;
-      } else {
-        p.y[r] = v;
-      }
+      if (p.residual) p.residual[r] = p.residual[r] + v;
+      else p.y[r] = v;
     }
     if (!ok) break;
   }
@@ -338,8 +356,15 @@ cudaError_t launch_q8(const DevCtx& c, const Q8Params& p, cudaStream_t s) {
 }
 
 // ============================ attention (decode) ============================
-constexpr int kAT = 64;        // positions per tile
-constexpr int kAThreads = 128;
+// Grid (splits, kv_heads), 4 warps per CTA, one cached position per lane: a split covers 128
+// consecutive positions.  Each lane dots its K row (read straight from the f32 cache) with
+// every query head of the GQA group (queries broadcast from shared memory); each warp keeps
+// its own softmax max/sum per head; P*V runs with lanes over head dimensions; the four warps
+// merge in shared memory; the last CTA of a kv head merges the splits, with the attention sink
+// in the denominator (ops/attention.rs:178-280).
+constexpr int kAWarps = 4;
+constexpr int kAThreads = kAWarps * 32;
+constexpr int kASplit = kAWarps * 32;   // positions per split
 
 __device__ __forceinline__ void rope_inplace(float* v, int rot, const float* c, const float* s) {
   // ops/attention.rs:96-118: half-rotate over the first `rot` dims
@@ -362,124 +387,126 @@ __device__ __forceinline__ void head_norm_warp(float* v, const float* w, int hd,
   __syncwarp();
 }
 
+template <int HD, int REP>
 __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint32_t* err) {
-  extern __shared__ __align__(16) float sm[];
-  const int rep = a.nh / a.nkv, hd = a.hd, hdp = hd + 1;
-  float* qs = sm;                          // [rep][hd]
-  float* kt = qs + rep * hd;               // [kAT][hd+1]
-  float* vt = kt + kAT * hdp;              // [kAT][hd]
-  float* sc = vt + kAT * hd;               // [rep][kAT]
-  float* os = sc + rep * kAT;              // [rep][hd]
-  float* ml = os + rep * hd;               // [rep][2] running max, sum
-  float* corr = ml + 2 * rep;              // [rep]
-  float* kn = corr + rep;                  // [hd] new k
-  float* vn = kn + hd;                     // [hd] new v
+  constexpr int DL = HD / 32;                  // head dims per lane in P*V
+  __shared__ __align__(16) float qs[REP * HD];
+  __shared__ __align__(16) float kn[HD];
+  __shared__ __align__(16) float vn[HD];
+  __shared__ float pw[kAWarps][REP][32];
+  __shared__ float mw[kAWarps][REP], lw[kAWarps][REP];
+  __shared__ __align__(16) float ow[kAWarps][REP][HD];
   __shared__ uint32_t last;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kh = blockIdx.y, sidx = blockIdx.x, S = gridDim.x;
   pdl_wait_prior();
   const int pos = *a.pos;
   const int lo = a.window ? max(0, pos - a.window + 1) : 0;
-  const int n = pos - lo + 1;
-  const int chunk = (n + S - 1) / S;
-  const int p0 = lo + sidx * chunk, p1 = min(p0 + chunk, pos + 1);
-  const bool has_new = (p0 < p1) && (p1 == pos + 1);
+  const int p0 = lo + sidx * kASplit, p1 = min(p0 + kASplit, pos + 1);
+  const bool active = p0 < p1;
+  const bool has_new = active && p1 == pos + 1;
   const int half = a.rot / 2;
-  const float* cs = a.cos_t + (size_t)pos * half;
-  const float* sn = a.sin_t + (size_t)pos * half;
-
-  // q heads of this kv group (+ QK-norm, RoPE)
-  for (int i = threadIdx.x; i < rep * hd; i += blockDim.x) qs[i] = a.qkv[(size_t)kh * rep * hd + i];
-  for (int i = threadIdx.x; i < rep * 2; i += blockDim.x) ml[i] = (i & 1) ? 0.f : -INFINITY;
-  for (int i = threadIdx.x; i < rep * hd; i += blockDim.x) os[i] = 0.f;
-  if (has_new) {
-    const float* kq = a.qkv + (size_t)a.nh * hd + (size_t)kh * hd;
-    const float* vq = a.qkv + (size_t)a.nh * hd + (size_t)a.nkv * hd + (size_t)kh * hd;
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) { kn[i] = kq[i]; vn[i] = vq[i]; }
-  }
-  __syncthreads();
-  if (a.q_norm) {
-    for (int h = warp; h < rep; h += nwarp) head_norm_warp(qs + h * hd, a.q_norm, hd, a.eps, lane);
-    if (has_new && warp == 0) head_norm_warp(kn, a.k_norm, hd, a.eps, lane);
-    __syncthreads();
-  }
-  for (int h = 0; h < rep; ++h) rope_inplace(qs + h * hd, a.rot, cs, sn);
-  if (has_new) rope_inplace(kn, a.rot, cs, sn);
-  __syncthreads();
-  if (has_new) {   // kv_cache.rs:37-60 append (ring slot for sliding-window layers)
-    const int slot = a.window ? pos % a.cap : pos;
-    float* kd = a.kc + ((size_t)kh * a.cap + slot) * hd;
-    float* vd = a.vc + ((size_t)kh * a.cap + slot) * hd;
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) { kd[i] = kn[i]; vd[i] = vn[i]; }
-  }
-
-  for (int t0 = p0; t0 < p1; t0 += kAT) {
-    const int tn = min(kAT, p1 - t0);
-    const int hd4 = hd / 4;
-    for (int i = threadIdx.x; i < tn * hd4; i += blockDim.x) {
-      const int j = i / hd4, d = (i - j * hd4) * 4, p = t0 + j;
-      float4 kv, vv;
-      if (p == pos) { kv = make_float4(kn[d], kn[d + 1], kn[d + 2], kn[d + 3]); vv = make_float4(vn[d], vn[d + 1], vn[d + 2], vn[d + 3]); }
-      else {
-        const int slot = a.window ? p % a.cap : p;
-        kv = *reinterpret_cast<const float4*>(a.kc + ((size_t)kh * a.cap + slot) * hd + d);
-        vv = *reinterpret_cast<const float4*>(a.vc + ((size_t)kh * a.cap + slot) * hd + d);
-      }
-      kt[j * hdp + d] = kv.x; kt[j * hdp + d + 1] = kv.y; kt[j * hdp + d + 2] = kv.z; kt[j * hdp + d + 3] = kv.w;
-      *reinterpret_cast<float4*>(vt + j * hd + d) = vv;
+  float* part = a.part + ((size_t)kh * S + sidx) * REP * (HD + 2);
+  if (active) {
+    const float* cs = a.cos_t + (size_t)pos * half;
+    const float* sn = a.sin_t + (size_t)pos * half;
+    for (int i = threadIdx.x; i < REP * HD; i += kAThreads) qs[i] = a.qkv[(size_t)kh * REP * HD + i];
+    if (has_new) {
+      const float* kq = a.qkv + (size_t)a.nh * HD + (size_t)kh * HD;
+      const float* vq = kq + (size_t)a.nkv * HD;
+      for (int i = threadIdx.x; i < HD; i += kAThreads) { kn[i] = kq[i]; vn[i] = vq[i]; }
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < rep * kAT; i += blockDim.x) {
-      const int h = i / kAT, j = i - h * kAT;
-      float s = -INFINITY;
-      if (j < tn) {
-        const float* q = qs + h * hd;
-        const float* k = kt + j * hdp;
-        float dot = 0.f;
-        for (int d = 0; d < hd; ++d) dot = fmaf(q[d], k[d], dot);
-        s = dot * a.scale;
-      }
-      sc[i] = s;
+    if (a.q_norm) {
+      for (int h = warp; h < REP; h += kAWarps) head_norm_warp(qs + h * HD, a.q_norm, HD, a.eps, lane);
+      if (has_new && warp == 0) head_norm_warp(kn, a.k_norm, HD, a.eps, lane);
+      __syncthreads();
     }
+    for (int h = 0; h < REP; ++h) rope_inplace(qs + h * HD, a.rot, cs, sn);
+    if (has_new) rope_inplace(kn, a.rot, cs, sn);
     __syncthreads();
-    for (int h = warp; h < rep; h += nwarp) {   // online softmax update per head
-      float v[kAT / 32];
-      float tm = -INFINITY;
+    if (has_new) {   // kv_cache.rs:37-60 append (ring slot for sliding-window layers)
+      const int slot = a.window ? pos % a.cap : pos;
+      float* kd = a.kc + ((size_t)kh * a.cap + slot) * HD;
+      float* vd = a.vc + ((size_t)kh * a.cap + slot) * HD;
+      for (int i = threadIdx.x; i < HD; i += kAThreads) { kd[i] = kn[i]; vd[i] = vn[i]; }
+    }
+    // ---- scores: one position per lane ----
+    const int p = p0 + warp * 32 + lane;
+    const bool valid = p < p1;
+    const int slot = a.window ? p % a.cap : p;
+    const float* krow = (p == pos) ? kn : a.kc + ((size_t)kh * a.cap + slot) * HD;
+    float dot[REP];
 #pragma unroll
-      for (int u = 0; u < kAT / 32; ++u) { v[u] = sc[h * kAT + 32 * u + lane]; tm = fmaxf(tm, v[u]); }
-      tm = warp_max(tm);
-      const float m_old = ml[2 * h], m_new = fmaxf(m_old, tm);
-      float ps = 0.f;
+    for (int h = 0; h < REP; ++h) dot[h] = 0.f;
+    if (valid) {
+#pragma unroll 4
+      for (int d = 0; d < HD; d += 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(krow + d);
 #pragma unroll
-      for (int u = 0; u < kAT / 32; ++u) {
-        const float pexp = (v[u] == -INFINITY) ? 0.f : expf(v[u] - m_new);
-        sc[h * kAT + 32 * u + lane] = pexp;
-        ps += pexp;
+        for (int h = 0; h < REP; ++h) {
+          const float4 q4 = *reinterpret_cast<const float4*>(qs + h * HD + d);
+          dot[h] = fmaf(q4.x, k4.x, fmaf(q4.y, k4.y, fmaf(q4.z, k4.z, fmaf(q4.w, k4.w, dot[h]))));
+        }
       }
-      const float psum = warp_sum(ps);
-      const float cr = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-      if (lane == 0) { ml[2 * h] = m_new; ml[2 * h + 1] = ml[2 * h + 1] * cr + psum; corr[h] = cr; }
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < rep * hd; i += blockDim.x) {
-      const int h = i / hd, d = i - h * hd;
-      float o = os[i] * corr[h];
-      const float* pp = sc + h * kAT;
-      for (int j = 0; j < tn; ++j) o = fmaf(pp[j], vt[j * hd + d], o);
-      os[i] = o;
+#pragma unroll
+    for (int h = 0; h < REP; ++h) {
+      const float sv = valid ? dot[h] * a.scale : -INFINITY;
+      const float m = warp_max(sv);
+      const float pe = (sv == -INFINITY) ? 0.f : expf(sv - m);
+      const float l = warp_sum(pe);
+      pw[warp][h][lane] = pe;
+      if (lane == 0) { mw[warp][h] = m; lw[warp][h] = l; }
     }
+    __syncwarp();
+    // ---- P * V: lanes over head dims ----
+    float o[REP][DL];
+#pragma unroll
+    for (int h = 0; h < REP; ++h)
+#pragma unroll
+      for (int t = 0; t < DL; ++t) o[h][t] = 0.f;
+    const int nvalid = min(32, p1 - (p0 + warp * 32));
+    for (int j = 0; j < nvalid; ++j) {
+      const int pj = p0 + warp * 32 + j;
+      const int sj = a.window ? pj % a.cap : pj;
+      const float* vrow = (pj == pos) ? vn : a.vc + ((size_t)kh * a.cap + sj) * HD;
+      float v[DL];
+#pragma unroll
+      for (int t = 0; t < DL; ++t) v[t] = vrow[lane + 32 * t];
+#pragma unroll
+      for (int h = 0; h < REP; ++h) {
+        const float pj_h = pw[warp][h][j];
+#pragma unroll
+        for (int t = 0; t < DL; ++t) o[h][t] = fmaf(pj_h, v[t], o[h][t]);
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < REP; ++h)
+#pragma unroll
+      for (int t = 0; t < DL; ++t) ow[warp][h][lane + 32 * t] = o[h][t];
     __syncthreads();
-  }
-  // partial (m, l, o) of this split
-  float* part = a.part + ((size_t)kh * S + sidx) * rep * (hd + 2);
-  for (int i = threadIdx.x; i < rep * hd; i += blockDim.x) {
-    const int h = i / hd, d = i - h * hd;
-    part[h * (hd + 2) + 2 + d] = os[i];
-  }
-  for (int h = threadIdx.x; h < rep; h += blockDim.x) {
-    part[h * (hd + 2)] = ml[2 * h];
-    part[h * (hd + 2) + 1] = ml[2 * h + 1];
+    // ---- merge the four warps into this split's (m, l, o) ----
+    for (int i = threadIdx.x; i < REP * HD; i += kAThreads) {
+      const int h = i / HD, d = i - h * HD;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kAWarps; ++w) M = fmaxf(M, mw[w][h]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int w = 0; w < kAWarps; ++w) {
+        const float m = mw[w][h];
+        if (m != -INFINITY) {
+          const float f = expf(m - M);
+          L = fmaf(lw[w][h], f, L);
+          O = fmaf(ow[w][h][d], f, O);
+        }
+      }
+      part[h * (HD + 2) + 2 + d] = O;
+      if (d == 0) { part[h * (HD + 2)] = M; part[h * (HD + 2) + 1] = L; }
+    }
+  } else {
+    for (int h = threadIdx.x; h < REP; h += kAThreads) { part[h * (HD + 2)] = -INFINITY; part[h * (HD + 2) + 1] = 0.f; }
   }
   __threadfence();
   __syncthreads();
@@ -487,39 +514,38 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
   __syncthreads();
   if (!last) return;
   __threadfence();
-  // merge the splits of this kv group (+ attention sink in the denominator): stage every
-  // split's (m, l) in shared memory, form per-split weights, then a parallel weighted sum
-  const float* gp = a.part + (size_t)kh * S * rep * (hd + 2);
-  float* wsm = sm;                      // [S][rep] split weights (reuses the tile area)
-  float* hm = sm + S * rep;             // [rep] merged max
-  float* hinv = hm + rep;               // [rep] 1 / denominator
-  for (int i = threadIdx.x; i < S * rep; i += blockDim.x) wsm[i] = __ldcg(&gp[(size_t)i * (hd + 2)]);
+  // ---- merge the splits of this kv group (+ attention sink) ----
+  const float* gp = a.part + (size_t)kh * S * REP * (HD + 2);
+  float* wsm = &pw[0][0][0];                         // [S][REP] split weights (S * REP <= 4 * REP * 32)
+  float* hm = &mw[0][0];
+  float* hinv = &lw[0][0];
+  for (int i = threadIdx.x; i < S * REP; i += kAThreads) wsm[i] = __ldcg(&gp[(size_t)i * (HD + 2)]);
   __syncthreads();
-  for (int h = threadIdx.x; h < rep; h += blockDim.x) {
+  for (int h = threadIdx.x; h < REP; h += kAThreads) {
     float M = -INFINITY;
-    for (int s = 0; s < S; ++s) M = fmaxf(M, wsm[s * rep + h]);
+    for (int s = 0; s < S; ++s) M = fmaxf(M, wsm[s * REP + h]);
     float sink = 0.f;
-    if (a.sinks) { sink = a.sinks[kh * rep + h]; M = 0.5f * ((M + sink) + fabsf(M - sink)); }
+    if (a.sinks) { sink = a.sinks[kh * REP + h]; M = 0.5f * ((M + sink) + fabsf(M - sink)); }
     float L = 0.f;
     for (int s = 0; s < S; ++s) {
-      const float m = wsm[s * rep + h];
-      if (m != -INFINITY) L += __ldcg(&gp[((size_t)s * rep + h) * (hd + 2) + 1]) * expf(m - M);
+      const float m = wsm[s * REP + h];
+      if (m != -INFINITY) L += __ldcg(&gp[((size_t)s * REP + h) * (HD + 2) + 1]) * expf(m - M);
     }
     if (a.sinks) L += expf(sink - M);
     hm[h] = M;
     hinv[h] = 1.0f / L;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < S * rep; i += blockDim.x) {
-    const int h = i % rep;
+  for (int i = threadIdx.x; i < S * REP; i += kAThreads) {
+    const int h = i % REP;
     const float m = wsm[i];
     wsm[i] = (m == -INFINITY) ? 0.f : expf(m - hm[h]) * hinv[h];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < rep * hd; i += blockDim.x) {
-    const int h = i / hd, d = i - h * hd;
-    const float* src = gp + (size_t)h * (hd + 2) + 2 + d;
-    const size_t stride = (size_t)rep * (hd + 2);
+  for (int i = threadIdx.x; i < REP * HD; i += kAThreads) {
+    const int h = i / HD, d = i - h * HD;
+    const float* src = gp + (size_t)h * (HD + 2) + 2 + d;
+    const size_t stride = (size_t)REP * (HD + 2);
     float o = 0.f;
     int s = 0;
     for (; s + 8 <= S; s += 8) {
@@ -527,10 +553,22 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
 #pragma unroll
       for (int u = 0; u < 8; ++u) v[u] = __ldcg(src + (size_t)(s + u) * stride);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) o = fmaf(wsm[(s + u) * rep + h], v[u], o);
+      for (int u = 0; u < 8; ++u) o = fmaf(wsm[(s + u) * REP + h], v[u], o);
     }
-    for (; s < S; ++s) o = fmaf(wsm[s * rep + h], __ldcg(src + (size_t)s * stride), o);
-    a.out[(size_t)(kh * rep + h) * hd + d] = o;
+    for (; s < S; ++s) o = fmaf(wsm[s * REP + h], __ldcg(src + (size_t)s * stride), o);
+    a.out[(size_t)(kh * REP + h) * HD + d] = o;
+    if (a.oq) ow[0][h][d] = o;
+  }
+  if (a.oq) {   // Q8_0 blocks of this group's output (the O-projection's activation)
+    __syncthreads();
+    const float* og = &ow[0][0][0];
+    for (int bl = threadIdx.x; bl < REP * HD / 32; bl += kAThreads) {
+      float v[32];
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = og[32 * bl + k];
+      const int gb = kh * REP * HD / 32 + bl;
+      quantize_q8_block(v, a.oq + 32 * gb, &a.od[gb]);
+    }
   }
   if (threadIdx.x == 0) a.cnt[kh] = 0u;
 }
@@ -551,13 +589,10 @@ __global__ void __launch_bounds__(kLWarps * 32, 1) lmhead_kernel(LmHeadArgs a) {
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[kLWarps];
   __shared__ unsigned long long bestk[kLWarps];
-  __shared__ CombineOrder co;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_wait_prior();
-  if (threadIdx.x == 0) { co.n = 0; if (a.x_pend.active()) combine_order(a.x_pend, &co); }
-  __syncthreads();
   for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
-    const float v = a.x_pend.active() ? a.x[i] + combine_at(a.x_pend, co, a.H, i) : a.x[i];
+    const float v = a.x[i];
     xs[i] = v;
     if (a.x_out && blockIdx.x == 0) a.x_out[i] = v;
   }
@@ -639,9 +674,11 @@ __global__ void gemv_f32_kernel(const float* __restrict__ w, int rows, int cols,
 }
 
 // ============================ embedding / step start ============================
-__global__ void embed_kernel(StepState* st, const void* table, int q, int H, int vocab, float* h, int* log,
-                             uint32_t* err) {
+__global__ void __launch_bounds__(1024) embed_kernel(StepState* st, const void* table, int q, int H, int vocab, float* h, int* log,
+                             uint32_t* err, const float* norm_w, float eps, int8_t* xq, float* xd) {
+  extern __shared__ float es[];   // [H]
   __shared__ int tok_s;
+  __shared__ float red[32];
   pdl_wait_prior();
   if (threadIdx.x == 0) {
     int tok = st->token_in;
@@ -663,9 +700,35 @@ __global__ void embed_kernel(StepState* st, const void* table, int q, int H, int
   }
   __syncthreads();
   const int tok = tok_s;
-  for (int i = threadIdx.x; i < H; i += blockDim.x)
-    h[i] = (q == Q_F16) ? __half2float(reinterpret_cast<const __half*>(table)[(size_t)tok * H + i])
-                        : reinterpret_cast<const float*>(table)[(size_t)tok * H + i];
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float v = (q == Q_F16) ? __half2float(reinterpret_cast<const __half*>(table)[(size_t)tok * H + i])
+                                 : reinterpret_cast<const float*>(table)[(size_t)tok * H + i];
+    h[i] = v;
+    es[i] = v;
+  }
+  if (!norm_w) return;
+  __syncthreads();
+  cta_rmsnorm_q8(es, H, norm_w, eps, xq, xd, red);   // layer 0's attention input
+}
+
+// h += MoE output (slots in ascending expert order, or the expert-parallel sum), then the next
+// layer's attention input: RMSNorm + Q8_0 quantization (when norm_w is set).  One CTA.
+__global__ void __launch_bounds__(1024) resid_norm_q8_kernel(PendingCombine pc, float* h, int H, const float* norm_w,
+                                                             float eps, int8_t* xq, float* xd) {
+  extern __shared__ float hs[];   // [H]
+  __shared__ CombineOrder co;
+  __shared__ float red[32];
+  pdl_wait_prior();
+  if (threadIdx.x == 0) combine_order(pc, &co);
+  __syncthreads();
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float v = h[i] + combine_at(pc, co, H, i);
+    h[i] = v;
+    hs[i] = v;
+  }
+  if (!norm_w) return;
+  __syncthreads();
+  cta_rmsnorm_q8(hs, H, norm_w, eps, xq, xd, red);
 }
 
 template <class Kern, class... Args>
@@ -712,7 +775,7 @@ cudaError_t launch_q8_gemv(const DevCtx& c, const Q8GemvArgs& a, cudaStream_t s)
   p.ns = (int)((180 * 1024) / p.stage_bytes);
   p.ns = p.ns > 6 ? 6 : (p.ns < 2 ? 2 : p.ns);
   p.x = a.x; p.norm_w = a.norm_w; p.eps = a.eps; p.bias = a.bias; p.y = a.y; p.residual = a.residual;
-  p.x_pend = a.x_pend; p.res_pend = a.res_pend;
+  p.xq_in = a.xq_in; p.xd_in = a.xd_in;
   p.err = c.err;
   const int nbl = (a.cols / 32 + 31) / 32;
   if (p.stage_rows > kQW) return cudaErrorInvalidValue;
@@ -724,17 +787,34 @@ cudaError_t launch_q8_gemv(const DevCtx& c, const Q8GemvArgs& a, cudaStream_t s)
   return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s) {
-  if (a.nkv <= 0 || a.nh % a.nkv || a.hd % 4 || a.S <= 0 || a.rot > a.hd || a.rot % 2) return cudaErrorInvalidValue;
-  const int rep = a.nh / a.nkv, hd = a.hd;
-  size_t smem = sizeof(float) * ((size_t)rep * hd + kAT * (hd + 1) + kAT * hd + rep * kAT + rep * hd +
-                                 3 * rep + 2 * hd);
-  smem = std::max(smem, sizeof(float) * ((size_t)a.S * rep + 2 * rep));
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+template <int HD>
+cudaError_t launch_attn_hd(const AttnArgs& a, const DevCtx& c, int rep, dim3 grid, cudaStream_t s) {
+  switch (rep) {
+    case 1: return launch_pdl(attn_decode_kernel<HD, 1>, grid, dim3(kAThreads), 0, s, a, c.err);
+    case 2: return launch_pdl(attn_decode_kernel<HD, 2>, grid, dim3(kAThreads), 0, s, a, c.err);
+    case 4: return launch_pdl(attn_decode_kernel<HD, 4>, grid, dim3(kAThreads), 0, s, a, c.err);
+    case 8: return launch_pdl(attn_decode_kernel<HD, 8>, grid, dim3(kAThreads), 0, s, a, c.err);
+    case 16:
+      if constexpr (HD <= 64) return launch_pdl(attn_decode_kernel<HD, 16>, grid, dim3(kAThreads), 0, s, a, c.err);
+      break;
   }
-  return launch_pdl(attn_decode_kernel, dim3((unsigned)a.S, (unsigned)a.nkv), dim3(kAThreads), smem, s, a, c.err);
+  return cudaErrorInvalidValue;
+}
+
+int attn_splits(int range) { return (range + kASplit - 1) / kASplit; }
+
+cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s) {
+  if (a.nkv <= 0 || a.nh % a.nkv || a.S <= 0 || a.rot > a.hd || a.rot % 2) return cudaErrorInvalidValue;
+  const int rep = a.nh / a.nkv;
+  if (a.S > kAWarps * 32) return cudaErrorInvalidValue;   // merge scratch holds S * rep weights
+  const dim3 grid((unsigned)a.S, (unsigned)a.nkv);
+  switch (a.hd) {
+    case 32: return launch_attn_hd<32>(a, c, rep, grid, s);
+    case 64: return launch_attn_hd<64>(a, c, rep, grid, s);
+    case 128: return launch_attn_hd<128>(a, c, rep, grid, s);
+    case 256: return launch_attn_hd<256>(a, c, rep, grid, s);
+  }
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_lmhead(const DevCtx& c, const LmHeadArgs& a, cudaStream_t s) {
@@ -759,14 +839,34 @@ cudaError_t launch_gemv_f32(const DevCtx& c, const float* w, int rows, int cols,
 }
 
 cudaError_t launch_embed(const DevCtx& c, StepState* st, const void* table, int table_q, int H, int vocab, float* h,
-                         int* token_log, cudaStream_t s) {
-  return launch_pdl(embed_kernel, dim3(1), dim3(256), 0, s, st, table, table_q, H, vocab, h, token_log, c.err);
+                         int* token_log, cudaStream_t s, const float* norm_w, float eps, int8_t* xq, float* xd) {
+  if (H % 32) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)H * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(embed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_pdl(embed_kernel, dim3(1), dim3(1024), smem, s, st, table, table_q, H, vocab, h, token_log, c.err,
+                    norm_w, eps, xq, xd);
+}
+
+cudaError_t launch_resid_norm_q8(const DevCtx& c, const PendingCombine& pc, float* h, int H, const float* norm_w,
+                                 float eps, int8_t* xq, float* xd, cudaStream_t s) {
+  if (H % 32) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)H * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(resid_norm_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_pdl(resid_norm_q8_kernel, dim3(1), dim3(1024), smem, s, pc, h, H, norm_w, eps, xq, xd);
 }
 
 cudaError_t launch_gemv(const DevCtx& c, const GemvArgs& a, cudaStream_t s) {
   switch (a.qtype) {
     case Q_MXFP4:
-      return launch_mxfp4_gemv(c, (const uint8_t*)a.w, a.rows, a.cols, a.x, a.bias, a.y, a.accumulate, s);
+    case Q_Q4_K:
+    case Q_Q6_K:
+      return launch_block_gemv(c, a.qtype, (const uint8_t*)a.w, a.rows, a.cols, a.x, a.bias, a.y, a.accumulate, s);
     case Q_F16: {
       LmHeadArgs l;
       l.w = (const uint16_t*)a.w; l.x = a.x; l.bias = a.bias; l.logits = a.y; l.V = a.rows; l.H = a.cols;

@@ -29,9 +29,12 @@ constexpr int kMaxStages = 8;
 constexpr int kRedRows = 32;              // per-warp partial sums per item (RT=2 gate/up: 16 gate + 16 up)
 
 enum { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_PLAIN = 2 };
+// weight block formats of the streamed matrix
+enum { FMT_MXFP4 = 0, FMT_Q4K = 1, FMT_Q6K = 2 };
 
 struct PhaseParams {
   int mode;
+  int fmt;                 // FMT_*
   const uint8_t* w0;       // gate (GATEUP) or down (DOWN/PLAIN), stacked [E_local, rows, cols]
   const uint8_t* w1;       // up (GATEUP)
   int64_t expert_stride;   // bytes per expert matrix
@@ -90,18 +93,113 @@ __device__ __forceinline__ void mx_block(const uint8_t* p0, const uint8_t* p1, c
   acc1 = fmaf(s1, d[2] + d[3], acc1);
 }
 
-// B fragments of the activation vector for the K-blocks this warp owns.
-template <int NBW>
+// 4 unsigned 6-bit-or-less codes (one per byte) -> two f16x2 of (code - bias): bytes are placed
+// under the f16 exponent of 1024 (0x64XX = 1024 + XX, exact) and the bias 1024 + b is subtracted.
+__device__ __forceinline__ void codes4_to_f16x2(uint32_t q, uint32_t bias_h2, uint32_t& p0, uint32_t& p1) {
+  const uint32_t t0 = __byte_perm(q, 0x64646464u, 0x4140u);   // [q0, 0x64, q1, 0x64]
+  const uint32_t t1 = __byte_perm(q, 0x64646464u, 0x4342u);   // [q2, 0x64, q3, 0x64]
+  const __half2 b = *reinterpret_cast<const __half2*>(&bias_h2);
+  const __half2 r0 = __hsub2(*reinterpret_cast<const __half2*>(&t0), b);
+  const __half2 r1 = __hsub2(*reinterpret_cast<const __half2*>(&t1), b);
+  p0 = *reinterpret_cast<const uint32_t*>(&r0);
+  p1 = *reinterpret_cast<const uint32_t*>(&r1);
+}
+
+// Q4_K sub-block j of one superblock for the thread's two MMA rows (gguf/dequant.rs:199-262):
+// value = d*sc_j*q - dmin*m_j; the block dot is d*sc_j * sum(q x) - dmin*m_j * sum(x).
+__device__ __forceinline__ void q4k_block(const uint8_t* sb0, const uint8_t* sb1, int j, int c, const uint32_t (&bf)[4],
+                                          float xscale, float xsum, float& acc0, float& acc1) {
+  const int jj = j & 3, nsh = (j & 1) * 4, qo = 16 + (j >> 1) * 32 + 4 * c;
+  float dot[2];
+  float dsc[2], dmn[2];
+  uint32_t p[2][2][2];   // [row][word][pair]
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const uint8_t* sb = r ? sb1 : sb0;
+    const uint32_t dm = *reinterpret_cast<const uint32_t*>(sb);
+    const uint32_t s0 = *reinterpret_cast<const uint32_t*>(sb + 4), s1 = *reinterpret_cast<const uint32_t*>(sb + 8),
+                   s2 = *reinterpret_cast<const uint32_t*>(sb + 12);
+    uint32_t sc, m;
+    if (j < 4) { sc = (s0 >> (8 * jj)) & 63u; m = (s1 >> (8 * jj)) & 63u; }
+    else {
+      sc = ((s2 >> (8 * jj)) & 0xFu) | (((s0 >> (8 * jj + 6)) & 3u) << 4);
+      m = ((s2 >> (8 * jj + 4)) & 0xFu) | (((s1 >> (8 * jj + 6)) & 3u) << 4);
+    }
+    const float d = h2f_bits((uint16_t)(dm & 0xffffu)), dmin = h2f_bits((uint16_t)(dm >> 16));
+    dsc[r] = (d * (float)sc) * xscale;
+    dmn[r] = dmin * (float)m;
+#pragma unroll
+    for (int w = 0; w < 2; ++w) {
+      const uint32_t q = (*reinterpret_cast<const uint32_t*>(sb + qo + 16 * w) >> nsh) & 0x0F0F0F0Fu;
+      codes4_to_f16x2(q, 0x64006400u, p[r][w][0], p[r][w][1]);
+    }
+  }
+  float dd[4] = {0.f, 0.f, 0.f, 0.f};
+  uint32_t a[4];
+  a[0] = p[0][0][0]; a[1] = p[1][0][0]; a[2] = p[0][0][1]; a[3] = p[1][0][1];
+  mma_f16_16816(dd, a, bf[0], bf[1]);
+  a[0] = p[0][1][0]; a[1] = p[1][1][0]; a[2] = p[0][1][1]; a[3] = p[1][1][1];
+  mma_f16_16816(dd, a, bf[2], bf[3]);
+  dot[0] = dd[0] + dd[1];
+  dot[1] = dd[2] + dd[3];
+  acc0 = fmaf(dsc[0], dot[0], fmaf(-dmn[0], xsum, acc0));
+  acc1 = fmaf(dsc[1], dot[1], fmaf(-dmn[1], xsum, acc1));
+}
+
+// Q6_K elements (n, quad, l = 0..31) of one superblock for the thread's two rows
+// (gguf/dequant.rs:335-378): q = (ql nibble | qh 2 bits << 4) - 32, scale d*sc[n*8 + l/16 + 2*quad].
+// The two 16-element scale groups use separate MMAs.  ql/qh words are read at 2-byte alignment
+// (rows of 210-byte blocks) through aligned loads and a funnel shift.
+__device__ __forceinline__ uint32_t ld_u32_a2(const uint8_t* p) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~(uintptr_t)3);
+  return __funnelshift_r(w[0], w[1], (uint32_t)(a & 3) * 8u);
+}
+__device__ __forceinline__ void q6k_block(const uint8_t* sb0, const uint8_t* sb1, int n, int quad, int c,
+                                          const uint32_t (&bf)[4], float xscale, float& acc0, float& acc1) {
+  const int qlo = n * 64 + (quad & 1) * 32 + 4 * c, qho = 128 + n * 32 + 4 * c;
+  const int nsh = (quad >> 1) * 4, hsh = 2 * quad;
+  uint32_t p[2][2][2];
+  float s0[2], s1[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const uint8_t* sb = r ? sb1 : sb0;
+    const uint16_t scw = *reinterpret_cast<const uint16_t*>(sb + 192 + n * 8 + 2 * quad);
+    const float d = h2f_bits(*reinterpret_cast<const uint16_t*>(sb + 208)) * xscale;
+    s0[r] = d * (float)(int8_t)(scw & 0xff);
+    s1[r] = d * (float)(int8_t)(scw >> 8);
+#pragma unroll
+    for (int w = 0; w < 2; ++w) {
+      const uint32_t ql = ld_u32_a2(sb + qlo + 16 * w), qh = ld_u32_a2(sb + qho + 16 * w);
+      const uint32_t q = ((ql >> nsh) & 0x0F0F0F0Fu) | (((qh >> hsh) & 0x03030303u) << 4);
+      codes4_to_f16x2(q, 0x64206420u, p[r][w][0], p[r][w][1]);   // 1024 + 32
+    }
+  }
+  float da[4] = {0.f, 0.f, 0.f, 0.f}, db[4] = {0.f, 0.f, 0.f, 0.f};
+  uint32_t a[4];
+  a[0] = p[0][0][0]; a[1] = p[1][0][0]; a[2] = p[0][0][1]; a[3] = p[1][0][1];
+  mma_f16_16816(da, a, bf[0], bf[1]);
+  a[0] = p[0][1][0]; a[1] = p[1][1][0]; a[2] = p[0][1][1]; a[3] = p[1][1][1];
+  mma_f16_16816(db, a, bf[2], bf[3]);
+  acc0 = fmaf(s0[0], da[0] + da[1], fmaf(s1[0], db[0] + db[1], acc0));
+  acc1 = fmaf(s0[1], da[2] + da[3], fmaf(s1[1], db[2] + db[3], acc1));
+}
+
+// B fragments of the activation vector for the K-blocks this warp owns.  MXFP4 pairs element
+// 4c+q with 4c+16+q (the two nibbles of one code byte); the K-quants pair consecutive elements.
+template <int FMT, int NBW>
 __device__ __forceinline__ void build_bfrag(const float* __restrict__ x, int nb, int warp, int lane,
-                                            uint32_t (&bf)[NBW][4], int (&kbs)[NBW]) {
+                                            uint32_t (&bf)[NBW][4], int (&kbs)[NBW], float (&xsum)[NBW]) {
   const int c = lane & 3, n = lane >> 2;
 #pragma unroll
   for (int i = 0; i < NBW; ++i) {
     const int b = warp + kCW * i;
     bf[i][0] = bf[i][1] = bf[i][2] = bf[i][3] = 0u;
     kbs[i] = 0;
+    xsum[i] = 0.f;
     if (b < nb) {
       const float v = x[32 * b + lane];
+      if (FMT == FMT_Q4K) xsum[i] = warp_sum(v);
       const float m = warp_max(fabsf(v));
       const int ef = (int)((__float_as_uint(m) >> 23) & 0xffu);
       const int k = (m > 0.f) ? (ef - 126) : 0;              // m * 2^-k in [0.5, 1)
@@ -112,15 +210,18 @@ __device__ __forceinline__ void build_bfrag(const float* __restrict__ x, int nb,
         const float4 hi4 = *reinterpret_cast<const float4*>(x + 32 * b + 16 + 4 * c);
         const float va[4] = {lo4.x, lo4.y, lo4.z, lo4.w};
         const float vb[4] = {hi4.x, hi4.y, hi4.z, hi4.w};
+        __half hv[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float a = (q < 4 ? va[q] : vb[q - 4]) * sc;
+          __half ah = __float2half_rn(a);
+          if (n == 1) ah = __float2half_rn(a - __half2float(ah));
+          hv[q] = ah;
+        }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const float a = va[q] * sc, bb = vb[q] * sc;
-          __half ah = __float2half_rn(a), bh = __float2half_rn(bb);
-          if (n == 1) {
-            ah = __float2half_rn(a - __half2float(ah));
-            bh = __float2half_rn(bb - __half2float(bh));
-          }
-          bf[i][q] = pack_half2(ah, bh);
+          if (FMT == FMT_MXFP4) bf[i][q] = pack_half2(hv[q], hv[4 + q]);     // (4c+q, 4c+16+q)
+          else bf[i][q] = pack_half2(hv[(q >> 1) * 4 + (q & 1) * 2], hv[(q >> 1) * 4 + (q & 1) * 2 + 1]);
         }
       }
     }
@@ -173,7 +274,7 @@ __device__ __forceinline__ void item_epilogue(const PhaseParams& p, const SlotIn
 }
 
 // RT = MMA row tiles per item: 2 for GATEUP (16 gate + 16 up rows), 1 for DOWN / PLAIN (16 rows).
-template <int NBW, int RT>
+template <int FMT, int NBW, int RT>
 __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
@@ -254,6 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
   const int c = lane & 3, g = lane >> 2;
   uint32_t bf[NBW][4];
   int kbs[NBW];
+  float xsum[NBW];
   // this thread's two MMA rows per row tile (byte offsets of row starts in the stage)
   uint32_t off0[RT], off1[RT];
 #pragma unroll
@@ -285,7 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
     const int ls = item / p.n_tiles, t = item % p.n_tiles;
     const int x_slot = (p.mode == MODE_GATEUP) ? 0 : si->slot[ls];
     if (x_slot != cur_slot) {
-      build_bfrag<NBW>(p.x + (size_t)x_slot * (p.mode == MODE_GATEUP ? 0 : p.cols), nb, warp, lane, bf, kbs);
+      build_bfrag<FMT, NBW>(p.x + (size_t)x_slot * (p.mode == MODE_GATEUP ? 0 : p.cols), nb, warp, lane, bf, kbs,
+                            xsum);
       cur_slot = x_slot;
     }
     float acc0[RT], acc1[RT];
@@ -300,12 +403,27 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
     for (int i = 0; i < NBW; ++i) {
       const int b = warp + kCW * i;
       if (b < nb) {
+        if constexpr (FMT == FMT_MXFP4) {
 #pragma unroll
-        for (int q = 0; q < RT; ++q)
-          mx_block(st + bs0[q] + kCW * 17 * i, st + bs1[q] + kCW * 17 * i,
-                   reinterpret_cast<const uint32_t*>(st + wa0[q] + kCW * 17 * i),
-                   reinterpret_cast<const uint32_t*>(st + wa1[q] + kCW * 17 * i), sh0[q], sh1[q], bf[i], kbs[i],
-                   acc0[q], acc1[q]);
+          for (int q = 0; q < RT; ++q)
+            mx_block(st + bs0[q] + kCW * 17 * i, st + bs1[q] + kCW * 17 * i,
+                     reinterpret_cast<const uint32_t*>(st + wa0[q] + kCW * 17 * i),
+                     reinterpret_cast<const uint32_t*>(st + wa1[q] + kCW * 17 * i), sh0[q], sh1[q], bf[i], kbs[i],
+                     acc0[q], acc1[q]);
+        } else {
+          // 32-column block b = warp + 16 i lies in superblock b / 8 at sub-block warp % 8
+          const float xscale = __int_as_float(max(127 * 8388608 + kbs[i], 0));   // 2^kb
+          const int sbk = b >> 3;
+#pragma unroll
+          for (int q = 0; q < RT; ++q) {
+            if constexpr (FMT == FMT_Q4K)
+              q4k_block(st + off0[q] + 144 * sbk, st + off1[q] + 144 * sbk, warp & 7, c, bf[i], xscale, xsum[i],
+                        acc0[q], acc1[q]);
+            else
+              q6k_block(st + off0[q] + 210 * sbk, st + off1[q] + 210 * sbk, (warp & 7) >> 2, warp & 3, c, bf[i],
+                        xscale, acc0[q], acc1[q]);
+          }
+        }
       }
     }
     __syncwarp();
@@ -336,11 +454,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
   }
 }
 
-template <int NBW, int RT>
+template <int FMT, int NBW, int RT>
 cudaError_t launch_phase(const DevCtx& c, const PhaseParams& p, cudaStream_t s) {
   const size_t smem = (size_t)p.ns * p.stage_bytes + (size_t)(p.ns + 1) * kCW * kRedRows * sizeof(float) +
                       2 * kMaxStages * 8 + (kMaxStages + 1) * 4 + sizeof(SlotInfo) + 16;
-  cudaError_t e = cudaFuncSetAttribute(moe_mxfp4_phase_kernel<NBW, RT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(moe_mxfp4_phase_kernel<FMT, NBW, RT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -353,22 +471,29 @@ cudaError_t launch_phase(const DevCtx& c, const PhaseParams& p, cudaStream_t s) 
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, moe_mxfp4_phase_kernel<NBW, RT>, p);
+  return cudaLaunchKernelEx(&cfg, moe_mxfp4_phase_kernel<FMT, NBW, RT>, p);
 }
 
-template <int RT>
+template <int FMT, int RT>
 cudaError_t dispatch_nbw(const DevCtx& c, const PhaseParams& p, cudaStream_t s) {
   const int nbw = (p.cols / 32 + kCW - 1) / kCW;
-  if (nbw <= 1) return launch_phase<1, RT>(c, p, s);
-  if (nbw <= 2) return launch_phase<2, RT>(c, p, s);
-  if (nbw <= 4) return launch_phase<4, RT>(c, p, s);
-  if (nbw <= 6) return launch_phase<6, RT>(c, p, s);
-  if (nbw <= 8) return launch_phase<8, RT>(c, p, s);
+  if (nbw <= 1) return launch_phase<FMT, 1, RT>(c, p, s);
+  if (nbw <= 2) return launch_phase<FMT, 2, RT>(c, p, s);
+  if (nbw <= 4) return launch_phase<FMT, 4, RT>(c, p, s);
+  if (nbw <= 6) return launch_phase<FMT, 6, RT>(c, p, s);
+  if (nbw <= 8) return launch_phase<FMT, 8, RT>(c, p, s);
   return cudaErrorInvalidValue;
 }
 
 cudaError_t dispatch_phase(const DevCtx& c, const PhaseParams& p, cudaStream_t s) {
-  return p.mode == MODE_GATEUP ? dispatch_nbw<2>(c, p, s) : dispatch_nbw<1>(c, p, s);
+  if (p.fmt == FMT_MXFP4) return p.mode == MODE_GATEUP ? dispatch_nbw<FMT_MXFP4, 2>(c, p, s) : dispatch_nbw<FMT_MXFP4, 1>(c, p, s);
+  if (p.fmt == FMT_Q4K) return p.mode == MODE_GATEUP ? dispatch_nbw<FMT_Q4K, 2>(c, p, s) : dispatch_nbw<FMT_Q4K, 1>(c, p, s);
+  if (p.fmt == FMT_Q6K) return p.mode == MODE_GATEUP ? dispatch_nbw<FMT_Q6K, 2>(c, p, s) : dispatch_nbw<FMT_Q6K, 1>(c, p, s);
+  return cudaErrorInvalidValue;
+}
+
+int fmt_of(int qtype) {
+  return qtype == Q_MXFP4 ? FMT_MXFP4 : qtype == Q_Q4_K ? FMT_Q4K : qtype == Q_Q6_K ? FMT_Q6K : -1;
 }
 
 int pick_stages(int stage_bytes) {
@@ -487,14 +612,15 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, ui
 
 }  // namespace
 
-cudaError_t launch_mxfp4_gemv(const DevCtx& c, const uint8_t* w, int rows, int cols, const float* x,
+cudaError_t launch_block_gemv(const DevCtx& c, int qtype, const uint8_t* w, int rows, int cols, const float* x,
                               const float* bias, float* y, int accumulate, cudaStream_t s) {
   // rows are streamed in 16-row tiles; the weight allocation must be padded to a whole tile
-  if (cols % 32 || rows <= 0) return cudaErrorInvalidValue;
-  const int rb = cols / 32 * 17;
+  const int fmt = fmt_of(qtype);
+  const int rb = (int)row_bytes(qtype, cols);
+  if (fmt < 0 || rb <= 0 || rows <= 0) return cudaErrorInvalidValue;
   if ((16 * rb) % 16) return cudaErrorInvalidValue;
   PhaseParams p = {};
-  p.mode = MODE_PLAIN; p.w0 = w; p.expert_stride = 0; p.rb = rb; p.cols = cols; p.rows = rows;
+  p.mode = MODE_PLAIN; p.fmt = fmt; p.w0 = w; p.expert_stride = 0; p.rb = rb; p.cols = cols; p.rows = rows;
   p.tile_rows = 16; p.n_tiles = (rows + 15) / 16; p.stage_bytes = 16 * rb; p.ns = pick_stages(p.stage_bytes);
   p.x = x; p.bias0 = bias; p.out = y; p.accumulate = accumulate; p.K = 1; p.err = c.err;
   return dispatch_phase(c, p, s);
@@ -548,20 +674,23 @@ cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s) 
 
 cudaError_t launch_moe_mxfp4(const DevCtx& c, const MoeArgs& a, cudaStream_t s) {
   if (a.K < 1 || a.K > kMaxK || a.H % 64 || a.I % 32 || a.n_local < 0) return cudaErrorInvalidValue;
-  const int rbg = a.H / 32 * 17;   // gate/up row bytes
-  const int rbd = a.I / 32 * 17;   // down row bytes
+  const int fg = fmt_of(a.gate_q), fd = fmt_of(a.down_q);
+  if (fg < 0 || fd < 0) return cudaErrorInvalidValue;
+  const int rbg = (int)row_bytes(a.gate_q, a.H);   // gate/up row bytes
+  const int rbd = (int)row_bytes(a.down_q, a.I);   // down row bytes
+  if (rbg <= 0 || rbd <= 0) return cudaErrorInvalidValue;
   PhaseParams p = {};
   p.K = a.K; p.idx = a.idx; p.wts = a.wts; p.expert_base = a.expert_base; p.n_local = a.n_local;
   p.oai = a.oai_swiglu; p.err = c.err;
   // phase 1: gate + up + activation
-  p.mode = MODE_GATEUP; p.w0 = a.gate; p.w1 = a.up; p.expert_stride = (int64_t)a.I * rbg; p.rb = rbg;
+  p.mode = MODE_GATEUP; p.fmt = fg; p.w0 = a.gate; p.w1 = a.up; p.expert_stride = (int64_t)a.I * rbg; p.rb = rbg;
   p.cols = a.H; p.rows = a.I; p.tile_rows = 16; p.n_tiles = a.I / 16; p.stage_bytes = 32 * rbg;
   p.ns = pick_stages(p.stage_bytes); p.x = a.x; p.bias0 = a.gate_b; p.bias1 = a.up_b; p.act = a.act;
   if ((16 * rbg) % 16 || p.expert_stride % 16 || a.I % 16 || a.H % 16) return cudaErrorInvalidValue;
   cudaError_t e = dispatch_phase(c, p, s);
   if (e != cudaSuccess) return e;
-  // phase 2: down + weighted combine (+ residual)
-  p.mode = MODE_DOWN; p.w0 = a.down; p.w1 = nullptr; p.expert_stride = (int64_t)a.H * rbd; p.rb = rbd;
+  // phase 2: down -> per-slot partial rows
+  p.mode = MODE_DOWN; p.fmt = fd; p.w0 = a.down; p.w1 = nullptr; p.expert_stride = (int64_t)a.H * rbd; p.rb = rbd;
   p.cols = a.I; p.rows = a.H; p.tile_rows = 16; p.n_tiles = a.H / 16; p.stage_bytes = 16 * rbd;
   p.ns = pick_stages(p.stage_bytes); p.x = a.act; p.bias0 = a.down_b; p.bias1 = nullptr;
   p.partial = a.partial; p.tile_cnt = a.tile_cnt; p.h = a.h; p.out = a.out;

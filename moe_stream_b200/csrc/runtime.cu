@@ -1,3 +1,4 @@
+#include <algorithm>
 // runtime.cu — host runtime and C ABI of the moe-stream B200 backend.
 //
 // Holds the context (device, stream, device error word, scratch), the model (weights
@@ -37,6 +38,7 @@ struct ms_ctx {
   size_t scratch_bytes = 0;
   uint32_t* counters = nullptr;   // zero-initialised, self-resetting
   size_t n_counters = 0;
+  std::vector<ms_model*> models;  // live models; ms_ctx_destroy frees any still open
 };
 
 namespace {
@@ -167,6 +169,10 @@ struct ms_model {
   ms_ctx* ctx = nullptr;
   ncclComm_t comm = nullptr;        // expert-parallel communicator (ep_size > 1)
   float* moe_out = nullptr;         // [H] local MoE output, all-reduced across the EP group
+  int8_t* xq_h = nullptr;           // Q8_0 codes of the next attention input [H]
+  float* xd_h = nullptr;            // and block scales [H / 32]
+  int8_t* xq_a = nullptr;           // Q8_0 codes of the attention output [Dq]
+  float* xd_a = nullptr;
   ms_model_config cfg{};
   std::vector<LayerW> L;
   void* embd = nullptr;
@@ -193,6 +199,7 @@ struct ms_model {
   int* h_tok = nullptr;             // pinned token staging [max_seq + 1]
   StepState* h_st = nullptr;        // pinned
   int kernels_per_step = 0;
+  int prof_class = -1;   // >= 0: enqueue only the launches of this class (ms_model_profile_step)
 
   template <class T>
   ms_status alloc(T** p, size_t bytes, bool zero = true) {
@@ -308,7 +315,8 @@ ms_status set_layer_tensor(ms_model* m, int li, const std::string& t, int q, con
     if (t == wn) {
       if (dims.size() != 3 || dims[0] != c.experts || dims[1] != x.rows || dims[2] != x.cols)
         return fail(m->ctx, MS_ERR_SHAPE, "%s: expected [%d, %d, %d]", nm, c.experts, x.rows, x.cols);
-      if (q != Q_MXFP4) return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: expert qtype %d not supported yet", nm, q);
+      if (q != Q_MXFP4 && q != Q_Q4_K && q != Q_Q6_K)
+        return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: expert qtype %d not supported", nm, q);
       const int64_t per = raw_bytes(q, (int64_t)x.rows * x.cols);
       ms_status s = m->alloc(x.w, padded((size_t)per * m->n_local));
       if (s != MS_OK) return s;
@@ -340,6 +348,15 @@ void rope_tables(int rot, int max_seq, double theta, std::vector<float>& cs, std
     }
 }
 
+// launch i of a step: 0 = embed, the last = LM head, else 1 + its position within the layer
+int launch_class(const ms_model* m, int i) {
+  const int kps = m->kernels_per_step;
+  const int per_layer = (kps - 2) / m->cfg.layers;
+  if (i == 0) return 0;
+  if (i >= kps - 1) return 1 + per_layer;
+  return 1 + (i - 1) % per_layer;
+}
+
 ms_status enqueue_step(ms_model* m, cudaStream_t s) {
   const ms_model_config& c = m->cfg;
   const DevCtx& dc = m->ctx->dc;
@@ -347,30 +364,33 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
   int nk = 0;
 #define LAUNCH(call)                                                       \
   do {                                                                     \
-    cudaError_t e_ = (call);                                               \
-    if (e_ != cudaSuccess) return cuda_fail(m->ctx, e_, #call);           \
+    if (m->prof_class < 0 || launch_class(m, nk) == m->prof_class) {       \
+      cudaError_t e_ = (call);                                             \
+      if (e_ != cudaSuccess) return cuda_fail(m->ctx, e_, #call);         \
+    }                                                                      \
     ++nk;                                                                  \
   } while (0)
-  LAUNCH(launch_embed(dc, m->st, m->embd, m->embd_q, H, c.vocab, m->h, m->token_log, s));
-  // the previous layer's MoE output stays pending: its consumers (this layer's QKV prologue and
-  // O-projection epilogue, or the LM head) add it to the residual stream
-  PendingCombine pend;
+  // Every Q8_0 projection gets its activation already quantized by the kernel that produced it:
+  // the embedding (layer 0), the residual-update kernel after each MoE (next layer's attention
+  // input), and the attention merge (O-projection input).
+  LAUNCH(launch_embed(dc, m->st, m->embd, m->embd_q, H, c.vocab, m->h, m->token_log, s, m->L[0].attn_norm, c.eps,
+                      m->xq_h, m->xd_h));
   for (int li = 0; li < c.layers; ++li) {
     LayerW& Lw = m->L[li];
     Q8GemvArgs qa;
-    qa.w = Lw.wqkv; qa.rows = Dq + 2 * Dkv; qa.cols = H; qa.x = m->h; qa.norm_w = Lw.attn_norm; qa.eps = c.eps;
-    qa.bias = Lw.bqkv; qa.y = m->qkv; qa.x_pend = pend;
+    qa.w = Lw.wqkv; qa.rows = Dq + 2 * Dkv; qa.cols = H; qa.xq_in = m->xq_h; qa.xd_in = m->xd_h;
+    qa.bias = Lw.bqkv; qa.y = m->qkv;
     LAUNCH(launch_q8_gemv(dc, qa, s));
     AttnArgs aa;
     aa.qkv = m->qkv; aa.q_norm = Lw.qn; aa.k_norm = Lw.kn; aa.eps = c.eps; aa.cos_t = m->cos_t; aa.sin_t = m->sin_t;
     aa.rot = c.rot_dim; aa.pos = &m->st->pos; aa.kc = Lw.kc; aa.vc = Lw.vc; aa.cap = Lw.cap; aa.window = Lw.window;
     aa.sinks = Lw.sinks; aa.part = m->attn_part; aa.cnt = m->attn_cnt; aa.out = m->attn_out; aa.nh = c.heads;
     aa.nkv = c.kv_heads; aa.hd = c.head_dim; aa.S = Lw.window ? m->splits_swa : m->splits_full;
-    aa.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
+    aa.scale = (float)(1.0 / std::sqrt((double)c.head_dim)); aa.oq = m->xq_a; aa.od = m->xd_a;
     LAUNCH(launch_attention(dc, aa, s));
     Q8GemvArgs oa;
-    oa.w = Lw.wo; oa.rows = H; oa.cols = Dq; oa.x = m->attn_out; oa.bias = Lw.bo; oa.residual = m->h;
-    oa.res_pend = pend;
+    oa.w = Lw.wo; oa.rows = H; oa.cols = Dq; oa.xq_in = m->xq_a; oa.xd_in = m->xd_a; oa.bias = Lw.bo;
+    oa.residual = m->h;
     LAUNCH(launch_q8_gemv(dc, oa, s));
     RouterArgs ra;
     ra.h = m->h; ra.norm_w = Lw.post_norm; ra.eps = c.eps; ra.xn = m->xn; ra.w = Lw.router_w; ra.b = Lw.router_b;
@@ -379,31 +399,35 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     ra.normalize = c.norm_topk_prob;
     LAUNCH(launch_router(dc, ra, s));
     MoeArgs ma;
+    ma.gate_q = Lw.gate_q; ma.down_q = Lw.down_q;
     ma.x = m->xn; ma.idx = Lw.idx; ma.wts = Lw.wts; ma.gate = Lw.gate; ma.up = Lw.up; ma.down = Lw.down;
     ma.gate_b = Lw.gate_b; ma.up_b = Lw.up_b; ma.down_b = Lw.down_b; ma.act = m->act; ma.partial = m->partial;
     ma.tile_cnt = m->tile_cnt; ma.h = m->h; ma.H = H; ma.I = c.inter; ma.K = c.top_k;
     ma.expert_base = m->expert_base; ma.n_local = m->n_local; ma.oai_swiglu = c.arch == MS_ARCH_GPT_OSS;
-    pend = PendingCombine();
+    PendingCombine pc;
     if (c.ep_size > 1) {
-      // expert parallel: combine the local experts into moe_out, sum it over the EP group,
-      // and let the consumers add the summed vector to the residual stream
+      // expert parallel: combine the local experts into moe_out, sum it over the EP group
       ma.defer_combine = 0; ma.out = m->moe_out;
       LAUNCH(launch_moe_mxfp4(dc, ma, s));
       nk += 2;   // gate/up, down, combine
       NcclApi* api = nccl_api();
       ncclResult_t r = api->all_reduce(m->moe_out, m->moe_out, (size_t)H, ncclFloat32, ncclSum, m->comm, s);
       if (r != ncclSuccess) return fail(m->ctx, MS_ERR_NCCL, "ncclAllReduce: %s", api->error_string(r));
-      pend.dense = m->moe_out;
+      pc.dense = m->moe_out;
     } else {
-      // single device: a small combine kernel adds the experts (ascending id) into h
-      ma.defer_combine = 0;
+      ma.defer_combine = 1;   // per-slot outputs stay in `partial`; the next kernel combines them
       LAUNCH(launch_moe_mxfp4(dc, ma, s));
-      nk += 2;   // gate/up, down, combine
+      ++nk;   // gate/up, down
+      pc.partial = m->partial; pc.idx = Lw.idx; pc.wts = Lw.wts; pc.K = c.top_k;
+      pc.expert_base = m->expert_base; pc.n_local = m->n_local;
     }
+    // h += MoE (ascending expert order); quantize the next layer's attention input
+    const float* next_norm = li + 1 < c.layers ? m->L[li + 1].attn_norm : nullptr;
+    LAUNCH(launch_resid_norm_q8(dc, pc, m->h, H, next_norm, c.eps, m->xq_h, m->xd_h, s));
   }
   LmHeadArgs la;
   la.w = m->out_w; la.x = m->h; la.norm_w = m->out_norm; la.eps = c.eps; la.bias = m->out_b; la.logits = m->logits;
-  la.key = &m->st->key; la.V = c.vocab; la.H = H; la.x_pend = pend; la.x_out = m->h_last;
+  la.key = &m->st->key; la.V = c.vocab; la.H = H; la.x_out = m->h_last;
   LAUNCH(launch_lmhead(dc, la, s));
 #undef LAUNCH
   m->kernels_per_step = nk;
@@ -523,6 +547,7 @@ ms_status ms_ctx_destroy(ms_ctx* c) {
   if (!c) return MS_ERR_INVALID_ARG;
   cudaSetDevice(c->device);
   cudaStreamSynchronize(c->stream);
+  while (!c->models.empty()) ms_model_destroy(c->models.back());
   if (c->scratch) cudaFree(c->scratch);
   if (c->counters) cudaFree(c->counters);
   if (c->dc.err) cudaFree(c->dc.err);
@@ -598,7 +623,8 @@ ms_status ms_rms_norm(ms_ctx* c, const float* x, const float* w, float* y, int r
 
 ms_status ms_gemv(ms_ctx* c, int q, const void* w, int rows, int cols, const float* x, const float* bias, float* y) {
   if (!c || !w || !x || !y || rows <= 0 || cols <= 0) return MS_ERR_INVALID_ARG;
-  if (q != Q_MXFP4 && q != Q_Q8_0 && q != Q_F16 && q != Q_F32) return fail(c, MS_ERR_UNSUPPORTED_QTYPE, "gemv qtype %d", q);
+  if (q != Q_MXFP4 && q != Q_Q8_0 && q != Q_F16 && q != Q_F32 && q != Q_Q4_K && q != Q_Q6_K)
+    return fail(c, MS_ERR_UNSUPPORTED_QTYPE, "gemv qtype %d", q);
   if (row_bytes(q, cols) < 0) return fail(c, MS_ERR_SHAPE, "cols %d not a whole number of blocks", cols);
   GemvArgs a;
   a.qtype = q; a.w = w; a.rows = rows; a.cols = cols; a.x = x; a.bias = bias; a.y = y;
@@ -655,6 +681,7 @@ ms_status ms_model_create(ms_ctx* c, const ms_model_config* cfg, ms_model** out)
   if (k.hidden % 64 || k.inter % 32) return fail(c, MS_ERR_SHAPE, "hidden %% 64 and inter %% 32 required");
   auto* m = new ms_model();
   m->ctx = c;
+  c->models.push_back(m);
   m->cfg = k;
   m->L.resize(k.layers);
   m->n_local = k.experts / k.ep_size;
@@ -724,14 +751,18 @@ ms_status ms_model_finalize(ms_model* m) {
     if (s != MS_OK) return s;
   }
   const int H = c.hidden, Dq = q_dim(c), Dkv = kv_dim(c), rep = c.heads / c.kv_heads;
-  int S = c.attn_splits;
-  if (S <= 0) { S = (2 * m->ctx->dc.sm_count + c.kv_heads - 1) / c.kv_heads; if (S > 64) S = 64; }
+  // decode attention splits: 128 positions each, sized for the longest attended range
+  const int S = attn_splits(c.max_seq_len);
   m->splits_full = S;
-  m->splits_swa = c.sliding_window > 0 ? std::max(1, std::min(S, (c.sliding_window + 31) / 32)) : S;
+  m->splits_swa = c.sliding_window > 0 ? attn_splits(std::min(c.sliding_window, c.max_seq_len)) : S;
   ms_status s = MS_OK;
   s = s ? s : m->alloc(&m->h, (size_t)H * 4);
   s = s ? s : m->alloc(&m->h_last, (size_t)H * 4);
   s = s ? s : m->alloc(&m->moe_out, (size_t)H * 4);
+  s = s ? s : m->alloc(&m->xq_h, (size_t)H + 64);
+  s = s ? s : m->alloc(&m->xd_h, (size_t)H / 32 * 4 + 64);
+  s = s ? s : m->alloc(&m->xq_a, (size_t)Dq + 64);
+  s = s ? s : m->alloc(&m->xd_a, (size_t)Dq / 32 * 4 + 64);
   s = s ? s : m->alloc(&m->qkv, (size_t)(Dq + 2 * Dkv) * 4);
   s = s ? s : m->alloc(&m->attn_out, (size_t)Dq * 4);
   s = s ? s : m->alloc(&m->xn, (size_t)H * 4);
@@ -774,6 +805,8 @@ ms_status ms_model_destroy(ms_model* m) {
   for (void* p : m->allocs) cudaFree(p);
   if (m->h_tok) cudaFreeHost(m->h_tok);
   if (m->h_st) cudaFreeHost(m->h_st);
+  auto& v = m->ctx->models;
+  v.erase(std::remove(v.begin(), v.end(), m), v.end());
   delete m;
   return MS_OK;
 }
@@ -948,6 +981,56 @@ ms_status ms_model_init_ep(ms_model* m, const void* unique_id, size_t bytes) {
   if (r != ncclSuccess) { m->comm = nullptr; return fail(m->ctx, MS_ERR_NCCL, "ncclCommInitRank: %s", api->error_string(r)); }
   if (m->graph) { cudaGraphExecDestroy(m->graph); m->graph = nullptr; }
   return MS_OK;
+}
+
+ms_status ms_model_profile_step(ms_model* m, float* us, int max, int* n) {
+  if (!m || !us || !n || max <= 0) return MS_ERR_INVALID_ARG;
+  if (!m->finalized || m->kernels_per_step <= 0)
+    return fail(m->ctx, MS_ERR_STATE, "profile after finalize and at least one decode step");
+  if (m->cfg.ep_size > 1) return fail(m->ctx, MS_ERR_STATE, "profiling is single-device only");
+  cudaSetDevice(m->ctx->device);
+  cudaStream_t s = m->ctx->stream, cs = m->ctx->own;
+  const int n_class = 2 + (m->kernels_per_step - 2) / m->cfg.layers;
+  constexpr int kWarm = 3, kRuns = 10;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  MS_CUDA(m->ctx, cudaEventCreate(&e0));
+  MS_CUDA(m->ctx, cudaEventCreate(&e1));
+  ms_status st = MS_OK;
+  int k = 0;
+  for (int c = 0; c < n_class && k < max && st == MS_OK; ++c) {
+    // a graph holding only this class's launches of one step, chained with PDL like the real step
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    st = ms_sync(m->ctx);
+    if (st != MS_OK) break;
+    MS_CUDA(m->ctx, cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    m->prof_class = c;
+    st = enqueue_step(m, cs);
+    m->prof_class = -1;
+    cudaError_t e = cudaStreamEndCapture(cs, &g);
+    if (st == MS_OK && e != cudaSuccess) st = cuda_fail(m->ctx, e, "cudaStreamEndCapture (profile)");
+    if (st == MS_OK && (e = cudaGraphInstantiate(&ge, g, 0)) != cudaSuccess)
+      st = cuda_fail(m->ctx, e, "cudaGraphInstantiate (profile)");
+    for (int r = 0; r < kWarm + kRuns && st == MS_OK; ++r) {
+      if (r == kWarm) cudaEventRecord(e0, s);
+      if ((e = cudaGraphLaunch(ge, s)) != cudaSuccess) st = cuda_fail(m->ctx, e, "cudaGraphLaunch (profile)");
+    }
+    if (st == MS_OK) {
+      cudaEventRecord(e1, s);
+      st = ms_sync(m->ctx);
+    }
+    if (st == MS_OK) {
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, e0, e1);
+      us[k++] = ms * 1000.f / kRuns;
+    }
+    if (ge) cudaGraphExecDestroy(ge);
+    if (g) cudaGraphDestroy(g);
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  *n = k;
+  return st;
 }
 
 ms_status ms_model_open_gguf(ms_ctx* c, const char* path, int max_seq_len, int ep_rank, int ep_size, ms_model** out) {

@@ -10,6 +10,7 @@ the CUDA library; nothing here computes on the CPU.
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 from typing import Optional, Sequence
 
 import numpy as np
@@ -35,6 +36,7 @@ class Context:
         check(lib().ms_ctx_create(device, C.byref(h)))
         self.h = h
         self.device = device
+        self._engines = weakref.WeakSet()   # closed before the context (their handles die with it)
         if stream is not None:
             self.set_stream(stream)
 
@@ -86,6 +88,8 @@ class Context:
 
     def close(self) -> None:
         if getattr(self, "h", None):
+            for e in list(getattr(self, "_engines", ())):
+                e.close()
             lib().ms_ctx_destroy(self.h)
             self.h = None
 
@@ -131,6 +135,7 @@ class Engine:
     def __init__(self, handle: C.c_void_p, ctx: Context):
         self.h = handle
         self.ctx = ctx
+        ctx._engines.add(self)
         cfg = ModelConfig()
         check(lib().ms_model_get_config(self.h, C.byref(cfg)), ctx.h)
         self.config = cfg
@@ -275,13 +280,22 @@ class Engine:
     def set_graph(self, enable: bool) -> None:
         check(lib().ms_model_set_graph(self.h, int(enable)), self.ctx.h)
 
+    def profile_step(self) -> list:
+        """Device microseconds of each kernel of one greedy decode step, in launch order."""
+        buf = np.empty(4096, dtype=np.float32)
+        n = C.c_int()
+        check(lib().ms_model_profile_step(self.h, buf.ctypes.data_as(C.POINTER(C.c_float)), buf.size, C.byref(n)),
+              self.ctx.h)
+        return buf[:n.value].tolist()
+
     @property
     def kernels_per_step(self) -> int:
         return lib().ms_model_kernels_per_step(self.h)
 
     def close(self) -> None:
         if getattr(self, "h", None):
-            lib().ms_model_destroy(self.h)
+            if getattr(self.ctx, "h", None):   # a closed context already freed its models
+                lib().ms_model_destroy(self.h)
             self.h = None
 
     def __del__(self):

@@ -94,6 +94,19 @@ def test_mxfp4_gemv_scale_extremes(ctx, orc):
     assert rel_err(y.cpu().numpy(), dense @ x.astype(np.float64)) < 1e-5
 
 
+@pytest.mark.parametrize("qtype,rows,cols", [(G.Q4_K, 768, 2048), (G.Q6_K, 2048, 768), (G.Q4_K, 16, 256),
+                                             (G.Q6_K, 37, 512), (G.Q4_K, 512, 2048)])
+def test_kquant_gemv(ctx, orc, qtype, rows, cols):
+    rng = np.random.default_rng(rows * 3 + cols + qtype)
+    w = synth.rand_q4_k(rng, rows * cols) if qtype == G.Q4_K else synth.rand_q6_k(rng, rows * cols)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = torch.empty(rows, dtype=torch.float32, device="cuda")
+    ctx.gemv(qtype, dev(pad_rows(w)), rows, cols, dev(x), y)
+    ctx.sync()
+    dense = orc.dequantize(qtype, w, rows * cols).reshape(rows, cols).astype(np.float64)
+    assert rel_err(y.cpu().numpy(), dense @ x.astype(np.float64)) < 1e-5
+
+
 @pytest.mark.parametrize("rows,cols", [(5120, 2880), (2880, 4096), (64, 64), (13, 2048)])
 def test_q8_0_gemv_activation_quantized(ctx, orc, rows, cols):
     rng = np.random.default_rng(rows + cols)
@@ -270,6 +283,26 @@ def test_in_memory_upload_matches_file(ctx, tiny_path):
     m = synth.build_model(synth.TINY_GPT_OSS, seed=7)
     eng = Engine.from_model(m, max_seq_len=256, ctx=ctx)
     assert eng.generate(f["tiny_gpt_oss_prompt"], 16) == f["tiny_gpt_oss_tokens"].tolist()
+    eng.close()
+
+
+@pytest.fixture(scope="module")
+def tiny_qwen_path(tmp_path_factory):
+    p = str(tmp_path_factory.mktemp("tq") / "tiny_qwen3.gguf")
+    synth.write_model(p, synth.TINY_QWEN3, seed=7)
+    return p
+
+
+def test_tiny_qwen3_q4k_q6k_model(ctx, orc, tiny_qwen_path):
+    """Qwen3-shaped model: Q4_K gate/up, Q6_K down, QK-norm, softmax over all experts + renorm"""
+    from moe_stream_b200.engine import Engine
+    f = np.load(os.path.join(GOLD, "tiny_models.npz"))
+    prompt = f["tiny_qwen3_prompt"]
+    eng = Engine.open(tiny_qwen_path, max_seq_len=256, ctx=ctx)
+    assert eng.generate(prompt, 16) == f["tiny_qwen3_tokens"].tolist()
+    eng.clear_cache()
+    assert rel_err(eng.forward(prompt), f["tiny_qwen3_logits"]) < REL_TOL
+    assert rel_err(eng.last_hidden(), f["tiny_qwen3_hidden"]) < REL_TOL
     eng.close()
 
 
