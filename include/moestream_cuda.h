@@ -137,6 +137,24 @@ MS_API ms_status ms_moe_mxfp4_decode_noalloc(ms_ctx* ctx, const void* d_gate, co
                                              int hidden, int inter, int n_experts, int top_k, int arch,
                                              const float* d_x, const int32_t* d_idx, const float* d_wts, float* d_h);
 
+/* ---- MXFP4 experts in the tensor-core layout ----
+ * The model loader repacks MXFP4 experts into 128-row tiles that the 5th-generation tensor cores
+ * read directly (block-scaled e2m1 x e2m1 MMA, ue8m0 scales; values unchanged).  These entry points
+ * expose the same path for caller-owned buffers (replaces GpuExpertProjection / PackedMxfp4Layer
+ * packing, metal/cache.rs:30-81, 289-308, and upload_mxfp4_weights, metal/mod.rs:1823).
+ * Bytes of the packed gate+up and down stacks of n_experts experts (hidden, inter multiples of 64). */
+MS_API ms_status ms_mxfp4_packed_bytes(int hidden, int inter, int n_experts, size_t* gate_up_bytes,
+                                       size_t* down_bytes);
+/* Repack device-resident native stacks (gate/up [E, inter, hidden], down [E, hidden, inter], GGUF
+ * MXFP4 blocks) into device buffers sized by ms_mxfp4_packed_bytes.  Enqueued on the ctx stream. */
+MS_API ms_status ms_mxfp4_pack_experts(ms_ctx* ctx, const void* gate, const void* up, const void* down, int hidden,
+                                       int inter, int n_experts, void* gate_up_packed, void* down_packed);
+/* ms_moe_mxfp4_decode over packed experts: h += sum_k w_k * FFN_{idx_k}(x) (ascending expert order). */
+MS_API ms_status ms_moe_mxfp4_decode_packed(ms_ctx* ctx, const void* gate_up_packed, const void* down_packed,
+                                            const float* gate_b, const float* up_b, const float* down_b, int hidden,
+                                            int inter, int n_experts, int top_k, int arch, const float* x,
+                                            const int32_t* idx, const float* wts, float* h);
+
 /* ---- model: the Engine surface (engine.rs open_with_device / preload_weights / forward /
  *      generate / clear_cache) ---- */
 typedef struct ms_model_config {

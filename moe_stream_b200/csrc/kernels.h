@@ -89,6 +89,7 @@ struct RouterArgs {
   int H = 0, E = 0, K = 0;
   int softmax_weight = 1;         // GPT-OSS: softmax over the selected k logits
   int normalize = 0;              // renormalise top-k probabilities (norm_topk_prob)
+  uint8_t* xterm = nullptr;       // optional: the normed x as MXFP4 B terms (tc_bterm_bytes(H/32))
 };
 cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s);
 
@@ -124,6 +125,40 @@ cudaError_t launch_moe_combine(const DevCtx& c, const PendingCombine& pc, int H,
 cudaError_t launch_block_gemv(const DevCtx& c, int qtype, const uint8_t* w, int rows, int cols, const float* x,
                               const float* bias, float* y, int accumulate, cudaStream_t s);
 
+// ---- MXFP4 expert FFN on tcgen05 (repacked tiles; kernels_moe_tc.cu) ----
+constexpr int kTcMaxSeg = 16;   // split-K ranges per item held in the partial-sum scratch
+int64_t tc_tile_bytes(int kc);            // one packed 128-row tile over kc chunk columns (K = 32 kc)
+int64_t tc_bterm_bytes(int kc);           // one 16-term B operand over kc chunk columns (umma::bterm_bytes)
+int tc_gu_tiles(int I);                   // gate_up tiles per expert (64 gate + 64 up rows each)
+int tc_down_tiles(int H);                 // down tiles per expert (128 rows each, last zero-padded)
+int tc_max_items(int H, int I, int K);    // rows of the split-K scratch
+bool tc_supported(int H, int I);          // H % 64 == 0 && I % 64 == 0
+struct TcMoeArgs {
+  const uint8_t* gu = nullptr;      // [E_local][tc_gu_tiles(I)][tc_tile_bytes(H/32)]
+  const uint8_t* down = nullptr;    // [E_local][tc_down_tiles(H)][tc_tile_bytes(I/32)]
+  const float* gate_b = nullptr;    // [E_local, I] or null
+  const float* up_b = nullptr;
+  const float* down_b = nullptr;    // [E_local, H] or null
+  const uint8_t* xterm = nullptr;   // B terms of the normed input (tc_bterm_bytes(H/32))
+  uint8_t* act_terms = nullptr;     // scratch [K][tc_bterm_bytes(I/32)]
+  float* act = nullptr;             // optional [K, I] f32 activations
+  float* partial = nullptr;         // [K, H] per-slot expert outputs (bias included)
+  float* part = nullptr;            // split-K scratch [tc_max_items][kTcMaxSeg][128]
+  uint32_t* cnt = nullptr;          // [tc_max_items] zero-initialised, self-resetting
+  const int* idx = nullptr;
+  const float* wts = nullptr;
+  int H = 0, I = 0, K = 0, expert_base = 0, n_local = 0, oai_swiglu = 1;
+  float* h = nullptr;               // as MoeArgs: h += moe(x), or out = moe(x)
+  float* out = nullptr;
+  int defer_combine = 0;
+};
+cudaError_t launch_moe_tc(const DevCtx& c, const TcMoeArgs& a, cudaStream_t s);
+// native GGUF MXFP4 [E][rows][cols] -> packed tiles: rows go to tile r / tile_rows_src at tile row
+// row_off + r % tile_rows_src (gate: 64, 0; up: 64, 64; down: 128, 0)
+cudaError_t launch_mxfp4_pack(const uint8_t* src, int E, int rows, int cols, int tile_rows_src, int row_off,
+                              int tiles, uint8_t* dst, cudaStream_t s);
+cudaError_t launch_xterms(const DevCtx& c, const float* x, int H, uint8_t* xterm, cudaStream_t s);
+
 // ---- attention (decode, one token) ----
 struct AttnArgs {
   const float* qkv = nullptr;      // [nh*hd + 2*nkv*hd] projections (+bias), before RoPE
@@ -149,7 +184,7 @@ struct AttnArgs {
 };
 cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s);
 // splits (grid.x) needed to cover `range` attended positions (128 positions per split)
-int attn_splits(int range);
+int attn_splits(int range, int hd);   // splits of a decode-attention launch covering `range` positions
 
 // ---- LM head / f16 GEMV ----
 // logits = W (RMSNorm(h)*norm_w if norm_w) (+bias); argmax (lowest index on ties) into *key.

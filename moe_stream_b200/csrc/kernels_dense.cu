@@ -219,6 +219,10 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
       int issued = 0;
       for (int j = 0; j < n_stage; ++j) {
         const int s = j % p.ns, n = j / p.ns;
+        if (j == p.ns) {   // ring full: the rest follows the consumers, which start after the wait
+          pdl_wait_prior();
+          pdl_launch_dependents();
+        }
         if (n > 0 && !mbar_wait(&empty[s], (uint32_t)((n - 1) & 1), p.err, EF_TIMEOUT_EMPTY)) break;
         const int r0 = r_begin + j * p.stage_rows;
         const int nr = min(p.stage_rows, r_end - r0);
@@ -230,14 +234,14 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
       for (int j = max(0, issued - p.ns); j < issued; ++j)
         mbar_wait(&full[j % p.ns], (uint32_t)((j / p.ns) & 1), p.err, EF_TIMEOUT_FULL);
     }
-    // the producer warp still joins the block-wide prologue barriers below? no: consumers use
-    // named barrier 1 only, so the producer may leave now.
+    // consumers use named barrier 1 only, so the producer warp may leave now
     return;
   }
 
   // ---- consumer prologue: the activation's Q8_0 blocks in registers.  They come quantized
   // from the producing kernel (xq_in / xd_in), or are made here: (RMSNorm) + Q8_0 quantization.
   pdl_wait_prior();
+  pdl_launch_dependents();   // the next kernel may start its own (weight) prefetch now
   const int nct = kQW * 32;
   const int8_t* xqs = p.xq_in;
   const float* xds = p.xd_in;
@@ -356,15 +360,20 @@ cudaError_t launch_q8(const DevCtx& c, const Q8Params& p, cudaStream_t s) {
 }
 
 // ============================ attention (decode) ============================
-// Grid (splits, kv_heads), 4 warps per CTA, one cached position per lane: a split covers 128
-// consecutive positions.  Each lane dots its K row (read straight from the f32 cache) with
-// every query head of the GQA group (queries broadcast from shared memory); each warp keeps
-// its own softmax max/sum per head; P*V runs with lanes over head dimensions; the four warps
+// Grid (splits, kv_heads), 4 warps per CTA.  A split covers attn_split_len(HD) consecutive
+// positions; right after the position is known, one thread issues bulk copies of the split's
+// cached K and V rows (contiguous in the [kv_head][slot][hd] cache; two pieces where a
+// sliding-window ring wraps) into shared memory, and the query load, QK-norm and RoPE run while
+// they are in flight.  Scores: one position per lane, the K row's float4 chunks visited in a
+// lane-rotated order so a quarter-warp touches distinct banks; each warp keeps its own softmax
+// max/sum per query head; P*V with lanes over head dims from the staged V tile; the four warps
 // merge in shared memory; the last CTA of a kv head merges the splits, with the attention sink
 // in the denominator (ops/attention.rs:178-280).
 constexpr int kAWarps = 4;
 constexpr int kAThreads = kAWarps * 32;
-constexpr int kASplit = kAWarps * 32;   // positions per split
+
+// positions per split: K + V tiles of one split fill 64 KB of shared memory
+__host__ __device__ constexpr int attn_split_len(int hd) { return hd <= 64 ? 128 : 8192 / hd; }
 
 __device__ __forceinline__ void rope_inplace(float* v, int rot, const float* c, const float* s) {
   // ops/attention.rs:96-118: half-rotate over the first `rot` dims
@@ -390,23 +399,55 @@ __device__ __forceinline__ void head_norm_warp(float* v, const float* w, int hd,
 template <int HD, int REP>
 __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint32_t* err) {
   constexpr int DL = HD / 32;                  // head dims per lane in P*V
+  constexpr int SPL = attn_split_len(HD);      // positions per split
+  constexpr int PW = SPL / kAWarps;            // positions per warp (<= 32)
+  constexpr int NC = HD / 4;                   // float4 chunks per row
+  extern __shared__ __align__(128) float dyn[];
+  float* Kt = dyn;                             // [SPL][HD] staged cache rows
+  float* Vt = Kt + SPL * HD;
+  float* wsm = Vt + SPL * HD;                  // [S][REP] split weights of the final merge
   __shared__ __align__(16) float qs[REP * HD];
   __shared__ __align__(16) float kn[HD];
   __shared__ __align__(16) float vn[HD];
   __shared__ float pw[kAWarps][REP][32];
   __shared__ float mw[kAWarps][REP], lw[kAWarps][REP];
   __shared__ __align__(16) float ow[kAWarps][REP][HD];
+  __shared__ __align__(8) uint64_t bar;
   __shared__ uint32_t last;
+  __shared__ int tile_ok;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kh = blockIdx.y, sidx = blockIdx.x, S = gridDim.x;
-  pdl_wait_prior();
+  // The position comes from the step's first kernel and the cached rows from earlier steps, both
+  // complete before the previous kernel started (every kernel lets its dependents launch only after
+  // its own wait), so the tile copies go out before this kernel waits for the projections.
   const int pos = *a.pos;
   const int lo = a.window ? max(0, pos - a.window + 1) : 0;
-  const int p0 = lo + sidx * kASplit, p1 = min(p0 + kASplit, pos + 1);
+  const int p0 = lo + sidx * SPL, p1 = min(p0 + SPL, pos + 1);
   const bool active = p0 < p1;
   const bool has_new = active && p1 == pos + 1;
+  const int pc1 = has_new ? pos : p1;          // cached rows [p0, pc1); the new row comes from qkv
   const int half = a.rot / 2;
   float* part = a.part + ((size_t)kh * S + sidx) * REP * (HD + 2);
+  if (threadIdx.x == 0) {
+    tile_ok = 1;
+    if (active && pc1 > p0) {
+      mbar_init(&bar, 1);
+      fence_mbar_init();
+      mbar_expect_tx(&bar, (uint32_t)(2 * (pc1 - p0) * HD * 4));
+      const float* kbase = a.kc + (size_t)kh * a.cap * HD;
+      const float* vbase = a.vc + (size_t)kh * a.cap * HD;
+      for (int q = p0; q < pc1;) {   // kv_cache.rs:37-60 slot order (ring for sliding-window layers)
+        const int slot = a.window ? q % a.cap : q;
+        const int n = a.window ? min(pc1 - q, a.cap - slot) : pc1 - q;
+        const uint32_t bytes = (uint32_t)(n * HD * 4);
+        bulk_g2s(Kt + (size_t)(q - p0) * HD, kbase + (size_t)slot * HD, bytes, &bar);
+        bulk_g2s(Vt + (size_t)(q - p0) * HD, vbase + (size_t)slot * HD, bytes, &bar);
+        q += n;
+      }
+    }
+  }
+  pdl_wait_prior();
+  pdl_launch_dependents();
   if (active) {
     const float* cs = a.cos_t + (size_t)pos * half;
     const float* sn = a.sin_t + (size_t)pos * half;
@@ -431,21 +472,23 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
       float* vd = a.vc + ((size_t)kh * a.cap + slot) * HD;
       for (int i = threadIdx.x; i < HD; i += kAThreads) { kd[i] = kn[i]; vd[i] = vn[i]; }
     }
+    if (pc1 > p0 && !mbar_wait(&bar, 0, err, EF_TIMEOUT_FULL)) tile_ok = 0;
     // ---- scores: one position per lane ----
-    const int p = p0 + warp * 32 + lane;
-    const bool valid = p < p1;
-    const int slot = a.window ? p % a.cap : p;
-    const float* krow = (p == pos) ? kn : a.kc + ((size_t)kh * a.cap + slot) * HD;
+    const int i_loc = warp * PW + lane;
+    const int p = p0 + i_loc;
+    const bool valid = lane < PW && p < p1;
+    const float* krow = (p == pos) ? kn : Kt + (size_t)i_loc * HD;
     float dot[REP];
 #pragma unroll
     for (int h = 0; h < REP; ++h) dot[h] = 0.f;
     if (valid) {
 #pragma unroll 4
-      for (int d = 0; d < HD; d += 4) {
-        const float4 k4 = *reinterpret_cast<const float4*>(krow + d);
+      for (int k = 0; k < NC; ++k) {
+        const int c = (k + lane) & (NC - 1);
+        const float4 k4 = *reinterpret_cast<const float4*>(krow + 4 * c);
 #pragma unroll
         for (int h = 0; h < REP; ++h) {
-          const float4 q4 = *reinterpret_cast<const float4*>(qs + h * HD + d);
+          const float4 q4 = *reinterpret_cast<const float4*>(qs + h * HD + 4 * c);
           dot[h] = fmaf(q4.x, k4.x, fmaf(q4.y, k4.y, fmaf(q4.z, k4.z, fmaf(q4.w, k4.w, dot[h]))));
         }
       }
@@ -466,11 +509,11 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
     for (int h = 0; h < REP; ++h)
 #pragma unroll
       for (int t = 0; t < DL; ++t) o[h][t] = 0.f;
-    const int nvalid = min(32, p1 - (p0 + warp * 32));
+    const int nvalid = max(0, min(PW, p1 - (p0 + warp * PW)));
+#pragma unroll 4
     for (int j = 0; j < nvalid; ++j) {
-      const int pj = p0 + warp * 32 + j;
-      const int sj = a.window ? pj % a.cap : pj;
-      const float* vrow = (pj == pos) ? vn : a.vc + ((size_t)kh * a.cap + sj) * HD;
+      const int jl = warp * PW + j;
+      const float* vrow = (p0 + jl == pos) ? vn : Vt + (size_t)jl * HD;
       float v[DL];
 #pragma unroll
       for (int t = 0; t < DL; ++t) v[t] = vrow[lane + 32 * t];
@@ -502,6 +545,7 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
           O = fmaf(ow[w][h][d], f, O);
         }
       }
+      if (!tile_ok) { M = -INFINITY; L = 0.f; O = 0.f; }   // a timed-out copy contributes nothing
       part[h * (HD + 2) + 2 + d] = O;
       if (d == 0) { part[h * (HD + 2)] = M; part[h * (HD + 2) + 1] = L; }
     }
@@ -516,7 +560,6 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
   __threadfence();
   // ---- merge the splits of this kv group (+ attention sink) ----
   const float* gp = a.part + (size_t)kh * S * REP * (HD + 2);
-  float* wsm = &pw[0][0][0];                         // [S][REP] split weights (S * REP <= 4 * REP * 32)
   float* hm = &mw[0][0];
   float* hinv = &lw[0][0];
   for (int i = threadIdx.x; i < S * REP; i += kAThreads) wsm[i] = __ldcg(&gp[(size_t)i * (HD + 2)]);
@@ -591,6 +634,7 @@ __global__ void __launch_bounds__(kLWarps * 32, 1) lmhead_kernel(LmHeadArgs a) {
   __shared__ unsigned long long bestk[kLWarps];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_wait_prior();
+  pdl_launch_dependents();   // the next kernel may start its own (weight) prefetch now
   for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
     const float v = a.x[i];
     xs[i] = v;
@@ -680,6 +724,7 @@ __global__ void __launch_bounds__(1024) embed_kernel(StepState* st, const void* 
   __shared__ int tok_s;
   __shared__ float red[32];
   pdl_wait_prior();
+  pdl_launch_dependents();   // the next kernel may start its own (weight) prefetch now
   if (threadIdx.x == 0) {
     int tok = st->token_in;
     if (st->use_argmax) {
@@ -719,6 +764,7 @@ __global__ void __launch_bounds__(1024) resid_norm_q8_kernel(PendingCombine pc, 
   __shared__ CombineOrder co;
   __shared__ float red[32];
   pdl_wait_prior();
+  pdl_launch_dependents();   // the next kernel may start its own (weight) prefetch now
   if (threadIdx.x == 0) combine_order(pc, &co);
   __syncthreads();
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
@@ -772,8 +818,9 @@ cudaError_t launch_q8_gemv(const DevCtx& c, const Q8GemvArgs& a, cudaStream_t s)
   p.stage_rows = kQW;                           // one row per consumer warp
   if (p.stage_rows % u) p.stage_rows = u;       // (u <= 16; rows per stage must keep alignment)
   p.stage_bytes = (int)((((int64_t)p.stage_rows * p.rb) + 15) & ~15ll);
-  p.ns = (int)((180 * 1024) / p.stage_bytes);
-  p.ns = p.ns > 6 ? 6 : (p.ns < 2 ? 2 : p.ns);
+  // <= ~128 KB of stages, so the neighbouring kernels' CTAs (attention, MoE) fit beside this one
+  p.ns = (int)((128 * 1024) / p.stage_bytes);
+  p.ns = p.ns > 5 ? 5 : (p.ns < 2 ? 2 : p.ns);
   p.x = a.x; p.norm_w = a.norm_w; p.eps = a.eps; p.bias = a.bias; p.y = a.y; p.residual = a.residual;
   p.xq_in = a.xq_in; p.xd_in = a.xd_in;
   p.err = c.err;
@@ -787,26 +834,35 @@ cudaError_t launch_q8_gemv(const DevCtx& c, const Q8GemvArgs& a, cudaStream_t s)
   return cudaErrorInvalidValue;
 }
 
+template <int HD, int REP>
+cudaError_t launch_attn_k(const AttnArgs& a, const DevCtx& c, dim3 grid, cudaStream_t s) {
+  const size_t smem = ((size_t)2 * attn_split_len(HD) * HD + (size_t)a.S * REP) * sizeof(float);
+  cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(attn_decode_kernel<HD, REP>, grid, dim3(kAThreads), smem, s, a, c.err);
+}
+
 template <int HD>
 cudaError_t launch_attn_hd(const AttnArgs& a, const DevCtx& c, int rep, dim3 grid, cudaStream_t s) {
   switch (rep) {
-    case 1: return launch_pdl(attn_decode_kernel<HD, 1>, grid, dim3(kAThreads), 0, s, a, c.err);
-    case 2: return launch_pdl(attn_decode_kernel<HD, 2>, grid, dim3(kAThreads), 0, s, a, c.err);
-    case 4: return launch_pdl(attn_decode_kernel<HD, 4>, grid, dim3(kAThreads), 0, s, a, c.err);
-    case 8: return launch_pdl(attn_decode_kernel<HD, 8>, grid, dim3(kAThreads), 0, s, a, c.err);
+    case 1: return launch_attn_k<HD, 1>(a, c, grid, s);
+    case 2: return launch_attn_k<HD, 2>(a, c, grid, s);
+    case 4: return launch_attn_k<HD, 4>(a, c, grid, s);
+    case 8: return launch_attn_k<HD, 8>(a, c, grid, s);
     case 16:
-      if constexpr (HD <= 64) return launch_pdl(attn_decode_kernel<HD, 16>, grid, dim3(kAThreads), 0, s, a, c.err);
+      if constexpr (HD <= 64) return launch_attn_k<HD, 16>(a, c, grid, s);
       break;
   }
   return cudaErrorInvalidValue;
 }
 
-int attn_splits(int range) { return (range + kASplit - 1) / kASplit; }
+int attn_splits(int range, int hd) { return (range + attn_split_len(hd) - 1) / attn_split_len(hd); }
 
 cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s) {
   if (a.nkv <= 0 || a.nh % a.nkv || a.S <= 0 || a.rot > a.hd || a.rot % 2) return cudaErrorInvalidValue;
   const int rep = a.nh / a.nkv;
-  if (a.S > kAWarps * 32) return cudaErrorInvalidValue;   // merge scratch holds S * rep weights
+  if ((size_t)a.S * rep > 8192) return cudaErrorInvalidValue;   // merge weights: <= 32 KB of shared memory
   const dim3 grid((unsigned)a.S, (unsigned)a.nkv);
   switch (a.hd) {
     case 32: return launch_attn_hd<32>(a, c, rep, grid, s);

@@ -18,9 +18,25 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "umma.cuh"
 
 namespace ms {
 namespace {
+
+// Optional timeline of the phase kernel (build with -DMS_TRACE): %globaltimer stamps per CTA in
+// g_phase_trace[mode][cta][slot] -- 0 entry, 1 prologue done, 2..9 warp 0's stage j ready,
+// 10 warp 0 done, 11 producer's last copy issued.
+#ifdef MS_TRACE
+__device__ unsigned long long g_phase_trace[3][1024][16];
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define PHASE_TRACE(k) (g_phase_trace[p.mode][blockIdx.x & 1023][(k)] = gtimer())
+#else
+#define PHASE_TRACE(k) ((void)0)
+#endif
 
 constexpr int kCW = 16;                   // consumer warps
 constexpr int kThreads = (kCW + 1) * 32;  // + one producer warp
@@ -288,7 +304,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+  if (threadIdx.x == 0) PHASE_TRACE(0);
   pdl_wait_prior();
+  pdl_launch_dependents();   // the next kernel may start its own (weight) prefetch now
   if (threadIdx.x == 0) {
     // local slots ordered by ascending expert id (the reference's accumulation order)
     int n = 0;
@@ -318,6 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
     fence_mbar_init();
   }
   __syncthreads();
+  if (threadIdx.x == 0) PHASE_TRACE(1);
 
   const int n_items = si->n * p.n_tiles;
   const int begin = (int)((int64_t)blockIdx.x * n_items / gridDim.x);
@@ -343,6 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
         if (p.mode == MODE_GATEUP) bulk_g2s_stream(dst + part_bytes, p.w1 + base, part_bytes, &full[s], pol);
         ++issued;
       }
+      PHASE_TRACE(11);
       // make sure no copy into this CTA's shared memory is still in flight at exit
       for (int j = max(0, issued - p.ns); j < issued; ++j)
         mbar_wait(&full[j % p.ns], (uint32_t)((j / p.ns) & 1), p.err, EF_TIMEOUT_FULL);
@@ -398,6 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
       if (lane == 0) atomicExch(abort_flag, 1);
       break;
     }
+    if (warp == 0 && lane == 0 && j < 8) PHASE_TRACE(2 + j);
     const uint8_t* st = stages + (size_t)s * p.stage_bytes;
 #pragma unroll
     for (int i = 0; i < NBW; ++i) {
@@ -452,6 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
       if (lane == 0) red_cnt[rbuf] = 0u;
     }
   }
+  if (warp == 0 && lane == 0) PHASE_TRACE(10);
 }
 
 template <int FMT, int NBW, int RT>
@@ -530,13 +552,15 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, ui
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x;
   pdl_wait_prior();
+  pdl_launch_dependents();   // the next kernel may start its own (weight) prefetch now
   const float* wr = a.w + (size_t)e * a.H;
   float dot = 0.f;
+  float inv = 1.f;
   if (a.h) {
     float ss = 0.f;
     for (int i = threadIdx.x; i < a.H; i += kRouterThreads) { const float v = a.h[i]; ss += v * v; }
     ss = router_block_sum(ss, red);
-    const float inv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
+    inv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
     for (int i = threadIdx.x; i < a.H; i += kRouterThreads) {
       const float v = (a.h[i] * inv) * a.norm_w[i];
       if (e == 0) a.xn[i] = v;
@@ -546,6 +570,16 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, ui
     for (int i = threadIdx.x; i < a.H; i += kRouterThreads) dot = fmaf(a.xn[i], __ldcs(wr + i), dot);
   }
   dot = router_block_sum(dot, red);
+  if (a.xterm) {
+    // the normed x as the expert GEMVs' B terms: warp w of CTA e takes 32-element blocks
+    // e*8 + w, e*8 + w + 8*E, ... (same arithmetic as xn above, so the terms encode xn exactly)
+    const int nb = a.H / 32, nw = kRouterThreads / 32;
+    for (int b = e * nw + warp; b < nb; b += (int)gridDim.x * nw) {
+      const int i = 32 * b + lane;
+      const float v = a.h ? (a.h[i] * inv) * a.norm_w[i] : a.xn[i];
+      umma::quantize_terms_warp(v, lane, a.xterm, nb, b);
+    }
+  }
   if (threadIdx.x == 0) {
     float v = dot + (a.b ? a.b[e] : 0.f);
     if (a.mask && a.mask[e]) v = -INFINITY;
@@ -634,6 +668,7 @@ size_t moe_mxfp4_smem_bytes(int H, int I) {
 __global__ void moe_combine_kernel(PendingCombine pc, int H, float* h, float* out) {
   __shared__ CombineOrder co;
   pdl_wait_prior();
+  pdl_launch_dependents();   // the next kernel may start its own (weight) prefetch now
   if (threadIdx.x == 0) combine_order(pc, &co);
   __syncthreads();
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < H; r += gridDim.x * blockDim.x) {

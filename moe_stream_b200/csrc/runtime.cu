@@ -14,6 +14,7 @@
 #include <unistd.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -86,7 +87,9 @@ ms_status ensure_scratch(ms_ctx* c, size_t bytes, size_t counters) {
     c->counters = nullptr;
     c->n_counters = 0;
     MS_CUDA(c, cudaMalloc(&c->counters, counters * 4));
-    MS_CUDA(c, cudaMemset(c->counters, 0, counters * 4));
+    // zeroed on the stream the kernels that use them are enqueued on (it may not synchronise
+    // with the legacy stream)
+    MS_CUDA(c, cudaMemsetAsync(c->counters, 0, counters * 4, c->stream));
     c->n_counters = counters;
   }
   return MS_OK;
@@ -135,6 +138,11 @@ struct LayerW {
   int* idx = nullptr;
   float* wts = nullptr;
   int qkv_parts = 0, bqkv_parts = 0;
+  // MXFP4 experts repacked for the tensor-core path (kernels_moe_tc.cu); native pointers stay null
+  uint8_t* gu_tc = nullptr;
+  uint8_t* down_tc = nullptr;
+  bool have_gate = false, have_up = false, have_down = false;
+  bool tc = false;
 };
 
 // NCCL is resolved at run time (dlopen), so a process that already loaded libnccl (torch does)
@@ -200,6 +208,11 @@ struct ms_model {
   StepState* h_st = nullptr;        // pinned
   int kernels_per_step = 0;
   int prof_class = -1;   // >= 0: enqueue only the launches of this class (ms_model_profile_step)
+  bool use_tc = true;    // repack MXFP4 experts for the tcgen05 path (MS_MOE_TC=0 keeps native blocks)
+  uint8_t* xterm = nullptr;       // B terms of the MoE input (tensor-core path)
+  uint8_t* act_terms = nullptr;   // [K] B terms of the expert activations
+  float* tc_part = nullptr;       // split-K partial sums
+  uint32_t* tc_cnt = nullptr;
 
   template <class T>
   ms_status alloc(T** p, size_t bytes, bool zero = true) {
@@ -318,9 +331,40 @@ ms_status set_layer_tensor(ms_model* m, int li, const std::string& t, int q, con
       if (q != Q_MXFP4 && q != Q_Q4_K && q != Q_Q6_K)
         return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: expert qtype %d not supported", nm, q);
       const int64_t per = raw_bytes(q, (int64_t)x.rows * x.cols);
+      *x.qt = q;
+      const bool is_down = x.w == &Lw.down;
+      (is_down ? Lw.have_down : (x.w == &Lw.gate ? Lw.have_gate : Lw.have_up)) = true;
+      if (q == Q_MXFP4 && m->use_tc && tc_supported(H, c.inter)) {
+        // repack this rank's experts into tensor-core tiles (gate rows 0-63 and up rows 64-127 of a
+        // gate_up tile; 128 hidden rows per down tile); the native blocks are not kept
+        uint8_t** dst = is_down ? &Lw.down_tc : &Lw.gu_tc;
+        const int tiles = is_down ? tc_down_tiles(H) : tc_gu_tiles(c.inter);
+        const int64_t tbytes = tc_tile_bytes(x.cols / 32);
+        // zeroing, upload and repack are ordered on the context's private stream (which does not
+        // synchronise with the legacy stream), then waited for
+        cudaStream_t os = m->ctx->own;
+        const size_t pbytes = (size_t)m->n_local * tiles * tbytes;
+        const bool fresh = *dst == nullptr;
+        if (fresh) {
+          ms_status s = m->alloc(dst, pbytes, false);
+          if (s != MS_OK) return s;
+        }
+        void* tmp = nullptr;
+        MS_CUDA(m->ctx, cudaMalloc(&tmp, (size_t)per * m->n_local));
+        cudaError_t e = fresh ? cudaMemsetAsync(*dst, 0, pbytes, os) : cudaSuccess;
+        if (e == cudaSuccess)
+          e = cudaMemcpyAsync(tmp, (const uint8_t*)data + per * m->expert_base, (size_t)per * m->n_local,
+                              cudaMemcpyHostToDevice, os);
+        if (e == cudaSuccess)
+          e = launch_mxfp4_pack((const uint8_t*)tmp, m->n_local, x.rows, x.cols, is_down ? 128 : 64,
+                                x.w == &Lw.up ? 64 : 0, tiles, *dst, os);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(os);
+        cudaFree(tmp);
+        if (e != cudaSuccess) return cuda_fail(m->ctx, e, "mxfp4 repack");
+        return MS_OK;
+      }
       ms_status s = m->alloc(x.w, padded((size_t)per * m->n_local));
       if (s != MS_OK) return s;
-      *x.qt = q;
       return upload(m, *x.w, (const uint8_t*)data + per * m->expert_base, (size_t)per * m->n_local);
     }
     if (t == bn) {
@@ -397,7 +441,13 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     ra.mask = Lw.mask; ra.logits = m->router_logits; ra.idx = Lw.idx; ra.wts = Lw.wts; ra.counter = m->router_cnt;
     ra.H = H; ra.E = c.experts; ra.K = c.top_k; ra.softmax_weight = c.arch == MS_ARCH_GPT_OSS;
     ra.normalize = c.norm_topk_prob;
+    if (Lw.tc) ra.xterm = m->xterm;
     LAUNCH(launch_router(dc, ra, s));
+    TcMoeArgs ta;
+    ta.gu = Lw.gu_tc; ta.down = Lw.down_tc; ta.gate_b = Lw.gate_b; ta.up_b = Lw.up_b; ta.down_b = Lw.down_b;
+    ta.xterm = m->xterm; ta.act_terms = m->act_terms; ta.act = m->act; ta.partial = m->partial; ta.part = m->tc_part;
+    ta.cnt = m->tc_cnt; ta.idx = Lw.idx; ta.wts = Lw.wts; ta.H = H; ta.I = c.inter; ta.K = c.top_k;
+    ta.expert_base = m->expert_base; ta.n_local = m->n_local; ta.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ta.h = m->h;
     MoeArgs ma;
     ma.gate_q = Lw.gate_q; ma.down_q = Lw.down_q;
     ma.x = m->xn; ma.idx = Lw.idx; ma.wts = Lw.wts; ma.gate = Lw.gate; ma.up = Lw.up; ma.down = Lw.down;
@@ -408,7 +458,9 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     if (c.ep_size > 1) {
       // expert parallel: combine the local experts into moe_out, sum it over the EP group
       ma.defer_combine = 0; ma.out = m->moe_out;
-      LAUNCH(launch_moe_mxfp4(dc, ma, s));
+      ta.defer_combine = 0; ta.out = m->moe_out;
+      if (Lw.tc) LAUNCH(launch_moe_tc(dc, ta, s));
+      else LAUNCH(launch_moe_mxfp4(dc, ma, s));
       nk += 2;   // gate/up, down, combine
       NcclApi* api = nccl_api();
       ncclResult_t r = api->all_reduce(m->moe_out, m->moe_out, (size_t)H, ncclFloat32, ncclSum, m->comm, s);
@@ -416,7 +468,9 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
       pc.dense = m->moe_out;
     } else {
       ma.defer_combine = 1;   // per-slot outputs stay in `partial`; the next kernel combines them
-      LAUNCH(launch_moe_mxfp4(dc, ma, s));
+      ta.defer_combine = 1;
+      if (Lw.tc) LAUNCH(launch_moe_tc(dc, ta, s));
+      else LAUNCH(launch_moe_mxfp4(dc, ma, s));
       ++nk;   // gate/up, down
       pc.partial = m->partial; pc.idx = Lw.idx; pc.wts = Lw.wts; pc.K = c.top_k;
       pc.expert_base = m->expert_base; pc.n_local = m->n_local;
@@ -668,6 +722,54 @@ ms_status ms_moe_mxfp4_decode(ms_ctx* c, const void* gate, const void* up, const
   return MS_OK;
 }
 
+ms_status ms_mxfp4_packed_bytes(int H, int I, int E, size_t* gu_bytes, size_t* down_bytes) {
+  if (!gu_bytes || !down_bytes || E <= 0 || H <= 0 || I <= 0) return MS_ERR_INVALID_ARG;
+  if (!tc_supported(H, I)) return MS_ERR_SHAPE;
+  *gu_bytes = (size_t)E * tc_gu_tiles(I) * tc_tile_bytes(H / 32);
+  *down_bytes = (size_t)E * tc_down_tiles(H) * tc_tile_bytes(I / 32);
+  return MS_OK;
+}
+
+ms_status ms_mxfp4_pack_experts(ms_ctx* c, const void* gate, const void* up, const void* down, int H, int I, int E,
+                                void* gu_packed, void* down_packed) {
+  if (!c || !gate || !up || !down || !gu_packed || !down_packed || E <= 0) return MS_ERR_INVALID_ARG;
+  size_t gb = 0, db = 0;
+  if (ms_mxfp4_packed_bytes(H, I, E, &gb, &db) != MS_OK) return fail(c, MS_ERR_SHAPE, "pack: hidden and inter must be multiples of 64");
+  cudaSetDevice(c->device);
+  MS_CUDA(c, cudaMemsetAsync(gu_packed, 0, gb, c->stream));
+  MS_CUDA(c, cudaMemsetAsync(down_packed, 0, db, c->stream));
+  MS_CUDA(c, launch_mxfp4_pack((const uint8_t*)gate, E, I, H, 64, 0, tc_gu_tiles(I), (uint8_t*)gu_packed, c->stream));
+  MS_CUDA(c, launch_mxfp4_pack((const uint8_t*)up, E, I, H, 64, 64, tc_gu_tiles(I), (uint8_t*)gu_packed, c->stream));
+  MS_CUDA(c, launch_mxfp4_pack((const uint8_t*)down, E, H, I, 128, 0, tc_down_tiles(H), (uint8_t*)down_packed,
+                               c->stream));
+  return MS_OK;
+}
+
+ms_status ms_moe_mxfp4_decode_packed(ms_ctx* c, const void* gu, const void* down, const float* gb, const float* ub,
+                                     const float* db, int H, int I, int E, int K, int arch, const float* x,
+                                     const int32_t* idx, const float* wts, float* h) {
+  if (!c || !gu || !down || !x || !idx || !wts || !h || K <= 0 || K > 16 || E <= 0) return MS_ERR_INVALID_ARG;
+  if (!tc_supported(H, I)) return fail(c, MS_ERR_SHAPE, "moe packed: hidden and inter must be multiples of 64");
+  const size_t al = 256;
+  auto up = [&](size_t b) { return (b + al - 1) & ~(al - 1); };
+  const size_t xt_b = up((size_t)tc_bterm_bytes(H / 32)), at_b = up((size_t)K * tc_bterm_bytes(I / 32));
+  const size_t act_b = up((size_t)K * I * 4), part_b = up((size_t)K * H * 4);
+  const int items = tc_max_items(H, I, K);
+  const size_t sp_b = up((size_t)items * kTcMaxSeg * 128 * 4);
+  ms_status s = ensure_scratch(c, xt_b + at_b + act_b + part_b + sp_b, 64 + 1024 + (size_t)items);
+  if (s != MS_OK) return s;
+  uint8_t* base = (uint8_t*)c->scratch;
+  TcMoeArgs a;
+  a.gu = (const uint8_t*)gu; a.down = (const uint8_t*)down; a.gate_b = gb; a.up_b = ub; a.down_b = db;
+  a.xterm = base; a.act_terms = base + xt_b; a.act = (float*)(base + xt_b + at_b);
+  a.partial = (float*)(base + xt_b + at_b + act_b); a.part = (float*)(base + xt_b + at_b + act_b + part_b);
+  a.cnt = c->counters + 64 + 1024; a.idx = idx; a.wts = wts; a.H = H; a.I = I; a.K = K; a.expert_base = 0;
+  a.n_local = E; a.oai_swiglu = arch == MS_ARCH_GPT_OSS; a.h = h;
+  MS_CUDA(c, launch_xterms(c->dc, x, H, base, c->stream));
+  MS_CUDA(c, launch_moe_tc(c->dc, a, c->stream));
+  return MS_OK;
+}
+
 // ---------------------------------------------------------------------------------
 ms_status ms_model_create(ms_ctx* c, const ms_model_config* cfg, ms_model** out) {
   if (!c || !cfg || !out) return MS_ERR_INVALID_ARG;
@@ -685,6 +787,7 @@ ms_status ms_model_create(ms_ctx* c, const ms_model_config* cfg, ms_model** out)
   m->cfg = k;
   m->L.resize(k.layers);
   m->n_local = k.experts / k.ep_size;
+  if (const char* v = getenv("MS_MOE_TC")) m->use_tc = atoi(v) != 0;
   m->expert_base = k.ep_rank * m->n_local;
   *out = m;
   return MS_OK;
@@ -734,10 +837,16 @@ ms_status ms_model_finalize(ms_model* m) {
   cudaSetDevice(m->ctx->device);
   const ms_model_config& c = m->cfg;
   if (!m->embd || !m->out_w || !m->out_norm) return fail(m->ctx, MS_ERR_STATE, "missing token_embd/output/output_norm");
+  bool any_tc = false;
   for (int li = 0; li < c.layers; ++li) {
     LayerW& Lw = m->L[li];
-    if (!Lw.attn_norm || !Lw.post_norm || Lw.qkv_parts != 3 || !Lw.wo || !Lw.router_w || !Lw.gate || !Lw.up || !Lw.down)
+    if (!Lw.attn_norm || !Lw.post_norm || Lw.qkv_parts != 3 || !Lw.wo || !Lw.router_w || !Lw.have_gate ||
+        !Lw.have_up || !Lw.have_down)
       return fail(m->ctx, MS_ERR_STATE, "layer %d: missing tensors", li);
+    Lw.tc = Lw.gu_tc && Lw.down_tc;
+    if ((Lw.gu_tc || Lw.down_tc) && !Lw.tc)
+      return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "layer %d: MXFP4 and K-quant experts mixed in one layer", li);
+    any_tc = any_tc || Lw.tc;
     if (Lw.bqkv_parts != 0 && Lw.bqkv_parts != 3) return fail(m->ctx, MS_ERR_STATE, "layer %d: partial qkv bias", li);
     if ((Lw.qn == nullptr) != (Lw.kn == nullptr)) return fail(m->ctx, MS_ERR_STATE, "layer %d: q/k norm mismatch", li);
     Lw.window = (c.sliding_window > 0 && li % 2 == 0) ? c.sliding_window : 0;   // config.rs:463-465
@@ -752,9 +861,9 @@ ms_status ms_model_finalize(ms_model* m) {
   }
   const int H = c.hidden, Dq = q_dim(c), Dkv = kv_dim(c), rep = c.heads / c.kv_heads;
   // decode attention splits: 128 positions each, sized for the longest attended range
-  const int S = attn_splits(c.max_seq_len);
+  const int S = attn_splits(c.max_seq_len, c.head_dim);
   m->splits_full = S;
-  m->splits_swa = c.sliding_window > 0 ? attn_splits(std::min(c.sliding_window, c.max_seq_len)) : S;
+  m->splits_swa = c.sliding_window > 0 ? attn_splits(std::min(c.sliding_window, c.max_seq_len), c.head_dim) : S;
   ms_status s = MS_OK;
   s = s ? s : m->alloc(&m->h, (size_t)H * 4);
   s = s ? s : m->alloc(&m->h_last, (size_t)H * 4);
@@ -776,6 +885,12 @@ ms_status ms_model_finalize(ms_model* m) {
   s = s ? s : m->alloc(&m->attn_cnt, (size_t)(c.kv_heads + 16) * 4);
   s = s ? s : m->alloc(&m->st, sizeof(StepState));
   s = s ? s : m->alloc(&m->token_log, (size_t)(c.max_seq_len + 1) * 4);
+  if (any_tc) {
+    s = s ? s : m->alloc(&m->xterm, (size_t)tc_bterm_bytes(H / 32));
+    s = s ? s : m->alloc(&m->act_terms, (size_t)c.top_k * tc_bterm_bytes(c.inter / 32));
+    s = s ? s : m->alloc(&m->tc_part, (size_t)tc_max_items(H, c.inter, c.top_k) * kTcMaxSeg * 128 * 4);
+    s = s ? s : m->alloc(&m->tc_cnt, (size_t)tc_max_items(H, c.inter, c.top_k) * 4);
+  }
   if (s != MS_OK) return s;
   std::vector<float> cs, sn;
   rope_tables(c.rot_dim, c.max_seq_len, (double)c.rope_theta, cs, sn);

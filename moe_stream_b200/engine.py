@@ -86,6 +86,24 @@ class Context:
                                                 _ptr(up_b), _ptr(down_b), hidden, inter, n_experts, top_k, arch,
                                                 _ptr(x), _ptr(idx), _ptr(wts), _ptr(h)), self.h)
 
+    @staticmethod
+    def mxfp4_packed_bytes(hidden: int, inter: int, n_experts: int):
+        """(gate_up_bytes, down_bytes) of the tensor-core expert layout."""
+        g, d = C.c_size_t(), C.c_size_t()
+        check(lib().ms_mxfp4_packed_bytes(hidden, inter, n_experts, C.byref(g), C.byref(d)))
+        return g.value, d.value
+
+    def mxfp4_pack_experts(self, gate, up, down, hidden, inter, n_experts, gu_packed, down_packed) -> None:
+        check(lib().ms_mxfp4_pack_experts(self.h, _ptr(gate), _ptr(up), _ptr(down), hidden, inter, n_experts,
+                                          _ptr(gu_packed), _ptr(down_packed)), self.h)
+
+    def moe_mxfp4_decode_packed(self, gu_packed, down_packed, gate_b, up_b, down_b, hidden, inter, n_experts, top_k,
+                                arch, x, idx, wts, h) -> None:
+        """The expert FFN on the tensor cores over packed experts (see mxfp4_pack_experts)."""
+        check(lib().ms_moe_mxfp4_decode_packed(self.h, _ptr(gu_packed), _ptr(down_packed), _ptr(gate_b), _ptr(up_b),
+                                               _ptr(down_b), hidden, inter, n_experts, top_k, arch, _ptr(x),
+                                               _ptr(idx), _ptr(wts), _ptr(h)), self.h)
+
     def close(self) -> None:
         if getattr(self, "h", None):
             for e in list(getattr(self, "_engines", ())):

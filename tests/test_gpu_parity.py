@@ -203,6 +203,63 @@ def test_moe_residual_accumulates(ctx, orc):
     assert rel_err(d_h.cpu().numpy() - h, want[0]) < REL_TOL
 
 
+def _packed(ctx, L, spec):
+    """native GGUF MXFP4 stacks -> the tensor-core tile layout, through the C ABI"""
+    from moe_stream_b200.engine import Context
+    H, I, E = spec.hidden, spec.inter, spec.experts
+    gb, db = Context.mxfp4_packed_bytes(H, I, E)
+    gu = torch.empty(gb, dtype=torch.uint8, device="cuda")
+    dn = torch.empty(db, dtype=torch.uint8, device="cuda")
+    ctx.mxfp4_pack_experts(dev(L["gate"]), dev(L["up"]), dev(L["down"]), H, I, E, gu, dn)
+    return gu, dn
+
+
+@pytest.mark.parametrize("spec", [synth.GPT_OSS_MOE_LAYER, synth.TINY_GPT_OSS], ids=["gpt-oss-20b", "tiny"])
+def test_moe_packed_tensor_core_layer(ctx, orc, spec):
+    """config 0 on the tcgen05 block-scaled path: packed experts, x as MXFP4 residual terms"""
+    L = _moe_layer_host(spec, seed=0)
+    x = synth.moe_layer_input(spec, seed=0)
+    want, want_idx, want_w = orc.moe_forward(L, x)
+    H, I, E, K = spec.hidden, spec.inter, spec.experts, spec.top_k
+    gu, dn = _packed(ctx, L, spec)
+    out = torch.zeros(H, dtype=torch.float32, device="cuda")
+    for _ in range(2):   # the second call checks the self-resetting split-K counters
+        out.zero_()
+        ctx.moe_mxfp4_decode_packed(gu, dn, dev(L["gate_bias"]), dev(L["up_bias"]), dev(L["down_bias"]), H, I, E, K,
+                                    0, dev(x), dev(want_idx[0].astype(np.int32)), dev(want_w[0]), out)
+        ctx.sync()
+        assert rel_err(out.cpu().numpy(), want[0]) < REL_TOL
+    assert ctx.error_flags() == 0
+
+
+def test_moe_packed_scale_range_and_residual(ctx, orc):
+    """wide e8m0 scale bytes, a residual stream to add to, and repeated experts in the routing"""
+    spec = synth.TINY_GPT_OSS
+    L = _moe_layer_host(spec, seed=5)
+    rng = np.random.default_rng(11)
+    for k in ("gate", "up", "down"):
+        w = L[k].copy()
+        w[::17] = rng.integers(105, 140, size=w[::17].shape, dtype=np.uint8)   # block scale bytes
+        L[k] = w
+    x = synth.moe_layer_input(spec, seed=5) * 7.0
+    H, I, E, K = spec.hidden, spec.inter, spec.experts, spec.top_k
+    idx = np.array([6, 1, 6, 3], np.int32)[:K]
+    wts = np.array([0.4, 0.3, 0.2, 0.1], np.float32)[:K]
+    h = rng.standard_normal(H).astype(np.float32)
+    d_h = dev(h)
+    gu, dn = _packed(ctx, L, spec)
+    ctx.moe_mxfp4_decode_packed(gu, dn, dev(L["gate_bias"]), dev(L["up_bias"]), dev(L["down_bias"]), H, I, E, K, 0,
+                                dev(x), dev(idx), dev(wts), d_h)
+    # the native-layout path (already pinned against the oracle) is the reference for this routing
+    ref = dev(h)
+    ctx.moe_mxfp4_decode(dev(pad_rows(L["gate"])), dev(pad_rows(L["up"])), dev(pad_rows(L["down"])),
+                         dev(L["gate_bias"]), dev(L["up_bias"]), dev(L["down_bias"]), H, I, E, K, 0,
+                         dev(x), dev(idx), dev(wts), ref)
+    ctx.sync()
+    assert rel_err(d_h.cpu().numpy() - h, ref.cpu().numpy() - h) < 1e-5
+    assert ctx.error_flags() == 0
+
+
 def test_router_dummy_mask_and_ties(ctx):
     H, E, K = 256, 16, 4
     w = np.zeros((E, H), np.float32)
@@ -291,6 +348,16 @@ def tiny_qwen_path(tmp_path_factory):
     p = str(tmp_path_factory.mktemp("tq") / "tiny_qwen3.gguf")
     synth.write_model(p, synth.TINY_QWEN3, seed=7)
     return p
+
+
+def test_tiny_model_native_expert_path(ctx, tiny_path, monkeypatch):
+    """MS_MOE_TC=0 keeps the native-block mma.sync expert kernels; same golden tokens"""
+    from moe_stream_b200.engine import Engine
+    monkeypatch.setenv("MS_MOE_TC", "0")
+    f = np.load(os.path.join(GOLD, "tiny_models.npz"))
+    eng = Engine.open(tiny_path, max_seq_len=256, ctx=ctx)
+    assert eng.generate(f["tiny_gpt_oss_prompt"], 16) == f["tiny_gpt_oss_tokens"].tolist()
+    eng.close()
 
 
 def test_tiny_qwen3_q4k_q6k_model(ctx, orc, tiny_qwen_path):
