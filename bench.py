@@ -303,8 +303,7 @@ def run_ours(args):
     breakdown = None
     if not ep and not args.no_profile:
         us = eng.profile_step()
-        names = ["embed", "qkv_q8", "attention", "o_q8", "router", "moe_ffn", "moe_combine", "resid_norm_q8",
-                 "lm_head"]
+        names = ["embed", "qkv_q8", "attention", "o_q8", "router", "moe_ffn", "resid_norm_q8", "lm_head"]
         breakdown = {names[i] if len(us) == len(names) else f"class{i}": round(v, 1) for i, v in enumerate(us)}
         breakdown["sum_us"] = round(sum(us), 1)
         log(f"[rank {rank}] per-step kernel-class us: {breakdown}")

@@ -36,11 +36,15 @@ cudaError_t launch_rms_norm(const DevCtx& c, const float* x, const float* w, flo
 struct PendingCombine {
   const float* dense = nullptr;    // [H] summed MoE output, or null
   const float* partial = nullptr;  // [K, H] per-slot expert outputs (bias included)
+  // or, from the tensor-core down projection: per-range partial sums [items][kTcMaxSeg][128] of
+  // item = local slot (ascending expert) x tile, split over seg_grid CTAs in K-word units
+  const float* seg_part = nullptr;
+  int seg_tiles = 0, seg_kw = 0, seg_grid = 0;
   const int* idx = nullptr;        // [K] expert ids
   const float* wts = nullptr;      // [K] routing weights
   int K = 0;
   int expert_base = 0, n_local = 0;
-  __host__ __device__ bool active() const { return dense != nullptr || partial != nullptr; }
+  __host__ __device__ bool active() const { return dense != nullptr || partial != nullptr || seg_part != nullptr; }
 };
 
 // y[r] = W[r,:] . x  (+bias[r]) (+residual: y[r] += y_in[r]);  MXFP4 / F16 / F32 weights.
@@ -127,11 +131,13 @@ cudaError_t launch_block_gemv(const DevCtx& c, int qtype, const uint8_t* w, int 
 
 // ---- MXFP4 expert FFN on tcgen05 (repacked tiles; kernels_moe_tc.cu) ----
 constexpr int kTcMaxSeg = 16;   // split-K ranges per item held in the partial-sum scratch
+constexpr int kTcMaxTiles = 64; // down tiles a combine can read (hidden <= 8192)
 int64_t tc_tile_bytes(int kc);            // one packed 128-row tile over kc chunk columns (K = 32 kc)
 int64_t tc_bterm_bytes(int kc);           // one 16-term B operand over kc chunk columns (umma::bterm_bytes)
 int tc_gu_tiles(int I);                   // gate_up tiles per expert (64 gate + 64 up rows each)
 int tc_down_tiles(int H);                 // down tiles per expert (128 rows each, last zero-padded)
-int tc_max_items(int H, int I, int K);    // rows of the split-K scratch
+int tc_max_items(int H, int I, int K);    // items per projection (split-K scratch rows)
+int tc_cnt_words(int H, int I, int K);    // counter words: 2 x items, per-slot ready counts, done
 bool tc_supported(int H, int I);          // H % 64 == 0 && I % 64 == 0
 struct TcMoeArgs {
   const uint8_t* gu = nullptr;      // [E_local][tc_gu_tiles(I)][tc_tile_bytes(H/32)]
@@ -143,8 +149,8 @@ struct TcMoeArgs {
   uint8_t* act_terms = nullptr;     // scratch [K][tc_bterm_bytes(I/32)]
   float* act = nullptr;             // optional [K, I] f32 activations
   float* partial = nullptr;         // [K, H] per-slot expert outputs (bias included)
-  float* part = nullptr;            // split-K scratch [tc_max_items][kTcMaxSeg][128]
-  uint32_t* cnt = nullptr;          // [tc_max_items] zero-initialised, self-resetting
+  float* part = nullptr;            // split-K scratch [2][tc_max_items][kTcMaxSeg][128]
+  uint32_t* cnt = nullptr;          // [tc_cnt_words] zero-initialised, self-resetting
   const int* idx = nullptr;
   const float* wts = nullptr;
   int H = 0, I = 0, K = 0, expert_base = 0, n_local = 0, oai_swiglu = 1;
@@ -153,6 +159,8 @@ struct TcMoeArgs {
   int defer_combine = 0;
 };
 cudaError_t launch_moe_tc(const DevCtx& c, const TcMoeArgs& a, cudaStream_t s);
+// the pending combine of a launch_moe_tc call made with defer_combine (reads its down partials)
+PendingCombine tc_pending_combine(const DevCtx& c, const TcMoeArgs& a);
 // native GGUF MXFP4 [E][rows][cols] -> packed tiles: rows go to tile r / tile_rows_src at tile row
 // row_off + r % tile_rows_src (gate: 64, 0; up: 64, 64; down: 128, 0)
 cudaError_t launch_mxfp4_pack(const uint8_t* src, int E, int rows, int cols, int tile_rows_src, int row_off,
@@ -223,8 +231,9 @@ struct StepState {
 cudaError_t launch_embed(const DevCtx& c, StepState* st, const void* table, int table_q, int H, int vocab,
                          float* h, int* token_log, cudaStream_t s, const float* norm_w = nullptr, float eps = 0.f,
                          int8_t* xq = nullptr, float* xd = nullptr);
-// h += MoE output, then (norm_w set) RMSNorm + Q8_0 quantization of h for the next projection
+// h += MoE output, then (norm_w set) RMSNorm + Q8_0 quantization of h for the next projection;
+// cnt: one zero-initialised, self-resetting counter word
 cudaError_t launch_resid_norm_q8(const DevCtx& c, const PendingCombine& pc, float* h, int H, const float* norm_w,
-                                 float eps, int8_t* xq, float* xd, cudaStream_t s);
+                                 float eps, int8_t* xq, float* xd, uint32_t* cnt, cudaStream_t s);
 
 }  // namespace ms

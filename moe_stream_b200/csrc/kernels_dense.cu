@@ -758,23 +758,45 @@ __global__ void __launch_bounds__(1024) embed_kernel(StepState* st, const void* 
 
 // h += MoE output (slots in ascending expert order, or the expert-parallel sum), then the next
 // layer's attention input: RMSNorm + Q8_0 quantization (when norm_w is set).  One CTA.
-__global__ void __launch_bounds__(1024) resid_norm_q8_kernel(PendingCombine pc, float* h, int H, const float* norm_w,
-                                                             float eps, int8_t* xq, float* xd) {
-  extern __shared__ float hs[];   // [H]
+// h += the pending MoE combine, spread over ceil(H / 256) CTAs of 256 rows each; the last CTA to
+// finish (counter) then normalises the whole h with the next layer's attention norm and writes
+// its Q8_0 blocks.
+constexpr int kResidRows = 256;
+__global__ void __launch_bounds__(kResidRows) resid_norm_q8_kernel(PendingCombine pc, float* h, int H,
+                                                                   const float* norm_w, float eps, int8_t* xq,
+                                                                   float* xd, uint32_t* cnt) {
+  extern __shared__ float hs[];   // [H] (last CTA)
   __shared__ CombineOrder co;
   __shared__ float red[32];
+  __shared__ int s_idx[16];
+  __shared__ float s_wts[16];
+  __shared__ uint32_t last;
   pdl_wait_prior();
   pdl_launch_dependents();   // the next kernel may start its own (weight) prefetch now
-  if (threadIdx.x == 0) combine_order(pc, &co);
-  __syncthreads();
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    const float v = h[i] + combine_at(pc, co, H, i);
-    h[i] = v;
-    hs[i] = v;
+  if (threadIdx.x < pc.K && threadIdx.x < 16 && pc.idx) {   // routing read in parallel, sorted by one thread
+    s_idx[threadIdx.x] = pc.idx[threadIdx.x];
+    s_wts[threadIdx.x] = pc.wts[threadIdx.x];
   }
+  __syncthreads();
+  if (threadIdx.x == 0) combine_order(pc, &co, pc.idx ? s_idx : nullptr, pc.idx ? s_wts : nullptr);
+  __syncthreads();
+  combine_prepare(pc, &co);
+  __syncthreads();
+  const int r = blockIdx.x * kResidRows + threadIdx.x;
+  if (r < H) h[r] = h[r] + combine_at(pc, co, H, r);
   if (!norm_w) return;
   __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();   // this CTA's rows (ordered before by the barrier), then the count
+    last = (atomicAdd(cnt, 1u) == gridDim.x - 1) ? 1u : 0u;
+    if (last) __threadfence();
+  }
+  __syncthreads();
+  if (!last) return;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) hs[i] = __ldcg(&h[i]);
+  __syncthreads();
   cta_rmsnorm_q8(hs, H, norm_w, eps, xq, xd, red);
+  if (threadIdx.x == 0) *cnt = 0u;
 }
 
 template <class Kern, class... Args>
@@ -907,14 +929,15 @@ cudaError_t launch_embed(const DevCtx& c, StepState* st, const void* table, int 
 }
 
 cudaError_t launch_resid_norm_q8(const DevCtx& c, const PendingCombine& pc, float* h, int H, const float* norm_w,
-                                 float eps, int8_t* xq, float* xd, cudaStream_t s) {
+                                 float eps, int8_t* xq, float* xd, uint32_t* cnt, cudaStream_t s) {
   if (H % 32) return cudaErrorInvalidValue;
   const size_t smem = (size_t)H * sizeof(float);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(resid_norm_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  return launch_pdl(resid_norm_q8_kernel, dim3(1), dim3(1024), smem, s, pc, h, H, norm_w, eps, xq, xd);
+  return launch_pdl(resid_norm_q8_kernel, dim3((unsigned)((H + kResidRows - 1) / kResidRows)), dim3(kResidRows), smem, s,
+                    pc, h, H, norm_w, eps, xq, xd, cnt);
 }
 
 cudaError_t launch_gemv(const DevCtx& c, const GemvArgs& a, cudaStream_t s) {

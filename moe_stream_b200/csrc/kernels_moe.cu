@@ -671,6 +671,8 @@ __global__ void moe_combine_kernel(PendingCombine pc, int H, float* h, float* ou
   pdl_launch_dependents();   // the next kernel may start its own (weight) prefetch now
   if (threadIdx.x == 0) combine_order(pc, &co);
   __syncthreads();
+  combine_prepare(pc, &co);
+  __syncthreads();
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < H; r += gridDim.x * blockDim.x) {
     const float v = combine_at(pc, co, H, r);
     if (out) out[r] = v;

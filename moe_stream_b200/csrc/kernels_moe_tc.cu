@@ -29,19 +29,26 @@
 
 namespace ms {
 
-// Optional timeline (build with -DMS_TRACE): %globaltimer stamps per CTA in g_tc_trace[mode][cta][k]:
-// 0 entry, 1 tensor memory ready, 2 first copy issued, 3 first stage landed (MMA warp),
-// 4 last MMA committed, 5 first accumulator ready (epilogue), 6 epilogue done, 7 last copy issued.
+// Optional timeline (build with -DMS_TRACE): %globaltimer stamps per CTA in g_tc_trace[0][cta][k]:
+// 0 entry, 1 slots known, 2 first gate_up copy issued, 3 down activation ready (producer),
+// 4 last gate_up MMA committed, 5 last down MMA committed, 6 epilogue done, 7 kernel exit.
 #ifdef MS_TRACE
 __device__ unsigned long long g_tc_trace[2][1024][8];
+#define TC_TRACE2(k)                                                                           \
+  do {                                                                                         \
+    unsigned long long t_;                                                                     \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                     \
+    g_tc_trace[1][blockIdx.x & 1023][(k)] = t_;                                                \
+  } while (0)
 #define TC_TRACE(k)                                                                            \
   do {                                                                                         \
     unsigned long long t_;                                                                     \
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                     \
-    g_tc_trace[p.mode][blockIdx.x & 1023][(k)] = t_;                                           \
+    g_tc_trace[0][blockIdx.x & 1023][(k)] = t_;                                           \
   } while (0)
 #else
 #define TC_TRACE(k) ((void)0)
+#define TC_TRACE2(k) ((void)0)
 #endif
 
 namespace {
@@ -53,9 +60,13 @@ constexpr int kStSFA = kKW * 512;            // A scale groups, one per K-word
 constexpr int kStB = kCS * 256;              // B codes: 16 chunks x 16 terms x 16 B
 constexpr int kStSFB = kKW * 512;            // B scale groups, one per K-word
 constexpr int kStageBytes = kStA + kStSFA + kStB + kStSFB;
-constexpr int kStages = 4;
+#ifndef MS_TC_CTAS_PER_SM
+#define MS_TC_CTAS_PER_SM 2
+#endif
+constexpr int kCtasPerSm = MS_TC_CTAS_PER_SM;   // independent copy / MMA / epilogue pipelines per SM
+constexpr int kStages = kCtasPerSm == 1 ? 4 : 2;
 constexpr int kThreads = 192;
-constexpr int kTmemCols = 256;
+constexpr int kTmemCols = kCtasPerSm == 1 ? 256 : 128;
 constexpr int kAccCols = 16;                 // one accumulator: 128 lanes x 16 f32 columns
 constexpr int kSubAcc = 2;                   // consecutive MMAs alternate between 2 accumulators
 constexpr int kAccSet = kSubAcc * kAccCols;  // columns of one (double-buffered) accumulator set
@@ -74,6 +85,7 @@ int64_t tc_tile_bytes(int kc) {
 int64_t tc_bterm_bytes(int kc) { return umma::bterm_bytes(kc); }
 int tc_gu_tiles(int I) { return I / 64; }
 int tc_down_tiles(int H) { return (H + 127) / 128; }
+int tc_cnt_words(int H, int I, int K) { return 2 * tc_max_items(H, I, K) + 16 + 1; }
 int tc_max_items(int H, int I, int K) { return K * (tc_gu_tiles(I) > tc_down_tiles(H) ? tc_gu_tiles(I) : tc_down_tiles(H)); }
 bool tc_supported(int H, int I) { return H % 64 == 0 && I % 64 == 0; }
 
@@ -135,55 +147,57 @@ __device__ __forceinline__ float swiglu_oai_tc(float g, float u) {   // ops/acti
 
 enum { TC_GATEUP = 0, TC_DOWN = 1 };
 
-struct TcParams {
-  int mode;
+// one projection: packed weight tiles times B terms
+struct TcPhase {
   const uint8_t* w;          // packed tiles [E_local][tiles][tile_bytes]
   int64_t tile_bytes;
   int tiles, kc;             // tiles per expert; chunk columns (reduction length / 32)
-  const uint8_t* bterm;      // B terms: x (GATEUP) or act_terms base (DOWN)
-  int64_t bterm_stride;      // per slot (DOWN), 0 (GATEUP)
+  const uint8_t* bterm;      // B terms: x (gate_up) or act_terms base (down)
+  int64_t bterm_stride;      // per slot (down), 0 (gate_up)
+  const float* bias0;        // gate_b (gate_up) / down_b (down)
+  const float* bias1;        // up_b
+  int rows;                  // rows per expert matrix of the output: I (gate_up) / H (down)
+};
+
+struct TcParams {
+  TcPhase ph[2];             // [TC_GATEUP], [TC_DOWN]
   const int* idx;
   int K, expert_base, n_local;
-  const float* bias0;        // gate_b (GATEUP) / down_b (DOWN)
-  const float* bias1;        // up_b
-  int rows;                  // rows per expert matrix of the output: I (GATEUP) / H (DOWN)
-  float* part;               // [max_items][kTcMaxSeg][128] split-K partials
-  uint32_t* cnt;             // [max_items] zero-initialised, self-resetting
+  float* part;               // [2][max_items][kTcMaxSeg][128] split-K partials
+  uint32_t* cnt;             // [2][max_items] item counters, then act_ready[kMaxK], then done: zeroed, self-resetting
   int max_items;
-  float* act;                // GATEUP: [K][I] f32 activations (optional)
-  uint8_t* act_terms;        // GATEUP: [K][tc_bterm_bytes(I/32)]
-  int kc_out;                // GATEUP: I / 32
+  float* act;                // [K][I] f32 activations (optional)
+  uint8_t* act_terms;        // [K][bterm_bytes(I/32)]
   int oai;
-  float* partial;            // DOWN: [K][H] per-slot expert outputs
+  float* partial;            // [K][H] per-slot expert outputs
   uint32_t* err;
 };
 
-// first CTA whose unit range [b*T/G, (b+1)*T/G) contains unit x
-__device__ __forceinline__ int cta_of_unit(int x, int T, int G) {
-  int b = (int)((int64_t)x * G / T);
-  while (b + 1 < G && (int)((int64_t)(b + 1) * T / G) <= x) ++b;
-  while (b > 0 && (int)((int64_t)b * T / G) > x) --b;
-  return b;
-}
-
-// This CTA's stages: its range of (item, K-word) units cut at slab boundaries.
+// This CTA's stages: its range of (item, K-word) units of gate_up, then of down, cut at slab
+// boundaries.
 struct Stage {
-  int item, w0, w1;          // K-words [w0, w1) of item, within one slab
+  int phase, item, w0, w1;   // K-words [w0, w1) of item, within one slab
   bool seg_start, seg_end;   // first / last stage of this CTA's range of the item
 };
 struct StageWalk {
-  int KW, u, u1, item, w, wend;
-  __device__ void init(int u0, int u1_, int kw) { KW = kw; u = u0; u1 = u1_; item = 0; w = wend = 0; }
+  int KW[2], u[2], u1[2], phase, item, w, wend;
+  __device__ void init(const int (&u0_)[2], const int (&u1_)[2], const int (&kw)[2]) {
+    for (int q = 0; q < 2; ++q) { KW[q] = kw[q]; u[q] = u0_[q]; u1[q] = u1_[q]; }
+    phase = 0; item = 0; w = wend = 0;
+  }
   __device__ bool next(Stage& st) {
     st.seg_start = false;
     if (w >= wend) {
-      if (u >= u1) return false;
-      item = u / KW;
-      w = u - item * KW;
-      wend = min(KW, u1 - item * KW);
-      u = item * KW + wend;
+      while (phase < 2 && u[phase] >= u1[phase]) ++phase;
+      if (phase >= 2) return false;
+      const int kw = KW[phase];
+      item = u[phase] / kw;
+      w = u[phase] - item * kw;
+      wend = min(kw, u1[phase] - item * kw);
+      u[phase] = item * kw + wend;
       st.seg_start = true;
     }
+    st.phase = phase;
     st.item = item;
     st.w0 = w;
     st.w1 = min(wend, (w / kKW + 1) * kKW);
@@ -193,16 +207,30 @@ struct StageWalk {
   }
 };
 
-__global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(TcParams p) {
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// gate_up and down in one persistent launch.  A CTA runs its gate_up range, then its down
+// range; the down producer issues each stage's weight copies at once and its activation-term
+// copies only after every gate_up tile of that slot is finished (per-slot counter), so down's
+// weight streaming overlaps gate_up's tail.  All CTAs are resident together (one per SM), and
+// gate_up work waits on nothing but its own copies, so the counters always complete.
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) moe_tc_kernel(TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int s_slot[kMaxKSlots], s_exp[kMaxKSlots], s_n, s_last, s_abort;
+  __shared__ float s_rows[128];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t* act_ready = p.cnt + 2 * p.max_items;       // [kMaxKSlots]
+  uint32_t* done = act_ready + kMaxKSlots;
 
-  if (threadIdx.x == 0) TC_TRACE(0);
   // barriers and tensor memory do not depend on the previous kernel: set them up before its wait
   if (threadIdx.x == 0) {
+    TC_TRACE(0);
     for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int a = 0; a < 2; ++a) { mbar_init(&acc_full[a], 1); mbar_init(&acc_empty[a], 128); }
     fence_mbar_init();
@@ -232,13 +260,17 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(TcParams p) {
   umma::fence_after_sync();
   const uint32_t tb = tmem_base;
   if (threadIdx.x == 0) TC_TRACE(1);
-  const int KW = (p.kc + 3) / 4;                            // K-words per item (the last may hold 2 chunks)
-  const int T = s_n * p.tiles * KW;
-  int G = (int)gridDim.x;
-  if (G > (T + 1) / 2) G = (T + 1) / 2;                      // at least ~2 K-words per CTA
-  const bool active = T > 0 && (int)blockIdx.x < G;
-  const int u0 = active ? (int)((int64_t)blockIdx.x * T / G) : 0;
-  const int u1 = active ? (int)((int64_t)(blockIdx.x + 1) * T / G) : 0;
+  int KW[2], T[2], G[2], u0[2], u1[2];
+  for (int q = 0; q < 2; ++q) {
+    KW[q] = (p.ph[q].kc + 3) / 4;                            // K-words per item (the last may hold 2 chunks)
+    T[q] = s_n * p.ph[q].tiles * KW[q];
+    G[q] = tc_split_grid(T[q], (int)gridDim.x);              // at least ~2 K-words per CTA
+    // gate_up: whole items, one per CTA, when they fit (no split-K merge before the activation)
+    if (q == TC_GATEUP && s_n * p.ph[q].tiles <= (int)gridDim.x) G[q] = s_n * p.ph[q].tiles;
+    const bool on = T[q] > 0 && (int)blockIdx.x < G[q];
+    u0[q] = on ? (int)((int64_t)blockIdx.x * T[q] / G[q]) : 0;
+    u1[q] = on ? (int)((int64_t)(blockIdx.x + 1) * T[q] / G[q]) : 0;
+  }
 
   if (warp == 0) {
     // ---------------- producer ----------------
@@ -247,13 +279,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(TcParams p) {
       StageWalk it;
       it.init(u0, u1, KW);
       Stage st;
-      int j = 0;
+      int j = 0, ready_slot = -1;
       while (!*reinterpret_cast<volatile int*>(&s_abort) && it.next(st)) {
-        const int ls = st.item / p.tiles, t = st.item % p.tiles;
-        const uint8_t* tile = p.w + ((int64_t)s_exp[ls] * p.tiles + t) * p.tile_bytes;
-        const uint8_t* bt = p.bterm + (int64_t)s_slot[ls] * p.bterm_stride;
-        const int slab = st.w0 / kKW, c0 = 4 * st.w0, c1 = min(p.kc, 4 * st.w1), sl0 = slab * kCS;
-        const int nch = min(kCS, p.kc - sl0);
+        const TcPhase& ph = p.ph[st.phase];
+        const int ls = st.item / ph.tiles, t = st.item % ph.tiles;
+        const uint8_t* tile = ph.w + ((int64_t)s_exp[ls] * ph.tiles + t) * ph.tile_bytes;
+        const uint8_t* bt = ph.bterm + (int64_t)s_slot[ls] * ph.bterm_stride;
+        const int slab = st.w0 / kKW, c0 = 4 * st.w0, c1 = min(ph.kc, 4 * st.w1), sl0 = slab * kCS;
+        const int nch = min(kCS, ph.kc - sl0);
         const int s = j % kStages, n = j / kStages;
         if (n > 0 && !mbar_wait(&empty[s], (uint32_t)((n - 1) & 1), p.err, EF_TIMEOUT_EMPTY)) { s_abort = 1; break; }
         uint8_t* sp = smem + (size_t)s * kStageBytes;
@@ -263,12 +296,21 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(TcParams p) {
         const uint8_t* sb = tile + slab_off(slab);
         bulk_g2s_stream(sp, sb + (int64_t)(c0 - sl0) * 2048, ab, &full[s], pol);
         bulk_g2s_stream(sp + kStA, sb + (int64_t)nch * 2048 + (st.w0 - slab * kKW) * 512, gb, &full[s], pol);
+        if (st.phase == TC_DOWN && ready_slot != s_slot[ls]) {
+          // this slot's activation terms are complete once all its gate_up tiles are finished
+          const uint32_t target = (uint32_t)p.ph[TC_GATEUP].tiles;
+          uint32_t it2 = 0;
+          while (ld_acquire_u32(&act_ready[s_slot[ls]]) < target && ++it2 < kWaitLimit) __nanosleep(32);
+          if (it2 >= kWaitLimit) { atomicOr(p.err, EF_TIMEOUT_FULL); s_abort = 1; }
+          asm volatile("fence.proxy.async.global;" ::: "memory");   // generic-proxy writes -> bulk-copy reads
+          ready_slot = s_slot[ls];
+          TC_TRACE(3);
+        }
         bulk_g2s(sp + kStA + kStSFA, bt + (int64_t)c0 * 256, bb, &full[s]);
-        bulk_g2s(sp + kStA + kStSFA + kStB, bt + (int64_t)p.kc * 256 + (int64_t)st.w0 * 512, gb, &full[s]);
+        bulk_g2s(sp + kStA + kStSFA + kStB, bt + (int64_t)ph.kc * 256 + (int64_t)st.w0 * 512, gb, &full[s]);
         if (j == 0) TC_TRACE(2);
         ++j;
       }
-      TC_TRACE(7);
       // no copy may still be landing in shared memory when the CTA exits
       for (int q = max(0, j - kStages); q < j; ++q)
         mbar_wait(&full[q % kStages], (uint32_t)((q / kStages) & 1), p.err, EF_TIMEOUT_FULL);
@@ -281,6 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(TcParams p) {
       Stage st;
       int j = 0, seg = 0, nmma = 0;
       while (!*reinterpret_cast<volatile int*>(&s_abort) && it.next(st)) {
+        const int kc = p.ph[st.phase].kc;
         const int a = seg & 1;
         if (st.seg_start) {
           if (seg >= 2 && !mbar_wait(&acc_empty[a], (uint32_t)(((seg >> 1) - 1) & 1), p.err, EF_TIMEOUT_EMPTY)) {
@@ -291,7 +334,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(TcParams p) {
         }
         const int s = j % kStages;
         if (!mbar_wait(&full[s], (uint32_t)((j / kStages) & 1), p.err, EF_TIMEOUT_FULL)) { s_abort = 1; break; }
-        if (j == 0) TC_TRACE(3);
         umma::fence_after_sync();
         const uint8_t* sp = smem + (size_t)s * kStageBytes;
         const uint32_t sfa_col = tb + (uint32_t)(2 * kAccSet + s * kSlotCols), sfb_col = sfa_col + 4 * kKW;
@@ -301,22 +343,22 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(TcParams p) {
           umma::cp_sf_group(sfb_col + 4 * g, sp + kStA + kStSFA + kStB + g * 512);
         }
         const uint32_t d_tmem = tb + (uint32_t)(a * kAccSet);
-        const int c0 = 4 * st.w0, c1 = min(p.kc, 4 * st.w1);
+        const int c0 = 4 * st.w0, c1 = min(kc, 4 * st.w1);
         for (int cc = c0; cc < c1; cc += 2) {
           const uint64_t ad = umma::smem_desc(sp + (cc - c0) * 2048, 2048, 128);
           const uint64_t bd = umma::smem_desc(sp + kStA + kStSFA + (cc - c0) * 256, 256, 128);
           const int wl = (cc >> 2) - st.w0;            // K-word within the stage
           const uint32_t byte = (uint32_t)(cc & 3);    // the pair of blocks within the K-word
           umma::mma_mxf4(d_tmem + (uint32_t)((nmma % kSubAcc) * kAccCols), ad, bd,
-                         umma::idesc_mxf4(128, 16, byte, byte), sfa_col + 4 * wl,
-                         sfb_col + 4 * wl, nmma >= kSubAcc);
+                         umma::idesc_mxf4(128, 16, byte, byte), sfa_col + 4 * wl, sfb_col + 4 * wl,
+                         nmma >= kSubAcc);
           ++nmma;
         }
         umma::commit(&empty[s]);   // the stage may be refilled once these MMAs have read it
         ++j;
         if (st.seg_end) {
           umma::commit(&acc_full[a]);
-          TC_TRACE(4);
+          TC_TRACE(4 + st.phase);
           ++seg;
         }
       }
@@ -330,13 +372,29 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(TcParams p) {
     Stage st;
     int seg = 0, nmma = 0;
     while (it.next(st)) {
+      const TcPhase& ph = p.ph[st.phase];
       if (st.seg_start) nmma = 0;
-      nmma += (min(p.kc, 4 * st.w1) - 4 * st.w0 + 1) / 2;
+      nmma += (min(ph.kc, 4 * st.w1) - 4 * st.w0 + 1) / 2;
       if (!st.seg_end) continue;
-      const int item = st.item;
+      const int item = st.item, q0 = st.phase;
+      const int ls = item / ph.tiles, t = item % ph.tiles;
+      const int e = s_exp[ls], slot = s_slot[ls];
+      const int first = tc_cta_of_unit(item * KW[q0], T[q0], G[q0]);
+      const int nseg = tc_cta_of_unit(item * KW[q0] + KW[q0] - 1, T[q0], G[q0]) - first + 1;
+      const int segi = (int)blockIdx.x - first;
+      // biases are read before the accumulator wait (they are off the critical path there)
+      float b0 = 0.f, b1 = 0.f;
+      if (q0 == TC_GATEUP) {
+        if (et < 64) {
+          if (ph.bias0) b0 = ph.bias0[(int64_t)e * ph.rows + t * 64 + et];
+          if (ph.bias1) b1 = ph.bias1[(int64_t)e * ph.rows + t * 64 + et];
+        }
+      } else if (segi == 0 && ph.bias0 && t * 128 + row < ph.rows) {
+        b0 = ph.bias0[(int64_t)e * ph.rows + t * 128 + row];
+      }
       const int a = seg & 1;
       const bool ok = mbar_wait(&acc_full[a], (uint32_t)((seg >> 1) & 1), p.err, EF_TIMEOUT_FULL);
-      if (seg == 0 && et == 0) TC_TRACE(5);
+      if (et == 0 && q0 == TC_GATEUP) TC_TRACE2(0);
       umma::fence_after_sync();
       float sum = 0.f;
       const int nsub = min(kSubAcc, nmma);
@@ -349,45 +407,58 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(TcParams p) {
       umma::fence_before_sync();
       mbar_arrive(&acc_empty[a]);
       if (!ok) break;
-      const int first = cta_of_unit(item * KW, T, G);
-      const int nseg = cta_of_unit(item * KW + KW - 1, T, G) - first + 1;
-      const int segi = (int)blockIdx.x - first;
-      p.part[((int64_t)item * kTcMaxSeg + segi) * 128 + row] = sum;
-      named_bar(1, 128);
-      if (et == 0) {
-        // release this CTA's partials (ordered before by the barrier) and count the range in
-        __threadfence();
-        s_last = (atomicAdd(&p.cnt[item], 1u) == (uint32_t)nseg - 1) ? 1 : 0;
-        if (s_last) __threadfence();
+      if (q0 == TC_DOWN) {
+        // per-range partial sums; the consumer of the MoE output adds the ranges in K order
+        p.part[(((int64_t)p.max_items + item) * kTcMaxSeg + segi) * 128 + row] = sum + b0;
+        ++seg;
+        continue;
       }
-      named_bar(1, 128);
-      if (s_last) {
-        const int ls = item / p.tiles, t = item % p.tiles;
-        const int e = s_exp[ls], slot = s_slot[ls];
-        const float* pp = p.part + (int64_t)item * kTcMaxSeg * 128;
-        if (p.mode == TC_GATEUP) {
-          if (et < 64) {
-            float g = 0.f, up = 0.f;
-            for (int q = 0; q < nseg; ++q) { g += __ldcg(pp + q * 128 + et); up += __ldcg(pp + q * 128 + 64 + et); }
-            const int r = t * 64 + et;
-            if (p.bias0) g += p.bias0[(int64_t)e * p.rows + r];
-            if (p.bias1) up += p.bias1[(int64_t)e * p.rows + r];
-            const float av = p.oai ? swiglu_oai_tc(g, up) : (g / (1.0f + expf(-g))) * up;
-            // this tile's 64 activations are chunk columns 2t, 2t+1 of the down projection's B terms
-            umma::quantize_terms_warp(av, lane, p.act_terms + (int64_t)slot * umma::bterm_bytes(p.kc_out), p.kc_out,
-                                      2 * t + (et >> 5));
-            if (p.act) p.act[(int64_t)slot * p.rows + r] = av;
-          }
-        } else {
-          const int r = t * 128 + et;
-          if (r < p.rows) {
-            float y = 0.f;
-            for (int q = 0; q < nseg; ++q) y += __ldcg(pp + q * 128 + et);
-            if (p.bias0) y += p.bias0[(int64_t)e * p.rows + r];
-            p.partial[(int64_t)slot * p.rows + r] = y;
+      // ---- gate_up: the item's 64 gate rows (TMEM rows 0-63) and up rows (64-127) ----
+      bool finish = nseg == 1;
+      const float* pp = s_rows;
+      if (nseg == 1) {
+        s_rows[row] = sum;
+        named_bar(1, 128);
+      } else {   // split item: the last range to finish adds the ranges in order
+        const int64_t gitem = item;
+        p.part[(gitem * kTcMaxSeg + segi) * 128 + row] = sum;
+        named_bar(1, 128);
+        if (et == 0) {
+          __threadfence();   // this CTA's partials (ordered before by the barrier), then the count
+          s_last = (atomicAdd(&p.cnt[gitem], 1u) == (uint32_t)nseg - 1) ? 1 : 0;
+          if (s_last) {
+            __threadfence();
+            p.cnt[gitem] = 0u;
           }
         }
-        if (et == 0) p.cnt[item] = 0u;
+        named_bar(1, 128);
+        finish = s_last != 0;
+        pp = p.part + gitem * kTcMaxSeg * 128;
+      }
+      if (et == 0) TC_TRACE2(2);
+      if (finish) {
+        const int kc_out = p.ph[TC_DOWN].kc;
+        if (et < 64) {
+          float g = 0.f, up = 0.f;
+          if (nseg == 1) { g = pp[et]; up = pp[64 + et]; }
+          else for (int q = 0; q < nseg; ++q) { g += __ldcg(pp + q * 128 + et); up += __ldcg(pp + q * 128 + 64 + et); }
+          g += b0;
+          up += b1;
+          const float av = p.oai ? swiglu_oai_tc(g, up) : (g / (1.0f + expf(-g))) * up;
+          // this tile's 64 activations are chunk columns 2t, 2t+1 of the down projection's B terms
+          umma::quantize_terms_warp(av, lane, p.act_terms + (int64_t)slot * umma::bterm_bytes(kc_out), kc_out,
+                                    2 * t + (et >> 5));
+          if (p.act) p.act[(int64_t)slot * ph.rows + t * 64 + et] = av;
+        }
+        if (et == 0) TC_TRACE2(3);
+        named_bar(1, 128);
+        if (et == 0) {
+          __threadfence();   // the tile's activation terms, then the slot's ready count
+          atomicAdd(&act_ready[slot], 1u);
+          TC_TRACE2(5);
+        }
+      } else if (nseg == 1) {
+        named_bar(1, 128);
       }
       ++seg;
     }
@@ -396,14 +467,25 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(TcParams p) {
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 1) umma::tmem_dealloc(tb, kTmemCols);
+  if (threadIdx.x == 0) TC_TRACE(7);
+  if (threadIdx.x == 0) {
+    // the last CTA out clears the per-slot ready counts for the next call (every CTA has read
+    // them by now: its producer finished)
+    __threadfence();
+    if (atomicAdd(done, 1u) == gridDim.x - 1) {
+      for (int k = 0; k < kMaxKSlots; ++k) act_ready[k] = 0u;
+      __threadfence();
+      *done = 0u;
+    }
+  }
 }
 
-cudaError_t launch_tc_phase(const DevCtx& c, const TcParams& p, cudaStream_t s) {
+cudaError_t launch_tc(const DevCtx& c, const TcParams& p, cudaStream_t s) {
   const size_t smem = (size_t)kStages * kStageBytes;
   cudaError_t e = cudaFuncSetAttribute(moe_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)c.sm_count);
+  cfg.gridDim = dim3((unsigned)(kCtasPerSm * c.sm_count));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -442,27 +524,33 @@ cudaError_t launch_xterms(const DevCtx& c, const float* x, int H, uint8_t* xterm
   return cudaLaunchKernelEx(&cfg, xterms_kernel, x, H, xterm);
 }
 
+PendingCombine tc_pending_combine(const DevCtx& c, const TcMoeArgs& a) {
+  PendingCombine pc;
+  pc.seg_part = a.part + (size_t)tc_max_items(a.H, a.I, a.K) * kTcMaxSeg * 128;
+  pc.seg_tiles = tc_down_tiles(a.H);
+  pc.seg_kw = (a.I / 32 + 3) / 4;
+  pc.seg_grid = kCtasPerSm * c.sm_count;
+  pc.idx = a.idx; pc.wts = a.wts; pc.K = a.K; pc.expert_base = a.expert_base; pc.n_local = a.n_local;
+  return pc;
+}
+
 cudaError_t launch_moe_tc(const DevCtx& c, const TcMoeArgs& a, cudaStream_t s) {
   if (a.K < 1 || a.K > kMaxKSlots || !tc_supported(a.H, a.I) || a.n_local < 0) return cudaErrorInvalidValue;
   TcParams p = {};
   p.idx = a.idx; p.K = a.K; p.expert_base = a.expert_base; p.n_local = a.n_local; p.err = c.err;
   p.part = a.part; p.cnt = a.cnt; p.max_items = tc_max_items(a.H, a.I, a.K);
-  // phase 1: gate + up (+ bias, activation, activation terms)
-  p.mode = TC_GATEUP; p.w = a.gu; p.kc = a.H / 32; p.tile_bytes = tc_tile_bytes(p.kc); p.tiles = tc_gu_tiles(a.I);
-  p.bterm = a.xterm; p.bterm_stride = 0; p.bias0 = a.gate_b; p.bias1 = a.up_b; p.rows = a.I; p.act = a.act;
-  p.act_terms = a.act_terms; p.kc_out = a.I / 32; p.oai = a.oai_swiglu;
-  cudaError_t e = launch_tc_phase(c, p, s);
-  if (e != cudaSuccess) return e;
-  // phase 2: down -> per-slot expert outputs
-  p.mode = TC_DOWN; p.w = a.down; p.kc = a.I / 32; p.tile_bytes = tc_tile_bytes(p.kc); p.tiles = tc_down_tiles(a.H);
-  p.bterm = a.act_terms; p.bterm_stride = tc_bterm_bytes(a.I / 32); p.bias0 = a.down_b; p.bias1 = nullptr;
-  p.rows = a.H; p.act = nullptr; p.act_terms = nullptr; p.partial = a.partial;
-  e = launch_tc_phase(c, p, s);
+  p.act = a.act; p.act_terms = a.act_terms; p.oai = a.oai_swiglu; p.partial = a.partial;
+  TcPhase& g = p.ph[TC_GATEUP];   // gate + up (+ bias, activation, activation terms)
+  g.w = a.gu; g.kc = a.H / 32; g.tile_bytes = tc_tile_bytes(g.kc); g.tiles = tc_gu_tiles(a.I);
+  g.bterm = a.xterm; g.bterm_stride = 0; g.bias0 = a.gate_b; g.bias1 = a.up_b; g.rows = a.I;
+  TcPhase& d = p.ph[TC_DOWN];     // down -> per-slot expert outputs
+  d.w = a.down; d.kc = a.I / 32; d.tile_bytes = tc_tile_bytes(d.kc); d.tiles = tc_down_tiles(a.H);
+  d.bterm = a.act_terms; d.bterm_stride = tc_bterm_bytes(a.I / 32); d.bias0 = a.down_b; d.bias1 = nullptr;
+  d.rows = a.H;
+  if (tc_down_tiles(a.H) > kTcMaxTiles) return cudaErrorInvalidValue;
+  cudaError_t e = launch_tc(c, p, s);
   if (e != cudaSuccess || a.defer_combine) return e;
-  PendingCombine pc;
-  pc.partial = a.partial; pc.idx = a.idx; pc.wts = a.wts; pc.K = a.K; pc.expert_base = a.expert_base;
-  pc.n_local = a.n_local;
-  return launch_moe_combine(c, pc, a.H, a.h, a.out, s);
+  return launch_moe_combine(c, tc_pending_combine(c, a), a.H, a.h, a.out, s);
 }
 
 }  // namespace ms

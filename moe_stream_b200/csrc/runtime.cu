@@ -193,7 +193,7 @@ struct ms_model {
   // per-step scratch
   float *h = nullptr, *qkv = nullptr, *attn_out = nullptr, *xn = nullptr, *router_logits = nullptr;
   float *act = nullptr, *partial = nullptr, *logits = nullptr, *attn_part = nullptr, *h_last = nullptr;
-  uint32_t *router_cnt = nullptr, *tile_cnt = nullptr, *attn_cnt = nullptr;
+  uint32_t *router_cnt = nullptr, *tile_cnt = nullptr, *attn_cnt = nullptr, *resid_cnt = nullptr;
   StepState* st = nullptr;
   int* token_log = nullptr;
   int expert_base = 0, n_local = 0;
@@ -459,9 +459,13 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
       // expert parallel: combine the local experts into moe_out, sum it over the EP group
       ma.defer_combine = 0; ma.out = m->moe_out;
       ta.defer_combine = 0; ta.out = m->moe_out;
-      if (Lw.tc) LAUNCH(launch_moe_tc(dc, ta, s));
-      else LAUNCH(launch_moe_mxfp4(dc, ma, s));
-      nk += 2;   // gate/up, down, combine
+      if (Lw.tc) {
+        LAUNCH(launch_moe_tc(dc, ta, s));
+        nk += 1;   // gate_up + down (one kernel), combine
+      } else {
+        LAUNCH(launch_moe_mxfp4(dc, ma, s));
+        nk += 2;   // gate/up, down, combine
+      }
       NcclApi* api = nccl_api();
       ncclResult_t r = api->all_reduce(m->moe_out, m->moe_out, (size_t)H, ncclFloat32, ncclSum, m->comm, s);
       if (r != ncclSuccess) return fail(m->ctx, MS_ERR_NCCL, "ncclAllReduce: %s", api->error_string(r));
@@ -469,15 +473,19 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     } else {
       ma.defer_combine = 1;   // per-slot outputs stay in `partial`; the next kernel combines them
       ta.defer_combine = 1;
-      if (Lw.tc) LAUNCH(launch_moe_tc(dc, ta, s));
-      else LAUNCH(launch_moe_mxfp4(dc, ma, s));
-      ++nk;   // gate/up, down
-      pc.partial = m->partial; pc.idx = Lw.idx; pc.wts = Lw.wts; pc.K = c.top_k;
-      pc.expert_base = m->expert_base; pc.n_local = m->n_local;
+      if (Lw.tc) {
+        LAUNCH(launch_moe_tc(dc, ta, s));   // gate_up + down in one kernel
+        pc = tc_pending_combine(dc, ta);
+      } else {
+        LAUNCH(launch_moe_mxfp4(dc, ma, s));
+        ++nk;   // gate/up, down
+        pc.partial = m->partial; pc.idx = Lw.idx; pc.wts = Lw.wts; pc.K = c.top_k;
+        pc.expert_base = m->expert_base; pc.n_local = m->n_local;
+      }
     }
     // h += MoE (ascending expert order); quantize the next layer's attention input
     const float* next_norm = li + 1 < c.layers ? m->L[li + 1].attn_norm : nullptr;
-    LAUNCH(launch_resid_norm_q8(dc, pc, m->h, H, next_norm, c.eps, m->xq_h, m->xd_h, s));
+    LAUNCH(launch_resid_norm_q8(dc, pc, m->h, H, next_norm, c.eps, m->xq_h, m->xd_h, m->resid_cnt, s));
   }
   LmHeadArgs la;
   la.w = m->out_w; la.x = m->h; la.norm_w = m->out_norm; la.eps = c.eps; la.bias = m->out_b; la.logits = m->logits;
@@ -755,8 +763,8 @@ ms_status ms_moe_mxfp4_decode_packed(ms_ctx* c, const void* gu, const void* down
   const size_t xt_b = up((size_t)tc_bterm_bytes(H / 32)), at_b = up((size_t)K * tc_bterm_bytes(I / 32));
   const size_t act_b = up((size_t)K * I * 4), part_b = up((size_t)K * H * 4);
   const int items = tc_max_items(H, I, K);
-  const size_t sp_b = up((size_t)items * kTcMaxSeg * 128 * 4);
-  ms_status s = ensure_scratch(c, xt_b + at_b + act_b + part_b + sp_b, 64 + 1024 + (size_t)items);
+  const size_t sp_b = up((size_t)2 * items * kTcMaxSeg * 128 * 4);
+  ms_status s = ensure_scratch(c, xt_b + at_b + act_b + part_b + sp_b, 64 + 1024 + (size_t)tc_cnt_words(H, I, K));
   if (s != MS_OK) return s;
   uint8_t* base = (uint8_t*)c->scratch;
   TcMoeArgs a;
@@ -881,6 +889,7 @@ ms_status ms_model_finalize(ms_model* m) {
   s = s ? s : m->alloc(&m->logits, (size_t)c.vocab * 4);
   s = s ? s : m->alloc(&m->attn_part, (size_t)c.kv_heads * S * rep * (c.head_dim + 2) * 4);
   s = s ? s : m->alloc(&m->router_cnt, 16);
+  s = s ? s : m->alloc(&m->resid_cnt, 16);
   s = s ? s : m->alloc(&m->tile_cnt, (size_t)(H / 16 + 16) * 4);
   s = s ? s : m->alloc(&m->attn_cnt, (size_t)(c.kv_heads + 16) * 4);
   s = s ? s : m->alloc(&m->st, sizeof(StepState));
@@ -888,8 +897,8 @@ ms_status ms_model_finalize(ms_model* m) {
   if (any_tc) {
     s = s ? s : m->alloc(&m->xterm, (size_t)tc_bterm_bytes(H / 32));
     s = s ? s : m->alloc(&m->act_terms, (size_t)c.top_k * tc_bterm_bytes(c.inter / 32));
-    s = s ? s : m->alloc(&m->tc_part, (size_t)tc_max_items(H, c.inter, c.top_k) * kTcMaxSeg * 128 * 4);
-    s = s ? s : m->alloc(&m->tc_cnt, (size_t)tc_max_items(H, c.inter, c.top_k) * 4);
+    s = s ? s : m->alloc(&m->tc_part, (size_t)2 * tc_max_items(H, c.inter, c.top_k) * kTcMaxSeg * 128 * 4);
+    s = s ? s : m->alloc(&m->tc_cnt, (size_t)tc_cnt_words(H, c.inter, c.top_k) * 4);
   }
   if (s != MS_OK) return s;
   std::vector<float> cs, sn;
