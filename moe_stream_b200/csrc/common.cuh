@@ -145,17 +145,16 @@ struct CombineOrder {
   int n;
   int slot[16];
   float w[16];
-  unsigned char nseg[16][kTcMaxTiles];   // split-K ranges of each (slot, tile) item (seg_part only)
 };
 
-// first CTA whose unit range [b*T/G, (b+1)*T/G) contains unit x (the tensor-core MoE split)
-__host__ __device__ __forceinline__ int tc_cta_of_unit(int x, int T, int G) {
-  int b = (int)((int64_t)x * G / T);
-  while (b + 1 < G && (int)((int64_t)(b + 1) * T / G) <= x) ++b;
-  while (b > 0 && (int)((int64_t)b * T / G) > x) --b;
-  return b;
+// The tensor-core MoE split: items (slot x tile) are cut into S equal K ranges (units), S the
+// largest count that still gives every CTA at most one unit, capped by the K-words per item.
+__host__ __device__ __forceinline__ int tc_splits(int n_items, int kw, int grid) {
+  int S = n_items > 0 ? grid / n_items : 1;
+  S = S < 1 ? 1 : S;
+  S = S > kw ? kw : S;
+  return S > kTcMaxSeg ? kTcMaxSeg : S;
 }
-__host__ __device__ __forceinline__ int tc_split_grid(int T, int grid) { return grid < (T + 1) / 2 ? grid : (T + 1) / 2; }
 
 // single thread: local slots ordered by ascending expert id.  ids / wts: the routing, either
 // pc.idx / pc.wts or a shared-memory copy of them.
@@ -180,47 +179,33 @@ __device__ __forceinline__ void combine_order(const PendingCombine& pc, CombineO
   co->n = n;
 }
 
-// all threads of the block, after combine_order and a barrier: range counts of every item
-__device__ __forceinline__ void combine_prepare(const PendingCombine& pc, CombineOrder* co) {
-  if (!pc.seg_part) return;
-  const int T = co->n * pc.seg_tiles * pc.seg_kw, G = tc_split_grid(T, pc.seg_grid);
-  for (int i = threadIdx.x; i < co->n * pc.seg_tiles; i += blockDim.x) {
-    const int first = tc_cta_of_unit(i * pc.seg_kw, T, G);
-    co->nseg[i / pc.seg_tiles][i % pc.seg_tiles] =
-        (unsigned char)(tc_cta_of_unit(i * pc.seg_kw + pc.seg_kw - 1, T, G) - first + 1);
-  }
-}
+// all threads of the block, after combine_order and a barrier (nothing to prepare any more)
+__device__ __forceinline__ void combine_prepare(const PendingCombine&, CombineOrder*) {}
 
 // moe_out[r], accumulated from zero in ascending expert order as the reference does
 __device__ __forceinline__ float combine_at(const PendingCombine& pc, const CombineOrder& co, int H, int r) {
   if (pc.dense) return pc.dense[r];
   float acc = 0.f;
   if (pc.seg_part) {
-    const int t = r >> 7;
+    const int t = r >> 7, ns = tc_splits(co.n * pc.seg_tiles, pc.seg_kw, pc.seg_grid);
     const size_t off = (size_t)t * kTcMaxSeg * 128 + (r & 127), qstride = (size_t)pc.seg_tiles * kTcMaxSeg * 128;
-    if (co.n <= 8) {
-      // up to 8 slots x 5 ranges as independent predicated loads, so they are in flight together
-      float y[8][5];
+    if (co.n <= 8 && ns <= 4) {
+      // up to 8 slots x 4 ranges as independent predicated loads, so they are in flight together
+      float y[8][4];
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        const int ns = q < co.n ? co.nseg[q][t] : 0;
         const float* sp = pc.seg_part + q * qstride + off;
 #pragma unroll
-        for (int s2 = 0; s2 < 5; ++s2) y[q][s2] = s2 < ns ? __ldcg(sp + s2 * 128) : 0.f;
+        for (int s2 = 0; s2 < 4; ++s2) y[q][s2] = (q < co.n && s2 < ns) ? __ldcg(sp + s2 * 128) : 0.f;
       }
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        if (q < co.n) {
-          float v = (((y[q][0] + y[q][1]) + y[q][2]) + y[q][3]) + y[q][4];   // ranges in K order
-          for (int s2 = 5; s2 < co.nseg[q][t]; ++s2) v += __ldcg(pc.seg_part + q * qstride + off + s2 * 128);
-          acc += v * co.w[q];
-        }
-      }
+      for (int q = 0; q < 8; ++q)
+        if (q < co.n) acc += ((((y[q][0] + y[q][1]) + y[q][2]) + y[q][3])) * co.w[q];   // ranges in K order
       return acc;
     }
     for (int q = 0; q < co.n; ++q) {
       float v = 0.f;
-      for (int s2 = 0; s2 < co.nseg[q][t]; ++s2) v += __ldcg(pc.seg_part + q * qstride + off + s2 * 128);
+      for (int s2 = 0; s2 < ns; ++s2) v += __ldcg(pc.seg_part + q * qstride + off + s2 * 128);
       acc += v * co.w[q];
     }
     return acc;

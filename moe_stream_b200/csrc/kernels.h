@@ -37,7 +37,7 @@ struct PendingCombine {
   const float* dense = nullptr;    // [H] summed MoE output, or null
   const float* partial = nullptr;  // [K, H] per-slot expert outputs (bias included)
   // or, from the tensor-core down projection: per-range partial sums [items][kTcMaxSeg][128] of
-  // item = local slot (ascending expert) x tile, split over seg_grid CTAs in K-word units
+  // item = local slot (ascending expert) x 128-row tile, tc_splits(items, seg_kw, seg_grid) ranges each
   const float* seg_part = nullptr;
   int seg_tiles = 0, seg_kw = 0, seg_grid = 0;
   const int* idx = nullptr;        // [K] expert ids

@@ -173,32 +173,34 @@ struct TcParams {
   uint32_t* err;
 };
 
-// This CTA's stages: its range of (item, K-word) units of gate_up, then of down, cut at slab
-// boundaries.
+// This CTA's stages: its units of gate_up, then of down -- a unit is one of the S equal K ranges
+// of an item -- each cut at slab boundaries.
 struct Stage {
-  int phase, item, w0, w1;   // K-words [w0, w1) of item, within one slab
-  bool seg_start, seg_end;   // first / last stage of this CTA's range of the item
+  int phase, item, seg, w0, w1;   // K-words [w0, w1) of item, within one slab; seg = the unit's range index
+  bool seg_start, seg_end;        // first / last stage of the unit
 };
 struct StageWalk {
-  int KW[2], u[2], u1[2], phase, item, w, wend;
-  __device__ void init(const int (&u0_)[2], const int (&u1_)[2], const int (&kw)[2]) {
-    for (int q = 0; q < 2; ++q) { KW[q] = kw[q]; u[q] = u0_[q]; u1[q] = u1_[q]; }
-    phase = 0; item = 0; w = wend = 0;
+  int KW[2], S[2], u[2], u1[2], phase, item, seg, w, wend;
+  __device__ void init(const int (&u0_)[2], const int (&u1_)[2], const int (&kw)[2], const int (&sp)[2]) {
+    for (int q = 0; q < 2; ++q) { KW[q] = kw[q]; S[q] = sp[q]; u[q] = u0_[q]; u1[q] = u1_[q]; }
+    phase = 0; item = 0; seg = 0; w = wend = 0;
   }
   __device__ bool next(Stage& st) {
     st.seg_start = false;
     if (w >= wend) {
       while (phase < 2 && u[phase] >= u1[phase]) ++phase;
       if (phase >= 2) return false;
-      const int kw = KW[phase];
-      item = u[phase] / kw;
-      w = u[phase] - item * kw;
-      wend = min(kw, u1[phase] - item * kw);
-      u[phase] = item * kw + wend;
+      const int n = S[phase], kw = KW[phase];
+      item = u[phase] / n;
+      seg = u[phase] - item * n;
+      w = seg * kw / n;
+      wend = (seg + 1) * kw / n;
+      ++u[phase];
       st.seg_start = true;
     }
     st.phase = phase;
     st.item = item;
+    st.seg = seg;
     st.w0 = w;
     st.w1 = min(wend, (w / kKW + 1) * kKW);
     w = st.w1;
@@ -260,16 +262,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) moe_tc_kernel(TcParams p
   umma::fence_after_sync();
   const uint32_t tb = tmem_base;
   if (threadIdx.x == 0) TC_TRACE(1);
-  int KW[2], T[2], G[2], u0[2], u1[2];
+  int KW[2], S[2], u0[2], u1[2];
   for (int q = 0; q < 2; ++q) {
     KW[q] = (p.ph[q].kc + 3) / 4;                            // K-words per item (the last may hold 2 chunks)
-    T[q] = s_n * p.ph[q].tiles * KW[q];
-    G[q] = tc_split_grid(T[q], (int)gridDim.x);              // at least ~2 K-words per CTA
-    // gate_up: whole items, one per CTA, when they fit (no split-K merge before the activation)
-    if (q == TC_GATEUP && s_n * p.ph[q].tiles <= (int)gridDim.x) G[q] = s_n * p.ph[q].tiles;
-    const bool on = T[q] > 0 && (int)blockIdx.x < G[q];
-    u0[q] = on ? (int)((int64_t)blockIdx.x * T[q] / G[q]) : 0;
-    u1[q] = on ? (int)((int64_t)(blockIdx.x + 1) * T[q] / G[q]) : 0;
+    const int n_items = s_n * p.ph[q].tiles;
+    S[q] = tc_splits(n_items, KW[q], (int)gridDim.x);
+    const int U = n_items * S[q], G = min((int)gridDim.x, U);
+    const bool on = U > 0 && (int)blockIdx.x < G;
+    u0[q] = on ? (int)((int64_t)blockIdx.x * U / G) : 0;
+    u1[q] = on ? (int)((int64_t)(blockIdx.x + 1) * U / G) : 0;
   }
 
   if (warp == 0) {
@@ -277,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) moe_tc_kernel(TcParams p
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       StageWalk it;
-      it.init(u0, u1, KW);
+      it.init(u0, u1, KW, S);
       Stage st;
       int j = 0, ready_slot = -1;
       while (!*reinterpret_cast<volatile int*>(&s_abort) && it.next(st)) {
@@ -319,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) moe_tc_kernel(TcParams p
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       StageWalk it;
-      it.init(u0, u1, KW);
+      it.init(u0, u1, KW, S);
       Stage st;
       int j = 0, seg = 0, nmma = 0;
       while (!*reinterpret_cast<volatile int*>(&s_abort) && it.next(st)) {
@@ -368,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) moe_tc_kernel(TcParams p
     const int quad = warp & 3, row = 32 * quad + lane;
     const int et = threadIdx.x - 64;   // 0..127
     StageWalk it;
-    it.init(u0, u1, KW);
+    it.init(u0, u1, KW, S);
     Stage st;
     int seg = 0, nmma = 0;
     while (it.next(st)) {
@@ -379,9 +380,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) moe_tc_kernel(TcParams p
       const int item = st.item, q0 = st.phase;
       const int ls = item / ph.tiles, t = item % ph.tiles;
       const int e = s_exp[ls], slot = s_slot[ls];
-      const int first = tc_cta_of_unit(item * KW[q0], T[q0], G[q0]);
-      const int nseg = tc_cta_of_unit(item * KW[q0] + KW[q0] - 1, T[q0], G[q0]) - first + 1;
-      const int segi = (int)blockIdx.x - first;
+      const int nseg = S[q0], segi = st.seg;
       // biases are read before the accumulator wait (they are off the critical path there)
       float b0 = 0.f, b1 = 0.f;
       if (q0 == TC_GATEUP) {
@@ -528,8 +527,9 @@ PendingCombine tc_pending_combine(const DevCtx& c, const TcMoeArgs& a) {
   PendingCombine pc;
   pc.seg_part = a.part + (size_t)tc_max_items(a.H, a.I, a.K) * kTcMaxSeg * 128;
   pc.seg_tiles = tc_down_tiles(a.H);
-  pc.seg_kw = (a.I / 32 + 3) / 4;
+  pc.seg_kw = (a.I / 32 + 3) / 4;                  // the kernel's split, recomputed from the routed slot count
   pc.seg_grid = kCtasPerSm * c.sm_count;
+
   pc.idx = a.idx; pc.wts = a.wts; pc.K = a.K; pc.expert_base = a.expert_base; pc.n_local = a.n_local;
   return pc;
 }
