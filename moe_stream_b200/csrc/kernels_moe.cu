@@ -541,35 +541,54 @@ __device__ __forceinline__ float router_block_sum(float v, float* red) {
   return t;
 }
 
-__global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, uint32_t* err) {
+// One CTA per expert row.  Before waiting for the previous kernel the CTA starts a bulk copy of
+// its router row into shared memory; then it normalises h (RMSNorm, h read twice, the second
+// time from L1), dots its row and writes one logit; CTAs 0.. also write the normed x as the
+// expert GEMVs' activation terms.  The last CTA to finish selects the top-k with one warp.
+__global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, uint32_t* err, int row_async) {
+  extern __shared__ __align__(16) float wrow[];   // [H] this expert's router row
   __shared__ float red[kRouterThreads / 32];
+  __shared__ __align__(8) uint64_t bar;
   __shared__ uint32_t last;
-  __shared__ float lg[kRouterMaxE];
-  __shared__ float sel_v[kMaxK];
-  __shared__ int sel_i[kMaxK];
-  __shared__ float bv[kRouterThreads / 32];
-  __shared__ int bi[kRouterThreads / 32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x;
+  const float* wr = a.w + (size_t)e * a.H;
+  if (row_async && threadIdx.x == 0) {   // weights do not depend on the previous kernel
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_expect_tx(&bar, (uint32_t)a.H * 4u);
+    bulk_g2s(wrow, wr, (uint32_t)a.H * 4u, &bar);
+  }
   pdl_wait_prior();
   pdl_launch_dependents();   // the next kernel may start its own (weight) prefetch now
-  const float* wr = a.w + (size_t)e * a.H;
   float dot = 0.f;
   float inv = 1.f;
   if (a.h) {
     float ss = 0.f;
     for (int i = threadIdx.x; i < a.H; i += kRouterThreads) { const float v = a.h[i]; ss += v * v; }
-    ss = router_block_sum(ss, red);
+    ss = router_block_sum(ss, red);   // (its barrier also publishes the mbarrier's initialisation)
     inv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
-    for (int i = threadIdx.x; i < a.H; i += kRouterThreads) {
-      const float v = (a.h[i] * inv) * a.norm_w[i];
-      if (e == 0) a.xn[i] = v;
-      dot = fmaf(v, __ldcs(wr + i), dot);
-    }
   } else {
-    for (int i = threadIdx.x; i < a.H; i += kRouterThreads) dot = fmaf(a.xn[i], __ldcs(wr + i), dot);
+    __syncthreads();
+  }
+  bool row_ok = true;
+  if (row_async) row_ok = mbar_wait(&bar, 0, err, EF_TIMEOUT_FULL);
+  const float* wsrc = row_async ? wrow : wr;
+  if (row_ok) {
+    for (int i = threadIdx.x; i < a.H; i += kRouterThreads) {
+      const float v = a.h ? (a.h[i] * inv) * a.norm_w[i] : a.xn[i];
+      if (a.h && e == 0) a.xn[i] = v;
+      dot = fmaf(v, wsrc[i], dot);
+    }
   }
   dot = router_block_sum(dot, red);
+  if (threadIdx.x == 0) {
+    float v = dot + (a.b ? a.b[e] : 0.f);
+    if (a.mask && a.mask[e]) v = -INFINITY;
+    a.logits[e] = v;
+    __threadfence();
+    last = (atomicAdd(a.counter, 1u) == gridDim.x - 1) ? 1u : 0u;
+  }
   if (a.xterm) {
     // the normed x as the expert GEMVs' B terms: warp w of CTA e takes 32-element blocks
     // e*8 + w, e*8 + w + 8*E, ... (same arithmetic as xn above, so the terms encode xn exactly)
@@ -580,27 +599,22 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, ui
       umma::quantize_terms_warp(v, lane, a.xterm, nb, b);
     }
   }
-  if (threadIdx.x == 0) {
-    float v = dot + (a.b ? a.b[e] : 0.f);
-    if (a.mask && a.mask[e]) v = -INFINITY;
-    a.logits[e] = v;
-    __threadfence();
-    last = (atomicAdd(a.counter, 1u) == gridDim.x - 1) ? 1u : 0u;
-  }
   __syncthreads();
-  if (!last) return;
+  if (!last || warp != 0) return;
   __threadfence();
-  // ---- top-k on the last CTA (ties -> lower index, as a stable descending sort) ----
-  for (int i = threadIdx.x; i < a.E; i += kRouterThreads) lg[i] = __ldcg(&a.logits[i]);
-  __syncthreads();
+  // ---- top-k by one warp (ties -> lower index, as a stable descending sort) ----
+  // lane l holds experts l, l + 32, ...; a 32-bit mask per lane marks the ones taken
+  const int per = (a.E + 31) / 32;
+  uint32_t taken = 0u;
+  float sel_v[kMaxK];
+  int sel_i[kMaxK];
   for (int k = 0; k < a.K; ++k) {
     float best = -INFINITY;
     int bidx = 0x7fffffff;
-    for (int i = threadIdx.x; i < a.E; i += kRouterThreads) {
-      const float v = lg[i];
-      bool taken = false;
-      for (int q = 0; q < k; ++q) taken |= (sel_i[q] == i);
-      if (taken) continue;
+    for (int j = 0; j < per; ++j) {
+      const int i = lane + 32 * j;
+      if (i >= a.E || ((taken >> j) & 1u)) continue;
+      const float v = __ldcg(&a.logits[i]);
       if (v > best || (v == best && i < bidx)) { best = v; bidx = i; }
     }
 #pragma unroll
@@ -609,18 +623,15 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, ui
       const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
       if (ov > best || (ov == best && oi < bidx)) { best = ov; bidx = oi; }
     }
-    if (lane == 0) { bv[warp] = best; bi[warp] = bidx; }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float bb = bv[0]; int ii = bi[0];
-      for (int w = 1; w < kRouterThreads / 32; ++w)
-        if (bv[w] > bb || (bv[w] == bb && bi[w] < ii)) { bb = bv[w]; ii = bi[w]; }
-      if (ii == 0x7fffffff) { ii = 0; atomicOr(err, EF_BAD_INDEX); }
-      sel_v[k] = bb; sel_i[k] = ii;
+    if (bidx == 0x7fffffff) {   // fewer selectable experts than k
+      if (lane == 0) atomicOr(err, EF_BAD_INDEX);
+      bidx = 0;
     }
-    __syncthreads();
+    if ((bidx & 31) == lane) taken |= 1u << (bidx >> 5);
+    sel_v[k] = best;
+    sel_i[k] = bidx;
   }
-  if (threadIdx.x == 0) {
+  if (lane == 0) {
     float w[kMaxK];
     if (a.softmax_weight) {              // layer.rs:2361-2372
       float mx = -INFINITY;
@@ -631,9 +642,9 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, ui
       for (int k = 0; k < a.K; ++k) w[k] = w[k] / sum;
     } else {                              // layer.rs:2374-2394
       float mx = -INFINITY;
-      for (int i = 0; i < a.E; ++i) mx = fmaxf(mx, lg[i]);
+      for (int i = 0; i < a.E; ++i) mx = fmaxf(mx, __ldcg(&a.logits[i]));
       float sum = 0.f;
-      for (int i = 0; i < a.E; ++i) sum += expf(lg[i] - mx);
+      for (int i = 0; i < a.E; ++i) sum += expf(__ldcg(&a.logits[i]) - mx);
       float ts = 0.f;
       for (int k = 0; k < a.K; ++k) { w[k] = expf(sel_v[k] - mx) / sum; }
       for (int k = 0; k < a.K; ++k) ts += w[k];
@@ -697,16 +708,24 @@ cudaError_t launch_moe_combine(const DevCtx& c, const PendingCombine& pc, int H,
 cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s) {
   if (a.K < 1 || a.K > kMaxK || a.K > a.E || a.E > kRouterMaxE || !a.counter) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
+  // the router row goes to shared memory by a bulk copy when it is 16-byte aligned (all rows are
+  // when the matrix is and H % 4 == 0)
+  const int row_async = (reinterpret_cast<uintptr_t>(a.w) % 16 == 0 && a.H % 4 == 0 && a.H <= 12288) ? 1 : 0;
+  const size_t smem = row_async ? (size_t)a.H * 4 : 0;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
   cfg.gridDim = dim3((unsigned)a.E);
   cfg.blockDim = dim3(kRouterThreads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, router_kernel, a, c.err);
+  return cudaLaunchKernelEx(&cfg, router_kernel, a, c.err, row_async);
 }
 
 cudaError_t launch_moe_mxfp4(const DevCtx& c, const MoeArgs& a, cudaStream_t s) {

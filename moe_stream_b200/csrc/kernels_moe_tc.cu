@@ -179,23 +179,25 @@ struct Stage {
   int phase, item, seg, w0, w1;   // K-words [w0, w1) of item, within one slab; seg = the unit's range index
   bool seg_start, seg_end;        // first / last stage of the unit
 };
-struct StageWalk {
-  int KW[2], S[2], u[2], u1[2], phase, item, seg, w, wend;
+struct StageWalk {   // two phases held as scalar pairs (no runtime-indexed arrays: registers only)
+  int kw0, kw1, s0, s1, ua, ua1, ub, ub1, phase, item, seg, w, wend;
   __device__ void init(const int (&u0_)[2], const int (&u1_)[2], const int (&kw)[2], const int (&sp)[2]) {
-    for (int q = 0; q < 2; ++q) { KW[q] = kw[q]; S[q] = sp[q]; u[q] = u0_[q]; u1[q] = u1_[q]; }
+    kw0 = kw[0]; kw1 = kw[1]; s0 = sp[0]; s1 = sp[1];
+    ua = u0_[0]; ua1 = u1_[0]; ub = u0_[1]; ub1 = u1_[1];
     phase = 0; item = 0; seg = 0; w = wend = 0;
   }
   __device__ bool next(Stage& st) {
     st.seg_start = false;
     if (w >= wend) {
-      while (phase < 2 && u[phase] >= u1[phase]) ++phase;
-      if (phase >= 2) return false;
-      const int n = S[phase], kw = KW[phase];
-      item = u[phase] / n;
-      seg = u[phase] - item * n;
+      if (phase == 0 && ua >= ua1) phase = 1;
+      if (phase == 1 && ub >= ub1) return false;
+      const int n = phase ? s1 : s0, kw = phase ? kw1 : kw0;
+      const int u = phase ? ub : ua;
+      item = u / n;
+      seg = u - item * n;
       w = seg * kw / n;
       wend = (seg + 1) * kw / n;
-      ++u[phase];
+      if (phase) ++ub; else ++ua;
       st.seg_start = true;
     }
     st.phase = phase;
@@ -220,7 +222,7 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
 // copies only after every gate_up tile of that slot is finished (per-slot counter), so down's
 // weight streaming overlaps gate_up's tail.  All CTAs are resident together (one per SM), and
 // gate_up work waits on nothing but its own copies, so the counters always complete.
-__global__ void __launch_bounds__(kThreads, kCtasPerSm) moe_tc_kernel(TcParams p) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) moe_tc_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
@@ -380,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) moe_tc_kernel(TcParams p
       const int item = st.item, q0 = st.phase;
       const int ls = item / ph.tiles, t = item % ph.tiles;
       const int e = s_exp[ls], slot = s_slot[ls];
-      const int nseg = S[q0], segi = st.seg;
+      const int nseg = q0 ? S[1] : S[0], segi = st.seg;
       // biases are read before the accumulator wait (they are off the critical path there)
       float b0 = 0.f, b1 = 0.f;
       if (q0 == TC_GATEUP) {
