@@ -361,6 +361,66 @@ def run_case_moe(args):
                       "achieved_gbs": round(MOE_BYTES / (ms * 1e-3) / 1e9, 1)}), flush=True)
 
 
+def run_case_prefill(args):
+    """Config 4's MoE step on one GPU: 8 prompts x 2048 tokens through one GPT-OSS-20B-shaped MoE
+    layer (uniform random top-4 routing, seeded), tokens sorted by expert into the grouped bf16
+    GEMM on tcgen05.  FLOPs = T x K x 3 x 2 x 2880^2 per layer; CUDA events on the stream."""
+    import torch
+    from moe_stream_b200.engine import Context
+    H = I = 2880
+    E, K, T = 32, 4, 8 * 2048
+    rb = H // 32 * 17
+    g = torch.Generator(device="cuda").manual_seed(0)
+    ctx = Context(0)
+    stream = torch.cuda.current_stream()
+    ctx.set_stream(stream)
+    gb, db = Context.mxfp4_packed_bytes(H, I, E)
+
+    def mx(n_rows):
+        b = torch.randint(0, 256, (E * n_rows * rb,), dtype=torch.uint8, device="cuda", generator=g)
+        b.view(-1, 17)[:, 0] = torch.randint(119, 124, (E * n_rows * rb // 17,), dtype=torch.uint8, device="cuda",
+                                             generator=g)
+        return b
+
+    gu = torch.empty(gb, dtype=torch.uint8, device="cuda")
+    dn = torch.empty(db, dtype=torch.uint8, device="cuda")
+    ctx.mxfp4_pack_experts(mx(I), mx(I), mx(H), H, I, E, gu, dn)
+    bias = [torch.randn(E * I, device="cuda", generator=g) * 0.01, torch.randn(E * I, device="cuda", generator=g) * 0.01,
+            torch.randn(E * H, device="cuda", generator=g) * 0.01]
+    x = torch.randn(T, H, device="cuda", generator=g)
+    x = x / torch.sqrt((x * x).mean(-1, keepdim=True) + 1e-5)
+    idx = torch.argsort(torch.rand(T, E, device="cuda", generator=g), dim=1)[:, :K].int().contiguous()
+    wts = torch.softmax(torch.randn(T, K, device="cuda", generator=g), -1).contiguous()
+    out = torch.empty(T, H, device="cuda")
+
+    def call():
+        ctx.moe_mxfp4_prefill_packed(gu, dn, bias[0], bias[1], bias[2], H, I, E, K, 0, x, T, idx, wts, out)
+
+    for _ in range(max(3, args.warmup)):
+        call()
+    torch.cuda.synchronize()
+    n = max(1, args.steps)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        s.record(stream)
+        for _ in range(n):
+            call()
+        e.record(stream)
+        torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / n
+    ctx.sync()
+    flops = T * K * 3 * 2 * H * I
+    pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    peak = float(pk.get("bf16_tflops_sustained", 1400.0))
+    tf = flops / (ms * 1e-3) / 1e12
+    print(json.dumps({"case": "prefill", "metric": "MoE prefill TFLOP/s (config 4, one layer)", "tokens": T,
+                      "ms_per_layer": round(ms, 3), "tflops": round(tf, 1), "peak_bf16_tflops": peak,
+                      "peak_kind": "measured sustained" if pk else "fallback", "frac": round(tf / peak, 4),
+                      "tok_s_prefill_24_layers_moe_only": round(T / (24 * ms * 1e-3), 1),
+                      "clocks": clk.summary()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -376,12 +436,15 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="profiling only: override the layer count")
     ap.add_argument("--mode", default="ep", choices=["ep", "replicas"],
                     help="N > 1: expert parallel over one sequence (default) or N independent replicas")
-    ap.add_argument("--case", default=None, choices=[None, "moe-layer"], help="small profiling case")
+    ap.add_argument("--case", default=None, choices=[None, "moe-layer", "prefill"],
+                    help="moe-layer: the decode expert FFN alone; prefill: config 4's MoE step")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.case == "moe-layer":
         run_case_moe(args)
+    elif args.case == "prefill":
+        run_case_prefill(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -154,6 +154,15 @@ MS_API ms_status ms_moe_mxfp4_decode_packed(ms_ctx* ctx, const void* gate_up_pac
                                             const float* gate_b, const float* up_b, const float* down_b, int hidden,
                                             int inter, int n_experts, int top_k, int arch, const float* x,
                                             const int32_t* idx, const float* wts, float* h);
+/* Batched prefill of one MoE layer over T tokens (replaces the multi-token expert branches,
+ * model/layer.rs:1316-1349, 1848-1894): tokens sorted by expert, a grouped GEMM on the tensor cores
+ * with the MXFP4 weights expanded exactly to bf16 in shared memory and bf16 activations, f32
+ * accumulation; out[t] = sum over the token's experts (ascending id) of w * FFN(x[t]).
+ * x [T, hidden], idx / wts [T, top_k], out [T, hidden], device pointers; packed experts as above. */
+MS_API ms_status ms_moe_mxfp4_prefill_packed(ms_ctx* ctx, const void* gate_up_packed, const void* down_packed,
+                                             const float* gate_b, const float* up_b, const float* down_b, int hidden,
+                                             int inter, int n_experts, int top_k, int arch, const float* x,
+                                             int n_tokens, const int32_t* idx, const float* wts, float* out);
 
 /* ---- model: the Engine surface (engine.rs open_with_device / preload_weights / forward /
  *      generate / clear_cache) ---- */

@@ -67,6 +67,8 @@ _SIGS = {
     "ms_mxfp4_pack_experts": (C.c_int, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "ms_moe_mxfp4_decode_packed": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp,
                                              _vp]),
+    "ms_moe_mxfp4_prefill_packed": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i, _vp,
+                                              _vp, _vp]),
     "ms_nccl_unique_id": (C.c_int, [_vp, _vp, C.c_size_t]),
     "ms_model_init_ep": (C.c_int, [_vp, _vp, C.c_size_t]),
     "ms_model_create": (C.c_int, [_vp, C.POINTER(ModelConfig), C.POINTER(_vp)]),

@@ -167,6 +167,23 @@ cudaError_t launch_mxfp4_pack(const uint8_t* src, int E, int rows, int cols, int
                               int tiles, uint8_t* dst, cudaStream_t s);
 cudaError_t launch_xterms(const DevCtx& c, const float* x, int H, uint8_t* xterm, cudaStream_t s);
 
+// ---- batched prefill: the expert FFN as a grouped bf16 GEMM on tcgen05 (kernels_prefill.cu) ----
+struct PrefillArgs {
+  const uint8_t* gu = nullptr;      // packed MXFP4 tiles, as TcMoeArgs
+  const uint8_t* down = nullptr;
+  const float* gate_b = nullptr;    // [E, I] or null
+  const float* up_b = nullptr;
+  const float* down_b = nullptr;    // [E, H] or null
+  const float* x = nullptr;         // [T, H] normed inputs
+  const int* idx = nullptr;         // [T, K] expert ids
+  const float* wts = nullptr;       // [T, K] routing weights
+  float* out = nullptr;             // [T, H]: = MoE(x), or += when accumulate
+  void* scratch = nullptr;          // pf_scratch_bytes(H, I, E, T, K) bytes
+  int H = 0, I = 0, E = 0, K = 0, T = 0, expert_base = 0, oai_swiglu = 1, accumulate = 0;
+};
+size_t pf_scratch_bytes(int H, int I, int E, int T, int K);
+cudaError_t launch_moe_prefill(const DevCtx& c, const PrefillArgs& a, cudaStream_t s);
+
 // ---- attention (decode, one token) ----
 struct AttnArgs {
   const float* qkv = nullptr;      // [nh*hd + 2*nkv*hd] projections (+bias), before RoPE

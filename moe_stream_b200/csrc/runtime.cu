@@ -778,6 +778,22 @@ ms_status ms_moe_mxfp4_decode_packed(ms_ctx* c, const void* gu, const void* down
   return MS_OK;
 }
 
+ms_status ms_moe_mxfp4_prefill_packed(ms_ctx* c, const void* gu, const void* down, const float* gb, const float* ub,
+                                      const float* db, int H, int I, int E, int K, int arch, const float* x, int T,
+                                      const int32_t* idx, const float* wts, float* out) {
+  if (!c || !gu || !down || !x || !idx || !wts || !out || K <= 0 || K > 16 || E <= 0 || E > 256 || T <= 0)
+    return MS_ERR_INVALID_ARG;
+  if (!tc_supported(H, I)) return fail(c, MS_ERR_SHAPE, "moe prefill: hidden and inter must be multiples of 64");
+  ms_status s = ensure_scratch(c, pf_scratch_bytes(H, I, E, T, K), 64);
+  if (s != MS_OK) return s;
+  PrefillArgs a;
+  a.gu = (const uint8_t*)gu; a.down = (const uint8_t*)down; a.gate_b = gb; a.up_b = ub; a.down_b = db;
+  a.x = x; a.idx = idx; a.wts = wts; a.out = out; a.scratch = c->scratch;
+  a.H = H; a.I = I; a.E = E; a.K = K; a.T = T; a.expert_base = 0; a.oai_swiglu = arch == MS_ARCH_GPT_OSS;
+  MS_CUDA(c, launch_moe_prefill(c->dc, a, c->stream));
+  return MS_OK;
+}
+
 // ---------------------------------------------------------------------------------
 ms_status ms_model_create(ms_ctx* c, const ms_model_config* cfg, ms_model** out) {
   if (!c || !cfg || !out) return MS_ERR_INVALID_ARG;

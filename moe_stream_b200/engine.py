@@ -104,6 +104,13 @@ class Context:
                                                _ptr(down_b), hidden, inter, n_experts, top_k, arch, _ptr(x),
                                                _ptr(idx), _ptr(wts), _ptr(h)), self.h)
 
+    def moe_mxfp4_prefill_packed(self, gu_packed, down_packed, gate_b, up_b, down_b, hidden, inter, n_experts,
+                                 top_k, arch, x, n_tokens, idx, wts, out) -> None:
+        """Batched prefill of one MoE layer: grouped bf16 GEMM on the tensor cores (out = MoE(x))."""
+        check(lib().ms_moe_mxfp4_prefill_packed(self.h, _ptr(gu_packed), _ptr(down_packed), _ptr(gate_b), _ptr(up_b),
+                                                _ptr(down_b), hidden, inter, n_experts, top_k, arch, _ptr(x),
+                                                n_tokens, _ptr(idx), _ptr(wts), _ptr(out)), self.h)
+
     def close(self) -> None:
         if getattr(self, "h", None):
             for e in list(getattr(self, "_engines", ())):

@@ -260,6 +260,31 @@ def test_moe_packed_scale_range_and_residual(ctx, orc):
     assert ctx.error_flags() == 0
 
 
+PREFILL_TOL = 2e-2   # bf16 activations on the prefill path (weights exact in bf16, f32 accumulation)
+
+
+@pytest.mark.parametrize("spec,n_tok", [(synth.TINY_GPT_OSS, 100), (synth.GPT_OSS_MOE_LAYER, 48)],
+                         ids=["tiny-100tok", "gpt-oss-20b-48tok"])
+def test_moe_prefill_grouped_gemm(ctx, orc, spec, n_tok):
+    """config 4's MoE step: tokens sorted by expert, grouped bf16 GEMM on tcgen05, against the oracle's
+    multi-token expert FFN (layer.rs:1848-1894) on the same tokens and routing"""
+    L = _moe_layer_host(spec, seed=9)
+    x = np.random.default_rng(9).standard_normal((n_tok, spec.hidden)).astype(np.float32)
+    x /= np.sqrt((x * x).mean(-1, keepdims=True) + spec.eps)
+    want, want_idx, want_w = orc.moe_forward(L, x)
+    H, I, E, K = spec.hidden, spec.inter, spec.experts, spec.top_k
+    gu, dn = _packed(ctx, L, spec)
+    out = torch.full((n_tok, H), float("nan"), dtype=torch.float32, device="cuda")
+    for _ in range(2):
+        ctx.moe_mxfp4_prefill_packed(gu, dn, dev(L["gate_bias"]), dev(L["up_bias"]), dev(L["down_bias"]), H, I, E, K,
+                                     0, dev(x), n_tok, dev(want_idx.astype(np.int32)), dev(want_w), out)
+        ctx.sync()
+        got = out.cpu().numpy()
+        assert np.isfinite(got).all()
+        assert rel_err(got, want) < PREFILL_TOL
+    assert ctx.error_flags() == 0
+
+
 def test_router_dummy_mask_and_ties(ctx):
     H, E, K = 256, 16, 4
     w = np.zeros((E, H), np.float32)
