@@ -17,7 +17,7 @@
 //
 // Operand layout (K-major, no swizzle, as umma.cuh): a matrix of R rows is stored as K/8 chunk
 // columns of R rows x 16 bytes (8 bf16).  Weights stay in the decode path's packed MXFP4 tiles;
-// per K = 128 stage, 8 dequant warps expand the stage's codes to bf16 chunk columns in shared memory
+// per K = 64 stage, 8 dequant warps expand the stage's codes to bf16 chunk columns in shared memory
 // (value = e2m1 * 2^(E-127), exact in bf16) while the tensor core consumes the previous stage.
 // Warp roles: 0 producer (1-D bulk copies), 1 MMA issuer + tensor-memory owner, 2-5 epilogue
 // (double-buffered accumulators), 6-13 dequant.  Every wait is bounded.
@@ -32,17 +32,19 @@ namespace ms {
 namespace {
 
 constexpr int kPfN = 256;                  // tokens per tile (MMA N)
-constexpr int kPfStA = 4 * 2048;           // MXFP4 codes of a stage: 4 chunks x 128 rows x 16 B
-constexpr int kPfStSF = 512;               // its scale group
-constexpr int kPfStB = 16 * kPfN * 16;     // tokens: 16 chunk columns x 256 rows x 16 B
+constexpr int kPfCh = 2;                   // MXFP4 chunks per stage (K = 64)
+constexpr int kPfStA = kPfCh * 2048;       // MXFP4 codes of a stage: 2 chunks x 128 rows x 16 B
+constexpr int kPfStSF = 512;               // the scale group holding them
+constexpr int kPfStB = 4 * kPfCh * kPfN * 16;   // tokens: 8 bf16 chunk columns x 256 rows x 16 B
 constexpr int kPfStage = kPfStA + kPfStSF + kPfStB;
-constexpr int kPfABf = 16 * 128 * 16;      // dequantized weights of a stage
-constexpr int kPfStages = 2;
+constexpr int kPfABf = 4 * kPfCh * 128 * 16;    // dequantized weights of a stage
+constexpr int kPfStages = 4;
+constexpr int kPfUpLd = 33;                // padded row of the up-row exchange buffer (no bank conflicts)
 constexpr int kPfThreads = 14 * 32;
 constexpr int kPfDeqThreads = 8 * 32;
 constexpr int kPfTmemCols = 512;           // two 256-column accumulators
 constexpr int kPfMaxE = 256;
-constexpr int kPfSmem = kPfStages * (kPfStage + kPfABf) + 64 * 32 * 4;
+constexpr int kPfSmem = kPfStages * (kPfStage + kPfABf) + 64 * kPfUpLd * 4;
 
 struct PfParams {
   int mode;                  // 0 gate_up, 1 down
@@ -164,11 +166,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* stage_base = smem;                                   // [kPfStages][kPfStage]
   uint8_t* abf_base = smem + kPfStages * kPfStage;              // [kPfStages][kPfABf]
-  float* s_up = reinterpret_cast<float*>(abf_base + kPfStages * kPfABf);   // [64][32] up rows of a column block
+  float* s_up = reinterpret_cast<float*>(abf_base + kPfStages * kPfABf);   // [64][33] up rows of a column block
   __shared__ __align__(8) uint64_t full[kPfStages], empty[kPfStages], deq[kPfStages], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int off[kPfMaxE + 1];
   __shared__ int s_abort;
+  __shared__ int s_ent[kPfN];
+  __shared__ float s_w[kPfN];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -183,7 +187,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
   umma::fence_after_sync();
   const uint32_t tb = tmem_base;
   const int n_items = off[p.E] * p.tiles;
-  const int KW = (p.kc + 3) / 4;        // stages per item (the last may hold 2 chunks)
+  const int KW = (p.kc + kPfCh - 1) / kPfCh;   // stages per item
   const int nch_b = p.kc * 4;           // bf16 chunk columns of the token operand (K / 8)
 
   if (warp == 0) {
@@ -200,7 +204,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
         for (int w = 0; w < KW; ++w) {
           const int s = j % kPfStages, n = j / kPfStages;
           if (n > 0 && !mbar_wait(&empty[s], (uint32_t)((n - 1) & 1), p.err, EF_TIMEOUT_EMPTY)) { s_abort = 1; break; }
-          const int c0 = 4 * w, c1 = min(p.kc, c0 + 4), slab = c0 / 16, sl0 = slab * 16, nchs = min(16, p.kc - sl0);
+          const int c0 = kPfCh * w, c1 = min(p.kc, c0 + kPfCh), slab = c0 / 16, sl0 = slab * 16, nchs = min(16, p.kc - sl0);
           const uint8_t* sb = wt + (int64_t)slab * (16 * 2048 + 4 * 512);
           uint8_t* sp = stage_base + (size_t)s * kPfStage;
           const uint32_t ab = (uint32_t)(c1 - c0) * 2048u, bb = (uint32_t)(c1 - c0) * 4u * kPfN * 16u;
@@ -216,7 +220,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
     }
   } else if (warp >= 6) {
     // ---------------- dequant: MXFP4 codes -> exact bf16 chunk columns ----------------
-    const int dt = threadIdx.x - 6 * 32, r = dt & 127, half = dt >> 7;   // row, which 2 of the 4 chunks
+    const int dt = threadIdx.x - 6 * 32, r = dt & 127, half = dt >> 7;   // row, which of the 2 chunks
     int j = 0;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
       for (int w = 0; w < KW; ++w, ++j) {
@@ -224,11 +228,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
         const bool ok = mbar_wait(&full[s], (uint32_t)((j / kPfStages) & 1), p.err, EF_TIMEOUT_FULL);
         const uint8_t* sp = stage_base + (size_t)s * kPfStage;
         uint8_t* ab = abf_base + (size_t)s * kPfABf;
-        const int nchunk = min(p.kc - 4 * w, 4);
+        const int nchunk = min(p.kc - kPfCh * w, kPfCh);
         if (ok) {
-          for (int cl = 2 * half; cl < 2 * half + 2 && cl < nchunk; ++cl) {
+          for (int cl = half; cl < half + 1 && cl < nchunk; ++cl) {
             const uint4 codes = *reinterpret_cast<const uint4*>(sp + cl * 2048 + r * 16);
-            const uint32_t eb = sp[kPfStA + 16 * (r & 31) + 4 * (r >> 5) + cl];
+            const uint32_t eb = sp[kPfStA + 16 * (r & 31) + 4 * (r >> 5) + ((kPfCh * w + cl) & 3)];
             const float sc = __uint_as_float(eb ? eb << 23 : 0x00400000u);   // 2^(E-127)
             const uint32_t cw[4] = {codes.x, codes.y, codes.z, codes.w};
 #pragma unroll
@@ -269,7 +273,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
           umma::fence_after_sync();
           const uint8_t* ab = abf_base + (size_t)s * kPfABf;
           const uint8_t* bb = stage_base + (size_t)s * kPfStage + kPfStA + kPfStSF;
-          const int nk = 2 * min(p.kc - 4 * w, 4);   // MMAs of K = 16 (two bf16 chunk columns each)
+          const int nk = 2 * min(p.kc - kPfCh * w, kPfCh);   // MMAs of K = 16 (two bf16 chunk columns each)
           for (int k = 0; k < nk; ++k) {
             const uint64_t ad = umma::smem_desc(ab + 2 * k * 2048, 2048, 128);
             const uint64_t bd = umma::smem_desc(bb + 2 * k * (kPfN * 16), kPfN * 16, 128);
@@ -304,20 +308,29 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
           umma::ld_32x32b_x32(tb + ((uint32_t)(32 * quad) << 16) + (uint32_t)(a * kPfN + cb * 32), v);
           if (row >= 64) {
 #pragma unroll
-            for (int n = 0; n < 32; ++n) s_up[r * 32 + n] = v[n];
+            for (int n = 0; n < 32; ++n) s_up[r * kPfUpLd + n] = v[n];
           }
           named_bar(1, 128);
           if (row < 64 && ok) {
 #pragma unroll
             for (int n = 0; n < 32; ++n) {
-              const float av = p.oai ? swiglu_pf(v[n] + bg, s_up[r * 32 + n] + bu)
-                                     : ((v[n] + bg) / (1.0f + expf(-(v[n] + bg)))) * (s_up[r * 32 + n] + bu);
+              const float av = p.oai ? swiglu_pf(v[n] + bg, s_up[r * kPfUpLd + n] + bu)
+                                     : ((v[n] + bg) / (1.0f + expf(-(v[n] + bg)))) * (s_up[r * kPfUpLd + n] + bu);
               *reinterpret_cast<__nv_bfloat16*>(at + (cb * 32 + n) * 16) = __float2bfloat16_rn(av);
             }
           }
           named_bar(1, 128);
         }
       } else {
+        // the tile's (token, k) entries and routing weights, read once
+        named_bar(1, 128);
+        for (int n = row; n < kPfN; n += 128) {
+          const int pos = tok0 + n;
+          const int ent = pos < cnt ? p.list[(size_t)e * p.T + pos] : -1;
+          s_ent[n] = ent;
+          s_w[n] = ent >= 0 ? p.wts[ent] : 0.f;
+        }
+        named_bar(1, 128);
         const int hr = mt * 128 + row;                  // hidden row
         const float bd = (p.bias0 && hr < p.H) ? p.bias0[(int64_t)e * p.H + hr] : 0.f;
         for (int cb = 0; cb < kPfN / 32; ++cb) {
@@ -325,10 +338,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
           umma::ld_32x32b_x32(tb + ((uint32_t)(32 * quad) << 16) + (uint32_t)(a * kPfN + cb * 32), v);
           if (ok && hr < p.H) {
             for (int n = 0; n < 32; ++n) {
-              const int pos = tok0 + cb * 32 + n;
-              if (pos >= cnt) break;
-              const int ent = p.list[(size_t)e * p.T + pos];
-              p.y[(size_t)ent * p.H + hr] = (v[n] + bd) * p.wts[ent];
+              const int ent = s_ent[cb * 32 + n];
+              if (ent < 0) break;
+              p.y[(size_t)ent * p.H + hr] = (v[n] + bd) * s_w[cb * 32 + n];
             }
           }
         }
