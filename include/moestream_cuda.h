@@ -164,6 +164,34 @@ MS_API ms_status ms_moe_mxfp4_prefill_packed(ms_ctx* ctx, const void* gate_up_pa
                                              int inter, int n_experts, int top_k, int arch, const float* x,
                                              int n_tokens, const int32_t* idx, const float* wts, float* out);
 
+/* ---- hybrid (Qwen3.5 / Qwen3-Next) blocks ---- */
+/* One Gated DeltaNet layer in device memory.  Projections are in native blocks (qtype as in
+ * ms_gemv): qkv [2*n_k_heads*head_k_dim + n_v_heads*head_v_dim, hidden] (q, k, v rows),
+ * gate (z) [n_v_heads*head_v_dim, hidden], ba [2*n_v_heads, hidden] (beta rows, then alpha rows),
+ * out [hidden, n_v_heads*head_v_dim]; f32 conv1d [conv_dim, conv_kernel], ssm_a, dt_bias
+ * [n_v_heads], norm [head_v_dim].  Mirrors the layer tensors deltanet.rs:204-260 reads. */
+typedef struct ms_deltanet_layer {
+  int hidden, n_k_heads, head_k_dim, n_v_heads, head_v_dim, conv_kernel;
+  float eps;
+  int qkv_q;  const void* qkv;
+  int gate_q; const void* gate;
+  int ba_q;   const void* ba;
+  int out_q;  const void* out;
+  const float *conv1d, *ssm_a, *dt_bias, *norm;
+} ms_deltanet_layer;
+
+/* One DeltaNet decode token (deltanet.rs:204-543): y = out(gated RMSNorm(delta-rule(conv(qkv x))))
+ * with conv_state [conv_dim, conv_kernel-1] and rec_state [n_v_heads, head_k_dim, head_v_dim]
+ * (f32, device) updated in place.  head_v_dim must be 128 and head_k_dim <= 128 (even). */
+MS_API ms_status ms_deltanet_decode(ms_ctx* ctx, const ms_deltanet_layer* layer, const float* d_x,
+                                    float* d_conv_state, float* d_rec_state, float* d_y);
+
+/* y += sigmoid(x . gate_inp) * down(silu(gate x) * up x) for one token (layer.rs:2250-2293 and
+ * its caller layer.rs:910-925).  gate_inp may be NULL (no scaling). */
+MS_API ms_status ms_shared_expert(ms_ctx* ctx, int gate_up_qtype, const void* d_gate, const void* d_up,
+                                  int down_qtype, const void* d_down, const float* d_gate_inp, int hidden,
+                                  int inter, const float* d_x, float* d_y);
+
 /* ---- model: the Engine surface (engine.rs open_with_device / preload_weights / forward /
  *      generate / clear_cache) ---- */
 typedef struct ms_model_config {

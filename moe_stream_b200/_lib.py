@@ -35,6 +35,15 @@ class ModelConfig(C.Structure):
                 ("max_seq_len", C.c_int), ("ep_rank", C.c_int), ("ep_size", C.c_int), ("attn_splits", C.c_int)]
 
 
+class DeltaNetLayer(C.Structure):
+    """ms_deltanet_layer: one Gated DeltaNet layer in device memory (device pointers as ints)."""
+    _fields_ = [("hidden", C.c_int), ("n_k_heads", C.c_int), ("head_k_dim", C.c_int), ("n_v_heads", C.c_int),
+                ("head_v_dim", C.c_int), ("conv_kernel", C.c_int), ("eps", C.c_float),
+                ("qkv_q", C.c_int), ("qkv", C.c_void_p), ("gate_q", C.c_int), ("gate", C.c_void_p),
+                ("ba_q", C.c_int), ("ba", C.c_void_p), ("out_q", C.c_int), ("out", C.c_void_p),
+                ("conv1d", C.c_void_p), ("ssm_a", C.c_void_p), ("dt_bias", C.c_void_p), ("norm", C.c_void_p)]
+
+
 _lib = None
 _vp, _i, _f = C.c_void_p, C.c_int, C.c_float
 _ip = C.POINTER(C.c_int32)
@@ -69,6 +78,8 @@ _SIGS = {
                                              _vp]),
     "ms_moe_mxfp4_prefill_packed": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i, _vp,
                                               _vp, _vp]),
+    "ms_deltanet_decode": (C.c_int, [_vp, C.POINTER(DeltaNetLayer), _vp, _vp, _vp, _vp]),
+    "ms_shared_expert": (C.c_int, [_vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _vp, _vp]),
     "ms_nccl_unique_id": (C.c_int, [_vp, _vp, C.c_size_t]),
     "ms_model_init_ep": (C.c_int, [_vp, _vp, C.c_size_t]),
     "ms_model_create": (C.c_int, [_vp, C.POINTER(ModelConfig), C.POINTER(_vp)]),

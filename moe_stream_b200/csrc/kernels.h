@@ -232,6 +232,22 @@ int argmax_from_key(unsigned long long key);
 cudaError_t launch_gemv_f32(const DevCtx& c, const float* w, int rows, int cols, const float* x,
                             const float* bias, float* y, int accumulate, cudaStream_t s);
 
+// ---- Gated DeltaNet / shared expert (kernels_ssm.cu) ----
+struct DeltaNetStep {
+  int nk = 0, hkd = 0, nv = 0, hvd = 0;
+  float eps = 0.f, scale = 0.f;
+  float* conv_out = nullptr;          // [2 nk hkd + nv hvd] after conv + SiLU
+  const float* ba = nullptr;          // [2 nv]: beta logits, then alpha logits
+  const float* z = nullptr;           // [nv hvd] output gate
+  const float *ssm_a = nullptr, *dt_bias = nullptr, *norm = nullptr;
+  float* state = nullptr;             // [nv, hkd, hvd]
+  float* out = nullptr;               // [nv hvd]
+};
+cudaError_t launch_deltanet_core(const DevCtx& c, const DeltaNetStep& a, int conv_dim, int ks, const float* mixed,
+                                 const float* conv_w, float* conv_state, cudaStream_t s);
+cudaError_t launch_silu_mul(const float* g, const float* u, float* o, int n, cudaStream_t s);
+cudaError_t launch_gated_accum(const float* x, const float* gate_inp, const float* v, float* y, int n, cudaStream_t s);
+
 // ---- step plumbing ----
 struct StepState {
   int token_in;            // host-provided token

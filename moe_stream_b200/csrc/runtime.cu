@@ -794,6 +794,67 @@ ms_status ms_moe_mxfp4_prefill_packed(ms_ctx* c, const void* gu, const void* dow
   return MS_OK;
 }
 
+// ---- hybrid blocks: Gated DeltaNet decode, shared expert ----
+static bool gemv_qtype_ok(int q) {
+  return q == Q_MXFP4 || q == Q_Q8_0 || q == Q_F16 || q == Q_F32 || q == Q_Q4_K || q == Q_Q6_K;
+}
+
+static ms_status gemv_into(ms_ctx* c, int q, const void* w, int rows, int cols, const float* x, float* y,
+                           const char* what) {
+  if (!w) return fail(c, MS_ERR_INVALID_ARG, "%s: null weight", what);
+  if (!gemv_qtype_ok(q)) return fail(c, MS_ERR_UNSUPPORTED_QTYPE, "%s qtype %d", what, q);
+  if (row_bytes(q, cols) < 0) return fail(c, MS_ERR_SHAPE, "%s: cols %d not a whole number of blocks", what, cols);
+  GemvArgs a;
+  a.qtype = q; a.w = w; a.rows = rows; a.cols = cols; a.x = x; a.y = y;
+  cudaError_t e = launch_gemv(c->dc, a, c->stream);
+  if (e == cudaErrorInvalidValue) return fail(c, MS_ERR_SHAPE, "%s: unsupported shape %dx%d", what, rows, cols);
+  if (e != cudaSuccess) return cuda_fail(c, e, what);
+  return MS_OK;
+}
+
+ms_status ms_deltanet_decode(ms_ctx* c, const ms_deltanet_layer* L, const float* x, float* conv_state, float* rec_state,
+                             float* y) {
+  if (!c || !L || !x || (!conv_state && L->conv_kernel > 1) || !rec_state || !y || !L->conv1d || !L->ssm_a || !L->dt_bias || !L->norm)
+    return MS_ERR_INVALID_ARG;
+  const int nk = L->n_k_heads, hkd = L->head_k_dim, nv = L->n_v_heads, hvd = L->head_v_dim, H = L->hidden;
+  if (H <= 0 || nk <= 0 || nv <= 0 || L->conv_kernel < 1 || nv % nk) return MS_ERR_INVALID_ARG;
+  if (hvd != 128 || hkd <= 0 || hkd > 128 || hkd % 2)
+    return fail(c, MS_ERR_SHAPE, "deltanet: head_v_dim 128 and even head_k_dim <= 128 required");
+  const int qt = nk * hkd, vt = nv * hvd, conv_dim = 2 * qt + vt;
+  // scratch (floats): mixed, conv_out, z, ba, o — each 64-float aligned
+  auto al = [](size_t n) { return (n + 63) & ~(size_t)63; };
+  const size_t o_mixed = 0, o_conv = al(conv_dim), o_z = o_conv + al(conv_dim), o_ba = o_z + al(vt),
+               o_o = o_ba + al(2 * nv), total = o_o + al(vt);
+  ms_status s = ensure_scratch(c, total * 4, 64);
+  if (s != MS_OK) return s;
+  float* f = (float*)c->scratch;
+  if ((s = gemv_into(c, L->qkv_q, L->qkv, conv_dim, H, x, f + o_mixed, "deltanet qkv")) != MS_OK) return s;
+  if ((s = gemv_into(c, L->gate_q, L->gate, vt, H, x, f + o_z, "deltanet gate")) != MS_OK) return s;
+  if ((s = gemv_into(c, L->ba_q, L->ba, 2 * nv, H, x, f + o_ba, "deltanet ba")) != MS_OK) return s;
+  DeltaNetStep a;
+  a.nk = nk; a.hkd = hkd; a.nv = nv; a.hvd = hvd; a.eps = L->eps; a.scale = 1.0f / sqrtf((float)hvd);
+  a.conv_out = f + o_conv; a.ba = f + o_ba; a.z = f + o_z; a.ssm_a = L->ssm_a; a.dt_bias = L->dt_bias;
+  a.norm = L->norm; a.state = rec_state; a.out = f + o_o;
+  MS_CUDA(c, launch_deltanet_core(c->dc, a, conv_dim, L->conv_kernel, f + o_mixed, L->conv1d, conv_state, c->stream));
+  return gemv_into(c, L->out_q, L->out, H, vt, f + o_o, y, "deltanet out");
+}
+
+ms_status ms_shared_expert(ms_ctx* c, int guq, const void* gate, const void* up, int dq, const void* down,
+                           const float* gate_inp, int H, int I, const float* x, float* y) {
+  if (!c || !gate || !up || !down || !x || !y || H <= 0 || I <= 0) return MS_ERR_INVALID_ARG;
+  auto al = [](size_t n) { return (n + 63) & ~(size_t)63; };
+  const size_t o_g = 0, o_u = al(I), o_a = o_u + al(I), o_o = o_a + al(I), total = o_o + al(H);
+  ms_status s = ensure_scratch(c, total * 4, 64);
+  if (s != MS_OK) return s;
+  float* f = (float*)c->scratch;
+  if ((s = gemv_into(c, guq, gate, I, H, x, f + o_g, "shared expert gate")) != MS_OK) return s;
+  if ((s = gemv_into(c, guq, up, I, H, x, f + o_u, "shared expert up")) != MS_OK) return s;
+  MS_CUDA(c, launch_silu_mul(f + o_g, f + o_u, f + o_a, I, c->stream));
+  if ((s = gemv_into(c, dq, down, H, I, f + o_a, f + o_o, "shared expert down")) != MS_OK) return s;
+  MS_CUDA(c, launch_gated_accum(x, gate_inp, f + o_o, y, H, c->stream));
+  return MS_OK;
+}
+
 // ---------------------------------------------------------------------------------
 ms_status ms_model_create(ms_ctx* c, const ms_model_config* cfg, ms_model** out) {
   if (!c || !cfg || !out) return MS_ERR_INVALID_ARG;

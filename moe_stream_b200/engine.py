@@ -111,6 +111,24 @@ class Context:
                                                 _ptr(down_b), hidden, inter, n_experts, top_k, arch, _ptr(x),
                                                 n_tokens, _ptr(idx), _ptr(wts), _ptr(out)), self.h)
 
+    def deltanet_decode(self, layer: dict, x, conv_state, rec_state, y) -> None:
+        """One Gated DeltaNet decode token.  layer: ints hidden, n_k_heads, head_k_dim, n_v_heads,
+        head_v_dim, conv_kernel, eps, qkv_q, gate_q, ba_q, out_q and device tensors qkv, gate, ba, out,
+        conv1d, ssm_a, dt_bias, norm.  conv_state / rec_state are updated in place; y = layer output."""
+        from ._lib import DeltaNetLayer
+        d = layer
+        L = DeltaNetLayer(d["hidden"], d["n_k_heads"], d["head_k_dim"], d["n_v_heads"], d["head_v_dim"],
+                          d["conv_kernel"], d["eps"], d["qkv_q"], _ptr(d["qkv"]), d["gate_q"], _ptr(d["gate"]),
+                          d["ba_q"], _ptr(d["ba"]), d["out_q"], _ptr(d["out"]), _ptr(d["conv1d"]),
+                          _ptr(d["ssm_a"]), _ptr(d["dt_bias"]), _ptr(d["norm"]))
+        check(lib().ms_deltanet_decode(self.h, C.byref(L), _ptr(x), _ptr(conv_state), _ptr(rec_state), _ptr(y)),
+              self.h)
+
+    def shared_expert(self, gu_qtype, gate, up, down_qtype, down, gate_inp, hidden, inter, x, y) -> None:
+        """y += sigmoid(x . gate_inp) * down(silu(gate x) * up x) for one token (gate_inp may be None)."""
+        check(lib().ms_shared_expert(self.h, gu_qtype, _ptr(gate), _ptr(up), down_qtype, _ptr(down), _ptr(gate_inp),
+                                     hidden, inter, _ptr(x), _ptr(y)), self.h)
+
     def close(self) -> None:
         if getattr(self, "h", None):
             for e in list(getattr(self, "_engines", ())):

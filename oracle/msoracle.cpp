@@ -842,4 +842,97 @@ int orc_model_generate(orc_model* m, const int32_t* prompt, int n_prompt, int ma
   return n_out;
 }
 
+// ---- Gated DeltaNet, one decode token (model/deltanet.rs:204-543) ----
+int orc_deltanet_step(const orc_deltanet_layer* L, const float* x, float* conv_state, float* rec_state, float* y) {
+  const int nk = L->n_k_heads, hkd = L->head_k_dim, nv = L->n_v_heads, hvd = L->head_v_dim, ks = L->conv_kernel;
+  const int vpk = nv / nk, q_total = nk * hkd, v_total = nv * hvd, conv_dim = 2 * q_total + v_total, H = L->hidden;
+  std::vector<float> mixed(conv_dim), z(v_total), ba(2 * nv);
+  // 1-3. input projections (dequantized f32 weights, deltanet.rs:237-245)
+  if (orc_gemv(L->qkv_q, L->qkv, conv_dim, H, x, mixed.data())) return -1;
+  if (orc_gemv(L->gate_q, L->gate, v_total, H, x, z.data())) return -1;
+  if (orc_gemv(L->ba_q, L->ba, 2 * nv, H, x, ba.data())) return -1;
+  // gates (deltanet.rs:298-310): alpha = ssm_a * softplus(alpha_log + dt_bias), beta = sigmoid
+  std::vector<float> alpha(nv), beta(nv);
+  for (int h = 0; h < nv; ++h) {
+    const float ab = ba[nv + h] + L->dt_bias[h];
+    alpha[h] = L->ssm_a[h] * std::log(1.0f + std::exp(ab));
+    beta[h] = 1.0f / (1.0f + std::exp(-ba[h]));
+  }
+  // 4. depthwise causal conv1d + state shift + SiLU (deltanet.rs:340-372)
+  std::vector<float> conv(conv_dim);
+  for (int c = 0; c < conv_dim; ++c) {
+    float* st = conv_state + (size_t)c * (ks - 1);
+    const float* w = L->conv1d + (size_t)c * ks;
+    float sum = 0.0f;
+    for (int j = 0; j < ks - 1; ++j) sum += st[j] * w[j];
+    sum += mixed[c] * w[ks - 1];
+    conv[c] = sum;
+    for (int j = 0; j + 1 < ks - 1; ++j) st[j] = st[j + 1];
+    if (ks > 1) st[ks - 2] = mixed[c];
+  }
+  for (int c = 0; c < conv_dim; ++c) conv[c] = conv[c] / (1.0f + std::exp(-conv[c]));
+  // 5-6. repeat-interleave to value heads, L2 norm of q (x 1/sqrt(hvd)) and k (deltanet.rs:379-417)
+  std::vector<float> q((size_t)nv * hkd), k((size_t)nv * hkd);
+  for (int g = 0; g < nk; ++g)
+    for (int r = 0; r < vpk; ++r)
+      for (int i = 0; i < hkd; ++i) {
+        q[(size_t)(g * vpk + r) * hkd + i] = conv[(size_t)g * hkd + i];
+        k[(size_t)(g * vpk + r) * hkd + i] = conv[(size_t)q_total + g * hkd + i];
+      }
+  const float scale = 1.0f / std::sqrt((float)hvd);
+  for (int h = 0; h < nv; ++h) {
+    float qs = 0.f, kss = 0.f;
+    for (int i = 0; i < hkd; ++i) qs += q[(size_t)h * hkd + i] * q[(size_t)h * hkd + i];
+    const float qn = std::max(std::sqrt(qs), L->eps);
+    for (int i = 0; i < hkd; ++i) q[(size_t)h * hkd + i] = q[(size_t)h * hkd + i] / qn * scale;
+    for (int i = 0; i < hkd; ++i) kss += k[(size_t)h * hkd + i] * k[(size_t)h * hkd + i];
+    const float kn = std::max(std::sqrt(kss), L->eps);
+    for (int i = 0; i < hkd; ++i) k[(size_t)h * hkd + i] /= kn;
+  }
+  // 7. delta rule (deltanet.rs:434-489)
+  std::vector<float> o(v_total, 0.0f);
+  for (int h = 0; h < nv; ++h) {
+    float* S = rec_state + (size_t)h * hkd * hvd;
+    const float decay = std::exp(alpha[h]);
+    for (int i = 0; i < hkd * hvd; ++i) S[i] *= decay;
+    std::vector<float> kv(hvd, 0.0f);
+    for (int i = 0; i < hkd; ++i)
+      for (int j = 0; j < hvd; ++j) kv[j] += k[(size_t)h * hkd + i] * S[(size_t)i * hvd + j];
+    std::vector<float> delta(hvd);
+    for (int j = 0; j < hvd; ++j) delta[j] = (conv[(size_t)2 * q_total + h * hvd + j] - kv[j]) * beta[h];
+    for (int i = 0; i < hkd; ++i)
+      for (int j = 0; j < hvd; ++j) S[(size_t)i * hvd + j] += k[(size_t)h * hkd + i] * delta[j];
+    for (int i = 0; i < hkd; ++i)
+      for (int j = 0; j < hvd; ++j) o[(size_t)h * hvd + j] += q[(size_t)h * hkd + i] * S[(size_t)i * hvd + j];
+  }
+  // 8-9. per-head RMSNorm x weight, x silu(z) (deltanet.rs:495-522)
+  for (int h = 0; h < nv; ++h) {
+    float sq = 0.f;
+    for (int j = 0; j < hvd; ++j) sq += o[(size_t)h * hvd + j] * o[(size_t)h * hvd + j];
+    const float rms = std::sqrt(sq / (float)hvd + L->eps);
+    for (int j = 0; j < hvd; ++j) o[(size_t)h * hvd + j] = o[(size_t)h * hvd + j] / rms * L->norm[j];
+  }
+  for (int i = 0; i < v_total; ++i) o[i] *= z[i] / (1.0f + std::exp(-z[i]));
+  // 10. output projection (deltanet.rs:527-534)
+  return orc_gemv(L->out_q, L->out, H, v_total, o.data(), y);
+}
+
+// ---- shared expert (model/layer.rs:2250-2293): y += sigmoid(x . gate_inp) * (silu(x Wg) * (x Wu)) Wd ----
+int orc_shared_expert(int gu_q, const void* gate, const void* up, int down_q, const void* down,
+                      const float* gate_inp, int hidden, int inter, const float* x, float* y) {
+  std::vector<float> g(inter), u(inter), a(inter), o(hidden);
+  if (orc_gemv(gu_q, gate, inter, hidden, x, g.data())) return -1;
+  if (orc_gemv(gu_q, up, inter, hidden, x, u.data())) return -1;
+  silu_and_mul(g.data(), u.data(), a.data(), inter);
+  if (orc_gemv(down_q, down, hidden, inter, a.data(), o.data())) return -1;
+  float sig = 1.0f;
+  if (gate_inp) {
+    float d = 0.f;
+    for (int i = 0; i < hidden; ++i) d += x[i] * gate_inp[i];
+    sig = 1.0f / (1.0f + std::exp(-d));
+  }
+  for (int i = 0; i < hidden; ++i) y[i] += o[i] * sig;
+  return 0;
+}
+
 }  // extern "C"

@@ -71,6 +71,25 @@ int orc_moe_forward(const orc_moe_layer* L, const float* x, int n_tok, float* ou
 /* the same layer restricted to experts [e_begin, e_end) (routing over all experts) */
 int orc_moe_forward_range(const orc_moe_layer* L, const float* x, int n_tok, float* out, int e_begin, int e_end);
 
+/* ---- Gated DeltaNet decode step (model/deltanet.rs:204-543) ---- */
+typedef struct {
+  int hidden, n_k_heads, head_k_dim, n_v_heads, head_v_dim, conv_kernel;
+  float eps;
+  int qkv_q; const void* qkv;     /* [2*nk*hkd + nv*hvd, hidden] (flat Q, K, V rows) */
+  int gate_q; const void* gate;   /* [nv*hvd, hidden] (z) */
+  int ba_q; const void* ba;       /* [2*nv, hidden] (flat beta, alpha) */
+  int out_q; const void* out;     /* [hidden, nv*hvd] */
+  const float* conv1d;            /* [conv_dim, conv_kernel] */
+  const float* ssm_a;             /* [nv] (-exp(A_log)) */
+  const float* dt_bias;           /* [nv] */
+  const float* norm;              /* [hvd] */
+} orc_deltanet_layer;
+/* one token: updates conv_state [conv_dim, k-1] and rec_state [nv, hkd, hvd]; y [hidden] */
+int orc_deltanet_step(const orc_deltanet_layer* L, const float* x, float* conv_state, float* rec_state, float* y);
+/* shared expert (layer.rs:1898-1953): y += sigmoid(x . gate_inp) * (silu(x Wg) * (x Wu)) Wd */
+int orc_shared_expert(int gu_q, const void* gate, const void* up, int down_q, const void* down,
+                      const float* gate_inp, int hidden, int inter, const float* x, float* y);
+
 /* ---- whole model (engine.rs:1869-2118) ---- */
 typedef struct orc_model orc_model;
 /* open a GGUF file (reader.rs:259-368, config.rs:253-434) */

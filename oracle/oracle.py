@@ -32,6 +32,13 @@ class MoeLayer(C.Structure):
                 ("oai_swiglu", C.c_int), ("norm_topk_prob", C.c_int)]
 
 
+class DeltaNetLayer(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("n_k_heads", C.c_int), ("head_k_dim", C.c_int), ("n_v_heads", C.c_int),
+                ("head_v_dim", C.c_int), ("conv_kernel", C.c_int), ("eps", C.c_float),
+                ("qkv_q", C.c_int), ("qkv", _vp), ("gate_q", C.c_int), ("gate", _vp), ("ba_q", C.c_int), ("ba", _vp),
+                ("out_q", C.c_int), ("out", _vp), ("conv1d", _fp), ("ssm_a", _fp), ("dt_bias", _fp), ("norm", _fp)]
+
+
 def build() -> str:
     """Compile the oracle with its Makefile (g++ only; no reference sources involved)."""
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
@@ -60,6 +67,8 @@ def lib():
         L.orc_top_k_routing.argtypes = [_fp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _i32p, _fp]
         L.orc_moe_forward.argtypes = [C.POINTER(MoeLayer), _fp, C.c_int, _fp, _i32p, _fp]
         L.orc_moe_forward_range.argtypes = [C.POINTER(MoeLayer), _fp, C.c_int, _fp, C.c_int, C.c_int]
+        L.orc_deltanet_step.argtypes = [C.POINTER(DeltaNetLayer), _fp, _fp, _fp, _fp]
+        L.orc_shared_expert.argtypes = [C.c_int, _vp, _vp, C.c_int, _vp, _fp, C.c_int, C.c_int, _fp, _fp]
         L.orc_model_open.restype = _vp
         L.orc_model_open.argtypes = [C.c_char_p, C.c_int, C.c_char_p, C.c_int]
         L.orc_model_set_attn_mode.argtypes = [_vp, C.c_int]
@@ -196,6 +205,40 @@ def moe_forward(layer: dict, x: np.ndarray, expert_range=None):
         return out, None, None
     lib().orc_moe_forward(C.byref(L), _f(x), n_tok, _f(out), _i(idx), _f(w))
     return out, idx, w
+
+
+def deltanet_layer(d: dict, keep: list) -> DeltaNetLayer:
+    """ctypes view of a DeltaNet layer dict (numpy arrays + ints); keep holds the buffers alive"""
+    def ptr(a, fp=False):
+        a = np.ascontiguousarray(a)
+        keep.append(a)
+        return a.ctypes.data_as(_fp) if fp else a.ctypes.data
+    return DeltaNetLayer(d["hidden"], d["n_k_heads"], d["head_k_dim"], d["n_v_heads"], d["head_v_dim"],
+                         d["conv_kernel"], d["eps"], d["qkv_q"], ptr(d["qkv"]), d["gate_q"], ptr(d["gate"]),
+                         d["ba_q"], ptr(d["ba"]), d["out_q"], ptr(d["out"]), ptr(d["conv1d"], True),
+                         ptr(d["ssm_a"], True), ptr(d["dt_bias"], True), ptr(d["norm"], True))
+
+
+def deltanet_step(d: dict, x, conv_state, rec_state) -> np.ndarray:
+    """one DeltaNet decode token; conv_state / rec_state (f32 numpy) are updated in place"""
+    keep = []
+    L = deltanet_layer(d, keep)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(d["hidden"], np.float32)
+    if lib().orc_deltanet_step(C.byref(L), _f(x), _f(conv_state), _f(rec_state), _f(y)) != 0:
+        raise ValueError("unsupported qtype")
+    return y
+
+
+def shared_expert(gu_q, gate, up, down_q, down, gate_inp, hidden, inter, x, y):
+    """y += shared expert(x), in place"""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    gi = np.ascontiguousarray(gate_inp, dtype=np.float32) if gate_inp is not None else None
+    if lib().orc_shared_expert(gu_q, np.ascontiguousarray(gate).ctypes.data, np.ascontiguousarray(up).ctypes.data,
+                               down_q, np.ascontiguousarray(down).ctypes.data, _f(gi) if gi is not None else _fp(),
+                               hidden, inter, _f(x), _f(y)) != 0:
+        raise ValueError("unsupported qtype")
+    return y
 
 
 class Model:

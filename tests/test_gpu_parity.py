@@ -12,6 +12,8 @@ import pytest
 from moe_stream_b200 import gguf as G
 from moe_stream_b200 import synth
 
+from . import hybrid_synth as hs
+
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
@@ -411,3 +413,70 @@ def test_long_context_sliding_window(ctx, orc, tmp_path):
     assert got == want
     om.close()
     eng.close()
+
+
+# ---- hybrid blocks: Gated DeltaNet decode (deltanet.rs:204-543), shared expert (layer.rs:2250-2293) ----
+
+
+def _dn_device(d):
+    out = dict(d)
+    for k in ("qkv", "gate", "ba", "out"):
+        out[k] = dev(pad_rows(d[k]))
+    for k in ("conv1d", "ssm_a", "dt_bias", "norm"):
+        out[k] = dev(d[k])
+    return out
+
+
+@pytest.mark.parametrize("shape,qtype", [
+    (dict(), G.F32),
+    (dict(nk=1, hkd=32, nv=2, ks=3), G.F32),
+    (dict(hidden=2048, nk=16, hkd=128, nv=32, ks=4), G.Q4_K),     # Qwen3-Next linear-attention layer
+    (dict(hidden=512, nk=4, hkd=128, nv=8, ks=4), G.Q6_K),
+])
+def test_deltanet_decode_multi_step(ctx, orc, shape, qtype):
+    d = hs.deltanet_layer(11, qtype=qtype, **shape)
+    dd = _dn_device(d)
+    nv, hkd, hvd, ks = d["n_v_heads"], d["head_k_dim"], d["head_v_dim"], d["conv_kernel"]
+    conv_dim = 2 * d["n_k_heads"] * hkd + nv * hvd
+    cs = np.zeros((conv_dim, ks - 1), np.float32)
+    rs = np.zeros((nv, hkd, hvd), np.float32)
+    cs_d, rs_d = dev(cs), dev(rs)
+    y_d = torch.empty(d["hidden"], dtype=torch.float32, device="cuda")
+    rng = np.random.default_rng(3)
+    for step in range(6):
+        x = rng.standard_normal(d["hidden"]).astype(np.float32)
+        want = orc.deltanet_step(d, x, cs, rs)
+        ctx.deltanet_decode(dd, dev(x), cs_d, rs_d, y_d)
+        ctx.sync()
+        assert rel_err(y_d.cpu().numpy(), want) < REL_TOL, step
+        assert rel_err(rs_d.cpu().numpy(), rs) < REL_TOL, step
+        assert rel_err(cs_d.cpu().numpy(), cs) < REL_TOL, step
+
+
+def test_deltanet_decode_rejects_unsupported_head_dim(ctx):
+    from moe_stream_b200._lib import MsError
+    d = _dn_device(hs.deltanet_layer(1, hvd=64))
+    with pytest.raises(MsError):
+        ctx.deltanet_decode(d, torch.zeros(d["hidden"], device="cuda"),
+                            torch.zeros(4096, device="cuda"), torch.zeros(1 << 16, device="cuda"),
+                            torch.zeros(d["hidden"], device="cuda"))
+
+
+@pytest.mark.parametrize("hidden,inter,gu_q,down_q,gated", [
+    (256, 128, G.F32, G.F32, True),
+    (2048, 512, G.Q4_K, G.Q6_K, True),      # Qwen3-Next shared expert shape
+    (512, 256, G.Q4_K, G.Q4_K, False),
+])
+def test_shared_expert(ctx, orc, hidden, inter, gu_q, down_q, gated):
+    e = hs.shared_expert(9, hidden, inter, gu_q, down_q, gated)
+    rng = np.random.default_rng(hidden + inter)
+    x = rng.standard_normal(hidden).astype(np.float32)
+    y0 = rng.standard_normal(hidden).astype(np.float32)
+    want = orc.shared_expert(e["gu_q"], e["gate"], e["up"], e["down_q"], e["down"], e["gate_inp"], hidden, inter,
+                             x, y0.copy())
+    y = dev(y0)
+    gi = dev(e["gate_inp"]) if gated else None
+    ctx.shared_expert(gu_q, dev(pad_rows(e["gate"])), dev(pad_rows(e["up"])), down_q, dev(pad_rows(e["down"])), gi,
+                      hidden, inter, dev(x), y)
+    ctx.sync()
+    assert rel_err(y.cpu().numpy(), want) < REL_TOL
