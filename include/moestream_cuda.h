@@ -164,6 +164,24 @@ MS_API ms_status ms_moe_mxfp4_prefill_packed(ms_ctx* ctx, const void* gate_up_pa
                                              int inter, int n_experts, int top_k, int arch, const float* x,
                                              int n_tokens, const int32_t* idx, const float* wts, float* out);
 
+/* ---- lockstep batch: B sequences at one shared position (Engine::forward over input_ids
+ *      [B, T], engine.rs:1869-2006, KV rows per batch entry kv_cache.rs:37-60) ----
+ * Every weight byte is streamed once per step for the whole batch: Q8_0 projections as int8 MMA
+ * over the batch, experts grouped by id (each expert once per group of <= 4 tokens), LM head as
+ * f16 MMA.  Needs native-layout experts (K-quants, or MXFP4 with MS_MOE_TC=0) and ep_size 1. */
+MS_API ms_status ms_model_batch_open(ms_model* m, int batch);     /* allocates B KV caches, 1 <= B <= 32 */
+MS_API ms_status ms_model_batch_close(ms_model* m);
+MS_API ms_status ms_model_batch_clear(ms_model* m);               /* all sequences back to length 0 */
+/* tokens [B][T] (row per sequence); next [B] = greedy token after the last position (or NULL) */
+MS_API ms_status ms_model_batch_forward(ms_model* m, const int32_t* tokens, int n_tokens, int32_t* next);
+/* n greedy steps, each step's argmax fed back on the device (no host sync) */
+MS_API ms_status ms_model_batch_decode_steps_device(ms_model* m, int n_steps);
+MS_API ms_status ms_model_batch_next_tokens(ms_model* m, int32_t* next);          /* [B] */
+/* tokens fed per step, [rows][B] */
+MS_API ms_status ms_model_batch_token_log(ms_model* m, int32_t* out, int max_rows, int* n_rows);
+MS_API ms_status ms_model_batch_last_logits(ms_model* m, float* out);             /* [B][vocab] */
+MS_API int ms_model_batch_kernels_per_step(const ms_model* m);
+
 /* ---- hybrid (Qwen3.5 / Qwen3-Next) blocks ---- */
 /* One Gated DeltaNet layer in device memory.  Projections are in native blocks (qtype as in
  * ms_gemv): qkv [2*n_k_heads*head_k_dim + n_v_heads*head_v_dim, hidden] (q, k, v rows),

@@ -92,6 +92,15 @@ _SIGS = {
     "ms_model_decode_step": (C.c_int, [_vp, C.c_int32, _ip]),
     "ms_model_generate": (C.c_int, [_vp, _ip, _i, _i, _ip, C.POINTER(C.c_int)]),
     "ms_model_decode_steps_device": (C.c_int, [_vp, _i]),
+    "ms_model_batch_open": (C.c_int, [_vp, _i]),
+    "ms_model_batch_close": (C.c_int, [_vp]),
+    "ms_model_batch_clear": (C.c_int, [_vp]),
+    "ms_model_batch_forward": (C.c_int, [_vp, _ip, _i, _ip]),
+    "ms_model_batch_decode_steps_device": (C.c_int, [_vp, _i]),
+    "ms_model_batch_next_tokens": (C.c_int, [_vp, _ip]),
+    "ms_model_batch_token_log": (C.c_int, [_vp, _ip, _i, C.POINTER(C.c_int)]),
+    "ms_model_batch_last_logits": (C.c_int, [_vp, _fp]),
+    "ms_model_batch_kernels_per_step": (C.c_int, [_vp]),
     "ms_model_token_log": (C.c_int, [_vp, _ip, _i, C.POINTER(C.c_int)]),
     "ms_model_clear_cache": (C.c_int, [_vp]),
     "ms_model_seq_len": (C.c_int, [_vp, C.POINTER(C.c_int)]),

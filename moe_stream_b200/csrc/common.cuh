@@ -214,6 +214,52 @@ __device__ __forceinline__ float combine_at(const PendingCombine& pc, const Comb
   return acc;
 }
 
+// Q8_0 quantization of one 32-element block as candle's BlockQ8_0::from_float does:
+// d = amax / 127 (stored as f16), q = roundf(x / d) with the unrounded f32 d.
+__device__ __forceinline__ void quantize_q8_block(const float (&v)[32], int8_t* q, float* d_out) {
+  float amax = 0.f;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) amax = fmaxf(amax, fabsf(v[k]));
+  const float d = amax / 127.0f;
+  const float id = d != 0.0f ? 1.0f / d : 0.0f;
+  int qw[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    uint32_t u = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) u |= ((uint32_t)(uint8_t)(int8_t)roundf(v[4 * k + j] * id)) << (8 * j);
+    qw[k] = (int)u;
+  }
+  int4* dst = reinterpret_cast<int4*>(q);
+  dst[0] = make_int4(qw[0], qw[1], qw[2], qw[3]);
+  dst[1] = make_int4(qw[4], qw[5], qw[6], qw[7]);
+  *d_out = __half2float(__float2half_rn(d));
+}
+
+// Whole-CTA RMSNorm (weights w) of xs[0..H) in shared memory, then Q8_0 quantization into
+// xq / xd (one thread per 32-element block).  red: >= 32 floats of shared scratch.
+__device__ __forceinline__ void cta_rmsnorm_q8(const float* xs, int H, const float* w, float eps, int8_t* xq,
+                                               float* xd, float* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) ss += xs[i] * xs[i];
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float t = 0.f;
+  for (int k = 0; k < nw; ++k) t += red[k];
+  const float inv = 1.0f / sqrtf(t / (float)H + eps);
+  for (int b = threadIdx.x; b < H / 32; b += blockDim.x) {
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      const int kk = (k + lane) & 31;   // rotate the start so lanes hit different banks
+      v[kk] = (xs[32 * b + kk] * inv) * w[32 * b + kk];
+    }
+    quantize_q8_block(v, xq + 32 * b, &xd[b]);
+  }
+}
+
 // Programmatic dependent launch: let the next kernel start its prologue early /
 // wait for the previous kernel's memory to be visible.
 __device__ __forceinline__ void pdl_launch_dependents() {

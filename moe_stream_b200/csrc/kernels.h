@@ -94,6 +94,7 @@ struct RouterArgs {
   int softmax_weight = 1;         // GPT-OSS: softmax over the selected k logits
   int normalize = 0;              // renormalise top-k probabilities (norm_topk_prob)
   uint8_t* xterm = nullptr;       // optional: the normed x as MXFP4 B terms (tc_bterm_bytes(H/32))
+  int batch = 1;                  // grid.y = tokens: h/xn + b*H, logits + b*E, idx/wts + b*K, counter + b
 };
 cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s);
 
@@ -206,6 +207,11 @@ struct AttnArgs {
   float* od = nullptr;             // and their block scales [nh*hd/32]
   int nh = 0, nkv = 0, hd = 0, S = 0;
   float scale = 1.0f;
+  // batched decode (B sequences in lockstep, one position): grid.z = batch; sequence b reads
+  // qkv + b*bs_qkv, its caches kc/vc + b*bs_kv, writes out/oq + b*bs_out, od + b*bs_out/32,
+  // part + b*(nkv*S*REP*(hd+2)) and counters cnt + b*nkv
+  int batch = 1;
+  int64_t bs_qkv = 0, bs_kv = 0, bs_out = 0;
 };
 cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s);
 // splits (grid.x) needed to cover `range` attended positions (128 positions per split)
@@ -231,6 +237,79 @@ int argmax_from_key(unsigned long long key);
 // f32 weights, y = W x (+bias)
 cudaError_t launch_gemv_f32(const DevCtx& c, const float* w, int rows, int cols, const float* x,
                             const float* bias, float* y, int accumulate, cudaStream_t s);
+
+// ---- batched decode: B sequences in lockstep at one position (kernels_batch.cu, kernels_moe.cu) ----
+constexpr int kMaxBatch = 32;
+struct BatchState {
+  int pos;                 // position written this step (shared by the batch)
+  int n_ctx;
+  int max_seq;
+  int use_argmax;          // 1: tokens from the previous step's argmax keys, else tok_in
+  int n_log;               // steps appended to the token log
+  int log_row;             // row of this step in the token log
+};
+// h[b] = embed(token b); xq/xd[b] = Q8_0(RMSNorm(h[b]) * norm_w); token log row n_log
+// pos = n_ctx, n_ctx += 1, log row = n_log, n_log += 1 (one thread, before the step's kernels)
+cudaError_t launch_batch_begin(const DevCtx& c, BatchState* st, cudaStream_t s);
+cudaError_t launch_embed_batch(const DevCtx& c, BatchState* st, const int* tok_in, const unsigned long long* keys,
+                               const void* table, int q, int H, int vocab, int B, float* h, int* log,
+                               const float* norm_w, float eps, int8_t* xq, float* xd, cudaStream_t s);
+// Q8_0 weights [rows, cols] x B Q8_0 activations (int8 MMA per 32-block, f32 block sums):
+// y[b][r] = W x_b + bias, or residual[b][r] += W x_b + bias
+struct Q8BatchArgs {
+  const uint8_t* w = nullptr;
+  int rows = 0, cols = 0, B = 0;
+  const int8_t* xq = nullptr;      // [B][cols]
+  const float* xd = nullptr;       // [B][cols / 32]
+  const float* bias = nullptr;
+  float* y = nullptr;              // [B][rows]
+  float* residual = nullptr;       // [B][rows]
+};
+cudaError_t launch_q8_gemm_batch(const DevCtx& c, const Q8BatchArgs& a, cudaStream_t s);
+// h[b] += sum over token b's local experts (ascending id) of w * y[entry]; then the next
+// attention input (xq/xd: Q8_0 of RMSNorm(h[b]) * norm_w) or the LM head input (xf: f32)
+struct BatchCombine {
+  const float* y = nullptr;        // [entries][H] expert outputs (bias included)
+  const int* ent_of = nullptr;     // [B][K] entry of each (token, slot), -1 when not local
+  const int* idx = nullptr;        // [B][K]
+  const float* wts = nullptr;      // [B][K]
+  int K = 0;
+};
+cudaError_t launch_resid_batch(const DevCtx& c, const BatchCombine& bc, float* h, int H, int B, const float* norm_w,
+                               float eps, int8_t* xq, float* xd, float* xf, cudaStream_t s);
+// logits[b] = W xf[b] (+bias), W f16 [V, H]; argmax keys[b] (lowest index on ties)
+struct LmBatchArgs {
+  const uint16_t* w = nullptr;
+  const float* xf = nullptr;       // [B][H] normed
+  int V = 0, H = 0, B = 0;
+  const float* bias = nullptr;
+  void* scratch = nullptr;         // lm_batch_scratch_bytes(V, H)
+  float* logits = nullptr;         // [B][V] or null
+  unsigned long long* keys = nullptr;  // [B]
+};
+int64_t lm_batch_scratch_bytes(int V, int H);
+cudaError_t launch_lmhead_batch(const DevCtx& c, const LmBatchArgs& a, cudaStream_t s);
+// expert FFN of a batch: tokens grouped by expert (each expert streamed once per group of <= 4
+// tokens), K-quant / native MXFP4 experts
+struct GroupMoeArgs {
+  const float* x = nullptr;        // [B][H] normed MoE input
+  const int* idx = nullptr;        // [B][K]
+  int B = 0, K = 0, H = 0, I = 0;
+  int gate_q = Q_Q4_K, down_q = Q_Q6_K;
+  const uint8_t* gate = nullptr;   // [E_local, I, H]
+  const uint8_t* up = nullptr;
+  const uint8_t* down = nullptr;   // [E_local, H, I]
+  const float *gate_b = nullptr, *up_b = nullptr, *down_b = nullptr;
+  int expert_base = 0, n_local = 0;
+  int oai_swiglu = 0;
+  int* grp = nullptr;              // scratch: group_table_words(B, K, n_local)
+  int* ent_tok = nullptr;          // [B*K]
+  int* ent_of = nullptr;           // [B*K] (read by the combine)
+  float* act = nullptr;            // [B*K][I]
+  float* y = nullptr;              // [B*K][H]
+};
+int group_table_words(int B, int K);
+cudaError_t launch_moe_group(const DevCtx& c, const GroupMoeArgs& a, cudaStream_t s);
 
 // ---- Gated DeltaNet / shared expert (kernels_ssm.cu) ----
 struct DeltaNetStep {

@@ -121,52 +121,6 @@ __global__ void rms_norm_kernel(const float* __restrict__ x, const float* __rest
 // 34 bytes (f16 d + 32 int8) at a 2-byte aligned offset, read with aligned words and a
 // 16-bit funnel shift, dotted with __dp4a.  Block sums follow candle's Q8_0 vec_dot:
 // (float)sum_i * d_w * d_x accumulated in f32.
-// Q8_0 quantization of one 32-element block as candle's BlockQ8_0::from_float does:
-// d = amax / 127 (stored as f16), q = roundf(x / d) with the unrounded f32 d.
-__device__ __forceinline__ void quantize_q8_block(const float (&v)[32], int8_t* q, float* d_out) {
-  float amax = 0.f;
-#pragma unroll
-  for (int k = 0; k < 32; ++k) amax = fmaxf(amax, fabsf(v[k]));
-  const float d = amax / 127.0f;
-  const float id = d != 0.0f ? 1.0f / d : 0.0f;
-  int qw[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    uint32_t u = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) u |= ((uint32_t)(uint8_t)(int8_t)roundf(v[4 * k + j] * id)) << (8 * j);
-    qw[k] = (int)u;
-  }
-  int4* dst = reinterpret_cast<int4*>(q);
-  dst[0] = make_int4(qw[0], qw[1], qw[2], qw[3]);
-  dst[1] = make_int4(qw[4], qw[5], qw[6], qw[7]);
-  *d_out = __half2float(__float2half_rn(d));
-}
-
-// Whole-CTA RMSNorm (weights w) of xs[0..H) in shared memory, then Q8_0 quantization into
-// xq / xd (one thread per 32-element block).  red: >= 32 floats of shared scratch.
-__device__ __forceinline__ void cta_rmsnorm_q8(const float* xs, int H, const float* w, float eps, int8_t* xq,
-                                               float* xd, float* red) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) ss += xs[i] * xs[i];
-  ss = warp_sum(ss);
-  if (lane == 0) red[warp] = ss;
-  __syncthreads();
-  float t = 0.f;
-  for (int k = 0; k < nw; ++k) t += red[k];
-  const float inv = 1.0f / sqrtf(t / (float)H + eps);
-  for (int b = threadIdx.x; b < H / 32; b += blockDim.x) {
-    float v[32];
-#pragma unroll
-    for (int k = 0; k < 32; ++k) {
-      const int kk = (k + lane) & 31;   // rotate the start so lanes hit different banks
-      v[kk] = (xs[32 * b + kk] * inv) * w[32 * b + kk];
-    }
-    quantize_q8_block(v, xq + 32 * b, &xd[b]);
-  }
-}
-
 constexpr int kQW = 8;
 constexpr int kQThreads = (kQW + 1) * 32;
 constexpr int kQMaxStages = 8;
@@ -417,6 +371,16 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
   __shared__ int tile_ok;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kh = blockIdx.y, sidx = blockIdx.x, S = gridDim.x;
+  if (blockIdx.z) {   // sequence b of a lockstep batch
+    const int64_t b = blockIdx.z;
+    a.qkv += b * a.bs_qkv;
+    a.kc += b * a.bs_kv;
+    a.vc += b * a.bs_kv;
+    a.out += b * a.bs_out;
+    if (a.oq) { a.oq += b * a.bs_out; a.od += b * a.bs_out / 32; }
+    a.part += b * (int64_t)gridDim.y * S * REP * (HD + 2);
+    a.cnt += b * gridDim.y;
+  }
   // The position comes from the step's first kernel and the cached rows from earlier steps, both
   // complete before the previous kernel started (every kernel lets its dependents launch only after
   // its own wait), so the tile copies go out before this kernel waits for the projections.
@@ -885,7 +849,8 @@ cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s)
   if (a.nkv <= 0 || a.nh % a.nkv || a.S <= 0 || a.rot > a.hd || a.rot % 2) return cudaErrorInvalidValue;
   const int rep = a.nh / a.nkv;
   if ((size_t)a.S * rep > 8192) return cudaErrorInvalidValue;   // merge weights: <= 32 KB of shared memory
-  const dim3 grid((unsigned)a.S, (unsigned)a.nkv);
+  if (a.batch < 1 || (a.batch > 1 && (a.bs_out % 32 || (a.oq && !a.od)))) return cudaErrorInvalidValue;
+  const dim3 grid((unsigned)a.S, (unsigned)a.nkv, (unsigned)a.batch);
   switch (a.hd) {
     case 32: return launch_attn_hd<32>(a, c, rep, grid, s);
     case 64: return launch_attn_hd<64>(a, c, rep, grid, s);

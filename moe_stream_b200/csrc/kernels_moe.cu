@@ -523,6 +523,388 @@ int pick_stages(int stage_bytes) {
   return ns < 2 ? 2 : (ns > 6 ? 6 : ns);
 }
 
+// ---------------- batched decode: tokens grouped by expert ----------------
+// A batch's (token, slot) entries are sorted by local expert (then token) by group_route_kernel and
+// cut into chunks of <= kGT tokens of one expert.  moe_group_kernel streams each chunk's expert
+// tiles once, exactly like moe_mxfp4_phase_kernel, with B column 2t / 2t+1 carrying token t's
+// x_hi / x_lo: MMA accumulator columns 2c, 2c+1 of lane (g, c) are token c, so each lane applies
+// token c's prescale (and, for Q4_K, its block sum) in the per-block epilogue.
+constexpr int kGT = 4;
+constexpr int kRouteThreads = 1024;
+
+struct GroupParams {
+  int mode;                // MODE_GATEUP / MODE_DOWN
+  int fmt;
+  const uint8_t* w0;
+  const uint8_t* w1;
+  int64_t expert_stride;
+  int rb, cols, rows, n_tiles, stage_bytes, ns;
+  const float* x;          // GATEUP: [B][cols] normed input; DOWN: act [entries][cols]
+  const int* grp;          // [0] chunks, then (expert_local, entry_begin, n_tok) per chunk
+  const int* ent_tok;      // token of each entry
+  const float* bias0;
+  const float* bias1;
+  float* out;              // GATEUP: act [entries][rows]; DOWN: y [entries][rows]
+  int oai;
+  uint32_t* err;
+};
+
+__device__ __forceinline__ int block_excl_scan(int v, int* wsum, int* total) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? wsum[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) wsum[lane] = w;   // inclusive warp totals
+    if (lane == nw - 1) *total = w;
+  }
+  __syncthreads();
+  const int r = x - v + (warp > 0 ? wsum[warp - 1] : 0);
+  __syncthreads();
+  return r;
+}
+
+// One CTA: count entries per local expert, place them in (expert, token) order, emit the chunks.
+__global__ void __launch_bounds__(kRouteThreads) group_route_kernel(const int* idx, int n_ent, int K, int expert_base,
+                                                                    int n_local, int* grp, int* ent_tok, int* ent_of,
+                                                                    uint32_t* err) {
+  __shared__ int cnt[kRouteThreads];
+  __shared__ int s_e[kMaxBatch * kMaxK];
+  __shared__ int wsum[32], tot0, tot1;
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int t = threadIdx.x;
+  cnt[t] = 0;
+  for (int i = t; i < n_ent; i += blockDim.x) {
+    const int id = idx[i], e = id - expert_base;
+    if (id < 0) atomicOr(err, EF_BAD_INDEX);
+    s_e[i] = (id >= 0 && e >= 0 && e < n_local) ? e : -1;
+  }
+  __syncthreads();
+  for (int i = t; i < n_ent; i += blockDim.x)
+    if (s_e[i] >= 0) atomicAdd(&cnt[s_e[i]], 1);
+  __syncthreads();
+  const int c = t < n_local ? cnt[t] : 0;
+  const int off = block_excl_scan(c, wsum, &tot0);
+  const int nch = (c + kGT - 1) / kGT;
+  const int coff = block_excl_scan(nch, wsum, &tot1);
+  for (int i = t; i < n_ent; i += blockDim.x) {
+    const int e = s_e[i];
+    if (e < 0) { ent_of[i] = -1; continue; }
+    int rank = 0;
+    for (int j = 0; j < i; ++j) rank += s_e[j] == e;
+    // the entry's slot is its expert's offset (scanned counts, published below) + rank
+    ent_of[i] = rank;   // provisional
+  }
+  __syncthreads();
+  cnt[t] = off;   // expert offsets
+  __syncthreads();
+  for (int i = t; i < n_ent; i += blockDim.x) {
+    const int e = s_e[i];
+    if (e < 0) continue;
+    const int pos = cnt[e] + ent_of[i];
+    ent_of[i] = pos;
+    ent_tok[pos] = i / K;
+  }
+  if (t < n_local)
+    for (int q = 0; q < nch; ++q) {
+      const int j = coff + q;
+      grp[1 + 3 * j] = t;
+      grp[2 + 3 * j] = off + kGT * q;
+      grp[3 + 3 * j] = min(kGT, c - kGT * q);
+    }
+  if (t == 0) grp[0] = tot1;
+}
+
+// B fragments of up to kGT tokens for the K-blocks this warp owns (column 2t: token t's x_hi,
+// 2t + 1: x_lo, each token prescaled by its own power of two); kbs / xsum: token c's (c = lane & 3)
+template <int FMT, int NBW>
+__device__ __forceinline__ void build_bfrag_group(const float* const (&xr)[kGT], int ntok, int nb, int warp, int lane,
+                                                  uint32_t (&bf)[NBW][4], int (&kbs)[NBW], float (&xsum)[NBW]) {
+  const int c = lane & 3, n = lane >> 2, tt = n >> 1, hl = n & 1;
+#pragma unroll
+  for (int i = 0; i < NBW; ++i) {
+    const int b = warp + kCW * i;
+    bf[i][0] = bf[i][1] = bf[i][2] = bf[i][3] = 0u;
+    kbs[i] = 0;
+    xsum[i] = 0.f;
+    if (b < nb) {
+      int kt[kGT];
+      float st = 1.f;
+#pragma unroll
+      for (int t = 0; t < kGT; ++t) {
+        kt[t] = 0;
+        if (t < ntok) {
+          const float v = xr[t][32 * b + lane];
+          if (FMT == FMT_Q4K) {
+            const float xs = warp_sum(v);
+            if (t == c) xsum[i] = xs;
+          }
+          const float m = warp_max(fabsf(v));
+          const int ef = (int)((__float_as_uint(m) >> 23) & 0xffu);
+          kt[t] = (m > 0.f) ? (ef - 126) : 0;
+          if (t == tt) st = __uint_as_float((uint32_t)(127 - kt[t]) << 23);
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < kGT; ++t)
+        if (t == c) kbs[i] = kt[t] * 8388608;
+      if (tt < ntok) {
+        const float* x = xr[tt];
+        const float4 lo4 = *reinterpret_cast<const float4*>(x + 32 * b + 4 * c);
+        const float4 hi4 = *reinterpret_cast<const float4*>(x + 32 * b + 16 + 4 * c);
+        const float va[4] = {lo4.x, lo4.y, lo4.z, lo4.w};
+        const float vb[4] = {hi4.x, hi4.y, hi4.z, hi4.w};
+        __half hv[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float a = (q < 4 ? va[q] : vb[q - 4]) * st;
+          __half ah = __float2half_rn(a);
+          if (hl) ah = __float2half_rn(a - __half2float(ah));
+          hv[q] = ah;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (FMT == FMT_MXFP4) bf[i][q] = pack_half2(hv[q], hv[4 + q]);
+          else bf[i][q] = pack_half2(hv[(q >> 1) * 4 + (q & 1) * 2], hv[(q >> 1) * 4 + (q & 1) * 2 + 1]);
+        }
+      }
+    }
+  }
+}
+
+template <int FMT, int NBW, int RT>
+__global__ void __launch_bounds__(kThreads, 1) moe_group_kernel(GroupParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int kGRed = kGT * kRedRows;   // per-warp partial sums per item
+  uint8_t* stages = smem;
+  const int nrb = p.ns + 1;
+  float* red = reinterpret_cast<float*>(smem + (size_t)p.ns * p.stage_bytes);   // [nrb][kCW][kGRed]
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + (size_t)nrb * kCW * kGRed);
+  uint64_t* empty = full + kMaxStages;
+  uint32_t* red_cnt = reinterpret_cast<uint32_t*>(empty + kMaxStages);
+  int* abort_flag = reinterpret_cast<int*>(red_cnt + kMaxStages + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int b = 0; b <= kMaxStages; ++b) red_cnt[b] = 0u;
+    for (int s = 0; s < p.ns; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kCW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int n_items = p.grp[0] * p.n_tiles;
+  const int begin = (int)((int64_t)blockIdx.x * n_items / gridDim.x);
+  const int end = (int)((int64_t)(blockIdx.x + 1) * n_items / gridDim.x);
+  const int my_n = end - begin;
+  if (my_n <= 0) return;
+
+  if (warp == kCW) {
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      const uint32_t part_bytes = (uint32_t)(16 * p.rb);
+      int issued = 0;
+      for (int j = 0; j < my_n; ++j) {
+        const int s = j % p.ns, n = j / p.ns;
+        if (n > 0 && !mbar_wait(&empty[s], (uint32_t)((n - 1) & 1), p.err, EF_TIMEOUT_EMPTY)) break;
+        const int item = begin + j;
+        const int ch = item / p.n_tiles, t = item % p.n_tiles;
+        const int64_t base = (int64_t)p.grp[1 + 3 * ch] * p.expert_stride + (int64_t)t * part_bytes;
+        uint8_t* dst = stages + (size_t)s * p.stage_bytes;
+        mbar_expect_tx(&full[s], (uint32_t)p.stage_bytes);
+        bulk_g2s_stream(dst, p.w0 + base, part_bytes, &full[s], pol);
+        if (p.mode == MODE_GATEUP) bulk_g2s_stream(dst + part_bytes, p.w1 + base, part_bytes, &full[s], pol);
+        ++issued;
+      }
+      for (int j = max(0, issued - p.ns); j < issued; ++j)
+        mbar_wait(&full[j % p.ns], (uint32_t)((j / p.ns) & 1), p.err, EF_TIMEOUT_FULL);
+    }
+    return;
+  }
+
+  const int nb = p.cols / 32;
+  const int c = lane & 3, g = lane >> 2;
+  uint32_t bf[NBW][4];
+  int kbs[NBW];
+  float xsum[NBW];
+  uint32_t off0[RT], off1[RT];
+#pragma unroll
+  for (int q = 0; q < RT; ++q) {
+    if (p.mode == MODE_GATEUP) {
+      off0[q] = (uint32_t)(8 * q + g) * p.rb;
+      off1[q] = (uint32_t)(16 + 8 * q + g) * p.rb;
+    } else {
+      off0[q] = (uint32_t)(16 * q + g) * p.rb;
+      off1[q] = (uint32_t)(16 * q + g + 8) * p.rb;
+    }
+  }
+  uint32_t bs0[RT], bs1[RT], wa0[RT], wa1[RT], sh0[RT], sh1[RT];
+#pragma unroll
+  for (int q = 0; q < RT; ++q) {
+    bs0[q] = off0[q] + 17u * warp;
+    bs1[q] = off1[q] + 17u * warp;
+    const uint32_t c0 = bs0[q] + 1 + 4 * c, c1 = bs1[q] + 1 + 4 * c;
+    wa0[q] = c0 & ~3u; sh0[q] = (c0 & 3u) * 8u;
+    wa1[q] = c1 & ~3u; sh1[q] = (c1 & 3u) * 8u;
+  }
+  int cur = -1, ntok = 0, ebeg = 0;
+  for (int j = 0; j < my_n; ++j) {
+    if (*reinterpret_cast<volatile int*>(abort_flag)) break;
+    const int s = j % p.ns, n = j / p.ns;
+    const int item = begin + j;
+    const int ch = item / p.n_tiles, t = item % p.n_tiles;
+    if (ch != cur) {
+      ebeg = p.grp[2 + 3 * ch];
+      ntok = p.grp[3 + 3 * ch];
+      const float* xr[kGT];
+#pragma unroll
+      for (int q = 0; q < kGT; ++q) {
+        const int ent = ebeg + min(q, ntok - 1);
+        const int row = p.mode == MODE_GATEUP ? p.ent_tok[ent] : ent;
+        xr[q] = p.x + (size_t)row * p.cols;
+      }
+      build_bfrag_group<FMT, NBW>(xr, ntok, nb, warp, lane, bf, kbs, xsum);
+      cur = ch;
+    }
+    float acc0[RT], acc1[RT];
+#pragma unroll
+    for (int q = 0; q < RT; ++q) acc0[q] = acc1[q] = 0.f;
+    if (!mbar_wait(&full[s], (uint32_t)(n & 1), p.err, EF_TIMEOUT_FULL)) {
+      if (lane == 0) atomicExch(abort_flag, 1);
+      break;
+    }
+    const uint8_t* st = stages + (size_t)s * p.stage_bytes;
+#pragma unroll
+    for (int i = 0; i < NBW; ++i) {
+      const int b = warp + kCW * i;
+      if (b < nb) {
+        if constexpr (FMT == FMT_MXFP4) {
+#pragma unroll
+          for (int q = 0; q < RT; ++q)
+            mx_block(st + bs0[q] + kCW * 17 * i, st + bs1[q] + kCW * 17 * i,
+                     reinterpret_cast<const uint32_t*>(st + wa0[q] + kCW * 17 * i),
+                     reinterpret_cast<const uint32_t*>(st + wa1[q] + kCW * 17 * i), sh0[q], sh1[q], bf[i], kbs[i],
+                     acc0[q], acc1[q]);
+        } else {
+          const float xscale = __int_as_float(max(127 * 8388608 + kbs[i], 0));
+          const int sbk = b >> 3;
+#pragma unroll
+          for (int q = 0; q < RT; ++q) {
+            if constexpr (FMT == FMT_Q4K)
+              q4k_block(st + off0[q] + 144 * sbk, st + off1[q] + 144 * sbk, warp & 7, c, bf[i], xscale, xsum[i],
+                        acc0[q], acc1[q]);
+            else
+              q6k_block(st + off0[q] + 210 * sbk, st + off1[q] + 210 * sbk, (warp & 7) >> 2, warp & 3, c, bf[i],
+                        xscale, acc0[q], acc1[q]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    const int rbuf = j % nrb;
+    float* rw = red + ((size_t)rbuf * kCW + warp) * kGRed + c * kRedRows;   // token c's rows
+#pragma unroll
+    for (int q = 0; q < RT; ++q) {
+      if (p.mode == MODE_GATEUP) { rw[8 * q + g] = acc0[q]; rw[16 + 8 * q + g] = acc1[q]; }
+      else { rw[16 * q + g] = acc0[q]; rw[16 * q + g + 8] = acc1[q]; }
+    }
+    __syncwarp();
+    uint32_t old = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      old = atomicAdd(&red_cnt[rbuf], 1u);
+    }
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old == kCW - 1) {
+      __threadfence_block();
+      const float* rr = red + (size_t)rbuf * kCW * kGRed;
+      const int e = p.grp[1 + 3 * ch];
+      for (int o = lane; o < kGT * 16; o += 32) {
+        const int tk = o >> 4, r = o & 15, row = t * 16 + r;
+        if (tk >= ntok) continue;
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int w = 0; w < kCW; ++w) {
+          a0 += rr[w * kGRed + tk * kRedRows + r];
+          if (p.mode == MODE_GATEUP) a1 += rr[w * kGRed + tk * kRedRows + 16 + r];
+        }
+        const size_t ent = (size_t)(ebeg + tk);
+        if (p.bias0) a0 += p.bias0[(size_t)e * p.rows + row];
+        if (p.mode == MODE_GATEUP) {
+          if (p.bias1) a1 += p.bias1[(size_t)e * p.rows + row];
+          p.out[ent * p.rows + row] = p.oai ? swiglu_oai(a0, a1) : silu_mul(a0, a1);
+        } else {
+          p.out[ent * p.rows + row] = a0;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) red_cnt[rbuf] = 0u;
+    }
+  }
+}
+
+template <int FMT, int NBW, int RT>
+cudaError_t launch_group(const DevCtx& c, const GroupParams& p, cudaStream_t s) {
+  const size_t smem = (size_t)p.ns * p.stage_bytes + (size_t)(p.ns + 1) * kCW * kGT * kRedRows * sizeof(float) +
+                      2 * kMaxStages * 8 + (kMaxStages + 1) * 4 + 16;
+  cudaError_t e = cudaFuncSetAttribute(moe_group_kernel<FMT, NBW, RT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)c.sm_count);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, moe_group_kernel<FMT, NBW, RT>, p);
+}
+
+template <int FMT, int RT>
+cudaError_t group_nbw(const DevCtx& c, const GroupParams& p, cudaStream_t s) {
+  const int nbw = (p.cols / 32 + kCW - 1) / kCW;
+  if (nbw <= 1) return launch_group<FMT, 1, RT>(c, p, s);
+  if (nbw <= 2) return launch_group<FMT, 2, RT>(c, p, s);
+  if (nbw <= 4) return launch_group<FMT, 4, RT>(c, p, s);
+  if (nbw <= 6) return launch_group<FMT, 6, RT>(c, p, s);
+  if (nbw <= 8) return launch_group<FMT, 8, RT>(c, p, s);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t dispatch_group(const DevCtx& c, const GroupParams& p, cudaStream_t s) {
+  const bool gu = p.mode == MODE_GATEUP;
+  if (p.fmt == FMT_MXFP4) return gu ? group_nbw<FMT_MXFP4, 2>(c, p, s) : group_nbw<FMT_MXFP4, 1>(c, p, s);
+  if (p.fmt == FMT_Q4K) return gu ? group_nbw<FMT_Q4K, 2>(c, p, s) : group_nbw<FMT_Q4K, 1>(c, p, s);
+  if (p.fmt == FMT_Q6K) return gu ? group_nbw<FMT_Q6K, 2>(c, p, s) : group_nbw<FMT_Q6K, 1>(c, p, s);
+  return cudaErrorInvalidValue;
+}
+
+// stages + the (kGT-wide) reduction buffers within ~220 KB
+int pick_group_stages(int stage_bytes) {
+  const int red = kCW * kGT * kRedRows * 4;
+  int ns = (220 * 1024 - red) / (stage_bytes + red);
+  return ns < 2 ? 2 : (ns > 6 ? 6 : ns);
+}
+
 // ---------------- router: RMSNorm + GEMV + bias + mask + top-k + softmax ----------------
 // One CTA per expert row: each recomputes the RMSNorm of h (L2-resident), dots its router row
 // and writes one logit; the last CTA to finish selects the top-k and the routing weights.
@@ -552,6 +934,15 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, ui
   __shared__ uint32_t last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x;
+  if (blockIdx.y) {   // token b of a batch
+    const int b = blockIdx.y;
+    if (a.h) a.h += (size_t)b * a.H;
+    a.xn += (size_t)b * a.H;
+    a.logits += (size_t)b * a.E;
+    a.idx += b * a.K;
+    a.wts += b * a.K;
+    a.counter += b;
+  }
   const float* wr = a.w + (size_t)e * a.H;
   if (row_async && threadIdx.x == 0) {   // weights do not depend on the previous kernel
     mbar_init(&bar, 1);
@@ -706,7 +1097,9 @@ cudaError_t launch_moe_combine(const DevCtx& c, const PendingCombine& pc, int H,
 }
 
 cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s) {
-  if (a.K < 1 || a.K > kMaxK || a.K > a.E || a.E > kRouterMaxE || !a.counter) return cudaErrorInvalidValue;
+  if (a.K < 1 || a.K > kMaxK || a.K > a.E || a.E > kRouterMaxE || !a.counter || a.batch < 1 ||
+      (a.batch > 1 && a.xterm))
+    return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   // the router row goes to shared memory by a bulk copy when it is 16-byte aligned (all rows are
   // when the matrix is and H % 4 == 0)
@@ -716,7 +1109,7 @@ cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s) 
     cudaError_t e = cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  cfg.gridDim = dim3((unsigned)a.E);
+  cfg.gridDim = dim3((unsigned)a.E, (unsigned)a.batch);
   cfg.blockDim = dim3(kRouterThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -757,6 +1150,44 @@ cudaError_t launch_moe_mxfp4(const DevCtx& c, const MoeArgs& a, cudaStream_t s) 
   pc.partial = a.partial; pc.idx = a.idx; pc.wts = a.wts; pc.K = a.K; pc.expert_base = a.expert_base;
   pc.n_local = a.n_local;
   return launch_moe_combine(c, pc, a.H, a.h, a.out, s);
+}
+
+int group_table_words(int B, int K) { return 1 + 3 * B * K; }
+
+cudaError_t launch_moe_group(const DevCtx& c, const GroupMoeArgs& a, cudaStream_t s) {
+  const int n_ent = a.B * a.K;
+  if (a.B < 1 || a.B > kMaxBatch || a.K < 1 || a.K > kMaxK || a.n_local < 0 || a.n_local > kRouteThreads ||
+      a.H % 64 || a.I % 32)
+    return cudaErrorInvalidValue;
+  const int fg = fmt_of(a.gate_q), fd = fmt_of(a.down_q);
+  if (fg < 0 || fd < 0) return cudaErrorInvalidValue;
+  const int rbg = (int)row_bytes(a.gate_q, a.H), rbd = (int)row_bytes(a.down_q, a.I);
+  if (rbg <= 0 || rbd <= 0) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kRouteThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, group_route_kernel, a.idx, n_ent, a.K, a.expert_base, a.n_local, a.grp,
+                                     a.ent_tok, a.ent_of, c.err);
+  if (e != cudaSuccess) return e;
+  GroupParams p = {};
+  p.grp = a.grp; p.ent_tok = a.ent_tok; p.oai = a.oai_swiglu; p.err = c.err;
+  p.mode = MODE_GATEUP; p.fmt = fg; p.w0 = a.gate; p.w1 = a.up; p.expert_stride = (int64_t)a.I * rbg; p.rb = rbg;
+  p.cols = a.H; p.rows = a.I; p.n_tiles = a.I / 16; p.stage_bytes = 32 * rbg; p.ns = pick_group_stages(p.stage_bytes);
+  p.x = a.x; p.bias0 = a.gate_b; p.bias1 = a.up_b; p.out = a.act;
+  if ((16 * rbg) % 16 || p.expert_stride % 16 || a.I % 16) return cudaErrorInvalidValue;
+  e = dispatch_group(c, p, s);
+  if (e != cudaSuccess) return e;
+  p.mode = MODE_DOWN; p.fmt = fd; p.w0 = a.down; p.w1 = nullptr; p.expert_stride = (int64_t)a.H * rbd; p.rb = rbd;
+  p.cols = a.I; p.rows = a.H; p.n_tiles = a.H / 16; p.stage_bytes = 16 * rbd; p.ns = pick_group_stages(p.stage_bytes);
+  p.x = a.act; p.bias0 = a.down_b; p.bias1 = nullptr; p.out = a.y;
+  if ((16 * rbd) % 16 || p.expert_stride % 16) return cudaErrorInvalidValue;
+  return dispatch_group(c, p, s);
 }
 
 }  // namespace ms

@@ -173,6 +173,31 @@ static NcclApi* nccl_api() {
   return api.ok ? &api : nullptr;
 }
 
+// Lockstep batch of B sequences sharing one position (Engine::forward over input_ids [B, T]).
+struct BatchRt {
+  int B = 0;
+  BatchState* st = nullptr;         // device
+  BatchState* h_st = nullptr;       // pinned
+  int* h_tok = nullptr;             // pinned token staging [max_seq][B] + constants 0, 1
+  unsigned long long* h_keys = nullptr;   // pinned [B]
+  int* tok_in = nullptr;            // [B]
+  unsigned long long* keys = nullptr;     // [B] argmax keys of the last step
+  int* log = nullptr;               // [max_seq][B] tokens fed per step
+  float *h = nullptr, *qkv = nullptr, *attn = nullptr, *xn = nullptr, *rlog = nullptr, *wts = nullptr;
+  float *act = nullptr, *y = nullptr, *xf = nullptr, *logits = nullptr, *part = nullptr;
+  int8_t *xq_h = nullptr, *xq_a = nullptr;
+  float *xd_h = nullptr, *xd_a = nullptr;
+  int *idx = nullptr, *grp = nullptr, *ent_tok = nullptr, *ent_of = nullptr;
+  uint32_t *attn_cnt = nullptr, *router_cnt = nullptr;
+  std::vector<float*> kc, vc;
+  void* lm_scratch = nullptr;
+  int64_t bs_kv_full = 0;
+  std::vector<void*> allocs;
+  cudaGraphExec_t graph = nullptr;
+  int seq = 0;
+  int kernels_per_step = 0;
+};
+
 struct ms_model {
   ms_ctx* ctx = nullptr;
   ncclComm_t comm = nullptr;        // expert-parallel communicator (ep_size > 1)
@@ -213,6 +238,7 @@ struct ms_model {
   uint8_t* act_terms = nullptr;   // [K] B terms of the expert activations
   float* tc_part = nullptr;       // split-K partial sums
   uint32_t* tc_cnt = nullptr;
+  BatchRt* bt = nullptr;          // lockstep batch state (ms_model_batch_open)
 
   template <class T>
   ms_status alloc(T** p, size_t bytes, bool zero = true) {
@@ -562,6 +588,134 @@ struct GgufParser {
     }
   }
 };
+
+}  // namespace
+
+// lockstep batch helpers (the entry points are below)
+namespace {
+
+void batch_free(ms_model* m) {
+  BatchRt* b = m->bt;
+  if (!b) return;
+  if (b->graph) cudaGraphExecDestroy(b->graph);
+  for (void* p : b->allocs) cudaFree(p);
+  if (b->h_st) cudaFreeHost(b->h_st);
+  if (b->h_tok) cudaFreeHost(b->h_tok);
+  if (b->h_keys) cudaFreeHost(b->h_keys);
+  delete b;
+  m->bt = nullptr;
+}
+
+template <class T>
+ms_status balloc(ms_model* m, T** p, size_t bytes) {
+  void* q = nullptr;
+  cudaError_t e = cudaMalloc(&q, bytes ? bytes : 16);
+  if (e != cudaSuccess) return cuda_fail(m->ctx, e, "cudaMalloc (batch)");
+  e = cudaMemset(q, 0, bytes ? bytes : 16);
+  if (e != cudaSuccess) { cudaFree(q); return cuda_fail(m->ctx, e, "cudaMemset (batch)"); }
+  m->bt->allocs.push_back(q);
+  *p = reinterpret_cast<T*>(q);
+  return MS_OK;
+}
+
+ms_status enqueue_batch_step(ms_model* m, cudaStream_t s) {
+  const ms_model_config& c = m->cfg;
+  const DevCtx& dc = m->ctx->dc;
+  BatchRt& b = *m->bt;
+  const int H = c.hidden, Dq = q_dim(c), Dkv = kv_dim(c), B = b.B;
+  int nk = 0;
+#define BLAUNCH(call)                                                \
+  do {                                                               \
+    cudaError_t e_ = (call);                                         \
+    if (e_ != cudaSuccess) return cuda_fail(m->ctx, e_, #call);      \
+    ++nk;                                                            \
+  } while (0)
+  BLAUNCH(launch_batch_begin(dc, b.st, s));
+  BLAUNCH(launch_embed_batch(dc, b.st, b.tok_in, b.keys, m->embd, m->embd_q, H, c.vocab, B, b.h, b.log,
+                             m->L[0].attn_norm, c.eps, b.xq_h, b.xd_h, s));
+  for (int li = 0; li < c.layers; ++li) {
+    LayerW& Lw = m->L[li];
+    Q8BatchArgs qa;
+    qa.w = Lw.wqkv; qa.rows = Dq + 2 * Dkv; qa.cols = H; qa.B = B; qa.xq = b.xq_h; qa.xd = b.xd_h; qa.bias = Lw.bqkv;
+    qa.y = b.qkv;
+    BLAUNCH(launch_q8_gemm_batch(dc, qa, s));
+    AttnArgs aa;
+    aa.qkv = b.qkv; aa.q_norm = Lw.qn; aa.k_norm = Lw.kn; aa.eps = c.eps; aa.cos_t = m->cos_t; aa.sin_t = m->sin_t;
+    aa.rot = c.rot_dim; aa.pos = &b.st->pos; aa.kc = b.kc[li]; aa.vc = b.vc[li]; aa.cap = Lw.cap; aa.window = Lw.window;
+    aa.sinks = Lw.sinks; aa.part = b.part; aa.cnt = b.attn_cnt; aa.out = b.attn; aa.nh = c.heads; aa.nkv = c.kv_heads;
+    aa.hd = c.head_dim; aa.S = Lw.window ? m->splits_swa : m->splits_full;
+    aa.scale = (float)(1.0 / std::sqrt((double)c.head_dim)); aa.oq = b.xq_a; aa.od = b.xd_a;
+    aa.batch = B; aa.bs_qkv = Dq + 2 * Dkv; aa.bs_kv = (int64_t)c.kv_heads * Lw.cap * c.head_dim; aa.bs_out = Dq;
+    BLAUNCH(launch_attention(dc, aa, s));
+    Q8BatchArgs oa;
+    oa.w = Lw.wo; oa.rows = H; oa.cols = Dq; oa.B = B; oa.xq = b.xq_a; oa.xd = b.xd_a; oa.bias = Lw.bo;
+    oa.residual = b.h;
+    BLAUNCH(launch_q8_gemm_batch(dc, oa, s));
+    RouterArgs ra;
+    ra.h = b.h; ra.norm_w = Lw.post_norm; ra.eps = c.eps; ra.xn = b.xn; ra.w = Lw.router_w; ra.b = Lw.router_b;
+    ra.mask = Lw.mask; ra.logits = b.rlog; ra.idx = b.idx; ra.wts = b.wts; ra.counter = b.router_cnt; ra.H = H;
+    ra.E = c.experts; ra.K = c.top_k; ra.softmax_weight = c.arch == MS_ARCH_GPT_OSS; ra.normalize = c.norm_topk_prob;
+    ra.batch = B;
+    BLAUNCH(launch_router(dc, ra, s));
+    GroupMoeArgs ga;
+    ga.x = b.xn; ga.idx = b.idx; ga.B = B; ga.K = c.top_k; ga.H = H; ga.I = c.inter; ga.gate_q = Lw.gate_q;
+    ga.down_q = Lw.down_q; ga.gate = Lw.gate; ga.up = Lw.up; ga.down = Lw.down; ga.gate_b = Lw.gate_b;
+    ga.up_b = Lw.up_b; ga.down_b = Lw.down_b; ga.expert_base = m->expert_base; ga.n_local = m->n_local;
+    ga.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ga.grp = b.grp; ga.ent_tok = b.ent_tok; ga.ent_of = b.ent_of;
+    ga.act = b.act; ga.y = b.y;
+    BLAUNCH(launch_moe_group(dc, ga, s));
+    nk += 2;   // route, gate_up, down
+    BatchCombine bc;
+    bc.y = b.y; bc.ent_of = b.ent_of; bc.idx = b.idx; bc.wts = b.wts; bc.K = c.top_k;
+    const bool last = li + 1 == c.layers;
+    BLAUNCH(launch_resid_batch(dc, bc, b.h, H, B, last ? m->out_norm : m->L[li + 1].attn_norm, c.eps,
+                               last ? nullptr : b.xq_h, last ? nullptr : b.xd_h, last ? b.xf : nullptr, s));
+  }
+  LmBatchArgs la;
+  la.w = m->out_w; la.xf = b.xf; la.V = c.vocab; la.H = H; la.B = B; la.bias = m->out_b; la.scratch = b.lm_scratch;
+  la.logits = b.logits; la.keys = b.keys;
+  BLAUNCH(launch_lmhead_batch(dc, la, s));
+  nk += 2;   // prep, GEMM, key reduction
+#undef BLAUNCH
+  b.kernels_per_step = nk;
+  return MS_OK;
+}
+
+ms_status run_batch_step(ms_model* m) {
+  BatchRt& b = *m->bt;
+  cudaStream_t s = m->ctx->stream;
+  if (!m->use_graph) return enqueue_batch_step(m, s);
+  if (!b.graph) {
+    cudaGraph_t g = nullptr;
+    cudaStream_t cs = m->ctx->own;
+    MS_CUDA(m->ctx, cudaStreamSynchronize(s));
+    MS_CUDA(m->ctx, cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    ms_status st = enqueue_batch_step(m, cs);
+    cudaError_t e = cudaStreamEndCapture(cs, &g);
+    if (st != MS_OK) { if (g) cudaGraphDestroy(g); return st; }
+    if (e != cudaSuccess) return cuda_fail(m->ctx, e, "cudaStreamEndCapture");
+    e = cudaGraphInstantiate(&b.graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) { b.graph = nullptr; return cuda_fail(m->ctx, e, "cudaGraphInstantiate"); }
+  }
+  MS_CUDA(m->ctx, cudaGraphLaunch(b.graph, s));
+  return MS_OK;
+}
+
+ms_status batch_feed(ms_model* m, int use_argmax) {
+  BatchRt& b = *m->bt;
+  const int* src = &b.h_tok[(size_t)m->cfg.max_seq_len * b.B + (use_argmax ? 1 : 0)];
+  MS_CUDA(m->ctx, cudaMemcpyAsync(&b.st->use_argmax, src, sizeof(int), cudaMemcpyHostToDevice, m->ctx->stream));
+  return MS_OK;
+}
+
+ms_status batch_ready(ms_model* m, int n_steps) {
+  if (!m) return MS_ERR_INVALID_ARG;
+  if (!m->bt) return fail(m->ctx, MS_ERR_STATE, "no batch open (ms_model_batch_open)");
+  if (m->bt->seq + n_steps > m->cfg.max_seq_len) return fail(m->ctx, MS_ERR_SHAPE, "batch sequence exceeds max_seq_len");
+  cudaSetDevice(m->ctx->device);
+  return MS_OK;
+}
 
 }  // namespace
 
@@ -997,12 +1151,180 @@ ms_status ms_model_finalize(ms_model* m) {
   return MS_OK;
 }
 
+// ---------------- lockstep batch (Engine::forward over input_ids [B, T], engine.rs:1869-2006) ----------------
+
+ms_status ms_model_batch_open(ms_model* m, int B) {
+  if (!m || B < 1 || B > kMaxBatch) return MS_ERR_INVALID_ARG;
+  if (!m->finalized) return fail(m->ctx, MS_ERR_STATE, "batch before finalize");
+  const ms_model_config& c = m->cfg;
+  if (c.ep_size > 1) return fail(m->ctx, MS_ERR_STATE, "batched decode runs on one GPU (ep_size 1)");
+  for (int li = 0; li < c.layers; ++li)
+    if (m->L[li].tc || !m->L[li].gate)
+      return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE,
+                  "batched decode needs native-layout experts (K-quants, or MXFP4 with MS_MOE_TC=0)");
+  const int H = c.hidden, Dq = q_dim(c), Dkv = kv_dim(c), rep = c.heads / c.kv_heads;
+  if ((Dq + 2 * Dkv) % 16 || H % 16) return fail(m->ctx, MS_ERR_SHAPE, "batched projections need rows %% 16");
+  cudaSetDevice(m->ctx->device);
+  MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+  batch_free(m);
+  m->bt = new BatchRt();
+  BatchRt& b = *m->bt;
+  b.B = B;
+  const int S = std::max(m->splits_full, m->splits_swa), EK = B * c.top_k;
+  ms_status s = MS_OK;
+  s = s ? s : balloc(m, &b.st, sizeof(BatchState));
+  s = s ? s : balloc(m, &b.tok_in, (size_t)B * 4);
+  s = s ? s : balloc(m, &b.keys, (size_t)B * 8);
+  s = s ? s : balloc(m, &b.log, (size_t)(c.max_seq_len + 1) * B * 4);
+  s = s ? s : balloc(m, &b.h, (size_t)B * H * 4);
+  s = s ? s : balloc(m, &b.qkv, (size_t)B * (Dq + 2 * Dkv) * 4);
+  s = s ? s : balloc(m, &b.attn, (size_t)B * Dq * 4);
+  s = s ? s : balloc(m, &b.xn, (size_t)B * H * 4);
+  s = s ? s : balloc(m, &b.rlog, (size_t)B * c.experts * 4);
+  s = s ? s : balloc(m, &b.idx, (size_t)EK * 4);
+  s = s ? s : balloc(m, &b.wts, (size_t)EK * 4);
+  s = s ? s : balloc(m, &b.grp, (size_t)group_table_words(B, c.top_k) * 4);
+  s = s ? s : balloc(m, &b.ent_tok, (size_t)EK * 4);
+  s = s ? s : balloc(m, &b.ent_of, (size_t)EK * 4);
+  s = s ? s : balloc(m, &b.act, (size_t)EK * c.inter * 4);
+  s = s ? s : balloc(m, &b.y, (size_t)EK * H * 4);
+  s = s ? s : balloc(m, &b.xf, (size_t)B * H * 4);
+  s = s ? s : balloc(m, &b.logits, (size_t)B * c.vocab * 4);
+  s = s ? s : balloc(m, &b.part, (size_t)B * c.kv_heads * S * rep * (c.head_dim + 2) * 4);
+  s = s ? s : balloc(m, &b.xq_h, (size_t)B * H + 64);
+  s = s ? s : balloc(m, &b.xd_h, (size_t)B * H / 32 * 4 + 64);
+  s = s ? s : balloc(m, &b.xq_a, (size_t)B * Dq + 64);
+  s = s ? s : balloc(m, &b.xd_a, (size_t)B * Dq / 32 * 4 + 64);
+  s = s ? s : balloc(m, &b.attn_cnt, (size_t)(B * c.kv_heads + 16) * 4);
+  s = s ? s : balloc(m, &b.router_cnt, (size_t)(B + 16) * 4);
+  s = s ? s : balloc(m, &b.lm_scratch, (size_t)lm_batch_scratch_bytes(c.vocab, H));
+  b.kc.resize(c.layers);
+  b.vc.resize(c.layers);
+  for (int li = 0; li < c.layers && s == MS_OK; ++li) {
+    const size_t kvb = (size_t)B * c.kv_heads * m->L[li].cap * c.head_dim * 4;
+    s = balloc(m, &b.kc[li], kvb);
+    s = s ? s : balloc(m, &b.vc[li], kvb);
+  }
+  if (s != MS_OK) { batch_free(m); return s; }
+  cudaError_t e = cudaMallocHost(&b.h_st, sizeof(BatchState));
+  if (e == cudaSuccess) e = cudaMallocHost(&b.h_tok, ((size_t)c.max_seq_len * B + 4) * 4);
+  if (e == cudaSuccess) e = cudaMallocHost(&b.h_keys, (size_t)B * 8);
+  if (e != cudaSuccess) { batch_free(m); return cuda_fail(m->ctx, e, "cudaMallocHost (batch)"); }
+  b.h_tok[(size_t)c.max_seq_len * B] = 0;
+  b.h_tok[(size_t)c.max_seq_len * B + 1] = 1;
+  memset(b.h_st, 0, sizeof(BatchState));
+  b.h_st->max_seq = c.max_seq_len;
+  MS_CUDA(m->ctx, cudaMemcpy(b.st, b.h_st, sizeof(BatchState), cudaMemcpyHostToDevice));
+  return MS_OK;
+}
+
+ms_status ms_model_batch_close(ms_model* m) {
+  if (!m) return MS_ERR_INVALID_ARG;
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  batch_free(m);
+  return MS_OK;
+}
+
+ms_status ms_model_batch_clear(ms_model* m) {
+  ms_status st = batch_ready(m, 0);
+  if (st != MS_OK) return st;
+  BatchRt& b = *m->bt;
+  MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+  memset(b.h_st, 0, sizeof(BatchState));
+  b.h_st->max_seq = m->cfg.max_seq_len;
+  MS_CUDA(m->ctx, cudaMemcpy(b.st, b.h_st, sizeof(BatchState), cudaMemcpyHostToDevice));
+  b.seq = 0;
+  return MS_OK;
+}
+
+ms_status ms_model_batch_forward(ms_model* m, const int32_t* tokens, int T, int32_t* next) {
+  if (!tokens || T <= 0) return MS_ERR_INVALID_ARG;
+  ms_status st = batch_ready(m, T);
+  if (st != MS_OK) return st;
+  BatchRt& b = *m->bt;
+  cudaStream_t s = m->ctx->stream;
+  MS_CUDA(m->ctx, cudaStreamSynchronize(s));   // pinned staging is reused below
+  for (int i = 0; i < b.B; ++i)
+    for (int t = 0; t < T; ++t) {
+      const int32_t tok = tokens[(size_t)i * T + t];
+      if (tok < 0 || tok >= m->cfg.vocab) return fail(m->ctx, MS_ERR_INVALID_ARG, "token %d out of range", tok);
+      b.h_tok[(size_t)t * b.B + i] = tok;
+    }
+  st = batch_feed(m, 0);
+  if (st != MS_OK) return st;
+  for (int t = 0; t < T; ++t) {
+    MS_CUDA(m->ctx, cudaMemcpyAsync(b.tok_in, &b.h_tok[(size_t)t * b.B], (size_t)b.B * 4, cudaMemcpyHostToDevice, s));
+    st = run_batch_step(m);
+    if (st != MS_OK) return st;
+  }
+  b.seq += T;
+  MS_CUDA(m->ctx, cudaMemcpyAsync(b.h_keys, b.keys, (size_t)b.B * 8, cudaMemcpyDeviceToHost, s));
+  st = ms_sync(m->ctx);
+  if (st != MS_OK) return st;
+  if (next)
+    for (int i = 0; i < b.B; ++i) next[i] = argmax_from_key(b.h_keys[i]);
+  return MS_OK;
+}
+
+ms_status ms_model_batch_decode_steps_device(ms_model* m, int n) {
+  if (n < 0) return MS_ERR_INVALID_ARG;
+  ms_status st = batch_ready(m, n);
+  if (st != MS_OK) return st;
+  st = batch_feed(m, 1);
+  if (st != MS_OK) return st;
+  for (int i = 0; i < n; ++i) {
+    st = run_batch_step(m);
+    if (st != MS_OK) return st;
+  }
+  m->bt->seq += n;
+  return MS_OK;
+}
+
+ms_status ms_model_batch_next_tokens(ms_model* m, int32_t* next) {
+  if (!next) return MS_ERR_INVALID_ARG;
+  ms_status st = batch_ready(m, 0);
+  if (st != MS_OK) return st;
+  BatchRt& b = *m->bt;
+  MS_CUDA(m->ctx, cudaMemcpyAsync(b.h_keys, b.keys, (size_t)b.B * 8, cudaMemcpyDeviceToHost, m->ctx->stream));
+  st = ms_sync(m->ctx);
+  if (st != MS_OK) return st;
+  for (int i = 0; i < b.B; ++i) next[i] = argmax_from_key(b.h_keys[i]);
+  return MS_OK;
+}
+
+ms_status ms_model_batch_token_log(ms_model* m, int32_t* out, int max_rows, int* n_rows) {
+  if (!out || !n_rows || max_rows < 0) return MS_ERR_INVALID_ARG;
+  ms_status st = batch_ready(m, 0);
+  if (st != MS_OK) return st;
+  BatchRt& b = *m->bt;
+  MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+  BatchState h;
+  MS_CUDA(m->ctx, cudaMemcpy(&h, b.st, sizeof h, cudaMemcpyDeviceToHost));
+  const int k = std::min(std::min(h.n_log, max_rows), m->cfg.max_seq_len);
+  if (k > 0) MS_CUDA(m->ctx, cudaMemcpy(out, b.log, (size_t)k * b.B * 4, cudaMemcpyDeviceToHost));
+  *n_rows = k;
+  return MS_OK;
+}
+
+ms_status ms_model_batch_last_logits(ms_model* m, float* out) {
+  if (!out) return MS_ERR_INVALID_ARG;
+  ms_status st = batch_ready(m, 0);
+  if (st != MS_OK) return st;
+  MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+  MS_CUDA(m->ctx, cudaMemcpy(out, m->bt->logits, (size_t)m->bt->B * m->cfg.vocab * 4, cudaMemcpyDeviceToHost));
+  return MS_OK;
+}
+
+int ms_model_batch_kernels_per_step(const ms_model* m) { return m && m->bt ? m->bt->kernels_per_step : 0; }
+
 ms_status ms_model_destroy(ms_model* m) {
   if (!m) return MS_ERR_INVALID_ARG;
   cudaSetDevice(m->ctx->device);
   cudaStreamSynchronize(m->ctx->stream);
   if (m->graph) cudaGraphExecDestroy(m->graph);
   if (m->comm) nccl_api()->comm_destroy(m->comm);
+  batch_free(m);
   for (void* p : m->allocs) cudaFree(p);
   if (m->h_tok) cudaFreeHost(m->h_tok);
   if (m->h_st) cudaFreeHost(m->h_st);

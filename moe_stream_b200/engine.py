@@ -335,6 +335,64 @@ class Engine:
     def kernels_per_step(self) -> int:
         return lib().ms_model_kernels_per_step(self.h)
 
+    # ---- lockstep batch: B sequences at one shared position (forward over input_ids [B, T]) ----
+    def batch_open(self, batch: int) -> None:
+        check(lib().ms_model_batch_open(self.h, batch), self.ctx.h)
+        self.batch = batch
+
+    def batch_close(self) -> None:
+        check(lib().ms_model_batch_close(self.h), self.ctx.h)
+
+    def batch_clear(self) -> None:
+        check(lib().ms_model_batch_clear(self.h), self.ctx.h)
+
+    def batch_forward(self, tokens) -> list:
+        """tokens [B, T]; returns each sequence's greedy next token after the last position"""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        if t.ndim != 2 or t.shape[0] != self.batch:
+            raise ValueError(f"tokens must be [{self.batch}, T]")
+        nxt = np.empty(self.batch, dtype=np.int32)
+        check(lib().ms_model_batch_forward(self.h, t.ctypes.data_as(C.POINTER(C.c_int32)), t.shape[1],
+                                           nxt.ctypes.data_as(C.POINTER(C.c_int32))), self.ctx.h)
+        return nxt.tolist()
+
+    def batch_decode_steps_device(self, n: int) -> None:
+        check(lib().ms_model_batch_decode_steps_device(self.h, n), self.ctx.h)
+
+    def batch_next_tokens(self) -> list:
+        nxt = np.empty(self.batch, dtype=np.int32)
+        check(lib().ms_model_batch_next_tokens(self.h, nxt.ctypes.data_as(C.POINTER(C.c_int32))), self.ctx.h)
+        return nxt.tolist()
+
+    def batch_token_log(self) -> np.ndarray:
+        """tokens fed per step, [steps, B]"""
+        cap = self.config.max_seq_len
+        out = np.empty((cap, self.batch), dtype=np.int32)
+        n = C.c_int()
+        check(lib().ms_model_batch_token_log(self.h, out.ctypes.data_as(C.POINTER(C.c_int32)), cap, C.byref(n)),
+              self.ctx.h)
+        return out[:n.value]
+
+    def batch_generate(self, prompts, max_new_tokens: int) -> np.ndarray:
+        """Greedy decode of B equal-length prompts in lockstep; returns [B, max_new_tokens]."""
+        self.batch_clear()
+        p = np.ascontiguousarray(prompts, dtype=np.int32)
+        self.batch_forward(p)
+        self.batch_decode_steps_device(max_new_tokens - 1)
+        last = self.batch_next_tokens()
+        log = self.batch_token_log()
+        gen = log[p.shape[1]:].T if max_new_tokens > 1 else np.empty((self.batch, 0), np.int32)
+        return np.concatenate([gen, np.asarray(last, np.int32)[:, None]], axis=1)
+
+    def batch_last_logits(self) -> np.ndarray:
+        o = np.empty((self.batch, self.config.vocab), dtype=np.float32)
+        check(lib().ms_model_batch_last_logits(self.h, o.ctypes.data_as(C.POINTER(C.c_float))), self.ctx.h)
+        return o
+
+    @property
+    def batch_kernels_per_step(self) -> int:
+        return lib().ms_model_batch_kernels_per_step(self.h)
+
     def close(self) -> None:
         if getattr(self, "h", None):
             if getattr(self.ctx, "h", None):   # a closed context already freed its models

@@ -480,3 +480,75 @@ def test_shared_expert(ctx, orc, hidden, inter, gu_q, down_q, gated):
                       hidden, inter, dev(x), y)
     ctx.sync()
     assert rel_err(y.cpu().numpy(), want) < REL_TOL
+
+
+# ---- lockstep batch decode (Engine::forward over input_ids [B, T], engine.rs:1869-2006) ----
+
+
+def _batch_prompts(spec, B, T, seed):
+    return np.stack([synth.prompt_ids(spec, T, seed=seed + b) for b in range(B)])
+
+
+def test_batch_decode_qwen3_matches_oracle_per_sequence(ctx, orc, tiny_qwen_path):
+    """B = 5 sequences (not a multiple of the 4-token MMA groups): each one's greedy tokens equal
+    the oracle's single-sequence generation; last-position logits match the bs1 engine"""
+    from moe_stream_b200.engine import Engine
+    B, T, N = 5, 12, 10
+    prompts = _batch_prompts(synth.TINY_QWEN3, B, T, 40)
+    eng = Engine.open(tiny_qwen_path, max_seq_len=128, ctx=ctx)
+    eng.batch_open(B)
+    got = eng.batch_generate(prompts, N)
+    om = orc.Model(tiny_qwen_path, max_seq_len=128)
+    for b in range(B):
+        om.clear_cache()
+        assert got[b].tolist() == om.generate(prompts[b], N).tolist(), b
+    om.close()
+    eng.batch_clear()
+    eng.batch_forward(prompts)
+    bl = eng.batch_last_logits()
+    for b in (0, B - 1):
+        eng.clear_cache()
+        assert rel_err(bl[b], eng.forward(prompts[b])) < REL_TOL
+    eng.close()
+
+
+def test_batch_decode_gpt_oss_native_mxfp4_sliding_window(ctx, orc, tmp_path, monkeypatch):
+    """native-layout MXFP4 experts with biases and OAI SwiGLU, sinks, 8-slot SWA ring passed"""
+    from moe_stream_b200.engine import Engine
+    monkeypatch.setenv("MS_MOE_TC", "0")
+    p = str(tmp_path / "g.gguf")
+    synth.write_model(p, synth.TINY_GPT_OSS, seed=5)
+    B, T, N = 3, 20, 12
+    prompts = _batch_prompts(synth.TINY_GPT_OSS, B, T, 70)
+    eng = Engine.open(p, max_seq_len=128, ctx=ctx)
+    eng.batch_open(B)
+    got = eng.batch_generate(prompts, N)
+    om = orc.Model(p, max_seq_len=128)
+    for b in range(B):
+        om.clear_cache()
+        assert got[b].tolist() == om.generate(prompts[b], N).tolist(), b
+    om.close()
+    eng.close()
+
+
+def test_batch_decode_full_batch_matches_single_sequence_engine(ctx, tiny_qwen_path):
+    """B = 32 (the maximum): every sequence equals the bs1 engine's generation"""
+    from moe_stream_b200.engine import Engine
+    B, T, N = 32, 6, 6
+    prompts = _batch_prompts(synth.TINY_QWEN3, B, T, 100)
+    eng = Engine.open(tiny_qwen_path, max_seq_len=64, ctx=ctx)
+    eng.batch_open(B)
+    got = eng.batch_generate(prompts, N)
+    for b in range(B):
+        assert got[b].tolist() == eng.generate(prompts[b], N), b
+    assert eng.batch_kernels_per_step == 2 + 8 * eng.config.layers + 3
+    eng.close()
+
+
+def test_batch_open_rejects_packed_experts(ctx, tiny_path):
+    from moe_stream_b200._lib import MsError
+    from moe_stream_b200.engine import Engine
+    eng = Engine.open(tiny_path, max_seq_len=64, ctx=ctx)
+    with pytest.raises(MsError):
+        eng.batch_open(4)
+    eng.close()
