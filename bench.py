@@ -421,6 +421,87 @@ def run_case_prefill(args):
                       "clocks": clk.summary()}), flush=True)
 
 
+def qwen3_step_bytes(spec, batch, ctx_len):
+    """Algorithmic HBM bytes of one config-2 decode step: every weight byte once per step (experts:
+    the expected unique experts of `batch` tokens under uniform routing, E(1 - (1 - k/E)^B)), the f32
+    KV of every sequence at `ctx_len` positions, the f16 LM head."""
+    H, L, E, k, I = spec.hidden, spec.layers, spec.experts, spec.top_k, spec.inter
+    q8 = lambda rows, cols: rows * (cols // 32) * 34
+    attn = q8(spec.q_dim + 2 * spec.kv_dim, H) + q8(H, spec.q_dim)
+    expert = 2 * I * (H // 256) * 144 + H * (I // 256) * 210
+    uniq = E * (1.0 - (1.0 - k / E) ** batch)
+    router = E * H * 4
+    kv = batch * ctx_len * spec.kv_heads * spec.head_dim * 4 * 2
+    per_layer = attn + router + uniq * expert + kv
+    return L * per_layer + spec.vocab * H * 2, uniq
+
+
+def run_case_qwen3(args):
+    """Config 2: Qwen3-30B-A3B-shaped Q4_K/Q6_K model, greedy decode at batch 1 and 32 with a
+    4096-token KV context.  bs1 runs the single-sequence step; bs32 the lockstep batch step (one
+    shared position, every weight byte streamed once per step).  Each batch prefills its prompt
+    (one step per position), then K device-resident greedy steps are timed with CUDA events."""
+    import torch
+    from dataclasses import replace
+    from moe_stream_b200 import synth
+    from moe_stream_b200.engine import Context, Engine
+    spec = synth.QWEN3_30B_A3B
+    if args.layers:
+        spec = replace(spec, layers=args.layers)
+    prompt_len = args.prompt
+    batches = [int(b) for b in args.batch.split(",")]
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx = Context(0)
+    ctx.set_stream(stream)
+    t0 = time.time()
+    eng = Engine.from_spec(spec, seed=0, max_seq_len=prompt_len + args.warmup + args.steps + 64, ctx=ctx)
+    log(f"qwen3 model generated + uploaded in {time.time() - t0:.1f}s")
+    peak, peak_kind = peaks()
+    out = {"case": "qwen3-30b-a3b", "metric": "decode tok/s (bs1, bs32)", "config": {
+        "workload": f"Qwen3-30B-A3B-shaped Q4_K/Q6_K greedy decode after a {prompt_len}-token prompt",
+        "layers": spec.layers, "kv_context": prompt_len, "l2": "no flush: each step streams > 2 GB"},
+        "steps": args.steps, "warmup": args.warmup}
+    for B in batches:
+        prompts = np.stack([synth.prompt_ids(spec, prompt_len, seed=b) for b in range(B)])
+        t0 = time.time()
+        if B == 1:
+            eng.clear_cache()
+            eng.forward(prompts[0])
+            run = eng.decode_steps_device
+        else:
+            eng.batch_open(B)
+            eng.batch_forward(prompts)
+            run = eng.batch_decode_steps_device
+        torch.cuda.synchronize()
+        log(f"bs{B}: prefill {prompt_len} positions in {time.time() - t0:.1f}s")
+        run(args.warmup)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(0) as clk:
+            s.record(stream)
+            run(args.steps)
+            e.record(stream)
+            torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / args.steps
+        ctx.sync()
+        nbytes, uniq = qwen3_step_bytes(spec, B, prompt_len + args.warmup + args.steps // 2)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[f"bs{B}"] = {"tok_s": round(B / (ms * 1e-3), 1), "ms_per_step": round(ms, 4),
+                         "kernels_per_step": eng.kernels_per_step if B == 1 else eng.batch_kernels_per_step,
+                         "algorithmic_bytes_per_step": int(nbytes), "expected_unique_experts_per_layer": round(uniq, 1),
+                         "achieved_gbs": round(gbs, 1), "hbm_frac": round(gbs / peak, 4), "peak_kind": peak_kind,
+                         "clocks": clk.summary()}
+        if not args.no_profile:
+            out[f"bs{B}"]["kernel_us_per_step"] = (eng.batch_profile_step() if B > 1 else
+                                                   [round(v, 1) for v in eng.profile_step()])
+        log(f"bs{B}: {out[f'bs{B}']}")
+        if B > 1:
+            eng.batch_close()
+    eng.close()
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -436,8 +517,10 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="profiling only: override the layer count")
     ap.add_argument("--mode", default="ep", choices=["ep", "replicas"],
                     help="N > 1: expert parallel over one sequence (default) or N independent replicas")
-    ap.add_argument("--case", default=None, choices=[None, "moe-layer", "prefill"],
-                    help="moe-layer: the decode expert FFN alone; prefill: config 4's MoE step")
+    ap.add_argument("--case", default=None, choices=[None, "moe-layer", "prefill", "qwen3"],
+                    help="moe-layer: the decode expert FFN alone; prefill: config 4's MoE step; "
+                         "qwen3: config 2 decode at the --batch sizes")
+    ap.add_argument("--batch", default="1,32", help="qwen3 case: comma-separated batch sizes")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -445,6 +528,10 @@ def main():
         run_case_moe(args)
     elif args.case == "prefill":
         run_case_prefill(args)
+    elif args.case == "qwen3":
+        if args.prompt == PROMPT:
+            args.prompt = 4096
+        run_case_qwen3(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

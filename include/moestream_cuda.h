@@ -181,6 +181,9 @@ MS_API ms_status ms_model_batch_next_tokens(ms_model* m, int32_t* next);        
 MS_API ms_status ms_model_batch_token_log(ms_model* m, int32_t* out, int max_rows, int* n_rows);
 MS_API ms_status ms_model_batch_last_logits(ms_model* m, float* out);             /* [B][vocab] */
 MS_API int ms_model_batch_kernels_per_step(const ms_model* m);
+/* device microseconds per batch step of each launch class alone (step start, QKV, attention, O,
+ * router, expert grouping, gate_up, down, residual, LM head) */
+MS_API ms_status ms_model_batch_profile_step(ms_model* m, float* us, int max, int* n);
 
 /* ---- hybrid (Qwen3.5 / Qwen3-Next) blocks ---- */
 /* One Gated DeltaNet layer in device memory.  Projections are in native blocks (qtype as in

@@ -101,6 +101,7 @@ _SIGS = {
     "ms_model_batch_token_log": (C.c_int, [_vp, _ip, _i, C.POINTER(C.c_int)]),
     "ms_model_batch_last_logits": (C.c_int, [_vp, _fp]),
     "ms_model_batch_kernels_per_step": (C.c_int, [_vp]),
+    "ms_model_batch_profile_step": (C.c_int, [_vp, _fp, _i, C.POINTER(C.c_int)]),
     "ms_model_token_log": (C.c_int, [_vp, _ip, _i, C.POINTER(C.c_int)]),
     "ms_model_clear_cache": (C.c_int, [_vp]),
     "ms_model_seq_len": (C.c_int, [_vp, C.POINTER(C.c_int)]),

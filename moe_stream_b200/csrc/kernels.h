@@ -212,10 +212,13 @@ struct AttnArgs {
   // part + b*(nkv*S*REP*(hd+2)) and counters cnt + b*nkv
   int batch = 1;
   int64_t bs_qkv = 0, bs_kv = 0, bs_out = 0;
+  int spl = 0;                     // streaming kernel: positions per split (a multiple of 32); 0: one-sequence tile kernel
 };
 cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s);
-// splits (grid.x) needed to cover `range` attended positions (128 positions per split)
+// tile-kernel splits (grid.x) needed to cover `range` attended positions
 int attn_splits(int range, int hd);   // splits of a decode-attention launch covering `range` positions
+// positions per split for `units` = kv_heads x sequences attending over `range` positions
+int attn_split_positions(int range, int units, int sm_count);
 
 // ---- LM head / f16 GEMV ----
 // logits = W (RMSNorm(h)*norm_w if norm_w) (+bias); argmax (lowest index on ties) into *key.
@@ -309,7 +312,8 @@ struct GroupMoeArgs {
   float* y = nullptr;              // [B*K][H]
 };
 int group_table_words(int B, int K);
-cudaError_t launch_moe_group(const DevCtx& c, const GroupMoeArgs& a, cudaStream_t s);
+// part: 0 grouping (route), 1 gate_up + activation, 2 down -- launched in that order
+cudaError_t launch_moe_group(const DevCtx& c, const GroupMoeArgs& a, int part, cudaStream_t s);
 
 // ---- Gated DeltaNet / shared expert (kernels_ssm.cu) ----
 struct DeltaNetStep {

@@ -438,8 +438,8 @@ cudaError_t launch_pdl_b(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_
   return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
+// dynamic shared memory opt-in (static + dynamic may exceed the 48 KB default)
 cudaError_t set_smem(const void* k, size_t smem) {
-  if (smem <= 48 * 1024) return cudaSuccess;
   return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
 

@@ -314,20 +314,22 @@ cudaError_t launch_q8(const DevCtx& c, const Q8Params& p, cudaStream_t s) {
 }
 
 // ============================ attention (decode) ============================
-// Grid (splits, kv_heads), 4 warps per CTA.  A split covers attn_split_len(HD) consecutive
-// positions; right after the position is known, one thread issues bulk copies of the split's
-// cached K and V rows (contiguous in the [kv_head][slot][hd] cache; two pieces where a
-// sliding-window ring wraps) into shared memory, and the query load, QK-norm and RoPE run while
-// they are in flight.  Scores: one position per lane, the K row's float4 chunks visited in a
-// lane-rotated order so a quarter-warp touches distinct banks; each warp keeps its own softmax
-// max/sum per query head; P*V with lanes over head dims from the staged V tile; the four warps
-// merge in shared memory; the last CTA of a kv head merges the splits, with the attention sink
-// in the denominator (ops/attention.rs:178-280).
-constexpr int kAWarps = 4;
+// Grid (splits, kv_heads, batch), 8 warps per CTA; a split covers 256 consecutive positions and
+// each warp 32 of them.  Lanes run over head dims (HD/32 each), so a cached K or V row is one
+// coalesced load per warp straight from HBM (no shared-memory staging); before waiting for the
+// projections each lane prefetches its part of the warp's rows into L2.  Scores: every lane forms
+// the REP per-head partial dots of a position with the query heads held in registers, and a
+// reduce-scatter over the warp (log2(REP) halving steps, then a full sum) leaves head h's score in
+// lanes h*32/REP ..; each such lane keeps its head's 32 scores and softmax state.  P*V: the
+// per-position weights are shuffled from those lanes and accumulated over the lane's dims.  The
+// warps merge in shared memory; the last CTA of a kv group merges the splits, with the attention
+// sink in the denominator (ops/attention.rs:178-280).
+constexpr int kAWarps = 8;
 constexpr int kAThreads = kAWarps * 32;
+constexpr int kAChunk = 32;   // positions per warp
 
-// positions per split: K + V tiles of one split fill 64 KB of shared memory
-__host__ __device__ constexpr int attn_split_len(int hd) { return hd <= 64 ? 128 : 8192 / hd; }
+// positions per split
+__host__ __device__ constexpr int attn_split_len(int) { return kAWarps * kAChunk; }
 
 __device__ __forceinline__ void rope_inplace(float* v, int rot, const float* c, const float* s) {
   // ops/attention.rs:96-118: half-rotate over the first `rot` dims
@@ -350,11 +352,27 @@ __device__ __forceinline__ void head_norm_warp(float* v, const float* w, int hd,
   __syncwarp();
 }
 
+// ============================ attention (decode, one sequence) ============================
+// Single-sequence decode (the lockstep batch uses attn_decode_kernel below).  Grid (splits, kv_heads), 4 warps per CTA.  A split covers attn_tile_len(HD) consecutive
+// positions; right after the position is known, one thread issues bulk copies of the split's
+// cached K and V rows (contiguous in the [kv_head][slot][hd] cache; two pieces where a
+// sliding-window ring wraps) into shared memory, and the query load, QK-norm and RoPE run while
+// they are in flight.  Scores: one position per lane, the K row's float4 chunks visited in a
+// lane-rotated order so a quarter-warp touches distinct banks; each warp keeps its own softmax
+// max/sum per query head; P*V with lanes over head dims from the staged V tile; the four warps
+// merge in shared memory; the last CTA of a kv head merges the splits, with the attention sink
+// in the denominator (ops/attention.rs:178-280).
+constexpr int kTWarps = 4;
+constexpr int kTThreads = kTWarps * 32;
+
+// positions per split: K + V tiles of one split fill 64 KB of shared memory
+__host__ __device__ constexpr int attn_tile_len(int hd) { return hd <= 64 ? 128 : 8192 / hd; }
+
 template <int HD, int REP>
-__global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint32_t* err) {
+__global__ void __launch_bounds__(kTThreads) attn_tile_kernel(AttnArgs a, uint32_t* err) {
   constexpr int DL = HD / 32;                  // head dims per lane in P*V
-  constexpr int SPL = attn_split_len(HD);      // positions per split
-  constexpr int PW = SPL / kAWarps;            // positions per warp (<= 32)
+  constexpr int SPL = attn_tile_len(HD);      // positions per split
+  constexpr int PW = SPL / kTWarps;            // positions per warp (<= 32)
   constexpr int NC = HD / 4;                   // float4 chunks per row
   extern __shared__ __align__(128) float dyn[];
   float* Kt = dyn;                             // [SPL][HD] staged cache rows
@@ -363,24 +381,14 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
   __shared__ __align__(16) float qs[REP * HD];
   __shared__ __align__(16) float kn[HD];
   __shared__ __align__(16) float vn[HD];
-  __shared__ float pw[kAWarps][REP][32];
-  __shared__ float mw[kAWarps][REP], lw[kAWarps][REP];
-  __shared__ __align__(16) float ow[kAWarps][REP][HD];
+  __shared__ float pw[kTWarps][REP][32];
+  __shared__ float mw[kTWarps][REP], lw[kTWarps][REP];
+  __shared__ __align__(16) float ow[kTWarps][REP][HD];
   __shared__ __align__(8) uint64_t bar;
   __shared__ uint32_t last;
   __shared__ int tile_ok;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kh = blockIdx.y, sidx = blockIdx.x, S = gridDim.x;
-  if (blockIdx.z) {   // sequence b of a lockstep batch
-    const int64_t b = blockIdx.z;
-    a.qkv += b * a.bs_qkv;
-    a.kc += b * a.bs_kv;
-    a.vc += b * a.bs_kv;
-    a.out += b * a.bs_out;
-    if (a.oq) { a.oq += b * a.bs_out; a.od += b * a.bs_out / 32; }
-    a.part += b * (int64_t)gridDim.y * S * REP * (HD + 2);
-    a.cnt += b * gridDim.y;
-  }
   // The position comes from the step's first kernel and the cached rows from earlier steps, both
   // complete before the previous kernel started (every kernel lets its dependents launch only after
   // its own wait), so the tile copies go out before this kernel waits for the projections.
@@ -415,15 +423,15 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
   if (active) {
     const float* cs = a.cos_t + (size_t)pos * half;
     const float* sn = a.sin_t + (size_t)pos * half;
-    for (int i = threadIdx.x; i < REP * HD; i += kAThreads) qs[i] = a.qkv[(size_t)kh * REP * HD + i];
+    for (int i = threadIdx.x; i < REP * HD; i += kTThreads) qs[i] = a.qkv[(size_t)kh * REP * HD + i];
     if (has_new) {
       const float* kq = a.qkv + (size_t)a.nh * HD + (size_t)kh * HD;
       const float* vq = kq + (size_t)a.nkv * HD;
-      for (int i = threadIdx.x; i < HD; i += kAThreads) { kn[i] = kq[i]; vn[i] = vq[i]; }
+      for (int i = threadIdx.x; i < HD; i += kTThreads) { kn[i] = kq[i]; vn[i] = vq[i]; }
     }
     __syncthreads();
     if (a.q_norm) {
-      for (int h = warp; h < REP; h += kAWarps) head_norm_warp(qs + h * HD, a.q_norm, HD, a.eps, lane);
+      for (int h = warp; h < REP; h += kTWarps) head_norm_warp(qs + h * HD, a.q_norm, HD, a.eps, lane);
       if (has_new && warp == 0) head_norm_warp(kn, a.k_norm, HD, a.eps, lane);
       __syncthreads();
     }
@@ -434,7 +442,7 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
       const int slot = a.window ? pos % a.cap : pos;
       float* kd = a.kc + ((size_t)kh * a.cap + slot) * HD;
       float* vd = a.vc + ((size_t)kh * a.cap + slot) * HD;
-      for (int i = threadIdx.x; i < HD; i += kAThreads) { kd[i] = kn[i]; vd[i] = vn[i]; }
+      for (int i = threadIdx.x; i < HD; i += kTThreads) { kd[i] = kn[i]; vd[i] = vn[i]; }
     }
     if (pc1 > p0 && !mbar_wait(&bar, 0, err, EF_TIMEOUT_FULL)) tile_ok = 0;
     // ---- scores: one position per lane ----
@@ -494,14 +502,14 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
       for (int t = 0; t < DL; ++t) ow[warp][h][lane + 32 * t] = o[h][t];
     __syncthreads();
     // ---- merge the four warps into this split's (m, l, o) ----
-    for (int i = threadIdx.x; i < REP * HD; i += kAThreads) {
+    for (int i = threadIdx.x; i < REP * HD; i += kTThreads) {
       const int h = i / HD, d = i - h * HD;
       float M = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < kAWarps; ++w) M = fmaxf(M, mw[w][h]);
+      for (int w = 0; w < kTWarps; ++w) M = fmaxf(M, mw[w][h]);
       float L = 0.f, O = 0.f;
 #pragma unroll
-      for (int w = 0; w < kAWarps; ++w) {
+      for (int w = 0; w < kTWarps; ++w) {
         const float m = mw[w][h];
         if (m != -INFINITY) {
           const float f = expf(m - M);
@@ -512,6 +520,290 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
       if (!tile_ok) { M = -INFINITY; L = 0.f; O = 0.f; }   // a timed-out copy contributes nothing
       part[h * (HD + 2) + 2 + d] = O;
       if (d == 0) { part[h * (HD + 2)] = M; part[h * (HD + 2) + 1] = L; }
+    }
+  } else {
+    for (int h = threadIdx.x; h < REP; h += kTThreads) { part[h * (HD + 2)] = -INFINITY; part[h * (HD + 2) + 1] = 0.f; }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = (atomicAdd(&a.cnt[kh], 1u) == (uint32_t)S - 1) ? 1u : 0u;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // ---- merge the splits of this kv group (+ attention sink) ----
+  const float* gp = a.part + (size_t)kh * S * REP * (HD + 2);
+  float* hm = &mw[0][0];
+  float* hinv = &lw[0][0];
+  for (int i = threadIdx.x; i < S * REP; i += kTThreads) wsm[i] = __ldcg(&gp[(size_t)i * (HD + 2)]);
+  __syncthreads();
+  for (int h = threadIdx.x; h < REP; h += kTThreads) {
+    float M = -INFINITY;
+    for (int s = 0; s < S; ++s) M = fmaxf(M, wsm[s * REP + h]);
+    float sink = 0.f;
+    if (a.sinks) { sink = a.sinks[kh * REP + h]; M = 0.5f * ((M + sink) + fabsf(M - sink)); }
+    float L = 0.f;
+    for (int s = 0; s < S; ++s) {
+      const float m = wsm[s * REP + h];
+      if (m != -INFINITY) L += __ldcg(&gp[((size_t)s * REP + h) * (HD + 2) + 1]) * expf(m - M);
+    }
+    if (a.sinks) L += expf(sink - M);
+    hm[h] = M;
+    hinv[h] = 1.0f / L;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < S * REP; i += kTThreads) {
+    const int h = i % REP;
+    const float m = wsm[i];
+    wsm[i] = (m == -INFINITY) ? 0.f : expf(m - hm[h]) * hinv[h];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < REP * HD; i += kTThreads) {
+    const int h = i / HD, d = i - h * HD;
+    const float* src = gp + (size_t)h * (HD + 2) + 2 + d;
+    const size_t stride = (size_t)REP * (HD + 2);
+    float o = 0.f;
+    int s = 0;
+    for (; s + 8 <= S; s += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldcg(src + (size_t)(s + u) * stride);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o = fmaf(wsm[(s + u) * REP + h], v[u], o);
+    }
+    for (; s < S; ++s) o = fmaf(wsm[s * REP + h], __ldcg(src + (size_t)s * stride), o);
+    a.out[(size_t)(kh * REP + h) * HD + d] = o;
+    if (a.oq) ow[0][h][d] = o;
+  }
+  if (a.oq) {   // Q8_0 blocks of this group's output (the O-projection's activation)
+    __syncthreads();
+    const float* og = &ow[0][0][0];
+    for (int bl = threadIdx.x; bl < REP * HD / 32; bl += kTThreads) {
+      float v[32];
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = og[32 * bl + k];
+      const int gb = kh * REP * HD / 32 + bl;
+      quantize_q8_block(v, a.oq + 32 * gb, &a.od[gb]);
+    }
+  }
+  if (threadIdx.x == 0) a.cnt[kh] = 0u;
+}
+
+template <int HD, int REP>
+__global__ void __launch_bounds__(kAThreads, 2) attn_decode_kernel(AttnArgs a, uint32_t* err) {
+  constexpr int DPL = HD / 32;                 // head dims per lane
+  constexpr int GL = 32 / REP;                 // lanes per head after the reduce-scatter
+  constexpr int PB = 8;                        // rows loaded per batch
+  extern __shared__ __align__(16) float dyn[];
+  float* ow = dyn;                             // [kAWarps][REP][HD] per-warp outputs
+  float* wsm = ow + kAWarps * REP * HD;        // [S][REP] split weights of the final merge
+  __shared__ __align__(16) float qs[REP * HD];
+  __shared__ __align__(16) float kn[HD];
+  __shared__ __align__(16) float vn[HD];
+  __shared__ float psm[kAWarps][REP][kAChunk];   // a chunk's scores, then its softmax weights
+  __shared__ float mw[kAWarps][REP], lw[kAWarps][REP];
+  __shared__ uint32_t last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kh = blockIdx.y, sidx = blockIdx.x, S = gridDim.x;
+  if (blockIdx.z) {   // sequence b of a lockstep batch
+    const int64_t b = blockIdx.z;
+    a.qkv += b * a.bs_qkv;
+    a.kc += b * a.bs_kv;
+    a.vc += b * a.bs_kv;
+    a.out += b * a.bs_out;
+    if (a.oq) { a.oq += b * a.bs_out; a.od += b * a.bs_out / 32; }
+    a.part += b * (int64_t)gridDim.y * S * REP * (HD + 2);
+    a.cnt += b * gridDim.y;
+  }
+  // The position comes from the step's first kernel and the cached rows from earlier steps, both
+  // complete before the previous kernel started (every kernel lets its dependents launch only after
+  // its own wait), so the first chunk's rows can be prefetched before this kernel waits.
+  const int spl = a.spl;
+  const int pos = *a.pos;
+  const int lo = a.window ? max(0, pos - a.window + 1) : 0;
+  const int p0 = lo + sidx * spl, p1 = min(p0 + spl, pos + 1);
+  const bool active = p0 < p1;
+  const bool has_new = active && p1 == pos + 1;
+  const float* kbase = a.kc + (size_t)kh * a.cap * HD;
+  const float* vbase = a.vc + (size_t)kh * a.cap * HD;
+  auto slot_of = [&](int q) { return a.window ? q % a.cap : q; };   // kv_cache.rs:37-60 (ring for SWA)
+  // chunks of this warp: c0, c0 + kAWarps, ... (32 positions each)
+  auto prefetch_chunk = [&](int cb) {
+    constexpr int LPR = HD * 4 / 128;           // 128-byte lines per row
+    for (int i = lane; i < 2 * kAChunk * LPR; i += 32) {
+      const int r = i / (2 * LPR), pt = i % (2 * LPR), q = cb + r;
+      if (q < min(p1, pos)) {
+        const float* base = (pt < LPR ? kbase : vbase) + (size_t)slot_of(q) * HD + (pt % LPR) * 32;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(base));
+      }
+    }
+  };
+  if (active && p0 + warp * kAChunk < p1) prefetch_chunk(p0 + warp * kAChunk);
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int half = a.rot / 2;
+  float* part = a.part + ((size_t)kh * S + sidx) * REP * (HD + 2);
+  if (active) {
+    const float* cs = a.cos_t + (size_t)pos * half;
+    const float* sn = a.sin_t + (size_t)pos * half;
+    for (int i = threadIdx.x; i < REP * HD; i += kAThreads) qs[i] = a.qkv[(size_t)kh * REP * HD + i];
+    if (has_new) {
+      const float* kq = a.qkv + (size_t)a.nh * HD + (size_t)kh * HD;
+      const float* vq = kq + (size_t)a.nkv * HD;
+      for (int i = threadIdx.x; i < HD; i += kAThreads) { kn[i] = kq[i]; vn[i] = vq[i]; }
+    }
+    __syncthreads();
+    if (a.q_norm) {
+      for (int h = warp; h < REP; h += kAWarps) head_norm_warp(qs + h * HD, a.q_norm, HD, a.eps, lane);
+      if (has_new && warp == 0) head_norm_warp(kn, a.k_norm, HD, a.eps, lane);
+      __syncthreads();
+    }
+    for (int h = 0; h < REP; ++h) rope_inplace(qs + h * HD, a.rot, cs, sn);
+    if (has_new) rope_inplace(kn, a.rot, cs, sn);
+    __syncthreads();
+    if (has_new) {   // kv_cache.rs:37-60 append (ring slot for sliding-window layers)
+      float* kd = a.kc + ((size_t)kh * a.cap + slot_of(pos)) * HD;
+      float* vd = a.vc + ((size_t)kh * a.cap + slot_of(pos)) * HD;
+      for (int i = threadIdx.x; i < HD; i += kAThreads) { kd[i] = kn[i]; vd[i] = vn[i]; }
+    }
+    const int my_h = lane / GL, gi = lane % GL;
+    float qr[REP][DPL];
+#pragma unroll
+    for (int h = 0; h < REP; ++h)
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) qr[h][d] = qs[h * HD + lane * DPL + d];
+    float o[REP][DPL];
+#pragma unroll
+    for (int h = 0; h < REP; ++h)
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) o[h][d] = 0.f;
+    float M = -INFINITY, L = 0.f;   // softmax state of head my_h
+    auto load_rows = [&](const float* base, const float* nrow, int q, int w1, float (&r)[DPL]) {
+      if (q >= w1) {
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) r[d] = 0.f;
+      } else if (q == pos) {
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) r[d] = nrow[lane * DPL + d];
+      } else {
+        const float* src = base + (size_t)slot_of(q) * HD + lane * DPL;
+        if constexpr (DPL % 4 == 0) {
+#pragma unroll
+          for (int d = 0; d < DPL; d += 4) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(src + d));
+            r[d] = v.x; r[d + 1] = v.y; r[d + 2] = v.z; r[d + 3] = v.w;
+          }
+        } else {
+#pragma unroll
+          for (int d = 0; d < DPL; d += 2) {
+            const float2 v = __ldg(reinterpret_cast<const float2*>(src + d));
+            r[d] = v.x; r[d + 1] = v.y;
+          }
+        }
+      }
+    };
+    for (int cb = p0 + warp * kAChunk; cb < p1; cb += kAWarps * kAChunk) {
+      const int w1 = min(cb + kAChunk, p1);
+      if (cb + kAWarps * kAChunk < p1) prefetch_chunk(cb + kAWarps * kAChunk);
+      // ---- scores of the chunk's positions -> psm[warp][h][j] ----
+#pragma unroll 1
+      for (int jb = 0; jb < kAChunk; jb += PB) {
+        float kr[PB][DPL];
+#pragma unroll
+        for (int u = 0; u < PB; ++u) load_rows(kbase, kn, cb + jb + u, w1, kr[u]);
+#pragma unroll
+        for (int u = 0; u < PB; ++u) {
+          float v[REP];
+#pragma unroll
+          for (int h = 0; h < REP; ++h) {
+            float t = 0.f;
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) t = fmaf(qr[h][d], kr[u][d], t);
+            v[h] = t;
+          }
+          // reduce-scatter: halving steps leave head (lane / GL) in v[0], then a sum over its GL lanes
+#pragma unroll
+          for (int o2 = 16, n = REP; n > 1; o2 >>= 1, n >>= 1) {
+            const bool up = (lane & o2) != 0;
+#pragma unroll
+            for (int i = 0; i < n / 2; ++i) {
+              const float send = up ? v[i] : v[i + n / 2];
+              const float keep = up ? v[i + n / 2] : v[i];
+              v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o2);
+            }
+          }
+#pragma unroll
+          for (int o2 = GL / 2; o2 > 0; o2 >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o2);
+          if (gi == 0) psm[warp][my_h][jb + u] = (cb + jb + u < w1) ? v[0] * a.scale : -INFINITY;
+        }
+      }
+      __syncwarp();
+      // ---- online softmax: lane (h, gi) owns positions gi, gi + GL, ... of head h ----
+      float cm = -INFINITY;
+      for (int j = gi; j < kAChunk; j += GL) cm = fmaxf(cm, psm[warp][my_h][j]);
+#pragma unroll
+      for (int o2 = GL / 2; o2 > 0; o2 >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o2));
+      const float Mn = fmaxf(M, cm);
+      const float corr = (M == -INFINITY) ? 0.f : expf(M - Mn);
+      float cl = 0.f;
+      for (int j = gi; j < kAChunk; j += GL) {
+        const float sv = psm[warp][my_h][j];
+        const float pe = (sv == -INFINITY) ? 0.f : expf(sv - Mn);
+        psm[warp][my_h][j] = pe;
+        cl += pe;
+      }
+#pragma unroll
+      for (int o2 = GL / 2; o2 > 0; o2 >>= 1) cl += __shfl_xor_sync(0xffffffffu, cl, o2);
+      L = L * corr + cl;
+      M = Mn;
+      __syncwarp();
+#pragma unroll
+      for (int h = 0; h < REP; ++h) {
+        const float ch = __shfl_sync(0xffffffffu, corr, h * GL);
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) o[h][d] *= ch;
+      }
+      // ---- P * V over this lane's dims ----
+#pragma unroll 1
+      for (int jb = 0; jb < kAChunk; jb += PB) {
+        float vr[PB][DPL];
+#pragma unroll
+        for (int u = 0; u < PB; ++u) load_rows(vbase, vn, cb + jb + u, w1, vr[u]);
+#pragma unroll
+        for (int u = 0; u < PB; ++u) {
+#pragma unroll
+          for (int h = 0; h < REP; ++h) {
+            const float pj = psm[warp][h][jb + u];
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) o[h][d] = fmaf(pj, vr[u][d], o[h][d]);
+          }
+        }
+      }
+      __syncwarp();
+    }
+    if (gi == 0) { mw[warp][my_h] = M; lw[warp][my_h] = L; }
+#pragma unroll
+    for (int h = 0; h < REP; ++h)
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) ow[(warp * REP + h) * HD + lane * DPL + d] = o[h][d];
+    __syncthreads();
+    // ---- merge the warps into this split's (m, l, o) ----
+    for (int i = threadIdx.x; i < REP * HD; i += kAThreads) {
+      const int h = i / HD, d = i - h * HD;
+      float Mx = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kAWarps; ++w) Mx = fmaxf(Mx, mw[w][h]);
+      float Ls = 0.f, Os = 0.f;
+#pragma unroll
+      for (int w = 0; w < kAWarps; ++w) {
+        const float mm = mw[w][h];
+        if (mm != -INFINITY) {
+          const float f = expf(mm - Mx);
+          Ls = fmaf(lw[w][h], f, Ls);
+          Os = fmaf(ow[(w * REP + h) * HD + d], f, Os);
+        }
+      }
+      part[h * (HD + 2) + 2 + d] = Os;
+      if (d == 0) { part[h * (HD + 2)] = Mx; part[h * (HD + 2) + 1] = Ls; }
     }
   } else {
     for (int h = threadIdx.x; h < REP; h += kAThreads) { part[h * (HD + 2)] = -INFINITY; part[h * (HD + 2) + 1] = 0.f; }
@@ -564,11 +856,11 @@ __global__ void __launch_bounds__(kAThreads) attn_decode_kernel(AttnArgs a, uint
     }
     for (; s < S; ++s) o = fmaf(wsm[s * REP + h], __ldcg(src + (size_t)s * stride), o);
     a.out[(size_t)(kh * REP + h) * HD + d] = o;
-    if (a.oq) ow[0][h][d] = o;
+    if (a.oq) ow[h * HD + d] = o;
   }
   if (a.oq) {   // Q8_0 blocks of this group's output (the O-projection's activation)
     __syncthreads();
-    const float* og = &ow[0][0][0];
+    const float* og = ow;
     for (int bl = threadIdx.x; bl < REP * HD / 32; bl += kAThreads) {
       float v[32];
 #pragma unroll
@@ -822,7 +1114,14 @@ cudaError_t launch_q8_gemv(const DevCtx& c, const Q8GemvArgs& a, cudaStream_t s)
 
 template <int HD, int REP>
 cudaError_t launch_attn_k(const AttnArgs& a, const DevCtx& c, dim3 grid, cudaStream_t s) {
-  const size_t smem = ((size_t)2 * attn_split_len(HD) * HD + (size_t)a.S * REP) * sizeof(float);
+  if (a.spl == 0) {   // one sequence: K/V tiles staged in shared memory before the wait
+    const size_t smem = ((size_t)2 * attn_tile_len(HD) * HD + (size_t)a.S * REP) * sizeof(float);
+    cudaError_t e = cudaFuncSetAttribute(attn_tile_kernel<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(attn_tile_kernel<HD, REP>, grid, dim3(kTThreads), smem, s, a, c.err);
+  }
+  const size_t smem = ((size_t)kAWarps * REP * HD + (size_t)a.S * REP) * sizeof(float);
   cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
@@ -843,13 +1142,32 @@ cudaError_t launch_attn_hd(const AttnArgs& a, const DevCtx& c, int rep, dim3 gri
   return cudaErrorInvalidValue;
 }
 
-int attn_splits(int range, int hd) { return (range + attn_split_len(hd) - 1) / attn_split_len(hd); }
+int attn_splits(int range, int hd) { return (range + attn_tile_len(hd) - 1) / attn_tile_len(hd); }
+
+int attn_split_positions(int range, int units, int sm_count) {
+  const int full = attn_split_len(0);
+  const int64_t target = 2LL * sm_count;   // CTAs: two resident per SM
+  if ((int64_t)((range + full - 1) / full) * units < target) {
+    // few sequences: shorter splits (whole 32-position chunks, >= 64) so the grid fills the GPU
+    int spl = (int)(((int64_t)range * units + target - 1) / target);
+    spl = (spl + kAChunk - 1) / kAChunk * kAChunk;
+    return spl < 2 * kAChunk ? 2 * kAChunk : (spl > full ? full : spl);
+  }
+  // many: the fewest chunks per warp that keep the grid within ~4 waves
+  const int chunks = (range + full - 1) / full;
+  int cpw = 1;
+  while (cpw < chunks && (int64_t)((chunks + cpw - 1) / cpw) * units > 4 * target) ++cpw;
+  return cpw * full;
+}
 
 cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s) {
   if (a.nkv <= 0 || a.nh % a.nkv || a.S <= 0 || a.rot > a.hd || a.rot % 2) return cudaErrorInvalidValue;
   const int rep = a.nh / a.nkv;
   if ((size_t)a.S * rep > 8192) return cudaErrorInvalidValue;   // merge weights: <= 32 KB of shared memory
   if (a.batch < 1 || (a.batch > 1 && (a.bs_out % 32 || (a.oq && !a.od)))) return cudaErrorInvalidValue;
+  // spl == 0: the single-sequence tile kernel (splits of attn_splits(range, hd) positions);
+  // otherwise the streaming kernel with spl positions per split
+  if (a.spl < 0 || a.spl % kAChunk || (a.spl == 0 && a.batch != 1)) return cudaErrorInvalidValue;
   const dim3 grid((unsigned)a.S, (unsigned)a.nkv, (unsigned)a.batch);
   switch (a.hd) {
     case 32: return launch_attn_hd<32>(a, c, rep, grid, s);

@@ -1154,7 +1154,7 @@ cudaError_t launch_moe_mxfp4(const DevCtx& c, const MoeArgs& a, cudaStream_t s) 
 
 int group_table_words(int B, int K) { return 1 + 3 * B * K; }
 
-cudaError_t launch_moe_group(const DevCtx& c, const GroupMoeArgs& a, cudaStream_t s) {
+cudaError_t launch_moe_group(const DevCtx& c, const GroupMoeArgs& a, int part, cudaStream_t s) {
   const int n_ent = a.B * a.K;
   if (a.B < 1 || a.B > kMaxBatch || a.K < 1 || a.K > kMaxK || a.n_local < 0 || a.n_local > kRouteThreads ||
       a.H % 64 || a.I % 32)
@@ -1172,17 +1172,16 @@ cudaError_t launch_moe_group(const DevCtx& c, const GroupMoeArgs& a, cudaStream_
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, group_route_kernel, a.idx, n_ent, a.K, a.expert_base, a.n_local, a.grp,
-                                     a.ent_tok, a.ent_of, c.err);
-  if (e != cudaSuccess) return e;
+  if (part == 0)
+    return cudaLaunchKernelEx(&cfg, group_route_kernel, a.idx, n_ent, a.K, a.expert_base, a.n_local, a.grp,
+                              a.ent_tok, a.ent_of, c.err);
   GroupParams p = {};
   p.grp = a.grp; p.ent_tok = a.ent_tok; p.oai = a.oai_swiglu; p.err = c.err;
   p.mode = MODE_GATEUP; p.fmt = fg; p.w0 = a.gate; p.w1 = a.up; p.expert_stride = (int64_t)a.I * rbg; p.rb = rbg;
   p.cols = a.H; p.rows = a.I; p.n_tiles = a.I / 16; p.stage_bytes = 32 * rbg; p.ns = pick_group_stages(p.stage_bytes);
   p.x = a.x; p.bias0 = a.gate_b; p.bias1 = a.up_b; p.out = a.act;
   if ((16 * rbg) % 16 || p.expert_stride % 16 || a.I % 16) return cudaErrorInvalidValue;
-  e = dispatch_group(c, p, s);
-  if (e != cudaSuccess) return e;
+  if (part == 1) return dispatch_group(c, p, s);
   p.mode = MODE_DOWN; p.fmt = fd; p.w0 = a.down; p.w1 = nullptr; p.expert_stride = (int64_t)a.H * rbd; p.rb = rbd;
   p.cols = a.I; p.rows = a.H; p.n_tiles = a.H / 16; p.stage_bytes = 16 * rbd; p.ns = pick_group_stages(p.stage_bytes);
   p.x = a.act; p.bias0 = a.down_b; p.bias1 = nullptr; p.out = a.y;

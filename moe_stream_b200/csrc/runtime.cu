@@ -196,6 +196,7 @@ struct BatchRt {
   cudaGraphExec_t graph = nullptr;
   int seq = 0;
   int kernels_per_step = 0;
+  int spl_full = 0, spl_swa = 0, S_full = 0, S_swa = 0;   // attention split sizes of the batch
 };
 
 struct ms_model {
@@ -223,6 +224,7 @@ struct ms_model {
   int* token_log = nullptr;
   int expert_base = 0, n_local = 0;
   int splits_full = 0, splits_swa = 0;
+  int attn_spl = 0;                 // single-sequence attention: 0 tile kernel, else streaming split length
   std::vector<void*> allocs;
   std::set<std::string> seen;
   cudaGraphExec_t graph = nullptr;
@@ -455,7 +457,7 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     aa.qkv = m->qkv; aa.q_norm = Lw.qn; aa.k_norm = Lw.kn; aa.eps = c.eps; aa.cos_t = m->cos_t; aa.sin_t = m->sin_t;
     aa.rot = c.rot_dim; aa.pos = &m->st->pos; aa.kc = Lw.kc; aa.vc = Lw.vc; aa.cap = Lw.cap; aa.window = Lw.window;
     aa.sinks = Lw.sinks; aa.part = m->attn_part; aa.cnt = m->attn_cnt; aa.out = m->attn_out; aa.nh = c.heads;
-    aa.nkv = c.kv_heads; aa.hd = c.head_dim; aa.S = Lw.window ? m->splits_swa : m->splits_full;
+    aa.nkv = c.kv_heads; aa.hd = c.head_dim; aa.S = Lw.window ? m->splits_swa : m->splits_full; aa.spl = m->attn_spl;
     aa.scale = (float)(1.0 / std::sqrt((double)c.head_dim)); aa.oq = m->xq_a; aa.od = m->xd_a;
     LAUNCH(launch_attention(dc, aa, s));
     Q8GemvArgs oa;
@@ -618,64 +620,70 @@ ms_status balloc(ms_model* m, T** p, size_t bytes) {
   return MS_OK;
 }
 
+// launch classes of the batch step (ms_model_batch_profile_step): 0 step start (begin, embed),
+// 1 QKV, 2 attention, 3 O, 4 router, 5 expert grouping, 6 gate_up, 7 down, 8 residual, 9 LM head
+constexpr int kBatchClasses = 10;
+
 ms_status enqueue_batch_step(ms_model* m, cudaStream_t s) {
   const ms_model_config& c = m->cfg;
   const DevCtx& dc = m->ctx->dc;
   BatchRt& b = *m->bt;
   const int H = c.hidden, Dq = q_dim(c), Dkv = kv_dim(c), B = b.B;
   int nk = 0;
-#define BLAUNCH(call)                                                \
-  do {                                                               \
-    cudaError_t e_ = (call);                                         \
-    if (e_ != cudaSuccess) return cuda_fail(m->ctx, e_, #call);      \
-    ++nk;                                                            \
+#define BLAUNCH(cls, n, call)                                          \
+  do {                                                                 \
+    if (m->prof_class < 0 || m->prof_class == (cls)) {                 \
+      cudaError_t e_ = (call);                                         \
+      if (e_ != cudaSuccess) return cuda_fail(m->ctx, e_, #call);      \
+    }                                                                  \
+    nk += (n);                                                         \
   } while (0)
-  BLAUNCH(launch_batch_begin(dc, b.st, s));
-  BLAUNCH(launch_embed_batch(dc, b.st, b.tok_in, b.keys, m->embd, m->embd_q, H, c.vocab, B, b.h, b.log,
-                             m->L[0].attn_norm, c.eps, b.xq_h, b.xd_h, s));
+  BLAUNCH(0, 1, launch_batch_begin(dc, b.st, s));
+  BLAUNCH(0, 1, launch_embed_batch(dc, b.st, b.tok_in, b.keys, m->embd, m->embd_q, H, c.vocab, B, b.h, b.log,
+                                   m->L[0].attn_norm, c.eps, b.xq_h, b.xd_h, s));
   for (int li = 0; li < c.layers; ++li) {
     LayerW& Lw = m->L[li];
     Q8BatchArgs qa;
     qa.w = Lw.wqkv; qa.rows = Dq + 2 * Dkv; qa.cols = H; qa.B = B; qa.xq = b.xq_h; qa.xd = b.xd_h; qa.bias = Lw.bqkv;
     qa.y = b.qkv;
-    BLAUNCH(launch_q8_gemm_batch(dc, qa, s));
+    BLAUNCH(1, 1, launch_q8_gemm_batch(dc, qa, s));
     AttnArgs aa;
     aa.qkv = b.qkv; aa.q_norm = Lw.qn; aa.k_norm = Lw.kn; aa.eps = c.eps; aa.cos_t = m->cos_t; aa.sin_t = m->sin_t;
     aa.rot = c.rot_dim; aa.pos = &b.st->pos; aa.kc = b.kc[li]; aa.vc = b.vc[li]; aa.cap = Lw.cap; aa.window = Lw.window;
     aa.sinks = Lw.sinks; aa.part = b.part; aa.cnt = b.attn_cnt; aa.out = b.attn; aa.nh = c.heads; aa.nkv = c.kv_heads;
-    aa.hd = c.head_dim; aa.S = Lw.window ? m->splits_swa : m->splits_full;
+    aa.hd = c.head_dim; aa.S = Lw.window ? b.S_swa : b.S_full; aa.spl = Lw.window ? b.spl_swa : b.spl_full;
     aa.scale = (float)(1.0 / std::sqrt((double)c.head_dim)); aa.oq = b.xq_a; aa.od = b.xd_a;
     aa.batch = B; aa.bs_qkv = Dq + 2 * Dkv; aa.bs_kv = (int64_t)c.kv_heads * Lw.cap * c.head_dim; aa.bs_out = Dq;
-    BLAUNCH(launch_attention(dc, aa, s));
+    BLAUNCH(2, 1, launch_attention(dc, aa, s));
     Q8BatchArgs oa;
     oa.w = Lw.wo; oa.rows = H; oa.cols = Dq; oa.B = B; oa.xq = b.xq_a; oa.xd = b.xd_a; oa.bias = Lw.bo;
     oa.residual = b.h;
-    BLAUNCH(launch_q8_gemm_batch(dc, oa, s));
+    BLAUNCH(3, 1, launch_q8_gemm_batch(dc, oa, s));
     RouterArgs ra;
     ra.h = b.h; ra.norm_w = Lw.post_norm; ra.eps = c.eps; ra.xn = b.xn; ra.w = Lw.router_w; ra.b = Lw.router_b;
     ra.mask = Lw.mask; ra.logits = b.rlog; ra.idx = b.idx; ra.wts = b.wts; ra.counter = b.router_cnt; ra.H = H;
     ra.E = c.experts; ra.K = c.top_k; ra.softmax_weight = c.arch == MS_ARCH_GPT_OSS; ra.normalize = c.norm_topk_prob;
     ra.batch = B;
-    BLAUNCH(launch_router(dc, ra, s));
+    BLAUNCH(4, 1, launch_router(dc, ra, s));
     GroupMoeArgs ga;
     ga.x = b.xn; ga.idx = b.idx; ga.B = B; ga.K = c.top_k; ga.H = H; ga.I = c.inter; ga.gate_q = Lw.gate_q;
     ga.down_q = Lw.down_q; ga.gate = Lw.gate; ga.up = Lw.up; ga.down = Lw.down; ga.gate_b = Lw.gate_b;
     ga.up_b = Lw.up_b; ga.down_b = Lw.down_b; ga.expert_base = m->expert_base; ga.n_local = m->n_local;
     ga.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ga.grp = b.grp; ga.ent_tok = b.ent_tok; ga.ent_of = b.ent_of;
     ga.act = b.act; ga.y = b.y;
-    BLAUNCH(launch_moe_group(dc, ga, s));
-    nk += 2;   // route, gate_up, down
+    BLAUNCH(5, 1, launch_moe_group(dc, ga, 0, s));
+    BLAUNCH(6, 1, launch_moe_group(dc, ga, 1, s));
+    BLAUNCH(7, 1, launch_moe_group(dc, ga, 2, s));
     BatchCombine bc;
     bc.y = b.y; bc.ent_of = b.ent_of; bc.idx = b.idx; bc.wts = b.wts; bc.K = c.top_k;
     const bool last = li + 1 == c.layers;
-    BLAUNCH(launch_resid_batch(dc, bc, b.h, H, B, last ? m->out_norm : m->L[li + 1].attn_norm, c.eps,
-                               last ? nullptr : b.xq_h, last ? nullptr : b.xd_h, last ? b.xf : nullptr, s));
+    BLAUNCH(8, 1, launch_resid_batch(dc, bc, b.h, H, B, last ? m->out_norm : m->L[li + 1].attn_norm, c.eps,
+                                     last ? nullptr : b.xq_h, last ? nullptr : b.xd_h, last ? b.xf : nullptr, s));
   }
   LmBatchArgs la;
   la.w = m->out_w; la.xf = b.xf; la.V = c.vocab; la.H = H; la.B = B; la.bias = m->out_b; la.scratch = b.lm_scratch;
   la.logits = b.logits; la.keys = b.keys;
-  BLAUNCH(launch_lmhead_batch(dc, la, s));
-  nk += 2;   // prep, GEMM, key reduction
+  BLAUNCH(9, 3, launch_lmhead_batch(dc, la, s));   // prep, GEMM, key reduction
 #undef BLAUNCH
   b.kernels_per_step = nk;
   return MS_OK;
@@ -1100,9 +1108,14 @@ ms_status ms_model_finalize(ms_model* m) {
   }
   const int H = c.hidden, Dq = q_dim(c), Dkv = kv_dim(c), rep = c.heads / c.kv_heads;
   // decode attention splits: 128 positions each, sized for the longest attended range
-  const int S = attn_splits(c.max_seq_len, c.head_dim);
+  // decode attention splits sized for the longest attended range of each layer kind: head_dim <= 64
+  // uses the tile kernel (whole K/V tiles staged before the wait), wider heads the streaming
+  // kernel with 256-position splits (measured faster at 128)
+  m->attn_spl = c.head_dim <= 64 ? 0 : 256;
+  auto n_splits = [&](int range) { return m->attn_spl ? (range + m->attn_spl - 1) / m->attn_spl : attn_splits(range, c.head_dim); };
+  const int S = n_splits(c.max_seq_len);
   m->splits_full = S;
-  m->splits_swa = c.sliding_window > 0 ? attn_splits(std::min(c.sliding_window, c.max_seq_len), c.head_dim) : S;
+  m->splits_swa = c.sliding_window > 0 ? n_splits(std::min(c.sliding_window, c.max_seq_len)) : S;
   ms_status s = MS_OK;
   s = s ? s : m->alloc(&m->h, (size_t)H * 4);
   s = s ? s : m->alloc(&m->h_last, (size_t)H * 4);
@@ -1170,7 +1183,13 @@ ms_status ms_model_batch_open(ms_model* m, int B) {
   m->bt = new BatchRt();
   BatchRt& b = *m->bt;
   b.B = B;
-  const int S = std::max(m->splits_full, m->splits_swa), EK = B * c.top_k;
+  const int units = c.kv_heads * B, sms = m->ctx->dc.sm_count;
+  b.spl_full = attn_split_positions(c.max_seq_len, units, sms);
+  b.S_full = (c.max_seq_len + b.spl_full - 1) / b.spl_full;
+  const int swa_range = c.sliding_window > 0 ? std::min(c.sliding_window, c.max_seq_len) : c.max_seq_len;
+  b.spl_swa = attn_split_positions(swa_range, units, sms);
+  b.S_swa = (swa_range + b.spl_swa - 1) / b.spl_swa;
+  const int S = std::max(b.S_full, b.S_swa), EK = B * c.top_k;
   ms_status s = MS_OK;
   s = s ? s : balloc(m, &b.st, sizeof(BatchState));
   s = s ? s : balloc(m, &b.tok_in, (size_t)B * 4);
@@ -1314,6 +1333,53 @@ ms_status ms_model_batch_last_logits(ms_model* m, float* out) {
   MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
   MS_CUDA(m->ctx, cudaMemcpy(out, m->bt->logits, (size_t)m->bt->B * m->cfg.vocab * 4, cudaMemcpyDeviceToHost));
   return MS_OK;
+}
+
+ms_status ms_model_batch_profile_step(ms_model* m, float* us, int max, int* n) {
+  if (!us || !n || max <= 0) return MS_ERR_INVALID_ARG;
+  ms_status st = batch_ready(m, 0);
+  if (st != MS_OK) return st;
+  if (m->bt->kernels_per_step <= 0) return fail(m->ctx, MS_ERR_STATE, "profile after at least one batch step");
+  cudaStream_t s = m->ctx->stream, cs = m->ctx->own;
+  constexpr int kWarm = 3, kRuns = 10;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  MS_CUDA(m->ctx, cudaEventCreate(&e0));
+  MS_CUDA(m->ctx, cudaEventCreate(&e1));
+  int k = 0;
+  for (int c = 0; c < kBatchClasses && k < max && st == MS_OK; ++c) {
+    // this class's launches of one batch step alone, PDL-chained as in the real step
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    st = ms_sync(m->ctx);
+    if (st != MS_OK) break;
+    MS_CUDA(m->ctx, cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    m->prof_class = c;
+    st = enqueue_batch_step(m, cs);
+    m->prof_class = -1;
+    cudaError_t e = cudaStreamEndCapture(cs, &g);
+    if (st == MS_OK && e != cudaSuccess) st = cuda_fail(m->ctx, e, "cudaStreamEndCapture (batch profile)");
+    if (st == MS_OK && (e = cudaGraphInstantiate(&ge, g, 0)) != cudaSuccess)
+      st = cuda_fail(m->ctx, e, "cudaGraphInstantiate (batch profile)");
+    for (int r = 0; r < kWarm + kRuns && st == MS_OK; ++r) {
+      if (r == kWarm) cudaEventRecord(e0, s);
+      if ((e = cudaGraphLaunch(ge, s)) != cudaSuccess) st = cuda_fail(m->ctx, e, "cudaGraphLaunch (batch profile)");
+    }
+    if (st == MS_OK) {
+      cudaEventRecord(e1, s);
+      st = ms_sync(m->ctx);
+    }
+    if (st == MS_OK) {
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, e0, e1);
+      us[k++] = ms * 1000.f / kRuns;
+    }
+    if (ge) cudaGraphExecDestroy(ge);
+    if (g) cudaGraphDestroy(g);
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  *n = k;
+  return st;
 }
 
 int ms_model_batch_kernels_per_step(const ms_model* m) { return m && m->bt ? m->bt->kernels_per_step : 0; }

@@ -389,6 +389,17 @@ class Engine:
         check(lib().ms_model_batch_last_logits(self.h, o.ctypes.data_as(C.POINTER(C.c_float))), self.ctx.h)
         return o
 
+    BATCH_CLASSES = ["step_start", "qkv_q8", "attention", "o_q8", "router", "expert_grouping", "gate_up", "down",
+                     "residual", "lm_head"]
+
+    def batch_profile_step(self) -> dict:
+        """Device microseconds of each launch class of one batch step, measured alone."""
+        buf = np.empty(64, dtype=np.float32)
+        n = C.c_int()
+        check(lib().ms_model_batch_profile_step(self.h, buf.ctypes.data_as(C.POINTER(C.c_float)), buf.size,
+                                                C.byref(n)), self.ctx.h)
+        return {k: round(float(v), 1) for k, v in zip(self.BATCH_CLASSES, buf[:n.value])}
+
     @property
     def batch_kernels_per_step(self) -> int:
         return lib().ms_model_batch_kernels_per_step(self.h)
