@@ -55,6 +55,7 @@ struct PhaseParams {
   const uint8_t* w1;       // up (GATEUP)
   int64_t expert_stride;   // bytes per expert matrix
   int rb;                  // bytes per streamed row
+  int rs;                  // row stride in a shared-memory stage (rb, or rb + 16 to spread banks)
   int cols;                // reduction length (H for GATEUP, I for DOWN)
   int rows;                // rows per expert matrix (I for GATEUP, H for DOWN)
   int tile_rows;           // output rows per item (16)
@@ -289,6 +290,34 @@ __device__ __forceinline__ void item_epilogue(const PhaseParams& p, const SlotIn
   }
 }
 
+// Shared-memory row stride of a stage: rows whose length is a multiple of 16 bytes but an even
+// number of 16-byte units would put the eight rows of an MMA fragment on the same banks; they get
+// 16 bytes of padding (copied row by row).  Other rows stay densely packed (one copy per matrix).
+__host__ __device__ __forceinline__ int stage_row_stride(int rb) {
+  return (rb % 16 == 0 && (rb / 16) % 2 == 0) ? rb + 16 : rb;
+}
+
+// Fills one stage (run by the whole producer warp): `tile_rows` rows of w0 (and of w1 after them
+// when two) starting at byte `base`, rows at stride rs in shared memory.
+__device__ __forceinline__ void issue_stage(uint8_t* dst, const uint8_t* w0, const uint8_t* w1, int64_t base, int rb,
+                                            int rs, int tile_rows, bool two, uint64_t* bar, uint64_t pol, int lane) {
+  const uint32_t part = (uint32_t)(tile_rows * rb);
+  if (lane == 0) mbar_expect_tx(bar, (two ? 2u : 1u) * part);
+  __syncwarp();
+  if (rs == rb) {
+    if (lane == 0) {
+      bulk_g2s_stream(dst, w0 + base, part, bar, pol);
+      if (two) bulk_g2s_stream(dst + part, w1 + base, part, bar, pol);
+    }
+  } else {
+    const int nr = (two ? 2 : 1) * tile_rows;
+    for (int r = lane; r < nr; r += 32) {
+      const uint8_t* src = (r < tile_rows ? w0 : w1) + base + (int64_t)(r % tile_rows) * rb;
+      bulk_g2s_stream(dst + (size_t)r * rs, src, (uint32_t)rb, bar, pol);
+    }
+  }
+}
+
 // RT = MMA row tiles per item: 2 for GATEUP (16 gate + 16 up rows), 1 for DOWN / PLAIN (16 rows).
 template <int FMT, int NBW, int RT>
 __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParams p) {
@@ -345,23 +374,22 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
   if (my_n <= 0) return;
 
   if (warp == kCW) {
-    // ---------------- producer ----------------
+    // ---------------- producer (whole warp: per-row copies when rows are padded) ----------------
+    const uint64_t pol = policy_evict_first();
+    const uint32_t part_bytes = (uint32_t)(p.tile_rows * p.rb);
+    int issued = 0;
+    for (int j = 0; j < my_n; ++j) {
+      const int s = j % p.ns, n = j / p.ns;
+      if (n > 0 && !__all_sync(0xffffffffu, mbar_wait(&empty[s], (uint32_t)((n - 1) & 1), p.err, EF_TIMEOUT_EMPTY)))
+        break;
+      const int item = begin + j;
+      const int ls = item / p.n_tiles, t = item % p.n_tiles;
+      const int64_t base = (int64_t)si->expert[ls] * p.expert_stride + (int64_t)t * part_bytes;
+      issue_stage(stages + (size_t)s * p.stage_bytes, p.w0, p.w1, base, p.rb, p.rs, p.tile_rows,
+                  p.mode == MODE_GATEUP, &full[s], pol, lane);
+      ++issued;
+    }
     if (lane == 0) {
-      const uint64_t pol = policy_evict_first();
-      const uint32_t part_bytes = (uint32_t)(p.tile_rows * p.rb);
-      int issued = 0;
-      for (int j = 0; j < my_n; ++j) {
-        const int s = j % p.ns, n = j / p.ns;
-        if (n > 0 && !mbar_wait(&empty[s], (uint32_t)((n - 1) & 1), p.err, EF_TIMEOUT_EMPTY)) break;
-        const int item = begin + j;
-        const int ls = item / p.n_tiles, t = item % p.n_tiles;
-        const int64_t base = (int64_t)si->expert[ls] * p.expert_stride + (int64_t)t * part_bytes;
-        uint8_t* dst = stages + (size_t)s * p.stage_bytes;
-        mbar_expect_tx(&full[s], (uint32_t)p.stage_bytes);
-        bulk_g2s_stream(dst, p.w0 + base, part_bytes, &full[s], pol);
-        if (p.mode == MODE_GATEUP) bulk_g2s_stream(dst + part_bytes, p.w1 + base, part_bytes, &full[s], pol);
-        ++issued;
-      }
       PHASE_TRACE(11);
       // make sure no copy into this CTA's shared memory is still in flight at exit
       for (int j = max(0, issued - p.ns); j < issued; ++j)
@@ -381,11 +409,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
 #pragma unroll
   for (int q = 0; q < RT; ++q) {
     if (p.mode == MODE_GATEUP) {
-      off0[q] = (uint32_t)(8 * q + g) * p.rb;           // gate row
-      off1[q] = (uint32_t)(16 + 8 * q + g) * p.rb;      // up row of the same output row
+      off0[q] = (uint32_t)(8 * q + g) * p.rs;           // gate row
+      off1[q] = (uint32_t)(16 + 8 * q + g) * p.rs;      // up row of the same output row
     } else {
-      off0[q] = (uint32_t)(16 * q + g) * p.rb;
-      off1[q] = (uint32_t)(16 * q + g + 8) * p.rb;
+      off0[q] = (uint32_t)(16 * q + g) * p.rs;
+      off1[q] = (uint32_t)(16 * q + g + 8) * p.rs;
     }
   }
   // Block b = warp + kCW*i of a row starts at row + 17*b; kCW*17 = 272 bytes is a multiple of 4,
@@ -538,7 +566,7 @@ struct GroupParams {
   const uint8_t* w0;
   const uint8_t* w1;
   int64_t expert_stride;
-  int rb, cols, rows, n_tiles, stage_bytes, ns;
+  int rb, rs, cols, rows, n_tiles, stage_bytes, ns;
   const float* x;          // GATEUP: [B][cols] normed input; DOWN: act [entries][cols]
   const int* grp;          // [0] chunks, then (expert_local, entry_begin, n_tok) per chunk
   const int* ent_tok;      // token of each entry
@@ -715,25 +743,23 @@ __global__ void __launch_bounds__(kThreads, 1) moe_group_kernel(GroupParams p) {
   if (my_n <= 0) return;
 
   if (warp == kCW) {
-    if (lane == 0) {
-      const uint64_t pol = policy_evict_first();
-      const uint32_t part_bytes = (uint32_t)(16 * p.rb);
-      int issued = 0;
-      for (int j = 0; j < my_n; ++j) {
-        const int s = j % p.ns, n = j / p.ns;
-        if (n > 0 && !mbar_wait(&empty[s], (uint32_t)((n - 1) & 1), p.err, EF_TIMEOUT_EMPTY)) break;
-        const int item = begin + j;
-        const int ch = item / p.n_tiles, t = item % p.n_tiles;
-        const int64_t base = (int64_t)p.grp[1 + 3 * ch] * p.expert_stride + (int64_t)t * part_bytes;
-        uint8_t* dst = stages + (size_t)s * p.stage_bytes;
-        mbar_expect_tx(&full[s], (uint32_t)p.stage_bytes);
-        bulk_g2s_stream(dst, p.w0 + base, part_bytes, &full[s], pol);
-        if (p.mode == MODE_GATEUP) bulk_g2s_stream(dst + part_bytes, p.w1 + base, part_bytes, &full[s], pol);
-        ++issued;
-      }
+    const uint64_t pol = policy_evict_first();
+    const uint32_t part_bytes = (uint32_t)(16 * p.rb);
+    int issued = 0;
+    for (int j = 0; j < my_n; ++j) {
+      const int s = j % p.ns, n = j / p.ns;
+      if (n > 0 && !__all_sync(0xffffffffu, mbar_wait(&empty[s], (uint32_t)((n - 1) & 1), p.err, EF_TIMEOUT_EMPTY)))
+        break;
+      const int item = begin + j;
+      const int ch = item / p.n_tiles, t = item % p.n_tiles;
+      const int64_t base = (int64_t)p.grp[1 + 3 * ch] * p.expert_stride + (int64_t)t * part_bytes;
+      issue_stage(stages + (size_t)s * p.stage_bytes, p.w0, p.w1, base, p.rb, p.rs, 16, p.mode == MODE_GATEUP,
+                  &full[s], pol, lane);
+      ++issued;
+    }
+    if (lane == 0)
       for (int j = max(0, issued - p.ns); j < issued; ++j)
         mbar_wait(&full[j % p.ns], (uint32_t)((j / p.ns) & 1), p.err, EF_TIMEOUT_FULL);
-    }
     return;
   }
 
@@ -746,11 +772,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_group_kernel(GroupParams p) {
 #pragma unroll
   for (int q = 0; q < RT; ++q) {
     if (p.mode == MODE_GATEUP) {
-      off0[q] = (uint32_t)(8 * q + g) * p.rb;
-      off1[q] = (uint32_t)(16 + 8 * q + g) * p.rb;
+      off0[q] = (uint32_t)(8 * q + g) * p.rs;
+      off1[q] = (uint32_t)(16 + 8 * q + g) * p.rs;
     } else {
-      off0[q] = (uint32_t)(16 * q + g) * p.rb;
-      off1[q] = (uint32_t)(16 * q + g + 8) * p.rb;
+      off0[q] = (uint32_t)(16 * q + g) * p.rs;
+      off1[q] = (uint32_t)(16 * q + g + 8) * p.rs;
     }
   }
   uint32_t bs0[RT], bs1[RT], wa0[RT], wa1[RT], sh0[RT], sh1[RT];
@@ -1057,7 +1083,8 @@ cudaError_t launch_block_gemv(const DevCtx& c, int qtype, const uint8_t* w, int 
   if ((16 * rb) % 16) return cudaErrorInvalidValue;
   PhaseParams p = {};
   p.mode = MODE_PLAIN; p.fmt = fmt; p.w0 = w; p.expert_stride = 0; p.rb = rb; p.cols = cols; p.rows = rows;
-  p.tile_rows = 16; p.n_tiles = (rows + 15) / 16; p.stage_bytes = 16 * rb; p.ns = pick_stages(p.stage_bytes);
+  p.tile_rows = 16; p.n_tiles = (rows + 15) / 16; p.rs = stage_row_stride(rb); p.stage_bytes = 16 * p.rs;
+  p.ns = pick_stages(p.stage_bytes);
   p.x = x; p.bias0 = bias; p.out = y; p.accumulate = accumulate; p.K = 1; p.err = c.err;
   return dispatch_phase(c, p, s);
 }
@@ -1133,14 +1160,16 @@ cudaError_t launch_moe_mxfp4(const DevCtx& c, const MoeArgs& a, cudaStream_t s) 
   p.oai = a.oai_swiglu; p.err = c.err;
   // phase 1: gate + up + activation
   p.mode = MODE_GATEUP; p.fmt = fg; p.w0 = a.gate; p.w1 = a.up; p.expert_stride = (int64_t)a.I * rbg; p.rb = rbg;
-  p.cols = a.H; p.rows = a.I; p.tile_rows = 16; p.n_tiles = a.I / 16; p.stage_bytes = 32 * rbg;
+  p.cols = a.H; p.rows = a.I; p.tile_rows = 16; p.n_tiles = a.I / 16; p.rs = stage_row_stride(rbg);
+  p.stage_bytes = 32 * p.rs;
   p.ns = pick_stages(p.stage_bytes); p.x = a.x; p.bias0 = a.gate_b; p.bias1 = a.up_b; p.act = a.act;
   if ((16 * rbg) % 16 || p.expert_stride % 16 || a.I % 16 || a.H % 16) return cudaErrorInvalidValue;
   cudaError_t e = dispatch_phase(c, p, s);
   if (e != cudaSuccess) return e;
   // phase 2: down -> per-slot partial rows
   p.mode = MODE_DOWN; p.fmt = fd; p.w0 = a.down; p.w1 = nullptr; p.expert_stride = (int64_t)a.H * rbd; p.rb = rbd;
-  p.cols = a.I; p.rows = a.H; p.tile_rows = 16; p.n_tiles = a.H / 16; p.stage_bytes = 16 * rbd;
+  p.cols = a.I; p.rows = a.H; p.tile_rows = 16; p.n_tiles = a.H / 16; p.rs = stage_row_stride(rbd);
+  p.stage_bytes = 16 * p.rs;
   p.ns = pick_stages(p.stage_bytes); p.x = a.act; p.bias0 = a.down_b; p.bias1 = nullptr;
   p.partial = a.partial; p.tile_cnt = a.tile_cnt; p.h = a.h; p.out = a.out;
   if ((16 * rbd) % 16 || p.expert_stride % 16) return cudaErrorInvalidValue;
@@ -1178,12 +1207,14 @@ cudaError_t launch_moe_group(const DevCtx& c, const GroupMoeArgs& a, int part, c
   GroupParams p = {};
   p.grp = a.grp; p.ent_tok = a.ent_tok; p.oai = a.oai_swiglu; p.err = c.err;
   p.mode = MODE_GATEUP; p.fmt = fg; p.w0 = a.gate; p.w1 = a.up; p.expert_stride = (int64_t)a.I * rbg; p.rb = rbg;
-  p.cols = a.H; p.rows = a.I; p.n_tiles = a.I / 16; p.stage_bytes = 32 * rbg; p.ns = pick_group_stages(p.stage_bytes);
+  p.cols = a.H; p.rows = a.I; p.n_tiles = a.I / 16; p.rs = stage_row_stride(rbg); p.stage_bytes = 32 * p.rs;
+  p.ns = pick_group_stages(p.stage_bytes);
   p.x = a.x; p.bias0 = a.gate_b; p.bias1 = a.up_b; p.out = a.act;
   if ((16 * rbg) % 16 || p.expert_stride % 16 || a.I % 16) return cudaErrorInvalidValue;
   if (part == 1) return dispatch_group(c, p, s);
   p.mode = MODE_DOWN; p.fmt = fd; p.w0 = a.down; p.w1 = nullptr; p.expert_stride = (int64_t)a.H * rbd; p.rb = rbd;
-  p.cols = a.I; p.rows = a.H; p.n_tiles = a.H / 16; p.stage_bytes = 16 * rbd; p.ns = pick_group_stages(p.stage_bytes);
+  p.cols = a.I; p.rows = a.H; p.n_tiles = a.H / 16; p.rs = stage_row_stride(rbd); p.stage_bytes = 16 * p.rs;
+  p.ns = pick_group_stages(p.stage_bytes);
   p.x = a.act; p.bias0 = a.down_b; p.bias1 = nullptr; p.out = a.y;
   if ((16 * rbd) % 16 || p.expert_stride % 16) return cudaErrorInvalidValue;
   return dispatch_group(c, p, s);
