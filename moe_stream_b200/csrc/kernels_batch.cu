@@ -99,30 +99,80 @@ __global__ void __launch_bounds__(256) embed_batch_kernel(const BatchState* st, 
 
 // ---------------- Q8_0 projection of a batch ----------------
 constexpr int kQBWarps = 8;
+constexpr int kQBChunk = 512;    // activation columns staged per pass (3 CTAs per SM)
 
-__global__ void __launch_bounds__(kQBWarps * 32) q8_gemm_batch_kernel(Q8BatchArgs a, int rb, uint32_t* err) {
-  extern __shared__ __align__(16) uint8_t wt[];   // [16][rb] (+16 bytes of slack)
+__global__ void __launch_bounds__(kQBWarps * 32, 3) q8_gemm_batch_kernel(Q8BatchArgs a, int rb, int kc, uint32_t* err) {
+  // shared memory: weight tile [16][rb] (+16) | codes [B][kc + 16] | scales [B][kc / 32 + 4], one
+  // kc-column slice of the activations at a time
+  extern __shared__ __align__(16) uint8_t sm[];
   __shared__ float red[kQBWarps][16][kMaxBatch + 1];
   __shared__ __align__(8) uint64_t bar;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int tile = blockIdx.x;
+  const int nb = a.cols / 32, B = a.B, NT = (B + 7) / 8;
+  const int nbc = kc / 32;
+  const int xs_stride = kc + 16, ds_stride = nbc + 4;
   const uint32_t bytes = (uint32_t)(16 * rb);
+  uint8_t* wt = sm;
+  int8_t* xs = reinterpret_cast<int8_t*>(sm + (((size_t)bytes + 16 + 15) & ~(size_t)15));
+  float* ds = reinterpret_cast<float*>(xs + (size_t)B * xs_stride);
   if (threadIdx.x == 0) {   // weights do not depend on the previous kernel
     mbar_init(&bar, 1);
     fence_mbar_init();
     mbar_expect_tx(&bar, bytes);
     bulk_g2s_stream(wt, a.w + (size_t)tile * bytes, bytes, &bar, policy_evict_first());
   }
-  __syncthreads();
   pdl_wait_prior();
   pdl_launch_dependents();
-  const bool ok = mbar_wait(&bar, 0, err, EF_TIMEOUT_FULL);
-  const int nb = a.cols / 32, B = a.B, NT = (B + 7) / 8;
+  bool ok = true;
   float acc[kMaxBatch / 8][4];
 #pragma unroll
   for (int t = 0; t < kMaxBatch / 8; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
-  if (ok) {
-    for (int blk = warp; blk < nb; blk += kQBWarps) {
+  for (int k0 = 0; k0 < a.cols; k0 += kc) {
+    // the batch's activation codes and block scales for columns [k0, k0 + kc) (L2-resident)
+    if (k0) __syncthreads();
+    const int vpr = kc / 16, b0k = k0 / 32;
+    {
+      // all of the slice's loads in flight before the shared-memory stores
+      constexpr int kU = 8;
+      for (int i0 = threadIdx.x; i0 < B * vpr; i0 += kU * blockDim.x) {
+        uint4 v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int i = i0 + u * blockDim.x;
+          if (i < B * vpr) {
+            const int tb = i / vpr, q = i - tb * vpr;
+            v[u] = __ldg(reinterpret_cast<const uint4*>(a.xq + (size_t)tb * a.cols + k0) + q);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int i = i0 + u * blockDim.x;
+          if (i < B * vpr) {
+            const int tb = i / vpr, q = i - tb * vpr;
+            *reinterpret_cast<uint4*>(xs + (size_t)tb * xs_stride + 16 * q) = v[u];
+          }
+        }
+      }
+      for (int i0 = threadIdx.x; i0 < B * nbc; i0 += kU * blockDim.x) {
+        float v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int i = i0 + u * blockDim.x;
+          v[u] = i < B * nbc ? __ldg(a.xd + (size_t)(i / nbc) * nb + b0k + i % nbc) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int i = i0 + u * blockDim.x;
+          if (i < B * nbc) ds[(i / nbc) * ds_stride + i % nbc] = v[u];
+        }
+      }
+    }
+    __syncthreads();
+    if (k0 == 0) ok = mbar_wait(&bar, 0, err, EF_TIMEOUT_FULL);
+    if (!ok) continue;
+    for (int bl = warp; bl < nbc; bl += kQBWarps) {
+      const int blk = b0k + bl;
       const uint8_t* r0 = wt + (size_t)g * rb + 34 * blk;
       const uint8_t* r1 = r0 + (size_t)8 * rb;
       const uint32_t a0 = lds_u32_a2(r0 + 2 + 4 * c), a1 = lds_u32_a2(r1 + 2 + 4 * c);
@@ -135,15 +185,15 @@ __global__ void __launch_bounds__(kQBWarps * 32) q8_gemm_batch_kernel(Q8BatchArg
           const int tb = 8 * t + g;   // this lane's B column
           uint32_t b0 = 0u, b1 = 0u;
           if (tb < B) {
-            const int8_t* xr = a.xq + (size_t)tb * a.cols + 32 * blk + 4 * c;
+            const int8_t* xr = xs + (size_t)tb * xs_stride + 32 * bl + 4 * c;
             b0 = *reinterpret_cast<const uint32_t*>(xr);
             b1 = *reinterpret_cast<const uint32_t*>(xr + 16);
           }
           int d[4] = {0, 0, 0, 0};
           mma_s8_16832(d, a0, a1, a2, a3, b0, b1);
           const int t0 = 8 * t + 2 * c;
-          const float dx0 = t0 < B ? a.xd[(size_t)t0 * nb + blk] : 0.f;
-          const float dx1 = t0 + 1 < B ? a.xd[(size_t)(t0 + 1) * nb + blk] : 0.f;
+          const float dx0 = t0 < B ? ds[t0 * ds_stride + bl] : 0.f;
+          const float dx1 = t0 + 1 < B ? ds[(t0 + 1) * ds_stride + bl] : 0.f;
           acc[t][0] = fmaf((float)d[0], dw0 * dx0, acc[t][0]);
           acc[t][1] = fmaf((float)d[1], dw0 * dx1, acc[t][1]);
           acc[t][2] = fmaf((float)d[2], dw1 * dx0, acc[t][2]);
@@ -465,11 +515,18 @@ cudaError_t launch_q8_gemm_batch(const DevCtx& c, const Q8BatchArgs& a, cudaStre
     return cudaErrorInvalidValue;
   if (reinterpret_cast<uintptr_t>(a.w) % 16 || reinterpret_cast<uintptr_t>(a.xq) % 4) return cudaErrorInvalidValue;
   const int rb = a.cols / 32 * 34;
-  const size_t smem = (size_t)16 * rb + 16;
+  // activation slices (whole 32-column blocks): 512 columns keep 3 CTAs per SM when the grid
+  // exceeds the SM count; a grid of at most one CTA per SM takes wider slices (fewer passes)
+  const int chunk = a.rows / 16 > c.sm_count ? kQBChunk : 4 * kQBChunk;
+  int np = (a.cols + chunk - 1) / chunk;
+  while (a.cols % np || (a.cols / np) % 32) ++np;
+  const int kc = a.cols / np;
+  const size_t smem = (((size_t)16 * rb + 16 + 15) & ~(size_t)15) + (size_t)a.B * (kc + 16) +
+                      (size_t)a.B * (kc / 32 + 4) * 4;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   cudaError_t e = set_smem((const void*)q8_gemm_batch_kernel, smem);
   if (e != cudaSuccess) return e;
-  return launch_pdl_b(q8_gemm_batch_kernel, dim3((unsigned)(a.rows / 16)), dim3(kQBWarps * 32), smem, s, a, rb,
+  return launch_pdl_b(q8_gemm_batch_kernel, dim3((unsigned)(a.rows / 16)), dim3(kQBWarps * 32), smem, s, a, rb, kc,
                       c.err);
 }
 

@@ -588,11 +588,10 @@ __global__ void __launch_bounds__(kTThreads) attn_tile_kernel(AttnArgs a, uint32
   if (threadIdx.x == 0) a.cnt[kh] = 0u;
 }
 
-template <int HD, int REP>
-__global__ void __launch_bounds__(kAThreads, 2) attn_decode_kernel(AttnArgs a, uint32_t* err) {
+template <int HD, int REP, int PB, int MINB>
+__global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a, uint32_t* err) {
   constexpr int DPL = HD / 32;                 // head dims per lane
   constexpr int GL = 32 / REP;                 // lanes per head after the reduce-scatter
-  constexpr int PB = 8;                        // rows loaded per batch
   extern __shared__ __align__(16) float dyn[];
   float* ow = dyn;                             // [kAWarps][REP][HD] per-warp outputs
   float* wsm = ow + kAWarps * REP * HD;        // [S][REP] split weights of the final merge
@@ -1122,10 +1121,19 @@ cudaError_t launch_attn_k(const AttnArgs& a, const DevCtx& c, dim3 grid, cudaStr
     return launch_pdl(attn_tile_kernel<HD, REP>, grid, dim3(kTThreads), smem, s, a, c.err);
   }
   const size_t smem = ((size_t)kAWarps * REP * HD + (size_t)a.S * REP) * sizeof(float);
-  cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-  if (e != cudaSuccess) return e;
-  return launch_pdl(attn_decode_kernel<HD, REP>, grid, dim3(kAThreads), smem, s, a, c.err);
+  static int variant = getenv("MS_ATTN_VARIANT") ? atoi(getenv("MS_ATTN_VARIANT")) : 0;
+#define ATTN_V(PB_, MB_)                                                                                 \
+  {                                                                                                      \
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD, REP, PB_, MB_>,                          \
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);        \
+    if (e != cudaSuccess) return e;                                                                      \
+    return launch_pdl(attn_decode_kernel<HD, REP, PB_, MB_>, grid, dim3(kAThreads), smem, s, a, c.err); \
+  }
+  if (variant == 1) ATTN_V(4, 3)
+  if (variant == 2) ATTN_V(16, 1)
+  if (variant == 3) ATTN_V(8, 1)
+  ATTN_V(8, 2)
+#undef ATTN_V
 }
 
 template <int HD>

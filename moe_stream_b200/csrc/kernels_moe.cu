@@ -949,76 +949,8 @@ __device__ __forceinline__ float router_block_sum(float v, float* red) {
   return t;
 }
 
-// One CTA per expert row.  Before waiting for the previous kernel the CTA starts a bulk copy of
-// its router row into shared memory; then it normalises h (RMSNorm, h read twice, the second
-// time from L1), dots its row and writes one logit; CTAs 0.. also write the normed x as the
-// expert GEMVs' activation terms.  The last CTA to finish selects the top-k with one warp.
-__global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, uint32_t* err, int row_async) {
-  extern __shared__ __align__(16) float wrow[];   // [H] this expert's router row
-  __shared__ float red[kRouterThreads / 32];
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ uint32_t last;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x;
-  if (blockIdx.y) {   // token b of a batch
-    const int b = blockIdx.y;
-    if (a.h) a.h += (size_t)b * a.H;
-    a.xn += (size_t)b * a.H;
-    a.logits += (size_t)b * a.E;
-    a.idx += b * a.K;
-    a.wts += b * a.K;
-    a.counter += b;
-  }
-  const float* wr = a.w + (size_t)e * a.H;
-  if (row_async && threadIdx.x == 0) {   // weights do not depend on the previous kernel
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-    mbar_expect_tx(&bar, (uint32_t)a.H * 4u);
-    bulk_g2s(wrow, wr, (uint32_t)a.H * 4u, &bar);
-  }
-  pdl_wait_prior();
-  pdl_launch_dependents();   // the next kernel may start its own (weight) prefetch now
-  float dot = 0.f;
-  float inv = 1.f;
-  if (a.h) {
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < a.H; i += kRouterThreads) { const float v = a.h[i]; ss += v * v; }
-    ss = router_block_sum(ss, red);   // (its barrier also publishes the mbarrier's initialisation)
-    inv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
-  } else {
-    __syncthreads();
-  }
-  bool row_ok = true;
-  if (row_async) row_ok = mbar_wait(&bar, 0, err, EF_TIMEOUT_FULL);
-  const float* wsrc = row_async ? wrow : wr;
-  if (row_ok) {
-    for (int i = threadIdx.x; i < a.H; i += kRouterThreads) {
-      const float v = a.h ? (a.h[i] * inv) * a.norm_w[i] : a.xn[i];
-      if (a.h && e == 0) a.xn[i] = v;
-      dot = fmaf(v, wsrc[i], dot);
-    }
-  }
-  dot = router_block_sum(dot, red);
-  if (threadIdx.x == 0) {
-    float v = dot + (a.b ? a.b[e] : 0.f);
-    if (a.mask && a.mask[e]) v = -INFINITY;
-    a.logits[e] = v;
-    __threadfence();
-    last = (atomicAdd(a.counter, 1u) == gridDim.x - 1) ? 1u : 0u;
-  }
-  if (a.xterm) {
-    // the normed x as the expert GEMVs' B terms: warp w of CTA e takes 32-element blocks
-    // e*8 + w, e*8 + w + 8*E, ... (same arithmetic as xn above, so the terms encode xn exactly)
-    const int nb = a.H / 32, nw = kRouterThreads / 32;
-    for (int b = e * nw + warp; b < nb; b += (int)gridDim.x * nw) {
-      const int i = 32 * b + lane;
-      const float v = a.h ? (a.h[i] * inv) * a.norm_w[i] : a.xn[i];
-      umma::quantize_terms_warp(v, lane, a.xterm, nb, b);
-    }
-  }
-  __syncthreads();
-  if (!last || warp != 0) return;
-  __threadfence();
+// Top-k selection and routing weights of one token by one warp, after every logit is written.
+__device__ __forceinline__ void router_select(const RouterArgs& a, uint32_t* err, int lane) {
   // ---- top-k by one warp (ties -> lower index, as a stable descending sort) ----
   // lane l holds experts l, l + 32, ...; a 32-bit mask per lane marks the ones taken
   const int per = (a.E + 31) / 32;
@@ -1070,6 +1002,129 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, ui
     for (int k = 0; k < a.K; ++k) { a.idx[k] = sel_i[k]; a.wts[k] = w[k]; }
     *a.counter = 0u;
   }
+}
+
+// One CTA per expert row.  Before waiting for the previous kernel the CTA starts a bulk copy of
+// its router row into shared memory; then it normalises h (RMSNorm, h read twice, the second
+// time from L1), dots its row and writes one logit; CTAs 0.. also write the normed x as the
+// expert GEMVs' activation terms.  The last CTA to finish selects the top-k with one warp.
+__global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, uint32_t* err, int row_async) {
+  extern __shared__ __align__(16) float wrow[];   // [H] this expert's router row
+  __shared__ float red[kRouterThreads / 32];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x;
+  const float* wr = a.w + (size_t)e * a.H;
+  if (row_async && threadIdx.x == 0) {   // weights do not depend on the previous kernel
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_expect_tx(&bar, (uint32_t)a.H * 4u);
+    bulk_g2s(wrow, wr, (uint32_t)a.H * 4u, &bar);
+  }
+  pdl_wait_prior();
+  pdl_launch_dependents();   // the next kernel may start its own (weight) prefetch now
+  float dot = 0.f;
+  float inv = 1.f;
+  if (a.h) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < a.H; i += kRouterThreads) { const float v = a.h[i]; ss += v * v; }
+    ss = router_block_sum(ss, red);   // (its barrier also publishes the mbarrier's initialisation)
+    inv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
+  } else {
+    __syncthreads();
+  }
+  bool row_ok = true;
+  if (row_async) row_ok = mbar_wait(&bar, 0, err, EF_TIMEOUT_FULL);
+  const float* wsrc = row_async ? wrow : wr;
+  if (row_ok) {
+    for (int i = threadIdx.x; i < a.H; i += kRouterThreads) {
+      const float v = a.h ? (a.h[i] * inv) * a.norm_w[i] : a.xn[i];
+      if (a.h && e == 0) a.xn[i] = v;
+      dot = fmaf(v, wsrc[i], dot);
+    }
+  }
+  dot = router_block_sum(dot, red);
+  if (threadIdx.x == 0) {
+    float v = dot + (a.b ? a.b[e] : 0.f);
+    if (a.mask && a.mask[e]) v = -INFINITY;
+    a.logits[e] = v;
+    __threadfence();
+    last = (atomicAdd(a.counter, 1u) == gridDim.x - 1) ? 1u : 0u;
+  }
+  if (a.xterm) {
+    // the normed x as the expert GEMVs' B terms: warp w of CTA e takes 32-element blocks
+    // e*8 + w, e*8 + w + 8*E, ... (same arithmetic as xn above, so the terms encode xn exactly)
+    const int nb = a.H / 32, nw = kRouterThreads / 32;
+    for (int b = e * nw + warp; b < nb; b += (int)gridDim.x * nw) {
+      const int i = 32 * b + lane;
+      const float v = a.h ? (a.h[i] * inv) * a.norm_w[i] : a.xn[i];
+      umma::quantize_terms_warp(v, lane, a.xterm, nb, b);
+    }
+  }
+  __syncthreads();
+  if (!last || warp != 0) return;
+  __threadfence();
+  router_select(a, err, lane);
+}
+
+// Batched router: grid (ceil(E / kRBRows), tokens).  Each CTA normalises its token's h into
+// shared memory and dots kRBRows router rows (a warp per row, float4 loads); the last CTA of a
+// token selects its top-k.
+constexpr int kRBRows = 16;
+__global__ void __launch_bounds__(kRouterThreads) router_batch_kernel(RouterArgs a, uint32_t* err) {
+  extern __shared__ __align__(16) float xs[];   // [H] normed input
+  __shared__ float red[kRouterThreads / 32];
+  __shared__ uint32_t last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y;
+  a.h += (size_t)b * a.H;
+  a.xn += (size_t)b * a.H;
+  a.logits += (size_t)b * a.E;
+  a.idx += b * a.K;
+  a.wts += b * a.K;
+  a.counter += b;
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < a.H; i += kRouterThreads) { const float v = a.h[i]; ss += v * v; }
+  ss = router_block_sum(ss, red);
+  const float inv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
+  for (int i = threadIdx.x; i < a.H; i += kRouterThreads) {
+    const float v = (a.h[i] * inv) * a.norm_w[i];
+    xs[i] = v;
+    if (blockIdx.x == 0) a.xn[i] = v;
+  }
+  __syncthreads();
+  for (int r = warp; r < kRBRows; r += kRouterThreads / 32) {
+    const int e = blockIdx.x * kRBRows + r;
+    if (e >= a.E) break;
+    const float4* w4 = reinterpret_cast<const float4*>(a.w + (size_t)e * a.H);
+    const float4* x4 = reinterpret_cast<const float4*>(xs);
+    float dot = 0.f;
+    for (int i = lane; i < a.H / 4; i += 32) {
+      const float4 w = __ldg(w4 + i), x = x4[i];
+      dot = fmaf(x.x, w.x, dot);
+      dot = fmaf(x.y, w.y, dot);
+      dot = fmaf(x.z, w.z, dot);
+      dot = fmaf(x.w, w.w, dot);
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) {
+      float v = dot + (a.b ? a.b[e] : 0.f);
+      if (a.mask && a.mask[e]) v = -INFINITY;
+      a.logits[e] = v;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = (atomicAdd(a.counter, 1u) == gridDim.x - 1) ? 1u : 0u;
+  }
+  __syncthreads();
+  if (!last || warp != 0) return;
+  __threadfence();
+  router_select(a, err, lane);
 }
 
 }  // namespace
@@ -1127,6 +1182,23 @@ cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s) 
   if (a.K < 1 || a.K > kMaxK || a.K > a.E || a.E > kRouterMaxE || !a.counter || a.batch < 1 ||
       (a.batch > 1 && a.xterm))
     return cudaErrorInvalidValue;
+  if (a.batch > 1) {
+    if (a.H % 4 || !a.h || reinterpret_cast<uintptr_t>(a.w) % 16) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)a.H * 4;
+    cudaError_t e = cudaFuncSetAttribute(router_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((a.E + kRBRows - 1) / kRBRows), (unsigned)a.batch);
+    cfg.blockDim = dim3(kRouterThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, router_batch_kernel, a, c.err);
+  }
   cudaLaunchConfig_t cfg = {};
   // the router row goes to shared memory by a bulk copy when it is 16-byte aligned (all rows are
   // when the matrix is and H % 4 == 0)
@@ -1136,7 +1208,7 @@ cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s) 
     cudaError_t e = cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  cfg.gridDim = dim3((unsigned)a.E, (unsigned)a.batch);
+  cfg.gridDim = dim3((unsigned)a.E);
   cfg.blockDim = dim3(kRouterThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
