@@ -1121,19 +1121,10 @@ cudaError_t launch_attn_k(const AttnArgs& a, const DevCtx& c, dim3 grid, cudaStr
     return launch_pdl(attn_tile_kernel<HD, REP>, grid, dim3(kTThreads), smem, s, a, c.err);
   }
   const size_t smem = ((size_t)kAWarps * REP * HD + (size_t)a.S * REP) * sizeof(float);
-  static int variant = getenv("MS_ATTN_VARIANT") ? atoi(getenv("MS_ATTN_VARIANT")) : 0;
-#define ATTN_V(PB_, MB_)                                                                                 \
-  {                                                                                                      \
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD, REP, PB_, MB_>,                          \
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);        \
-    if (e != cudaSuccess) return e;                                                                      \
-    return launch_pdl(attn_decode_kernel<HD, REP, PB_, MB_>, grid, dim3(kAThreads), smem, s, a, c.err); \
-  }
-  if (variant == 1) ATTN_V(4, 3)
-  if (variant == 2) ATTN_V(16, 1)
-  if (variant == 3) ATTN_V(8, 1)
-  ATTN_V(8, 2)
-#undef ATTN_V
+  cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD, REP, 8, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(attn_decode_kernel<HD, REP, 8, 2>, grid, dim3(kAThreads), smem, s, a, c.err);
 }
 
 template <int HD>

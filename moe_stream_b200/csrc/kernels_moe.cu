@@ -559,6 +559,8 @@ int pick_stages(int stage_bytes) {
 // token c's prescale (and, for Q4_K, its block sum) in the per-block epilogue.
 constexpr int kGT = 4;
 constexpr int kRouteThreads = 1024;
+constexpr int kGroupMaxStages = 16;
+constexpr int kGroupRedCnt = 64;   // reduction counters: groups x buffers per group
 
 struct GroupParams {
   int mode;                // MODE_GATEUP / MODE_DOWN
@@ -657,13 +659,13 @@ __global__ void __launch_bounds__(kRouteThreads) group_route_kernel(const int* i
 
 // B fragments of up to kGT tokens for the K-blocks this warp owns (column 2t: token t's x_hi,
 // 2t + 1: x_lo, each token prescaled by its own power of two); kbs / xsum: token c's (c = lane & 3)
-template <int FMT, int NBW>
-__device__ __forceinline__ void build_bfrag_group(const float* const (&xr)[kGT], int ntok, int nb, int warp, int lane,
+template <int FMT, int NBW, int GW>
+__device__ __forceinline__ void build_bfrag_group(const float* const (&xr)[kGT], int ntok, int nb, int wi, int lane,
                                                   uint32_t (&bf)[NBW][4], int (&kbs)[NBW], float (&xsum)[NBW]) {
   const int c = lane & 3, n = lane >> 2, tt = n >> 1, hl = n & 1;
 #pragma unroll
   for (int i = 0; i < NBW; ++i) {
-    const int b = warp + kCW * i;
+    const int b = wi + GW * i;
     bf[i][0] = bf[i][1] = bf[i][2] = bf[i][3] = 0u;
     kbs[i] = 0;
     xsum[i] = 0.f;
@@ -712,26 +714,28 @@ __device__ __forceinline__ void build_bfrag_group(const float* const (&xr)[kGT],
   }
 }
 
-template <int FMT, int NBW, int RT>
+// GW consumer warps share an item (split over its K blocks); the kCW / GW groups take items in turn.
+template <int FMT, int NBW, int RT, int GW>
 __global__ void __launch_bounds__(kThreads, 1) moe_group_kernel(GroupParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int G = kCW / GW;             // items in flight at once
   constexpr int kGRed = kGT * kRedRows;   // per-warp partial sums per item
+  extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
-  const int nrb = p.ns + 1;
-  float* red = reinterpret_cast<float*>(smem + (size_t)p.ns * p.stage_bytes);   // [nrb][kCW][kGRed]
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + (size_t)nrb * kCW * kGRed);
-  uint64_t* empty = full + kMaxStages;
-  uint32_t* red_cnt = reinterpret_cast<uint32_t*>(empty + kMaxStages);
-  int* abort_flag = reinterpret_cast<int*>(red_cnt + kMaxStages + 1);
+  const int nrbg = (p.ns + G - 1) / G + 1;   // reduction buffers per group: its warps run < ns items apart
+  float* red = reinterpret_cast<float*>(smem + (size_t)p.ns * p.stage_bytes);   // [G][nrbg][GW][kGRed]
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + (size_t)G * nrbg * GW * kGRed);
+  uint64_t* empty = full + kGroupMaxStages;
+  uint32_t* red_cnt = reinterpret_cast<uint32_t*>(empty + kGroupMaxStages);   // [G][nrbg]
+  int* abort_flag = reinterpret_cast<int*>(red_cnt + kGroupRedCnt);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_wait_prior();
   pdl_launch_dependents();
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    for (int b = 0; b <= kMaxStages; ++b) red_cnt[b] = 0u;
+    for (int b = 0; b < kGroupRedCnt; ++b) red_cnt[b] = 0u;
     for (int s = 0; s < p.ns; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kCW);
+      mbar_init(&empty[s], GW);
     }
     fence_mbar_init();
   }
@@ -763,6 +767,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_group_kernel(GroupParams p) {
     return;
   }
 
+  const int grp_i = warp / GW, wi = warp % GW;
   const int nb = p.cols / 32;
   const int c = lane & 3, g = lane >> 2;
   uint32_t bf[NBW][4];
@@ -782,14 +787,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_group_kernel(GroupParams p) {
   uint32_t bs0[RT], bs1[RT], wa0[RT], wa1[RT], sh0[RT], sh1[RT];
 #pragma unroll
   for (int q = 0; q < RT; ++q) {
-    bs0[q] = off0[q] + 17u * warp;
-    bs1[q] = off1[q] + 17u * warp;
+    bs0[q] = off0[q] + 17u * wi;
+    bs1[q] = off1[q] + 17u * wi;
     const uint32_t c0 = bs0[q] + 1 + 4 * c, c1 = bs1[q] + 1 + 4 * c;
     wa0[q] = c0 & ~3u; sh0[q] = (c0 & 3u) * 8u;
     wa1[q] = c1 & ~3u; sh1[q] = (c1 & 3u) * 8u;
   }
   int cur = -1, ntok = 0, ebeg = 0;
-  for (int j = 0; j < my_n; ++j) {
+  for (int j = grp_i; j < my_n; j += G) {
     if (*reinterpret_cast<volatile int*>(abort_flag)) break;
     const int s = j % p.ns, n = j / p.ns;
     const int item = begin + j;
@@ -804,7 +809,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_group_kernel(GroupParams p) {
         const int row = p.mode == MODE_GATEUP ? p.ent_tok[ent] : ent;
         xr[q] = p.x + (size_t)row * p.cols;
       }
-      build_bfrag_group<FMT, NBW>(xr, ntok, nb, warp, lane, bf, kbs, xsum);
+      build_bfrag_group<FMT, NBW, GW>(xr, ntok, nb, wi, lane, bf, kbs, xsum);
       cur = ch;
     }
     float acc0[RT], acc1[RT];
@@ -817,34 +822,34 @@ __global__ void __launch_bounds__(kThreads, 1) moe_group_kernel(GroupParams p) {
     const uint8_t* st = stages + (size_t)s * p.stage_bytes;
 #pragma unroll
     for (int i = 0; i < NBW; ++i) {
-      const int b = warp + kCW * i;
+      const int b = wi + GW * i;
       if (b < nb) {
         if constexpr (FMT == FMT_MXFP4) {
 #pragma unroll
           for (int q = 0; q < RT; ++q)
-            mx_block(st + bs0[q] + kCW * 17 * i, st + bs1[q] + kCW * 17 * i,
-                     reinterpret_cast<const uint32_t*>(st + wa0[q] + kCW * 17 * i),
-                     reinterpret_cast<const uint32_t*>(st + wa1[q] + kCW * 17 * i), sh0[q], sh1[q], bf[i], kbs[i],
+            mx_block(st + bs0[q] + GW * 17 * i, st + bs1[q] + GW * 17 * i,
+                     reinterpret_cast<const uint32_t*>(st + wa0[q] + GW * 17 * i),
+                     reinterpret_cast<const uint32_t*>(st + wa1[q] + GW * 17 * i), sh0[q], sh1[q], bf[i], kbs[i],
                      acc0[q], acc1[q]);
         } else {
           const float xscale = __int_as_float(max(127 * 8388608 + kbs[i], 0));
-          const int sbk = b >> 3;
+          const int sbk = b >> 3, sub = b & 7;
 #pragma unroll
           for (int q = 0; q < RT; ++q) {
             if constexpr (FMT == FMT_Q4K)
-              q4k_block(st + off0[q] + 144 * sbk, st + off1[q] + 144 * sbk, warp & 7, c, bf[i], xscale, xsum[i],
+              q4k_block(st + off0[q] + 144 * sbk, st + off1[q] + 144 * sbk, sub, c, bf[i], xscale, xsum[i],
                         acc0[q], acc1[q]);
             else
-              q6k_block(st + off0[q] + 210 * sbk, st + off1[q] + 210 * sbk, (warp & 7) >> 2, warp & 3, c, bf[i],
-                        xscale, acc0[q], acc1[q]);
+              q6k_block(st + off0[q] + 210 * sbk, st + off1[q] + 210 * sbk, sub >> 2, sub & 3, c, bf[i], xscale,
+                        acc0[q], acc1[q]);
           }
         }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    const int rbuf = j % nrb;
-    float* rw = red + ((size_t)rbuf * kCW + warp) * kGRed + c * kRedRows;   // token c's rows
+    const int rbuf = grp_i * nrbg + (j / G) % nrbg;
+    float* rw = red + ((size_t)rbuf * GW + wi) * kGRed + c * kRedRows;   // token c's rows
 #pragma unroll
     for (int q = 0; q < RT; ++q) {
       if (p.mode == MODE_GATEUP) { rw[8 * q + g] = acc0[q]; rw[16 + 8 * q + g] = acc1[q]; }
@@ -857,16 +862,16 @@ __global__ void __launch_bounds__(kThreads, 1) moe_group_kernel(GroupParams p) {
       old = atomicAdd(&red_cnt[rbuf], 1u);
     }
     old = __shfl_sync(0xffffffffu, old, 0);
-    if (old == kCW - 1) {
+    if (old == GW - 1) {
       __threadfence_block();
-      const float* rr = red + (size_t)rbuf * kCW * kGRed;
+      const float* rr = red + (size_t)rbuf * GW * kGRed;
       const int e = p.grp[1 + 3 * ch];
       for (int o = lane; o < kGT * 16; o += 32) {
         const int tk = o >> 4, r = o & 15, row = t * 16 + r;
         if (tk >= ntok) continue;
         float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-        for (int w = 0; w < kCW; ++w) {
+        for (int w = 0; w < GW; ++w) {
           a0 += rr[w * kGRed + tk * kRedRows + r];
           if (p.mode == MODE_GATEUP) a1 += rr[w * kGRed + tk * kRedRows + 16 + r];
         }
@@ -885,11 +890,16 @@ __global__ void __launch_bounds__(kThreads, 1) moe_group_kernel(GroupParams p) {
   }
 }
 
-template <int FMT, int NBW, int RT>
+size_t group_smem_bytes(int ns, int stage_bytes, int gw) {
+  const int g = kCW / gw, nrbg = (ns + g - 1) / g + 1;
+  return (size_t)ns * stage_bytes + (size_t)g * nrbg * gw * kGT * kRedRows * sizeof(float) + 2 * kGroupMaxStages * 8 +
+         kGroupRedCnt * 4 + 16;
+}
+
+template <int FMT, int NBW, int RT, int GW>
 cudaError_t launch_group(const DevCtx& c, const GroupParams& p, cudaStream_t s) {
-  const size_t smem = (size_t)p.ns * p.stage_bytes + (size_t)(p.ns + 1) * kCW * kGT * kRedRows * sizeof(float) +
-                      2 * kMaxStages * 8 + (kMaxStages + 1) * 4 + 16;
-  cudaError_t e = cudaFuncSetAttribute(moe_group_kernel<FMT, NBW, RT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  const size_t smem = group_smem_bytes(p.ns, p.stage_bytes, GW);
+  cudaError_t e = cudaFuncSetAttribute(moe_group_kernel<FMT, NBW, RT, GW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -902,33 +912,44 @@ cudaError_t launch_group(const DevCtx& c, const GroupParams& p, cudaStream_t s) 
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, moe_group_kernel<FMT, NBW, RT>, p);
+  return cudaLaunchKernelEx(&cfg, moe_group_kernel<FMT, NBW, RT, GW>, p);
 }
 
-template <int FMT, int RT>
+// gate_up (long K): all 16 warps on one item; down (short K): 4 items at once, 4 warps each
+template <int FMT, int RT, int GW>
 cudaError_t group_nbw(const DevCtx& c, const GroupParams& p, cudaStream_t s) {
-  const int nbw = (p.cols / 32 + kCW - 1) / kCW;
-  if (nbw <= 1) return launch_group<FMT, 1, RT>(c, p, s);
-  if (nbw <= 2) return launch_group<FMT, 2, RT>(c, p, s);
-  if (nbw <= 4) return launch_group<FMT, 4, RT>(c, p, s);
-  if (nbw <= 6) return launch_group<FMT, 6, RT>(c, p, s);
-  if (nbw <= 8) return launch_group<FMT, 8, RT>(c, p, s);
+  const int nbw = (p.cols / 32 + GW - 1) / GW;
+  if (nbw <= 1) return launch_group<FMT, 1, RT, GW>(c, p, s);
+  if (nbw <= 2) return launch_group<FMT, 2, RT, GW>(c, p, s);
+  if (nbw <= 4) return launch_group<FMT, 4, RT, GW>(c, p, s);
+  if (nbw <= 6) return launch_group<FMT, 6, RT, GW>(c, p, s);
+  if (nbw <= 8) return launch_group<FMT, 8, RT, GW>(c, p, s);
   return cudaErrorInvalidValue;
+}
+
+int group_warps(const GroupParams& p) {   // measured: 16 for gate_up at hidden 2048, 4 for down at 768
+  return (p.mode == MODE_DOWN && (p.cols / 32 + 3) / 4 <= 8) ? 4 : kCW;
 }
 
 cudaError_t dispatch_group(const DevCtx& c, const GroupParams& p, cudaStream_t s) {
   const bool gu = p.mode == MODE_GATEUP;
-  if (p.fmt == FMT_MXFP4) return gu ? group_nbw<FMT_MXFP4, 2>(c, p, s) : group_nbw<FMT_MXFP4, 1>(c, p, s);
-  if (p.fmt == FMT_Q4K) return gu ? group_nbw<FMT_Q4K, 2>(c, p, s) : group_nbw<FMT_Q4K, 1>(c, p, s);
-  if (p.fmt == FMT_Q6K) return gu ? group_nbw<FMT_Q6K, 2>(c, p, s) : group_nbw<FMT_Q6K, 1>(c, p, s);
+  if (!gu && group_warps(p) == 4) {
+    if (p.fmt == FMT_MXFP4) return group_nbw<FMT_MXFP4, 1, 4>(c, p, s);
+    if (p.fmt == FMT_Q4K) return group_nbw<FMT_Q4K, 1, 4>(c, p, s);
+    if (p.fmt == FMT_Q6K) return group_nbw<FMT_Q6K, 1, 4>(c, p, s);
+    return cudaErrorInvalidValue;
+  }
+  if (p.fmt == FMT_MXFP4) return gu ? group_nbw<FMT_MXFP4, 2, kCW>(c, p, s) : group_nbw<FMT_MXFP4, 1, kCW>(c, p, s);
+  if (p.fmt == FMT_Q4K) return gu ? group_nbw<FMT_Q4K, 2, kCW>(c, p, s) : group_nbw<FMT_Q4K, 1, kCW>(c, p, s);
+  if (p.fmt == FMT_Q6K) return gu ? group_nbw<FMT_Q6K, 2, kCW>(c, p, s) : group_nbw<FMT_Q6K, 1, kCW>(c, p, s);
   return cudaErrorInvalidValue;
 }
 
-// stages + the (kGT-wide) reduction buffers within ~220 KB
-int pick_group_stages(int stage_bytes) {
-  const int red = kCW * kGT * kRedRows * 4;
-  int ns = (220 * 1024 - red) / (stage_bytes + red);
-  return ns < 2 ? 2 : (ns > 6 ? 6 : ns);
+// stages + the reduction buffers within ~220 KB
+int pick_group_stages(int stage_bytes, int gw) {
+  int ns = kGroupMaxStages;
+  while (ns > 2 && group_smem_bytes(ns, stage_bytes, gw) > 220 * 1024) --ns;
+  return ns;
 }
 
 // ---------------- router: RMSNorm + GEMV + bias + mask + top-k + softmax ----------------
@@ -1280,13 +1301,13 @@ cudaError_t launch_moe_group(const DevCtx& c, const GroupMoeArgs& a, int part, c
   p.grp = a.grp; p.ent_tok = a.ent_tok; p.oai = a.oai_swiglu; p.err = c.err;
   p.mode = MODE_GATEUP; p.fmt = fg; p.w0 = a.gate; p.w1 = a.up; p.expert_stride = (int64_t)a.I * rbg; p.rb = rbg;
   p.cols = a.H; p.rows = a.I; p.n_tiles = a.I / 16; p.rs = stage_row_stride(rbg); p.stage_bytes = 32 * p.rs;
-  p.ns = pick_group_stages(p.stage_bytes);
+  p.ns = pick_group_stages(p.stage_bytes, group_warps(p));
   p.x = a.x; p.bias0 = a.gate_b; p.bias1 = a.up_b; p.out = a.act;
   if ((16 * rbg) % 16 || p.expert_stride % 16 || a.I % 16) return cudaErrorInvalidValue;
   if (part == 1) return dispatch_group(c, p, s);
   p.mode = MODE_DOWN; p.fmt = fd; p.w0 = a.down; p.w1 = nullptr; p.expert_stride = (int64_t)a.H * rbd; p.rb = rbd;
   p.cols = a.I; p.rows = a.H; p.n_tiles = a.H / 16; p.rs = stage_row_stride(rbd); p.stage_bytes = 16 * p.rs;
-  p.ns = pick_group_stages(p.stage_bytes);
+  p.ns = pick_group_stages(p.stage_bytes, group_warps(p));
   p.x = a.act; p.bias0 = a.down_b; p.bias1 = nullptr; p.out = a.y;
   if ((16 * rbd) % 16 || p.expert_stride % 16) return cudaErrorInvalidValue;
   return dispatch_group(c, p, s);
