@@ -272,7 +272,7 @@ cudaError_t launch_q8_gemm_batch(const DevCtx& c, const Q8BatchArgs& a, cudaStre
 // h[b] += sum over token b's local experts (ascending id) of w * y[entry]; then the next
 // attention input (xq/xd: Q8_0 of RMSNorm(h[b]) * norm_w) or the LM head input (xf: f32)
 struct BatchCombine {
-  const float* y = nullptr;        // [entries][H] expert outputs (bias included)
+  const float* y = nullptr;        // [B][K][H] expert outputs (bias included)
   const int* ent_of = nullptr;     // [B][K] entry of each (token, slot), -1 when not local
   const int* idx = nullptr;        // [B][K]
   const float* wts = nullptr;      // [B][K]
@@ -306,10 +306,10 @@ struct GroupMoeArgs {
   int expert_base = 0, n_local = 0;
   int oai_swiglu = 0;
   int* grp = nullptr;              // scratch: group_table_words(B, K, n_local)
-  int* ent_tok = nullptr;          // [B*K]
-  int* ent_of = nullptr;           // [B*K] (read by the combine)
-  float* act = nullptr;            // [B*K][I]
-  float* y = nullptr;              // [B*K][H]
+  int* ent_slot = nullptr;         // [B*K] (token, slot) of each entry
+  int* ent_of = nullptr;           // [B*K] entry of each (token, slot), -1 when not local
+  float* act = nullptr;            // [B*K][I] by entry
+  float* y = nullptr;              // [B][K][H] by (token, slot)
 };
 int group_table_words(int B, int K);
 // part: 0 grouping (route), 1 gate_up + activation, 2 down -- launched in that order

@@ -240,13 +240,12 @@ __global__ void __launch_bounds__(256) resid_batch_kernel(BatchCombine bc, float
   if (threadIdx.x == 0) {   // this token's local experts in ascending id (the reference's order)
     int n = 0, ids[16];
     for (int k = 0; k < bc.K; ++k) {
-      const int ent = bc.ent_of[b * bc.K + k];
-      if (ent < 0) continue;
+      if (bc.ent_of[b * bc.K + k] < 0) continue;
       const int e = bc.idx[b * bc.K + k];
       int j = n++;
       while (j > 0 && ids[j - 1] > e) { ids[j] = ids[j - 1]; s_ent[j] = s_ent[j - 1]; s_w[j] = s_w[j - 1]; --j; }
       ids[j] = e;
-      s_ent[j] = ent;
+      s_ent[j] = b * bc.K + k;   // row of y
       s_w[j] = bc.wts[b * bc.K + k];
     }
     s_n = n;

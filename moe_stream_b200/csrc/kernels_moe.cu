@@ -571,7 +571,8 @@ struct GroupParams {
   int rb, rs, cols, rows, n_tiles, stage_bytes, ns;
   const float* x;          // GATEUP: [B][cols] normed input; DOWN: act [entries][cols]
   const int* grp;          // [0] chunks, then (expert_local, entry_begin, n_tok) per chunk
-  const int* ent_tok;      // token of each entry
+  const int* ent_slot;     // flat (token, slot) index b * K + k of each entry
+  int K;                   // slots per token
   const float* bias0;
   const float* bias1;
   float* out;              // GATEUP: act [entries][rows]; DOWN: y [entries][rows]
@@ -607,7 +608,7 @@ __device__ __forceinline__ int block_excl_scan(int v, int* wsum, int* total) {
 
 // One CTA: count entries per local expert, place them in (expert, token) order, emit the chunks.
 __global__ void __launch_bounds__(kRouteThreads) group_route_kernel(const int* idx, int n_ent, int K, int expert_base,
-                                                                    int n_local, int* grp, int* ent_tok, int* ent_of,
+                                                                    int n_local, int* grp, int* ent_slot, int* ent_of,
                                                                     uint32_t* err) {
   __shared__ int cnt[kRouteThreads];
   __shared__ int s_e[kMaxBatch * kMaxK];
@@ -645,7 +646,7 @@ __global__ void __launch_bounds__(kRouteThreads) group_route_kernel(const int* i
     if (e < 0) continue;
     const int pos = cnt[e] + ent_of[i];
     ent_of[i] = pos;
-    ent_tok[pos] = i / K;
+    ent_slot[pos] = i;
   }
   if (t < n_local)
     for (int q = 0; q < nch; ++q) {
@@ -806,7 +807,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_group_kernel(GroupParams p) {
 #pragma unroll
       for (int q = 0; q < kGT; ++q) {
         const int ent = ebeg + min(q, ntok - 1);
-        const int row = p.mode == MODE_GATEUP ? p.ent_tok[ent] : ent;
+        const int row = p.mode == MODE_GATEUP ? p.ent_slot[ent] / p.K : ent;
         xr[q] = p.x + (size_t)row * p.cols;
       }
       build_bfrag_group<FMT, NBW, GW>(xr, ntok, nb, wi, lane, bf, kbs, xsum);
@@ -877,11 +878,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_group_kernel(GroupParams p) {
         }
         const size_t ent = (size_t)(ebeg + tk);
         if (p.bias0) a0 += p.bias0[(size_t)e * p.rows + row];
-        if (p.mode == MODE_GATEUP) {
+        if (p.mode == MODE_GATEUP) {   // activation rows by entry (the down phase's input order)
           if (p.bias1) a1 += p.bias1[(size_t)e * p.rows + row];
           p.out[ent * p.rows + row] = p.oai ? swiglu_oai(a0, a1) : silu_mul(a0, a1);
-        } else {
-          p.out[ent * p.rows + row] = a0;
+        } else {                       // expert outputs by (token, slot)
+          p.out[(size_t)p.ent_slot[ent] * p.rows + row] = a0;
         }
       }
       __syncwarp();
@@ -1296,9 +1297,9 @@ cudaError_t launch_moe_group(const DevCtx& c, const GroupMoeArgs& a, int part, c
   cfg.numAttrs = 1;
   if (part == 0)
     return cudaLaunchKernelEx(&cfg, group_route_kernel, a.idx, n_ent, a.K, a.expert_base, a.n_local, a.grp,
-                              a.ent_tok, a.ent_of, c.err);
+                              a.ent_slot, a.ent_of, c.err);
   GroupParams p = {};
-  p.grp = a.grp; p.ent_tok = a.ent_tok; p.oai = a.oai_swiglu; p.err = c.err;
+  p.grp = a.grp; p.ent_slot = a.ent_slot; p.K = a.K; p.oai = a.oai_swiglu; p.err = c.err;
   p.mode = MODE_GATEUP; p.fmt = fg; p.w0 = a.gate; p.w1 = a.up; p.expert_stride = (int64_t)a.I * rbg; p.rb = rbg;
   p.cols = a.H; p.rows = a.I; p.n_tiles = a.I / 16; p.rs = stage_row_stride(rbg); p.stage_bytes = 32 * p.rs;
   p.ns = pick_group_stages(p.stage_bytes, group_warps(p));

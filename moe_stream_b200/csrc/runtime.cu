@@ -187,7 +187,7 @@ struct BatchRt {
   float *act = nullptr, *y = nullptr, *xf = nullptr, *logits = nullptr, *part = nullptr;
   int8_t *xq_h = nullptr, *xq_a = nullptr;
   float *xd_h = nullptr, *xd_a = nullptr;
-  int *idx = nullptr, *grp = nullptr, *ent_tok = nullptr, *ent_of = nullptr;
+  int *idx = nullptr, *grp = nullptr, *ent_slot = nullptr, *ent_of = nullptr;
   uint32_t *attn_cnt = nullptr, *router_cnt = nullptr;
   std::vector<float*> kc, vc;
   void* lm_scratch = nullptr;
@@ -505,6 +505,7 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
         LAUNCH(launch_moe_tc(dc, ta, s));   // gate_up + down in one kernel
         pc = tc_pending_combine(dc, ta);
       } else {
+        // one token: the per-slot phase kernels (measured faster here than the grouped ones)
         LAUNCH(launch_moe_mxfp4(dc, ma, s));
         ++nk;   // gate/up, down
         pc.partial = m->partial; pc.idx = Lw.idx; pc.wts = Lw.wts; pc.K = c.top_k;
@@ -669,7 +670,7 @@ ms_status enqueue_batch_step(ms_model* m, cudaStream_t s) {
     ga.x = b.xn; ga.idx = b.idx; ga.B = B; ga.K = c.top_k; ga.H = H; ga.I = c.inter; ga.gate_q = Lw.gate_q;
     ga.down_q = Lw.down_q; ga.gate = Lw.gate; ga.up = Lw.up; ga.down = Lw.down; ga.gate_b = Lw.gate_b;
     ga.up_b = Lw.up_b; ga.down_b = Lw.down_b; ga.expert_base = m->expert_base; ga.n_local = m->n_local;
-    ga.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ga.grp = b.grp; ga.ent_tok = b.ent_tok; ga.ent_of = b.ent_of;
+    ga.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ga.grp = b.grp; ga.ent_slot = b.ent_slot; ga.ent_of = b.ent_of;
     ga.act = b.act; ga.y = b.y;
     BLAUNCH(5, 1, launch_moe_group(dc, ga, 0, s));
     BLAUNCH(6, 1, launch_moe_group(dc, ga, 1, s));
@@ -1203,7 +1204,7 @@ ms_status ms_model_batch_open(ms_model* m, int B) {
   s = s ? s : balloc(m, &b.idx, (size_t)EK * 4);
   s = s ? s : balloc(m, &b.wts, (size_t)EK * 4);
   s = s ? s : balloc(m, &b.grp, (size_t)group_table_words(B, c.top_k) * 4);
-  s = s ? s : balloc(m, &b.ent_tok, (size_t)EK * 4);
+  s = s ? s : balloc(m, &b.ent_slot, (size_t)EK * 4);
   s = s ? s : balloc(m, &b.ent_of, (size_t)EK * 4);
   s = s ? s : balloc(m, &b.act, (size_t)EK * c.inter * 4);
   s = s ? s : balloc(m, &b.y, (size_t)EK * H * 4);
