@@ -255,10 +255,12 @@ def run_ours(args):
     ep = ws > 1 and args.mode == "ep"
     eng = Engine.from_spec(spec, seed=0, max_seq_len=max_seq, ctx=ctx,
                            ep_rank=rank if ep else 0, ep_size=ws if ep else 1)
-    if ep:
+    if ep and args.exchange == "nccl":
         uid = [Engine.nccl_unique_id(ctx) if rank == 0 else None]
         torch.distributed.broadcast_object_list(uid, src=0)
         eng.init_ep(uid[0])
+    elif ep:
+        eng.init_ep_p2p()   # MoE exchange by direct stores into the peers' mailboxes (NVLink)
     log(f"[rank {rank}] model generated + uploaded in {time.time() - t0:.1f}s")
     prompt = synth.prompt_ids(spec, prompt_len, seed=0)
     t0 = time.time()
@@ -332,6 +334,7 @@ def run_ours(args):
         "config": {"workload": "GPT-OSS-20B-shaped MXFP4 greedy decode, bs1, after a 2048-token prompt",
                    "model": "gpt-oss-20b-shaped", "global_batch": streams, "seq_len": prompt_len,
                    "parallelism": (f"ep{ws}" if ep else f"replicas{ws}"),
+                   "ep_exchange": (args.exchange if ep else None),
                    "l2": "no flush: each step streams ~3.1 GB of weights (> 126 MB L2)"},
         "e2e": {"value": round(streams * args.steps / e2e_s, 2) if e2e_s == e2e_s else None, "unit": "tok/s", "h2d_bytes_per_step": 4 + 4,
                 "d2h_bytes_per_step": 8},
@@ -515,6 +518,8 @@ def main():
     ap.add_argument("--no-profile", action="store_true", help="skip the per-kernel-class breakdown")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (default 2048)")
     ap.add_argument("--layers", type=int, default=0, help="profiling only: override the layer count")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="expert-parallel MoE exchange: peer-memory stores (default) or NCCL all-reduce")
     ap.add_argument("--mode", default="ep", choices=["ep", "replicas"],
                     help="N > 1: expert parallel over one sequence (default) or N independent replicas")
     ap.add_argument("--case", default=None, choices=[None, "moe-layer", "prefill", "qwen3"],

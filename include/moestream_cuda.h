@@ -242,6 +242,13 @@ MS_API ms_status ms_model_finalize(ms_model* m);
  * each rank calls ms_model_init_ep before its first forward. */
 MS_API ms_status ms_nccl_unique_id(ms_ctx* ctx, void* out, size_t bytes);
 MS_API ms_status ms_model_init_ep(ms_model* m, const void* unique_id, size_t bytes);
+/* Expert parallel over NVLink peer memory instead of NCCL: each rank gets its mailbox's CUDA IPC
+ * handle (64 bytes), the caller gathers all ranks' handles in rank order (any host channel) and
+ * passes them to ms_model_ep_connect.  Each layer's local MoE combine is then stored directly into
+ * every rank's mailbox by one kernel, and the residual kernel sums the ranks' partials in rank
+ * order after a bounded wait on their flags. */
+MS_API ms_status ms_model_ep_handle(ms_model* m, void* out, size_t bytes);
+MS_API ms_status ms_model_ep_connect(ms_model* m, const void* handles, size_t bytes);
 /* Parse a GGUF file (reader.rs:259-368, config.rs:253-434) and upload everything. */
 MS_API ms_status ms_model_open_gguf(ms_ctx* ctx, const char* path, int max_seq_len, int ep_rank, int ep_size,
                              ms_model** out);

@@ -82,6 +82,8 @@ _SIGS = {
     "ms_shared_expert": (C.c_int, [_vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _vp, _vp]),
     "ms_nccl_unique_id": (C.c_int, [_vp, _vp, C.c_size_t]),
     "ms_model_init_ep": (C.c_int, [_vp, _vp, C.c_size_t]),
+    "ms_model_ep_handle": (C.c_int, [_vp, _vp, C.c_size_t]),
+    "ms_model_ep_connect": (C.c_int, [_vp, _vp, C.c_size_t]),
     "ms_model_create": (C.c_int, [_vp, C.POINTER(ModelConfig), C.POINTER(_vp)]),
     "ms_model_set_tensor": (C.c_int, [_vp, C.c_char_p, _i, _i, C.POINTER(C.c_int64), _vp, C.c_size_t]),
     "ms_model_finalize": (C.c_int, [_vp]),

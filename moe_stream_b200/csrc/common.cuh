@@ -145,6 +145,7 @@ struct CombineOrder {
   int n;
   int slot[16];
   float w[16];
+  uint32_t seq;   // expert-parallel mailbox: the step's sequence number
 };
 
 // The tensor-core MoE split: items (slot x tile) are cut into S equal K ranges (units), S the
@@ -185,6 +186,12 @@ __device__ __forceinline__ void combine_prepare(const PendingCombine&, CombineOr
 // moe_out[r], accumulated from zero in ascending expert order as the reference does
 __device__ __forceinline__ float combine_at(const PendingCombine& pc, const CombineOrder& co, int H, int r) {
   if (pc.dense) return pc.dense[r];
+  if (pc.ep_recv) {   // the ranks' partial outputs, summed in rank order (written by peers: L2 loads)
+    const float* rb = pc.ep_recv + (size_t)(co.seq & 1u) * pc.ep_n * H + r;
+    float acc = 0.f;
+    for (int j = 0; j < pc.ep_n; ++j) acc += __ldcg(rb + (size_t)j * H);
+    return acc;
+  }
   float acc = 0.f;
   if (pc.seg_part) {
     const int t = r >> 7, ns = tc_splits(co.n * pc.seg_tiles, pc.seg_kw, pc.seg_grid);
@@ -257,6 +264,28 @@ __device__ __forceinline__ void cta_rmsnorm_q8(const float* xs, int H, const flo
       v[kk] = (xs[32 * b + kk] * inv) * w[32 * b + kk];
     }
     quantize_q8_block(v, xq + 32 * b, &xd[b]);
+  }
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Single thread: wait (bounded) until every rank's mailbox flag of this step is released; the
+// sequence number goes to co->seq.  On expiry the error word gets EF_TIMEOUT_FULL.
+__device__ __forceinline__ void ep_wait(const PendingCombine& pc, CombineOrder* co, uint32_t* err) {
+  const uint32_t seq = *reinterpret_cast<const volatile uint32_t*>(pc.ep_seq);
+  co->seq = seq;
+  const uint32_t* f = pc.ep_flags + (size_t)(seq & 1u) * pc.ep_n;
+  for (int j = 0; j < pc.ep_n; ++j) {
+    uint32_t it = 0;
+    while ((int32_t)(ld_acquire_sys_u32(f + j) - seq) < 0 && ++it < kWaitLimit) __nanosleep(64);
+    if (it >= kWaitLimit) { atomicOr(err, EF_TIMEOUT_FULL); return; }
   }
 }
 

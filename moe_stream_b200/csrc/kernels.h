@@ -44,8 +44,29 @@ struct PendingCombine {
   const float* wts = nullptr;      // [K] routing weights
   int K = 0;
   int expert_base = 0, n_local = 0;
-  __host__ __device__ bool active() const { return dense != nullptr || partial != nullptr || seg_part != nullptr; }
+  // or, expert parallel over peer memory: every rank's partial MoE output in this rank's mailbox,
+  // recv[parity][rank][H], complete once flags[parity][rank] >= *ep_seq (parity = *ep_seq & 1)
+  const float* ep_recv = nullptr;
+  const uint32_t* ep_flags = nullptr;
+  const uint32_t* ep_seq = nullptr;
+  int ep_n = 0;
+  __host__ __device__ bool active() const {
+    return dense != nullptr || partial != nullptr || seg_part != nullptr || ep_recv != nullptr;
+  }
 };
+
+// Expert-parallel exchange over NVLink peer memory (kernels_dense.cu): this rank's combined MoE
+// output is stored into every rank's mailbox slot [parity][rank], then each rank's flag
+// [parity][rank] is released with the step's sequence number.
+constexpr int kMaxEp = 8;
+struct EpSend {
+  float* recv[kMaxEp];             // each rank's mailbox (peer pointers; own rank local)
+  uint32_t* flags[kMaxEp];         // each rank's flag array [2][n]
+  uint32_t* seq = nullptr;         // this rank's sequence counter (device)
+  uint32_t* cnt = nullptr;         // CTA counter (device, zero, self-resetting)
+  int rank = 0, n = 0;
+};
+cudaError_t launch_ep_send(const DevCtx& c, const PendingCombine& pc, int H, const EpSend& e, cudaStream_t s);
 
 // y[r] = W[r,:] . x  (+bias[r]) (+residual: y[r] += y_in[r]);  MXFP4 / F16 / F32 weights.
 struct GemvArgs {

@@ -1019,7 +1019,7 @@ __global__ void __launch_bounds__(1024) embed_kernel(StepState* st, const void* 
 constexpr int kResidRows = 256;
 __global__ void __launch_bounds__(kResidRows) resid_norm_q8_kernel(PendingCombine pc, float* h, int H,
                                                                    const float* norm_w, float eps, int8_t* xq,
-                                                                   float* xd, uint32_t* cnt) {
+                                                                   float* xd, uint32_t* cnt, uint32_t* err) {
   extern __shared__ float hs[];   // [H] (last CTA)
   __shared__ CombineOrder co;
   __shared__ float red[32];
@@ -1033,7 +1033,10 @@ __global__ void __launch_bounds__(kResidRows) resid_norm_q8_kernel(PendingCombin
     s_wts[threadIdx.x] = pc.wts[threadIdx.x];
   }
   __syncthreads();
-  if (threadIdx.x == 0) combine_order(pc, &co, pc.idx ? s_idx : nullptr, pc.idx ? s_wts : nullptr);
+  if (threadIdx.x == 0) {
+    if (pc.ep_recv) ep_wait(pc, &co, err);   // the other ranks' partial outputs have landed
+    combine_order(pc, &co, pc.idx ? s_idx : nullptr, pc.idx ? s_wts : nullptr);
+  }
   __syncthreads();
   combine_prepare(pc, &co);
   __syncthreads();
@@ -1052,6 +1055,41 @@ __global__ void __launch_bounds__(kResidRows) resid_norm_q8_kernel(PendingCombin
   __syncthreads();
   cta_rmsnorm_q8(hs, H, norm_w, eps, xq, xd, red);
   if (threadIdx.x == 0) *cnt = 0u;
+}
+
+// Expert parallel over peer memory: this rank's MoE output (the pending combine of its local
+// experts) is stored into slot [parity][rank] of every rank's mailbox over NVLink; the last CTA
+// then releases flag [parity][rank] at every rank with the step's sequence number.  A mailbox slot
+// of parity p is rewritten two steps later, after every rank has consumed it (the next step's
+// combine needs every rank's release, which each rank issues after its own consumption).
+__global__ void __launch_bounds__(256) ep_send_kernel(PendingCombine pc, int H, EpSend e) {
+  __shared__ CombineOrder co;
+  __shared__ uint32_t s_seq, last;
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    combine_order(pc, &co);
+    s_seq = *reinterpret_cast<const volatile uint32_t*>(e.seq) + 1u;
+  }
+  __syncthreads();
+  combine_prepare(pc, &co);
+  __syncthreads();
+  const uint32_t seq = s_seq, par = seq & 1u;
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < H; r += gridDim.x * blockDim.x) {
+    const float v = combine_at(pc, co, H, r);
+    for (int j = 0; j < e.n; ++j) e.recv[j][((size_t)par * e.n + e.rank) * H + r] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) last = (atomicAdd(e.cnt, 1u) == gridDim.x - 1) ? 1u : 0u;
+  __syncthreads();
+  if (!last) return;
+  __threadfence_system();
+  if ((int)threadIdx.x < e.n) st_release_sys_u32(e.flags[threadIdx.x] + par * e.n + e.rank, seq);
+  if (threadIdx.x == 0) {
+    *e.seq = seq;
+    *e.cnt = 0u;
+  }
 }
 
 template <class Kern, class... Args>
@@ -1219,7 +1257,7 @@ cudaError_t launch_resid_norm_q8(const DevCtx& c, const PendingCombine& pc, floa
     if (e != cudaSuccess) return e;
   }
   return launch_pdl(resid_norm_q8_kernel, dim3((unsigned)((H + kResidRows - 1) / kResidRows)), dim3(kResidRows), smem, s,
-                    pc, h, H, norm_w, eps, xq, xd, cnt);
+                    pc, h, H, norm_w, eps, xq, xd, cnt, c.err);
 }
 
 cudaError_t launch_gemv(const DevCtx& c, const GemvArgs& a, cudaStream_t s) {
@@ -1244,6 +1282,12 @@ cudaError_t launch_gemv(const DevCtx& c, const GemvArgs& a, cudaStream_t s) {
     }
   }
   return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_ep_send(const DevCtx& c, const PendingCombine& pc, int H, const EpSend& e, cudaStream_t s) {
+  (void)c;
+  if (e.n < 1 || e.n > kMaxEp || e.rank < 0 || e.rank >= e.n || !e.seq || !e.cnt) return cudaErrorInvalidValue;
+  return launch_pdl(ep_send_kernel, dim3((unsigned)((H + 255) / 256)), dim3(256), 0, s, pc, H, e);
 }
 
 }  // namespace ms

@@ -202,6 +202,12 @@ struct BatchRt {
 struct ms_model {
   ms_ctx* ctx = nullptr;
   ncclComm_t comm = nullptr;        // expert-parallel communicator (ep_size > 1)
+  // expert parallel over peer memory (ms_model_ep_connect): mailbox recv [2][n][H] floats then
+  // flags [2][n]; peers' mailboxes opened through CUDA IPC
+  float* ep_mail = nullptr;
+  uint32_t *ep_seq = nullptr, *ep_cnt = nullptr;
+  void* ep_peer[kMaxEp] = {};
+  bool ep_p2p = false;
   float* moe_out = nullptr;         // [H] local MoE output, all-reduced across the EP group
   int8_t* xq_h = nullptr;           // Q8_0 codes of the next attention input [H]
   float* xd_h = nullptr;            // and block scales [H / 32]
@@ -483,7 +489,33 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     ma.tile_cnt = m->tile_cnt; ma.h = m->h; ma.H = H; ma.I = c.inter; ma.K = c.top_k;
     ma.expert_base = m->expert_base; ma.n_local = m->n_local; ma.oai_swiglu = c.arch == MS_ARCH_GPT_OSS;
     PendingCombine pc;
-    if (c.ep_size > 1) {
+    if (c.ep_size > 1 && m->ep_p2p) {
+      // expert parallel over peer memory: the local experts' combine goes straight into every
+      // rank's mailbox (one kernel); the residual kernel waits for all ranks and sums them
+      ma.defer_combine = 1;
+      ta.defer_combine = 1;
+      PendingCombine lc;
+      if (Lw.tc) {
+        LAUNCH(launch_moe_tc(dc, ta, s));
+        lc = tc_pending_combine(dc, ta);
+      } else {
+        LAUNCH(launch_moe_mxfp4(dc, ma, s));
+        ++nk;   // gate/up, down
+        lc.partial = m->partial; lc.idx = Lw.idx; lc.wts = Lw.wts; lc.K = c.top_k;
+        lc.expert_base = m->expert_base; lc.n_local = m->n_local;
+      }
+      const int n = c.ep_size;
+      EpSend e;
+      for (int j = 0; j < n; ++j) {
+        float* mb = j == c.ep_rank ? m->ep_mail : reinterpret_cast<float*>(m->ep_peer[j]);
+        e.recv[j] = mb;
+        e.flags[j] = reinterpret_cast<uint32_t*>(mb + (size_t)2 * n * H);
+      }
+      e.seq = m->ep_seq; e.cnt = m->ep_cnt; e.rank = c.ep_rank; e.n = n;
+      LAUNCH(launch_ep_send(dc, lc, H, e, s));
+      pc.ep_recv = m->ep_mail; pc.ep_flags = reinterpret_cast<const uint32_t*>(m->ep_mail + (size_t)2 * n * H);
+      pc.ep_seq = m->ep_seq; pc.ep_n = n;
+    } else if (c.ep_size > 1) {
       // expert parallel: combine the local experts into moe_out, sum it over the EP group
       ma.defer_combine = 0; ma.out = m->moe_out;
       ta.defer_combine = 0; ta.out = m->moe_out;
@@ -527,7 +559,8 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
 
 ms_status run_step(ms_model* m) {
   cudaStream_t s = m->ctx->stream;
-  if (m->cfg.ep_size > 1 && !m->comm) return fail(m->ctx, MS_ERR_STATE, "expert-parallel model: call ms_model_init_ep first");
+  if (m->cfg.ep_size > 1 && !m->comm && !m->ep_p2p)
+    return fail(m->ctx, MS_ERR_STATE, "expert-parallel model: call ms_model_init_ep or ms_model_ep_connect first");
   if (!m->use_graph) return enqueue_step(m, s);
   if (!m->graph) {
     // capture on the context's private stream (the caller's stream may be the legacy default
@@ -1391,6 +1424,8 @@ ms_status ms_model_destroy(ms_model* m) {
   cudaStreamSynchronize(m->ctx->stream);
   if (m->graph) cudaGraphExecDestroy(m->graph);
   if (m->comm) nccl_api()->comm_destroy(m->comm);
+  for (void* p : m->ep_peer)
+    if (p) cudaIpcCloseMemHandle(p);
   batch_free(m);
   for (void* p : m->allocs) cudaFree(p);
   if (m->h_tok) cudaFreeHost(m->h_tok);
@@ -1569,6 +1604,50 @@ ms_status ms_model_init_ep(ms_model* m, const void* unique_id, size_t bytes) {
   memcpy(&id, unique_id, sizeof id);
   ncclResult_t r = api->comm_init_rank(&m->comm, m->cfg.ep_size, id, m->cfg.ep_rank);
   if (r != ncclSuccess) { m->comm = nullptr; return fail(m->ctx, MS_ERR_NCCL, "ncclCommInitRank: %s", api->error_string(r)); }
+  if (m->graph) { cudaGraphExecDestroy(m->graph); m->graph = nullptr; }
+  return MS_OK;
+}
+
+ms_status ms_model_ep_handle(ms_model* m, void* out, size_t bytes) {
+  if (!m || !out || bytes < sizeof(cudaIpcMemHandle_t)) return MS_ERR_INVALID_ARG;
+  if (!m->finalized || m->cfg.ep_size <= 1) return fail(m->ctx, MS_ERR_STATE, "needs a finalized expert-parallel model");
+  if (m->cfg.ep_size > kMaxEp) return fail(m->ctx, MS_ERR_INVALID_ARG, "peer-memory exchange supports <= %d ranks", kMaxEp);
+  cudaSetDevice(m->ctx->device);
+  if (!m->ep_mail) {
+    const size_t mb = (size_t)2 * m->cfg.ep_size * m->cfg.hidden * 4 + (size_t)2 * m->cfg.ep_size * 4;
+    ms_status s = m->alloc(&m->ep_mail, mb);
+    s = s ? s : m->alloc(&m->ep_seq, 16);
+    s = s ? s : m->alloc(&m->ep_cnt, 16);
+    if (s != MS_OK) return s;
+    MS_CUDA(m->ctx, cudaDeviceSynchronize());
+  }
+  cudaIpcMemHandle_t h;
+  MS_CUDA(m->ctx, cudaIpcGetMemHandle(&h, m->ep_mail));
+  memcpy(out, &h, sizeof h);
+  return MS_OK;
+}
+
+ms_status ms_model_ep_connect(ms_model* m, const void* handles, size_t bytes) {
+  if (!m || !handles) return MS_ERR_INVALID_ARG;
+  const int n = m->cfg.ep_size;
+  if (!m->ep_mail) return fail(m->ctx, MS_ERR_STATE, "call ms_model_ep_handle first");
+  if (bytes < (size_t)n * sizeof(cudaIpcMemHandle_t)) return MS_ERR_INVALID_ARG;
+  if (m->ep_p2p) return fail(m->ctx, MS_ERR_STATE, "peer mailboxes already connected");
+  cudaSetDevice(m->ctx->device);
+  for (int j = 0; j < n; ++j) {
+    if (j == m->cfg.ep_rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)j * sizeof h, sizeof h);
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < j; ++q)
+        if (m->ep_peer[q]) { cudaIpcCloseMemHandle(m->ep_peer[q]); m->ep_peer[q] = nullptr; }
+      return cuda_fail(m->ctx, e, "cudaIpcOpenMemHandle (peer mailbox)");
+    }
+    m->ep_peer[j] = p;
+  }
+  m->ep_p2p = true;
   if (m->graph) { cudaGraphExecDestroy(m->graph); m->graph = nullptr; }
   return MS_OK;
 }

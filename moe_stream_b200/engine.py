@@ -255,6 +255,26 @@ class Engine:
         buf = (C.c_uint8 * 128).from_buffer_copy(unique_id[:128])
         check(lib().ms_model_init_ep(self.h, buf, 128), self.ctx.h)
 
+    def ep_handle(self) -> bytes:
+        """This rank's peer-memory mailbox handle (CUDA IPC, 64 bytes)."""
+        buf = (C.c_uint8 * 64)()
+        check(lib().ms_model_ep_handle(self.h, buf, 64), self.ctx.h)
+        return bytes(buf)
+
+    def ep_connect(self, handles: Sequence[bytes]) -> None:
+        """Open every rank's mailbox (handles in rank order): the MoE exchange then runs over
+        NVLink peer memory instead of NCCL."""
+        b = b"".join(handles)
+        buf = (C.c_uint8 * len(b)).from_buffer_copy(b)
+        check(lib().ms_model_ep_connect(self.h, buf, len(b)), self.ctx.h)
+
+    def init_ep_p2p(self) -> None:
+        """ep_handle + all-gather over torch.distributed + ep_connect."""
+        import torch.distributed as dist
+        hs = [None] * dist.get_world_size()
+        dist.all_gather_object(hs, self.ep_handle())
+        self.ep_connect(hs)
+
     def preload_weights(self) -> None:
         """Weights are uploaded to HBM at open; nothing to preload (engine.rs:1551)."""
 

@@ -4,8 +4,9 @@ CPU (gloo, world size 2): the decomposition the CUDA path uses — each rank com
 contiguous expert slice [rank*E/N, (rank+1)*E/N), then a sum all-reduce — reproduces the
 single-device MoE layer (oracle, routing over all experts on every rank).
 
-GPU (2 devices): a tiny GPT-OSS-shaped model split over two ranks through the C ABI
-(ms_model_init_ep + in-graph NCCL all-reduce) decodes the same greedy tokens as one device.
+GPU (2 devices): a tiny GPT-OSS-shaped model split over two ranks through the C ABI decodes the
+same greedy tokens as one device, with the MoE exchange as an in-graph NCCL all-reduce
+(ms_model_init_ep) and as direct stores into the peers' mailboxes over NVLink (ms_model_ep_connect).
 """
 import os
 import socket
@@ -69,7 +70,7 @@ def test_ep_decomposition_gloo(orc, tmp_path):
     assert np.abs(got - full).max() / np.abs(full).max() < 1e-5
 
 
-def _gpu_rank(rank, world, port, path, prompt, out_dir):
+def _gpu_rank(rank, world, port, path, prompt, out_dir, exchange):
     import torch
     import torch.distributed as dist
     from moe_stream_b200.engine import Context, Engine
@@ -77,9 +78,12 @@ def _gpu_rank(rank, world, port, path, prompt, out_dir):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     ctx = Context(rank)
     eng = Engine.open(path, max_seq_len=256, ep_rank=rank, ep_size=world, ctx=ctx)
-    uid = [Engine.nccl_unique_id(ctx) if rank == 0 else None]
-    dist.broadcast_object_list(uid, src=0)
-    eng.init_ep(uid[0])
+    if exchange == "p2p":
+        eng.init_ep_p2p()
+    else:
+        uid = [Engine.nccl_unique_id(ctx) if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        eng.init_ep(uid[0])
     toks = eng.generate(prompt, 16)
     np.save(os.path.join(out_dir, f"tok{rank}.npy"), np.array(toks, np.int32))
     eng.close()
@@ -88,7 +92,8 @@ def _gpu_rank(rank, world, port, path, prompt, out_dir):
 
 
 @pytest.mark.gpu
-def test_ep_two_gpus_greedy_tokens(tmp_path):
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+def test_ep_two_gpus_greedy_tokens(tmp_path, exchange):
     import torch
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -96,6 +101,7 @@ def test_ep_two_gpus_greedy_tokens(tmp_path):
     f = np.load(os.path.join(GOLD, "tiny_models.npz"))
     path = str(tmp_path / "tiny.gguf")
     synth.write_model(path, synth.TINY_GPT_OSS, seed=7)
-    mp.spawn(_gpu_rank, args=(2, _free_port(), path, f["tiny_gpt_oss_prompt"], str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_gpu_rank, args=(2, _free_port(), path, f["tiny_gpt_oss_prompt"], str(tmp_path), exchange), nprocs=2,
+             join=True)
     for r in range(2):
         assert np.load(str(tmp_path / f"tok{r}.npy")).tolist() == f["tiny_gpt_oss_tokens"].tolist()
