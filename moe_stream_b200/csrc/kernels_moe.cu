@@ -127,24 +127,28 @@ __device__ __forceinline__ void codes4_to_f16x2(uint32_t q, uint32_t bias_h2, ui
 __device__ __forceinline__ void q4k_block(const uint8_t* sb0, const uint8_t* sb1, int j, int c, const uint32_t (&bf)[4],
                                           float xscale, float xsum, float& acc0, float& acc1) {
   const int jj = j & 3, nsh = (j & 1) * 4, qo = 16 + (j >> 1) * 32 + 4 * c;
-  float dot[2];
-  float dsc[2], dmn[2];
+  // the quad's four lanes decode one scale each -- lane c: row (c < 2 ? g : g + 8), d*sc (c even)
+  // or dmin*m (c odd) -- and exchange them (the 6-bit fields of gguf/dequant.rs:199-208)
+  const uint8_t* sbr = c < 2 ? sb0 : sb1;
+  const int odd = c & 1;
+  const uint32_t dm = *reinterpret_cast<const uint32_t*>(sbr);
+  const uint32_t sa = *reinterpret_cast<const uint32_t*>(sbr + 4 + 4 * odd);   // scales (s0) or mins (s1)
+  uint32_t v6;
+  if (j < 4) {
+    v6 = (sa >> (8 * jj)) & 63u;
+  } else {
+    const uint32_t s2 = *reinterpret_cast<const uint32_t*>(sbr + 12);
+    v6 = ((s2 >> (8 * jj + 4 * odd)) & 0xFu) | (((sa >> (8 * jj + 6)) & 3u) << 4);
+  }
+  const float val = h2f_bits((uint16_t)((dm >> (16 * odd)) & 0xffffu)) * (float)v6;
+  const float dsc0 = __shfl_sync(0xffffffffu, val, 0, 4) * xscale;
+  const float dmn0 = __shfl_sync(0xffffffffu, val, 1, 4);
+  const float dsc1 = __shfl_sync(0xffffffffu, val, 2, 4) * xscale;
+  const float dmn1 = __shfl_sync(0xffffffffu, val, 3, 4);
   uint32_t p[2][2][2];   // [row][word][pair]
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const uint8_t* sb = r ? sb1 : sb0;
-    const uint32_t dm = *reinterpret_cast<const uint32_t*>(sb);
-    const uint32_t s0 = *reinterpret_cast<const uint32_t*>(sb + 4), s1 = *reinterpret_cast<const uint32_t*>(sb + 8),
-                   s2 = *reinterpret_cast<const uint32_t*>(sb + 12);
-    uint32_t sc, m;
-    if (j < 4) { sc = (s0 >> (8 * jj)) & 63u; m = (s1 >> (8 * jj)) & 63u; }
-    else {
-      sc = ((s2 >> (8 * jj)) & 0xFu) | (((s0 >> (8 * jj + 6)) & 3u) << 4);
-      m = ((s2 >> (8 * jj + 4)) & 0xFu) | (((s1 >> (8 * jj + 6)) & 3u) << 4);
-    }
-    const float d = h2f_bits((uint16_t)(dm & 0xffffu)), dmin = h2f_bits((uint16_t)(dm >> 16));
-    dsc[r] = (d * (float)sc) * xscale;
-    dmn[r] = dmin * (float)m;
 #pragma unroll
     for (int w = 0; w < 2; ++w) {
       const uint32_t q = (*reinterpret_cast<const uint32_t*>(sb + qo + 16 * w) >> nsh) & 0x0F0F0F0Fu;
@@ -157,10 +161,8 @@ __device__ __forceinline__ void q4k_block(const uint8_t* sb0, const uint8_t* sb1
   mma_f16_16816(dd, a, bf[0], bf[1]);
   a[0] = p[0][1][0]; a[1] = p[1][1][0]; a[2] = p[0][1][1]; a[3] = p[1][1][1];
   mma_f16_16816(dd, a, bf[2], bf[3]);
-  dot[0] = dd[0] + dd[1];
-  dot[1] = dd[2] + dd[3];
-  acc0 = fmaf(dsc[0], dot[0], fmaf(-dmn[0], xsum, acc0));
-  acc1 = fmaf(dsc[1], dot[1], fmaf(-dmn[1], xsum, acc1));
+  acc0 = fmaf(dsc0, dd[0] + dd[1], fmaf(-dmn0, xsum, acc0));
+  acc1 = fmaf(dsc1, dd[2] + dd[3], fmaf(-dmn1, xsum, acc1));
 }
 
 // Q6_K elements (n, quad, l = 0..31) of one superblock for the thread's two rows
