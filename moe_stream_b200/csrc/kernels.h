@@ -14,7 +14,12 @@ enum : uint32_t {
   EF_BAD_SHAPE = 1u << 3,
 };
 
-enum QType : int { Q_F32 = 0, Q_F16 = 1, Q_Q8_0 = 8, Q_Q4_K = 12, Q_Q6_K = 14, Q_MXFP4 = 39 };
+enum QType : int { Q_F32 = 0, Q_F16 = 1, Q_Q8_0 = 8, Q_Q4_K = 12, Q_Q6_K = 14, Q_MXFP4 = 39,
+                   // internal: Q6_K expert rows repacked at upload into 224-byte superblocks (the
+                   // 210 bytes unchanged, then 14 bytes of padding) so every code word is aligned
+                   Q_Q6_K_PAD = 1014 };
+constexpr int kQ6PadBytes = 224;
+cudaError_t launch_q6k_pad(const uint8_t* src, int64_t n_superblocks, uint8_t* dst, cudaStream_t s);
 
 // bytes of one row of `cols` elements in GGML block layout; -1 when not representable
 int64_t row_bytes(int qtype, int64_t cols);

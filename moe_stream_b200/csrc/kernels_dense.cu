@@ -24,6 +24,7 @@ int64_t row_bytes(int q, int64_t cols) {
     case Q_Q8_0: return cols % 32 ? -1 : cols / 32 * 34;
     case Q_Q4_K: return cols % 256 ? -1 : cols / 256 * 144;
     case Q_Q6_K: return cols % 256 ? -1 : cols / 256 * 210;
+    case Q_Q6_K_PAD: return cols % 256 ? -1 : cols / 256 * kQ6PadBytes;
     case Q_MXFP4: return cols % 32 ? -1 : cols / 32 * 17;
   }
   return -1;
@@ -1288,6 +1289,22 @@ cudaError_t launch_ep_send(const DevCtx& c, const PendingCombine& pc, int H, con
   (void)c;
   if (e.n < 1 || e.n > kMaxEp || e.rank < 0 || e.rank >= e.n || !e.seq || !e.cnt) return cudaErrorInvalidValue;
   return launch_pdl(ep_send_kernel, dim3((unsigned)((H + 255) / 256)), dim3(256), 0, s, pc, H, e);
+}
+
+__global__ void q6k_pad_kernel(const uint16_t* __restrict__ src, int64_t n_sb, uint16_t* __restrict__ dst) {
+  constexpr int kIn = 105, kOut = kQ6PadBytes / 2;   // 16-bit words per superblock
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_sb * kOut; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t sb = i / kOut;
+    const int w = (int)(i - sb * kOut);
+    dst[i] = w < kIn ? src[sb * kIn + w] : (uint16_t)0;
+  }
+}
+
+cudaError_t launch_q6k_pad(const uint8_t* src, int64_t n_sb, uint8_t* dst, cudaStream_t s) {
+  if (n_sb <= 0) return cudaSuccess;
+  if (reinterpret_cast<uintptr_t>(src) % 2 || reinterpret_cast<uintptr_t>(dst) % 16) return cudaErrorInvalidValue;
+  q6k_pad_kernel<<<1184, 256, 0, s>>>(reinterpret_cast<const uint16_t*>(src), n_sb, reinterpret_cast<uint16_t*>(dst));
+  return cudaGetLastError();
 }
 
 }  // namespace ms

@@ -46,7 +46,7 @@ constexpr int kRedRows = 32;              // per-warp partial sums per item (RT=
 
 enum { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_PLAIN = 2 };
 // weight block formats of the streamed matrix
-enum { FMT_MXFP4 = 0, FMT_Q4K = 1, FMT_Q6K = 2 };
+enum { FMT_MXFP4 = 0, FMT_Q4K = 1, FMT_Q6K = 2, FMT_Q6KP = 3 };   // Q6KP: Q6_K in 224-byte superblocks
 
 struct PhaseParams {
   int mode;
@@ -174,6 +174,7 @@ __device__ __forceinline__ uint32_t ld_u32_a2(const uint8_t* p) {
   const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~(uintptr_t)3);
   return __funnelshift_r(w[0], w[1], (uint32_t)(a & 3) * 8u);
 }
+template <bool PAD>
 __device__ __forceinline__ void q6k_block(const uint8_t* sb0, const uint8_t* sb1, int n, int quad, int c,
                                           const uint32_t (&bf)[4], float xscale, float& acc0, float& acc1) {
   const int qlo = n * 64 + (quad & 1) * 32 + 4 * c, qho = 128 + n * 32 + 4 * c;
@@ -189,7 +190,9 @@ __device__ __forceinline__ void q6k_block(const uint8_t* sb0, const uint8_t* sb1
     s1[r] = d * (float)(int8_t)(scw >> 8);
 #pragma unroll
     for (int w = 0; w < 2; ++w) {
-      const uint32_t ql = ld_u32_a2(sb + qlo + 16 * w), qh = ld_u32_a2(sb + qho + 16 * w);
+      // padded superblocks start 16-byte aligned: aligned words; native 210-byte ones: funnel shift
+      const uint32_t ql = PAD ? *reinterpret_cast<const uint32_t*>(sb + qlo + 16 * w) : ld_u32_a2(sb + qlo + 16 * w);
+      const uint32_t qh = PAD ? *reinterpret_cast<const uint32_t*>(sb + qho + 16 * w) : ld_u32_a2(sb + qho + 16 * w);
       const uint32_t q = ((ql >> nsh) & 0x0F0F0F0Fu) | (((qh >> hsh) & 0x03030303u) << 4);
       codes4_to_f16x2(q, 0x64206420u, p[r][w][0], p[r][w][1]);   // 1024 + 32
     }
@@ -464,6 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
         } else {
           // 32-column block b = warp + 16 i lies in superblock b / 8 at sub-block warp % 8
           const float xscale = __int_as_float(max(127 * 8388608 + kbs[i], 0));   // 2^kb
+          constexpr int kSb = FMT == FMT_Q6KP ? kQ6PadBytes : 210;                // Q6_K superblock stride
           const int sbk = b >> 3;
 #pragma unroll
           for (int q = 0; q < RT; ++q) {
@@ -471,8 +475,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_mxfp4_phase_kernel(PhaseParam
               q4k_block(st + off0[q] + 144 * sbk, st + off1[q] + 144 * sbk, warp & 7, c, bf[i], xscale, xsum[i],
                         acc0[q], acc1[q]);
             else
-              q6k_block(st + off0[q] + 210 * sbk, st + off1[q] + 210 * sbk, (warp & 7) >> 2, warp & 3, c, bf[i],
-                        xscale, acc0[q], acc1[q]);
+              q6k_block<FMT == FMT_Q6KP>(st + off0[q] + kSb * sbk, st + off1[q] + kSb * sbk, (warp & 7) >> 2,
+                                         warp & 3, c, bf[i], xscale, acc0[q], acc1[q]);
           }
         }
       }
@@ -541,11 +545,13 @@ cudaError_t dispatch_phase(const DevCtx& c, const PhaseParams& p, cudaStream_t s
   if (p.fmt == FMT_MXFP4) return p.mode == MODE_GATEUP ? dispatch_nbw<FMT_MXFP4, 2>(c, p, s) : dispatch_nbw<FMT_MXFP4, 1>(c, p, s);
   if (p.fmt == FMT_Q4K) return p.mode == MODE_GATEUP ? dispatch_nbw<FMT_Q4K, 2>(c, p, s) : dispatch_nbw<FMT_Q4K, 1>(c, p, s);
   if (p.fmt == FMT_Q6K) return p.mode == MODE_GATEUP ? dispatch_nbw<FMT_Q6K, 2>(c, p, s) : dispatch_nbw<FMT_Q6K, 1>(c, p, s);
+  if (p.fmt == FMT_Q6KP) return p.mode == MODE_GATEUP ? dispatch_nbw<FMT_Q6KP, 2>(c, p, s) : dispatch_nbw<FMT_Q6KP, 1>(c, p, s);
   return cudaErrorInvalidValue;
 }
 
 int fmt_of(int qtype) {
-  return qtype == Q_MXFP4 ? FMT_MXFP4 : qtype == Q_Q4_K ? FMT_Q4K : qtype == Q_Q6_K ? FMT_Q6K : -1;
+  return qtype == Q_MXFP4 ? FMT_MXFP4 : qtype == Q_Q4_K ? FMT_Q4K : qtype == Q_Q6_K ? FMT_Q6K
+       : qtype == Q_Q6_K_PAD ? FMT_Q6KP : -1;
 }
 
 int pick_stages(int stage_bytes) {
@@ -836,6 +842,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_group_kernel(GroupParams p) {
                      acc0[q], acc1[q]);
         } else {
           const float xscale = __int_as_float(max(127 * 8388608 + kbs[i], 0));
+          constexpr int kSb = FMT == FMT_Q6KP ? kQ6PadBytes : 210;   // Q6_K superblock stride
           const int sbk = b >> 3, sub = b & 7;
 #pragma unroll
           for (int q = 0; q < RT; ++q) {
@@ -843,8 +850,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_group_kernel(GroupParams p) {
               q4k_block(st + off0[q] + 144 * sbk, st + off1[q] + 144 * sbk, sub, c, bf[i], xscale, xsum[i],
                         acc0[q], acc1[q]);
             else
-              q6k_block(st + off0[q] + 210 * sbk, st + off1[q] + 210 * sbk, sub >> 2, sub & 3, c, bf[i], xscale,
-                        acc0[q], acc1[q]);
+              q6k_block<FMT == FMT_Q6KP>(st + off0[q] + kSb * sbk, st + off1[q] + kSb * sbk, sub >> 2, sub & 3, c,
+                                         bf[i], xscale, acc0[q], acc1[q]);
           }
         }
       }
@@ -940,11 +947,13 @@ cudaError_t dispatch_group(const DevCtx& c, const GroupParams& p, cudaStream_t s
     if (p.fmt == FMT_MXFP4) return group_nbw<FMT_MXFP4, 1, 4>(c, p, s);
     if (p.fmt == FMT_Q4K) return group_nbw<FMT_Q4K, 1, 4>(c, p, s);
     if (p.fmt == FMT_Q6K) return group_nbw<FMT_Q6K, 1, 4>(c, p, s);
+    if (p.fmt == FMT_Q6KP) return group_nbw<FMT_Q6KP, 1, 4>(c, p, s);
     return cudaErrorInvalidValue;
   }
   if (p.fmt == FMT_MXFP4) return gu ? group_nbw<FMT_MXFP4, 2, kCW>(c, p, s) : group_nbw<FMT_MXFP4, 1, kCW>(c, p, s);
   if (p.fmt == FMT_Q4K) return gu ? group_nbw<FMT_Q4K, 2, kCW>(c, p, s) : group_nbw<FMT_Q4K, 1, kCW>(c, p, s);
   if (p.fmt == FMT_Q6K) return gu ? group_nbw<FMT_Q6K, 2, kCW>(c, p, s) : group_nbw<FMT_Q6K, 1, kCW>(c, p, s);
+  if (p.fmt == FMT_Q6KP) return gu ? group_nbw<FMT_Q6KP, 2, kCW>(c, p, s) : group_nbw<FMT_Q6KP, 1, kCW>(c, p, s);
   return cudaErrorInvalidValue;
 }
 
@@ -974,20 +983,27 @@ __device__ __forceinline__ float router_block_sum(float v, float* red) {
 }
 
 // Top-k selection and routing weights of one token by one warp, after every logit is written.
-__device__ __forceinline__ void router_select(const RouterArgs& a, uint32_t* err, int lane) {
-  // ---- top-k by one warp (ties -> lower index, as a stable descending sort) ----
-  // lane l holds experts l, l + 32, ...; a 32-bit mask per lane marks the ones taken
-  const int per = (a.E + 31) / 32;
+// Lane l holds logits l, l + 32, ... in registers (read once); ties go to the lower index, as a
+// stable descending sort does (layer.rs:2346-2403).
+template <int kPer>
+__device__ __forceinline__ void router_select_t(const RouterArgs& a, uint32_t* err, int lane) {
+  float lv[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = lane + 32 * j;
+    lv[j] = i < a.E ? __ldcg(&a.logits[i]) : -INFINITY;
+  }
   uint32_t taken = 0u;
   float sel_v[kMaxK];
   int sel_i[kMaxK];
   for (int k = 0; k < a.K; ++k) {
     float best = -INFINITY;
     int bidx = 0x7fffffff;
-    for (int j = 0; j < per; ++j) {
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
       const int i = lane + 32 * j;
       if (i >= a.E || ((taken >> j) & 1u)) continue;
-      const float v = __ldcg(&a.logits[i]);
+      const float v = lv[j];
       if (v > best || (v == best && i < bidx)) { best = v; bidx = i; }
     }
 #pragma unroll
@@ -1004,28 +1020,43 @@ __device__ __forceinline__ void router_select(const RouterArgs& a, uint32_t* err
     sel_v[k] = best;
     sel_i[k] = bidx;
   }
+  float w[kMaxK];
+  if (a.softmax_weight) {              // layer.rs:2361-2372: softmax over the selected logits
+    float mx = -INFINITY;
+    for (int k = 0; k < a.K; ++k) mx = fmaxf(mx, sel_v[k]);
+    float sum = 0.f;
+    for (int k = 0; k < a.K; ++k) { w[k] = expf(sel_v[k] - mx); }
+    for (int k = 0; k < a.K; ++k) sum += w[k];
+    for (int k = 0; k < a.K; ++k) w[k] = w[k] / sum;
+  } else {                              // layer.rs:2374-2394: softmax over all, then (re)normalise
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) mx = fmaxf(mx, lv[j]);
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (lane + 32 * j < a.E) sum += expf(lv[j] - mx);
+    sum = warp_sum(sum);
+    float ts = 0.f;
+    for (int k = 0; k < a.K; ++k) { w[k] = expf(sel_v[k] - mx) / sum; }
+    for (int k = 0; k < a.K; ++k) ts += w[k];
+    if (a.normalize) for (int k = 0; k < a.K; ++k) w[k] = w[k] / ts;
+  }
   if (lane == 0) {
-    float w[kMaxK];
-    if (a.softmax_weight) {              // layer.rs:2361-2372
-      float mx = -INFINITY;
-      for (int k = 0; k < a.K; ++k) mx = fmaxf(mx, sel_v[k]);
-      float sum = 0.f;
-      for (int k = 0; k < a.K; ++k) { w[k] = expf(sel_v[k] - mx); }
-      for (int k = 0; k < a.K; ++k) sum += w[k];
-      for (int k = 0; k < a.K; ++k) w[k] = w[k] / sum;
-    } else {                              // layer.rs:2374-2394
-      float mx = -INFINITY;
-      for (int i = 0; i < a.E; ++i) mx = fmaxf(mx, __ldcg(&a.logits[i]));
-      float sum = 0.f;
-      for (int i = 0; i < a.E; ++i) sum += expf(__ldcg(&a.logits[i]) - mx);
-      float ts = 0.f;
-      for (int k = 0; k < a.K; ++k) { w[k] = expf(sel_v[k] - mx) / sum; }
-      for (int k = 0; k < a.K; ++k) ts += w[k];
-      if (a.normalize) for (int k = 0; k < a.K; ++k) w[k] = w[k] / ts;
-    }
     for (int k = 0; k < a.K; ++k) { a.idx[k] = sel_i[k]; a.wts[k] = w[k]; }
     *a.counter = 0u;
   }
+}
+
+// logits per lane sized to the expert count
+__device__ __forceinline__ void router_select(const RouterArgs& a, uint32_t* err, int lane) {
+  const int per = (a.E + 31) / 32;
+  if (per <= 1) router_select_t<1>(a, err, lane);
+  else if (per <= 4) router_select_t<4>(a, err, lane);
+  else if (per <= 8) router_select_t<8>(a, err, lane);
+  else if (per <= 16) router_select_t<16>(a, err, lane);
+  else router_select_t<kRouterMaxE / 32>(a, err, lane);
 }
 
 // One CTA per expert row.  Before waiting for the previous kernel the CTA starts a bulk copy of

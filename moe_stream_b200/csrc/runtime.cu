@@ -397,6 +397,24 @@ ms_status set_layer_tensor(ms_model* m, int li, const std::string& t, int q, con
         if (e != cudaSuccess) return cuda_fail(m->ctx, e, "mxfp4 repack");
         return MS_OK;
       }
+      if (q == Q_Q6_K) {
+        // Q6_K rows are repacked into 224-byte superblocks (same bytes + 14 bytes of padding) so
+        // the expert kernels read aligned code words and copy rows into bank-padded stages
+        const int64_t n_sb = (int64_t)m->n_local * x.rows * (x.cols / 256);
+        ms_status s = m->alloc(x.w, padded((size_t)n_sb * kQ6PadBytes));
+        if (s != MS_OK) return s;
+        cudaStream_t os = m->ctx->own;
+        void* tmp = nullptr;
+        MS_CUDA(m->ctx, cudaMalloc(&tmp, (size_t)per * m->n_local));
+        cudaError_t e = cudaMemcpyAsync(tmp, (const uint8_t*)data + per * m->expert_base, (size_t)per * m->n_local,
+                                        cudaMemcpyHostToDevice, os);
+        if (e == cudaSuccess) e = launch_q6k_pad((const uint8_t*)tmp, n_sb, *x.w, os);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(os);
+        cudaFree(tmp);
+        if (e != cudaSuccess) return cuda_fail(m->ctx, e, "q6_k repack");
+        *x.qt = Q_Q6_K_PAD;
+        return MS_OK;
+      }
       ms_status s = m->alloc(x.w, padded((size_t)per * m->n_local));
       if (s != MS_OK) return s;
       return upload(m, *x.w, (const uint8_t*)data + per * m->expert_base, (size_t)per * m->n_local);
