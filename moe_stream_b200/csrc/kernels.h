@@ -239,6 +239,7 @@ struct AttnArgs {
   int batch = 1;
   int64_t bs_qkv = 0, bs_kv = 0, bs_out = 0;
   int spl = 0;                     // streaming kernel: positions per split (a multiple of 32); 0: one-sequence tile kernel
+  int head_split = 1;              // streaming kernel: CTAs sharing a kv head, each with nh/nkv/head_split query heads
 };
 cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s);
 // tile-kernel splits (grid.x) needed to cover `range` attended positions

@@ -603,7 +603,7 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
   __shared__ float mw[kAWarps][REP], lw[kAWarps][REP];
   __shared__ uint32_t last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kh = blockIdx.y, sidx = blockIdx.x, S = gridDim.x;
+  const int vh = blockIdx.y, kh = vh / a.head_split, sidx = blockIdx.x, S = gridDim.x;   // vh: kv head x query-head group
   if (blockIdx.z) {   // sequence b of a lockstep batch
     const int64_t b = blockIdx.z;
     a.qkv += b * a.bs_qkv;
@@ -641,11 +641,11 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
   pdl_wait_prior();
   pdl_launch_dependents();
   const int half = a.rot / 2;
-  float* part = a.part + ((size_t)kh * S + sidx) * REP * (HD + 2);
+  float* part = a.part + ((size_t)vh * S + sidx) * REP * (HD + 2);
   if (active) {
     const float* cs = a.cos_t + (size_t)pos * half;
     const float* sn = a.sin_t + (size_t)pos * half;
-    for (int i = threadIdx.x; i < REP * HD; i += kAThreads) qs[i] = a.qkv[(size_t)kh * REP * HD + i];
+    for (int i = threadIdx.x; i < REP * HD; i += kAThreads) qs[i] = a.qkv[(size_t)vh * REP * HD + i];
     if (has_new) {
       const float* kq = a.qkv + (size_t)a.nh * HD + (size_t)kh * HD;
       const float* vq = kq + (size_t)a.nkv * HD;
@@ -660,7 +660,7 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
     for (int h = 0; h < REP; ++h) rope_inplace(qs + h * HD, a.rot, cs, sn);
     if (has_new) rope_inplace(kn, a.rot, cs, sn);
     __syncthreads();
-    if (has_new) {   // kv_cache.rs:37-60 append (ring slot for sliding-window layers)
+    if (has_new && vh % a.head_split == 0) {   // kv_cache.rs:37-60 append (by the kv head's first query-head group)
       float* kd = a.kc + ((size_t)kh * a.cap + slot_of(pos)) * HD;
       float* vd = a.vc + ((size_t)kh * a.cap + slot_of(pos)) * HD;
       for (int i = threadIdx.x; i < HD; i += kAThreads) { kd[i] = kn[i]; vd[i] = vn[i]; }
@@ -810,12 +810,12 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
   }
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) last = (atomicAdd(&a.cnt[kh], 1u) == (uint32_t)S - 1) ? 1u : 0u;
+  if (threadIdx.x == 0) last = (atomicAdd(&a.cnt[vh], 1u) == (uint32_t)S - 1) ? 1u : 0u;
   __syncthreads();
   if (!last) return;
   __threadfence();
   // ---- merge the splits of this kv group (+ attention sink) ----
-  const float* gp = a.part + (size_t)kh * S * REP * (HD + 2);
+  const float* gp = a.part + (size_t)vh * S * REP * (HD + 2);
   float* hm = &mw[0][0];
   float* hinv = &lw[0][0];
   for (int i = threadIdx.x; i < S * REP; i += kAThreads) wsm[i] = __ldcg(&gp[(size_t)i * (HD + 2)]);
@@ -824,7 +824,7 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
     float M = -INFINITY;
     for (int s = 0; s < S; ++s) M = fmaxf(M, wsm[s * REP + h]);
     float sink = 0.f;
-    if (a.sinks) { sink = a.sinks[kh * REP + h]; M = 0.5f * ((M + sink) + fabsf(M - sink)); }
+    if (a.sinks) { sink = a.sinks[vh * REP + h]; M = 0.5f * ((M + sink) + fabsf(M - sink)); }
     float L = 0.f;
     for (int s = 0; s < S; ++s) {
       const float m = wsm[s * REP + h];
@@ -855,7 +855,7 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
       for (int u = 0; u < 8; ++u) o = fmaf(wsm[(s + u) * REP + h], v[u], o);
     }
     for (; s < S; ++s) o = fmaf(wsm[s * REP + h], __ldcg(src + (size_t)s * stride), o);
-    a.out[(size_t)(kh * REP + h) * HD + d] = o;
+    a.out[(size_t)(vh * REP + h) * HD + d] = o;
     if (a.oq) ow[h * HD + d] = o;
   }
   if (a.oq) {   // Q8_0 blocks of this group's output (the O-projection's activation)
@@ -865,11 +865,11 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
       float v[32];
 #pragma unroll
       for (int k = 0; k < 32; ++k) v[k] = og[32 * bl + k];
-      const int gb = kh * REP * HD / 32 + bl;
+      const int gb = vh * REP * HD / 32 + bl;
       quantize_q8_block(v, a.oq + 32 * gb, &a.od[gb]);
     }
   }
-  if (threadIdx.x == 0) a.cnt[kh] = 0u;
+  if (threadIdx.x == 0) a.cnt[vh] = 0u;
 }
 
 // ============================ LM head (f16) + argmax ============================
@@ -1200,13 +1200,14 @@ int attn_split_positions(int range, int units, int sm_count) {
 
 cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s) {
   if (a.nkv <= 0 || a.nh % a.nkv || a.S <= 0 || a.rot > a.hd || a.rot % 2) return cudaErrorInvalidValue;
-  const int rep = a.nh / a.nkv;
+  if (a.head_split < 1 || (a.nh / a.nkv) % a.head_split || (a.head_split > 1 && a.spl == 0)) return cudaErrorInvalidValue;
+  const int rep = a.nh / a.nkv / a.head_split;   // query heads per CTA
   if ((size_t)a.S * rep > 8192) return cudaErrorInvalidValue;   // merge weights: <= 32 KB of shared memory
   if (a.batch < 1 || (a.batch > 1 && (a.bs_out % 32 || (a.oq && !a.od)))) return cudaErrorInvalidValue;
   // spl == 0: the single-sequence tile kernel (splits of attn_splits(range, hd) positions);
   // otherwise the streaming kernel with spl positions per split
   if (a.spl < 0 || a.spl % kAChunk || (a.spl == 0 && a.batch != 1)) return cudaErrorInvalidValue;
-  const dim3 grid((unsigned)a.S, (unsigned)a.nkv, (unsigned)a.batch);
+  const dim3 grid((unsigned)a.S, (unsigned)(a.nkv * a.head_split), (unsigned)a.batch);
   switch (a.hd) {
     case 32: return launch_attn_hd<32>(a, c, rep, grid, s);
     case 64: return launch_attn_hd<64>(a, c, rep, grid, s);
