@@ -482,8 +482,9 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     aa.rot = c.rot_dim; aa.pos = &m->st->pos; aa.kc = Lw.kc; aa.vc = Lw.vc; aa.cap = Lw.cap; aa.window = Lw.window;
     aa.sinks = Lw.sinks; aa.part = m->attn_part; aa.cnt = m->attn_cnt; aa.out = m->attn_out; aa.nh = c.heads;
     aa.nkv = c.kv_heads; aa.hd = c.head_dim; aa.S = Lw.window ? m->splits_swa : m->splits_full; aa.spl = m->attn_spl;
-    // single sequence, streaming kernel: two CTAs per kv head (each half its query heads) fill the GPU
-    if (m->attn_spl && (c.heads / c.kv_heads) % 2 == 0 && c.heads / c.kv_heads >= 4) aa.head_split = 2;
+    // single sequence, streaming kernel: several CTAs per kv head (each a group of its query heads) fill the GPU
+    if (m->attn_spl && (c.heads / c.kv_heads) % 4 == 0) aa.head_split = 4;
+    else if (m->attn_spl && (c.heads / c.kv_heads) % 2 == 0 && c.heads / c.kv_heads >= 4) aa.head_split = 2;
     aa.scale = (float)(1.0 / std::sqrt((double)c.head_dim)); aa.oq = m->xq_a; aa.od = m->xd_a;
     LAUNCH(launch_attention(dc, aa, s));
     Q8GemvArgs oa;
@@ -1189,7 +1190,7 @@ ms_status ms_model_finalize(ms_model* m) {
   s = s ? s : m->alloc(&m->router_cnt, 16);
   s = s ? s : m->alloc(&m->resid_cnt, 16);
   s = s ? s : m->alloc(&m->tile_cnt, (size_t)(H / 16 + 16) * 4);
-  s = s ? s : m->alloc(&m->attn_cnt, (size_t)(2 * c.kv_heads + 16) * 4);
+  s = s ? s : m->alloc(&m->attn_cnt, (size_t)(4 * c.kv_heads + 16) * 4);
   s = s ? s : m->alloc(&m->st, sizeof(StepState));
   s = s ? s : m->alloc(&m->token_log, (size_t)(c.max_seq_len + 1) * 4);
   if (any_tc) {
