@@ -703,13 +703,36 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
     };
     for (int cb = p0 + warp * kAChunk; cb < p1; cb += kAWarps * kAChunk) {
       const int w1 = min(cb + kAChunk, p1);
+      // a full chunk without the new row, contiguous in the cache: plain strided row loads
+      const bool fast = w1 - cb == kAChunk && !(cb <= pos && pos < cb + kAChunk) &&
+                        (!a.window || slot_of(cb) + kAChunk <= a.cap);
+      const size_t row0 = (size_t)(fast ? slot_of(cb) : 0) * HD + lane * DPL;
+      auto load_fast = [&](const float* base, int u, float (&r)[DPL]) {
+        const float* src = base + row0 + (size_t)u * HD;
+        if constexpr (DPL % 4 == 0) {
+#pragma unroll
+          for (int d = 0; d < DPL; d += 4) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(src + d));
+            r[d] = v.x; r[d + 1] = v.y; r[d + 2] = v.z; r[d + 3] = v.w;
+          }
+        } else {
+#pragma unroll
+          for (int d = 0; d < DPL; d += 2) {
+            const float2 v = __ldg(reinterpret_cast<const float2*>(src + d));
+            r[d] = v.x; r[d + 1] = v.y;
+          }
+        }
+      };
       if (cb + kAWarps * kAChunk < p1) prefetch_chunk(cb + kAWarps * kAChunk);
       // ---- scores of the chunk's positions -> psm[warp][h][j] ----
 #pragma unroll 1
       for (int jb = 0; jb < kAChunk; jb += PB) {
         float kr[PB][DPL];
 #pragma unroll
-        for (int u = 0; u < PB; ++u) load_rows(kbase, kn, cb + jb + u, w1, kr[u]);
+        for (int u = 0; u < PB; ++u) {
+          if (fast) load_fast(kbase, jb + u, kr[u]);
+          else load_rows(kbase, kn, cb + jb + u, w1, kr[u]);
+        }
 #pragma unroll
         for (int u = 0; u < PB; ++u) {
           float v[REP];
@@ -767,7 +790,10 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
       for (int jb = 0; jb < kAChunk; jb += PB) {
         float vr[PB][DPL];
 #pragma unroll
-        for (int u = 0; u < PB; ++u) load_rows(vbase, vn, cb + jb + u, w1, vr[u]);
+        for (int u = 0; u < PB; ++u) {
+          if (fast) load_fast(vbase, jb + u, vr[u]);
+          else load_rows(vbase, vn, cb + jb + u, w1, vr[u]);
+        }
 #pragma unroll
         for (int u = 0; u < PB; ++u) {
 #pragma unroll
