@@ -666,11 +666,12 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
       for (int i = threadIdx.x; i < HD; i += kAThreads) { kd[i] = kn[i]; vd[i] = vn[i]; }
     }
     const int my_h = lane / GL, gi = lane % GL;
+    // query heads in lane order h ^ my_h: the reduce-scatter below then always keeps the lower half
     float qr[REP][DPL];
 #pragma unroll
     for (int h = 0; h < REP; ++h)
 #pragma unroll
-      for (int d = 0; d < DPL; ++d) qr[h][d] = qs[h * HD + lane * DPL + d];
+      for (int d = 0; d < DPL; ++d) qr[h][d] = qs[(h ^ my_h) * HD + lane * DPL + d];
     float o[REP][DPL];
 #pragma unroll
     for (int h = 0; h < REP; ++h)
@@ -743,16 +744,13 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
             for (int d = 0; d < DPL; ++d) t = fmaf(qr[h][d], kr[u][d], t);
             v[h] = t;
           }
-          // reduce-scatter: halving steps leave head (lane / GL) in v[0], then a sum over its GL lanes
+          // reduce-scatter: v[i] is head i ^ my_h, so each halving step keeps v[0 .. n/2) and adds the
+          // partner's v[n/2 .. n) (the same heads in its order); v[0] ends as head my_h, then a sum
+          // over its GL lanes
 #pragma unroll
           for (int o2 = 16, n = REP; n > 1; o2 >>= 1, n >>= 1) {
-            const bool up = (lane & o2) != 0;
 #pragma unroll
-            for (int i = 0; i < n / 2; ++i) {
-              const float send = up ? v[i] : v[i + n / 2];
-              const float keep = up ? v[i + n / 2] : v[i];
-              v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o2);
-            }
+            for (int i = 0; i < n / 2; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i + n / 2], o2);
           }
 #pragma unroll
           for (int o2 = GL / 2; o2 > 0; o2 >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o2);
