@@ -111,6 +111,41 @@ MS_API ms_status ms_router_topk(ms_ctx* ctx, const float* d_h, const float* d_no
                          const float* d_router_b, const uint8_t* d_mask, int hidden, int n_experts, int top_k,
                          int arch, int norm_topk_prob, float* d_xn, float* d_logits, int32_t* d_idx, float* d_wts);
 
+/* RoPE, NeoX half-rotation of the first rot_dim dims of every head (dims beyond pass through):
+ * y = rope(x), x / y [n_tokens][heads][head_dim] (y must not overlap x), per-token tables
+ * cos / sin [n_tokens][rot_dim / 2] already sliced at each token's position.  Replaces
+ * fused_rope_metal (metal/mod.rs:383-472) and rotary_embedding / partial_rotary_embedding
+ * (ops/attention.rs:49-164). */
+MS_API ms_status ms_rope(ms_ctx* ctx, const float* d_x, const float* d_cos, const float* d_sin, int n_tokens,
+                         int heads, int head_dim, int rot_dim, float* d_y);
+
+/* One attention half-layer in device memory (layer.rs:511-749 for a single decode token). */
+typedef struct ms_attn_layer {
+  int hidden, heads, kv_heads, head_dim, rot_dim;
+  float eps;                  /* RMSNorm epsilon (attention norm and QK-norm) */
+  int window;                 /* > 0: sliding window (the cache is a ring of `window` slots) */
+  int cap;                    /* cache slots per kv head (== window for a sliding-window layer) */
+  const float* attn_norm;     /* [hidden] */
+  const void* wqkv;           /* Q8_0 [heads*hd + 2*kv_heads*hd, hidden]: q, k, v rows concatenated */
+  const float* bqkv;          /* [heads*hd + 2*kv_heads*hd] or NULL */
+  const void* wo;             /* Q8_0 [hidden, heads*hd] */
+  const float* bo;            /* [hidden] or NULL */
+  const float* sinks;         /* [heads] or NULL */
+  const float* q_norm;        /* [head_dim] QK-RMSNorm weights, or NULL (both or neither) */
+  const float* k_norm;
+  float* k_cache;             /* f32 [kv_heads][cap][head_dim], updated in place */
+  float* v_cache;
+  const float* cos_t;         /* RoPE tables [max_seq][rot_dim / 2] */
+  const float* sin_t;
+} ms_attn_layer;
+
+/* h += O(SDPA(RoPE(QKV(RMSNorm(h))))) for one token at position pos, appending its K/V to the
+ * cache (slot pos, or pos % window).  Q8_0 projections with the activation quantized to Q8_0
+ * (candle QMatMul numerics), GQA, attention sinks, sliding window.  Replaces the per-layer attention
+ * dispatch of the Metal decode path (quantized_attn_matmul_metal_gpu_batched, metal/mod.rs:1123,
+ * fused_rope_metal 383, and LayerForward's attention branch, model/layer.rs:393-503, 511-749). */
+MS_API ms_status ms_attn_layer_decode(ms_ctx* ctx, const ms_attn_layer* layer, int pos, float* d_h);
+
 /* One-token MXFP4 expert FFN with weighted combine into the residual stream:
  * d_h += sum over selected experts e (ascending id) of w_e * (Wd_e act_e + bd_e),
  * act_e = SwiGLU(Wg_e x + bg_e, Wu_e x + bu_e).  Replaces gpu_routed_moe_forward_metal
@@ -126,12 +161,14 @@ MS_API ms_status ms_moe_mxfp4_decode(ms_ctx* ctx, const void* d_gate, const void
  * memory when they run the MoE step (a fixed memory pool owns the whole budget, or the
  * step runs where cudaMalloc is not allowed).  No counterpart in the reference: the Metal
  * path allocates its routing buffers up front.  Same arguments and result as
- * ms_moe_mxfp4_decode; the scratch lives in one fixed device array of 513 KiB that every
+ * ms_moe_mxfp4_decode; the scratch lives in one fixed device array of 512 KiB that every
  * GPU loading this library keeps until exit, so top_k <= 16, hidden <= 4096 and
  * inter <= 4096 (larger sizes return MS_ERR_SHAPE).  The first call on a device looks up
- * the array's device address; make that first call before any stream capture.  Every call
- * shares the array: calls that overlap on the GPU (other streams or contexts on the same
- * device) race and must be serialised by the caller. */
+ * the array's device address; make that first call before any stream capture, and do not
+ * use the entry point across a cudaDeviceReset (the looked-up address would be stale).
+ * Every call shares the array: calls that overlap on the GPU (other streams or contexts on
+ * the same device) race and must be serialised by the caller.  The calling thread's current
+ * device is left as it was. */
 MS_API ms_status ms_moe_mxfp4_decode_noalloc(ms_ctx* ctx, const void* d_gate, const void* d_up, const void* d_down,
                                              const float* d_gate_b, const float* d_up_b, const float* d_down_b,
                                              int hidden, int inter, int n_experts, int top_k, int arch,
@@ -274,6 +311,13 @@ MS_API ms_status ms_model_seq_len(const ms_model* m, int* n);
 MS_API ms_status ms_model_last_hidden(ms_model* m, float* out);
 MS_API ms_status ms_model_last_routing(ms_model* m, int layer, int32_t* idx, float* wts);
 MS_API ms_status ms_model_last_logits(ms_model* m, float* out);
+/* Layer trace for parity tests (single sequence): when enabled, every later step also copies the
+ * residual stream after each layer and each layer's router logits (after bias and dummy mask) into
+ * model buffers; ms_model_layer_trace reads those of the last step: hidden [layers][hidden],
+ * logits [layers][experts] (either may be NULL).  Mirrors the per-layer dumps of the reference's
+ * examples/full_compare.rs. */
+MS_API ms_status ms_model_set_trace(ms_model* m, int enable);
+MS_API ms_status ms_model_layer_trace(ms_model* m, float* hidden, float* logits);
 /* 1 (default): replay each step as a captured CUDA graph; 0: plain stream launches. */
 MS_API ms_status ms_model_set_graph(ms_model* m, int enable);
 /* Tracing (single device, after at least one decode step): the decode step's launches grouped by

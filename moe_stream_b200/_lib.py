@@ -35,6 +35,15 @@ class ModelConfig(C.Structure):
                 ("max_seq_len", C.c_int), ("ep_rank", C.c_int), ("ep_size", C.c_int), ("attn_splits", C.c_int)]
 
 
+class AttnLayer(C.Structure):
+    """ms_attn_layer: one attention half-layer in device memory (device pointers as ints)."""
+    _fields_ = [("hidden", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int), ("head_dim", C.c_int),
+                ("rot_dim", C.c_int), ("eps", C.c_float), ("window", C.c_int), ("cap", C.c_int),
+                ("attn_norm", C.c_void_p), ("wqkv", C.c_void_p), ("bqkv", C.c_void_p), ("wo", C.c_void_p),
+                ("bo", C.c_void_p), ("sinks", C.c_void_p), ("q_norm", C.c_void_p), ("k_norm", C.c_void_p),
+                ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("cos_t", C.c_void_p), ("sin_t", C.c_void_p)]
+
+
 class DeltaNetLayer(C.Structure):
     """ms_deltanet_layer: one Gated DeltaNet layer in device memory (device pointers as ints)."""
     _fields_ = [("hidden", C.c_int), ("n_k_heads", C.c_int), ("head_k_dim", C.c_int), ("n_v_heads", C.c_int),
@@ -78,6 +87,8 @@ _SIGS = {
                                              _vp]),
     "ms_moe_mxfp4_prefill_packed": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i, _vp,
                                               _vp, _vp]),
+    "ms_rope": (C.c_int, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "ms_attn_layer_decode": (C.c_int, [_vp, C.POINTER(AttnLayer), _i, _vp]),
     "ms_deltanet_decode": (C.c_int, [_vp, C.POINTER(DeltaNetLayer), _vp, _vp, _vp, _vp]),
     "ms_shared_expert": (C.c_int, [_vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _vp, _vp]),
     "ms_nccl_unique_id": (C.c_int, [_vp, _vp, C.c_size_t]),
@@ -110,6 +121,8 @@ _SIGS = {
     "ms_model_last_hidden": (C.c_int, [_vp, _fp]),
     "ms_model_last_routing": (C.c_int, [_vp, _i, _ip, _fp]),
     "ms_model_last_logits": (C.c_int, [_vp, _fp]),
+    "ms_model_set_trace": (C.c_int, [_vp, _i]),
+    "ms_model_layer_trace": (C.c_int, [_vp, _fp, _fp]),
     "ms_model_set_graph": (C.c_int, [_vp, _i]),
     "ms_model_kernels_per_step": (C.c_int, [_vp]),
     "ms_model_profile_step": (C.c_int, [_vp, _fp, _i, C.POINTER(C.c_int)]),

@@ -28,16 +28,22 @@ def build(verbose: bool = False) -> str:
     os.makedirs(OUT, exist_ok=True)
     headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
     headers.append(os.path.join(os.path.dirname(HERE), "include", "moestream_cuda.h"))
-    objs = []
+    objs, cmds = [], []
     for src in SOURCES:
         s = os.path.join(CSRC, src)
         o = os.path.join(OUT, src.replace(".cu", ".o"))
         if _stale(o, [s] + headers):
-            cmd = [NVCC, *FLAGS, "-c", s, "-o", o]
-            if verbose:
-                print(" ".join(cmd), file=sys.stderr)
-            subprocess.run(cmd, check=True)
+            cmds.append([NVCC, *FLAGS, "-c", s, "-o", o])
         objs.append(o)
+    # translation units compile in parallel (one nvcc process each)
+    procs = []
+    for cmd in cmds:
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        procs.append((cmd, subprocess.Popen(cmd)))
+    failed = [cmd for cmd, p in procs if p.wait() != 0]
+    if failed:
+        raise subprocess.CalledProcessError(1, failed[0])
     if _stale(SO, objs):
         subprocess.run([NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", SO, *objs,
                         "-Xcompiler", "-fPIC", "-lcuda"], check=True)

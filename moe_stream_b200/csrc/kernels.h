@@ -33,6 +33,12 @@ struct DevCtx {
 cudaError_t launch_dequantize(const DevCtx& c, int qtype, const void* blocks, int64_t n, float* out, cudaStream_t s);
 cudaError_t launch_rms_norm(const DevCtx& c, const float* x, const float* w, float* y, int rows, int dim, float eps,
                             cudaStream_t s);
+// RoPE (NeoX half-rotation of the first rot dims) of x [n_tok][heads][hd] with per-token tables
+// cos/sin [n_tok][rot/2] -> y (y must not overlap x)
+cudaError_t launch_rope(const float* x, const float* cs, const float* sn, float* y, int n_tok, int heads, int hd,
+                        int rot, cudaStream_t s);
+// *p = v on the stream (a capturable scalar upload)
+cudaError_t launch_set_i32(int* p, int v, cudaStream_t s);
 
 // A MoE combine not yet applied to the residual stream: the stream's value is
 // h[r] + sum over local slots, in ascending expert id, of partial[slot][r] * wts[slot]
@@ -140,7 +146,7 @@ struct MoeArgs {
   const float* down_b = nullptr;   // [E_local, H] or null
   float* act = nullptr;            // [K, I] scratch
   float* partial = nullptr;        // [K, H] scratch
-  uint32_t* tile_cnt = nullptr;    // [H/16] scratch counters, zero-initialised, self-resetting
+  uint32_t* tile_cnt = nullptr;    // reserved (no kernel reads it; may be null)
   float* h = nullptr;              // [H] residual stream: h += moe(x)   (when out == null)
   float* out = nullptr;            // [H] if set: out = moe(x) (no residual), for EP partial sums
   int H = 0, I = 0, K = 0;

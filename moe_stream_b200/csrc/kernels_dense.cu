@@ -693,12 +693,15 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
             const float4 v = __ldg(reinterpret_cast<const float4*>(src + d));
             r[d] = v.x; r[d + 1] = v.y; r[d + 2] = v.z; r[d + 3] = v.w;
           }
-        } else {
+        } else if constexpr (DPL % 2 == 0) {
 #pragma unroll
           for (int d = 0; d < DPL; d += 2) {
             const float2 v = __ldg(reinterpret_cast<const float2*>(src + d));
             r[d] = v.x; r[d + 1] = v.y;
           }
+        } else {
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) r[d] = __ldg(src + d);   // head_dim 32: one value per lane
         }
       }
     };
@@ -716,12 +719,15 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
             const float4 v = __ldg(reinterpret_cast<const float4*>(src + d));
             r[d] = v.x; r[d + 1] = v.y; r[d + 2] = v.z; r[d + 3] = v.w;
           }
-        } else {
+        } else if constexpr (DPL % 2 == 0) {
 #pragma unroll
           for (int d = 0; d < DPL; d += 2) {
             const float2 v = __ldg(reinterpret_cast<const float2*>(src + d));
             r[d] = v.x; r[d + 1] = v.y;
           }
+        } else {
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) r[d] = __ldg(src + d);   // head_dim 32: one value per lane
         }
       };
       if (cb + kAWarps * kAChunk < p1) prefetch_chunk(cb + kAWarps * kAChunk);
@@ -1138,6 +1144,46 @@ cudaError_t launch_dequantize(const DevCtx& c, int q, const void* blocks, int64_
   if (n <= 0) return cudaSuccess;
   const int bs = 256;
   dequant_kernel<<<(unsigned)((n + bs - 1) / bs), bs, 0, s>>>(q, (const uint8_t*)blocks, n, out);
+  return cudaGetLastError();
+}
+
+// NeoX half-rotation of the first `rot` dims of every head (ops/attention.rs:96-164): for i < rot/2,
+// out[i] = x[i] c - x[i + rot/2] s and out[i + rot/2] = x[i + rot/2] c + x[i] s; dims >= rot pass
+// through.  Products and sums are rounded separately (no fused multiply-add), as the reference's
+// separate tensor ops round them.  One thread per (token, head, dim); cos/sin rows per token.
+__global__ void rope_kernel(const float* __restrict__ x, const float* __restrict__ cs, const float* __restrict__ sn,
+                            float* __restrict__ y, int n_tok, int heads, int hd, int rot) {
+  const int64_t total = (int64_t)n_tok * heads * hd;
+  const int half = rot / 2;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int d = (int)(i % hd);
+    const int64_t t = i / ((int64_t)heads * hd);
+    const float* xh = x + (i - d);
+    float v;
+    if (d < half) {
+      const float c = cs[t * half + d], s = sn[t * half + d];
+      v = __fsub_rn(__fmul_rn(xh[d], c), __fmul_rn(xh[d + half], s));
+    } else if (d < rot) {
+      const float c = cs[t * half + d - half], s = sn[t * half + d - half];
+      v = __fadd_rn(__fmul_rn(xh[d], c), __fmul_rn(xh[d - half], s));
+    } else {
+      v = xh[d];
+    }
+    y[i] = v;
+  }
+}
+
+cudaError_t launch_rope(const float* x, const float* cs, const float* sn, float* y, int n_tok, int heads, int hd,
+                        int rot, cudaStream_t s) {
+  const int64_t total = (int64_t)n_tok * heads * hd;
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4096);
+  rope_kernel<<<blocks, 256, 0, s>>>(x, cs, sn, y, n_tok, heads, hd, rot);
+  return cudaGetLastError();
+}
+
+__global__ void set_i32_kernel(int* p, int v) { *p = v; }
+cudaError_t launch_set_i32(int* p, int v, cudaStream_t s) {
+  set_i32_kernel<<<1, 1, 0, s>>>(p, v);
   return cudaGetLastError();
 }
 

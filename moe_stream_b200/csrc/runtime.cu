@@ -247,6 +247,11 @@ struct ms_model {
   float* tc_part = nullptr;       // split-K partial sums
   uint32_t* tc_cnt = nullptr;
   BatchRt* bt = nullptr;          // lockstep batch state (ms_model_batch_open)
+  // layer trace (ms_model_set_trace): residual stream after each layer [layers][H] and router
+  // logits per layer [layers][E] of the last step, copied inside the step when enabled
+  float* trace_h = nullptr;
+  float* trace_logits = nullptr;
+  bool trace = false;
 
   template <class T>
   ms_status alloc(T** p, size_t bytes, bool zero = true) {
@@ -498,6 +503,11 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     ra.normalize = c.norm_topk_prob;
     if (Lw.tc) ra.xterm = m->xterm;
     LAUNCH(launch_router(dc, ra, s));
+    if (m->trace && m->prof_class < 0) {
+      cudaError_t e_ = cudaMemcpyAsync(m->trace_logits + (size_t)li * c.experts, m->router_logits,
+                                       (size_t)c.experts * 4, cudaMemcpyDeviceToDevice, s);
+      if (e_ != cudaSuccess) return cuda_fail(m->ctx, e_, "trace copy");
+    }
     TcMoeArgs ta;
     ta.gu = Lw.gu_tc; ta.down = Lw.down_tc; ta.gate_b = Lw.gate_b; ta.up_b = Lw.up_b; ta.down_b = Lw.down_b;
     ta.xterm = m->xterm; ta.act_terms = m->act_terms; ta.act = m->act; ta.partial = m->partial; ta.part = m->tc_part;
@@ -568,6 +578,10 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     // h += MoE (ascending expert order); quantize the next layer's attention input
     const float* next_norm = li + 1 < c.layers ? m->L[li + 1].attn_norm : nullptr;
     LAUNCH(launch_resid_norm_q8(dc, pc, m->h, H, next_norm, c.eps, m->xq_h, m->xd_h, m->resid_cnt, s));
+    if (m->trace && m->prof_class < 0) {
+      cudaError_t e_ = cudaMemcpyAsync(m->trace_h + (size_t)li * H, m->h, (size_t)H * 4, cudaMemcpyDeviceToDevice, s);
+      if (e_ != cudaSuccess) return cuda_fail(m->ctx, e_, "trace copy");
+    }
   }
   LmHeadArgs la;
   la.w = m->out_w; la.x = m->h; la.norm_w = m->out_norm; la.eps = c.eps; la.bias = m->out_b; la.logits = m->logits;
@@ -1008,6 +1022,62 @@ ms_status ms_moe_mxfp4_prefill_packed(ms_ctx* c, const void* gu, const void* dow
   a.x = x; a.idx = idx; a.wts = wts; a.out = out; a.scratch = c->scratch;
   a.H = H; a.I = I; a.E = E; a.K = K; a.T = T; a.expert_base = 0; a.oai_swiglu = arch == MS_ARCH_GPT_OSS;
   MS_CUDA(c, launch_moe_prefill(c->dc, a, c->stream));
+  return MS_OK;
+}
+
+ms_status ms_rope(ms_ctx* c, const float* x, const float* cs, const float* sn, int n_tok, int heads, int hd, int rot,
+                  float* y) {
+  if (!c || !x || !cs || !sn || !y || n_tok <= 0 || heads <= 0 || hd <= 0) return MS_ERR_INVALID_ARG;
+  if (rot <= 0 || rot > hd || rot % 2) return fail(c, MS_ERR_SHAPE, "rope: rot_dim %d must be even and <= head_dim %d", rot, hd);
+  if (x == y) return fail(c, MS_ERR_INVALID_ARG, "rope: output must not overlap the input");
+  MS_CUDA(c, launch_rope(x, cs, sn, y, n_tok, heads, hd, rot, c->stream));
+  return MS_OK;
+}
+
+ms_status ms_attn_layer_decode(ms_ctx* c, const ms_attn_layer* L, int pos, float* h) {
+  if (!c || !L || !h || !L->attn_norm || !L->wqkv || !L->wo || !L->k_cache || !L->v_cache || !L->cos_t || !L->sin_t)
+    return MS_ERR_INVALID_ARG;
+  const int H = L->hidden, nh = L->heads, nkv = L->kv_heads, hd = L->head_dim;
+  if (H <= 0 || nh <= 0 || nkv <= 0 || nh % nkv || hd <= 0 || L->cap <= 0 || pos < 0)
+    return fail(c, MS_ERR_SHAPE, "attn layer: invalid shape");
+  if (H % 32 || (nh * hd) % 32 || (hd != 32 && hd != 64 && hd != 128 && hd != 256) || L->rot_dim <= 0 ||
+      L->rot_dim > hd || L->rot_dim % 2)
+    return fail(c, MS_ERR_SHAPE, "attn layer: hidden and q_dim multiples of 32, head_dim 32/64/128/256 required");
+  if ((L->q_norm == nullptr) != (L->k_norm == nullptr)) return fail(c, MS_ERR_INVALID_ARG, "attn layer: q_norm and k_norm go together");
+  if (L->window <= 0 && pos >= L->cap) return fail(c, MS_ERR_SHAPE, "attn layer: position %d beyond the cache", pos);
+  if (L->window > 0 && L->cap != L->window) return fail(c, MS_ERR_SHAPE, "attn layer: sliding-window cache must hold window slots");
+  const int Dq = nh * hd, Dkv = nkv * hd, rep = nh / nkv;
+  const int spl = hd <= 64 ? 0 : 256;
+  const int range = L->cap;
+  const int S = spl ? (range + spl - 1) / spl : attn_splits(range, hd);
+  auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
+  const size_t o_qkv = 0, o_att = o_qkv + up((size_t)(Dq + 2 * Dkv) * 4), o_oq = o_att + up((size_t)Dq * 4),
+               o_od = o_oq + up((size_t)Dq + 64), o_part = o_od + up((size_t)Dq / 32 * 4 + 64),
+               o_pos = o_part + up((size_t)nkv * S * rep * (hd + 2) * 4), total = o_pos + 256;
+  // counter words [4096, 4096 + 4 nkv + 16) are this entry point's (self-resetting)
+  ms_status st = ensure_scratch(c, total, 4096 + 4 * (size_t)nkv + 16);
+  if (st != MS_OK) return st;
+  uint8_t* base = (uint8_t*)c->scratch;
+  int* d_pos = (int*)(base + o_pos);
+  MS_CUDA(c, launch_set_i32(d_pos, pos, c->stream));
+  Q8GemvArgs qa;
+  qa.w = (const uint8_t*)L->wqkv; qa.rows = Dq + 2 * Dkv; qa.cols = H; qa.x = h; qa.norm_w = L->attn_norm;
+  qa.eps = L->eps; qa.bias = L->bqkv; qa.y = (float*)(base + o_qkv);
+  MS_CUDA(c, launch_q8_gemv(c->dc, qa, c->stream));
+  AttnArgs aa;
+  aa.qkv = (const float*)(base + o_qkv); aa.q_norm = L->q_norm; aa.k_norm = L->k_norm; aa.eps = L->eps;
+  aa.cos_t = L->cos_t; aa.sin_t = L->sin_t; aa.rot = L->rot_dim; aa.pos = d_pos; aa.kc = L->k_cache; aa.vc = L->v_cache;
+  aa.cap = L->cap; aa.window = L->window > 0 ? L->window : 0; aa.sinks = L->sinks; aa.part = (float*)(base + o_part);
+  aa.cnt = c->counters + 4096; aa.out = (float*)(base + o_att); aa.nh = nh; aa.nkv = nkv; aa.hd = hd; aa.S = S;
+  aa.spl = spl; aa.scale = (float)(1.0 / std::sqrt((double)hd)); aa.oq = (int8_t*)(base + o_oq);
+  aa.od = (float*)(base + o_od);
+  if (spl && rep % 4 == 0) aa.head_split = 4;
+  else if (spl && rep % 2 == 0 && rep >= 4) aa.head_split = 2;
+  MS_CUDA(c, launch_attention(c->dc, aa, c->stream));
+  Q8GemvArgs oa;
+  oa.w = (const uint8_t*)L->wo; oa.rows = H; oa.cols = Dq; oa.xq_in = aa.oq; oa.xd_in = aa.od; oa.bias = L->bo;
+  oa.residual = h;
+  MS_CUDA(c, launch_q8_gemv(c->dc, oa, c->stream));
   return MS_OK;
 }
 
@@ -1596,6 +1666,32 @@ ms_status ms_model_last_routing(ms_model* m, int layer, int32_t* idx, float* wts
   return MS_OK;
 }
 
+ms_status ms_model_set_trace(ms_model* m, int enable) {
+  if (!m) return MS_ERR_INVALID_ARG;
+  if (!m->finalized) return fail(m->ctx, MS_ERR_STATE, "trace before finalize");
+  cudaSetDevice(m->ctx->device);
+  if (enable && !m->trace_h) {
+    ms_status s = m->alloc(&m->trace_h, (size_t)m->cfg.layers * m->cfg.hidden * 4);
+    s = s ? s : m->alloc(&m->trace_logits, (size_t)m->cfg.layers * m->cfg.experts * 4);
+    if (s != MS_OK) return s;
+  }
+  if (m->trace != (enable != 0)) {
+    MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+    m->trace = enable != 0;
+    if (m->graph) { cudaGraphExecDestroy(m->graph); m->graph = nullptr; }   // re-captured with the copies
+  }
+  return MS_OK;
+}
+
+ms_status ms_model_layer_trace(ms_model* m, float* hidden, float* logits) {
+  if (!m || (!hidden && !logits)) return MS_ERR_INVALID_ARG;
+  if (!m->trace_h) return fail(m->ctx, MS_ERR_STATE, "enable the trace (ms_model_set_trace) before the step");
+  MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+  if (hidden) MS_CUDA(m->ctx, cudaMemcpy(hidden, m->trace_h, (size_t)m->cfg.layers * m->cfg.hidden * 4, cudaMemcpyDeviceToHost));
+  if (logits) MS_CUDA(m->ctx, cudaMemcpy(logits, m->trace_logits, (size_t)m->cfg.layers * m->cfg.experts * 4, cudaMemcpyDeviceToHost));
+  return MS_OK;
+}
+
 ms_status ms_model_last_logits(ms_model* m, float* out) {
   if (!m || !out) return MS_ERR_INVALID_ARG;
   MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
@@ -1834,8 +1930,7 @@ ms_status ms_model_open_gguf(ms_ctx* c, const char* path, int max_seq_len, int e
 // caller that has handed its whole memory budget to a fixed-size pool, a real-time
 // loop that must not enter the CUDA allocator, or a host that replays the step from
 // a context where cudaMalloc is forbidden.  For them this entry point keeps the FFN's
-// scratch (per-slot activations, per-slot partial outputs and per-tile arrival
-// counters) in one file-scope device array instead of context-owned cudaMalloc'd
+// scratch (per-slot activations and per-slot partial outputs) in one file-scope device array instead of context-owned cudaMalloc'd
 // memory.  Every GPU that loads this library holds the array until the process exits.
 // =====================================================================================
 namespace {
@@ -1844,10 +1939,10 @@ constexpr int kNoAllocMaxTopK = 16;      // experts per token
 constexpr int kNoAllocMaxDim = 4096;     // max hidden size and max expert intermediate size
 constexpr size_t kNoAllocActFloats = (size_t)kNoAllocMaxTopK * kNoAllocMaxDim;
 constexpr size_t kNoAllocPartFloats = (size_t)kNoAllocMaxTopK * kNoAllocMaxDim;
-constexpr size_t kNoAllocCounters = kNoAllocMaxDim / 16;
-constexpr size_t kNoAllocFloats = kNoAllocActFloats + kNoAllocPartFloats + kNoAllocCounters;
+constexpr size_t kNoAllocFloats = kNoAllocActFloats + kNoAllocPartFloats;
 
-// act [K*I] | partial [K*H] | tile counters [H/16] (as uint32): 513 KiB per device
+// act [K*I] | partial [K*H]: 512 KiB per device.  Both slices are fully written by the
+// kernels of each call before they are read, so no clearing is needed between calls.
 static __device__ __align__(256) float g_moe_noalloc_scratch[kNoAllocFloats];
 
 constexpr int kNoAllocMaxDevices = 64;
@@ -1855,7 +1950,9 @@ float* g_noalloc_addr[kNoAllocMaxDevices] = {};
 std::mutex g_noalloc_mu;
 
 // once per device, with that device current: the device address of the array (the
-// array's name in host code is only a host-side stand-in and must not reach a kernel)
+// array's name in host code is only a host-side stand-in and must not reach a kernel).
+// The cached address belongs to the device's primary context: after a cudaDeviceReset in
+// the same process it is stale, so the entry point must not be used across a reset.
 ms_status noalloc_setup(ms_ctx* c, float** out) {
   if (c->device < 0 || c->device >= kNoAllocMaxDevices) return fail(c, MS_ERR_INVALID_ARG, "device index too large");
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
@@ -1876,23 +1973,25 @@ extern "C" ms_status ms_moe_mxfp4_decode_noalloc(ms_ctx* c, const void* gate, co
                                                  int E, int K, int arch, const float* x, const int32_t* idx,
                                                  const float* wts, float* h) {
   if (!c || !gate || !up || !down || !x || !idx || !wts || !h || K <= 0 || E <= 0) return MS_ERR_INVALID_ARG;
+  if (H <= 0 || I <= 0) return fail(c, MS_ERR_SHAPE, "moe noalloc: hidden and inter must be positive");
   if (K > kNoAllocMaxTopK || H > kNoAllocMaxDim || I > kNoAllocMaxDim)
     return fail(c, MS_ERR_SHAPE, "moe noalloc: top_k %d / hidden %d / inter %d exceed the fixed scratch "
                 "(top_k <= %d, hidden <= %d, inter <= %d)", K, H, I, kNoAllocMaxTopK, kNoAllocMaxDim, kNoAllocMaxDim);
   if (H % 64 || I % 32) return fail(c, MS_ERR_SHAPE, "moe: hidden %% 64 and inter %% 32 required");
-  cudaError_t e = cudaSetDevice(c->device);
+  // the caller's current device is restored on return
+  int prev = -1;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return cuda_fail(c, e, "cudaGetDevice");
+  struct Restore { int d; ~Restore() { if (d >= 0) cudaSetDevice(d); } } restore{prev != c->device ? prev : -1};
+  e = cudaSetDevice(c->device);
   if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
   float* base = nullptr;
   ms_status s = noalloc_setup(c, &base);
   if (s != MS_OK) return s;
-  uint32_t* cnt = reinterpret_cast<uint32_t*>(base + kNoAllocActFloats + kNoAllocPartFloats);
-  // the array keeps the previous call's contents; the arrival counters must start at zero
-  e = cudaMemsetAsync(cnt, 0, (size_t)(H / 16) * sizeof(uint32_t), c->stream);
-  if (e != cudaSuccess) return cuda_fail(c, e, "cudaMemsetAsync");
   MoeArgs a;
   a.x = x; a.idx = idx; a.wts = wts; a.gate = (const uint8_t*)gate; a.up = (const uint8_t*)up;
   a.down = (const uint8_t*)down; a.gate_b = gb; a.up_b = ub; a.down_b = db;
-  a.act = base; a.partial = base + kNoAllocActFloats; a.tile_cnt = cnt; a.h = h;
+  a.act = base; a.partial = base + kNoAllocActFloats; a.tile_cnt = nullptr; a.h = h;
   a.H = H; a.I = I; a.K = K; a.expert_base = 0; a.n_local = E; a.oai_swiglu = arch == MS_ARCH_GPT_OSS;
   e = launch_moe_mxfp4(c->dc, a, c->stream);
   if (e != cudaSuccess) return cuda_fail(c, e, "moe_mxfp4 (noalloc)");

@@ -111,6 +111,24 @@ class Context:
                                                 _ptr(down_b), hidden, inter, n_experts, top_k, arch, _ptr(x),
                                                 n_tokens, _ptr(idx), _ptr(wts), _ptr(out)), self.h)
 
+    def rope(self, x, cos, sin, n_tokens: int, heads: int, head_dim: int, rot_dim: int, y) -> None:
+        """y = RoPE(x) with per-token cos/sin rows (fused_rope_metal, metal/mod.rs:383-472)."""
+        check(lib().ms_rope(self.h, _ptr(x), _ptr(cos), _ptr(sin), n_tokens, heads, head_dim, rot_dim, _ptr(y)),
+              self.h)
+
+    def attn_layer_decode(self, layer: dict, pos: int, h) -> None:
+        """h += attention(RMSNorm(h)) for one token at `pos` (layer.rs:511-749).  layer: ints hidden,
+        heads, kv_heads, head_dim, rot_dim, window, cap, float eps and device tensors attn_norm, wqkv,
+        wo, k_cache, v_cache, cos_t, sin_t (bqkv, bo, sinks, q_norm, k_norm optional)."""
+        from ._lib import AttnLayer
+        d = layer
+        L = AttnLayer(d["hidden"], d["heads"], d["kv_heads"], d["head_dim"], d["rot_dim"], d["eps"],
+                      d.get("window", 0), d["cap"], _ptr(d["attn_norm"]), _ptr(d["wqkv"]), _ptr(d.get("bqkv")),
+                      _ptr(d["wo"]), _ptr(d.get("bo")), _ptr(d.get("sinks")), _ptr(d.get("q_norm")),
+                      _ptr(d.get("k_norm")), _ptr(d["k_cache"]), _ptr(d["v_cache"]), _ptr(d["cos_t"]),
+                      _ptr(d["sin_t"]))
+        check(lib().ms_attn_layer_decode(self.h, C.byref(L), pos, _ptr(h)), self.h)
+
     def deltanet_decode(self, layer: dict, x, conv_state, rec_state, y) -> None:
         """One Gated DeltaNet decode token.  layer: ints hidden, n_k_heads, head_k_dim, n_v_heads,
         head_v_dim, conv_kernel, eps, qkv_q, gate_q, ba_q, out_q and device tensors qkv, gate, ba, out,
@@ -339,6 +357,19 @@ class Engine:
         o = np.empty(self.config.vocab, dtype=np.float32)
         check(lib().ms_model_last_logits(self.h, o.ctypes.data_as(C.POINTER(C.c_float))), self.ctx.h)
         return o
+
+    def set_trace(self, enable: bool) -> None:
+        """Copy each layer's output and router logits during later steps (parity diagnostics)."""
+        check(lib().ms_model_set_trace(self.h, int(enable)), self.ctx.h)
+
+    def layer_trace(self):
+        """(hidden after each layer [layers, H], router logits [layers, E]) of the last step."""
+        c = self.config
+        hid = np.empty(c.layers * c.hidden, dtype=np.float32)
+        lg = np.empty(c.layers * c.experts, dtype=np.float32)
+        fp = C.POINTER(C.c_float)
+        check(lib().ms_model_layer_trace(self.h, hid.ctypes.data_as(fp), lg.ctypes.data_as(fp)), self.ctx.h)
+        return hid.reshape(c.layers, c.hidden), lg.reshape(c.layers, c.experts)
 
     def set_graph(self, enable: bool) -> None:
         check(lib().ms_model_set_graph(self.h, int(enable)), self.ctx.h)

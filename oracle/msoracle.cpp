@@ -354,7 +354,8 @@ void rope_apply(float* x, int rot_dim, const float* c, const float* s) {
 // ---------------------------------------------------------------------------
 // MoE FFN (layer.rs:756-1895, default f32 path)
 int moe_forward(const orc_moe_layer* L, const float* x, int n_tok, float* out, int32_t* idx_out, float* w_out,
-                const std::vector<int>* dummies, int threads, int e_begin = 0, int e_end = 1 << 30) {
+                const std::vector<int>* dummies, int threads, int e_begin = 0, int e_end = 1 << 30,
+                float* last_logits = nullptr) {
   const int H = L->hidden, I = L->inter, E = L->n_experts, K = L->top_k;
   std::vector<float> logits((size_t)n_tok * E);
   matmul_xwt(x, n_tok, L->router_w, E, H, logits.data(), threads);       // layer.rs:818-820
@@ -362,6 +363,7 @@ int moe_forward(const orc_moe_layer* L, const float* x, int n_tok, float* out, i
     for (int t = 0; t < n_tok; ++t) for (int e = 0; e < E; ++e) logits[(size_t)t * E + e] += L->router_b[e];
   if (dummies)                                                           // layer.rs:1016-1026
     for (int t = 0; t < n_tok; ++t) for (int d : *dummies) logits[(size_t)t * E + d] += -INFINITY;
+  if (last_logits) std::memcpy(last_logits, &logits[(size_t)(n_tok - 1) * E], (size_t)E * 4);
   std::vector<int32_t> idx((size_t)n_tok * K); std::vector<float> wts((size_t)n_tok * K);
   top_k_routing(logits.data(), n_tok, E, K, L->norm_topk_prob != 0, L->oai_swiglu != 0, idx.data(), wts.data());
   if (idx_out) std::memcpy(idx_out, idx.data(), idx.size() * 4);
@@ -523,6 +525,9 @@ struct orc_model {
   const GTensor *embd = nullptr, *out = nullptr; const float* out_norm = nullptr; const float* out_bias = nullptr;
   int seq = 0;
   std::vector<float> last_hidden; std::vector<int32_t> last_idx; std::vector<float> last_w;
+  // per layer, last position of the last forward: residual stream after the layer [layers][H]
+  // and the router logits after bias and dummy mask [layers][E] (test diagnostics)
+  std::vector<float> layer_hidden, layer_logits;
 };
 
 namespace {
@@ -682,6 +687,51 @@ int orc_moe_forward(const orc_moe_layer* L, const float* x, int n_tok, float* ou
   return moe_forward(L, x, n_tok, out, idx_out, w_out, nullptr, hw_threads());
 }
 
+void orc_rope(const float* x, const float* cs, const float* sn, int n_tok, int heads, int hd, int rot, float* y) {
+  const int half = rot / 2;
+  std::memcpy(y, x, sizeof(float) * (size_t)n_tok * heads * hd);
+  for (int t = 0; t < n_tok; ++t)
+    for (int h = 0; h < heads; ++h) rope_apply(&y[((size_t)t * heads + h) * hd], rot, &cs[(size_t)t * half], &sn[(size_t)t * half]);
+}
+
+// layer.rs:511-749 for one decode token, outside a model: the same steps as attention() above
+int orc_attn_decode(const orc_attn_layer* L, float* K, float* V, int pos, float* h) {
+  const int H = L->hidden, nh = L->heads, nkv = L->kv_heads, hd = L->head_dim, Dq = nh * hd, Dkv = nkv * hd;
+  const int th = hw_threads();
+  std::vector<float> xn(H), q(Dq), k(Dkv), v(Dkv), attn(Dq), o(H);
+  rms_norm(h, L->attn_norm, xn.data(), 1, H, L->eps);
+  auto proj = [&](const uint8_t* w, int rows, int cols, const float* x, float* y) {
+    if (L->attn_mode == 1) { q8_0_gemv_actq(w, rows, cols, x, y, th); return; }
+    std::vector<float> Wf((size_t)rows * cols);
+    dequant_matrix(ORC_Q8_0, w, rows, cols, Wf.data(), th);
+    matmul_xwt(x, 1, Wf.data(), rows, cols, y, th);
+  };
+  proj(L->wq, Dq, H, xn.data(), q.data()); proj(L->wk, Dkv, H, xn.data(), k.data()); proj(L->wv, Dkv, H, xn.data(), v.data());
+  if (L->bq) for (int i = 0; i < Dq; ++i) q[i] += L->bq[i];
+  if (L->bk) for (int i = 0; i < Dkv; ++i) k[i] += L->bk[i];
+  if (L->bv) for (int i = 0; i < Dkv; ++i) v[i] += L->bv[i];
+  if (L->q_norm && L->k_norm) {
+    std::vector<float> tmp(hd);
+    for (int i = 0; i < nh; ++i) { rms_norm(&q[(size_t)i * hd], L->q_norm, tmp.data(), 1, hd, L->eps); std::memcpy(&q[(size_t)i * hd], tmp.data(), hd * 4); }
+    for (int i = 0; i < nkv; ++i) { rms_norm(&k[(size_t)i * hd], L->k_norm, tmp.data(), 1, hd, L->eps); std::memcpy(&k[(size_t)i * hd], tmp.data(), hd * 4); }
+  }
+  const int half = L->rot_dim / 2;
+  std::vector<float> cs((size_t)(pos + 1) * half), sn(cs.size());
+  rope_tables(L->rot_dim, pos + 1, (double)L->rope_theta, cs.data(), sn.data());
+  for (int i = 0; i < nh; ++i) rope_apply(&q[(size_t)i * hd], L->rot_dim, &cs[(size_t)pos * half], &sn[(size_t)pos * half]);
+  for (int i = 0; i < nkv; ++i) rope_apply(&k[(size_t)i * hd], L->rot_dim, &cs[(size_t)pos * half], &sn[(size_t)pos * half]);
+  const int Lk = pos + 1;   // caches hold [nkv][Lk][hd]; rows < pos were written by earlier calls
+  for (int i = 0; i < nkv; ++i) {
+    std::memcpy(&K[((size_t)i * Lk + pos) * hd], &k[(size_t)i * hd], hd * 4);
+    std::memcpy(&V[((size_t)i * Lk + pos) * hd], &v[(size_t)i * hd], hd * 4);
+  }
+  const float scale = (float)(1.0 / std::sqrt((double)hd));
+  sdpa(q.data(), K, V, nh, nkv, 1, Lk, hd, scale, false, L->sinks, L->window, attn.data(), th);
+  proj(L->wo, H, Dq, attn.data(), o.data());
+  for (int i = 0; i < H; ++i) h[i] = h[i] + (L->bo ? o[i] + L->bo[i] : o[i]);
+  return 0;
+}
+
 orc_model* orc_model_open(const char* path, int max_seq_len, char* err, int err_len) {
   auto* m = new orc_model();
   std::string e;
@@ -771,6 +821,11 @@ void orc_model_last_routing(const orc_model* m, int32_t* idx, float* w) {
   std::memcpy(idx, m->last_idx.data(), m->last_idx.size() * 4); std::memcpy(w, m->last_w.data(), m->last_w.size() * 4);
 }
 
+void orc_model_layer_trace(const orc_model* m, float* hidden, float* logits) {
+  if (hidden) std::memcpy(hidden, m->layer_hidden.data(), m->layer_hidden.size() * 4);
+  if (logits) std::memcpy(logits, m->layer_logits.data(), m->layer_logits.size() * 4);
+}
+
 // engine.rs:1963-1987: final RMSNorm + LM head (f16 weights converted exactly to f32)
 static void lm_head(orc_model* m, const float* hidden, float* logits) {
   const int H = m->hidden;
@@ -803,6 +858,8 @@ int orc_model_forward(orc_model* m, const int32_t* tokens, int n, float* logits)
     dequant(m->embd->qtype, m->embd->data + (int64_t)tokens[t] * erb, H, &h[(size_t)t * H]);
   }
   m->last_idx.assign((size_t)m->layers * K, 0); m->last_w.assign((size_t)m->layers * K, 0.0f);
+  const int E = m->experts;
+  m->layer_hidden.assign((size_t)m->layers * H, 0.0f); m->layer_logits.assign((size_t)m->layers * E, 0.0f);
   std::vector<int32_t> idx((size_t)n * K); std::vector<float> w((size_t)n * K);
   for (int li = 0; li < m->layers; ++li) {  // layer.rs:393-503
     auto& Ly = m->L[li];
@@ -810,8 +867,10 @@ int orc_model_forward(orc_model* m, const int32_t* tokens, int n, float* logits)
     attention(m, Ly, li, xn.data(), n, tmp.data());
     for (size_t i = 0; i < h.size(); ++i) h[i] = h[i] + tmp[i];
     rms_norm(h.data(), Ly.post_norm, xn.data(), n, H, m->eps);
-    moe_forward(&Ly.moe, xn.data(), n, tmp.data(), idx.data(), w.data(), &Ly.dummies, th);
+    moe_forward(&Ly.moe, xn.data(), n, tmp.data(), idx.data(), w.data(), &Ly.dummies, th, 0, 1 << 30,
+                &m->layer_logits[(size_t)li * E]);
     for (size_t i = 0; i < h.size(); ++i) h[i] = h[i] + tmp[i];
+    std::memcpy(&m->layer_hidden[(size_t)li * H], &h[(size_t)(n - 1) * H], (size_t)H * 4);
     std::memcpy(&m->last_idx[(size_t)li * K], &idx[(size_t)(n - 1) * K], K * 4);
     std::memcpy(&m->last_w[(size_t)li * K], &w[(size_t)(n - 1) * K], K * 4);
   }

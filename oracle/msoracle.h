@@ -49,6 +49,8 @@ void orc_silu_and_mul(const float* g, const float* u, float* out, int64_t n);
 /* ops/attention.rs:178-280; q [seq_q][nh][hd], k/v [nkv][seq_k][hd], out [seq_q][nh][hd] */
 void orc_sdpa(const float* q, const float* k, const float* v, int nh, int nkv, int seq_q, int seq_k, int hd,
               double scale, int causal, const float* sinks, int sliding_window, float* out);
+/* RoPE of x [n_tok][heads][hd] with per-token tables cos/sin [n_tok][rot/2] (ops/attention.rs:96-164) */
+void orc_rope(const float* x, const float* cos_t, const float* sin_t, int n_tok, int heads, int hd, int rot, float* y);
 /* layer.rs:2346-2403; returns indices/weights [n_tok, k] */
 void orc_top_k_routing(const float* logits, int n_tok, int n_exp, int k, int normalize, int softmax_weight,
                        int32_t* idx, float* w);
@@ -70,6 +72,20 @@ int orc_moe_forward(const orc_moe_layer* L, const float* x, int n_tok, float* ou
 
 /* the same layer restricted to experts [e_begin, e_end) (routing over all experts) */
 int orc_moe_forward_range(const orc_moe_layer* L, const float* x, int n_tok, float* out, int e_begin, int e_end);
+
+/* ---- one attention half-layer for one decode token (layer.rs:511-749) ----
+ * h += O(SDPA(RoPE(QKV(RMSNorm(h))))).  K, V: [kv_heads][pos+1][head_dim] f32 (the caller grows
+ * them; rows < pos hold earlier tokens, row pos is written here).  Q8_0 projections. */
+typedef struct {
+  int hidden, heads, kv_heads, head_dim, rot_dim;
+  float eps, rope_theta;
+  int window;                        /* > 0: sliding window */
+  int attn_mode;                     /* 1 = candle QMatMul (activation quantized), 0 = exact f32 */
+  const float* attn_norm;
+  const uint8_t *wq, *wk, *wv, *wo;  /* Q8_0 */
+  const float *bq, *bk, *bv, *bo, *sinks, *q_norm, *k_norm;   /* or NULL */
+} orc_attn_layer;
+int orc_attn_decode(const orc_attn_layer* L, float* K, float* V, int pos, float* h);
 
 /* ---- Gated DeltaNet decode step (model/deltanet.rs:204-543) ---- */
 typedef struct {
@@ -110,6 +126,9 @@ void orc_model_clear_cache(orc_model* m);
 void orc_model_last_hidden(const orc_model* m, float* out);
 /* routed experts of the last position per layer [layers*k] */
 void orc_model_last_routing(const orc_model* m, int32_t* idx, float* w);
+/* last forward, last position, every layer: residual stream after the layer [layers][hidden] and
+ * router logits after bias and dummy mask [layers][n_experts]; either pointer may be NULL */
+void orc_model_layer_trace(const orc_model* m, float* hidden, float* logits);
 /* final norm + LM head of one hidden vector [hidden] -> logits [vocab] (timing / tests) */
 void orc_model_lm_head(orc_model* m, const float* hidden, float* logits);
 void orc_model_destroy(orc_model* m);

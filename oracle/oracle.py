@@ -32,6 +32,14 @@ class MoeLayer(C.Structure):
                 ("oai_swiglu", C.c_int), ("norm_topk_prob", C.c_int)]
 
 
+class AttnLayer(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int), ("head_dim", C.c_int),
+                ("rot_dim", C.c_int), ("eps", C.c_float), ("rope_theta", C.c_float), ("window", C.c_int),
+                ("attn_mode", C.c_int), ("attn_norm", _fp), ("wq", _vp), ("wk", _vp), ("wv", _vp), ("wo", _vp),
+                ("bq", _fp), ("bk", _fp), ("bv", _fp), ("bo", _fp), ("sinks", _fp), ("q_norm", _fp),
+                ("k_norm", _fp)]
+
+
 class DeltaNetLayer(C.Structure):
     _fields_ = [("hidden", C.c_int), ("n_k_heads", C.c_int), ("head_k_dim", C.c_int), ("n_v_heads", C.c_int),
                 ("head_v_dim", C.c_int), ("conv_kernel", C.c_int), ("eps", C.c_float),
@@ -67,6 +75,8 @@ def lib():
         L.orc_top_k_routing.argtypes = [_fp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _i32p, _fp]
         L.orc_moe_forward.argtypes = [C.POINTER(MoeLayer), _fp, C.c_int, _fp, _i32p, _fp]
         L.orc_moe_forward_range.argtypes = [C.POINTER(MoeLayer), _fp, C.c_int, _fp, C.c_int, C.c_int]
+        L.orc_rope.argtypes = [_fp, _fp, _fp, C.c_int, C.c_int, C.c_int, C.c_int, _fp]
+        L.orc_attn_decode.argtypes = [C.POINTER(AttnLayer), _fp, _fp, C.c_int, _fp]
         L.orc_deltanet_step.argtypes = [C.POINTER(DeltaNetLayer), _fp, _fp, _fp, _fp]
         L.orc_shared_expert.argtypes = [C.c_int, _vp, _vp, C.c_int, _vp, _fp, C.c_int, C.c_int, _fp, _fp]
         L.orc_model_open.restype = _vp
@@ -81,6 +91,7 @@ def lib():
         L.orc_model_clear_cache.argtypes = [_vp]
         L.orc_model_last_hidden.argtypes = [_vp, _fp]
         L.orc_model_last_routing.argtypes = [_vp, _i32p, _fp]
+        L.orc_model_layer_trace.argtypes = [_vp, _fp, _fp]
         L.orc_model_lm_head.argtypes = [_vp, _fp, _fp]
         L.orc_model_destroy.argtypes = [_vp]
         _lib = L
@@ -207,6 +218,46 @@ def moe_forward(layer: dict, x: np.ndarray, expert_range=None):
     return out, idx, w
 
 
+def rope(x, cos, sin, n_tok, heads, hd, rot):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().orc_rope(_f(x), _f(np.ascontiguousarray(cos, np.float32)), _f(np.ascontiguousarray(sin, np.float32)),
+                   n_tok, heads, hd, rot, _f(y))
+    return y
+
+
+class AttnState:
+    """One attention half-layer with its f32 K/V history (layer.rs:511-749), stepped a token at a time."""
+
+    def __init__(self, d: dict, attn_mode: int = 1):
+        self.keep = []
+
+        def ptr(a, fp=False):
+            if a is None:
+                return _fp() if fp else None
+            a = np.ascontiguousarray(a)
+            self.keep.append(a)
+            return a.ctypes.data_as(_fp) if fp else a.ctypes.data
+        self.d = d
+        self.L = AttnLayer(d["hidden"], d["heads"], d["kv_heads"], d["head_dim"], d["rot_dim"], d["eps"],
+                           d["rope_theta"], d.get("window", 0), attn_mode, ptr(d["attn_norm"], True),
+                           ptr(d["wq"]), ptr(d["wk"]), ptr(d["wv"]), ptr(d["wo"]), ptr(d.get("bq"), True),
+                           ptr(d.get("bk"), True), ptr(d.get("bv"), True), ptr(d.get("bo"), True),
+                           ptr(d.get("sinks"), True), ptr(d.get("q_norm"), True), ptr(d.get("k_norm"), True))
+        self.K = np.zeros((d["kv_heads"], 0, d["head_dim"]), np.float32)
+        self.V = np.zeros_like(self.K)
+
+    def step(self, h: np.ndarray) -> np.ndarray:
+        pos = self.K.shape[1]
+        z = np.zeros((self.K.shape[0], 1, self.K.shape[2]), np.float32)
+        K = np.ascontiguousarray(np.concatenate([self.K, z], 1))
+        V = np.ascontiguousarray(np.concatenate([self.V, z], 1))
+        out = np.ascontiguousarray(h, dtype=np.float32).copy()
+        lib().orc_attn_decode(C.byref(self.L), _f(K), _f(V), pos, _f(out))
+        self.K, self.V = K, V
+        return out
+
+
 def deltanet_layer(d: dict, keep: list) -> DeltaNetLayer:
     """ctypes view of a DeltaNet layer dict (numpy arrays + ints); keep holds the buffers alive"""
     def ptr(a, fp=False):
@@ -275,6 +326,20 @@ class Model:
         o = np.empty(self.hidden, dtype=np.float32)
         lib().orc_model_last_hidden(self.h, _f(o))
         return o
+
+    def last_routing(self, layers: int, k: int):
+        """routed experts and weights of the last position, [layers, k] each"""
+        idx = np.empty(layers * k, np.int32)
+        w = np.empty(layers * k, np.float32)
+        lib().orc_model_last_routing(self.h, _i(idx), _f(w))
+        return idx.reshape(layers, k), w.reshape(layers, k)
+
+    def layer_trace(self, layers: int, experts: int):
+        """(hidden after each layer [layers, H], router logits per layer [layers, E]), last position"""
+        hid = np.empty(layers * self.hidden, np.float32)
+        lg = np.empty(layers * experts, np.float32)
+        lib().orc_model_layer_trace(self.h, _f(hid), _f(lg))
+        return hid.reshape(layers, self.hidden), lg.reshape(layers, experts)
 
     def lm_head(self, hidden: np.ndarray) -> np.ndarray:
         hidden = np.ascontiguousarray(hidden, dtype=np.float32)

@@ -588,3 +588,79 @@ def test_batch_decode_gqa8_attention(ctx, orc, tmp_path, head_dim):
             assert int(bl[b].argmax()) == int(want.argmax()) == int(single.argmax()), b
     om.close()
     eng.close()
+
+
+# ---- the per-dispatch seam: RoPE (fused_rope_metal) and one attention half-layer ----
+
+
+@pytest.mark.parametrize("heads,hd,rot,n_tok", [(64, 64, 64, 1), (8, 128, 128, 5), (16, 256, 64, 3)])
+def test_rope_bit_exact(ctx, orc, heads, hd, rot, n_tok):
+    """NeoX rotation of the first rot dims (partial rotary passes the rest through), bit for bit"""
+    rng = np.random.default_rng(heads + hd + rot)
+    cs, sn = orc.rope_tables(rot, 4096, 150000.0)
+    pos = rng.integers(0, 4096, n_tok)
+    x = rng.standard_normal((n_tok, heads, hd)).astype(np.float32) * 3
+    y = torch.empty(x.size, dtype=torch.float32, device="cuda")
+    ctx.rope(dev(x), dev(cs[pos]), dev(sn[pos]), n_tok, heads, hd, rot, y)
+    ctx.sync()
+    want = orc.rope(x, cs[pos], sn[pos], n_tok, heads, hd, rot)
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), want.reshape(-1).view(np.uint32))
+
+
+def _attn_layer(seed, H, nh, nkv, hd, rot, window=0, sinks=False, bias=False, qk_norm=False, theta=150000.0):
+    rng = np.random.default_rng(seed)
+    Dq, Dkv = nh * hd, nkv * hd
+    d = dict(hidden=H, heads=nh, kv_heads=nkv, head_dim=hd, rot_dim=rot, eps=1e-5, rope_theta=theta, window=window,
+             attn_norm=(1 + 0.1 * rng.standard_normal(H)).astype(np.float32),
+             wq=synth.rand_q8_0(rng, Dq * H), wk=synth.rand_q8_0(rng, Dkv * H), wv=synth.rand_q8_0(rng, Dkv * H),
+             wo=synth.rand_q8_0(rng, H * Dq))
+    if bias:
+        for k, n in (("bq", Dq), ("bk", Dkv), ("bv", Dkv), ("bo", H)):
+            d[k] = (rng.standard_normal(n) * 0.01).astype(np.float32)
+    if sinks:
+        d["sinks"] = rng.standard_normal(nh).astype(np.float32)
+    if qk_norm:
+        d["q_norm"] = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+        d["k_norm"] = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    return d
+
+
+@pytest.mark.parametrize("shape", [
+    dict(H=2880, nh=64, nkv=8, hd=64, rot=64, window=128, sinks=True, bias=True, steps=150),    # GPT-OSS SWA layer
+    dict(H=2880, nh=64, nkv=8, hd=64, rot=64, sinks=True, bias=True, steps=40),                 # GPT-OSS full layer
+    dict(H=2048, nh=32, nkv=4, hd=128, rot=128, qk_norm=True, theta=1e6, steps=40),            # Qwen3-30B-A3B
+    dict(H=2048, nh=16, nkv=2, hd=256, rot=64, qk_norm=True, theta=1e7, steps=24),             # head_dim 256, rotary 0.25
+], ids=["gpt-oss-swa", "gpt-oss-full", "qwen3", "hd256-partial-rope"])
+def test_attn_layer_decode(ctx, orc, shape):
+    """ms_attn_layer_decode step by step against the oracle's attention half-layer: the residual
+    increment of every step within 1e-3 (fresh input each step; both keep their own K/V)"""
+    shape = dict(shape)
+    steps = shape.pop("steps")
+    theta = shape.pop("theta", 150000.0)
+    d = _attn_layer(17, theta=theta, **shape)
+    H, nkv, hd, window = d["hidden"], d["kv_heads"], d["head_dim"], d["window"]
+    cap = window if window else steps
+    cs, sn = orc.rope_tables(d["rot_dim"], steps, theta)
+    ostate = orc.AttnState(d)
+    wqkv = np.concatenate([d["wq"], d["wk"], d["wv"]])
+    bqkv = np.concatenate([d["bq"], d["bk"], d["bv"]]) if "bq" in d else None
+    kc = torch.zeros(nkv * cap * hd, device="cuda")
+    vc = torch.zeros_like(kc)
+    g = dict(hidden=H, heads=d["heads"], kv_heads=nkv, head_dim=hd, rot_dim=d["rot_dim"], eps=d["eps"], window=window,
+             cap=cap, attn_norm=dev(d["attn_norm"]), wqkv=dev(pad_rows(wqkv)), wo=dev(pad_rows(d["wo"])),
+             bqkv=dev(bqkv) if bqkv is not None else None, bo=dev(d["bo"]) if "bo" in d else None,
+             sinks=dev(d["sinks"]) if "sinks" in d else None, q_norm=dev(d["q_norm"]) if "q_norm" in d else None,
+             k_norm=dev(d["k_norm"]) if "k_norm" in d else None, k_cache=kc, v_cache=vc, cos_t=dev(cs), sin_t=dev(sn))
+    rng = np.random.default_rng(5)
+    worst = 0.0
+    for pos in range(steps):
+        h = rng.standard_normal(H).astype(np.float32)
+        want = ostate.step(h) - h
+        hd_ = dev(h)
+        ctx.attn_layer_decode(g, pos, hd_)
+        ctx.sync()
+        e = rel_err(hd_.cpu().numpy() - h, want)
+        worst = max(worst, e)
+        assert e < REL_TOL, f"position {pos}: {e:.3g}"
+    assert ctx.error_flags() == 0
+    print(f"worst step error {worst:.3g}")

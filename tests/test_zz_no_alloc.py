@@ -75,3 +75,29 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(setup):
         ctx.moe_mxfp4_decode_noalloc(W["gate"], W["up"], W["down"], None, None, None, 8192, 2880, 32, 4, 0,
                                      x, idx, wts, x)
     assert ei.value.status == 7 and "exceed the fixed scratch" in str(ei.value)
+
+
+def test_noalloc_at_its_size_limits(setup):
+    """top_k 16 with hidden = inter = 4096: the activation and partial slices fill the array"""
+    ctx, _, _ = setup
+    H = I = 4096
+    E, K = 16, 16
+    rng = np.random.default_rng(8)
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    pad = np.zeros(16 * 4352, np.uint8)
+    gate = d(np.concatenate([synth.rand_mxfp4(rng, E * I * H), pad]))
+    up = d(np.concatenate([synth.rand_mxfp4(rng, E * I * H), pad]))
+    down = d(np.concatenate([synth.rand_mxfp4(rng, E * H * I), pad]))
+    bias = [d((rng.standard_normal(E * n) * 0.01).astype(np.float32)) for n in (I, I, H)]
+    for call in range(2):
+        x = d(rng.standard_normal(H).astype(np.float32))
+        h0 = d(rng.standard_normal(H).astype(np.float32))
+        idx = d(rng.permutation(E)[:K].astype(np.int32))
+        wts = torch.softmax(torch.from_numpy(rng.standard_normal(K).astype(np.float32)), 0).cuda()
+        outs = []
+        for fn in (ctx.moe_mxfp4_decode, ctx.moe_mxfp4_decode_noalloc):
+            h = h0.clone()
+            fn(gate, up, down, bias[0], bias[1], bias[2], H, I, E, K, 0, x, idx, wts, h)
+            ctx.sync()
+            outs.append(h.cpu().numpy() - h0.cpu().numpy())
+        assert _rel(outs[1], outs[0]) < REL_TOL, f"call {call}"
