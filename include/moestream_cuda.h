@@ -20,7 +20,7 @@
 extern "C" {
 #endif
 
-#define MS_ABI_VERSION 1
+#define MS_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define MS_API __attribute__((visibility("default")))
@@ -195,11 +195,14 @@ MS_API ms_status ms_moe_mxfp4_decode_packed(ms_ctx* ctx, const void* gate_up_pac
  * model/layer.rs:1316-1349, 1848-1894): tokens sorted by expert, a grouped GEMM on the tensor cores
  * with the MXFP4 weights expanded exactly to bf16 in shared memory and bf16 activations, f32
  * accumulation; out[t] = sum over the token's experts (ascending id) of w * FFN(x[t]).
- * x [T, hidden], idx / wts [T, top_k], out [T, hidden], device pointers; packed experts as above. */
+ * x [T, hidden], idx / wts [T, top_k], out [T, hidden], device pointers; packed experts as above.
+ * precise = 1 carries each activation as a bf16 hi + lo pair (two MMAs per K step, ~2^-18 relative
+ * instead of bf16's 2^-9; about twice the tensor time). */
 MS_API ms_status ms_moe_mxfp4_prefill_packed(ms_ctx* ctx, const void* gate_up_packed, const void* down_packed,
                                              const float* gate_b, const float* up_b, const float* down_b, int hidden,
                                              int inter, int n_experts, int top_k, int arch, const float* x,
-                                             int n_tokens, const int32_t* idx, const float* wts, float* out);
+                                             int n_tokens, const int32_t* idx, const float* wts, float* out,
+                                             int precise);
 
 /* ---- lockstep batch: B sequences at one shared position (Engine::forward over input_ids
  *      [B, T], engine.rs:1869-2006, KV rows per batch entry kv_cache.rs:37-60) ----
@@ -295,6 +298,26 @@ MS_API ms_status ms_model_destroy(ms_model* m);
 /* Run n tokens through the model at the current position (engine.rs:1869-2006); writes the
  * last position's logits [vocab] to host memory when logits != NULL. */
 MS_API ms_status ms_model_forward(ms_model* m, const int32_t* tokens, int n_tokens, float* logits);
+/* Decode numerics.  1 (default): every dot product and sum of the decode step (projections,
+ * attention scores, softmax denominators, P*V, router, expert GEMVs, RMSNorm, LM head) is
+ * accumulated in double and rounded to f32 once, and exp is the double exp rounded to f32; each
+ * op's result is then its exact value correctly rounded, whatever the summation order, so greedy
+ * tokens, routed experts and the Q8_0 activation codes are reproducible bit for bit against a CPU
+ * evaluation of the reference's ops (engine.rs:1869-2118) that rounds the same way.  0: the
+ * pipelined f32 kernels (tensor-core experts, split-K attention), results within ~1e-6 relative
+ * of 1 per op but not bit-identical.  MXFP4 experts and head dims 32/64/128 have order-independent
+ * kernels; K-quant experts use the pipelined kernels in both modes. */
+MS_API ms_status ms_model_set_exact(ms_model* m, int enable);
+/* How ms_model_forward runs more than one token (a prompt).  1 (default): batched passes of up to
+ * 2048 tokens -- Q8_0 projections of all tokens, QK-norm + RoPE at absolute positions, causal
+ * attention with the sliding-window mask and sinks over the cache and the chunk, the router of
+ * every token, and the experts as a grouped GEMM on the tensor cores (MXFP4 experts exact in bf16,
+ * activations as bf16 hi + lo pairs, f32 accumulation: ~2^-18 relative); K-quant experts in groups
+ * of 32 tokens.  2: the same with plain bf16 activations (fastest; ~1e-2 relative).  0: one decode
+ * step per token.  Replaces the reference's multi-token forward (engine.rs:1869-2006;
+ * layer.rs:1316-1349, 1848-1894; ops/attention.rs:210-244).  Expert-parallel models exchanging over
+ * peer mailboxes fall back to mode 0; with NCCL the experts' output is all-reduced per layer. */
+MS_API ms_status ms_model_set_prefill(ms_model* m, int mode);
 /* One decode step with host buffers: token in, greedy next token out (argmax, lowest id on ties). */
 MS_API ms_status ms_model_decode_step(ms_model* m, int32_t token, int32_t* next_token);
 /* Greedy generation (engine.rs:2011-2118): clears the cache, prefill, max_new tokens out. */

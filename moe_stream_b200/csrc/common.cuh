@@ -163,7 +163,7 @@ __device__ __forceinline__ void combine_order(const PendingCombine& pc, CombineO
                                               const float* wv = nullptr) {
   if (!ids) { ids = pc.idx; wv = pc.wts; }
   int n = 0;
-  if (pc.partial || pc.seg_part) {
+  if (pc.partial || pc.seg_part || pc.dpart) {
     for (int k = 0; k < pc.K; ++k) {
       const int e = ids[k] - pc.expert_base;
       if (e < 0 || e >= pc.n_local) continue;
@@ -193,6 +193,17 @@ __device__ __forceinline__ float combine_at(const PendingCombine& pc, const Comb
     return acc;
   }
   float acc = 0.f;
+  if (pc.dpart) {   // ascending expert id: y = (segments summed in f64, rounded) + bias; out += y * w
+    for (int q = 0; q < co.n; ++q) {
+      const double* dp = pc.dpart + (size_t)co.slot[q] * pc.n_dseg * pc.dpad + r;
+      double t = 0.0;
+      for (int s2 = 0; s2 < pc.n_dseg; ++s2) t += __ldcg(dp + (size_t)s2 * pc.dpad);
+      float y = (float)t;
+      if (pc.down_b) y = __fadd_rn(y, pc.down_b[(size_t)(pc.idx[co.slot[q]] - pc.expert_base) * H + r]);
+      acc = __fadd_rn(acc, __fmul_rn(y, co.w[q]));
+    }
+    return acc;
+  }
   if (pc.seg_part) {
     const int t = r >> 7, ns = tc_splits(co.n * pc.seg_tiles, pc.seg_kw, pc.seg_grid);
     const size_t off = (size_t)t * kTcMaxSeg * 128 + (r & 127), qstride = (size_t)pc.seg_tiles * kTcMaxSeg * 128;
@@ -217,7 +228,8 @@ __device__ __forceinline__ float combine_at(const PendingCombine& pc, const Comb
     }
     return acc;
   }
-  for (int q = 0; q < co.n; ++q) acc += pc.partial[(size_t)co.slot[q] * H + r] * co.w[q];
+  // ascending expert id, each product rounded before the sum (out += y * w, layer.rs:1845-1847)
+  for (int q = 0; q < co.n; ++q) acc = __fadd_rn(acc, __fmul_rn(pc.partial[(size_t)co.slot[q] * H + r], co.w[q]));
   return acc;
 }
 
@@ -243,25 +255,59 @@ __device__ __forceinline__ void quantize_q8_block(const float (&v)[32], int8_t* 
   *d_out = __half2float(__float2half_rn(d));
 }
 
+// ---- order-independent f32 results ----
+// Every reduction that produces an f32 value (dot products, sums, the RMSNorm mean) is taken in
+// double and rounded once, and exp is the double exp rounded to f32: the f32 result is then the
+// exact value correctly rounded (except when it lies within ~1e-16 relative of a rounding midpoint),
+// whatever the summation order.  The CPU oracle evaluates the reference's ops the same way, so both
+// produce the same bits -- including the Q8_0 codes and routing decisions that follow them.
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float expcr(float x) { return (float)exp((double)x); }
+
+// inverse RMS with the reference's op sequence (ops/norm.rs:16-37): x.sqr() in f32, mean_keepdim =
+// (sum rounded to f32) * f32(1/n) (candle's affine), + eps, sqrt, recip.  Threads tid in [0, nthr)
+// (nthr a multiple of 32) take part; bar() synchronises them; every one gets the result.
+template <class Bar>
+__device__ __forceinline__ float rms_inv_cr(const float* x, int n, float eps, int tid, int nthr, Bar bar) {
+  __shared__ double s_rms_red[33];
+  double ss = 0.0;
+  for (int i = tid; i < n; i += nthr) ss += (double)__fmul_rn(x[i], x[i]);
+  ss = warp_sum_d(ss);
+  if ((tid & 31) == 0) s_rms_red[tid >> 5] = ss;
+  bar();
+  double t = 0.0;
+  for (int w = 0; w < (nthr >> 5); ++w) t += s_rms_red[w];
+  bar();   // s_rms_red may be reused
+  const float var = __fadd_rn(__fmul_rn((float)t, (float)(1.0 / (double)n)), 0.0f);
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+}
+
+// the same for one vector held by one warp (per-head QK-norm)
+__device__ __forceinline__ float rms_inv_cr_warp(const float* x, int n, float eps, int lane) {
+  double ss = 0.0;
+  for (int i = lane; i < n; i += 32) ss += (double)__fmul_rn(x[i], x[i]);
+  ss = warp_sum_d(ss);
+  const float var = __fadd_rn(__fmul_rn((float)ss, (float)(1.0 / (double)n)), 0.0f);
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+}
+
 // Whole-CTA RMSNorm (weights w) of xs[0..H) in shared memory, then Q8_0 quantization into
-// xq / xd (one thread per 32-element block).  red: >= 32 floats of shared scratch.
+// xq / xd (one thread per 32-element block).  red: >= 256 floats of shared scratch.
 __device__ __forceinline__ void cta_rmsnorm_q8(const float* xs, int H, const float* w, float eps, int8_t* xq,
                                                float* xd, float* red) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) ss += xs[i] * xs[i];
-  ss = warp_sum(ss);
-  if (lane == 0) red[warp] = ss;
-  __syncthreads();
-  float t = 0.f;
-  for (int k = 0; k < nw; ++k) t += red[k];
-  const float inv = 1.0f / sqrtf(t / (float)H + eps);
+  (void)red;
+  const int lane = threadIdx.x & 31;
+  const float inv = rms_inv_cr(xs, H, eps, threadIdx.x, blockDim.x, [] { __syncthreads(); });
   for (int b = threadIdx.x; b < H / 32; b += blockDim.x) {
     float v[32];
 #pragma unroll
     for (int k = 0; k < 32; ++k) {
       const int kk = (k + lane) & 31;   // rotate the start so lanes hit different banks
-      v[kk] = (xs[32 * b + kk] * inv) * w[32 * b + kk];
+      v[kk] = __fmul_rn(__fmul_rn(xs[32 * b + kk], inv), w[32 * b + kk]);
     }
     quantize_q8_block(v, xq + 32 * b, &xd[b]);
   }

@@ -61,8 +61,13 @@ struct PendingCombine {
   const uint32_t* ep_flags = nullptr;
   const uint32_t* ep_seq = nullptr;
   int ep_n = 0;
+  // or, from the order-independent expert kernels: f64 partial dots of each slot's down rows
+  // [K][n_dseg][dpad]; slot output = (sum over segments, rounded to f32) + down bias
+  const double* dpart = nullptr;
+  const float* down_b = nullptr;   // [n_local][H] or null
+  int n_dseg = 0, dpad = 0;
   __host__ __device__ bool active() const {
-    return dense != nullptr || partial != nullptr || seg_part != nullptr || ep_recv != nullptr;
+    return dense != nullptr || partial != nullptr || seg_part != nullptr || ep_recv != nullptr || dpart != nullptr;
   }
 };
 
@@ -213,9 +218,43 @@ struct PrefillArgs {
   float* out = nullptr;             // [T, H]: = MoE(x), or += when accumulate
   void* scratch = nullptr;          // pf_scratch_bytes(H, I, E, T, K) bytes
   int H = 0, I = 0, E = 0, K = 0, T = 0, expert_base = 0, oai_swiglu = 1, accumulate = 0;
+  int precise = 0;                  // 1: activations as bf16 hi + lo pairs (two MMAs per K step, ~2^-18 relative)
 };
-size_t pf_scratch_bytes(int H, int I, int E, int T, int K);
+size_t pf_scratch_bytes(int H, int I, int E, int T, int K, int precise = 0);
 cudaError_t launch_moe_prefill(const DevCtx& c, const PrefillArgs& a, cudaStream_t s);
+
+// ---- multi-token forward (prompt prefill), kernels_prefill_attn.cu ----
+// h[t] = embedding(tok[t]); xq/xd[t] = Q8_0(RMSNorm(h[t]) * norm_w)   (one CTA per token)
+cudaError_t launch_pf_embed(const DevCtx& c, const int* tok, int T, const void* table, int q, int H, int vocab,
+                            float* h, const float* norm_w, float eps, int8_t* xq, float* xd, cudaStream_t s);
+// xq/xd[t] = Q8_0(RMSNorm(h[t]) * norm_w)
+cudaError_t launch_pf_norm_q8(const float* h, int T, int H, const float* norm_w, float eps, int8_t* xq, float* xd,
+                              cudaStream_t s);
+// Q8_0 blocks of x[0..n) (n % 32 == 0)
+cudaError_t launch_pf_quant(const float* x, int64_t n, int8_t* xq, float* xd, cudaStream_t s);
+// h[i] += y[i]
+cudaError_t launch_pf_add(float* h, const float* y, int64_t n, cudaStream_t s);
+// QK-norm + RoPE of T tokens' projections, causal (sliding-window) attention with sinks over the
+// cache (positions < pos0) and the chunk, then the chunk's K/V appended to the cache
+struct PfAttnLaunch {
+  const float* qkv = nullptr;      // [T][nh*hd + 2*nkv*hd]
+  const float* q_norm = nullptr;   // [hd] or null (with k_norm)
+  const float* k_norm = nullptr;
+  float eps = 1e-6f;
+  const float* cos_t = nullptr;    // [max_seq][rot/2]
+  const float* sin_t = nullptr;
+  int rot = 0, pos0 = 0, T = 0, nh = 0, nkv = 0, hd = 0;
+  float* kc = nullptr;             // layer cache [nkv][cap][hd]
+  float* vc = nullptr;
+  int cap = 0, window = 0;
+  const float* sinks = nullptr;
+  float scale = 1.f;
+  float* q = nullptr;              // scratch [T][nh][hd]
+  float* kn = nullptr;             // scratch [T][nkv][hd]
+  float* vn = nullptr;             // scratch [T][nkv][hd]
+  float* out = nullptr;            // [T][nh*hd]
+};
+cudaError_t launch_pf_attention(const DevCtx& c, const PfAttnLaunch& L, cudaStream_t s);
 
 // ---- attention (decode, one token) ----
 struct AttnArgs {
@@ -252,6 +291,31 @@ cudaError_t launch_attention(const DevCtx& c, const AttnArgs& a, cudaStream_t s)
 int attn_splits(int range, int hd);   // splits of a decode-attention launch covering `range` positions
 // positions per split for `units` = kv_heads x sequences attending over `range` positions
 int attn_split_positions(int range, int units, int sm_count);
+
+// ---- order-independent decode kernels (kernels_exact.cu): f64 reductions rounded once ----
+// decode attention for one token per sequence (AttnArgs as launch_attention; oq / od written when
+// set); `range` = the most positions a sequence can attend to (cache slots, or the window)
+cudaError_t launch_exact_attention(const DevCtx& c, const AttnArgs& a, int range, cudaStream_t s);
+int exact_attn_cluster(int range);
+// the expert FFN of one token over packed MXFP4 tiles: f64 partial dots of gate/up rows per K
+// segment (gp), then the activations and f64 partial dots of the down rows (dp); the consumer
+// (PendingCombine.dpart) sums the down segments, adds the bias and combines in ascending expert id
+struct ExactMoeArgs {
+  const uint8_t* gu = nullptr;      // packed tiles, as TcMoeArgs
+  const uint8_t* down = nullptr;
+  const float* gate_b = nullptr;    // [E_local, I] or null
+  const float* up_b = nullptr;
+  const float* x = nullptr;         // [H] normed input
+  const int* idx = nullptr;         // [K]
+  int H = 0, I = 0, K = 0, expert_base = 0, n_local = 0, oai_swiglu = 1;
+  double* gp = nullptr;             // [K][n_seg_gu][2 I]
+  double* dp = nullptr;             // [K][n_seg_down][h_pad]
+  int n_seg_gu = 0, n_seg_down = 0, h_pad = 0;
+  int gu_tiles = 0, down_tiles = 0;           // filled by launch_exact_moe
+  int64_t gu_tile_bytes = 0, down_tile_bytes = 0;
+};
+int exact_seg_count(int kc);        // K segments over kc 32-element chunks
+cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a, cudaStream_t s);
 
 // ---- LM head / f16 GEMV ----
 // logits = W (RMSNorm(h)*norm_w if norm_w) (+bias); argmax (lowest index on ties) into *key.

@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(256) embed_batch_kernel(const BatchState* st, 
                                                           int H, int vocab, int B, float* h, int* log, uint32_t* err,
                                                           const float* norm_w, float eps, int8_t* xq, float* xd) {
   extern __shared__ float es[];   // [H]
-  __shared__ float red[32];
+  __shared__ float red[256];
   __shared__ int tok_s;
   const int b = blockIdx.x;
   pdl_wait_prior();
@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kQBWarps * 32, 3) q8_gemm_batch_kernel(Q8Batch
   // shared memory: weight tile [16][rb] (+16) | codes [B][kc + 16] | scales [B][kc / 32 + 4], one
   // kc-column slice of the activations at a time
   extern __shared__ __align__(16) uint8_t sm[];
-  __shared__ float red[kQBWarps][16][kMaxBatch + 1];
+  __shared__ double red[kQBWarps][16][kMaxBatch + 1];
   __shared__ __align__(8) uint64_t bar;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int tile = blockIdx.x;
@@ -125,9 +125,9 @@ __global__ void __launch_bounds__(kQBWarps * 32, 3) q8_gemm_batch_kernel(Q8Batch
   pdl_wait_prior();
   pdl_launch_dependents();
   bool ok = true;
-  float acc[kMaxBatch / 8][4];
+  double acc[kMaxBatch / 8][4];   // block terms (int32 dot x d_w x d_x) are exact in double
 #pragma unroll
-  for (int t = 0; t < kMaxBatch / 8; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+  for (int t = 0; t < kMaxBatch / 8; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0;
   for (int k0 = 0; k0 < a.cols; k0 += kc) {
     // the batch's activation codes and block scales for columns [k0, k0 + kc) (L2-resident)
     if (k0) __syncthreads();
@@ -194,10 +194,10 @@ __global__ void __launch_bounds__(kQBWarps * 32, 3) q8_gemm_batch_kernel(Q8Batch
           const int t0 = 8 * t + 2 * c;
           const float dx0 = t0 < B ? ds[t0 * ds_stride + bl] : 0.f;
           const float dx1 = t0 + 1 < B ? ds[(t0 + 1) * ds_stride + bl] : 0.f;
-          acc[t][0] = fmaf((float)d[0], dw0 * dx0, acc[t][0]);
-          acc[t][1] = fmaf((float)d[1], dw0 * dx1, acc[t][1]);
-          acc[t][2] = fmaf((float)d[2], dw1 * dx0, acc[t][2]);
-          acc[t][3] = fmaf((float)d[3], dw1 * dx1, acc[t][3]);
+          acc[t][0] += (double)d[0] * (double)dw0 * (double)dx0;
+          acc[t][1] += (double)d[1] * (double)dw0 * (double)dx1;
+          acc[t][2] += (double)d[2] * (double)dw1 * (double)dx0;
+          acc[t][3] += (double)d[3] * (double)dw1 * (double)dx1;
         }
       }
     }
@@ -215,13 +215,14 @@ __global__ void __launch_bounds__(kQBWarps * 32, 3) q8_gemm_batch_kernel(Q8Batch
   __syncthreads();
   for (int i = threadIdx.x; i < 16 * B; i += blockDim.x) {
     const int r = i % 16, tb = i / 16;
-    float v = 0.f;
+    double vd = 0.0;
 #pragma unroll
-    for (int w = 0; w < kQBWarps; ++w) v += red[w][r][tb];
+    for (int w = 0; w < kQBWarps; ++w) vd += red[w][r][tb];
     const int row = tile * 16 + r;
-    if (a.bias) v += a.bias[row];
+    float v = (float)vd;
+    if (a.bias) v = __fadd_rn(v, a.bias[row]);
     if (!ok) v = 0.f;
-    if (a.residual) a.residual[(size_t)tb * a.rows + row] += v;
+    if (a.residual) a.residual[(size_t)tb * a.rows + row] = __fadd_rn(a.residual[(size_t)tb * a.rows + row], v);
     else a.y[(size_t)tb * a.rows + row] = v;
   }
 }
@@ -233,7 +234,7 @@ __global__ void __launch_bounds__(256) resid_batch_kernel(BatchCombine bc, float
   __shared__ int s_ent[16];
   __shared__ float s_w[16];
   __shared__ int s_n;
-  __shared__ float red[32];
+  __shared__ float red[256];
   const int b = blockIdx.x;
   pdl_wait_prior();
   pdl_launch_dependents();
@@ -255,8 +256,8 @@ __global__ void __launch_bounds__(256) resid_batch_kernel(BatchCombine bc, float
   float* hb = h + (size_t)b * H;
   for (int r = threadIdx.x; r < H; r += blockDim.x) {
     float acc = 0.f;
-    for (int q = 0; q < n; ++q) acc += bc.y[(size_t)s_ent[q] * H + r] * s_w[q];
-    const float v = hb[r] + acc;
+    for (int q = 0; q < n; ++q) acc = __fadd_rn(acc, __fmul_rn(bc.y[(size_t)s_ent[q] * H + r], s_w[q]));
+    const float v = __fadd_rn(hb[r], acc);
     hb[r] = v;
     hs[r] = v;
   }
@@ -264,12 +265,9 @@ __global__ void __launch_bounds__(256) resid_batch_kernel(BatchCombine bc, float
   if (xq) {
     cta_rmsnorm_q8(hs, H, norm_w, eps, xq + (size_t)b * H, xd + (size_t)b * (H / 32), red);
   } else if (xf) {
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) ss += hs[i] * hs[i];
-    ss = cta_sum(ss, red);
-    const float inv = 1.0f / sqrtf(ss / (float)H + eps);
+    const float inv = rms_inv_cr(hs, H, eps, threadIdx.x, blockDim.x, [] { __syncthreads(); });
     for (int i = threadIdx.x; i < H; i += blockDim.x)
-      xf[(size_t)b * H + i] = norm_w ? (hs[i] * inv) * norm_w[i] : hs[i];
+      xf[(size_t)b * H + i] = norm_w ? __fmul_rn(__fmul_rn(hs[i], inv), norm_w[i]) : hs[i];
   }
 }
 

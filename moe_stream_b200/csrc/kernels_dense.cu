@@ -105,14 +105,10 @@ __global__ void dequant_kernel(int q, const uint8_t* __restrict__ src, int64_t n
 // ============================ RMSNorm ============================
 __global__ void rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ y,
                                 int dim, float eps) {
-  __shared__ float red[32];
   const float* xr = x + (size_t)blockIdx.x * dim;
   float* yr = y + (size_t)blockIdx.x * dim;
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) ss += xr[i] * xr[i];
-  ss = block_sum(ss, red);
-  const float inv = 1.0f / sqrtf(ss / (float)dim + eps);
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) yr[i] = (xr[i] * inv) * w[i];
+  const float inv = rms_inv_cr(xr, dim, eps, threadIdx.x, blockDim.x, [] { __syncthreads(); });
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
 }
 
 // ============================ Q8_0 projection ============================
@@ -149,7 +145,7 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
   float* xf = xd + ((p.cols / 32 + 3) & ~3);                                       // [cols]
   uint64_t* full = reinterpret_cast<uint64_t*>(xf + p.cols);
   uint64_t* empty = full + kQMaxStages;
-  __shared__ float red[32];
+  __shared__ float red[256];
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -202,16 +198,7 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
   const float* xds = p.xd_in;
   if (!xqs) {
     float inv = 1.f;
-    if (p.norm_w) {
-      float ss = 0.f;
-      for (int i = threadIdx.x; i < p.cols; i += nct) { const float v = p.x[i]; ss += v * v; }
-      ss = warp_sum(ss);
-      if (lane == 0) red[warp] = ss;
-      named_bar(1, nct);
-      float t = 0.f;
-      for (int w = 0; w < kQW; ++w) t += red[w];
-      inv = 1.0f / sqrtf(t / (float)p.cols + p.eps);
-    }
+    if (p.norm_w) inv = rms_inv_cr(p.x, p.cols, p.eps, threadIdx.x, nct, [nct] { named_bar(1, nct); });
     for (int b = threadIdx.x; b < nb; b += nct) {
       float v[32];
       const float4* x4 = reinterpret_cast<const float4*>(p.x + 32 * b);
@@ -225,8 +212,10 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float4 t = w4[k];
-          v[4 * k] = (v[4 * k] * inv) * t.x; v[4 * k + 1] = (v[4 * k + 1] * inv) * t.y;
-          v[4 * k + 2] = (v[4 * k + 2] * inv) * t.z; v[4 * k + 3] = (v[4 * k + 3] * inv) * t.w;
+          v[4 * k] = __fmul_rn(__fmul_rn(v[4 * k], inv), t.x);
+          v[4 * k + 1] = __fmul_rn(__fmul_rn(v[4 * k + 1], inv), t.y);
+          v[4 * k + 2] = __fmul_rn(__fmul_rn(v[4 * k + 2], inv), t.z);
+          v[4 * k + 3] = __fmul_rn(__fmul_rn(v[4 * k + 3], inv), t.w);
         }
       }
       quantize_q8_block(v, xq + 32 * b, &xd[b]);
@@ -258,7 +247,7 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
     const int nr = min(p.stage_rows, r_end - r0);
     const bool ok = mbar_wait(&full[s], (uint32_t)(n & 1), p.err, EF_TIMEOUT_FULL);
     if (!ok) { if (lane == 0) atomicExch(&abort_flag, 1); }
-    float acc = 0.f;
+    double acc = 0.0;   // block terms sum_i * d_w * d_x are exact in double
     if (ok && warp < nr) {
       const uint8_t* row = stages + (size_t)s * p.stage_bytes + (size_t)warp * p.rb;
       // block b = lane + 32 i starts at 34 b; 34 * 32 = 1088 is a multiple of 4, so the
@@ -278,17 +267,18 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
           int sumi = 0;
 #pragma unroll
           for (int k = 0; k < 8; ++k) sumi = __dp4a((int)__funnelshift_r(wd[k], wd[k + 1], sh), xr[i][k], sumi);
-          acc += (float)sumi * h2f_bits(dw) * xdr[i];
+          acc += (double)sumi * (double)h2f_bits(dw) * (double)xdr[i];
         }
       }
     }
     __syncwarp();
     if (ok && lane == 0) mbar_arrive(&empty[s]);
-    acc = warp_sum(acc);
+    acc = warp_sum_d(acc);
     if (ok && warp < nr && lane == 0) {
       const int r = r0 + warp;
-      const float v = acc + (p.bias ? p.bias[r] : 0.f);
-      if (p.residual) p.residual[r] = p.residual[r] + v;
+      float v = (float)acc;
+      if (p.bias) v = __fadd_rn(v, p.bias[r]);
+      if (p.residual) p.residual[r] = __fadd_rn(p.residual[r], v);
       else p.y[r] = v;
     }
     if (!ok) break;
@@ -344,12 +334,9 @@ __device__ __forceinline__ void rope_inplace(float* v, int rot, const float* c, 
 
 // per-head RMSNorm over hd by one warp (layer.rs:643-650)
 __device__ __forceinline__ void head_norm_warp(float* v, const float* w, int hd, float eps, int lane) {
-  float ss = 0.f;
-  for (int i = lane; i < hd; i += 32) ss += v[i] * v[i];
-  ss = warp_sum(ss);
-  const float inv = 1.0f / sqrtf(ss / (float)hd + eps);
+  const float inv = rms_inv_cr_warp(v, hd, eps, lane);
   __syncwarp();
-  for (int i = lane; i < hd; i += 32) v[i] = (v[i] * inv) * w[i];
+  for (int i = lane; i < hd; i += 32) v[i] = __fmul_rn(__fmul_rn(v[i], inv), w[i]);
   __syncwarp();
 }
 
@@ -928,18 +915,10 @@ __global__ void __launch_bounds__(kLWarps * 32, 1) lmhead_kernel(LmHeadArgs a) {
   }
   __syncthreads();
   float inv = 1.f;
-  if (a.norm_w) {
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < a.H; i += blockDim.x) ss += xs[i] * xs[i];
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
-    __syncthreads();
-    float t = 0.f;
-    for (int w = 0; w < kLWarps; ++w) t += red[w];
-    inv = 1.0f / sqrtf(t / (float)a.H + a.eps);
-  }
+  if (a.norm_w) inv = rms_inv_cr(xs, a.H, a.eps, threadIdx.x, blockDim.x, [] { __syncthreads(); });
   __syncthreads();
-  for (int i = threadIdx.x; i < a.H; i += blockDim.x) xs[i] = a.norm_w ? (xs[i] * inv) * a.norm_w[i] : xs[i];
+  for (int i = threadIdx.x; i < a.H; i += blockDim.x)
+    xs[i] = a.norm_w ? __fmul_rn(__fmul_rn(xs[i], inv), a.norm_w[i]) : xs[i];
   __syncthreads();
   const int nch = a.H / 8;
   float xr[NCH][8];
@@ -961,20 +940,21 @@ __global__ void __launch_bounds__(kLWarps * 32, 1) lmhead_kernel(LmHeadArgs a) {
       if (ch < nch) wv[i] = __ldcs(wr + ch);
       else wv[i] = make_uint4(0, 0, 0, 0);
     }
-    float acc = 0.f;
+    double acc = 0.0;   // f16 x f32 products are exact in double
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
       const uint32_t u[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[k]));
-        acc = fmaf(f.x, xr[i][2 * k], acc);
-        acc = fmaf(f.y, xr[i][2 * k + 1], acc);
+        acc = fma((double)f.x, (double)xr[i][2 * k], acc);
+        acc = fma((double)f.y, (double)xr[i][2 * k + 1], acc);
       }
     }
-    acc = warp_sum(acc);
+    acc = warp_sum_d(acc);
     if (lane == 0) {
-      float v = acc + (a.bias ? a.bias[r] : 0.f);
+      float v = (float)acc;
+      if (a.bias) v = __fadd_rn(v, a.bias[r]);
       if (a.logits) { if (a.accumulate) v += a.logits[r]; a.logits[r] = v; }
       if (v == v) { const unsigned long long k = argmax_key(v, r); best = k > best ? k : best; }
     }
@@ -1008,7 +988,7 @@ __global__ void __launch_bounds__(1024) embed_kernel(StepState* st, const void* 
                              uint32_t* err, const float* norm_w, float eps, int8_t* xq, float* xd) {
   extern __shared__ float es[];   // [H]
   __shared__ int tok_s;
-  __shared__ float red[32];
+  __shared__ float red[256];
   pdl_wait_prior();
   pdl_launch_dependents();   // the next kernel may start its own (weight) prefetch now
   if (threadIdx.x == 0) {
@@ -1053,7 +1033,7 @@ __global__ void __launch_bounds__(kResidRows) resid_norm_q8_kernel(PendingCombin
                                                                    float* xd, uint32_t* cnt, uint32_t* err) {
   extern __shared__ float hs[];   // [H] (last CTA)
   __shared__ CombineOrder co;
-  __shared__ float red[32];
+  __shared__ float red[256];
   __shared__ int s_idx[16];
   __shared__ float s_wts[16];
   __shared__ uint32_t last;

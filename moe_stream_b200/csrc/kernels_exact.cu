@@ -1,0 +1,464 @@
+// kernels_exact.cu — decode-step kernels whose f32 results do not depend on summation order.
+//
+// Every dot product and sum is accumulated in double (f32 x f32 and MXFP4 x f32 products are exact
+// in double) and rounded to f32 once; exp is the double exp rounded to f32.  The result of each
+// reference op is then its exact value correctly rounded, so these kernels and the CPU oracle (which
+// evaluates the reference ops the same way) agree bit for bit, and with them every downstream
+// discrete decision: the Q8_0 codes of the next projection's activation, the routed experts and the
+// greedy token.
+//
+//   exact_attn_kernel   decode attention (ops/attention.rs:178-280) for one token per sequence:
+//                       a thread-block cluster per (kv head, sequence) splits the positions; the
+//                       softmax needs the global max before any exp, so the CTAs exchange their
+//                       maxima, then their f64 denominator sums, then their f64 P*V partials
+//                       through distributed shared memory (three cluster barriers).
+//   exact_gu_kernel     expert gate/up rows of the selected experts (MXFP4 tensor-core tiles read
+//                       thread-per-row, coalesced 16-byte code loads) over a K segment -> f64
+//                       partial dots.
+//   exact_down_kernel   rebuilds its K segment of the activation from the gate/up partials
+//                       (bias, OAI SwiGLU or SiLU*up, model/layer.rs:1797-1845, ops/activation.rs)
+//                       and writes f64 partial dots of the down rows; the residual kernel sums the
+//                       segments, adds the bias and combines the experts in ascending id.
+#include <cooperative_groups.h>
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace cg = cooperative_groups;
+
+namespace ms {
+namespace {
+
+// ============================ attention ============================
+constexpr int kXThreads = 256;
+constexpr int kXWarps = kXThreads / 32;
+
+// Reduce-scatter of 32 per-lane partials v[0..32) over a warp: afterwards lane L holds the sum
+// over all lanes of v[L] (in v[0]).  Five halving rounds; double values.
+__device__ __forceinline__ double warp_reduce_scatter32(double (&v)[32], int lane) {
+#pragma unroll
+  for (int o = 16, n = 32; o >= 1; o >>= 1, n >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (i < n / 2) {
+        const double send = up ? v[i] : v[i + n / 2];
+        const double keep = up ? v[i + n / 2] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+    }
+  }
+  return v[0];
+}
+
+template <int HD, int REP>
+__global__ void __launch_bounds__(kXThreads) exact_attn_kernel(AttnArgs a, uint32_t* err, int max_per_cta) {
+  constexpr int DPL = HD / 32;
+  constexpr int G = 32 / REP;              // positions per group (REP <= 32)
+  extern __shared__ __align__(16) uint8_t xsm[];
+  cg::cluster_group cl = cg::this_cluster();
+  const int C = (int)cl.num_blocks(), rank = (int)cl.block_rank();
+  float* qs = reinterpret_cast<float*>(xsm);                 // [REP][HD] normed, rotated queries
+  float* kn = qs + REP * HD;                                  // [HD] new key
+  float* vn = kn + HD;                                        // [HD] new value
+  float* sc = vn + HD;                                        // [REP][max_per_cta] scores -> exp
+  double* cl_max = reinterpret_cast<double*>(sc + (size_t)REP * max_per_cta);   // [C][REP] (as double)
+  double* cl_sum = cl_max + 8 * REP;                          // [C][REP]
+  double* wred = cl_sum + 8 * REP;                            // [kXWarps][REP][HD] warp partials
+  double* cl_o = wred + (size_t)kXWarps * REP * HD;           // [C][REP][HD] (rank 0)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.y, b = blockIdx.z;
+  const float* qkv = a.qkv + (size_t)b * a.bs_qkv;
+  float* kc = a.kc + (size_t)b * a.bs_kv;
+  float* vc = a.vc + (size_t)b * a.bs_kv;
+  const int Dq = a.nh * HD, Dkv = a.nkv * HD;
+
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int pos = *a.pos;
+  const int lo = a.window > 0 ? max(0, pos - a.window + 1) : 0;
+  const int range = pos - lo + 1;
+  const int per = (range + C - 1) / C;
+  const int p0 = lo + rank * per, p1 = min(pos + 1, p0 + per);   // this CTA's positions [p0, p1)
+  if (per > max_per_cta) {
+    if (threadIdx.x == 0) atomicOr(err, EF_BAD_SHAPE);
+  }
+  // ---- queries, new key / value: QK-norm then RoPE at pos (layer.rs:643-664) ----
+  for (int i = threadIdx.x; i < REP * HD; i += kXThreads) qs[i] = qkv[(size_t)(g * REP) * HD + i];
+  for (int i = threadIdx.x; i < HD; i += kXThreads) {
+    kn[i] = qkv[Dq + (size_t)g * HD + i];
+    vn[i] = qkv[Dq + Dkv + (size_t)g * HD + i];
+  }
+  __syncthreads();
+  const int half = a.rot / 2;
+  const float* cs = a.cos_t + (size_t)pos * half;
+  const float* sn = a.sin_t + (size_t)pos * half;
+  for (int h = warp; h <= REP; h += kXWarps) {   // h == REP: the key
+    float* v = h < REP ? qs + h * HD : kn;
+    const float* nw = h < REP ? a.q_norm : a.k_norm;
+    if (nw) {
+      const float inv = rms_inv_cr_warp(v, HD, a.eps, lane);
+      __syncwarp();
+      for (int i = lane; i < HD; i += 32) v[i] = __fmul_rn(__fmul_rn(v[i], inv), nw[i]);
+      __syncwarp();
+    }
+    for (int i = lane; i < half; i += 32) {
+      const float x1 = v[i], x2 = v[i + half];
+      v[i] = __fsub_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x2, sn[i]));
+      v[i + half] = __fadd_rn(__fmul_rn(x2, cs[i]), __fmul_rn(x1, sn[i]));
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+  auto slot_of = [&](int p) { return a.window > 0 ? p % a.cap : p; };
+  // ---- scores: s = round(q . k) * scale (f64 dot), groups of G positions per warp ----
+  double qd[REP][DPL];
+#pragma unroll
+  for (int h = 0; h < REP; ++h)
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) qd[h][d] = (double)qs[h * HD + lane + 32 * d];
+  const int n_my = max(0, p1 - p0);
+  for (int gb = warp * G; gb < n_my; gb += kXWarps * G) {
+    double v[32];
+#pragma unroll
+    for (int u = 0; u < G; ++u) {
+      const int p = p0 + gb + u;
+      float kr[DPL];
+      if (gb + u < n_my) {
+        const float* krow = p == pos ? kn : kc + ((size_t)g * a.cap + slot_of(p)) * HD;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) kr[d] = krow[lane + 32 * d];
+      } else {
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) kr[d] = 0.f;
+      }
+#pragma unroll
+      for (int h = 0; h < REP; ++h) {
+        double t = 0.0;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) t = fma(qd[h][d], (double)kr[d], t);
+        v[u * REP + h] = t;
+      }
+    }
+    const double dot = warp_reduce_scatter32(v, lane);   // lane = u * REP + h
+    const int u = lane / REP, h = lane % REP;
+    if (gb + u < n_my) {
+      const float s = __fmul_rn((float)dot, a.scale);
+      sc[(size_t)h * max_per_cta + gb + u] = s;
+    }
+  }
+  __syncthreads();
+  // local maxima per head, then every CTA's maxima to every CTA of the cluster
+  for (int h = warp; h < REP; h += kXWarps) {
+    float m = -INFINITY;
+    for (int j = lane; j < n_my; j += 32) m = fmaxf(m, sc[(size_t)h * max_per_cta + j]);
+    m = warp_max(m);
+    if (lane < C) {
+      double* dst = cl.map_shared_rank(cl_max, lane);
+      dst[rank * REP + h] = (double)m;
+    }
+  }
+  cl.sync();
+  // ---- exp(s - m') with the sink-aware max, f64 partial denominators ----
+  __shared__ float s_mp[32];
+  __shared__ float s_den[32];
+  if (threadIdx.x < REP) {
+    const int h = threadIdx.x;
+    float m = -INFINITY;
+    for (int r = 0; r < C; ++r) m = fmaxf(m, (float)cl_max[r * REP + h]);
+    if (a.sinks) {
+      const float sk = a.sinks[g * REP + h];
+      m = __fmul_rn(__fadd_rn(__fadd_rn(m, sk), fabsf(__fsub_rn(m, sk))), 0.5f);
+    }
+    s_mp[h] = m;
+  }
+  __syncthreads();
+  for (int h = warp; h < REP; h += kXWarps) {
+    const float m = s_mp[h];
+    double t = 0.0;
+    for (int j = lane; j < n_my; j += 32) {
+      const float e = expcr(__fsub_rn(sc[(size_t)h * max_per_cta + j], m));
+      sc[(size_t)h * max_per_cta + j] = e;
+      t += (double)e;
+    }
+    t = warp_sum_d(t);
+    if (lane < C) {
+      double* dst = cl.map_shared_rank(cl_sum, lane);
+      dst[rank * REP + h] = t;
+    }
+  }
+  cl.sync();
+  if (threadIdx.x < REP) {
+    const int h = threadIdx.x;
+    double t = 0.0;
+    for (int r = 0; r < C; ++r) t += cl_sum[r * REP + h];
+    float den = (float)t;
+    if (a.sinks) den = __fadd_rn(den, expcr(__fsub_rn(a.sinks[g * REP + h], s_mp[h])));
+    s_den[h] = den;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < REP * n_my; i += kXThreads) {   // weights e / den (f32)
+    const int h = i / n_my, j = i % n_my;
+    sc[(size_t)h * max_per_cta + j] = __fdiv_rn(sc[(size_t)h * max_per_cta + j], s_den[h]);
+  }
+  __syncthreads();
+  // ---- P*V: weights p = e / den (f32), f64 accumulation over positions, lanes over dims ----
+  double o[REP][DPL];
+#pragma unroll
+  for (int h = 0; h < REP; ++h)
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) o[h][d] = 0.0;
+  for (int j = warp; j < n_my; j += kXWarps) {
+    const int p = p0 + j;
+    const float* vrow = p == pos ? vn : vc + ((size_t)g * a.cap + slot_of(p)) * HD;
+    float vr[DPL];
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) vr[d] = vrow[lane + 32 * d];
+#pragma unroll
+    for (int h = 0; h < REP; ++h) {
+      const float pw = sc[(size_t)h * max_per_cta + j];
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) o[h][d] = fma((double)pw, (double)vr[d], o[h][d]);
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < REP; ++h)
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) wred[((size_t)warp * REP + h) * HD + lane + 32 * d] = o[h][d];
+  __syncthreads();
+  {
+    double* dst0 = cl.map_shared_rank(cl_o, 0);
+    for (int i = threadIdx.x; i < REP * HD; i += kXThreads) {
+      double t = 0.0;
+#pragma unroll
+      for (int w = 0; w < kXWarps; ++w) t += wred[(size_t)w * REP * HD + i];
+      dst0[(size_t)rank * REP * HD + i] = t;
+    }
+  }
+  // the new key / value row goes to the cache once this CTA has read everything it needs
+  if (p0 <= pos && pos < p1) {
+    for (int i = threadIdx.x; i < HD; i += kXThreads) {
+      kc[((size_t)g * a.cap + slot_of(pos)) * HD + i] = kn[i];
+      vc[((size_t)g * a.cap + slot_of(pos)) * HD + i] = vn[i];
+    }
+  }
+  cl.sync();
+  if (rank != 0) return;
+  // ---- rank 0: the heads' outputs (rounded once) and their Q8_0 blocks for the O projection ----
+  float* outp = a.out + (size_t)b * a.bs_out + (size_t)g * REP * HD;
+  for (int i = threadIdx.x; i < REP * HD; i += kXThreads) {
+    double t = 0.0;
+    for (int r = 0; r < C; ++r) t += cl_o[(size_t)r * REP * HD + i];
+    const float v = (float)t;
+    qs[i] = v;
+    outp[i] = v;
+  }
+  __syncthreads();
+  if (a.oq) {
+    const int nblk = REP * HD / 32;
+    for (int blk = threadIdx.x; blk < nblk; blk += kXThreads) {
+      float v[32];
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = qs[32 * blk + k];
+      const size_t o0 = (size_t)b * a.bs_out + (size_t)g * REP * HD + 32 * (size_t)blk;
+      quantize_q8_block(v, a.oq + o0, &a.od[o0 / 32]);
+    }
+  }
+}
+
+template <int HD, int REP>
+cudaError_t launch_exact_attn_t(const AttnArgs& a, const DevCtx& c, int C, int max_per, cudaStream_t s) {
+  const size_t smem = (size_t)(REP * HD + 2 * HD) * 4 + (size_t)REP * max_per * 4 + 2 * 8 * REP * 8 +
+                      (size_t)kXWarps * REP * HD * 8 + (size_t)C * REP * HD * 8 + 64;
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(exact_attn_kernel<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)C, (unsigned)a.nkv, (unsigned)a.batch);
+  cfg.blockDim = dim3(kXThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = (unsigned)C;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, exact_attn_kernel<HD, REP>, a, c.err, max_per);
+}
+
+template <int HD>
+cudaError_t launch_exact_attn_hd(const AttnArgs& a, const DevCtx& c, int rep, int C, int max_per, cudaStream_t s) {
+  switch (rep) {
+    case 1: return launch_exact_attn_t<HD, 1>(a, c, C, max_per, s);
+    case 2: return launch_exact_attn_t<HD, 2>(a, c, C, max_per, s);
+    case 4: return launch_exact_attn_t<HD, 4>(a, c, C, max_per, s);
+    case 8: return launch_exact_attn_t<HD, 8>(a, c, C, max_per, s);
+    case 16:
+      if constexpr (HD <= 64) return launch_exact_attn_t<HD, 16>(a, c, C, max_per, s);
+      break;
+  }
+  return cudaErrorInvalidValue;
+}
+
+// ============================ experts (MXFP4 tensor-core tiles) ============================
+constexpr int kEThreads = 128;    // one thread per tile row
+constexpr int kESegChunks = 16;   // 32-element chunks per K segment
+
+// one row's dot over chunks [c0, c1) of a packed tile (tile layout: slabs of 16 chunk columns,
+// codes [chunk][128 rows][16 B] then a 512-byte scale group per 4 chunks, element 2i / 2i+1 in the
+// low / high nibble of code byte i), x as doubles in shared memory
+__device__ __forceinline__ double tile_row_dot(const uint8_t* tile, int kc, int r, int c0, int c1, const double* xs) {
+  double acc = 0.0;
+  for (int c = c0; c < c1; ++c) {
+    const int slab = c >> 4, nchs = min(16, kc - slab * 16), cl = c & 15;
+    const uint8_t* sb = tile + (size_t)slab * (16 * 2048 + 4 * 512);
+    const uint4 codes = __ldcs(reinterpret_cast<const uint4*>(sb + cl * 2048 + r * 16));
+    const uint32_t eb = sb[nchs * 2048 + (cl >> 2) * 512 + 16 * (r & 31) + 4 * (r >> 5) + (c & 3)];
+    const uint32_t cw[4] = {codes.x, codes.y, codes.z, codes.w};
+    const double* xc = xs + 32 * c;
+    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+      for (int bi = 0; bi < 4; ++bi) {
+        const uint32_t h2 = e2m1x2_to_f16x2((cw[q] >> (8 * bi)) & 0xFFu);
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+        const int i = 8 * q + 2 * bi;
+        if (bi & 1) { a2 = fma((double)f.x, xc[i], a2); a3 = fma((double)f.y, xc[i + 1], a3); }
+        else { a0 = fma((double)f.x, xc[i], a0); a1 = fma((double)f.y, xc[i + 1], a1); }
+      }
+    }
+    acc = fma((a0 + a1) + (a2 + a3), ldexp(1.0, (int)eb - 127), acc);   // scale 2^(E-127): exact
+  }
+  return acc;
+}
+
+// gate/up: grid (segments, gate_up tiles, slots); thread r of a tile = gate row (r < 64) or up row
+__global__ void __launch_bounds__(kEThreads) exact_gu_kernel(ExactMoeArgs a, uint32_t* err) {
+  extern __shared__ double xs[];   // this segment's slice of x as doubles (indexed from 0 .. H)
+  const int seg = blockIdx.x, mt = blockIdx.y, k = blockIdx.z, r = threadIdx.x;
+  const int kc = a.H / 32, c0 = seg * kESegChunks, c1 = min(kc, c0 + kESegChunks);
+  const int tiles = a.gu_tiles;
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int e = a.idx[k] - a.expert_base;
+  if (e < 0 || e >= a.n_local) return;   // another rank's expert (or out of range: the combine skips it)
+  for (int i = 32 * c0 + threadIdx.x; i < 32 * c1; i += kEThreads) xs[i] = (double)a.x[i];
+  __syncthreads();
+  const uint8_t* tile = a.gu + ((size_t)e * tiles + mt) * (size_t)a.gu_tile_bytes;
+  const double d = tile_row_dot(tile, kc, r, c0, c1, xs);
+  a.gp[((size_t)k * a.n_seg_gu + seg) * (2 * a.I) + (size_t)mt * 128 + r] = d;
+  (void)err;
+}
+
+__device__ __forceinline__ float act_exact(float g, float u, int oai) {
+  if (oai) {   // ops/activation.rs:25-45 (clamp 7, alpha 1.702)
+    const float gc = fminf(g, 7.0f);
+    const float uc = fminf(fmaxf(u, -7.0f), 7.0f);
+    const float sg = __fdiv_rn(1.0f, __fadd_rn(expcr(-__fadd_rn(__fmul_rn(gc, 1.702f), 0.0f)), 1.0f));
+    return __fmul_rn(__fmul_rn(gc, sg), __fadd_rn(uc, 1.0f));
+  }
+  // ops/activation.rs:13-15: silu(g) * u with silu(x) = x / (1 + exp(-x))
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expcr(-g))), u);
+}
+
+// down: grid (segments, down tiles, slots).  The segment's activations are rebuilt from the gate/up
+// partial dots (sum of segments rounded once, + bias, activation) into shared memory first.
+__global__ void __launch_bounds__(kEThreads) exact_down_kernel(ExactMoeArgs a, uint32_t* err) {
+  extern __shared__ double as[];
+  const int seg = blockIdx.x, mt = blockIdx.y, k = blockIdx.z, r = threadIdx.x;
+  const int kc = a.I / 32, c0 = seg * kESegChunks, c1 = min(kc, c0 + kESegChunks);
+  const int tiles = a.down_tiles;
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int e = a.idx[k] - a.expert_base;
+  if (e < 0 || e >= a.n_local) return;
+  const double* gp = a.gp + (size_t)k * a.n_seg_gu * (2 * a.I);
+  for (int i = 32 * c0 + threadIdx.x; i < 32 * c1; i += kEThreads) {
+    const int gr = (i >> 6) * 128 + (i & 63), ur = gr + 64;   // gate / up rows of activation i
+    double gs = 0.0, us = 0.0;
+    for (int s2 = 0; s2 < a.n_seg_gu; ++s2) {
+      gs += gp[(size_t)s2 * (2 * a.I) + gr];
+      us += gp[(size_t)s2 * (2 * a.I) + ur];
+    }
+    float gv = (float)gs, uv = (float)us;
+    if (a.gate_b) gv = __fadd_rn(gv, a.gate_b[(size_t)e * a.I + i]);
+    if (a.up_b) uv = __fadd_rn(uv, a.up_b[(size_t)e * a.I + i]);
+    as[i] = (double)act_exact(gv, uv, a.oai_swiglu);
+  }
+  __syncthreads();
+  const uint8_t* tile = a.down + ((size_t)e * tiles + mt) * (size_t)a.down_tile_bytes;
+  const double d = tile_row_dot(tile, kc, r, c0, c1, as);
+  const int row = mt * 128 + r;
+  a.dp[((size_t)k * a.n_seg_down + seg) * a.h_pad + row] = d;
+  (void)err;
+}
+
+template <class Kern>
+cudaError_t launch_pdl_x(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const ExactMoeArgs& a,
+                         uint32_t* err) {
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, a, err);
+}
+
+}  // namespace
+
+int exact_attn_cluster(int range) {
+  int C = (range + 255) / 256;
+  return C < 1 ? 1 : (C > 8 ? 8 : C);
+}
+
+cudaError_t launch_exact_attention(const DevCtx& c, const AttnArgs& a, int range, cudaStream_t s) {
+  if (a.nkv <= 0 || a.nh % a.nkv || a.rot > a.hd || a.rot % 2 || a.batch < 1 || range <= 0) return cudaErrorInvalidValue;
+  if (a.batch > 1 && a.bs_out % 32) return cudaErrorInvalidValue;
+  const int rep = a.nh / a.nkv;
+  if (32 % rep) return cudaErrorInvalidValue;
+  const int C = exact_attn_cluster(range);
+  const int max_per = (range + C - 1) / C;
+  switch (a.hd) {
+    case 32: return launch_exact_attn_hd<32>(a, c, rep, C, max_per, s);
+    case 64: return launch_exact_attn_hd<64>(a, c, rep, C, max_per, s);
+    case 128: return launch_exact_attn_hd<128>(a, c, rep, C, max_per, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+int exact_seg_count(int kc) { return (kc + kESegChunks - 1) / kESegChunks; }
+
+cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a0, cudaStream_t s) {
+  ExactMoeArgs a = a0;
+  if (!tc_supported(a.H, a.I) || a.K < 1 || a.K > 16 || !a.gp || !a.dp) return cudaErrorInvalidValue;
+  a.gu_tiles = tc_gu_tiles(a.I);
+  a.down_tiles = tc_down_tiles(a.H);
+  a.gu_tile_bytes = tc_tile_bytes(a.H / 32);
+  a.down_tile_bytes = tc_tile_bytes(a.I / 32);
+  if (a.n_seg_gu != exact_seg_count(a.H / 32) || a.n_seg_down != exact_seg_count(a.I / 32) ||
+      a.h_pad < tc_down_tiles(a.H) * 128)
+    return cudaErrorInvalidValue;
+  cudaError_t e = launch_pdl_x(exact_gu_kernel, dim3((unsigned)a.n_seg_gu, (unsigned)tc_gu_tiles(a.I), (unsigned)a.K),
+                               dim3(kEThreads), (size_t)a.H * 8, s, a, c.err);
+  if (e != cudaSuccess) return e;
+  return launch_pdl_x(exact_down_kernel, dim3((unsigned)a.n_seg_down, (unsigned)tc_down_tiles(a.H), (unsigned)a.K),
+                      dim3(kEThreads), (size_t)a.I * 8, s, a, c.err);
+}
+
+}  // namespace ms

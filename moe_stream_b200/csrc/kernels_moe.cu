@@ -1024,24 +1024,26 @@ __device__ __forceinline__ void router_select_t(const RouterArgs& a, uint32_t* e
   if (a.softmax_weight) {              // layer.rs:2361-2372: softmax over the selected logits
     float mx = -INFINITY;
     for (int k = 0; k < a.K; ++k) mx = fmaxf(mx, sel_v[k]);
-    float sum = 0.f;
-    for (int k = 0; k < a.K; ++k) { w[k] = expf(sel_v[k] - mx); }
-    for (int k = 0; k < a.K; ++k) sum += w[k];
-    for (int k = 0; k < a.K; ++k) w[k] = w[k] / sum;
+    double sum = 0.0;
+    for (int k = 0; k < a.K; ++k) { w[k] = expcr(__fsub_rn(sel_v[k], mx)); }
+    for (int k = 0; k < a.K; ++k) sum += (double)w[k];
+    const float s32 = (float)sum;
+    for (int k = 0; k < a.K; ++k) w[k] = __fdiv_rn(w[k], s32);
   } else {                              // layer.rs:2374-2394: softmax over all, then (re)normalise
     float mx = -INFINITY;
 #pragma unroll
     for (int j = 0; j < kPer; ++j) mx = fmaxf(mx, lv[j]);
     mx = warp_max(mx);
-    float sum = 0.f;
+    double sum = 0.0;
 #pragma unroll
     for (int j = 0; j < kPer; ++j)
-      if (lane + 32 * j < a.E) sum += expf(lv[j] - mx);
-    sum = warp_sum(sum);
-    float ts = 0.f;
-    for (int k = 0; k < a.K; ++k) { w[k] = expf(sel_v[k] - mx) / sum; }
-    for (int k = 0; k < a.K; ++k) ts += w[k];
-    if (a.normalize) for (int k = 0; k < a.K; ++k) w[k] = w[k] / ts;
+      if (lane + 32 * j < a.E) sum += (double)expcr(__fsub_rn(lv[j], mx));
+    const float s32 = (float)warp_sum_d(sum);
+    double ts = 0.0;
+    for (int k = 0; k < a.K; ++k) { w[k] = __fdiv_rn(expcr(__fsub_rn(sel_v[k], mx)), s32); }
+    for (int k = 0; k < a.K; ++k) ts += (double)w[k];
+    const float t32 = (float)ts;
+    if (a.normalize) for (int k = 0; k < a.K; ++k) w[k] = __fdiv_rn(w[k], t32);
   }
   if (lane == 0) {
     for (int k = 0; k < a.K; ++k) { a.idx[k] = sel_i[k]; a.wts[k] = w[k]; }
@@ -1079,29 +1081,30 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, ui
   }
   pdl_wait_prior();
   pdl_launch_dependents();   // the next kernel may start its own (weight) prefetch now
-  float dot = 0.f;
+  double dot = 0.0;
   float inv = 1.f;
-  if (a.h) {
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < a.H; i += kRouterThreads) { const float v = a.h[i]; ss += v * v; }
-    ss = router_block_sum(ss, red);   // (its barrier also publishes the mbarrier's initialisation)
-    inv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
-  } else {
-    __syncthreads();
-  }
+  // (the barriers of the RMSNorm also publish the mbarrier's initialisation)
+  if (a.h) inv = rms_inv_cr(a.h, a.H, a.eps, threadIdx.x, kRouterThreads, [] { __syncthreads(); });
+  else __syncthreads();
   bool row_ok = true;
   if (row_async) row_ok = mbar_wait(&bar, 0, err, EF_TIMEOUT_FULL);
   const float* wsrc = row_async ? wrow : wr;
   if (row_ok) {
     for (int i = threadIdx.x; i < a.H; i += kRouterThreads) {
-      const float v = a.h ? (a.h[i] * inv) * a.norm_w[i] : a.xn[i];
+      const float v = a.h ? __fmul_rn(__fmul_rn(a.h[i], inv), a.norm_w[i]) : a.xn[i];
       if (a.h && e == 0) a.xn[i] = v;
-      dot = fmaf(v, wsrc[i], dot);
+      dot = fma((double)v, (double)wsrc[i], dot);
     }
   }
-  dot = router_block_sum(dot, red);
+  dot = warp_sum_d(dot);
+  __shared__ double redd[kRouterThreads / 32];
+  if (lane == 0) redd[warp] = dot;
+  __syncthreads();
   if (threadIdx.x == 0) {
-    float v = dot + (a.b ? a.b[e] : 0.f);
+    double t = 0.0;
+    for (int w = 0; w < kRouterThreads / 32; ++w) t += redd[w];
+    float v = (float)t;
+    if (a.b) v = __fadd_rn(v, a.b[e]);
     if (a.mask && a.mask[e]) v = -INFINITY;
     a.logits[e] = v;
     __threadfence();
@@ -1113,7 +1116,7 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, ui
     const int nb = a.H / 32, nw = kRouterThreads / 32;
     for (int b = e * nw + warp; b < nb; b += (int)gridDim.x * nw) {
       const int i = 32 * b + lane;
-      const float v = a.h ? (a.h[i] * inv) * a.norm_w[i] : a.xn[i];
+      const float v = a.h ? __fmul_rn(__fmul_rn(a.h[i], inv), a.norm_w[i]) : a.xn[i];
       umma::quantize_terms_warp(v, lane, a.xterm, nb, b);
     }
   }
@@ -1141,12 +1144,9 @@ __global__ void __launch_bounds__(kRouterThreads) router_batch_kernel(RouterArgs
   a.counter += b;
   pdl_wait_prior();
   pdl_launch_dependents();
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < a.H; i += kRouterThreads) { const float v = a.h[i]; ss += v * v; }
-  ss = router_block_sum(ss, red);
-  const float inv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
+  const float inv = rms_inv_cr(a.h, a.H, a.eps, threadIdx.x, kRouterThreads, [] { __syncthreads(); });
   for (int i = threadIdx.x; i < a.H; i += kRouterThreads) {
-    const float v = (a.h[i] * inv) * a.norm_w[i];
+    const float v = __fmul_rn(__fmul_rn(a.h[i], inv), a.norm_w[i]);
     xs[i] = v;
     if (blockIdx.x == 0) a.xn[i] = v;
   }
@@ -1156,17 +1156,18 @@ __global__ void __launch_bounds__(kRouterThreads) router_batch_kernel(RouterArgs
     if (e >= a.E) break;
     const float4* w4 = reinterpret_cast<const float4*>(a.w + (size_t)e * a.H);
     const float4* x4 = reinterpret_cast<const float4*>(xs);
-    float dot = 0.f;
+    double dot = 0.0;
     for (int i = lane; i < a.H / 4; i += 32) {
       const float4 w = __ldg(w4 + i), x = x4[i];
-      dot = fmaf(x.x, w.x, dot);
-      dot = fmaf(x.y, w.y, dot);
-      dot = fmaf(x.z, w.z, dot);
-      dot = fmaf(x.w, w.w, dot);
+      dot = fma((double)x.x, (double)w.x, dot);
+      dot = fma((double)x.y, (double)w.y, dot);
+      dot = fma((double)x.z, (double)w.z, dot);
+      dot = fma((double)x.w, (double)w.w, dot);
     }
-    dot = warp_sum(dot);
+    dot = warp_sum_d(dot);
     if (lane == 0) {
-      float v = dot + (a.b ? a.b[e] : 0.f);
+      float v = (float)dot;
+      if (a.b) v = __fadd_rn(v, a.b[e]);
       if (a.mask && a.mask[e]) v = -INFINITY;
       a.logits[e] = v;
     }

@@ -36,15 +36,21 @@ constexpr int kPfCh = 2;                   // MXFP4 chunks per stage (K = 64)
 constexpr int kPfStA = kPfCh * 2048;       // MXFP4 codes of a stage: 2 chunks x 128 rows x 16 B
 constexpr int kPfStSF = 512;               // the scale group holding them
 constexpr int kPfStB = 4 * kPfCh * kPfN * 16;   // tokens: 8 bf16 chunk columns x 256 rows x 16 B
-constexpr int kPfStage = kPfStA + kPfStSF + kPfStB;
 constexpr int kPfABf = 4 * kPfCh * 128 * 16;    // dequantized weights of a stage
-constexpr int kPfStages = 4;
+// PREC = 1 ("precise"): every token operand is a bf16 pair hi + lo (hi = bf16(x), lo = bf16(x - hi),
+// |x - hi - lo| <= 2^-18 |x|) and each K step issues two MMAs into the same f32 accumulator, so the
+// activations carry ~17 significant bits instead of 8 (the weights are exact in bf16 either way).
+template <int PREC> struct PfCfg {
+  static constexpr int kStage = kPfStA + kPfStSF + (PREC ? 2 : 1) * kPfStB;
+  static constexpr int kStages = PREC ? 2 : 4;
+};
 constexpr int kPfUpLd = 33;                // padded row of the up-row exchange buffer (no bank conflicts)
 constexpr int kPfThreads = 14 * 32;
 constexpr int kPfDeqThreads = 8 * 32;
 constexpr int kPfTmemCols = 512;           // two 256-column accumulators
 constexpr int kPfMaxE = 256;
-constexpr int kPfSmem = kPfStages * (kPfStage + kPfABf) + 64 * kPfUpLd * 4;
+template <int PREC>
+constexpr int pf_smem() { return PfCfg<PREC>::kStages * (PfCfg<PREC>::kStage + kPfABf) + 64 * kPfUpLd * 4; }
 
 struct PfParams {
   int mode;                  // 0 gate_up, 1 down
@@ -52,6 +58,7 @@ struct PfParams {
   int64_t tile_bytes;
   int tiles, kc;             // weight tiles per expert; K / 32
   const uint8_t* b;          // token operand tiles: [tile][K / 8][256][16 B] bf16
+  const uint8_t* b_lo;       // precise mode: the low bf16 halves, same layout
   const int* count;          // [E] tokens per expert
   const int* list;           // [E][T] (t * K + k) entries in token order
   int E, T, K, H, I;
@@ -59,6 +66,7 @@ struct PfParams {
   const float* bias1;        // up_b
   const float* wts;          // [T * K] routing weights (down)
   uint8_t* act;              // gate_up output: token operand tiles of the activation
+  uint8_t* act_lo;           // precise mode: their low halves
   float* y;                  // down output [T * K][H]
   int oai;
   uint32_t* err;
@@ -108,7 +116,7 @@ __global__ void __launch_bounds__(256) pf_route_kernel(const int* idx, int T, in
 
 // ---------------- gather: x [T][H] f32 -> bf16 token tiles [tile][H/8][256][8] ----------------
 __global__ void pf_gather_kernel(const float* __restrict__ x, int H, int K, const int* count, const int* list, int E,
-                                 int T, uint8_t* __restrict__ b) {
+                                 int T, uint8_t* __restrict__ b, uint8_t* __restrict__ b_lo) {
   __shared__ int off[kPfMaxE + 1];
   pf_tile_offsets(count, E, off);
   const int nch = H / 8;
@@ -121,17 +129,27 @@ __global__ void pf_gather_kernel(const float* __restrict__ x, int H, int K, cons
     int e = 0;
     while (e + 1 < E && off[e + 1] <= tile) ++e;
     const int pos = (tile - off[e]) * kPfN + row;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    uint4 v = make_uint4(0u, 0u, 0u, 0u), vl = v;
     if (pos < count[e]) {
       const int t = list[(size_t)e * T + pos] / K;
       const float4* src = reinterpret_cast<const float4*>(x + (size_t)t * H + 8 * ch);
       const float4 a = src[0], c = src[1];
-      const __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x, a.y), p1 = __floats2bfloat162_rn(a.z, a.w);
-      const __nv_bfloat162 p2 = __floats2bfloat162_rn(c.x, c.y), p3 = __floats2bfloat162_rn(c.z, c.w);
-      v = make_uint4(*reinterpret_cast<const uint32_t*>(&p0), *reinterpret_cast<const uint32_t*>(&p1),
-                     *reinterpret_cast<const uint32_t*>(&p2), *reinterpret_cast<const uint32_t*>(&p3));
+      const float f[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const __nv_bfloat162 hi = __floats2bfloat162_rn(f[2 * q], f[2 * q + 1]);
+        const float2 hf = __bfloat1622float2(hi);
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(f[2 * q] - hf.x, f[2 * q + 1] - hf.y);
+        hw[q] = *reinterpret_cast<const uint32_t*>(&hi);
+        lw[q] = *reinterpret_cast<const uint32_t*>(&lo);
+      }
+      v = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      vl = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
-    *reinterpret_cast<uint4*>(b + ((int64_t)tile * nch + ch) * (kPfN * 16) + row * 16) = v;
+    const int64_t o = ((int64_t)tile * nch + ch) * (kPfN * 16) + row * 16;
+    *reinterpret_cast<uint4*>(b + o) = v;
+    if (b_lo) *reinterpret_cast<uint4*>(b_lo + o) = vl;
   }
 }
 
@@ -161,8 +179,9 @@ __global__ void pf_combine_kernel(const float* __restrict__ y, const int* idx, i
 }
 
 // ---------------- grouped GEMM ----------------
-template <int MODE>
+template <int MODE, int PREC>
 __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_constant__ PfParams p) {
+  constexpr int kPfStages = PfCfg<PREC>::kStages, kPfStage = PfCfg<PREC>::kStage;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* stage_base = smem;                                   // [kPfStages][kPfStage]
   uint8_t* abf_base = smem + kPfStages * kPfStage;              // [kPfStages][kPfABf]
@@ -208,10 +227,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
           const uint8_t* sb = wt + (int64_t)slab * (16 * 2048 + 4 * 512);
           uint8_t* sp = stage_base + (size_t)s * kPfStage;
           const uint32_t ab = (uint32_t)(c1 - c0) * 2048u, bb = (uint32_t)(c1 - c0) * 4u * kPfN * 16u;
-          mbar_expect_tx(&full[s], ab + 512u + bb);
+          mbar_expect_tx(&full[s], ab + 512u + (PREC ? 2u : 1u) * bb);
           bulk_g2s_stream(sp, sb + (int64_t)(c0 - sl0) * 2048, ab, &full[s], pol);
           bulk_g2s_stream(sp + kPfStA, sb + (int64_t)nchs * 2048 + ((c0 - sl0) >> 2) * 512, 512u, &full[s], pol);
           bulk_g2s(sp + kPfStA + kPfStSF, bt + (int64_t)(4 * c0) * (kPfN * 16), bb, &full[s]);
+          if (PREC)
+            bulk_g2s(sp + kPfStA + kPfStSF + kPfStB,
+                     p.b_lo + (int64_t)tile * nch_b * (kPfN * 16) + (int64_t)(4 * c0) * (kPfN * 16), bb, &full[s]);
           ++j;
         }
       }
@@ -279,6 +301,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
             const uint64_t bd = umma::smem_desc(bb + 2 * k * (kPfN * 16), kPfN * 16, 128);
             umma::mma_bf16(d, ad, bd, idesc, nmma > 0);
             ++nmma;
+            if (PREC) {   // the low halves of the same token columns, same weights
+              const uint64_t bl = umma::smem_desc(bb + kPfStB + 2 * k * (kPfN * 16), kPfN * 16, 128);
+              umma::mma_bf16(d, ad, bl, idesc, 1);
+            }
           }
           umma::commit(&empty[s]);
         }
@@ -302,7 +328,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
         const int ai = mt * 64 + r;                     // activation index
         const float bg = p.bias0 ? p.bias0[(int64_t)e * p.I + ai] : 0.f;
         const float bu = p.bias1 ? p.bias1[(int64_t)e * p.I + ai] : 0.f;
-        uint8_t* at = p.act + (int64_t)tile * (p.I / 8) * (kPfN * 16) + (int64_t)(ai >> 3) * (kPfN * 16) + (ai & 7) * 2;
+        const int64_t ao = (int64_t)tile * (p.I / 8) * (kPfN * 16) + (int64_t)(ai >> 3) * (kPfN * 16) + (ai & 7) * 2;
+        uint8_t* at = p.act + ao;
+        uint8_t* atl = PREC ? p.act_lo + ao : nullptr;
         for (int cb = 0; cb < kPfN / 32; ++cb) {
           float v[32];
           umma::ld_32x32b_x32(tb + ((uint32_t)(32 * quad) << 16) + (uint32_t)(a * kPfN + cb * 32), v);
@@ -316,7 +344,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
             for (int n = 0; n < 32; ++n) {
               const float av = p.oai ? swiglu_pf(v[n] + bg, s_up[r * kPfUpLd + n] + bu)
                                      : ((v[n] + bg) / (1.0f + expf(-(v[n] + bg)))) * (s_up[r * kPfUpLd + n] + bu);
-              *reinterpret_cast<__nv_bfloat16*>(at + (cb * 32 + n) * 16) = __float2bfloat16_rn(av);
+              const __nv_bfloat16 hi = __float2bfloat16_rn(av);
+              *reinterpret_cast<__nv_bfloat16*>(at + (cb * 32 + n) * 16) = hi;
+              if (PREC) *reinterpret_cast<__nv_bfloat16*>(atl + (cb * 32 + n) * 16) = __float2bfloat16_rn(av - __bfloat162float(hi));
             }
           }
           named_bar(1, 128);
@@ -354,20 +384,22 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
   if (warp == 1) umma::tmem_dealloc(tb, kPfTmemCols);
 }
 
-template <int MODE>
+template <int MODE, int PREC>
 cudaError_t launch_pf_gemm(const DevCtx& c, const PfParams& p, cudaStream_t s) {
-  cudaError_t e = cudaFuncSetAttribute(pf_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
+  constexpr int smem = pf_smem<PREC>();
+  cudaError_t e = cudaFuncSetAttribute(pf_gemm_kernel<MODE, PREC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  pf_gemm_kernel<MODE><<<c.sm_count, kPfThreads, kPfSmem, s>>>(p);
+  pf_gemm_kernel<MODE, PREC><<<c.sm_count, kPfThreads, smem, s>>>(p);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-size_t pf_scratch_bytes(int H, int I, int E, int T, int K) {
+size_t pf_scratch_bytes(int H, int I, int E, int T, int K, int precise) {
   const size_t tiles = (size_t)(T * K) / kPfN + E + 1;   // upper bound on sum over experts of ceil(n_e / 256)
+  const size_t m = precise ? 2 : 1;                       // token operands: hi (and lo) halves
   auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
-  return up((size_t)E * 4) + up((size_t)E * T * 4) + up(tiles * H * kPfN * 2) + up(tiles * I * kPfN * 2) +
+  return up((size_t)E * 4) + up((size_t)E * T * 4) + m * up(tiles * H * kPfN * 2) + m * up(tiles * I * kPfN * 2) +
          up((size_t)T * K * H * 4);
 }
 
@@ -377,23 +409,26 @@ cudaError_t launch_moe_prefill(const DevCtx& c, const PrefillArgs& a, cudaStream
   auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
   uint8_t* base = reinterpret_cast<uint8_t*>(a.scratch);
   const size_t tiles = (size_t)(a.T * a.K) / kPfN + a.E + 1;
+  const size_t xb_b = up(tiles * a.H * kPfN * 2), act_b = up(tiles * a.I * kPfN * 2);
   int* count = reinterpret_cast<int*>(base);
   int* list = reinterpret_cast<int*>(base + up((size_t)a.E * 4));
   uint8_t* xb = base + up((size_t)a.E * 4) + up((size_t)a.E * a.T * 4);
-  uint8_t* act = xb + up(tiles * a.H * kPfN * 2);
-  float* y = reinterpret_cast<float*>(act + up(tiles * a.I * kPfN * 2));
+  uint8_t* xb_lo = a.precise ? xb + xb_b : nullptr;
+  uint8_t* act = xb + (a.precise ? 2 : 1) * xb_b;
+  uint8_t* act_lo = a.precise ? act + act_b : nullptr;
+  float* y = reinterpret_cast<float*>(act + (a.precise ? 2 : 1) * act_b);
   pf_route_kernel<<<a.E, 256, 0, s>>>(a.idx, a.T, a.K, a.expert_base, a.E, count, list);
-  pf_gather_kernel<<<4 * c.sm_count, 256, 0, s>>>(a.x, a.H, a.K, count, list, a.E, a.T, xb);
+  pf_gather_kernel<<<4 * c.sm_count, 256, 0, s>>>(a.x, a.H, a.K, count, list, a.E, a.T, xb, xb_lo);
   PfParams p = {};
   p.count = count; p.list = list; p.E = a.E; p.T = a.T; p.K = a.K; p.H = a.H; p.I = a.I; p.wts = a.wts;
-  p.act = act; p.y = y; p.oai = a.oai_swiglu; p.err = c.err;
+  p.act = act; p.act_lo = act_lo; p.y = y; p.oai = a.oai_swiglu; p.err = c.err;
   p.mode = 0; p.w = a.gu; p.kc = a.H / 32; p.tile_bytes = tc_tile_bytes(p.kc); p.tiles = tc_gu_tiles(a.I);
-  p.b = xb; p.bias0 = a.gate_b; p.bias1 = a.up_b;
-  cudaError_t e = launch_pf_gemm<0>(c, p, s);
+  p.b = xb; p.b_lo = xb_lo; p.bias0 = a.gate_b; p.bias1 = a.up_b;
+  cudaError_t e = a.precise ? launch_pf_gemm<0, 1>(c, p, s) : launch_pf_gemm<0, 0>(c, p, s);
   if (e != cudaSuccess) return e;
   p.mode = 1; p.w = a.down; p.kc = a.I / 32; p.tile_bytes = tc_tile_bytes(p.kc); p.tiles = tc_down_tiles(a.H);
-  p.b = act; p.bias0 = a.down_b; p.bias1 = nullptr;
-  e = launch_pf_gemm<1>(c, p, s);
+  p.b = act; p.b_lo = act_lo; p.bias0 = a.down_b; p.bias1 = nullptr;
+  e = a.precise ? launch_pf_gemm<1, 1>(c, p, s) : launch_pf_gemm<1, 0>(c, p, s);
   if (e != cudaSuccess) return e;
   pf_combine_kernel<<<a.T, 256, 0, s>>>(y, a.idx, a.K, a.expert_base, a.E, a.H, a.out, a.accumulate);
   return cudaGetLastError();

@@ -252,6 +252,27 @@ struct ms_model {
   float* trace_h = nullptr;
   float* trace_logits = nullptr;
   bool trace = false;
+  // multi-token forward (prompt prefill): 0 = one decode step per token, 1 = batched with the
+  // expert GEMM's activations as bf16 hi + lo pairs (default), 2 = batched with bf16 activations
+  int prefill_mode = 1;
+  // order-independent decode kernels (f64 reductions rounded once; bit-identical to the oracle):
+  // attention and MXFP4 experts; ms_model_set_exact(m, 0) selects the pipelined f32 kernels
+  bool exact = true;
+  double* ex_gp = nullptr;          // [K][segments][2 I] gate/up partial dots
+  double* ex_dp = nullptr;          // [K][segments][h_pad] down partial dots
+  int ex_seg_gu = 0, ex_seg_down = 0, ex_hpad = 0;
+  struct Prefill {
+    int cap = 0;                       // tokens the buffers hold
+    std::vector<void*> allocs;
+    int* tok = nullptr;
+    float *h = nullptr, *qkv = nullptr, *q = nullptr, *kn = nullptr, *vn = nullptr, *attn = nullptr;
+    float *xn = nullptr, *rlog = nullptr, *wts = nullptr, *moe_y = nullptr, *gy = nullptr, *gact = nullptr;
+    int8_t* xq = nullptr;
+    float* xd = nullptr;
+    int *idx = nullptr, *grp = nullptr, *ent_slot = nullptr, *ent_of = nullptr;
+    uint32_t* rcnt = nullptr;
+    void* moe_scratch = nullptr;
+  } pf;
 
   template <class T>
   ms_status alloc(T** p, size_t bytes, bool zero = true) {
@@ -458,6 +479,14 @@ int launch_class(const ms_model* m, int i) {
   return 1 + (i - 1) % per_layer;
 }
 
+// the order-independent attention covers head dims 32 / 64 / 128 and up to 32 query heads per kv head
+bool exact_attn_ok(const ms_model* m) {
+  const ms_model_config& c = m->cfg;
+  const int rep = c.heads / c.kv_heads;
+  return m->exact && (c.head_dim == 32 || c.head_dim == 64 || c.head_dim == 128) && 32 % rep == 0 &&
+         (c.head_dim < 128 || rep <= 8);
+}
+
 ms_status enqueue_step(ms_model* m, cudaStream_t s) {
   const ms_model_config& c = m->cfg;
   const DevCtx& dc = m->ctx->dc;
@@ -491,7 +520,8 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     if (m->attn_spl && (c.heads / c.kv_heads) % 4 == 0) aa.head_split = 4;
     else if (m->attn_spl && (c.heads / c.kv_heads) % 2 == 0 && c.heads / c.kv_heads >= 4) aa.head_split = 2;
     aa.scale = (float)(1.0 / std::sqrt((double)c.head_dim)); aa.oq = m->xq_a; aa.od = m->xd_a;
-    LAUNCH(launch_attention(dc, aa, s));
+    if (exact_attn_ok(m)) LAUNCH(launch_exact_attention(dc, aa, Lw.window ? Lw.cap : c.max_seq_len, s));
+    else LAUNCH(launch_attention(dc, aa, s));
     Q8GemvArgs oa;
     oa.w = Lw.wo; oa.rows = H; oa.cols = Dq; oa.xq_in = m->xq_a; oa.xd_in = m->xd_a; oa.bias = Lw.bo;
     oa.residual = m->h;
@@ -520,7 +550,41 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     ma.tile_cnt = m->tile_cnt; ma.h = m->h; ma.H = H; ma.I = c.inter; ma.K = c.top_k;
     ma.expert_base = m->expert_base; ma.n_local = m->n_local; ma.oai_swiglu = c.arch == MS_ARCH_GPT_OSS;
     PendingCombine pc;
-    if (c.ep_size > 1 && m->ep_p2p) {
+    if (m->exact && Lw.tc) {
+      // order-independent experts: f64 partial dots; the combine (residual kernel, the peer-mailbox
+      // send, or a combine kernel before the NCCL all-reduce) sums segments in ascending expert id
+      ExactMoeArgs ea;
+      ea.gu = Lw.gu_tc; ea.down = Lw.down_tc; ea.gate_b = Lw.gate_b; ea.up_b = Lw.up_b; ea.x = m->xn; ea.idx = Lw.idx;
+      ea.H = H; ea.I = c.inter; ea.K = c.top_k; ea.expert_base = m->expert_base; ea.n_local = m->n_local;
+      ea.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ea.gp = m->ex_gp; ea.dp = m->ex_dp; ea.n_seg_gu = m->ex_seg_gu;
+      ea.n_seg_down = m->ex_seg_down; ea.h_pad = m->ex_hpad;
+      LAUNCH(launch_exact_moe(dc, ea, s));
+      ++nk;   // gate/up, down
+      PendingCombine lc;
+      lc.dpart = m->ex_dp; lc.down_b = Lw.down_b; lc.n_dseg = m->ex_seg_down; lc.dpad = m->ex_hpad;
+      lc.idx = Lw.idx; lc.wts = Lw.wts; lc.K = c.top_k; lc.expert_base = m->expert_base; lc.n_local = m->n_local;
+      if (c.ep_size > 1 && m->ep_p2p) {
+        const int n = c.ep_size;
+        EpSend e;
+        for (int j = 0; j < n; ++j) {
+          float* mb = j == c.ep_rank ? m->ep_mail : reinterpret_cast<float*>(m->ep_peer[j]);
+          e.recv[j] = mb;
+          e.flags[j] = reinterpret_cast<uint32_t*>(mb + (size_t)2 * n * H);
+        }
+        e.seq = m->ep_seq; e.cnt = m->ep_cnt; e.rank = c.ep_rank; e.n = n;
+        LAUNCH(launch_ep_send(dc, lc, H, e, s));
+        pc.ep_recv = m->ep_mail; pc.ep_flags = reinterpret_cast<const uint32_t*>(m->ep_mail + (size_t)2 * n * H);
+        pc.ep_seq = m->ep_seq; pc.ep_n = n;
+      } else if (c.ep_size > 1) {
+        LAUNCH(launch_moe_combine(dc, lc, H, nullptr, m->moe_out, s));
+        NcclApi* api = nccl_api();
+        ncclResult_t r = api->all_reduce(m->moe_out, m->moe_out, (size_t)H, ncclFloat32, ncclSum, m->comm, s);
+        if (r != ncclSuccess) return fail(m->ctx, MS_ERR_NCCL, "ncclAllReduce: %s", api->error_string(r));
+        pc.dense = m->moe_out;
+      } else {
+        pc = lc;
+      }
+    } else if (c.ep_size > 1 && m->ep_p2p) {
       // expert parallel over peer memory: the local experts' combine goes straight into every
       // rank's mailbox (one kernel); the residual kernel waits for all ranks and sums them
       ma.defer_combine = 1;
@@ -613,6 +677,199 @@ ms_status run_step(ms_model* m) {
     if (e != cudaSuccess) { m->graph = nullptr; return cuda_fail(m->ctx, e, "cudaGraphInstantiate"); }
   }
   MS_CUDA(m->ctx, cudaGraphLaunch(m->graph, s));
+  return MS_OK;
+}
+
+// ---------------- multi-token forward (engine.rs:1869-2006 over a [1, T] prompt) ----------------
+constexpr int kPrefillChunk = 2048;   // tokens per batched pass (bounds the scratch)
+
+template <class T>
+ms_status pf_alloc(ms_model* m, T** p, size_t bytes) {
+  void* q = nullptr;
+  cudaError_t e = cudaMalloc(&q, bytes ? bytes : 16);
+  if (e != cudaSuccess) return cuda_fail(m->ctx, e, "cudaMalloc (prefill)");
+  e = cudaMemset(q, 0, bytes ? bytes : 16);
+  if (e != cudaSuccess) { cudaFree(q); return cuda_fail(m->ctx, e, "cudaMemset (prefill)"); }
+  m->pf.allocs.push_back(q);
+  *p = reinterpret_cast<T*>(q);
+  return MS_OK;
+}
+
+ms_status pf_reserve(ms_model* m, int T) {
+  auto& P = m->pf;
+  if (P.cap >= T) return MS_OK;
+  MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+  for (void* q : P.allocs) cudaFree(q);
+  P = ms_model::Prefill();
+  const ms_model_config& c = m->cfg;
+  const int H = c.hidden, Dq = q_dim(c), Dkv = kv_dim(c), K = c.top_k, E = c.experts;
+  const int Wq = std::max(H, Dq);
+  bool any_tc = false, any_native = false;
+  for (auto& Lw : m->L) { any_tc = any_tc || Lw.tc; any_native = any_native || !Lw.tc; }
+  ms_status s = MS_OK;
+  s = s ? s : pf_alloc(m, &P.tok, (size_t)T * 4);
+  s = s ? s : pf_alloc(m, &P.h, (size_t)T * H * 4);
+  s = s ? s : pf_alloc(m, &P.xq, (size_t)T * Wq + 64);
+  s = s ? s : pf_alloc(m, &P.xd, (size_t)T * Wq / 32 * 4 + 64);
+  s = s ? s : pf_alloc(m, &P.qkv, (size_t)T * (Dq + 2 * Dkv) * 4);
+  s = s ? s : pf_alloc(m, &P.q, (size_t)T * Dq * 4);
+  s = s ? s : pf_alloc(m, &P.kn, (size_t)T * Dkv * 4);
+  s = s ? s : pf_alloc(m, &P.vn, (size_t)T * Dkv * 4);
+  s = s ? s : pf_alloc(m, &P.attn, (size_t)T * Dq * 4);
+  s = s ? s : pf_alloc(m, &P.xn, (size_t)T * H * 4);
+  s = s ? s : pf_alloc(m, &P.rlog, (size_t)T * E * 4);
+  s = s ? s : pf_alloc(m, &P.idx, (size_t)T * K * 4);
+  s = s ? s : pf_alloc(m, &P.wts, (size_t)T * K * 4);
+  s = s ? s : pf_alloc(m, &P.rcnt, (size_t)(T + 16) * 4);
+  if (c.ep_size > 1) s = s ? s : pf_alloc(m, &P.moe_y, (size_t)T * H * 4);
+  if (any_tc) s = s ? s : pf_alloc(m, &P.moe_scratch, pf_scratch_bytes(H, c.inter, m->n_local, T, K, 1));
+  if (any_native) {
+    s = s ? s : pf_alloc(m, &P.grp, (size_t)group_table_words(kMaxBatch, K) * 4);
+    s = s ? s : pf_alloc(m, &P.ent_slot, (size_t)kMaxBatch * K * 4);
+    s = s ? s : pf_alloc(m, &P.ent_of, (size_t)kMaxBatch * K * 4);
+    s = s ? s : pf_alloc(m, &P.gact, (size_t)kMaxBatch * K * c.inter * 4);
+    s = s ? s : pf_alloc(m, &P.gy, (size_t)kMaxBatch * K * H * 4);
+  }
+  if (s != MS_OK) {
+    for (void* q : P.allocs) cudaFree(q);
+    P = ms_model::Prefill();
+    return s;
+  }
+  P.cap = T;
+  return MS_OK;
+}
+
+// whether the batched prefill covers this model (else the prompt runs one decode step per token)
+bool pf_supported(const ms_model* m) {
+  const ms_model_config& c = m->cfg;
+  if (m->prefill_mode == 0) return false;
+  if (c.ep_size > 1 && !m->comm) return false;   // the peer-mailbox exchange is sized for one token
+  if (c.hidden % 32 || (c.heads * c.head_dim) % 32 || c.head_dim % 32 || c.head_dim > 256) return false;
+  return true;
+}
+
+// one batched pass over T <= kPrefillChunk tokens at positions [seq, seq + T)
+ms_status pf_chunk(ms_model* m, const int32_t* tokens, int T, bool last_chunk) {
+  const ms_model_config& c = m->cfg;
+  const DevCtx& dc = m->ctx->dc;
+  cudaStream_t s = m->ctx->stream;
+  auto& P = m->pf;
+  const int H = c.hidden, Dq = q_dim(c), Dkv = kv_dim(c), K = c.top_k, E = c.experts, pos0 = m->seq;
+  for (int i = 0; i < T; ++i) m->h_tok[i] = tokens[i];
+  MS_CUDA(m->ctx, cudaMemcpyAsync(P.tok, m->h_tok, (size_t)T * 4, cudaMemcpyHostToDevice, s));
+#define PCALL(call)                                                    \
+  do {                                                                 \
+    cudaError_t e_ = (call);                                           \
+    if (e_ != cudaSuccess) return cuda_fail(m->ctx, e_, #call);       \
+  } while (0)
+  PCALL(launch_pf_embed(dc, P.tok, T, m->embd, m->embd_q, H, c.vocab, P.h, m->L[0].attn_norm, c.eps, P.xq, P.xd, s));
+  for (int li = 0; li < c.layers; ++li) {
+    LayerW& Lw = m->L[li];
+    // Q/K/V of all tokens (Q8_0 weights x Q8_0 activations, 32 tokens per pass)
+    for (int c0 = 0; c0 < T; c0 += kMaxBatch) {
+      Q8BatchArgs qa;
+      qa.w = Lw.wqkv; qa.rows = Dq + 2 * Dkv; qa.cols = H; qa.B = std::min(kMaxBatch, T - c0);
+      qa.xq = P.xq + (size_t)c0 * H; qa.xd = P.xd + (size_t)c0 * (H / 32); qa.bias = Lw.bqkv;
+      qa.y = P.qkv + (size_t)c0 * (Dq + 2 * Dkv);
+      PCALL(launch_q8_gemm_batch(dc, qa, s));
+    }
+    PfAttnLaunch al;
+    al.qkv = P.qkv; al.q_norm = Lw.qn; al.k_norm = Lw.kn; al.eps = c.eps; al.cos_t = m->cos_t; al.sin_t = m->sin_t;
+    al.rot = c.rot_dim; al.pos0 = pos0; al.T = T; al.nh = c.heads; al.nkv = c.kv_heads; al.hd = c.head_dim;
+    al.kc = Lw.kc; al.vc = Lw.vc; al.cap = Lw.cap; al.window = Lw.window; al.sinks = Lw.sinks;
+    al.scale = (float)(1.0 / std::sqrt((double)c.head_dim)); al.q = P.q; al.kn = P.kn; al.vn = P.vn; al.out = P.attn;
+    PCALL(launch_pf_attention(dc, al, s));
+    // O projection into the residual stream
+    PCALL(launch_pf_quant(P.attn, (int64_t)T * Dq, P.xq, P.xd, s));
+    for (int c0 = 0; c0 < T; c0 += kMaxBatch) {
+      Q8BatchArgs oa;
+      oa.w = Lw.wo; oa.rows = H; oa.cols = Dq; oa.B = std::min(kMaxBatch, T - c0);
+      oa.xq = P.xq + (size_t)c0 * Dq; oa.xd = P.xd + (size_t)c0 * (Dq / 32); oa.bias = Lw.bo;
+      oa.residual = P.h + (size_t)c0 * H;
+      PCALL(launch_q8_gemm_batch(dc, oa, s));
+    }
+    // router of every token (RMSNorm, logits, dummy mask, top-k)
+    RouterArgs ra;
+    ra.h = P.h; ra.norm_w = Lw.post_norm; ra.eps = c.eps; ra.xn = P.xn; ra.w = Lw.router_w; ra.b = Lw.router_b;
+    ra.mask = Lw.mask; ra.logits = P.rlog; ra.idx = P.idx; ra.wts = P.wts; ra.counter = P.rcnt; ra.H = H; ra.E = E;
+    ra.K = K; ra.softmax_weight = c.arch == MS_ARCH_GPT_OSS; ra.normalize = c.norm_topk_prob; ra.batch = T;
+    PCALL(launch_router(dc, ra, s));
+    // experts: h += MoE(xn) (local experts; summed over the expert-parallel group by NCCL)
+    float* moe_dst = c.ep_size > 1 ? P.moe_y : P.h;
+    if (Lw.tc) {
+      PrefillArgs pa;
+      pa.gu = Lw.gu_tc; pa.down = Lw.down_tc; pa.gate_b = Lw.gate_b; pa.up_b = Lw.up_b; pa.down_b = Lw.down_b;
+      pa.x = P.xn; pa.idx = P.idx; pa.wts = P.wts; pa.out = moe_dst; pa.scratch = P.moe_scratch; pa.H = H;
+      pa.I = c.inter; pa.E = m->n_local; pa.K = K; pa.T = T; pa.expert_base = m->expert_base;
+      pa.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; pa.accumulate = c.ep_size > 1 ? 0 : 1;
+      pa.precise = m->prefill_mode == 1;
+      PCALL(launch_moe_prefill(dc, pa, s));
+    } else {
+      if (c.ep_size > 1) MS_CUDA(m->ctx, cudaMemsetAsync(P.moe_y, 0, (size_t)T * H * 4, s));
+      for (int c0 = 0; c0 < T; c0 += kMaxBatch) {
+        const int B = std::min(kMaxBatch, T - c0);
+        GroupMoeArgs ga;
+        ga.x = P.xn + (size_t)c0 * H; ga.idx = P.idx + (size_t)c0 * K; ga.B = B; ga.K = K; ga.H = H; ga.I = c.inter;
+        ga.gate_q = Lw.gate_q; ga.down_q = Lw.down_q; ga.gate = Lw.gate; ga.up = Lw.up; ga.down = Lw.down;
+        ga.gate_b = Lw.gate_b; ga.up_b = Lw.up_b; ga.down_b = Lw.down_b; ga.expert_base = m->expert_base;
+        ga.n_local = m->n_local; ga.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ga.grp = P.grp; ga.ent_slot = P.ent_slot;
+        ga.ent_of = P.ent_of; ga.act = P.gact; ga.y = P.gy;
+        for (int part = 0; part < 3; ++part) PCALL(launch_moe_group(dc, ga, part, s));
+        BatchCombine bc;
+        bc.y = P.gy; bc.ent_of = P.ent_of; bc.idx = P.idx + (size_t)c0 * K; bc.wts = P.wts + (size_t)c0 * K; bc.K = K;
+        PCALL(launch_resid_batch(dc, bc, moe_dst + (size_t)c0 * H, H, B, nullptr, c.eps, nullptr, nullptr, nullptr, s));
+      }
+    }
+    if (c.ep_size > 1) {
+      NcclApi* api = nccl_api();
+      ncclResult_t r = api->all_reduce(P.moe_y, P.moe_y, (size_t)T * H, ncclFloat32, ncclSum, m->comm, s);
+      if (r != ncclSuccess) return fail(m->ctx, MS_ERR_NCCL, "ncclAllReduce (prefill): %s", api->error_string(r));
+      PCALL(launch_pf_add(P.h, P.moe_y, (int64_t)T * H, s));
+    }
+    if (m->trace) {   // the last token's residual stream and router logits after this layer
+      MS_CUDA(m->ctx, cudaMemcpyAsync(m->trace_h + (size_t)li * H, P.h + (size_t)(T - 1) * H, (size_t)H * 4,
+                                      cudaMemcpyDeviceToDevice, s));
+      MS_CUDA(m->ctx, cudaMemcpyAsync(m->trace_logits + (size_t)li * E, P.rlog + (size_t)(T - 1) * E, (size_t)E * 4,
+                                      cudaMemcpyDeviceToDevice, s));
+    }
+    if (last_chunk) {   // routing of the last position (ms_model_last_routing)
+      MS_CUDA(m->ctx, cudaMemcpyAsync(Lw.idx, P.idx + (size_t)(T - 1) * K, (size_t)K * 4, cudaMemcpyDeviceToDevice, s));
+      MS_CUDA(m->ctx, cudaMemcpyAsync(Lw.wts, P.wts + (size_t)(T - 1) * K, (size_t)K * 4, cudaMemcpyDeviceToDevice, s));
+    }
+    if (li + 1 < c.layers) PCALL(launch_pf_norm_q8(P.h, T, H, m->L[li + 1].attn_norm, c.eps, P.xq, P.xd, s));
+  }
+  if (last_chunk) {   // final norm + LM head of the last position (engine.rs:1963-1987, 2033)
+    MS_CUDA(m->ctx, cudaMemsetAsync(&m->st->key, 0, sizeof(unsigned long long), s));
+    LmHeadArgs la;
+    la.w = m->out_w; la.x = P.h + (size_t)(T - 1) * H; la.norm_w = m->out_norm; la.eps = c.eps; la.bias = m->out_b;
+    la.logits = m->logits; la.key = &m->st->key; la.V = c.vocab; la.H = H; la.x_out = m->h_last;
+    PCALL(launch_lmhead(dc, la, s));
+  }
+#undef PCALL
+  // the token log and the step state continue after the prompt
+  MS_CUDA(m->ctx, cudaStreamSynchronize(s));
+  StepState st;
+  MS_CUDA(m->ctx, cudaMemcpy(&st, m->st, sizeof st, cudaMemcpyDeviceToHost));
+  const int room = std::max(0, std::min(T, c.max_seq_len - st.n_log));
+  if (room > 0) MS_CUDA(m->ctx, cudaMemcpy(m->token_log + st.n_log, tokens, (size_t)room * 4, cudaMemcpyHostToDevice));
+  st.n_log += T;
+  st.n_ctx = pos0 + T;
+  st.pos = pos0 + T - 1;
+  st.last_token = tokens[T - 1];
+  MS_CUDA(m->ctx, cudaMemcpy(m->st, &st, sizeof st, cudaMemcpyHostToDevice));
+  m->seq += T;
+  return MS_OK;
+}
+
+ms_status pf_forward(ms_model* m, const int32_t* tokens, int n) {
+  const int chunk = std::min(n, kPrefillChunk);
+  ms_status st = pf_reserve(m, chunk);
+  if (st != MS_OK) return st;
+  for (int i = 0; i < n; i += kPrefillChunk) {
+    const int t = std::min(kPrefillChunk, n - i);
+    st = pf_chunk(m, tokens + i, t, i + t == n);
+    if (st != MS_OK) return st;
+  }
   return MS_OK;
 }
 
@@ -1011,16 +1268,18 @@ ms_status ms_moe_mxfp4_decode_packed(ms_ctx* c, const void* gu, const void* down
 
 ms_status ms_moe_mxfp4_prefill_packed(ms_ctx* c, const void* gu, const void* down, const float* gb, const float* ub,
                                       const float* db, int H, int I, int E, int K, int arch, const float* x, int T,
-                                      const int32_t* idx, const float* wts, float* out) {
+                                      const int32_t* idx, const float* wts, float* out, int precise) {
   if (!c || !gu || !down || !x || !idx || !wts || !out || K <= 0 || K > 16 || E <= 0 || E > 256 || T <= 0)
     return MS_ERR_INVALID_ARG;
   if (!tc_supported(H, I)) return fail(c, MS_ERR_SHAPE, "moe prefill: hidden and inter must be multiples of 64");
-  ms_status s = ensure_scratch(c, pf_scratch_bytes(H, I, E, T, K), 64);
+  if (precise != 0 && precise != 1) return MS_ERR_INVALID_ARG;
+  ms_status s = ensure_scratch(c, pf_scratch_bytes(H, I, E, T, K, precise), 64);
   if (s != MS_OK) return s;
   PrefillArgs a;
   a.gu = (const uint8_t*)gu; a.down = (const uint8_t*)down; a.gate_b = gb; a.up_b = ub; a.down_b = db;
   a.x = x; a.idx = idx; a.wts = wts; a.out = out; a.scratch = c->scratch;
   a.H = H; a.I = I; a.E = E; a.K = K; a.T = T; a.expert_base = 0; a.oai_swiglu = arch == MS_ARCH_GPT_OSS;
+  a.precise = precise;
   MS_CUDA(c, launch_moe_prefill(c->dc, a, c->stream));
   return MS_OK;
 }
@@ -1073,7 +1332,11 @@ ms_status ms_attn_layer_decode(ms_ctx* c, const ms_attn_layer* L, int pos, float
   aa.od = (float*)(base + o_od);
   if (spl && rep % 4 == 0) aa.head_split = 4;
   else if (spl && rep % 2 == 0 && rep >= 4) aa.head_split = 2;
-  MS_CUDA(c, launch_attention(c->dc, aa, c->stream));
+  // order-independent attention (f64 reductions rounded once) where it has a kernel
+  if ((hd == 32 || hd == 64 || (hd == 128 && rep <= 8)) && 32 % rep == 0)
+    MS_CUDA(c, launch_exact_attention(c->dc, aa, range, c->stream));
+  else
+    MS_CUDA(c, launch_attention(c->dc, aa, c->stream));
   Q8GemvArgs oa;
   oa.w = (const uint8_t*)L->wo; oa.rows = H; oa.cols = Dq; oa.xq_in = aa.oq; oa.xd_in = aa.od; oa.bias = L->bo;
   oa.residual = h;
@@ -1160,6 +1423,7 @@ ms_status ms_model_create(ms_ctx* c, const ms_model_config* cfg, ms_model** out)
   m->L.resize(k.layers);
   m->n_local = k.experts / k.ep_size;
   if (const char* v = getenv("MS_MOE_TC")) m->use_tc = atoi(v) != 0;
+  if (const char* v = getenv("MS_EXACT")) m->exact = atoi(v) != 0;
   m->expert_base = k.ep_rank * m->n_local;
   *out = m;
   return MS_OK;
@@ -1264,6 +1528,11 @@ ms_status ms_model_finalize(ms_model* m) {
   s = s ? s : m->alloc(&m->st, sizeof(StepState));
   s = s ? s : m->alloc(&m->token_log, (size_t)(c.max_seq_len + 1) * 4);
   if (any_tc) {
+    m->ex_seg_gu = exact_seg_count(H / 32);
+    m->ex_seg_down = exact_seg_count(c.inter / 32);
+    m->ex_hpad = tc_down_tiles(H) * 128;
+    s = s ? s : m->alloc(&m->ex_gp, (size_t)c.top_k * m->ex_seg_gu * 2 * c.inter * 8);
+    s = s ? s : m->alloc(&m->ex_dp, (size_t)c.top_k * m->ex_seg_down * m->ex_hpad * 8);
     s = s ? s : m->alloc(&m->xterm, (size_t)tc_bterm_bytes(H / 32));
     s = s ? s : m->alloc(&m->act_terms, (size_t)c.top_k * tc_bterm_bytes(c.inter / 32));
     s = s ? s : m->alloc(&m->tc_part, (size_t)2 * tc_max_items(H, c.inter, c.top_k) * kTcMaxSeg * 128 * 4);
@@ -1518,6 +1787,7 @@ ms_status ms_model_destroy(ms_model* m) {
   for (void* p : m->ep_peer)
     if (p) cudaIpcCloseMemHandle(p);
   batch_free(m);
+  for (void* p : m->pf.allocs) cudaFree(p);
   for (void* p : m->allocs) cudaFree(p);
   if (m->h_tok) cudaFreeHost(m->h_tok);
   if (m->h_st) cudaFreeHost(m->h_st);
@@ -1567,6 +1837,15 @@ ms_status ms_model_forward(ms_model* m, const int32_t* tokens, int n, float* log
   for (int i = 0; i < n; ++i) {
     if (tokens[i] < 0 || tokens[i] >= m->cfg.vocab) return fail(m->ctx, MS_ERR_INVALID_ARG, "token %d out of range", tokens[i]);
     m->h_tok[i] = tokens[i];
+  }
+  if (n > 1 && pf_supported(m)) {
+    // the whole prompt in batched passes (engine.rs:1869-2006 with seq_len > 1)
+    ms_status st = set_feed(m, 0);
+    if (st != MS_OK) return st;
+    st = pf_forward(m, tokens, n);
+    if (st != MS_OK) return st;
+    if (logits) MS_CUDA(m->ctx, cudaMemcpyAsync(logits, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, s));
+    return ms_sync(m->ctx);
   }
   ms_status st = set_feed(m, 0);
   if (st != MS_OK) return st;
@@ -1663,6 +1942,22 @@ ms_status ms_model_last_routing(ms_model* m, int layer, int32_t* idx, float* wts
   MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
   MS_CUDA(m->ctx, cudaMemcpy(idx, m->L[layer].idx, (size_t)m->cfg.top_k * 4, cudaMemcpyDeviceToHost));
   MS_CUDA(m->ctx, cudaMemcpy(wts, m->L[layer].wts, (size_t)m->cfg.top_k * 4, cudaMemcpyDeviceToHost));
+  return MS_OK;
+}
+
+ms_status ms_model_set_exact(ms_model* m, int enable) {
+  if (!m) return MS_ERR_INVALID_ARG;
+  cudaSetDevice(m->ctx->device);
+  MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+  m->exact = enable != 0;
+  if (m->graph) { cudaGraphExecDestroy(m->graph); m->graph = nullptr; }
+  if (m->bt && m->bt->graph) { cudaGraphExecDestroy(m->bt->graph); m->bt->graph = nullptr; }
+  return MS_OK;
+}
+
+ms_status ms_model_set_prefill(ms_model* m, int mode) {
+  if (!m || mode < 0 || mode > 2) return MS_ERR_INVALID_ARG;
+  m->prefill_mode = mode;
   return MS_OK;
 }
 

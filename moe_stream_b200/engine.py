@@ -105,11 +105,12 @@ class Context:
                                                _ptr(idx), _ptr(wts), _ptr(h)), self.h)
 
     def moe_mxfp4_prefill_packed(self, gu_packed, down_packed, gate_b, up_b, down_b, hidden, inter, n_experts,
-                                 top_k, arch, x, n_tokens, idx, wts, out) -> None:
-        """Batched prefill of one MoE layer: grouped bf16 GEMM on the tensor cores (out = MoE(x))."""
+                                 top_k, arch, x, n_tokens, idx, wts, out, precise: bool = False) -> None:
+        """Batched prefill of one MoE layer: grouped bf16 GEMM on the tensor cores (out = MoE(x));
+        precise: activations as bf16 hi + lo pairs."""
         check(lib().ms_moe_mxfp4_prefill_packed(self.h, _ptr(gu_packed), _ptr(down_packed), _ptr(gate_b), _ptr(up_b),
                                                 _ptr(down_b), hidden, inter, n_experts, top_k, arch, _ptr(x),
-                                                n_tokens, _ptr(idx), _ptr(wts), _ptr(out)), self.h)
+                                                n_tokens, _ptr(idx), _ptr(wts), _ptr(out), int(bool(precise))), self.h)
 
     def rope(self, x, cos, sin, n_tokens: int, heads: int, head_dim: int, rot_dim: int, y) -> None:
         """y = RoPE(x) with per-token cos/sin rows (fused_rope_metal, metal/mod.rs:383-472)."""
@@ -357,6 +358,16 @@ class Engine:
         o = np.empty(self.config.vocab, dtype=np.float32)
         check(lib().ms_model_last_logits(self.h, o.ctypes.data_as(C.POINTER(C.c_float))), self.ctx.h)
         return o
+
+    def set_exact(self, enable: bool) -> None:
+        """Order-independent decode numerics (f64 reductions rounded once; default) or the
+        pipelined f32 kernels."""
+        check(lib().ms_model_set_exact(self.h, int(enable)), self.ctx.h)
+
+    def set_prefill(self, mode: int) -> None:
+        """Prompt handling of forward(): 1 batched (bf16 hi/lo expert GEMM, default), 2 batched
+        (plain bf16), 0 one decode step per token."""
+        check(lib().ms_model_set_prefill(self.h, int(mode)), self.ctx.h)
 
     def set_trace(self, enable: bool) -> None:
         """Copy each layer's output and router logits during later steps (parity diagnostics)."""

@@ -25,6 +25,17 @@
 namespace {
 
 // ---------------------------------------------------------------------------
+// Numeric convention.  Every f32 tensor op of the reference is evaluated as IEEE f32 (elementwise
+// add, mul, div, sqrt, min/max) and every reduction (matmul / dot, sum) and exp / log as the exact
+// value rounded once to f32: summed in double (the f32 x f32 products are exact in double), then
+// converted.  candle's own summation order is third-party and not pinned by any reference test;
+// rounding the exact result makes the oracle's values independent of summation order, so the CUDA
+// kernels (which also reduce in double) reproduce them bit for bit.
+inline float round_f32(double v) { return (float)v; }
+inline float expcr(float x) { return (float)std::exp((double)x); }
+inline float logcr(float x) { return (float)std::log((double)x); }
+
+// ---------------------------------------------------------------------------
 // threading: static row chunking across hardware threads (dequant.rs:650-692 style)
 int g_default_threads = 0;
 int hw_threads() {
@@ -217,9 +228,9 @@ void matmul_xwt(const float* x, int64_t n_tok, const float* W, int64_t rows, int
       const float* xt = x + t * cols;
       for (int64_t r = b; r < e; ++r) {
         const float* w = W + r * cols;
-        float acc = 0.0f;
-        for (int64_t c = 0; c < cols; ++c) acc += xt[c] * w[c];
-        y[t * rows + r] = acc;
+        double acc = 0.0;
+        for (int64_t c = 0; c < cols; ++c) acc += (double)xt[c] * (double)w[c];
+        y[t * rows + r] = round_f32(acc);
       }
     }
   });
@@ -250,14 +261,14 @@ void q8_0_gemv_actq(const uint8_t* w, int64_t rows, int64_t cols, const float* x
       const uint8_t* xt = xq.data() + t * rb;
       for (int64_t r = b; r < e; ++r) {
         const uint8_t* wr = w + r * rb;
-        float sumf = 0.0f;
+        double sumf = 0.0;
         for (int64_t k = 0; k < nb; ++k) {
           const uint8_t* wb = wr + k * 34; const uint8_t* xb = xt + k * 34;
           int32_t sumi = 0;
           for (int i = 0; i < 32; ++i) sumi += (int32_t)(int8_t)wb[2 + i] * (int32_t)(int8_t)xb[2 + i];
-          sumf += (float)sumi * h2f(rd16(wb)) * h2f(rd16(xb));
+          sumf += (double)sumi * (double)h2f(rd16(wb)) * (double)h2f(rd16(xb));   // exact in double
         }
-        y[t * rows + r] = sumf;
+        y[t * rows + r] = round_f32(sumf);
       }
     }
   });
@@ -267,30 +278,31 @@ void q8_0_gemv_actq(const uint8_t* w, int64_t rows, int64_t cols, const float* x
 void rms_norm(const float* x, const float* w, float* y, int64_t rows, int64_t dim, float eps) {
   for (int64_t r = 0; r < rows; ++r) {
     const float* xr = x + r * dim; float* yr = y + r * dim;
-    float ss = 0.0f;
-    for (int64_t i = 0; i < dim; ++i) ss += xr[i] * xr[i];
-    float var = ss / (float)dim;
-    float inv = 1.0f / std::sqrt(var + eps);
+    // x.sqr() (f32), mean_keepdim = sum * (1/n) (candle's affine), + eps, sqrt, recip
+    double ss = 0.0;
+    for (int64_t i = 0; i < dim; ++i) ss += (double)(xr[i] * xr[i]);
+    const float var = round_f32(ss) * (float)(1.0 / (double)dim) + 0.0f;
+    const float inv = 1.0f / std::sqrt(var + eps);
     for (int64_t i = 0; i < dim; ++i) yr[i] = (xr[i] * inv) * w[i];
   }
 }
 
 // ops/activation.rs:41-45
-inline float sigmoid_ref(float x) { return 1.0f / (std::exp(-x) + 1.0f); }
+inline float sigmoid_ref(float x) { return 1.0f / (expcr(-x) + 1.0f); }
 
 // ops/activation.rs:25-38
 void swiglu_oai(const float* g, const float* u, float* out, int64_t n, float alpha, float limit) {
   for (int64_t i = 0; i < n; ++i) {
     float gc = std::min(g[i], limit);
     float uc = std::min(std::max(u[i], -limit), limit);
-    float ga = gc * sigmoid_ref(gc * alpha);
+    float ga = gc * sigmoid_ref(gc * alpha + 0.0f);
     out[i] = ga * (uc + 1.0f);
   }
 }
 
 // ops/activation.rs:13-15 (candle_nn silu: x / (1 + exp(-x)))
 void silu_and_mul(const float* g, const float* u, float* out, int64_t n) {
-  for (int64_t i = 0; i < n; ++i) out[i] = (g[i] / (1.0f + std::exp(-g[i]))) * u[i];
+  for (int64_t i = 0; i < n; ++i) out[i] = (g[i] / (1.0f + expcr(-g[i]))) * u[i];
 }
 
 // layer.rs:2346-2403 (stable descending sort, ties -> lower index first)
@@ -305,20 +317,23 @@ void top_k_routing(const float* logits, int n_tok, int n_exp, int k, bool normal
       std::stable_sort(v.begin(), v.end(), desc);
       float mx = -std::numeric_limits<float>::infinity();
       for (int j = 0; j < k; ++j) mx = std::max(mx, v[j].second);
-      std::vector<float> ex(k); float sum = 0.0f;
-      for (int j = 0; j < k; ++j) { ex[j] = std::exp(v[j].second - mx); }
-      for (int j = 0; j < k; ++j) sum += ex[j];
+      std::vector<float> ex(k); double sum64 = 0.0;
+      for (int j = 0; j < k; ++j) { ex[j] = expcr(v[j].second - mx); }
+      for (int j = 0; j < k; ++j) sum64 += ex[j];
+      const float sum = round_f32(sum64);
       for (int j = 0; j < k; ++j) { idx[t * k + j] = v[j].first; wout[t * k + j] = ex[j] / sum; }
     } else {
       float mx = -std::numeric_limits<float>::infinity();
       for (int e = 0; e < n_exp; ++e) mx = std::max(mx, row[e]);
-      std::vector<float> ex(n_exp); float sum = 0.0f;
-      for (int e = 0; e < n_exp; ++e) ex[e] = std::exp(row[e] - mx);
-      for (int e = 0; e < n_exp; ++e) sum += ex[e];
+      std::vector<float> ex(n_exp); double sum64 = 0.0;
+      for (int e = 0; e < n_exp; ++e) ex[e] = expcr(row[e] - mx);
+      for (int e = 0; e < n_exp; ++e) sum64 += ex[e];
+      const float sum = round_f32(sum64);
       for (int e = 0; e < n_exp; ++e) v[e] = {e, ex[e] / sum};
       std::stable_sort(v.begin(), v.end(), desc);
-      float ts = 0.0f;
-      for (int j = 0; j < k; ++j) ts += v[j].second;
+      double ts64 = 0.0;
+      for (int j = 0; j < k; ++j) ts64 += v[j].second;
+      const float ts = round_f32(ts64);
       for (int j = 0; j < k; ++j) {
         idx[t * k + j] = v[j].first;
         wout[t * k + j] = normalize ? v[j].second / ts : v[j].second;
@@ -556,31 +571,35 @@ void sdpa(const float* q, const float* K, const float* V, int nh, int nkv, int n
       float mx = -INFINITY;
       for (int j = 0; j < Lk; ++j) {
         const float* kv = &K[((size_t)kvh * Lk + j) * hd];
-        float dot = 0.0f;
-        for (int d = 0; d < hd; ++d) dot += qv[d] * kv[d];
-        float s = dot * scale + 0.0f;
+        double dot = 0.0;
+        for (int d = 0; d < hd; ++d) dot += (double)qv[d] * (double)kv[d];
+        float s = round_f32(dot) * scale + 0.0f;
         bool masked = (causal && j > qabs) || (sw > 0 && qabs - j >= sw);
         if (masked) s = -INFINITY;
         sc[j] = s; mx = std::max(mx, s);
       }
       float denom = 0.0f;
+      double den64 = 0.0;
       if (sinks) {
         float sk = sinks[h];
         float mprime = ((mx + sk) + std::fabs(mx - sk)) * 0.5f;
-        for (int j = 0; j < Lk; ++j) sc[j] = std::exp(sc[j] - mprime);
-        for (int j = 0; j < Lk; ++j) denom += sc[j];
-        denom += std::exp(sk - mprime);
+        for (int j = 0; j < Lk; ++j) sc[j] = expcr(sc[j] - mprime);
+        for (int j = 0; j < Lk; ++j) den64 += sc[j];
+        denom = round_f32(den64) + expcr(sk - mprime);
       } else {
-        for (int j = 0; j < Lk; ++j) sc[j] = std::exp(sc[j] - mx);
-        for (int j = 0; j < Lk; ++j) denom += sc[j];
+        for (int j = 0; j < Lk; ++j) sc[j] = expcr(sc[j] - mx);
+        for (int j = 0; j < Lk; ++j) den64 += sc[j];
+        denom = round_f32(den64);
+      }
+      std::vector<double> acc(hd, 0.0);
+      for (int j = 0; j < Lk; ++j) {
+        const float p = sc[j] / denom;
+        if (p == 0.0f) continue;
+        const float* vv = &V[((size_t)kvh * Lk + j) * hd];
+        for (int d = 0; d < hd; ++d) acc[d] += (double)p * (double)vv[d];
       }
       float* o = &attn[((size_t)t * nh + h) * hd];
-      for (int d = 0; d < hd; ++d) o[d] = 0.0f;
-      for (int j = 0; j < Lk; ++j) {
-        float p = sc[j] / denom;
-        const float* vv = &V[((size_t)kvh * Lk + j) * hd];
-        for (int d = 0; d < hd; ++d) o[d] += p * vv[d];
-      }
+      for (int d = 0; d < hd; ++d) o[d] = round_f32(acc[d]);
     }
   });
 }
@@ -837,9 +856,9 @@ static void lm_head(orc_model* m, const float* hidden, float* logits) {
     std::vector<float> row(H);
     for (int64_t r = b; r < e; ++r) {
       dequant(m->out->qtype, m->out->data + r * rb, H, row.data());
-      float acc = 0.0f;
-      for (int i = 0; i < H; ++i) acc += last[i] * row[i];
-      logits[r] = m->out_bias ? acc + m->out_bias[r] : acc;
+      double acc = 0.0;
+      for (int i = 0; i < H; ++i) acc += (double)last[i] * (double)row[i];
+      logits[r] = m->out_bias ? round_f32(acc) + m->out_bias[r] : round_f32(acc);
     }
   });
 }

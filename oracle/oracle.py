@@ -248,6 +248,7 @@ class AttnState:
         self.V = np.zeros_like(self.K)
 
     def step(self, h: np.ndarray) -> np.ndarray:
+        """h + attention(RMSNorm(h)) at the next position"""
         pos = self.K.shape[1]
         z = np.zeros((self.K.shape[0], 1, self.K.shape[2]), np.float32)
         K = np.ascontiguousarray(np.concatenate([self.K, z], 1))
