@@ -315,6 +315,23 @@ struct ExactMoeArgs {
   int64_t gu_tile_bytes = 0, down_tile_bytes = 0;
 };
 int exact_seg_count(int kc);        // K segments over kc 32-element chunks
+// the same for K-quant experts in native blocks (Q4_K, or Q6_K repacked to 224-byte superblocks):
+// gate / up rows -> gu_out [K][2][I] (f32, rounded once, + bias), down rows -> y [K][H] (+ bias);
+// the consumer combines y (PendingCombine.partial) in ascending expert id
+struct ExactKqArgs {
+  const uint8_t* gate = nullptr;    // [E_local, I, H]
+  const uint8_t* up = nullptr;
+  const uint8_t* down = nullptr;    // [E_local, H, I]
+  int gate_fmt = Q_Q4_K, down_fmt = Q_Q6_K_PAD;
+  const float *gate_b = nullptr, *up_b = nullptr, *down_b = nullptr;
+  const float* x = nullptr;
+  const int* idx = nullptr;
+  int H = 0, I = 0, K = 0, expert_base = 0, n_local = 0, oai_swiglu = 0;
+  float* gu_out = nullptr;
+  float* y = nullptr;
+};
+bool exact_kq_supported(int gate_q, int down_q, int H, int I);
+cudaError_t launch_exact_kq_moe(const DevCtx& c, const ExactKqArgs& a, cudaStream_t s);
 cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a, cudaStream_t s);
 
 // ---- LM head / f16 GEMV ----

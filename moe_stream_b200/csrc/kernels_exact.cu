@@ -400,9 +400,134 @@ __global__ void __launch_bounds__(kEThreads) exact_down_kernel(ExactMoeArgs a, u
   (void)err;
 }
 
-template <class Kern>
-cudaError_t launch_pdl_x(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const ExactMoeArgs& a,
-                         uint32_t* err) {
+// ============================ experts (K-quant native blocks) ============================
+// A lane takes 64 elements of a row: group q (0..3) of a 256-element superblock -- Q4_K: the low
+// and high nibbles of 32 code bytes (sub-blocks 2q, 2q+1); Q6_K: element runs l and l + 64 (q even)
+// or l + 32 and l + 96 (q odd) of one half.  Element values are dequantized with the reference's
+// f32 op order (dequant.rs:218-262, 335-378), then dotted with x in double.
+__device__ __forceinline__ double kq_group_dot(int fmt, const uint8_t* blk, int q, const double* xs) {
+  double a0 = 0.0, a1 = 0.0;
+  if (fmt == Q_Q4_K) {
+    const float d = h2f_bits((uint16_t)(blk[0] | (blk[1] << 8)));
+    const float dmin = h2f_bits((uint16_t)(blk[2] | (blk[3] << 8)));
+    const uint8_t* sc = blk + 4;
+    const int is0 = 2 * q, is1 = 2 * q + 1;
+    uint32_t s0, m0, s1, m1;
+    if (is0 < 4) { s0 = sc[is0] & 63; m0 = sc[is0 + 4] & 63; }
+    else { s0 = (sc[is0 + 4] & 0xf) | ((sc[is0 - 4] >> 6) << 4); m0 = (sc[is0 + 4] >> 4) | ((sc[is0] >> 6) << 4); }
+    if (is1 < 4) { s1 = sc[is1] & 63; m1 = sc[is1 + 4] & 63; }
+    else { s1 = (sc[is1 + 4] & 0xf) | ((sc[is1 - 4] >> 6) << 4); m1 = (sc[is1 + 4] >> 4) | ((sc[is1] >> 6) << 4); }
+    const float d1 = __fmul_rn(d, (float)s0), mf1 = __fmul_rn(dmin, (float)m0);
+    const float d2 = __fmul_rn(d, (float)s1), mf2 = __fmul_rn(dmin, (float)m1);
+    const uint4* qp = reinterpret_cast<const uint4*>(blk + 16 + 32 * q);
+    const uint4 w0 = qp[0], w1 = qp[1];
+    const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    const double* xl = xs + 64 * q;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+#pragma unroll
+      for (int bi = 0; bi < 4; ++bi) {
+        const uint32_t byte = (wv[t] >> (8 * bi)) & 0xFFu;
+        const int l = 4 * t + bi;
+        const float lo = __fsub_rn(__fmul_rn(d1, (float)(byte & 0xF)), mf1);
+        const float hi = __fsub_rn(__fmul_rn(d2, (float)(byte >> 4)), mf2);
+        a0 = fma((double)lo, xl[l], a0);
+        a1 = fma((double)hi, xl[32 + l], a1);
+      }
+    }
+  } else {   // Q6_K (224-byte padded superblocks)
+    const float d = h2f_bits((uint16_t)(blk[208] | (blk[209] << 8)));
+    const int8_t* scv = reinterpret_cast<const int8_t*>(blk + 192);
+    const int half = q >> 1, sub = q & 1;
+    const uint8_t* ql = blk + half * 64 + 32 * sub;
+    const uint8_t* qh = blk + 128 + half * 32;
+    const double* xl = xs + half * 128 + 32 * sub;
+#pragma unroll 8
+    for (int l = 0; l < 32; ++l) {
+      const uint32_t lb = ql[l], hb = qh[l];
+      const int qa = (int)((lb & 0xF) | (((hb >> (2 * sub)) & 3) << 4)) - 32;
+      const int qb = (int)((lb >> 4) | (((hb >> (4 + 2 * sub)) & 3) << 4)) - 32;
+      const int isa = half * 8 + l / 16 + 2 * sub, isb = isa + 4;
+      const float va = __fmul_rn(__fmul_rn(d, (float)scv[isa]), (float)qa);
+      const float vb = __fmul_rn(__fmul_rn(d, (float)scv[isb]), (float)qb);
+      a0 = fma((double)va, xl[l], a0);
+      a1 = fma((double)vb, xl[64 + l], a1);
+    }
+  }
+  return a0 + a1;
+}
+
+constexpr int kKThreads = 256;
+
+// rows of one expert matrix (native K-quant blocks), G = cols / 64 lanes per row, 32 / G rows per
+// warp (one row and several groups per lane when cols > 2048); y[row] = round(dot) (+ bias)
+__device__ __forceinline__ void kq_rows(int fmt, const uint8_t* w, int64_t rb, int rows, int cols, const double* xs,
+                                        int row0, const float* bias, float* y, double* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = cols / 64, R = G >= 32 ? 1 : 32 / G;
+  const int sb_bytes = fmt == Q_Q4_K ? 144 : kQ6PadBytes;
+  const int sub = lane / (G >= 32 ? 32 : G), grp0 = lane % (G >= 32 ? 32 : G);
+  const int row = row0 + warp * R + sub;
+  double part = 0.0;
+  if (sub < R && row < rows) {
+    const uint8_t* wr = w + (int64_t)row * rb;
+    for (int gi = grp0; gi < G; gi += 32) part += kq_group_dot(fmt, wr + (gi >> 2) * sb_bytes, gi & 3, xs + 256 * (gi >> 2));
+  }
+  red[threadIdx.x] = part;
+  __syncwarp();
+  if (lane < R) {
+    const int r2 = row0 + warp * R + lane;
+    if (r2 < rows) {
+      const int gw = G >= 32 ? 32 : G;
+      double t = 0.0;
+      for (int i = 0; i < gw; ++i) t += red[warp * 32 + lane * gw + i];
+      float v = (float)t;
+      if (bias) v = __fadd_rn(v, bias[r2]);
+      y[r2] = v;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kKThreads) exact_kq_gu_kernel(ExactKqArgs a, uint32_t* err) {
+  extern __shared__ double xk[];   // [H]
+  __shared__ double red[kKThreads];
+  const int k = blockIdx.y, which = blockIdx.z;   // 0 gate, 1 up
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int e = a.idx[k] - a.expert_base;
+  if (e < 0 || e >= a.n_local) return;
+  for (int i = threadIdx.x; i < a.H; i += kKThreads) xk[i] = (double)a.x[i];
+  __syncthreads();
+  const int G = a.H / 64, R = G >= 32 ? 1 : 32 / G;
+  const int64_t rb = (int64_t)(a.H / 256) * (a.gate_fmt == Q_Q4_K ? 144 : kQ6PadBytes);
+  const uint8_t* w = (which ? a.up : a.gate) + (int64_t)e * a.I * rb;
+  const float* bias = which ? (a.up_b ? a.up_b + (size_t)e * a.I : nullptr) : (a.gate_b ? a.gate_b + (size_t)e * a.I : nullptr);
+  kq_rows(a.gate_fmt, w, rb, a.I, a.H, xk, blockIdx.x * (kKThreads / 32) * R, bias, a.gu_out + ((size_t)k * 2 + which) * a.I,
+          red);
+  (void)err;
+}
+
+__global__ void __launch_bounds__(kKThreads) exact_kq_down_kernel(ExactKqArgs a, uint32_t* err) {
+  extern __shared__ double ak[];   // [I] activations
+  __shared__ double red[kKThreads];
+  const int k = blockIdx.y;
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int e = a.idx[k] - a.expert_base;
+  if (e < 0 || e >= a.n_local) return;
+  const float* g = a.gu_out + (size_t)k * 2 * a.I;
+  for (int i = threadIdx.x; i < a.I; i += kKThreads) ak[i] = (double)act_exact(g[i], g[a.I + i], a.oai_swiglu);
+  __syncthreads();
+  const int G = a.I / 64, R = G >= 32 ? 1 : 32 / G;
+  const int64_t rb = (int64_t)(a.I / 256) * (a.down_fmt == Q_Q4_K ? 144 : kQ6PadBytes);
+  const uint8_t* w = a.down + (int64_t)e * a.H * rb;
+  kq_rows(a.down_fmt, w, rb, a.H, a.I, ak, blockIdx.x * (kKThreads / 32) * R,
+          a.down_b ? a.down_b + (size_t)e * a.H : nullptr, a.y + (size_t)k * a.H, red);
+  (void)err;
+}
+
+template <class Kern, class Args>
+cudaError_t launch_pdl_x(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const Args& a, uint32_t* err) {
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -459,6 +584,23 @@ cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a0, cudaStream
   if (e != cudaSuccess) return e;
   return launch_pdl_x(exact_down_kernel, dim3((unsigned)a.n_seg_down, (unsigned)tc_down_tiles(a.H), (unsigned)a.K),
                       dim3(kEThreads), (size_t)a.I * 8, s, a, c.err);
+}
+
+bool exact_kq_supported(int gate_q, int down_q, int H, int I) {
+  auto ok = [](int q) { return q == Q_Q4_K || q == Q_Q6_K_PAD; };
+  return ok(gate_q) && ok(down_q) && H % 256 == 0 && I % 256 == 0;
+}
+
+cudaError_t launch_exact_kq_moe(const DevCtx& c, const ExactKqArgs& a, cudaStream_t s) {
+  if (!exact_kq_supported(a.gate_fmt, a.down_fmt, a.H, a.I) || a.K < 1 || a.K > 16 || !a.gu_out || !a.y)
+    return cudaErrorInvalidValue;
+  auto rows_per_cta = [](int cols) { const int G = cols / 64; return (kKThreads / 32) * (G >= 32 ? 1 : 32 / G); };
+  const int rg = rows_per_cta(a.H), rd = rows_per_cta(a.I);
+  cudaError_t e = launch_pdl_x(exact_kq_gu_kernel, dim3((unsigned)((a.I + rg - 1) / rg), (unsigned)a.K, 2u),
+                               dim3(kKThreads), (size_t)a.H * 8, s, a, c.err);
+  if (e != cudaSuccess) return e;
+  return launch_pdl_x(exact_kq_down_kernel, dim3((unsigned)((a.H + rd - 1) / rd), (unsigned)a.K), dim3(kKThreads),
+                      (size_t)a.I * 8, s, a, c.err);
 }
 
 }  // namespace ms

@@ -261,6 +261,7 @@ struct ms_model {
   double* ex_gp = nullptr;          // [K][segments][2 I] gate/up partial dots
   double* ex_dp = nullptr;          // [K][segments][h_pad] down partial dots
   int ex_seg_gu = 0, ex_seg_down = 0, ex_hpad = 0;
+  float* ex_kgu = nullptr;          // K-quant experts: gate / up outputs [K][2][I]
   struct Prefill {
     int cap = 0;                       // tokens the buffers hold
     std::vector<void*> allocs;
@@ -550,18 +551,30 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     ma.tile_cnt = m->tile_cnt; ma.h = m->h; ma.H = H; ma.I = c.inter; ma.K = c.top_k;
     ma.expert_base = m->expert_base; ma.n_local = m->n_local; ma.oai_swiglu = c.arch == MS_ARCH_GPT_OSS;
     PendingCombine pc;
-    if (m->exact && Lw.tc) {
+    const bool exact_kq = m->exact && !Lw.tc && exact_kq_supported(Lw.gate_q, Lw.down_q, H, c.inter) &&
+                          Lw.up_q == Lw.gate_q;
+    if ((m->exact && Lw.tc) || exact_kq) {
       // order-independent experts: f64 partial dots; the combine (residual kernel, the peer-mailbox
       // send, or a combine kernel before the NCCL all-reduce) sums segments in ascending expert id
-      ExactMoeArgs ea;
-      ea.gu = Lw.gu_tc; ea.down = Lw.down_tc; ea.gate_b = Lw.gate_b; ea.up_b = Lw.up_b; ea.x = m->xn; ea.idx = Lw.idx;
-      ea.H = H; ea.I = c.inter; ea.K = c.top_k; ea.expert_base = m->expert_base; ea.n_local = m->n_local;
-      ea.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ea.gp = m->ex_gp; ea.dp = m->ex_dp; ea.n_seg_gu = m->ex_seg_gu;
-      ea.n_seg_down = m->ex_seg_down; ea.h_pad = m->ex_hpad;
-      LAUNCH(launch_exact_moe(dc, ea, s));
-      ++nk;   // gate/up, down
       PendingCombine lc;
-      lc.dpart = m->ex_dp; lc.down_b = Lw.down_b; lc.n_dseg = m->ex_seg_down; lc.dpad = m->ex_hpad;
+      if (Lw.tc) {
+        ExactMoeArgs ea;
+        ea.gu = Lw.gu_tc; ea.down = Lw.down_tc; ea.gate_b = Lw.gate_b; ea.up_b = Lw.up_b; ea.x = m->xn; ea.idx = Lw.idx;
+        ea.H = H; ea.I = c.inter; ea.K = c.top_k; ea.expert_base = m->expert_base; ea.n_local = m->n_local;
+        ea.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ea.gp = m->ex_gp; ea.dp = m->ex_dp; ea.n_seg_gu = m->ex_seg_gu;
+        ea.n_seg_down = m->ex_seg_down; ea.h_pad = m->ex_hpad;
+        LAUNCH(launch_exact_moe(dc, ea, s));
+        lc.dpart = m->ex_dp; lc.down_b = Lw.down_b; lc.n_dseg = m->ex_seg_down; lc.dpad = m->ex_hpad;
+      } else {
+        ExactKqArgs ka;
+        ka.gate = Lw.gate; ka.up = Lw.up; ka.down = Lw.down; ka.gate_fmt = Lw.gate_q; ka.down_fmt = Lw.down_q;
+        ka.gate_b = Lw.gate_b; ka.up_b = Lw.up_b; ka.down_b = Lw.down_b; ka.x = m->xn; ka.idx = Lw.idx; ka.H = H;
+        ka.I = c.inter; ka.K = c.top_k; ka.expert_base = m->expert_base; ka.n_local = m->n_local;
+        ka.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ka.gu_out = m->ex_kgu; ka.y = m->partial;
+        LAUNCH(launch_exact_kq_moe(dc, ka, s));
+        lc.partial = m->partial;
+      }
+      ++nk;   // gate/up, down
       lc.idx = Lw.idx; lc.wts = Lw.wts; lc.K = c.top_k; lc.expert_base = m->expert_base; lc.n_local = m->n_local;
       if (c.ep_size > 1 && m->ep_p2p) {
         const int n = c.ep_size;
@@ -1527,6 +1540,7 @@ ms_status ms_model_finalize(ms_model* m) {
   s = s ? s : m->alloc(&m->attn_cnt, (size_t)(4 * c.kv_heads + 16) * 4);
   s = s ? s : m->alloc(&m->st, sizeof(StepState));
   s = s ? s : m->alloc(&m->token_log, (size_t)(c.max_seq_len + 1) * 4);
+  s = s ? s : m->alloc(&m->ex_kgu, (size_t)c.top_k * 2 * c.inter * 4);
   if (any_tc) {
     m->ex_seg_gu = exact_seg_count(H / 32);
     m->ex_seg_down = exact_seg_count(c.inter / 32);
