@@ -327,10 +327,15 @@ struct ExactKqArgs {
   const float* x = nullptr;
   const int* idx = nullptr;
   int H = 0, I = 0, K = 0, expert_base = 0, n_local = 0, oai_swiglu = 0;
+  int B = 1;                        // tokens: x [B][H], idx [B][K], gu_out [B K][2][I], y [B K][H]
   float* gu_out = nullptr;
   float* y = nullptr;
 };
 bool exact_kq_supported(int gate_q, int down_q, int H, int I);
+// keys[b] = exact greedy token of sequence b: ids within a band of the approximate maximum of
+// logits [B][V] re-scored with f64 dots of the f16 rows w [V][H] and the normed xf [B][H]
+cudaError_t launch_exact_argmax_refine(const uint16_t* w, const float* xf, const float* bias, const float* logits,
+                                       int V, int H, int B, unsigned long long* keys, const DevCtx& c, cudaStream_t s);
 cudaError_t launch_exact_kq_moe(const DevCtx& c, const ExactKqArgs& a, cudaStream_t s);
 cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a, cudaStream_t s);
 

@@ -491,12 +491,13 @@ __device__ __forceinline__ void kq_rows(int fmt, const uint8_t* w, int64_t rb, i
 __global__ void __launch_bounds__(kKThreads) exact_kq_gu_kernel(ExactKqArgs a, uint32_t* err) {
   extern __shared__ double xk[];   // [H]
   __shared__ double red[kKThreads];
-  const int k = blockIdx.y, which = blockIdx.z;   // 0 gate, 1 up
+  const int which = blockIdx.z & 1, b = blockIdx.z >> 1;   // 0 gate, 1 up; token b
+  const int k = b * a.K + blockIdx.y;                       // (token, slot)
   pdl_wait_prior();
   pdl_launch_dependents();
   const int e = a.idx[k] - a.expert_base;
   if (e < 0 || e >= a.n_local) return;
-  for (int i = threadIdx.x; i < a.H; i += kKThreads) xk[i] = (double)a.x[i];
+  for (int i = threadIdx.x; i < a.H; i += kKThreads) xk[i] = (double)a.x[(size_t)b * a.H + i];
   __syncthreads();
   const int G = a.H / 64, R = G >= 32 ? 1 : 32 / G;
   const int64_t rb = (int64_t)(a.H / 256) * (a.gate_fmt == Q_Q4_K ? 144 : kQ6PadBytes);
@@ -510,7 +511,7 @@ __global__ void __launch_bounds__(kKThreads) exact_kq_gu_kernel(ExactKqArgs a, u
 __global__ void __launch_bounds__(kKThreads) exact_kq_down_kernel(ExactKqArgs a, uint32_t* err) {
   extern __shared__ double ak[];   // [I] activations
   __shared__ double red[kKThreads];
-  const int k = blockIdx.y;
+  const int k = blockIdx.z * a.K + blockIdx.y;               // (token, slot)
   pdl_wait_prior();
   pdl_launch_dependents();
   const int e = a.idx[k] - a.expert_base;
@@ -586,6 +587,82 @@ cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a0, cudaStream
                       dim3(kEThreads), (size_t)a.I * 8, s, a, c.err);
 }
 
+namespace {
+// Greedy token of each sequence from approximate logits: every id within `band` of the
+// approximate maximum is re-scored exactly (f64 dot of the f16 row with the normed x, rounded once,
+// + bias) by one warp each; the best exact value wins, ties to the lower id.  The approximate logits
+// carry errors far below `band`, so the exact maximum is always among the candidates.
+constexpr int kRefMaxCand = 64;
+__global__ void __launch_bounds__(256) exact_argmax_refine_kernel(const uint16_t* __restrict__ w,
+                                                                  const float* __restrict__ xf,
+                                                                  const float* __restrict__ bias, const float* logits,
+                                                                  int V, int H, unsigned long long* keys, uint32_t* err) {
+  __shared__ float s_max;
+  __shared__ float wm[8];
+  __shared__ int s_n;
+  __shared__ int s_cand[kRefMaxCand];
+  __shared__ unsigned long long s_best;
+  const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* lg = logits + (size_t)b * V;
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) m = fmaxf(m, lg[i]);
+  m = warp_max(m);
+  if (threadIdx.x == 0) { s_n = 0; s_best = 0ull; }
+  if (lane == 0) wm[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = -INFINITY;
+    for (int i = 0; i < 8; ++i) t = fmaxf(t, wm[i]);
+    s_max = t;
+  }
+  __syncthreads();
+  const float band = 1e-4f * fabsf(s_max) + 1e-5f;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    if (lg[i] >= s_max - band) {
+      const int slot = atomicAdd(&s_n, 1);
+      if (slot < kRefMaxCand) s_cand[slot] = i;
+      else atomicOr(err, EF_BAD_SHAPE);
+    }
+  }
+  __syncthreads();
+  const int n = min(s_n, kRefMaxCand);
+  const float* x = xf + (size_t)b * H;
+  for (int c = warp; c < n; c += 8) {
+    const int r = s_cand[c];
+    const __half* row = reinterpret_cast<const __half*>(w) + (size_t)r * H;
+    double acc = 0.0;
+    for (int i = lane; i < H; i += 32) acc = fma((double)__half2float(row[i]), (double)x[i], acc);
+    acc = warp_sum_d(acc);
+    if (lane == 0) {
+      float v = (float)acc;
+      if (bias) v = __fadd_rn(v, bias[r]);
+      uint32_t bits = __float_as_uint(v);
+      bits = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+      const unsigned long long key = ((unsigned long long)bits << 32) | (uint32_t)(0xffffffffu - (uint32_t)r);
+      atomicMax(&s_best, key);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) keys[b] = s_best;
+}
+}  // namespace
+
+cudaError_t launch_exact_argmax_refine(const uint16_t* w, const float* xf, const float* bias, const float* logits,
+                                       int V, int H, int B, unsigned long long* keys, const DevCtx& c, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)B);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, exact_argmax_refine_kernel, w, xf, bias, logits, V, H, keys, c.err);
+}
+
 bool exact_kq_supported(int gate_q, int down_q, int H, int I) {
   auto ok = [](int q) { return q == Q_Q4_K || q == Q_Q6_K_PAD; };
   return ok(gate_q) && ok(down_q) && H % 256 == 0 && I % 256 == 0;
@@ -596,11 +673,12 @@ cudaError_t launch_exact_kq_moe(const DevCtx& c, const ExactKqArgs& a, cudaStrea
     return cudaErrorInvalidValue;
   auto rows_per_cta = [](int cols) { const int G = cols / 64; return (kKThreads / 32) * (G >= 32 ? 1 : 32 / G); };
   const int rg = rows_per_cta(a.H), rd = rows_per_cta(a.I);
-  cudaError_t e = launch_pdl_x(exact_kq_gu_kernel, dim3((unsigned)((a.I + rg - 1) / rg), (unsigned)a.K, 2u),
+  if (a.B < 1) return cudaErrorInvalidValue;
+  cudaError_t e = launch_pdl_x(exact_kq_gu_kernel, dim3((unsigned)((a.I + rg - 1) / rg), (unsigned)a.K, 2u * a.B),
                                dim3(kKThreads), (size_t)a.H * 8, s, a, c.err);
   if (e != cudaSuccess) return e;
-  return launch_pdl_x(exact_kq_down_kernel, dim3((unsigned)((a.H + rd - 1) / rd), (unsigned)a.K), dim3(kKThreads),
-                      (size_t)a.I * 8, s, a, c.err);
+  return launch_pdl_x(exact_kq_down_kernel, dim3((unsigned)((a.H + rd - 1) / rd), (unsigned)a.K, (unsigned)a.B),
+                      dim3(kKThreads), (size_t)a.I * 8, s, a, c.err);
 }
 
 }  // namespace ms

@@ -188,6 +188,7 @@ struct BatchRt {
   int8_t *xq_h = nullptr, *xq_a = nullptr;
   float *xd_h = nullptr, *xd_a = nullptr;
   int *idx = nullptr, *grp = nullptr, *ent_slot = nullptr, *ent_of = nullptr;
+  int* ent_zero = nullptr;          // [B K] zeros: every (token, slot) entry local (exact experts)
   uint32_t *attn_cnt = nullptr, *router_cnt = nullptr;
   std::vector<float*> kc, vc;
   void* lm_scratch = nullptr;
@@ -993,7 +994,8 @@ ms_status enqueue_batch_step(ms_model* m, cudaStream_t s) {
     aa.hd = c.head_dim; aa.S = Lw.window ? b.S_swa : b.S_full; aa.spl = Lw.window ? b.spl_swa : b.spl_full;
     aa.scale = (float)(1.0 / std::sqrt((double)c.head_dim)); aa.oq = b.xq_a; aa.od = b.xd_a;
     aa.batch = B; aa.bs_qkv = Dq + 2 * Dkv; aa.bs_kv = (int64_t)c.kv_heads * Lw.cap * c.head_dim; aa.bs_out = Dq;
-    BLAUNCH(2, 1, launch_attention(dc, aa, s));
+    if (exact_attn_ok(m)) BLAUNCH(2, 1, launch_exact_attention(dc, aa, Lw.window ? Lw.cap : c.max_seq_len, s));
+    else BLAUNCH(2, 1, launch_attention(dc, aa, s));
     Q8BatchArgs oa;
     oa.w = Lw.wo; oa.rows = H; oa.cols = Dq; oa.B = B; oa.xq = b.xq_a; oa.xd = b.xd_a; oa.bias = Lw.bo;
     oa.residual = b.h;
@@ -1010,11 +1012,22 @@ ms_status enqueue_batch_step(ms_model* m, cudaStream_t s) {
     ga.up_b = Lw.up_b; ga.down_b = Lw.down_b; ga.expert_base = m->expert_base; ga.n_local = m->n_local;
     ga.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ga.grp = b.grp; ga.ent_slot = b.ent_slot; ga.ent_of = b.ent_of;
     ga.act = b.act; ga.y = b.y;
-    BLAUNCH(5, 1, launch_moe_group(dc, ga, 0, s));
-    BLAUNCH(6, 1, launch_moe_group(dc, ga, 1, s));
-    BLAUNCH(7, 1, launch_moe_group(dc, ga, 2, s));
     BatchCombine bc;
     bc.y = b.y; bc.ent_of = b.ent_of; bc.idx = b.idx; bc.wts = b.wts; bc.K = c.top_k;
+    if (m->exact && exact_kq_supported(Lw.gate_q, Lw.down_q, H, c.inter) && Lw.up_q == Lw.gate_q) {
+      // order-independent experts per (token, slot): y [B][K][H] with the bias, every entry local
+      ExactKqArgs ka;
+      ka.gate = Lw.gate; ka.up = Lw.up; ka.down = Lw.down; ka.gate_fmt = Lw.gate_q; ka.down_fmt = Lw.down_q;
+      ka.gate_b = Lw.gate_b; ka.up_b = Lw.up_b; ka.down_b = Lw.down_b; ka.x = b.xn; ka.idx = b.idx; ka.H = H;
+      ka.I = c.inter; ka.K = c.top_k; ka.expert_base = m->expert_base; ka.n_local = m->n_local;
+      ka.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ka.B = B; ka.gu_out = b.act; ka.y = b.y;
+      BLAUNCH(6, 2, launch_exact_kq_moe(dc, ka, s));
+      bc.ent_of = b.ent_zero;
+    } else {
+      BLAUNCH(5, 1, launch_moe_group(dc, ga, 0, s));
+      BLAUNCH(6, 1, launch_moe_group(dc, ga, 1, s));
+      BLAUNCH(7, 1, launch_moe_group(dc, ga, 2, s));
+    }
     const bool last = li + 1 == c.layers;
     BLAUNCH(8, 1, launch_resid_batch(dc, bc, b.h, H, B, last ? m->out_norm : m->L[li + 1].attn_norm, c.eps,
                                      last ? nullptr : b.xq_h, last ? nullptr : b.xd_h, last ? b.xf : nullptr, s));
@@ -1023,6 +1036,8 @@ ms_status enqueue_batch_step(ms_model* m, cudaStream_t s) {
   la.w = m->out_w; la.xf = b.xf; la.V = c.vocab; la.H = H; la.B = B; la.bias = m->out_b; la.scratch = b.lm_scratch;
   la.logits = b.logits; la.keys = b.keys;
   BLAUNCH(9, 3, launch_lmhead_batch(dc, la, s));   // prep, GEMM, key reduction
+  if (m->exact)   // exact re-scoring of the near-maximal ids (the greedy token, bit for bit)
+    BLAUNCH(9, 1, launch_exact_argmax_refine(m->out_w, b.xf, m->out_b, b.logits, c.vocab, H, B, b.keys, dc, s));
 #undef BLAUNCH
   b.kernels_per_step = nk;
   return MS_OK;
@@ -1613,7 +1628,8 @@ ms_status ms_model_batch_open(ms_model* m, int B) {
   s = s ? s : balloc(m, &b.grp, (size_t)group_table_words(B, c.top_k) * 4);
   s = s ? s : balloc(m, &b.ent_slot, (size_t)EK * 4);
   s = s ? s : balloc(m, &b.ent_of, (size_t)EK * 4);
-  s = s ? s : balloc(m, &b.act, (size_t)EK * c.inter * 4);
+  s = s ? s : balloc(m, &b.ent_zero, (size_t)EK * 4);
+  s = s ? s : balloc(m, &b.act, (size_t)EK * 2 * c.inter * 4);
   s = s ? s : balloc(m, &b.y, (size_t)EK * H * 4);
   s = s ? s : balloc(m, &b.xf, (size_t)B * H * 4);
   s = s ? s : balloc(m, &b.logits, (size_t)B * c.vocab * 4);

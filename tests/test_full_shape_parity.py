@@ -79,6 +79,8 @@ def _greedy_against_golden(eng, g, spec):
     report = {"ties": 0}
     bad = []
     eng.set_trace(True)
+    eng.set_exact(True)
+    eng.set_prefill(0)   # the prompt through the same order-independent decode step, one token at a time
     eng.clear_cache()
     tok = None
     for f in range(n):
