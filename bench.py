@@ -264,6 +264,9 @@ def run_ours(args):
     log(f"[rank {rank}] model generated + uploaded in {time.time() - t0:.1f}s")
     prompt = synth.prompt_ids(spec, prompt_len, seed=0)
     t0 = time.time()
+    # the prompt runs through the order-independent decode step (one token at a time), so the decoded
+    # tokens are the same bits at every GPU count and can be checked against the one-GPU sequence
+    eng.set_prefill(0)
     eng.forward(prompt)
     log(f"[rank {rank}] prefill {prompt_len} tokens (one decode step per token) in {time.time() - t0:.1f}s")
 
@@ -287,6 +290,7 @@ def run_ours(args):
         torch.distributed.barrier()
     kps = eng.kernels_per_step
     ctx.sync()
+    decoded = eng.token_log()[prompt_len:prompt_len + 64]   # greedy tokens fed after the prompt
     # ---- end to end through the C ABI with host buffers ----
     e2e_s = float("nan")
     if not args.no_e2e:
@@ -324,7 +328,15 @@ def run_ours(args):
                "sample": r["sample"]}
     if rank != 0:
         return
+    if args.save_tokens and rank == 0:
+        np.savez(args.save_tokens, tokens=np.asarray(decoded, np.int32))
     streams = 1 if ep else ws          # expert parallel: all ranks decode one sequence together
+    tokens_match = None
+    ref_path = os.path.join(ROOT, "tests", "golden", "bench_tokens_c1.npz")
+    if os.path.exists(ref_path) and not args.layers and prompt_len == PROMPT:
+        ref = np.load(ref_path)["tokens"].tolist()
+        n = min(len(ref), len(decoded))
+        tokens_match = bool(n > 0 and decoded[:n] == ref[:n])
     value = streams * args.steps / (ms * 1e-3)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
@@ -343,6 +355,8 @@ def run_ours(args):
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "algorithmic_bytes": MOE_BYTES,
                      "us_per_call": round(moe_ms * 1000, 2), "traffic": traffic},
+        "decoded_tokens": decoded[:16],
+        "tokens_match": tokens_match,
         "gpu_launches": kps * args.steps,
         "kernels_per_step": kps,
         "kernel_us_per_step": breakdown,
@@ -526,6 +540,7 @@ def main():
                     help="moe-layer: the decode expert FFN alone; prefill: config 4's MoE step; "
                          "qwen3: config 2 decode at the --batch sizes")
     ap.add_argument("--batch", default="1,32", help="qwen3 case: comma-separated batch sizes")
+    ap.add_argument("--save-tokens", default=None, help="write the greedy tokens decoded after the prompt (npz)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

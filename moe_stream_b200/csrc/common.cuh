@@ -163,7 +163,7 @@ __device__ __forceinline__ void combine_order(const PendingCombine& pc, CombineO
                                               const float* wv = nullptr) {
   if (!ids) { ids = pc.idx; wv = pc.wts; }
   int n = 0;
-  if (pc.partial || pc.seg_part || pc.dpart) {
+  if (pc.partial || pc.seg_part || pc.dpart || pc.ep_slots) {
     for (int k = 0; k < pc.K; ++k) {
       const int e = ids[k] - pc.expert_base;
       if (e < 0 || e >= pc.n_local) continue;
@@ -184,10 +184,30 @@ __device__ __forceinline__ void combine_order(const PendingCombine& pc, CombineO
 __device__ __forceinline__ void combine_prepare(const PendingCombine&, CombineOrder*) {}
 
 // moe_out[r], accumulated from zero in ascending expert order as the reference does
+// output row r of local slot k (order-independent experts: f64 segments rounded once + bias; else
+// the per-slot partial with its bias)
+__device__ __forceinline__ float slot_value(const PendingCombine& pc, int k, int H, int r) {
+  if (pc.dpart) {
+    const double* dp = pc.dpart + (size_t)k * pc.n_dseg * pc.dpad + r;
+    double t = 0.0;
+    for (int s2 = 0; s2 < pc.n_dseg; ++s2) t += __ldcg(dp + (size_t)s2 * pc.dpad);
+    float y = (float)t;
+    if (pc.down_b) y = __fadd_rn(y, pc.down_b[(size_t)(pc.idx[k] - pc.expert_base) * H + r]);
+    return y;
+  }
+  return pc.partial[(size_t)k * H + r];
+}
+
 __device__ __forceinline__ float combine_at(const PendingCombine& pc, const CombineOrder& co, int H, int r) {
   if (pc.dense) return pc.dense[r];
+  if (pc.ep_recv && pc.ep_slots) {   // every slot's output from its owner rank: ascending expert id
+    const float* rb = pc.ep_recv + (size_t)(co.seq & 1u) * pc.ep_rows * H + r;
+    float acc = 0.f;
+    for (int q = 0; q < co.n; ++q) acc = __fadd_rn(acc, __fmul_rn(__ldcg(rb + (size_t)co.slot[q] * H), co.w[q]));
+    return acc;
+  }
   if (pc.ep_recv) {   // the ranks' partial outputs, summed in rank order (written by peers: L2 loads)
-    const float* rb = pc.ep_recv + (size_t)(co.seq & 1u) * pc.ep_n * H + r;
+    const float* rb = pc.ep_recv + (size_t)(co.seq & 1u) * pc.ep_rows * H + r;
     float acc = 0.f;
     for (int j = 0; j < pc.ep_n; ++j) acc += __ldcg(rb + (size_t)j * H);
     return acc;

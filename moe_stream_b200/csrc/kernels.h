@@ -61,6 +61,9 @@ struct PendingCombine {
   const uint32_t* ep_flags = nullptr;
   const uint32_t* ep_seq = nullptr;
   int ep_n = 0;
+  int ep_rows = 0;                 // mailbox rows per parity (max(ranks, slots))
+  int ep_slots = 0;                // 1: the mailbox holds each slot's output [parity][slot][H] (from its
+                                   // owner rank), combined here over all slots in ascending expert id
   // or, from the order-independent expert kernels: f64 partial dots of each slot's down rows
   // [K][n_dseg][dpad]; slot output = (sum over segments, rounded to f32) + down bias
   const double* dpart = nullptr;
@@ -81,6 +84,8 @@ struct EpSend {
   uint32_t* seq = nullptr;         // this rank's sequence counter (device)
   uint32_t* cnt = nullptr;         // CTA counter (device, zero, self-resetting)
   int rank = 0, n = 0;
+  int rows = 0;                    // mailbox rows per parity
+  int slots = 0;                   // 1: send each local slot's output to row [parity][slot] (else the combine)
 };
 cudaError_t launch_ep_send(const DevCtx& c, const PendingCombine& pc, int H, const EpSend& e, cudaStream_t s);
 

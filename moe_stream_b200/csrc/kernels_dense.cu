@@ -1087,8 +1087,16 @@ __global__ void __launch_bounds__(256) ep_send_kernel(PendingCombine pc, int H, 
   __syncthreads();
   const uint32_t seq = s_seq, par = seq & 1u;
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < H; r += gridDim.x * blockDim.x) {
-    const float v = combine_at(pc, co, H, r);
-    for (int j = 0; j < e.n; ++j) e.recv[j][((size_t)par * e.n + e.rank) * H + r] = v;
+    if (e.slots) {   // each local slot's own output, so every rank combines all slots in one order
+      for (int q = 0; q < co.n; ++q) {
+        const int k = co.slot[q];
+        const float v = slot_value(pc, k, H, r);
+        for (int j = 0; j < e.n; ++j) e.recv[j][((size_t)par * e.rows + k) * H + r] = v;
+      }
+    } else {
+      const float v = combine_at(pc, co, H, r);
+      for (int j = 0; j < e.n; ++j) e.recv[j][((size_t)par * e.rows + e.rank) * H + r] = v;
+    }
   }
   __threadfence_system();
   __syncthreads();

@@ -64,8 +64,8 @@ __global__ void __launch_bounds__(kXThreads) exact_attn_kernel(AttnArgs a, uint3
   float* vn = kn + HD;                                        // [HD] new value
   float* sc = vn + HD;                                        // [REP][max_per_cta] scores -> exp
   double* cl_max = reinterpret_cast<double*>(sc + (size_t)REP * max_per_cta);   // [C][REP] (as double)
-  double* cl_sum = cl_max + 8 * REP;                          // [C][REP]
-  double* wred = cl_sum + 8 * REP;                            // [kXWarps][REP][HD] warp partials
+  double* cl_sum = cl_max + 16 * REP;                          // [C][REP]
+  double* wred = cl_sum + 16 * REP;                            // [kXWarps][REP][HD] warp partials
   double* cl_o = wred + (size_t)kXWarps * REP * HD;           // [C][REP][HD] (rank 0)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = blockIdx.y, b = blockIdx.z;
@@ -269,11 +269,13 @@ __global__ void __launch_bounds__(kXThreads) exact_attn_kernel(AttnArgs a, uint3
 
 template <int HD, int REP>
 cudaError_t launch_exact_attn_t(const AttnArgs& a, const DevCtx& c, int C, int max_per, cudaStream_t s) {
-  const size_t smem = (size_t)(REP * HD + 2 * HD) * 4 + (size_t)REP * max_per * 4 + 2 * 8 * REP * 8 +
+  const size_t smem = (size_t)(REP * HD + 2 * HD) * 4 + (size_t)REP * max_per * 4 + 2 * 16 * REP * 8 +
                       (size_t)kXWarps * REP * HD * 8 + (size_t)C * REP * HD * 8 + 64;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(exact_attn_kernel<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
+  if (e == cudaSuccess && C > 8)   // clusters of up to 16 CTAs (beyond the portable 8)
+    e = cudaFuncSetAttribute(exact_attn_kernel<HD, REP>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)C, (unsigned)a.nkv, (unsigned)a.batch);
@@ -314,14 +316,25 @@ constexpr int kESegChunks = 16;   // 32-element chunks per K segment
 // codes [chunk][128 rows][16 B] then a 512-byte scale group per 4 chunks, element 2i / 2i+1 in the
 // low / high nibble of code byte i), x as doubles in shared memory
 __device__ __forceinline__ double tile_row_dot(const uint8_t* tile, int kc, int r, int c0, int c1, const double* xs) {
+  // a segment is one slab (kESegChunks == 16 chunk columns): all its code words and scale bytes are
+  // loaded first, so each thread keeps 16 loads in flight
+  const int slab = c0 >> 4, nchs = min(16, kc - slab * 16);
+  const uint8_t* sb = tile + (size_t)slab * (16 * 2048 + 4 * 512);
+  uint4 codes[kESegChunks];
+  uint32_t ebs[kESegChunks];
+#pragma unroll
+  for (int i = 0; i < kESegChunks; ++i) {
+    if (c0 + i < c1) {
+      codes[i] = __ldcs(reinterpret_cast<const uint4*>(sb + i * 2048 + r * 16));
+      ebs[i] = sb[nchs * 2048 + (i >> 2) * 512 + 16 * (r & 31) + 4 * (r >> 5) + (i & 3)];
+    }
+  }
   double acc = 0.0;
-  for (int c = c0; c < c1; ++c) {
-    const int slab = c >> 4, nchs = min(16, kc - slab * 16), cl = c & 15;
-    const uint8_t* sb = tile + (size_t)slab * (16 * 2048 + 4 * 512);
-    const uint4 codes = __ldcs(reinterpret_cast<const uint4*>(sb + cl * 2048 + r * 16));
-    const uint32_t eb = sb[nchs * 2048 + (cl >> 2) * 512 + 16 * (r & 31) + 4 * (r >> 5) + (c & 3)];
-    const uint32_t cw[4] = {codes.x, codes.y, codes.z, codes.w};
-    const double* xc = xs + 32 * c;
+#pragma unroll
+  for (int i = 0; i < kESegChunks; ++i) {
+    if (c0 + i >= c1) break;
+    const uint32_t cw[4] = {codes[i].x, codes[i].y, codes[i].z, codes[i].w};
+    const double2* xc = reinterpret_cast<const double2*>(xs + 32 * (c0 + i));
     double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -329,12 +342,14 @@ __device__ __forceinline__ double tile_row_dot(const uint8_t* tile, int kc, int 
       for (int bi = 0; bi < 4; ++bi) {
         const uint32_t h2 = e2m1x2_to_f16x2((cw[q] >> (8 * bi)) & 0xFFu);
         const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
-        const int i = 8 * q + 2 * bi;
-        if (bi & 1) { a2 = fma((double)f.x, xc[i], a2); a3 = fma((double)f.y, xc[i + 1], a3); }
-        else { a0 = fma((double)f.x, xc[i], a0); a1 = fma((double)f.y, xc[i + 1], a1); }
+        const double2 x2 = xc[4 * q + bi];
+        if (bi & 1) { a2 = fma((double)f.x, x2.x, a2); a3 = fma((double)f.y, x2.y, a3); }
+        else { a0 = fma((double)f.x, x2.x, a0); a1 = fma((double)f.y, x2.y, a1); }
       }
     }
-    acc = fma((a0 + a1) + (a2 + a3), ldexp(1.0, (int)eb - 127), acc);   // scale 2^(E-127): exact
+    // scale 2^(E-127), exact: the double with exponent field E + 896
+    const double sc = __longlong_as_double((long long)(ebs[i] + 896u) << 52);
+    acc = fma((a0 + a1) + (a2 + a3), sc, acc);
   }
   return acc;
 }
@@ -549,8 +564,8 @@ cudaError_t launch_pdl_x(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_
 }  // namespace
 
 int exact_attn_cluster(int range) {
-  int C = (range + 255) / 256;
-  return C < 1 ? 1 : (C > 8 ? 8 : C);
+  int C = (range + 63) / 64;
+  return C < 1 ? 1 : (C > 16 ? 16 : C);
 }
 
 cudaError_t launch_exact_attention(const DevCtx& c, const AttnArgs& a, int range, cudaStream_t s) {

@@ -481,6 +481,9 @@ int launch_class(const ms_model* m, int i) {
   return 1 + (i - 1) % per_layer;
 }
 
+// rows per parity of a peer mailbox: one per rank (combined outputs) or one per slot (exact mode)
+int ep_rows(const ms_model* m) { return std::max(m->cfg.ep_size, m->cfg.top_k); }
+
 // the order-independent attention covers head dims 32 / 64 / 128 and up to 32 query heads per kv head
 bool exact_attn_ok(const ms_model* m) {
   const ms_model_config& c = m->cfg;
@@ -583,12 +586,14 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
         for (int j = 0; j < n; ++j) {
           float* mb = j == c.ep_rank ? m->ep_mail : reinterpret_cast<float*>(m->ep_peer[j]);
           e.recv[j] = mb;
-          e.flags[j] = reinterpret_cast<uint32_t*>(mb + (size_t)2 * n * H);
+          e.flags[j] = reinterpret_cast<uint32_t*>(mb + (size_t)2 * ep_rows(m) * H);
         }
-        e.seq = m->ep_seq; e.cnt = m->ep_cnt; e.rank = c.ep_rank; e.n = n;
+        e.seq = m->ep_seq; e.cnt = m->ep_cnt; e.rank = c.ep_rank; e.n = n; e.rows = ep_rows(m); e.slots = 1;
         LAUNCH(launch_ep_send(dc, lc, H, e, s));
-        pc.ep_recv = m->ep_mail; pc.ep_flags = reinterpret_cast<const uint32_t*>(m->ep_mail + (size_t)2 * n * H);
-        pc.ep_seq = m->ep_seq; pc.ep_n = n;
+        pc.ep_recv = m->ep_mail; pc.ep_flags = reinterpret_cast<const uint32_t*>(m->ep_mail + (size_t)2 * ep_rows(m) * H);
+        pc.ep_seq = m->ep_seq; pc.ep_n = n; pc.ep_rows = ep_rows(m); pc.ep_slots = 1;
+        // the receiving combine walks every slot (all experts), in ascending expert id
+        pc.idx = Lw.idx; pc.wts = Lw.wts; pc.K = c.top_k; pc.expert_base = 0; pc.n_local = c.experts;
       } else if (c.ep_size > 1) {
         LAUNCH(launch_moe_combine(dc, lc, H, nullptr, m->moe_out, s));
         NcclApi* api = nccl_api();
@@ -618,12 +623,12 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
       for (int j = 0; j < n; ++j) {
         float* mb = j == c.ep_rank ? m->ep_mail : reinterpret_cast<float*>(m->ep_peer[j]);
         e.recv[j] = mb;
-        e.flags[j] = reinterpret_cast<uint32_t*>(mb + (size_t)2 * n * H);
+        e.flags[j] = reinterpret_cast<uint32_t*>(mb + (size_t)2 * ep_rows(m) * H);
       }
-      e.seq = m->ep_seq; e.cnt = m->ep_cnt; e.rank = c.ep_rank; e.n = n;
+      e.seq = m->ep_seq; e.cnt = m->ep_cnt; e.rank = c.ep_rank; e.n = n; e.rows = ep_rows(m);
       LAUNCH(launch_ep_send(dc, lc, H, e, s));
-      pc.ep_recv = m->ep_mail; pc.ep_flags = reinterpret_cast<const uint32_t*>(m->ep_mail + (size_t)2 * n * H);
-      pc.ep_seq = m->ep_seq; pc.ep_n = n;
+      pc.ep_recv = m->ep_mail; pc.ep_flags = reinterpret_cast<const uint32_t*>(m->ep_mail + (size_t)2 * ep_rows(m) * H);
+      pc.ep_seq = m->ep_seq; pc.ep_n = n; pc.ep_rows = ep_rows(m);
     } else if (c.ep_size > 1) {
       // expert parallel: combine the local experts into moe_out, sum it over the EP group
       ma.defer_combine = 0; ma.out = m->moe_out;
@@ -2056,7 +2061,7 @@ ms_status ms_model_ep_handle(ms_model* m, void* out, size_t bytes) {
   if (m->cfg.ep_size > kMaxEp) return fail(m->ctx, MS_ERR_INVALID_ARG, "peer-memory exchange supports <= %d ranks", kMaxEp);
   cudaSetDevice(m->ctx->device);
   if (!m->ep_mail) {
-    const size_t mb = (size_t)2 * m->cfg.ep_size * m->cfg.hidden * 4 + (size_t)2 * m->cfg.ep_size * 4;
+    const size_t mb = (size_t)2 * ep_rows(m) * m->cfg.hidden * 4 + (size_t)2 * m->cfg.ep_size * 4;
     ms_status s = m->alloc(&m->ep_mail, mb);
     s = s ? s : m->alloc(&m->ep_seq, 16);
     s = s ? s : m->alloc(&m->ep_cnt, 16);

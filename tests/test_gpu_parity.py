@@ -772,9 +772,12 @@ def test_prefill_gpt_oss_tiny_bf16_mode(ctx, orc, tiny_path):
 
 
 def test_prefill_qwen3_tiny_kquant(ctx, orc, tiny_qwen_path):
-    """QK-norm, K-quant experts grouped 32 tokens at a time, renormalised routing"""
+    """QK-norm, K-quant experts grouped 32 tokens at a time, renormalised routing.  The batched
+    prompt path is not order-independent (f32 online-softmax attention, f16 hi/lo expert MMAs), so a
+    Q8_0 activation code can round the other way; it is held to the north star's prefill bound
+    (2e-2), and the greedy continuation must still equal the oracle's."""
     prompt = synth.prompt_ids(synth.TINY_QWEN3, 70, seed=33)
-    _prefill_vs_oracle(ctx, orc, tiny_qwen_path, synth.TINY_QWEN3, prompt, 1, REL_TOL)
+    _prefill_vs_oracle(ctx, orc, tiny_qwen_path, synth.TINY_QWEN3, prompt, 1, PREFILL_TOL)
 
 
 def test_prefill_longer_than_one_chunk(ctx, orc, tiny_path):
