@@ -83,6 +83,11 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return p;
 }
 
+// prefetch [p, p + bytes) of global memory into L2 (bytes a multiple of 16, p 16-byte aligned)
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // named barrier among `nthreads` threads (consumer warps only)
 __device__ __forceinline__ void named_bar(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

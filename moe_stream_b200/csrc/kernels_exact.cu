@@ -66,7 +66,7 @@ __global__ void __launch_bounds__(kXThreads) exact_attn_kernel(AttnArgs a, uint3
   double* cl_max = reinterpret_cast<double*>(sc + (size_t)REP * max_per_cta);   // [C][REP] (as double)
   double* cl_sum = cl_max + 16 * REP;                          // [C][REP]
   double* wred = cl_sum + 16 * REP;                            // [kXWarps][REP][HD] warp partials
-  double* cl_o = wred + (size_t)kXWarps * REP * HD;           // [C][REP][HD] (rank 0)
+  double* cl_o = wred + (size_t)kXWarps * REP * HD;           // [C][slice] (slice owners)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = blockIdx.y, b = blockIdx.z;
   const float* qkv = a.qkv + (size_t)b * a.bs_qkv;
@@ -74,13 +74,27 @@ __global__ void __launch_bounds__(kXThreads) exact_attn_kernel(AttnArgs a, uint3
   float* vc = a.vc + (size_t)b * a.bs_kv;
   const int Dq = a.nh * HD, Dkv = a.nkv * HD;
 
-  pdl_wait_prior();
-  pdl_launch_dependents();
+  // the position comes from the step's first kernel (at least two launches back), so it and the
+  // cached K/V rows of earlier positions may be read before waiting for the projections: this CTA's
+  // rows are prefetched into L2 while the previous kernel runs
   const int pos = *a.pos;
   const int lo = a.window > 0 ? max(0, pos - a.window + 1) : 0;
   const int range = pos - lo + 1;
   const int per = (range + C - 1) / C;
   const int p0 = lo + rank * per, p1 = min(pos + 1, p0 + per);   // this CTA's positions [p0, p1)
+  auto slot_of = [&](int p) { return a.window > 0 ? p % a.cap : p; };
+  if (threadIdx.x < 2 && p1 - 1 > p0) {
+    float* base = threadIdx.x == 0 ? kc : vc;
+    const int s0 = slot_of(p0), s1 = slot_of(p1 - 2);   // rows before pos (pos itself is new)
+    if (s1 >= s0) {
+      bulk_prefetch_l2(base + ((size_t)g * a.cap + s0) * HD, (uint32_t)(s1 - s0 + 1) * HD * 4u);
+    } else {   // the ring wraps
+      bulk_prefetch_l2(base + ((size_t)g * a.cap + s0) * HD, (uint32_t)(a.cap - s0) * HD * 4u);
+      bulk_prefetch_l2(base + (size_t)g * a.cap * HD, (uint32_t)(s1 + 1) * HD * 4u);
+    }
+  }
+  pdl_wait_prior();
+  pdl_launch_dependents();
   if (per > max_per_cta) {
     if (threadIdx.x == 0) atomicOr(err, EF_BAD_SHAPE);
   }
@@ -111,7 +125,6 @@ __global__ void __launch_bounds__(kXThreads) exact_attn_kernel(AttnArgs a, uint3
     __syncwarp();
   }
   __syncthreads();
-  auto slot_of = [&](int p) { return a.window > 0 ? p % a.cap : p; };
   // ---- scores: s = round(q . k) * scale (f64 dot), groups of G positions per warp ----
   double qd[REP][DPL];
 #pragma unroll
@@ -227,14 +240,14 @@ __global__ void __launch_bounds__(kXThreads) exact_attn_kernel(AttnArgs a, uint3
 #pragma unroll
     for (int d = 0; d < DPL; ++d) wred[((size_t)warp * REP + h) * HD + lane + 32 * d] = o[h][d];
   __syncthreads();
-  {
-    double* dst0 = cl.map_shared_rank(cl_o, 0);
-    for (int i = threadIdx.x; i < REP * HD; i += kXThreads) {
-      double t = 0.0;
+  // every CTA's partial P*V to the rank that owns its slice of the outputs (32-element multiples)
+  const int NS = min(C, REP * HD / 32), SL = REP * HD / NS;
+  for (int i = threadIdx.x; i < REP * HD; i += kXThreads) {
+    double t = 0.0;
 #pragma unroll
-      for (int w = 0; w < kXWarps; ++w) t += wred[(size_t)w * REP * HD + i];
-      dst0[(size_t)rank * REP * HD + i] = t;
-    }
+    for (int w = 0; w < kXWarps; ++w) t += wred[(size_t)w * REP * HD + i];
+    double* dst = cl.map_shared_rank(cl_o, i / SL);
+    dst[(size_t)rank * SL + i % SL] = t;
   }
   // the new key / value row goes to the cache once this CTA has read everything it needs
   if (p0 <= pos && pos < p1) {
@@ -244,25 +257,23 @@ __global__ void __launch_bounds__(kXThreads) exact_attn_kernel(AttnArgs a, uint3
     }
   }
   cl.sync();
-  if (rank != 0) return;
-  // ---- rank 0: the heads' outputs (rounded once) and their Q8_0 blocks for the O projection ----
-  float* outp = a.out + (size_t)b * a.bs_out + (size_t)g * REP * HD;
-  for (int i = threadIdx.x; i < REP * HD; i += kXThreads) {
+  if (rank >= NS) return;
+  // ---- the outputs of this rank's slice (rounded once) and their Q8_0 blocks for the O projection ----
+  const size_t o0 = (size_t)b * a.bs_out + (size_t)g * REP * HD + (size_t)rank * SL;
+  for (int j = threadIdx.x; j < SL; j += kXThreads) {
     double t = 0.0;
-    for (int r = 0; r < C; ++r) t += cl_o[(size_t)r * REP * HD + i];
+    for (int r = 0; r < C; ++r) t += cl_o[(size_t)r * SL + j];
     const float v = (float)t;
-    qs[i] = v;
-    outp[i] = v;
+    qs[j] = v;
+    a.out[o0 + j] = v;
   }
   __syncthreads();
   if (a.oq) {
-    const int nblk = REP * HD / 32;
-    for (int blk = threadIdx.x; blk < nblk; blk += kXThreads) {
+    for (int blk = threadIdx.x; blk < SL / 32; blk += kXThreads) {
       float v[32];
 #pragma unroll
       for (int k = 0; k < 32; ++k) v[k] = qs[32 * blk + k];
-      const size_t o0 = (size_t)b * a.bs_out + (size_t)g * REP * HD + 32 * (size_t)blk;
-      quantize_q8_block(v, a.oq + o0, &a.od[o0 / 32]);
+      quantize_q8_block(v, a.oq + o0 + 32 * blk, &a.od[(o0 + 32 * blk) / 32]);
     }
   }
 }
@@ -270,7 +281,7 @@ __global__ void __launch_bounds__(kXThreads) exact_attn_kernel(AttnArgs a, uint3
 template <int HD, int REP>
 cudaError_t launch_exact_attn_t(const AttnArgs& a, const DevCtx& c, int C, int max_per, cudaStream_t s) {
   const size_t smem = (size_t)(REP * HD + 2 * HD) * 4 + (size_t)REP * max_per * 4 + 2 * 16 * REP * 8 +
-                      (size_t)kXWarps * REP * HD * 8 + (size_t)C * REP * HD * 8 + 64;
+                      (size_t)kXWarps * REP * HD * 8 + (size_t)C * (REP * HD / std::min(C, REP * HD / 32)) * 8 + 64;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(exact_attn_kernel<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
@@ -315,60 +326,129 @@ constexpr int kESegChunks = 16;   // 32-element chunks per K segment
 // one row's dot over chunks [c0, c1) of a packed tile (tile layout: slabs of 16 chunk columns,
 // codes [chunk][128 rows][16 B] then a 512-byte scale group per 4 chunks, element 2i / 2i+1 in the
 // low / high nibble of code byte i), x as doubles in shared memory
-__device__ __forceinline__ double tile_row_dot(const uint8_t* tile, int kc, int r, int c0, int c1, const double* xs) {
-  // a segment is one slab (kESegChunks == 16 chunk columns): all its code words and scale bytes are
-  // loaded first, so each thread keeps 16 loads in flight
-  const int slab = c0 >> 4, nchs = min(16, kc - slab * 16);
-  const uint8_t* sb = tile + (size_t)slab * (16 * 2048 + 4 * 512);
-  uint4 codes[kESegChunks];
-  uint32_t ebs[kESegChunks];
+// ---- exact dots of MXFP4 rows on the integer tensor cores ----
+// x (f32) is written per 32-element block as X_j = round(x_j 2^F) with F = 180 - (the block's largest
+// biased exponent), so |X_j| < 2^54 and X carries every bit of the block's larger elements (smaller
+// ones lose bits below 2^-54 of the block maximum, as a double accumulation would).  X is split into
+// 7 signed base-256 digits; the MXFP4 codes become doubled e2m1 integers n in [-12, 12].  One
+// mma.sync.m16n8k32.s8 per (16 rows, 32 elements) then yields, exactly in int32, the 7 digit dots of
+// 16 rows (B column = digit); each lane folds its two digits into a double scaled by
+// 2^(E_w - 128 - F + 16t) and accumulates in double.
+struct Limbs {
+  int8_t* lim;   // [chunk][8 digits][32 elements]
+  int* F;        // [chunk]
+};
+
+// warp w writes the digits of chunks w, w + nw, ... of xs[32 c ..] (f32, 32 per chunk), n_ch chunks
+__device__ __forceinline__ void make_limbs(const float* xs, int n_ch, Limbs L, int warp, int nw, int lane) {
+  for (int i = warp; i < n_ch; i += nw) {
+    const float x = xs[32 * i + lane];
+    const int e = (int)((__float_as_uint(x) >> 23) & 0xFFu);
+    int eb = e;
 #pragma unroll
-  for (int i = 0; i < kESegChunks; ++i) {
-    if (c0 + i < c1) {
-      codes[i] = __ldcs(reinterpret_cast<const uint4*>(sb + i * 2048 + r * 16));
-      ebs[i] = sb[nchs * 2048 + (i >> 2) * 512 + 16 * (r & 31) + 4 * (r >> 5) + (i & 3)];
+    for (int o = 16; o > 0; o >>= 1) eb = max(eb, __shfl_xor_sync(0xffffffffu, eb, o));
+    const int F = 180 - eb;
+    const double p2 = __longlong_as_double((long long)(F + 1023) << 52);
+    long long X = __double2ll_rn((double)x * p2);
+#pragma unroll
+    for (int n = 0; n < 7; ++n) {
+      int d = (int)(X & 255);
+      if (d > 127) d -= 256;
+      X = (X - d) >> 8;
+      L.lim[(i * 8 + n) * 32 + lane] = (int8_t)d;
     }
+    L.lim[(i * 8 + 7) * 32 + lane] = 0;
+    if (lane == 0) L.F[i] = F;
   }
-  double acc = 0.0;
-#pragma unroll
-  for (int i = 0; i < kESegChunks; ++i) {
-    if (c0 + i >= c1) break;
-    const uint32_t cw[4] = {codes[i].x, codes[i].y, codes[i].z, codes[i].w};
-    const double2* xc = reinterpret_cast<const double2*>(xs + 32 * (c0 + i));
-    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-#pragma unroll
-      for (int bi = 0; bi < 4; ++bi) {
-        const uint32_t h2 = e2m1x2_to_f16x2((cw[q] >> (8 * bi)) & 0xFFu);
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
-        const double2 x2 = xc[4 * q + bi];
-        if (bi & 1) { a2 = fma((double)f.x, x2.x, a2); a3 = fma((double)f.y, x2.y, a3); }
-        else { a0 = fma((double)f.x, x2.x, a0); a1 = fma((double)f.y, x2.y, a1); }
-      }
-    }
-    // scale 2^(E-127), exact: the double with exponent field E + 896
-    const double sc = __longlong_as_double((long long)(ebs[i] + 896u) << 52);
-    acc = fma((a0 + a1) + (a2 + a3), sc, acc);
-  }
-  return acc;
 }
 
-// gate/up: grid (segments, gate_up tiles, slots); thread r of a tile = gate row (r < 64) or up row
+// four e2m1 codes (16 bits, element order low nibble first) -> four doubled values as int8
+__device__ __forceinline__ uint32_t e2m1x4_to_s8(uint32_t u) {
+  const uint32_t m7 = u & 0x7777u;
+  const uint32_t pos = __byte_perm(0x03020100u, 0x0C080604u, m7);   // 0 1 2 3 4 6 8 12
+  const uint32_t neg = __byte_perm(0xFDFEFF00u, 0xF4F8FAFCu, m7);   // their negatives
+  return __byte_perm(pos, neg, ((u >> 1) & 0x4444u) | 0x3210u);
+}
+
+__device__ __forceinline__ double i32_to_double(int v) {   // exact, on the FP64 pipe
+  const double magic = 6755399441055744.0;                   // 2^52 + 2^51
+  return __hiloint2double(0x43380000, v ^ 0x80000000) - (magic + 2147483648.0);
+}
+
+__device__ __forceinline__ void mma_s8_m16n8k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// rows rb .. rb+15 of a packed tile over chunks c0 .. c1 (one slab); returns, in lanes with
+// (lane & 3) == 0, the f64 dots of rows rb + (lane >> 2) (first) and rb + 8 + (lane >> 2) (second)
+__device__ __forceinline__ void tile_rows16_dot(const uint8_t* tile, int kc, int rb, int c0, int c1, Limbs L,
+                                                int lane, double& out0, double& out1) {
+  const int g = lane >> 2, t = lane & 3;
+  const int slab = c0 >> 4, nchs = min(16, kc - slab * 16);
+  const uint8_t* sb = tile + (size_t)slab * (16 * 2048 + 4 * 512);
+  const int r0 = rb + g, r1 = rb + g + 8;
+  double acc0 = 0.0, acc1 = 0.0;
+  const int sh = 16 * (t & 1), wo = 4 * (t >> 1);
+#pragma unroll 4
+  for (int i = 0; i < c1 - c0; ++i) {
+    const uint8_t* cb = sb + (size_t)i * 2048;
+    const uint32_t w00 = __ldcs(reinterpret_cast<const uint32_t*>(cb + r0 * 16 + wo));
+    const uint32_t w01 = __ldcs(reinterpret_cast<const uint32_t*>(cb + r0 * 16 + 8 + wo));
+    const uint32_t w10 = __ldcs(reinterpret_cast<const uint32_t*>(cb + r1 * 16 + wo));
+    const uint32_t w11 = __ldcs(reinterpret_cast<const uint32_t*>(cb + r1 * 16 + 8 + wo));
+    const uint8_t* scb = sb + nchs * 2048 + (i >> 2) * 512 + (i & 3);
+    const int e0 = scb[16 * (r0 & 31) + 4 * (r0 >> 5)], e1 = scb[16 * (r1 & 31) + 4 * (r1 >> 5)];
+    const int8_t* lb = L.lim + i * 256;
+    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(lb + g * 32 + 4 * t);
+    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(lb + g * 32 + 16 + 4 * t);
+    int d[4] = {0, 0, 0, 0};
+    mma_s8_m16n8k32(d, e2m1x4_to_s8(w00 >> sh), e2m1x4_to_s8(w10 >> sh), e2m1x4_to_s8(w01 >> sh),
+                    e2m1x4_to_s8(w11 >> sh), b0, b1);
+    const int F = L.F[i];
+    const double s0 = __longlong_as_double((long long)(e0 - 128 - F + 16 * t + 1023) << 52);
+    const double s1 = __longlong_as_double((long long)(e1 - 128 - F + 16 * t + 1023) << 52);
+    acc0 = fma(i32_to_double(d[0] + (d[1] << 8)), s0, acc0);   // digits 2t, 2t+1 of row r0
+    acc1 = fma(i32_to_double(d[2] + (d[3] << 8)), s1, acc1);
+  }
+  acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+  acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+  acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+  acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+  out0 = acc0;
+  out1 = acc1;
+}
+
+// gate/up: grid (segments, gate_up tiles, slots); 4 warps x 2 groups of 16 rows = the 128-row tile
+// (rows < 64 gate, >= 64 up)
 __global__ void __launch_bounds__(kEThreads) exact_gu_kernel(ExactMoeArgs a, uint32_t* err) {
-  extern __shared__ double xs[];   // this segment's slice of x as doubles (indexed from 0 .. H)
-  const int seg = blockIdx.x, mt = blockIdx.y, k = blockIdx.z, r = threadIdx.x;
+  __shared__ __align__(16) int8_t lim[kESegChunks * 256];
+  __shared__ int Fs[kESegChunks];
+  __shared__ float xs[kESegChunks * 32];
+  const int seg = blockIdx.x, mt = blockIdx.y, k = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kc = a.H / 32, c0 = seg * kESegChunks, c1 = min(kc, c0 + kESegChunks);
-  const int tiles = a.gu_tiles;
   pdl_wait_prior();
   pdl_launch_dependents();
   const int e = a.idx[k] - a.expert_base;
   if (e < 0 || e >= a.n_local) return;   // another rank's expert (or out of range: the combine skips it)
-  for (int i = 32 * c0 + threadIdx.x; i < 32 * c1; i += kEThreads) xs[i] = (double)a.x[i];
+  for (int i = threadIdx.x; i < 32 * (c1 - c0); i += kEThreads) xs[i] = a.x[32 * c0 + i];
   __syncthreads();
-  const uint8_t* tile = a.gu + ((size_t)e * tiles + mt) * (size_t)a.gu_tile_bytes;
-  const double d = tile_row_dot(tile, kc, r, c0, c1, xs);
-  a.gp[((size_t)k * a.n_seg_gu + seg) * (2 * a.I) + (size_t)mt * 128 + r] = d;
+  make_limbs(xs, c1 - c0, Limbs{lim, Fs}, warp, kEThreads / 32, lane);
+  __syncthreads();
+  const uint8_t* tile = a.gu + ((size_t)e * a.gu_tiles + mt) * (size_t)a.gu_tile_bytes;
+  double* gp = a.gp + ((size_t)k * a.n_seg_gu + seg) * (2 * a.I) + (size_t)mt * 128;
+  for (int grp = warp; grp < 8; grp += kEThreads / 32) {
+    double o0, o1;
+    tile_rows16_dot(tile, kc, 16 * grp, c0, c1, Limbs{lim, Fs}, lane, o0, o1);
+    if ((lane & 3) == 0) {
+      gp[16 * grp + (lane >> 2)] = o0;
+      gp[16 * grp + 8 + (lane >> 2)] = o1;
+    }
+  }
   (void)err;
 }
 
@@ -384,18 +464,21 @@ __device__ __forceinline__ float act_exact(float g, float u, int oai) {
 }
 
 // down: grid (segments, down tiles, slots).  The segment's activations are rebuilt from the gate/up
-// partial dots (sum of segments rounded once, + bias, activation) into shared memory first.
+// partial dots (sum of segments rounded once, + bias, activation) first.
 __global__ void __launch_bounds__(kEThreads) exact_down_kernel(ExactMoeArgs a, uint32_t* err) {
-  extern __shared__ double as[];
-  const int seg = blockIdx.x, mt = blockIdx.y, k = blockIdx.z, r = threadIdx.x;
+  __shared__ __align__(16) int8_t lim[kESegChunks * 256];
+  __shared__ int Fs[kESegChunks];
+  __shared__ float as[kESegChunks * 32];
+  const int seg = blockIdx.x, mt = blockIdx.y, k = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kc = a.I / 32, c0 = seg * kESegChunks, c1 = min(kc, c0 + kESegChunks);
-  const int tiles = a.down_tiles;
   pdl_wait_prior();
   pdl_launch_dependents();
   const int e = a.idx[k] - a.expert_base;
   if (e < 0 || e >= a.n_local) return;
   const double* gp = a.gp + (size_t)k * a.n_seg_gu * (2 * a.I);
-  for (int i = 32 * c0 + threadIdx.x; i < 32 * c1; i += kEThreads) {
+  for (int j = threadIdx.x; j < 32 * (c1 - c0); j += kEThreads) {
+    const int i = 32 * c0 + j;
     const int gr = (i >> 6) * 128 + (i & 63), ur = gr + 64;   // gate / up rows of activation i
     double gs = 0.0, us = 0.0;
     for (int s2 = 0; s2 < a.n_seg_gu; ++s2) {
@@ -405,13 +488,21 @@ __global__ void __launch_bounds__(kEThreads) exact_down_kernel(ExactMoeArgs a, u
     float gv = (float)gs, uv = (float)us;
     if (a.gate_b) gv = __fadd_rn(gv, a.gate_b[(size_t)e * a.I + i]);
     if (a.up_b) uv = __fadd_rn(uv, a.up_b[(size_t)e * a.I + i]);
-    as[i] = (double)act_exact(gv, uv, a.oai_swiglu);
+    as[j] = act_exact(gv, uv, a.oai_swiglu);
   }
   __syncthreads();
-  const uint8_t* tile = a.down + ((size_t)e * tiles + mt) * (size_t)a.down_tile_bytes;
-  const double d = tile_row_dot(tile, kc, r, c0, c1, as);
-  const int row = mt * 128 + r;
-  a.dp[((size_t)k * a.n_seg_down + seg) * a.h_pad + row] = d;
+  make_limbs(as, c1 - c0, Limbs{lim, Fs}, warp, kEThreads / 32, lane);
+  __syncthreads();
+  const uint8_t* tile = a.down + ((size_t)e * a.down_tiles + mt) * (size_t)a.down_tile_bytes;
+  double* dp = a.dp + ((size_t)k * a.n_seg_down + seg) * a.h_pad + (size_t)mt * 128;
+  for (int grp = warp; grp < 8; grp += kEThreads / 32) {
+    double o0, o1;
+    tile_rows16_dot(tile, kc, 16 * grp, c0, c1, Limbs{lim, Fs}, lane, o0, o1);
+    if ((lane & 3) == 0) {
+      dp[16 * grp + (lane >> 2)] = o0;
+      dp[16 * grp + 8 + (lane >> 2)] = o1;
+    }
+  }
   (void)err;
 }
 
@@ -563,9 +654,10 @@ cudaError_t launch_pdl_x(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_
 
 }  // namespace
 
-int exact_attn_cluster(int range) {
-  int C = (range + 63) / 64;
-  return C < 1 ? 1 : (C > 16 ? 16 : C);
+int exact_attn_cluster(int range) {   // a power of two, so the output slices divide evenly
+  int C = 1;
+  while (C < 16 && C * 64 < range) C *= 2;
+  return C;
 }
 
 cudaError_t launch_exact_attention(const DevCtx& c, const AttnArgs& a, int range, cudaStream_t s) {
@@ -596,10 +688,10 @@ cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a0, cudaStream
       a.h_pad < tc_down_tiles(a.H) * 128)
     return cudaErrorInvalidValue;
   cudaError_t e = launch_pdl_x(exact_gu_kernel, dim3((unsigned)a.n_seg_gu, (unsigned)tc_gu_tiles(a.I), (unsigned)a.K),
-                               dim3(kEThreads), (size_t)a.H * 8, s, a, c.err);
+                               dim3(kEThreads), 0, s, a, c.err);
   if (e != cudaSuccess) return e;
   return launch_pdl_x(exact_down_kernel, dim3((unsigned)a.n_seg_down, (unsigned)tc_down_tiles(a.H), (unsigned)a.K),
-                      dim3(kEThreads), (size_t)a.I * 8, s, a, c.err);
+                      dim3(kEThreads), 0, s, a, c.err);
 }
 
 namespace {
