@@ -357,6 +357,7 @@ struct LmHeadArgs {
   int V = 0, H = 0;
   int accumulate = 0;
   float* x_out = nullptr;             // effective x (before the norm) written by CTA 0, or null
+  float* xn_out = nullptr;            // x after the final norm (CTA 0), or null
 };
 cudaError_t launch_lmhead(const DevCtx& c, const LmHeadArgs& a, cudaStream_t s);
 int argmax_from_key(unsigned long long key);

@@ -917,8 +917,10 @@ __global__ void __launch_bounds__(kLWarps * 32, 1) lmhead_kernel(LmHeadArgs a) {
   float inv = 1.f;
   if (a.norm_w) inv = rms_inv_cr(xs, a.H, a.eps, threadIdx.x, blockDim.x, [] { __syncthreads(); });
   __syncthreads();
-  for (int i = threadIdx.x; i < a.H; i += blockDim.x)
+  for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
     xs[i] = a.norm_w ? __fmul_rn(__fmul_rn(xs[i], inv), a.norm_w[i]) : xs[i];
+    if (a.xn_out && blockIdx.x == 0) a.xn_out[i] = xs[i];
+  }
   __syncthreads();
   const int nch = a.H / 8;
   float xr[NCH][8];
@@ -940,20 +942,22 @@ __global__ void __launch_bounds__(kLWarps * 32, 1) lmhead_kernel(LmHeadArgs a) {
       if (ch < nch) wv[i] = __ldcs(wr + ch);
       else wv[i] = make_uint4(0, 0, 0, 0);
     }
-    double acc = 0.0;   // f16 x f32 products are exact in double
+    // f32 accumulation; with order-independent numerics the greedy token is then re-scored exactly
+    // among the near-maximal ids (launch_exact_argmax_refine)
+    float acc = 0.f;
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
       const uint32_t u[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[k]));
-        acc = fma((double)f.x, (double)xr[i][2 * k], acc);
-        acc = fma((double)f.y, (double)xr[i][2 * k + 1], acc);
+        acc = fmaf(f.x, xr[i][2 * k], acc);
+        acc = fmaf(f.y, xr[i][2 * k + 1], acc);
       }
     }
-    acc = warp_sum_d(acc);
+    acc = warp_sum(acc);
     if (lane == 0) {
-      float v = (float)acc;
+      float v = acc;
       if (a.bias) v = __fadd_rn(v, a.bias[r]);
       if (a.logits) { if (a.accumulate) v += a.logits[r]; a.logits[r] = v; }
       if (v == v) { const unsigned long long k = argmax_key(v, r); best = k > best ? k : best; }

@@ -320,7 +320,7 @@ cudaError_t launch_exact_attn_hd(const AttnArgs& a, const DevCtx& c, int rep, in
 }
 
 // ============================ experts (MXFP4 tensor-core tiles) ============================
-constexpr int kEThreads = 128;    // one thread per tile row
+constexpr int kEThreads = 256;    // 8 warps: one 16-row group of the 128-row tile each
 constexpr int kESegChunks = 16;   // 32-element chunks per K segment
 
 // one row's dot over chunks [c0, c1) of a packed tile (tile layout: slabs of 16 chunk columns,
@@ -393,24 +393,35 @@ __device__ __forceinline__ void tile_rows16_dot(const uint8_t* tile, int kc, int
   const int r0 = rb + g, r1 = rb + g + 8;
   double acc0 = 0.0, acc1 = 0.0;
   const int sh = 16 * (t & 1), wo = 4 * (t >> 1);
-#pragma unroll 4
-  for (int i = 0; i < c1 - c0; ++i) {
-    const uint8_t* cb = sb + (size_t)i * 2048;
-    const uint32_t w00 = __ldcs(reinterpret_cast<const uint32_t*>(cb + r0 * 16 + wo));
-    const uint32_t w01 = __ldcs(reinterpret_cast<const uint32_t*>(cb + r0 * 16 + 8 + wo));
-    const uint32_t w10 = __ldcs(reinterpret_cast<const uint32_t*>(cb + r1 * 16 + wo));
-    const uint32_t w11 = __ldcs(reinterpret_cast<const uint32_t*>(cb + r1 * 16 + 8 + wo));
-    const uint8_t* scb = sb + nchs * 2048 + (i >> 2) * 512 + (i & 3);
-    const int e0 = scb[16 * (r0 & 31) + 4 * (r0 >> 5)], e1 = scb[16 * (r1 & 31) + 4 * (r1 >> 5)];
+  const int n = c1 - c0;
+  // every code word and scale byte of the segment first (16 chunks x 4 words in flight per lane)
+  uint32_t w[kESegChunks][4];
+  int es[kESegChunks][2];
+#pragma unroll
+  for (int i = 0; i < kESegChunks; ++i) {
+    if (i < n) {
+      const uint8_t* cb = sb + (size_t)i * 2048;
+      w[i][0] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r0 * 16 + wo));
+      w[i][1] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r0 * 16 + 8 + wo));
+      w[i][2] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r1 * 16 + wo));
+      w[i][3] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r1 * 16 + 8 + wo));
+      const uint8_t* scb = sb + nchs * 2048 + (i >> 2) * 512 + (i & 3);
+      es[i][0] = scb[16 * (r0 & 31) + 4 * (r0 >> 5)];
+      es[i][1] = scb[16 * (r1 & 31) + 4 * (r1 >> 5)];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kESegChunks; ++i) {
+    if (i >= n) break;
     const int8_t* lb = L.lim + i * 256;
     const uint32_t b0 = *reinterpret_cast<const uint32_t*>(lb + g * 32 + 4 * t);
     const uint32_t b1 = *reinterpret_cast<const uint32_t*>(lb + g * 32 + 16 + 4 * t);
     int d[4] = {0, 0, 0, 0};
-    mma_s8_m16n8k32(d, e2m1x4_to_s8(w00 >> sh), e2m1x4_to_s8(w10 >> sh), e2m1x4_to_s8(w01 >> sh),
-                    e2m1x4_to_s8(w11 >> sh), b0, b1);
+    mma_s8_m16n8k32(d, e2m1x4_to_s8(w[i][0] >> sh), e2m1x4_to_s8(w[i][2] >> sh), e2m1x4_to_s8(w[i][1] >> sh),
+                    e2m1x4_to_s8(w[i][3] >> sh), b0, b1);
     const int F = L.F[i];
-    const double s0 = __longlong_as_double((long long)(e0 - 128 - F + 16 * t + 1023) << 52);
-    const double s1 = __longlong_as_double((long long)(e1 - 128 - F + 16 * t + 1023) << 52);
+    const double s0 = __longlong_as_double((long long)(es[i][0] - 128 - F + 16 * t + 1023) << 52);
+    const double s1 = __longlong_as_double((long long)(es[i][1] - 128 - F + 16 * t + 1023) << 52);
     acc0 = fma(i32_to_double(d[0] + (d[1] << 8)), s0, acc0);   // digits 2t, 2t+1 of row r0
     acc1 = fma(i32_to_double(d[2] + (d[3] << 8)), s1, acc1);
   }

@@ -263,6 +263,8 @@ struct ms_model {
   double* ex_dp = nullptr;          // [K][segments][h_pad] down partial dots
   int ex_seg_gu = 0, ex_seg_down = 0, ex_hpad = 0;
   float* ex_kgu = nullptr;          // K-quant experts: gate / up outputs [K][2][I]
+  float* xn_final = nullptr;        // the LM head's input after the final norm [H]
+  int head_start = 1;               // index of the step's first LM-head launch (profiling classes)
   struct Prefill {
     int cap = 0;                       // tokens the buffers hold
     std::vector<void*> allocs;
@@ -474,10 +476,9 @@ void rope_tables(int rot, int max_seq, double theta, std::vector<float>& cs, std
 
 // launch i of a step: 0 = embed, the last = LM head, else 1 + its position within the layer
 int launch_class(const ms_model* m, int i) {
-  const int kps = m->kernels_per_step;
-  const int per_layer = (kps - 2) / m->cfg.layers;
+  const int per_layer = (m->head_start - 1) / m->cfg.layers;
   if (i == 0) return 0;
-  if (i >= kps - 1) return 1 + per_layer;
+  if (i >= m->head_start) return 1 + per_layer;
   return 1 + (i - 1) % per_layer;
 }
 
@@ -666,10 +667,14 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
       if (e_ != cudaSuccess) return cuda_fail(m->ctx, e_, "trace copy");
     }
   }
+  m->head_start = nk;
   LmHeadArgs la;
   la.w = m->out_w; la.x = m->h; la.norm_w = m->out_norm; la.eps = c.eps; la.bias = m->out_b; la.logits = m->logits;
   la.key = &m->st->key; la.V = c.vocab; la.H = H; la.x_out = m->h_last;
+  if (m->exact) la.xn_out = m->xn_final;
   LAUNCH(launch_lmhead(dc, la, s));
+  if (m->exact)   // the greedy token from exact re-scoring of the near-maximal ids
+    LAUNCH(launch_exact_argmax_refine(m->out_w, m->xn_final, m->out_b, m->logits, c.vocab, H, 1, &m->st->key, dc, s));
 #undef LAUNCH
   m->kernels_per_step = nk;
   return MS_OK;
@@ -862,7 +867,10 @@ ms_status pf_chunk(ms_model* m, const int32_t* tokens, int T, bool last_chunk) {
     LmHeadArgs la;
     la.w = m->out_w; la.x = P.h + (size_t)(T - 1) * H; la.norm_w = m->out_norm; la.eps = c.eps; la.bias = m->out_b;
     la.logits = m->logits; la.key = &m->st->key; la.V = c.vocab; la.H = H; la.x_out = m->h_last;
+    if (m->exact) la.xn_out = m->xn_final;
     PCALL(launch_lmhead(dc, la, s));
+    if (m->exact)
+      PCALL(launch_exact_argmax_refine(m->out_w, m->xn_final, m->out_b, m->logits, c.vocab, H, 1, &m->st->key, dc, s));
   }
 #undef PCALL
   // the token log and the step state continue after the prompt
@@ -1561,6 +1569,7 @@ ms_status ms_model_finalize(ms_model* m) {
   s = s ? s : m->alloc(&m->st, sizeof(StepState));
   s = s ? s : m->alloc(&m->token_log, (size_t)(c.max_seq_len + 1) * 4);
   s = s ? s : m->alloc(&m->ex_kgu, (size_t)c.top_k * 2 * c.inter * 4);
+  s = s ? s : m->alloc(&m->xn_final, (size_t)H * 4);
   if (any_tc) {
     m->ex_seg_gu = exact_seg_count(H / 32);
     m->ex_seg_down = exact_seg_count(c.inter / 32);
@@ -2106,7 +2115,7 @@ ms_status ms_model_profile_step(ms_model* m, float* us, int max, int* n) {
   if (m->cfg.ep_size > 1) return fail(m->ctx, MS_ERR_STATE, "profiling is single-device only");
   cudaSetDevice(m->ctx->device);
   cudaStream_t s = m->ctx->stream, cs = m->ctx->own;
-  const int n_class = 2 + (m->kernels_per_step - 2) / m->cfg.layers;
+  const int n_class = 2 + (m->head_start - 1) / m->cfg.layers;
   constexpr int kWarm = 3, kRuns = 10;
   cudaEvent_t e0 = nullptr, e1 = nullptr;
   MS_CUDA(m->ctx, cudaEventCreate(&e0));
