@@ -339,8 +339,12 @@ struct ExactKqArgs {
 bool exact_kq_supported(int gate_q, int down_q, int H, int I);
 // keys[b] = exact greedy token of sequence b: ids within a band of the approximate maximum of
 // logits [B][V] re-scored with f64 dots of the f16 rows w [V][H] and the normed xf [B][H]
+// (keys[b] must hold the approximate argmax key of logits b on entry; scratch: exact_refine_scratch_ints(B)
+// ints, zero-initialised, self-resetting)
 cudaError_t launch_exact_argmax_refine(const uint16_t* w, const float* xf, const float* bias, const float* logits,
-                                       int V, int H, int B, unsigned long long* keys, const DevCtx& c, cudaStream_t s);
+                                       int V, int H, int B, unsigned long long* keys, int* scratch, const DevCtx& c,
+                                       cudaStream_t s);
+int exact_refine_scratch_ints(int B);
 cudaError_t launch_exact_kq_moe(const DevCtx& c, const ExactKqArgs& a, cudaStream_t s);
 cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a, cudaStream_t s);
 

@@ -321,7 +321,7 @@ cudaError_t launch_exact_attn_hd(const AttnArgs& a, const DevCtx& c, int rep, in
 
 // ============================ experts (MXFP4 tensor-core tiles) ============================
 constexpr int kEThreads = 256;    // 8 warps: one 16-row group of the 128-row tile each
-constexpr int kESegChunks = 16;   // 32-element chunks per K segment
+constexpr int kESegChunks = 8;    // 32-element chunks per K segment (within one 16-chunk slab)
 
 // one row's dot over chunks [c0, c1) of a packed tile (tile layout: slabs of 16 chunk columns,
 // codes [chunk][128 rows][16 B] then a 512-byte scale group per 4 chunks, element 2i / 2i+1 in the
@@ -385,31 +385,39 @@ __device__ __forceinline__ void mma_s8_m16n8k32(int (&d)[4], uint32_t a0, uint32
 
 // rows rb .. rb+15 of a packed tile over chunks c0 .. c1 (one slab); returns, in lanes with
 // (lane & 3) == 0, the f64 dots of rows rb + (lane >> 2) (first) and rb + 8 + (lane >> 2) (second)
-__device__ __forceinline__ void tile_rows16_dot(const uint8_t* tile, int kc, int rb, int c0, int c1, Limbs L,
-                                                int lane, double& out0, double& out1) {
-  const int g = lane >> 2, t = lane & 3;
-  const int slab = c0 >> 4, nchs = min(16, kc - slab * 16);
-  const uint8_t* sb = tile + (size_t)slab * (16 * 2048 + 4 * 512);
-  const int r0 = rb + g, r1 = rb + g + 8;
-  double acc0 = 0.0, acc1 = 0.0;
-  const int sh = 16 * (t & 1), wo = 4 * (t >> 1);
-  const int n = c1 - c0;
-  // every code word and scale byte of the segment first (16 chunks x 4 words in flight per lane)
+// Rows rb .. rb+15 of a packed tile over chunks [c0, c1) (inside one 16-chunk slab): the lane's
+// code words and scale bytes, loaded as soon as the expert is known ...
+struct Rows16 {
   uint32_t w[kESegChunks][4];
-  int es[kESegChunks][2];
+  uint32_t es[kESegChunks / 2];   // scale bytes of rows r0 / r1, two chunks per word
+};
+__device__ __forceinline__ void rows16_load(const uint8_t* tile, int kc, int rb, int c0, int c1, int lane, Rows16& R) {
+  const int g = lane >> 2, t = lane & 3;
+  const int slab = c0 >> 4, nchs = min(16, kc - slab * 16), cl0 = c0 & 15;
+  const uint8_t* sb = tile + (size_t)slab * (16 * 2048 + 4 * 512);
+  const int r0 = rb + g, r1 = rb + g + 8, wo = 4 * (t >> 1);
 #pragma unroll
   for (int i = 0; i < kESegChunks; ++i) {
-    if (i < n) {
-      const uint8_t* cb = sb + (size_t)i * 2048;
-      w[i][0] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r0 * 16 + wo));
-      w[i][1] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r0 * 16 + 8 + wo));
-      w[i][2] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r1 * 16 + wo));
-      w[i][3] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r1 * 16 + 8 + wo));
-      const uint8_t* scb = sb + nchs * 2048 + (i >> 2) * 512 + (i & 3);
-      es[i][0] = scb[16 * (r0 & 31) + 4 * (r0 >> 5)];
-      es[i][1] = scb[16 * (r1 & 31) + 4 * (r1 >> 5)];
+    if (c0 + i < c1) {
+      const int cl = cl0 + i;
+      const uint8_t* cb = sb + (size_t)cl * 2048;
+      R.w[i][0] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r0 * 16 + wo));
+      R.w[i][1] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r0 * 16 + 8 + wo));
+      R.w[i][2] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r1 * 16 + wo));
+      R.w[i][3] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r1 * 16 + 8 + wo));
+      const uint8_t* scb = sb + nchs * 2048 + (cl >> 2) * 512 + (cl & 3);
+      const uint32_t e2 = (uint32_t)scb[16 * (r0 & 31) + 4 * (r0 >> 5)] | ((uint32_t)scb[16 * (r1 & 31) + 4 * (r1 >> 5)] << 8);
+      if (i & 1) R.es[i >> 1] |= e2 << 16;
+      else R.es[i >> 1] = e2;
     }
   }
+}
+
+// ... then, once the activation digits are in shared memory, the dots: returns, in lanes with
+// (lane & 3) == 0, the f64 dots of rows rb + (lane >> 2) (out0) and rb + 8 + (lane >> 2) (out1)
+__device__ __forceinline__ void rows16_dot(const Rows16& R, int n, Limbs L, int lane, double& out0, double& out1) {
+  const int g = lane >> 2, t = lane & 3, sh = 16 * (t & 1);
+  double acc0 = 0.0, acc1 = 0.0;
 #pragma unroll
   for (int i = 0; i < kESegChunks; ++i) {
     if (i >= n) break;
@@ -417,11 +425,13 @@ __device__ __forceinline__ void tile_rows16_dot(const uint8_t* tile, int kc, int
     const uint32_t b0 = *reinterpret_cast<const uint32_t*>(lb + g * 32 + 4 * t);
     const uint32_t b1 = *reinterpret_cast<const uint32_t*>(lb + g * 32 + 16 + 4 * t);
     int d[4] = {0, 0, 0, 0};
-    mma_s8_m16n8k32(d, e2m1x4_to_s8(w[i][0] >> sh), e2m1x4_to_s8(w[i][2] >> sh), e2m1x4_to_s8(w[i][1] >> sh),
-                    e2m1x4_to_s8(w[i][3] >> sh), b0, b1);
+    mma_s8_m16n8k32(d, e2m1x4_to_s8(R.w[i][0] >> sh), e2m1x4_to_s8(R.w[i][2] >> sh), e2m1x4_to_s8(R.w[i][1] >> sh),
+                    e2m1x4_to_s8(R.w[i][3] >> sh), b0, b1);
     const int F = L.F[i];
-    const double s0 = __longlong_as_double((long long)(es[i][0] - 128 - F + 16 * t + 1023) << 52);
-    const double s1 = __longlong_as_double((long long)(es[i][1] - 128 - F + 16 * t + 1023) << 52);
+    const uint32_t e2 = R.es[i >> 1] >> (16 * (i & 1));
+    const int e0 = (int)(e2 & 0xFFu), e1 = (int)((e2 >> 8) & 0xFFu);
+    const double s0 = __longlong_as_double((long long)(e0 - 128 - F + 16 * t + 1023) << 52);
+    const double s1 = __longlong_as_double((long long)(e1 - 128 - F + 16 * t + 1023) << 52);
     acc0 = fma(i32_to_double(d[0] + (d[1] << 8)), s0, acc0);   // digits 2t, 2t+1 of row r0
     acc1 = fma(i32_to_double(d[2] + (d[3] << 8)), s1, acc1);
   }
@@ -433,9 +443,9 @@ __device__ __forceinline__ void tile_rows16_dot(const uint8_t* tile, int kc, int
   out1 = acc1;
 }
 
-// gate/up: grid (segments, gate_up tiles, slots); 4 warps x 2 groups of 16 rows = the 128-row tile
-// (rows < 64 gate, >= 64 up)
-__global__ void __launch_bounds__(kEThreads) exact_gu_kernel(ExactMoeArgs a, uint32_t* err) {
+// gate/up: grid (segments, gate_up tiles, slots); 8 warps = the 8 groups of 16 rows of a 128-row
+// tile (rows < 64 gate, >= 64 up)
+__global__ void __launch_bounds__(kEThreads, 3) exact_gu_kernel(ExactMoeArgs a, uint32_t* err) {
   __shared__ __align__(16) int8_t lim[kESegChunks * 256];
   __shared__ int Fs[kESegChunks];
   __shared__ float xs[kESegChunks * 32];
@@ -446,19 +456,19 @@ __global__ void __launch_bounds__(kEThreads) exact_gu_kernel(ExactMoeArgs a, uin
   pdl_launch_dependents();
   const int e = a.idx[k] - a.expert_base;
   if (e < 0 || e >= a.n_local) return;   // another rank's expert (or out of range: the combine skips it)
+  const uint8_t* tile = a.gu + ((size_t)e * a.gu_tiles + mt) * (size_t)a.gu_tile_bytes;
+  Rows16 R;
+  rows16_load(tile, kc, 16 * warp, c0, c1, lane, R);
   for (int i = threadIdx.x; i < 32 * (c1 - c0); i += kEThreads) xs[i] = a.x[32 * c0 + i];
   __syncthreads();
   make_limbs(xs, c1 - c0, Limbs{lim, Fs}, warp, kEThreads / 32, lane);
   __syncthreads();
-  const uint8_t* tile = a.gu + ((size_t)e * a.gu_tiles + mt) * (size_t)a.gu_tile_bytes;
-  double* gp = a.gp + ((size_t)k * a.n_seg_gu + seg) * (2 * a.I) + (size_t)mt * 128;
-  for (int grp = warp; grp < 8; grp += kEThreads / 32) {
-    double o0, o1;
-    tile_rows16_dot(tile, kc, 16 * grp, c0, c1, Limbs{lim, Fs}, lane, o0, o1);
-    if ((lane & 3) == 0) {
-      gp[16 * grp + (lane >> 2)] = o0;
-      gp[16 * grp + 8 + (lane >> 2)] = o1;
-    }
+  double o0, o1;
+  rows16_dot(R, c1 - c0, Limbs{lim, Fs}, lane, o0, o1);
+  if ((lane & 3) == 0) {
+    double* gp = a.gp + ((size_t)k * a.n_seg_gu + seg) * (2 * a.I) + (size_t)mt * 128 + 16 * warp;
+    gp[lane >> 2] = o0;
+    gp[8 + (lane >> 2)] = o1;
   }
   (void)err;
 }
@@ -476,7 +486,7 @@ __device__ __forceinline__ float act_exact(float g, float u, int oai) {
 
 // down: grid (segments, down tiles, slots).  The segment's activations are rebuilt from the gate/up
 // partial dots (sum of segments rounded once, + bias, activation) first.
-__global__ void __launch_bounds__(kEThreads) exact_down_kernel(ExactMoeArgs a, uint32_t* err) {
+__global__ void __launch_bounds__(kEThreads, 3) exact_down_kernel(ExactMoeArgs a, uint32_t* err) {
   __shared__ __align__(16) int8_t lim[kESegChunks * 256];
   __shared__ int Fs[kESegChunks];
   __shared__ float as[kESegChunks * 32];
@@ -487,14 +497,17 @@ __global__ void __launch_bounds__(kEThreads) exact_down_kernel(ExactMoeArgs a, u
   pdl_launch_dependents();
   const int e = a.idx[k] - a.expert_base;
   if (e < 0 || e >= a.n_local) return;
+  const uint8_t* tile = a.down + ((size_t)e * a.down_tiles + mt) * (size_t)a.down_tile_bytes;
+  Rows16 R;
+  rows16_load(tile, kc, 16 * warp, c0, c1, lane, R);
   const double* gp = a.gp + (size_t)k * a.n_seg_gu * (2 * a.I);
   for (int j = threadIdx.x; j < 32 * (c1 - c0); j += kEThreads) {
     const int i = 32 * c0 + j;
     const int gr = (i >> 6) * 128 + (i & 63), ur = gr + 64;   // gate / up rows of activation i
     double gs = 0.0, us = 0.0;
     for (int s2 = 0; s2 < a.n_seg_gu; ++s2) {
-      gs += gp[(size_t)s2 * (2 * a.I) + gr];
-      us += gp[(size_t)s2 * (2 * a.I) + ur];
+      gs += __ldcg(gp + (size_t)s2 * (2 * a.I) + gr);
+      us += __ldcg(gp + (size_t)s2 * (2 * a.I) + ur);
     }
     float gv = (float)gs, uv = (float)us;
     if (a.gate_b) gv = __fadd_rn(gv, a.gate_b[(size_t)e * a.I + i]);
@@ -504,15 +517,12 @@ __global__ void __launch_bounds__(kEThreads) exact_down_kernel(ExactMoeArgs a, u
   __syncthreads();
   make_limbs(as, c1 - c0, Limbs{lim, Fs}, warp, kEThreads / 32, lane);
   __syncthreads();
-  const uint8_t* tile = a.down + ((size_t)e * a.down_tiles + mt) * (size_t)a.down_tile_bytes;
-  double* dp = a.dp + ((size_t)k * a.n_seg_down + seg) * a.h_pad + (size_t)mt * 128;
-  for (int grp = warp; grp < 8; grp += kEThreads / 32) {
-    double o0, o1;
-    tile_rows16_dot(tile, kc, 16 * grp, c0, c1, Limbs{lim, Fs}, lane, o0, o1);
-    if ((lane & 3) == 0) {
-      dp[16 * grp + (lane >> 2)] = o0;
-      dp[16 * grp + 8 + (lane >> 2)] = o1;
-    }
+  double o0, o1;
+  rows16_dot(R, c1 - c0, Limbs{lim, Fs}, lane, o0, o1);
+  if ((lane & 3) == 0) {
+    double* dp = a.dp + ((size_t)k * a.n_seg_down + seg) * a.h_pad + (size_t)mt * 128 + 16 * warp;
+    dp[lane >> 2] = o0;
+    dp[8 + (lane >> 2)] = o1;
   }
   (void)err;
 }
@@ -706,49 +716,55 @@ cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a0, cudaStream
 }
 
 namespace {
-// Greedy token of each sequence from approximate logits: every id within `band` of the
-// approximate maximum is re-scored exactly (f64 dot of the f16 row with the normed x, rounded once,
-// + bias) by one warp each; the best exact value wins, ties to the lower id.  The approximate logits
-// carry errors far below `band`, so the exact maximum is always among the candidates.
+// Greedy token of each sequence from approximate logits: every id within `band` of the approximate
+// maximum (already in keys[b], from the LM head) is re-scored exactly -- f64 dot of the f16 row with
+// the normed x, rounded once, + bias -- and the best exact value wins, ties to the lower id.  The
+// approximate logits carry errors far below `band`, so the exact maximum is among the candidates.
+// Grid (slices, sequences): each CTA scans a slice of the logits; the last CTA of a sequence
+// re-scores the candidates.  scratch per sequence: [kRefMaxCand] ids, count, CTA counter (zero,
+// self-resetting).
 constexpr int kRefMaxCand = 64;
+__device__ __forceinline__ float key_value(unsigned long long key) {
+  const uint32_t b = (uint32_t)(key >> 32);
+  return __uint_as_float((b & 0x80000000u) ? (b & 0x7fffffffu) : ~b);
+}
 __global__ void __launch_bounds__(256) exact_argmax_refine_kernel(const uint16_t* __restrict__ w,
                                                                   const float* __restrict__ xf,
                                                                   const float* __restrict__ bias, const float* logits,
-                                                                  int V, int H, unsigned long long* keys, uint32_t* err) {
-  __shared__ float s_max;
-  __shared__ float wm[8];
-  __shared__ int s_n;
-  __shared__ int s_cand[kRefMaxCand];
+                                                                  int V, int H, unsigned long long* keys, int* scratch,
+                                                                  uint32_t* err) {
+  __shared__ uint32_t last;
   __shared__ unsigned long long s_best;
-  const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* cand = scratch + (size_t)b * (kRefMaxCand + 2);
+  int* cnt = cand + kRefMaxCand;
+  uint32_t* done = reinterpret_cast<uint32_t*>(cnt + 1);
   const float* lg = logits + (size_t)b * V;
   pdl_wait_prior();
   pdl_launch_dependents();
-  float m = -INFINITY;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) m = fmaxf(m, lg[i]);
-  m = warp_max(m);
-  if (threadIdx.x == 0) { s_n = 0; s_best = 0ull; }
-  if (lane == 0) wm[warp] = m;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = -INFINITY;
-    for (int i = 0; i < 8; ++i) t = fmaxf(t, wm[i]);
-    s_max = t;
-  }
-  __syncthreads();
-  const float band = 1e-4f * fabsf(s_max) + 1e-5f;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    if (lg[i] >= s_max - band) {
-      const int slot = atomicAdd(&s_n, 1);
-      if (slot < kRefMaxCand) s_cand[slot] = i;
+  const float mx = key_value(keys[b]);
+  const float band = 1e-4f * fabsf(mx) + 1e-5f;
+  const int per = (V + gridDim.x - 1) / gridDim.x, i0 = blockIdx.x * per, i1 = min(V, i0 + per);
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    if (__ldcg(lg + i) >= mx - band) {
+      const int slot = atomicAdd(cnt, 1);
+      if (slot < kRefMaxCand) cand[slot] = i;
       else atomicOr(err, EF_BAD_SHAPE);
     }
   }
+  __threadfence();
   __syncthreads();
-  const int n = min(s_n, kRefMaxCand);
+  if (threadIdx.x == 0) {
+    last = (atomicAdd(done, 1u) == gridDim.x - 1) ? 1u : 0u;
+    s_best = 0ull;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const int n = min(*reinterpret_cast<volatile int*>(cnt), kRefMaxCand);
   const float* x = xf + (size_t)b * H;
-  for (int c = warp; c < n; c += 8) {
-    const int r = s_cand[c];
+  for (int c = warp; c < n; c += blockDim.x / 32) {
+    const int r = __ldcg(cand + c);
     const __half* row = reinterpret_cast<const __half*>(w) + (size_t)r * H;
     double acc = 0.0;
     for (int i = lane; i < H; i += 32) acc = fma((double)__half2float(row[i]), (double)x[i], acc);
@@ -763,14 +779,21 @@ __global__ void __launch_bounds__(256) exact_argmax_refine_kernel(const uint16_t
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) keys[b] = s_best;
+  if (threadIdx.x == 0) {
+    if (n > 0) keys[b] = s_best;
+    *cnt = 0;
+    *done = 0u;
+  }
 }
 }  // namespace
 
+int exact_refine_scratch_ints(int B) { return B * (kRefMaxCand + 2); }
+
 cudaError_t launch_exact_argmax_refine(const uint16_t* w, const float* xf, const float* bias, const float* logits,
-                                       int V, int H, int B, unsigned long long* keys, const DevCtx& c, cudaStream_t s) {
+                                       int V, int H, int B, unsigned long long* keys, int* scratch, const DevCtx& c,
+                                       cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)B);
+  cfg.gridDim = dim3((unsigned)std::min(c.sm_count, (V + 255) / 256), (unsigned)B);
   cfg.blockDim = dim3(256);
   cfg.stream = s;
   cudaLaunchAttribute at[1];
@@ -778,7 +801,7 @@ cudaError_t launch_exact_argmax_refine(const uint16_t* w, const float* xf, const
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, exact_argmax_refine_kernel, w, xf, bias, logits, V, H, keys, c.err);
+  return cudaLaunchKernelEx(&cfg, exact_argmax_refine_kernel, w, xf, bias, logits, V, H, keys, scratch, c.err);
 }
 
 bool exact_kq_supported(int gate_q, int down_q, int H, int I) {

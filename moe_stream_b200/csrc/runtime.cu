@@ -189,6 +189,7 @@ struct BatchRt {
   float *xd_h = nullptr, *xd_a = nullptr;
   int *idx = nullptr, *grp = nullptr, *ent_slot = nullptr, *ent_of = nullptr;
   int* ent_zero = nullptr;          // [B K] zeros: every (token, slot) entry local (exact experts)
+  int* ref_scratch = nullptr;       // exact greedy re-scoring scratch
   uint32_t *attn_cnt = nullptr, *router_cnt = nullptr;
   std::vector<float*> kc, vc;
   void* lm_scratch = nullptr;
@@ -265,6 +266,7 @@ struct ms_model {
   float* ex_kgu = nullptr;          // K-quant experts: gate / up outputs [K][2][I]
   float* xn_final = nullptr;        // the LM head's input after the final norm [H]
   int head_start = 1;               // index of the step's first LM-head launch (profiling classes)
+  int* ref_scratch = nullptr;       // exact greedy re-scoring: candidate ids, counters
   struct Prefill {
     int cap = 0;                       // tokens the buffers hold
     std::vector<void*> allocs;
@@ -674,7 +676,7 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
   if (m->exact) la.xn_out = m->xn_final;
   LAUNCH(launch_lmhead(dc, la, s));
   if (m->exact)   // the greedy token from exact re-scoring of the near-maximal ids
-    LAUNCH(launch_exact_argmax_refine(m->out_w, m->xn_final, m->out_b, m->logits, c.vocab, H, 1, &m->st->key, dc, s));
+    LAUNCH(launch_exact_argmax_refine(m->out_w, m->xn_final, m->out_b, m->logits, c.vocab, H, 1, &m->st->key, m->ref_scratch, dc, s));
 #undef LAUNCH
   m->kernels_per_step = nk;
   return MS_OK;
@@ -870,7 +872,7 @@ ms_status pf_chunk(ms_model* m, const int32_t* tokens, int T, bool last_chunk) {
     if (m->exact) la.xn_out = m->xn_final;
     PCALL(launch_lmhead(dc, la, s));
     if (m->exact)
-      PCALL(launch_exact_argmax_refine(m->out_w, m->xn_final, m->out_b, m->logits, c.vocab, H, 1, &m->st->key, dc, s));
+      PCALL(launch_exact_argmax_refine(m->out_w, m->xn_final, m->out_b, m->logits, c.vocab, H, 1, &m->st->key, m->ref_scratch, dc, s));
   }
 #undef PCALL
   // the token log and the step state continue after the prompt
@@ -1050,7 +1052,7 @@ ms_status enqueue_batch_step(ms_model* m, cudaStream_t s) {
   la.logits = b.logits; la.keys = b.keys;
   BLAUNCH(9, 3, launch_lmhead_batch(dc, la, s));   // prep, GEMM, key reduction
   if (m->exact)   // exact re-scoring of the near-maximal ids (the greedy token, bit for bit)
-    BLAUNCH(9, 1, launch_exact_argmax_refine(m->out_w, b.xf, m->out_b, b.logits, c.vocab, H, B, b.keys, dc, s));
+    BLAUNCH(9, 1, launch_exact_argmax_refine(m->out_w, b.xf, m->out_b, b.logits, c.vocab, H, B, b.keys, b.ref_scratch, dc, s));
 #undef BLAUNCH
   b.kernels_per_step = nk;
   return MS_OK;
@@ -1570,6 +1572,7 @@ ms_status ms_model_finalize(ms_model* m) {
   s = s ? s : m->alloc(&m->token_log, (size_t)(c.max_seq_len + 1) * 4);
   s = s ? s : m->alloc(&m->ex_kgu, (size_t)c.top_k * 2 * c.inter * 4);
   s = s ? s : m->alloc(&m->xn_final, (size_t)H * 4);
+  s = s ? s : m->alloc(&m->ref_scratch, (size_t)exact_refine_scratch_ints(1) * 4);
   if (any_tc) {
     m->ex_seg_gu = exact_seg_count(H / 32);
     m->ex_seg_down = exact_seg_count(c.inter / 32);
@@ -1643,6 +1646,7 @@ ms_status ms_model_batch_open(ms_model* m, int B) {
   s = s ? s : balloc(m, &b.ent_slot, (size_t)EK * 4);
   s = s ? s : balloc(m, &b.ent_of, (size_t)EK * 4);
   s = s ? s : balloc(m, &b.ent_zero, (size_t)EK * 4);
+  s = s ? s : balloc(m, &b.ref_scratch, (size_t)exact_refine_scratch_ints(B) * 4);
   s = s ? s : balloc(m, &b.act, (size_t)EK * 2 * c.inter * 4);
   s = s ? s : balloc(m, &b.y, (size_t)EK * H * 4);
   s = s ? s : balloc(m, &b.xf, (size_t)B * H * 4);
