@@ -84,6 +84,7 @@ def _gpu_rank(rank, world, port, path, prompt, out_dir, exchange):
         uid = [Engine.nccl_unique_id(ctx) if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         eng.init_ep(uid[0])
+    eng.set_prefill(0)   # the prompt through the decode step, as on one device
     toks = eng.generate(prompt, 16)
     np.save(os.path.join(out_dir, f"tok{rank}.npy"), np.array(toks, np.int32))
     eng.close()
