@@ -336,7 +336,7 @@ constexpr int kESegChunks = 8;    // 32-element chunks per K segment (within one
 // 2^(E_w - 128 - F + 16t) and accumulates in double.
 struct Limbs {
   int8_t* lim;   // [chunk][8 digits][32 elements]
-  int* F;        // [chunk]
+  int* F;        // [chunk]: 1023 - 128 - F, the chunk's part of the scale exponent
 };
 
 // warp w writes the digits of chunks w, w + nw, ... of xs[32 c ..] (f32, 32 per chunk), n_ch chunks
@@ -358,7 +358,7 @@ __device__ __forceinline__ void make_limbs(const float* xs, int n_ch, Limbs L, i
       L.lim[(i * 8 + n) * 32 + lane] = (int8_t)d;
     }
     L.lim[(i * 8 + 7) * 32 + lane] = 0;
-    if (lane == 0) L.F[i] = F;
+    if (lane == 0) L.F[i] = 1023 - 128 - F;   // the chunk's part of the scale exponent
   }
 }
 
@@ -385,28 +385,30 @@ __device__ __forceinline__ void mma_s8_m16n8k32(int (&d)[4], uint32_t a0, uint32
 
 // rows rb .. rb+15 of a packed tile over chunks c0 .. c1 (one slab); returns, in lanes with
 // (lane & 3) == 0, the f64 dots of rows rb + (lane >> 2) (first) and rb + 8 + (lane >> 2) (second)
-// Rows rb .. rb+15 of a packed tile over chunks [c0, c1) (inside one 16-chunk slab): the lane's
-// code words and scale bytes, loaded as soon as the expert is known ...
+// Rows rb .. rb+15 of a packed tile over chunks [c0, c1) (inside one 16-chunk slab).  The MMA's k
+// order is permuted so each lane's A elements are contiguous: lane (g, t) takes code word t of rows
+// g and g + 8 (elements 8t .. 8t+7) as its k = 4t.. and k = 16 + 4t.. fragments, and the activation
+// digits are read in the same order.  The lane's code words and scale bytes are loaded as soon as
+// the expert is known ...
 struct Rows16 {
-  uint32_t w[kESegChunks][4];
+  uint32_t w[kESegChunks][2];
   uint32_t es[kESegChunks / 2];   // scale bytes of rows r0 / r1, two chunks per word
 };
 __device__ __forceinline__ void rows16_load(const uint8_t* tile, int kc, int rb, int c0, int c1, int lane, Rows16& R) {
   const int g = lane >> 2, t = lane & 3;
   const int slab = c0 >> 4, nchs = min(16, kc - slab * 16), cl0 = c0 & 15;
-  const uint8_t* sb = tile + (size_t)slab * (16 * 2048 + 4 * 512);
-  const int r0 = rb + g, r1 = rb + g + 8, wo = 4 * (t >> 1);
+  const uint8_t* cb = tile + (size_t)slab * (16 * 2048 + 4 * 512) + (size_t)cl0 * 2048 + (rb + g) * 16 + 4 * t;
+  const uint8_t* scb = tile + (size_t)slab * (16 * 2048 + 4 * 512) + nchs * 2048;
+  const int r0 = rb + g, r1 = rb + g + 8;
+  const int so0 = 16 * (r0 & 31) + 4 * (r0 >> 5), so1 = 16 * (r1 & 31) + 4 * (r1 >> 5);
 #pragma unroll
   for (int i = 0; i < kESegChunks; ++i) {
     if (c0 + i < c1) {
+      R.w[i][0] = __ldcs(reinterpret_cast<const uint32_t*>(cb + i * 2048));
+      R.w[i][1] = __ldcs(reinterpret_cast<const uint32_t*>(cb + i * 2048 + 8 * 16));
       const int cl = cl0 + i;
-      const uint8_t* cb = sb + (size_t)cl * 2048;
-      R.w[i][0] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r0 * 16 + wo));
-      R.w[i][1] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r0 * 16 + 8 + wo));
-      R.w[i][2] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r1 * 16 + wo));
-      R.w[i][3] = __ldcs(reinterpret_cast<const uint32_t*>(cb + r1 * 16 + 8 + wo));
-      const uint8_t* scb = sb + nchs * 2048 + (cl >> 2) * 512 + (cl & 3);
-      const uint32_t e2 = (uint32_t)scb[16 * (r0 & 31) + 4 * (r0 >> 5)] | ((uint32_t)scb[16 * (r1 & 31) + 4 * (r1 >> 5)] << 8);
+      const uint8_t* sg = scb + (cl >> 2) * 512 + (cl & 3);
+      const uint32_t e2 = (uint32_t)sg[so0] | ((uint32_t)sg[so1] << 8);
       if (i & 1) R.es[i >> 1] |= e2 << 16;
       else R.es[i >> 1] = e2;
     }
@@ -414,24 +416,23 @@ __device__ __forceinline__ void rows16_load(const uint8_t* tile, int kc, int rb,
 }
 
 // ... then, once the activation digits are in shared memory, the dots: returns, in lanes with
-// (lane & 3) == 0, the f64 dots of rows rb + (lane >> 2) (out0) and rb + 8 + (lane >> 2) (out1)
+// (lane & 3) == 0, the f64 dots of rows rb + (lane >> 2) (out0) and rb + 8 + (lane >> 2) (out1).
+// L.F holds, per chunk, the lane-independent part of the scale exponent: 1023 - 128 - F.
 __device__ __forceinline__ void rows16_dot(const Rows16& R, int n, Limbs L, int lane, double& out0, double& out1) {
-  const int g = lane >> 2, t = lane & 3, sh = 16 * (t & 1);
+  const int g = lane >> 2, t = lane & 3;
   double acc0 = 0.0, acc1 = 0.0;
+  const int8_t* lb = L.lim + g * 32 + 8 * t;
 #pragma unroll
   for (int i = 0; i < kESegChunks; ++i) {
     if (i >= n) break;
-    const int8_t* lb = L.lim + i * 256;
-    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(lb + g * 32 + 4 * t);
-    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(lb + g * 32 + 16 + 4 * t);
+    const uint2 bv = *reinterpret_cast<const uint2*>(lb + i * 256);   // digits of elements 8t .. 8t+7
     int d[4] = {0, 0, 0, 0};
-    mma_s8_m16n8k32(d, e2m1x4_to_s8(R.w[i][0] >> sh), e2m1x4_to_s8(R.w[i][2] >> sh), e2m1x4_to_s8(R.w[i][1] >> sh),
-                    e2m1x4_to_s8(R.w[i][3] >> sh), b0, b1);
-    const int F = L.F[i];
+    mma_s8_m16n8k32(d, e2m1x4_to_s8(R.w[i][0]), e2m1x4_to_s8(R.w[i][1]), e2m1x4_to_s8(R.w[i][0] >> 16),
+                    e2m1x4_to_s8(R.w[i][1] >> 16), bv.x, bv.y);
+    const int base = L.F[i] + 16 * t;
     const uint32_t e2 = R.es[i >> 1] >> (16 * (i & 1));
-    const int e0 = (int)(e2 & 0xFFu), e1 = (int)((e2 >> 8) & 0xFFu);
-    const double s0 = __longlong_as_double((long long)(e0 - 128 - F + 16 * t + 1023) << 52);
-    const double s1 = __longlong_as_double((long long)(e1 - 128 - F + 16 * t + 1023) << 52);
+    const double s0 = __longlong_as_double((long long)((int)(e2 & 0xFFu) + base) << 52);
+    const double s1 = __longlong_as_double((long long)((int)((e2 >> 8) & 0xFFu) + base) << 52);
     acc0 = fma(i32_to_double(d[0] + (d[1] << 8)), s0, acc0);   // digits 2t, 2t+1 of row r0
     acc1 = fma(i32_to_double(d[2] + (d[3] << 8)), s1, acc1);
   }
