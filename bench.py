@@ -309,8 +309,10 @@ def run_ours(args):
     breakdown = None
     if not ep and not args.no_profile:
         us = eng.profile_step()
-        names = ["embed", "qkv_q8", "attention", "o_q8", "router", "moe_ffn", "resid_norm_q8", "lm_head"]
-        breakdown = {names[i] if len(us) == len(names) else f"class{i}": round(v, 1) for i, v in enumerate(us)}
+        names = {8: ["embed", "qkv_q8", "attention", "o_q8", "router", "moe_ffn", "resid_norm_q8", "lm_head"],
+                 9: ["embed", "qkv_q8", "attention", "o_q8", "router", "moe_gate_up", "moe_down", "resid_norm_q8",
+                     "lm_head"]}.get(len(us))
+        breakdown = {names[i] if names else f"class{i}": round(v, 1) for i, v in enumerate(us)}
         breakdown["sum_us"] = round(sum(us), 1)
         log(f"[rank {rank}] per-step kernel-class us: {breakdown}")
     eng.close()

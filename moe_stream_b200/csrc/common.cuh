@@ -293,6 +293,26 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 }
 __device__ __forceinline__ float expcr(float x) { return (float)exp((double)x); }
 
+// Exact integer digits of one 32-element f32 block (one element per lane), the activation side of
+// the exact MXFP4 expert dots: X_j = round(x_j 2^F) with F = 180 - (the block's largest biased
+// exponent), so |X_j| < 2^54 and X keeps every bit of the block's larger elements; X is written as
+// 7 signed base-256 digits, dig[n * 32 + lane] = digit n of element lane (n = 0..6; row 7 is never
+// read).  *fexp = 1023 - 128 - F, the block's part of the double scale exponent.
+__device__ __forceinline__ void exact_digits_warp(float x, int lane, int8_t* dig, int* fexp) {
+  int eb = (int)((__float_as_uint(x) >> 23) & 0xFFu);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) eb = max(eb, __shfl_xor_sync(0xffffffffu, eb, o));
+  const int F = 180 - eb;
+  long long X = __double2ll_rn((double)x * __longlong_as_double((long long)(F + 1023) << 52));
+#pragma unroll
+  for (int n = 0; n < 7; ++n) {
+    const int d = (int)(int8_t)(X & 255);   // the balanced digit in [-128, 127]
+    X = (X - d) >> 8;
+    dig[n * 32 + lane] = (int8_t)d;
+  }
+  if (lane == 0) *fexp = 1023 - 128 - F;
+}
+
 // inverse RMS with the reference's op sequence (ops/norm.rs:16-37): x.sqr() in f32, mean_keepdim =
 // (sum rounded to f32) * f32(1/n) (candle's affine), + eps, sqrt, recip.  Threads tid in [0, nthr)
 // (nthr a multiple of 32) take part; bar() synchronises them; every one gets the result.

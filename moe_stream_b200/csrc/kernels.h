@@ -136,6 +136,8 @@ struct RouterArgs {
   int softmax_weight = 1;         // GPT-OSS: softmax over the selected k logits
   int normalize = 0;              // renormalise top-k probabilities (norm_topk_prob)
   uint8_t* xterm = nullptr;       // optional: the normed x as MXFP4 B terms (tc_bterm_bytes(H/32))
+  int8_t* xdig = nullptr;         // optional: the normed x as exact digits ([H/32][256], exact_digits_warp)
+  int* xfe = nullptr;             //   and their scale exponents [H/32]
   int batch = 1;                  // grid.y = tokens: h/xn + b*H, logits + b*E, idx/wts + b*K, counter + b
 };
 cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s);
@@ -316,6 +318,11 @@ struct ExactMoeArgs {
   double* gp = nullptr;             // [K][n_seg_gu][2 I]
   double* dp = nullptr;             // [K][n_seg_down][h_pad]
   int n_seg_gu = 0, n_seg_down = 0, h_pad = 0;
+  const int8_t* xdig = nullptr;     // [H/32][256] digits of x (exact_digits_warp), written by the router
+  const int* xfe = nullptr;         // [H/32] their scale exponents
+  int8_t* adig = nullptr;           // [K][I/32][256] digits of the activations (written by gate/up)
+  int* afe = nullptr;               // [K][I/32]
+  uint32_t* cnt = nullptr;          // [K][gate/up tiles] zero-initialised, self-resetting
   int gu_tiles = 0, down_tiles = 0;           // filled by launch_exact_moe
   int64_t gu_tile_bytes = 0, down_tile_bytes = 0;
 };
@@ -346,7 +353,7 @@ cudaError_t launch_exact_argmax_refine(const uint16_t* w, const float* xf, const
                                        cudaStream_t s);
 int exact_refine_scratch_ints(int B);
 cudaError_t launch_exact_kq_moe(const DevCtx& c, const ExactKqArgs& a, cudaStream_t s);
-cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a, cudaStream_t s);
+cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a, cudaStream_t s, int part = -1);
 
 // ---- LM head / f16 GEMV ----
 // logits = W (RMSNorm(h)*norm_w if norm_w) (+bias); argmax (lowest index on ties) into *key.

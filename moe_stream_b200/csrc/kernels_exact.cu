@@ -334,34 +334,6 @@ constexpr int kESegChunks = 8;    // 32-element chunks per K segment (within one
 // mma.sync.m16n8k32.s8 per (16 rows, 32 elements) then yields, exactly in int32, the 7 digit dots of
 // 16 rows (B column = digit); each lane folds its two digits into a double scaled by
 // 2^(E_w - 128 - F + 16t) and accumulates in double.
-struct Limbs {
-  int8_t* lim;   // [chunk][8 digits][32 elements]
-  int* F;        // [chunk]: 1023 - 128 - F, the chunk's part of the scale exponent
-};
-
-// warp w writes the digits of chunks w, w + nw, ... of xs[32 c ..] (f32, 32 per chunk), n_ch chunks
-__device__ __forceinline__ void make_limbs(const float* xs, int n_ch, Limbs L, int warp, int nw, int lane) {
-  for (int i = warp; i < n_ch; i += nw) {
-    const float x = xs[32 * i + lane];
-    const int e = (int)((__float_as_uint(x) >> 23) & 0xFFu);
-    int eb = e;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) eb = max(eb, __shfl_xor_sync(0xffffffffu, eb, o));
-    const int F = 180 - eb;
-    const double p2 = __longlong_as_double((long long)(F + 1023) << 52);
-    long long X = __double2ll_rn((double)x * p2);
-#pragma unroll
-    for (int n = 0; n < 7; ++n) {
-      int d = (int)(X & 255);
-      if (d > 127) d -= 256;
-      X = (X - d) >> 8;
-      L.lim[(i * 8 + n) * 32 + lane] = (int8_t)d;
-    }
-    L.lim[(i * 8 + 7) * 32 + lane] = 0;
-    if (lane == 0) L.F[i] = 1023 - 128 - F;   // the chunk's part of the scale exponent
-  }
-}
-
 // four e2m1 codes (16 bits, element order low nibble first) -> four doubled values as int8
 __device__ __forceinline__ uint32_t e2m1x4_to_s8(uint32_t u) {
   const uint32_t m7 = u & 0x7777u;
@@ -383,8 +355,6 @@ __device__ __forceinline__ void mma_s8_m16n8k32(int (&d)[4], uint32_t a0, uint32
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// rows rb .. rb+15 of a packed tile over chunks c0 .. c1 (one slab); returns, in lanes with
-// (lane & 3) == 0, the f64 dots of rows rb + (lane >> 2) (first) and rb + 8 + (lane >> 2) (second)
 // Rows rb .. rb+15 of a packed tile over chunks [c0, c1) (inside one 16-chunk slab).  The MMA's k
 // order is permuted so each lane's A elements are contiguous: lane (g, t) takes code word t of rows
 // g and g + 8 (elements 8t .. 8t+7) as its k = 4t.. and k = 16 + 4t.. fragments, and the activation
@@ -392,49 +362,75 @@ __device__ __forceinline__ void mma_s8_m16n8k32(int (&d)[4], uint32_t a0, uint32
 // the expert is known ...
 struct Rows16 {
   uint32_t w[kESegChunks][2];
-  uint32_t es[kESegChunks / 2];   // scale bytes of rows r0 / r1, two chunks per word
+  uint32_t es[4];   // scale bytes: rows r0 / r1 (es[0..1] / es[2..3]) of the segment's two 4-chunk groups
 };
-__device__ __forceinline__ void rows16_load(const uint8_t* tile, int kc, int rb, int c0, int c1, int lane, Rows16& R) {
+static_assert(kESegChunks == 8, "a segment is two 4-chunk scale groups");
+// n = c1 - c0 chunks (c0 a multiple of 8); FULL: n == 8
+template <bool FULL>
+__device__ __forceinline__ void rows16_load(const uint8_t* tile, int kc, int rb, int c0, int n, int lane, Rows16& R) {
   const int g = lane >> 2, t = lane & 3;
   const int slab = c0 >> 4, nchs = min(16, kc - slab * 16), cl0 = c0 & 15;
-  const uint8_t* cb = tile + (size_t)slab * (16 * 2048 + 4 * 512) + (size_t)cl0 * 2048 + (rb + g) * 16 + 4 * t;
-  const uint8_t* scb = tile + (size_t)slab * (16 * 2048 + 4 * 512) + nchs * 2048;
-  const int r0 = rb + g, r1 = rb + g + 8;
-  const int so0 = 16 * (r0 & 31) + 4 * (r0 >> 5), so1 = 16 * (r1 & 31) + 4 * (r1 >> 5);
+  const uint8_t* sb = tile + (size_t)slab * (16 * 2048 + 4 * 512);
+  const uint8_t* cb = sb + (size_t)cl0 * 2048 + (rb + g) * 16 + 4 * t;
 #pragma unroll
   for (int i = 0; i < kESegChunks; ++i) {
-    if (c0 + i < c1) {
+    if (FULL || i < n) {
       R.w[i][0] = __ldcs(reinterpret_cast<const uint32_t*>(cb + i * 2048));
       R.w[i][1] = __ldcs(reinterpret_cast<const uint32_t*>(cb + i * 2048 + 8 * 16));
-      const int cl = cl0 + i;
-      const uint8_t* sg = scb + (cl >> 2) * 512 + (cl & 3);
-      const uint32_t e2 = (uint32_t)sg[so0] | ((uint32_t)sg[so1] << 8);
-      if (i & 1) R.es[i >> 1] |= e2 << 16;
-      else R.es[i >> 1] = e2;
+    } else {
+      R.w[i][0] = R.w[i][1] = 0u;
     }
+  }
+  // the scale group of 4 chunks holds, per row r, the 4 chunks' scale bytes as one aligned word at
+  // 16 (r & 31) + 4 (r >> 5)
+  const int r0 = rb + g, r1 = rb + g + 8;
+  const uint8_t* sg = sb + nchs * 2048 + (cl0 >> 2) * 512;
+  R.es[0] = __ldcs(reinterpret_cast<const uint32_t*>(sg + 16 * (r0 & 31) + 4 * (r0 >> 5)));
+  R.es[2] = __ldcs(reinterpret_cast<const uint32_t*>(sg + 16 * (r1 & 31) + 4 * (r1 >> 5)));
+  if (FULL || n > 4) {
+    R.es[1] = __ldcs(reinterpret_cast<const uint32_t*>(sg + 512 + 16 * (r0 & 31) + 4 * (r0 >> 5)));
+    R.es[3] = __ldcs(reinterpret_cast<const uint32_t*>(sg + 512 + 16 * (r1 & 31) + 4 * (r1 >> 5)));
+  } else {
+    R.es[1] = R.es[3] = 0u;
   }
 }
 
-// ... then, once the activation digits are in shared memory, the dots: returns, in lanes with
-// (lane & 3) == 0, the f64 dots of rows rb + (lane >> 2) (out0) and rb + 8 + (lane >> 2) (out1).
-// L.F holds, per chunk, the lane-independent part of the scale exponent: 1023 - 128 - F.
-__device__ __forceinline__ void rows16_dot(const Rows16& R, int n, Limbs L, int lane, double& out0, double& out1) {
+// ... then, once the activation digits are written (dig: the segment's first chunk, 256 bytes per
+// chunk; fe: its scale exponents), the dots: returns, in lanes with (lane & 3) == 0, the f64 dots of
+// rows rb + (lane >> 2) (out0) and rb + 8 + (lane >> 2) (out1).  B column g of the MMA is digit g;
+// column 7 is zero.  The scale of a (row, chunk) term is 2^(E_w + fe + 16 t - 1023), built as the
+// high word (E_w + fe + 16 t) << 20 of a double.
+template <bool FULL>
+__device__ __forceinline__ void rows16_dot(const Rows16& R, int n, const int8_t* dig, const int* fe, int lane,
+                                           double& out0, double& out1) {
   const int g = lane >> 2, t = lane & 3;
-  double acc0 = 0.0, acc1 = 0.0;
-  const int8_t* lb = L.lim + g * 32 + 8 * t;
+  uint2 bv[kESegChunks];
+  int fx[kESegChunks];
+  const int8_t* lb = dig + g * 32 + 8 * t;
 #pragma unroll
   for (int i = 0; i < kESegChunks; ++i) {
-    if (i >= n) break;
-    const uint2 bv = *reinterpret_cast<const uint2*>(lb + i * 256);   // digits of elements 8t .. 8t+7
-    int d[4] = {0, 0, 0, 0};
-    mma_s8_m16n8k32(d, e2m1x4_to_s8(R.w[i][0]), e2m1x4_to_s8(R.w[i][1]), e2m1x4_to_s8(R.w[i][0] >> 16),
-                    e2m1x4_to_s8(R.w[i][1] >> 16), bv.x, bv.y);
-    const int base = L.F[i] + 16 * t;
-    const uint32_t e2 = R.es[i >> 1] >> (16 * (i & 1));
-    const double s0 = __longlong_as_double((long long)((int)(e2 & 0xFFu) + base) << 52);
-    const double s1 = __longlong_as_double((long long)((int)((e2 >> 8) & 0xFFu) + base) << 52);
-    acc0 = fma(i32_to_double(d[0] + (d[1] << 8)), s0, acc0);   // digits 2t, 2t+1 of row r0
-    acc1 = fma(i32_to_double(d[2] + (d[3] << 8)), s1, acc1);
+    bv[i] = make_uint2(0u, 0u);
+    fx[i] = 0;
+    if (FULL || i < n) {
+      if (g < 7) bv[i] = __ldcg(reinterpret_cast<const uint2*>(lb + i * 256));   // digits of elements 8t .. 8t+7
+      fx[i] = (__ldcg(fe + i) + 16 * t) << 20;
+    }
+  }
+  double acc0 = 0.0, acc1 = 0.0;
+#pragma unroll
+  for (int i = 0; i < kESegChunks; ++i) {
+    if (FULL || i < n) {
+      int d[4] = {0, 0, 0, 0};
+      const uint32_t w0 = R.w[i][0], w1 = R.w[i][1];
+      mma_s8_m16n8k32(d, e2m1x4_to_s8(w0), e2m1x4_to_s8(w1), e2m1x4_to_s8(w0 >> 16), e2m1x4_to_s8(w1 >> 16), bv[i].x,
+                      bv[i].y);
+      const uint32_t e0 = __byte_perm(R.es[i >> 2], 0u, 0x4440u | (i & 3));       // E_w of row r0
+      const uint32_t e1 = __byte_perm(R.es[2 + (i >> 2)], 0u, 0x4440u | (i & 3)); // and of row r1
+      const double s0 = __hiloint2double((int)(e0 * (1u << 20) + (uint32_t)fx[i]), 0);
+      const double s1 = __hiloint2double((int)(e1 * (1u << 20) + (uint32_t)fx[i]), 0);
+      acc0 = fma(i32_to_double(d[0] + (d[1] << 8)), s0, acc0);   // digits 2t, 2t+1 of row r0
+      acc1 = fma(i32_to_double(d[2] + (d[3] << 8)), s1, acc1);
+    }
   }
   acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
   acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
@@ -444,34 +440,17 @@ __device__ __forceinline__ void rows16_dot(const Rows16& R, int n, Limbs L, int 
   out1 = acc1;
 }
 
-// gate/up: grid (segments, gate_up tiles, slots); 8 warps = the 8 groups of 16 rows of a 128-row
-// tile (rows < 64 gate, >= 64 up)
-__global__ void __launch_bounds__(kEThreads, 3) exact_gu_kernel(ExactMoeArgs a, uint32_t* err) {
-  __shared__ __align__(16) int8_t lim[kESegChunks * 256];
-  __shared__ int Fs[kESegChunks];
-  __shared__ float xs[kESegChunks * 32];
-  const int seg = blockIdx.x, mt = blockIdx.y, k = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kc = a.H / 32, c0 = seg * kESegChunks, c1 = min(kc, c0 + kESegChunks);
-  pdl_wait_prior();
-  pdl_launch_dependents();
-  const int e = a.idx[k] - a.expert_base;
-  if (e < 0 || e >= a.n_local) return;   // another rank's expert (or out of range: the combine skips it)
-  const uint8_t* tile = a.gu + ((size_t)e * a.gu_tiles + mt) * (size_t)a.gu_tile_bytes;
+// both halves of a segment: the full fast path, or the guarded one for a slab's last segment
+__device__ __forceinline__ void rows16_seg(const uint8_t* tile, int kc, int rb, int c0, int n, const int8_t* dig,
+                                           const int* fe, int lane, double& o0, double& o1) {
   Rows16 R;
-  rows16_load(tile, kc, 16 * warp, c0, c1, lane, R);
-  for (int i = threadIdx.x; i < 32 * (c1 - c0); i += kEThreads) xs[i] = a.x[32 * c0 + i];
-  __syncthreads();
-  make_limbs(xs, c1 - c0, Limbs{lim, Fs}, warp, kEThreads / 32, lane);
-  __syncthreads();
-  double o0, o1;
-  rows16_dot(R, c1 - c0, Limbs{lim, Fs}, lane, o0, o1);
-  if ((lane & 3) == 0) {
-    double* gp = a.gp + ((size_t)k * a.n_seg_gu + seg) * (2 * a.I) + (size_t)mt * 128 + 16 * warp;
-    gp[lane >> 2] = o0;
-    gp[8 + (lane >> 2)] = o1;
+  if (n == kESegChunks) {
+    rows16_load<true>(tile, kc, rb, c0, n, lane, R);
+    rows16_dot<true>(R, n, dig, fe, lane, o0, o1);
+  } else {
+    rows16_load<false>(tile, kc, rb, c0, n, lane, R);
+    rows16_dot<false>(R, n, dig, fe, lane, o0, o1);
   }
-  (void)err;
 }
 
 __device__ __forceinline__ float act_exact(float g, float u, int oai) {
@@ -485,12 +464,67 @@ __device__ __forceinline__ float act_exact(float g, float u, int oai) {
   return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expcr(-g))), u);
 }
 
-// down: grid (segments, down tiles, slots).  The segment's activations are rebuilt from the gate/up
-// partial dots (sum of segments rounded once, + bias, activation) first.
+// gate/up: grid (segments, gate_up tiles, slots); 8 warps = the 8 groups of 16 rows of a 128-row
+// tile (rows < 64 gate, >= 64 up).  The last CTA to finish a (tile, slot) sums its 64 gate and up
+// rows over the segments (in segment order, rounded once), adds the biases, applies the activation
+// and writes the 64 activations as exact digits for the down kernel.
+__global__ void __launch_bounds__(kEThreads, 3) exact_gu_kernel(ExactMoeArgs a, uint32_t* err) {
+  __shared__ uint32_t last;
+  const int seg = blockIdx.x, mt = blockIdx.y, k = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kc = a.H / 32, c0 = seg * kESegChunks, c1 = min(kc, c0 + kESegChunks);
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int e = a.idx[k] - a.expert_base;
+  if (e < 0 || e >= a.n_local) return;   // another rank's expert (or out of range: the combine skips it)
+  const uint8_t* tile = a.gu + ((size_t)e * a.gu_tiles + mt) * (size_t)a.gu_tile_bytes;
+  double o0, o1;
+  rows16_seg(tile, kc, 16 * warp, c0, c1 - c0, a.xdig + (size_t)c0 * 256, a.xfe + c0, lane, o0, o1);
+  double* gp = a.gp + (size_t)k * a.n_seg_gu * (2 * a.I);
+  if ((lane & 3) == 0) {
+    double* o = gp + (size_t)seg * (2 * a.I) + (size_t)mt * 128 + 16 * warp;
+    o[lane >> 2] = o0;
+    o[8 + (lane >> 2)] = o1;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* c = a.cnt + (size_t)k * a.gu_tiles + mt;
+    last = atomicAdd(c, 1u) == (uint32_t)a.n_seg_gu - 1 ? 1u : 0u;
+    if (last) *c = 0u;
+  }
+  __syncthreads();
+  if (!last || warp >= 2) return;
+  __threadfence();
+  const int i = mt * 64 + 32 * warp + lane;           // activation index; its gate / up rows:
+  const int gr = mt * 128 + 32 * warp + lane, ur = gr + 64;
+  double gs = 0.0, us = 0.0;
+  for (int s0 = 0; s0 < a.n_seg_gu; s0 += 8) {   // 16 loads in flight, summed in segment order
+    double gl[8], ul[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const bool in = s0 + j < a.n_seg_gu;
+      gl[j] = in ? __ldcg(gp + (size_t)(s0 + j) * (2 * a.I) + gr) : 0.0;
+      ul[j] = in ? __ldcg(gp + (size_t)(s0 + j) * (2 * a.I) + ur) : 0.0;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (s0 + j < a.n_seg_gu) {
+        gs += gl[j];
+        us += ul[j];
+      }
+    }
+  }
+  float gv = (float)gs, uv = (float)us;
+  if (a.gate_b) gv = __fadd_rn(gv, a.gate_b[(size_t)e * a.I + i]);
+  if (a.up_b) uv = __fadd_rn(uv, a.up_b[(size_t)e * a.I + i]);
+  const size_t chunk = (size_t)k * (a.I / 32) + 2 * mt + warp;
+  exact_digits_warp(act_exact(gv, uv, a.oai_swiglu), lane, a.adig + (size_t)chunk * 256, a.afe + chunk);
+  (void)err;
+}
+
+// down: grid (segments, down tiles, slots), over the activation digits written by gate/up
 __global__ void __launch_bounds__(kEThreads, 3) exact_down_kernel(ExactMoeArgs a, uint32_t* err) {
-  __shared__ __align__(16) int8_t lim[kESegChunks * 256];
-  __shared__ int Fs[kESegChunks];
-  __shared__ float as[kESegChunks * 32];
   const int seg = blockIdx.x, mt = blockIdx.y, k = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kc = a.I / 32, c0 = seg * kESegChunks, c1 = min(kc, c0 + kESegChunks);
@@ -499,27 +533,9 @@ __global__ void __launch_bounds__(kEThreads, 3) exact_down_kernel(ExactMoeArgs a
   const int e = a.idx[k] - a.expert_base;
   if (e < 0 || e >= a.n_local) return;
   const uint8_t* tile = a.down + ((size_t)e * a.down_tiles + mt) * (size_t)a.down_tile_bytes;
-  Rows16 R;
-  rows16_load(tile, kc, 16 * warp, c0, c1, lane, R);
-  const double* gp = a.gp + (size_t)k * a.n_seg_gu * (2 * a.I);
-  for (int j = threadIdx.x; j < 32 * (c1 - c0); j += kEThreads) {
-    const int i = 32 * c0 + j;
-    const int gr = (i >> 6) * 128 + (i & 63), ur = gr + 64;   // gate / up rows of activation i
-    double gs = 0.0, us = 0.0;
-    for (int s2 = 0; s2 < a.n_seg_gu; ++s2) {
-      gs += __ldcg(gp + (size_t)s2 * (2 * a.I) + gr);
-      us += __ldcg(gp + (size_t)s2 * (2 * a.I) + ur);
-    }
-    float gv = (float)gs, uv = (float)us;
-    if (a.gate_b) gv = __fadd_rn(gv, a.gate_b[(size_t)e * a.I + i]);
-    if (a.up_b) uv = __fadd_rn(uv, a.up_b[(size_t)e * a.I + i]);
-    as[j] = act_exact(gv, uv, a.oai_swiglu);
-  }
-  __syncthreads();
-  make_limbs(as, c1 - c0, Limbs{lim, Fs}, warp, kEThreads / 32, lane);
-  __syncthreads();
+  const size_t ch = (size_t)k * kc + c0;
   double o0, o1;
-  rows16_dot(R, c1 - c0, Limbs{lim, Fs}, lane, o0, o1);
+  rows16_seg(tile, kc, 16 * warp, c0, c1 - c0, a.adig + ch * 256, a.afe + ch, lane, o0, o1);
   if ((lane & 3) == 0) {
     double* dp = a.dp + ((size_t)k * a.n_seg_down + seg) * a.h_pad + (size_t)mt * 128 + 16 * warp;
     dp[lane >> 2] = o0;
@@ -699,9 +715,11 @@ cudaError_t launch_exact_attention(const DevCtx& c, const AttnArgs& a, int range
 
 int exact_seg_count(int kc) { return (kc + kESegChunks - 1) / kESegChunks; }
 
-cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a0, cudaStream_t s) {
+cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a0, cudaStream_t s, int part) {
   ExactMoeArgs a = a0;
-  if (!tc_supported(a.H, a.I) || a.K < 1 || a.K > 16 || !a.gp || !a.dp) return cudaErrorInvalidValue;
+  if (!tc_supported(a.H, a.I) || a.K < 1 || a.K > 16 || !a.gp || !a.dp || !a.xdig || !a.xfe || !a.adig || !a.afe ||
+      !a.cnt || a.I % 64)
+    return cudaErrorInvalidValue;
   a.gu_tiles = tc_gu_tiles(a.I);
   a.down_tiles = tc_down_tiles(a.H);
   a.gu_tile_bytes = tc_tile_bytes(a.H / 32);
@@ -709,9 +727,11 @@ cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a0, cudaStream
   if (a.n_seg_gu != exact_seg_count(a.H / 32) || a.n_seg_down != exact_seg_count(a.I / 32) ||
       a.h_pad < tc_down_tiles(a.H) * 128)
     return cudaErrorInvalidValue;
-  cudaError_t e = launch_pdl_x(exact_gu_kernel, dim3((unsigned)a.n_seg_gu, (unsigned)tc_gu_tiles(a.I), (unsigned)a.K),
-                               dim3(kEThreads), 0, s, a, c.err);
-  if (e != cudaSuccess) return e;
+  if (part != 1) {
+    cudaError_t e = launch_pdl_x(exact_gu_kernel, dim3((unsigned)a.n_seg_gu, (unsigned)tc_gu_tiles(a.I), (unsigned)a.K),
+                                 dim3(kEThreads), 0, s, a, c.err);
+    if (e != cudaSuccess || part == 0) return e;
+  }
   return launch_pdl_x(exact_down_kernel, dim3((unsigned)a.n_seg_down, (unsigned)tc_down_tiles(a.H), (unsigned)a.K),
                       dim3(kEThreads), 0, s, a, c.err);
 }

@@ -262,6 +262,11 @@ struct ms_model {
   bool exact = true;
   double* ex_gp = nullptr;          // [K][segments][2 I] gate/up partial dots
   double* ex_dp = nullptr;          // [K][segments][h_pad] down partial dots
+  int8_t* ex_xdig = nullptr;        // [H/32][256] exact digits of the MoE input
+  int* ex_xfe = nullptr;            // [H/32]
+  int8_t* ex_adig = nullptr;        // [K][I/32][256] exact digits of the activations
+  int* ex_afe = nullptr;            // [K][I/32]
+  uint32_t* ex_cnt = nullptr;       // [K][gate/up tiles] per-tile arrival counters
   int ex_seg_gu = 0, ex_seg_down = 0, ex_hpad = 0;
   float* ex_kgu = nullptr;          // K-quant experts: gate / up outputs [K][2][I]
   float* xn_final = nullptr;        // the LM head's input after the final norm [H]
@@ -539,7 +544,12 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     ra.mask = Lw.mask; ra.logits = m->router_logits; ra.idx = Lw.idx; ra.wts = Lw.wts; ra.counter = m->router_cnt;
     ra.H = H; ra.E = c.experts; ra.K = c.top_k; ra.softmax_weight = c.arch == MS_ARCH_GPT_OSS;
     ra.normalize = c.norm_topk_prob;
-    if (Lw.tc) ra.xterm = m->xterm;
+    if (Lw.tc && m->exact) {
+      ra.xdig = m->ex_xdig;
+      ra.xfe = m->ex_xfe;
+    } else if (Lw.tc) {
+      ra.xterm = m->xterm;
+    }
     LAUNCH(launch_router(dc, ra, s));
     if (m->trace && m->prof_class < 0) {
       cudaError_t e_ = cudaMemcpyAsync(m->trace_logits + (size_t)li * c.experts, m->router_logits,
@@ -570,7 +580,9 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
         ea.H = H; ea.I = c.inter; ea.K = c.top_k; ea.expert_base = m->expert_base; ea.n_local = m->n_local;
         ea.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ea.gp = m->ex_gp; ea.dp = m->ex_dp; ea.n_seg_gu = m->ex_seg_gu;
         ea.n_seg_down = m->ex_seg_down; ea.h_pad = m->ex_hpad;
-        LAUNCH(launch_exact_moe(dc, ea, s));
+        ea.xdig = m->ex_xdig; ea.xfe = m->ex_xfe; ea.adig = m->ex_adig; ea.afe = m->ex_afe; ea.cnt = m->ex_cnt;
+        LAUNCH(launch_exact_moe(dc, ea, s, 0));   // gate/up (+ activation digits)
+        LAUNCH(launch_exact_moe(dc, ea, s, 1));   // down
         lc.dpart = m->ex_dp; lc.down_b = Lw.down_b; lc.n_dseg = m->ex_seg_down; lc.dpad = m->ex_hpad;
       } else {
         ExactKqArgs ka;
@@ -579,9 +591,9 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
         ka.I = c.inter; ka.K = c.top_k; ka.expert_base = m->expert_base; ka.n_local = m->n_local;
         ka.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ka.gu_out = m->ex_kgu; ka.y = m->partial;
         LAUNCH(launch_exact_kq_moe(dc, ka, s));
+        ++nk;   // gate/up, down
         lc.partial = m->partial;
       }
-      ++nk;   // gate/up, down
       lc.idx = Lw.idx; lc.wts = Lw.wts; lc.K = c.top_k; lc.expert_base = m->expert_base; lc.n_local = m->n_local;
       if (c.ep_size > 1 && m->ep_p2p) {
         const int n = c.ep_size;
@@ -1579,6 +1591,11 @@ ms_status ms_model_finalize(ms_model* m) {
     m->ex_hpad = tc_down_tiles(H) * 128;
     s = s ? s : m->alloc(&m->ex_gp, (size_t)c.top_k * m->ex_seg_gu * 2 * c.inter * 8);
     s = s ? s : m->alloc(&m->ex_dp, (size_t)c.top_k * m->ex_seg_down * m->ex_hpad * 8);
+    s = s ? s : m->alloc(&m->ex_xdig, (size_t)(H / 32) * 256);
+    s = s ? s : m->alloc(&m->ex_xfe, (size_t)(H / 32) * 4);
+    s = s ? s : m->alloc(&m->ex_adig, (size_t)c.top_k * (c.inter / 32) * 256);
+    s = s ? s : m->alloc(&m->ex_afe, (size_t)c.top_k * (c.inter / 32) * 4);
+    s = s ? s : m->alloc(&m->ex_cnt, (size_t)c.top_k * tc_gu_tiles(c.inter) * 4);
     s = s ? s : m->alloc(&m->xterm, (size_t)tc_bterm_bytes(H / 32));
     s = s ? s : m->alloc(&m->act_terms, (size_t)c.top_k * tc_bterm_bytes(c.inter / 32));
     s = s ? s : m->alloc(&m->tc_part, (size_t)2 * tc_max_items(H, c.inter, c.top_k) * kTcMaxSeg * 128 * 4);
