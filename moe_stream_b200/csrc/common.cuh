@@ -168,7 +168,7 @@ __device__ __forceinline__ void combine_order(const PendingCombine& pc, CombineO
                                               const float* wv = nullptr) {
   if (!ids) { ids = pc.idx; wv = pc.wts; }
   int n = 0;
-  if (pc.partial || pc.seg_part || pc.dpart || pc.ep_slots) {
+  if (pc.partial || pc.seg_part || pc.ep_slots) {
     for (int k = 0; k < pc.K; ++k) {
       const int e = ids[k] - pc.expert_base;
       if (e < 0 || e >= pc.n_local) continue;
@@ -189,17 +189,9 @@ __device__ __forceinline__ void combine_order(const PendingCombine& pc, CombineO
 __device__ __forceinline__ void combine_prepare(const PendingCombine&, CombineOrder*) {}
 
 // moe_out[r], accumulated from zero in ascending expert order as the reference does
-// output row r of local slot k (order-independent experts: f64 segments rounded once + bias; else
-// the per-slot partial with its bias)
+// output row r of local slot k
 __device__ __forceinline__ float slot_value(const PendingCombine& pc, int k, int H, int r) {
-  if (pc.dpart) {
-    const double* dp = pc.dpart + (size_t)k * pc.n_dseg * pc.dpad + r;
-    double t = 0.0;
-    for (int s2 = 0; s2 < pc.n_dseg; ++s2) t += __ldcg(dp + (size_t)s2 * pc.dpad);
-    float y = (float)t;
-    if (pc.down_b) y = __fadd_rn(y, pc.down_b[(size_t)(pc.idx[k] - pc.expert_base) * H + r]);
-    return y;
-  }
+  (void)H;
   return pc.partial[(size_t)k * H + r];
 }
 
@@ -218,17 +210,6 @@ __device__ __forceinline__ float combine_at(const PendingCombine& pc, const Comb
     return acc;
   }
   float acc = 0.f;
-  if (pc.dpart) {   // ascending expert id: y = (segments summed in f64, rounded) + bias; out += y * w
-    for (int q = 0; q < co.n; ++q) {
-      const double* dp = pc.dpart + (size_t)co.slot[q] * pc.n_dseg * pc.dpad + r;
-      double t = 0.0;
-      for (int s2 = 0; s2 < pc.n_dseg; ++s2) t += __ldcg(dp + (size_t)s2 * pc.dpad);
-      float y = (float)t;
-      if (pc.down_b) y = __fadd_rn(y, pc.down_b[(size_t)(pc.idx[co.slot[q]] - pc.expert_base) * H + r]);
-      acc = __fadd_rn(acc, __fmul_rn(y, co.w[q]));
-    }
-    return acc;
-  }
   if (pc.seg_part) {
     const int t = r >> 7, ns = tc_splits(co.n * pc.seg_tiles, pc.seg_kw, pc.seg_grid);
     const size_t off = (size_t)t * kTcMaxSeg * 128 + (r & 127), qstride = (size_t)pc.seg_tiles * kTcMaxSeg * 128;
@@ -254,6 +235,15 @@ __device__ __forceinline__ float combine_at(const PendingCombine& pc, const Comb
     return acc;
   }
   // ascending expert id, each product rounded before the sum (out += y * w, layer.rs:1845-1847)
+  if (co.n <= 8) {   // the slots' loads in flight together
+    float y[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) y[q] = q < co.n ? pc.partial[(size_t)co.slot[q] * H + r] : 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (q < co.n) acc = __fadd_rn(acc, __fmul_rn(y[q], co.w[q]));
+    return acc;
+  }
   for (int q = 0; q < co.n; ++q) acc = __fadd_rn(acc, __fmul_rn(pc.partial[(size_t)co.slot[q] * H + r], co.w[q]));
   return acc;
 }

@@ -64,13 +64,8 @@ struct PendingCombine {
   int ep_rows = 0;                 // mailbox rows per parity (max(ranks, slots))
   int ep_slots = 0;                // 1: the mailbox holds each slot's output [parity][slot][H] (from its
                                    // owner rank), combined here over all slots in ascending expert id
-  // or, from the order-independent expert kernels: f64 partial dots of each slot's down rows
-  // [K][n_dseg][dpad]; slot output = (sum over segments, rounded to f32) + down bias
-  const double* dpart = nullptr;
-  const float* down_b = nullptr;   // [n_local][H] or null
-  int n_dseg = 0, dpad = 0;
   __host__ __device__ bool active() const {
-    return dense != nullptr || partial != nullptr || seg_part != nullptr || ep_recv != nullptr || dpart != nullptr;
+    return dense != nullptr || partial != nullptr || seg_part != nullptr || ep_recv != nullptr;
   }
 };
 
@@ -305,8 +300,9 @@ int attn_split_positions(int range, int units, int sm_count);
 cudaError_t launch_exact_attention(const DevCtx& c, const AttnArgs& a, int range, cudaStream_t s);
 int exact_attn_cluster(int range);
 // the expert FFN of one token over packed MXFP4 tiles: f64 partial dots of gate/up rows per K
-// segment (gp), then the activations and f64 partial dots of the down rows (dp); the consumer
-// (PendingCombine.dpart) sums the down segments, adds the bias and combines in ascending expert id
+// segment (gp), the activations as exact digits, f64 partial dots of the down rows (dp), and each
+// slot's output y = (segments summed in f64, rounded) + bias; the consumer (PendingCombine.partial
+// = y) combines the slots in ascending expert id
 struct ExactMoeArgs {
   const uint8_t* gu = nullptr;      // packed tiles, as TcMoeArgs
   const uint8_t* down = nullptr;
@@ -322,7 +318,9 @@ struct ExactMoeArgs {
   const int* xfe = nullptr;         // [H/32] their scale exponents
   int8_t* adig = nullptr;           // [K][I/32][256] digits of the activations (written by gate/up)
   int* afe = nullptr;               // [K][I/32]
-  uint32_t* cnt = nullptr;          // [K][gate/up tiles] zero-initialised, self-resetting
+  uint32_t* cnt = nullptr;          // [K][gate/up tiles] + [K][down tiles], zero-initialised, self-resetting
+  const float* down_b = nullptr;    // [E_local, H] or null
+  float* y = nullptr;               // [K][H] each slot's output (the combine's PendingCombine.partial)
   int gu_tiles = 0, down_tiles = 0;           // filled by launch_exact_moe
   int64_t gu_tile_bytes = 0, down_tile_bytes = 0;
 };

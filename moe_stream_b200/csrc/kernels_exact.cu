@@ -132,28 +132,42 @@ __global__ void __launch_bounds__(kXThreads) exact_attn_kernel(AttnArgs a, uint3
 #pragma unroll
     for (int d = 0; d < DPL; ++d) qd[h][d] = (double)qs[h * HD + lane + 32 * d];
   const int n_my = max(0, p1 - p0);
-  for (int gb = warp * G; gb < n_my; gb += kXWarps * G) {
-    double v[32];
+  // the group's K rows (G positions, DPL values per lane); the next group's are loaded before this
+  // group's dots so the L2 reads overlap
+  auto load_k = [&](int gb, float (&kr)[G][DPL]) {
 #pragma unroll
     for (int u = 0; u < G; ++u) {
       const int p = p0 + gb + u;
-      float kr[DPL];
       if (gb + u < n_my) {
         const float* krow = p == pos ? kn : kc + ((size_t)g * a.cap + slot_of(p)) * HD;
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) kr[d] = krow[lane + 32 * d];
+        for (int d = 0; d < DPL; ++d) kr[u][d] = krow[lane + 32 * d];
       } else {
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) kr[d] = 0.f;
+        for (int d = 0; d < DPL; ++d) kr[u][d] = 0.f;
       }
+    }
+  };
+  float kcur[G][DPL];
+  if (warp * G < n_my) load_k(warp * G, kcur);
+  for (int gb = warp * G; gb < n_my; gb += kXWarps * G) {
+    float knext[G][DPL];
+    if (gb + kXWarps * G < n_my) load_k(gb + kXWarps * G, knext);
+    double v[32];
+#pragma unroll
+    for (int u = 0; u < G; ++u) {
 #pragma unroll
       for (int h = 0; h < REP; ++h) {
         double t = 0.0;
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) t = fma(qd[h][d], (double)kr[d], t);
+        for (int d = 0; d < DPL; ++d) t = fma(qd[h][d], (double)kcur[u][d], t);
         v[u * REP + h] = t;
       }
     }
+#pragma unroll
+    for (int u = 0; u < G; ++u)
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) kcur[u][d] = knext[u][d];
     const double dot = warp_reduce_scatter32(v, lane);   // lane = u * REP + h
     const int u = lane / REP, h = lane % REP;
     if (gb + u < n_my) {
@@ -222,17 +236,28 @@ __global__ void __launch_bounds__(kXThreads) exact_attn_kernel(AttnArgs a, uint3
   for (int h = 0; h < REP; ++h)
 #pragma unroll
     for (int d = 0; d < DPL; ++d) o[h][d] = 0.0;
-  for (int j = warp; j < n_my; j += kXWarps) {
-    const int p = p0 + j;
-    const float* vrow = p == pos ? vn : vc + ((size_t)g * a.cap + slot_of(p)) * HD;
-    float vr[DPL];
+  constexpr int U = DPL <= 2 ? 8 : 4;   // V rows per warp per round, loaded together
+  for (int j0 = warp * U; j0 < n_my; j0 += kXWarps * U) {
+    float vr[U][DPL];
 #pragma unroll
-    for (int d = 0; d < DPL; ++d) vr[d] = vrow[lane + 32 * d];
+    for (int u = 0; u < U; ++u) {
+      const int p = p0 + j0 + u;
+      if (j0 + u < n_my) {
+        const float* vrow = p == pos ? vn : vc + ((size_t)g * a.cap + slot_of(p)) * HD;
 #pragma unroll
-    for (int h = 0; h < REP; ++h) {
-      const float pw = sc[(size_t)h * max_per_cta + j];
+        for (int d = 0; d < DPL; ++d) vr[u][d] = vrow[lane + 32 * d];
+      }
+    }
 #pragma unroll
-      for (int d = 0; d < DPL; ++d) o[h][d] = fma((double)pw, (double)vr[d], o[h][d]);
+    for (int u = 0; u < U; ++u) {
+      if (j0 + u < n_my) {
+#pragma unroll
+        for (int h = 0; h < REP; ++h) {
+          const float pw = sc[(size_t)h * max_per_cta + j0 + u];
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) o[h][d] = fma((double)pw, (double)vr[u][d], o[h][d]);
+        }
+      }
     }
   }
 #pragma unroll
@@ -523,8 +548,11 @@ __global__ void __launch_bounds__(kEThreads, 3) exact_gu_kernel(ExactMoeArgs a, 
   (void)err;
 }
 
-// down: grid (segments, down tiles, slots), over the activation digits written by gate/up
+// down: grid (segments, down tiles, slots), over the activation digits written by gate/up.  The
+// last CTA to finish a (tile, slot) sums its 128 rows over the segments (in segment order, rounded
+// once), adds the bias and writes the slot's output rows y[k][r].
 __global__ void __launch_bounds__(kEThreads, 3) exact_down_kernel(ExactMoeArgs a, uint32_t* err) {
+  __shared__ uint32_t last;
   const int seg = blockIdx.x, mt = blockIdx.y, k = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kc = a.I / 32, c0 = seg * kESegChunks, c1 = min(kc, c0 + kESegChunks);
@@ -536,11 +564,36 @@ __global__ void __launch_bounds__(kEThreads, 3) exact_down_kernel(ExactMoeArgs a
   const size_t ch = (size_t)k * kc + c0;
   double o0, o1;
   rows16_seg(tile, kc, 16 * warp, c0, c1 - c0, a.adig + ch * 256, a.afe + ch, lane, o0, o1);
+  const double* dk = a.dp + (size_t)k * a.n_seg_down * a.h_pad;
   if ((lane & 3) == 0) {
-    double* dp = a.dp + ((size_t)k * a.n_seg_down + seg) * a.h_pad + (size_t)mt * 128 + 16 * warp;
+    double* dp = const_cast<double*>(dk) + (size_t)seg * a.h_pad + (size_t)mt * 128 + 16 * warp;
     dp[lane >> 2] = o0;
     dp[8 + (lane >> 2)] = o1;
   }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* c = a.cnt + (size_t)a.K * a.gu_tiles + (size_t)k * a.down_tiles + mt;
+    last = atomicAdd(c, 1u) == (uint32_t)a.n_seg_down - 1 ? 1u : 0u;
+    if (last) *c = 0u;
+  }
+  __syncthreads();
+  if (!last || threadIdx.x >= 128) return;
+  __threadfence();
+  const int r = mt * 128 + threadIdx.x;
+  if (r >= a.H) return;
+  double t = 0.0;
+  for (int s0 = 0; s0 < a.n_seg_down; s0 += 8) {   // 8 loads in flight, summed in segment order
+    double v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = s0 + j < a.n_seg_down ? __ldcg(dk + (size_t)(s0 + j) * a.h_pad + r) : 0.0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (s0 + j < a.n_seg_down) t += v[j];
+  }
+  float y = (float)t;
+  if (a.down_b) y = __fadd_rn(y, a.down_b[(size_t)e * a.H + r]);
+  a.y[(size_t)k * a.H + r] = y;
   (void)err;
 }
 
@@ -718,7 +771,7 @@ int exact_seg_count(int kc) { return (kc + kESegChunks - 1) / kESegChunks; }
 cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a0, cudaStream_t s, int part) {
   ExactMoeArgs a = a0;
   if (!tc_supported(a.H, a.I) || a.K < 1 || a.K > 16 || !a.gp || !a.dp || !a.xdig || !a.xfe || !a.adig || !a.afe ||
-      !a.cnt || a.I % 64)
+      !a.cnt || !a.y || a.I % 64)
     return cudaErrorInvalidValue;
   a.gu_tiles = tc_gu_tiles(a.I);
   a.down_tiles = tc_down_tiles(a.H);

@@ -581,9 +581,10 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
         ea.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ea.gp = m->ex_gp; ea.dp = m->ex_dp; ea.n_seg_gu = m->ex_seg_gu;
         ea.n_seg_down = m->ex_seg_down; ea.h_pad = m->ex_hpad;
         ea.xdig = m->ex_xdig; ea.xfe = m->ex_xfe; ea.adig = m->ex_adig; ea.afe = m->ex_afe; ea.cnt = m->ex_cnt;
+        ea.down_b = Lw.down_b; ea.y = m->partial;
         LAUNCH(launch_exact_moe(dc, ea, s, 0));   // gate/up (+ activation digits)
         LAUNCH(launch_exact_moe(dc, ea, s, 1));   // down
-        lc.dpart = m->ex_dp; lc.down_b = Lw.down_b; lc.n_dseg = m->ex_seg_down; lc.dpad = m->ex_hpad;
+        lc.partial = m->partial;
       } else {
         ExactKqArgs ka;
         ka.gate = Lw.gate; ka.up = Lw.up; ka.down = Lw.down; ka.gate_fmt = Lw.gate_q; ka.down_fmt = Lw.down_q;
@@ -1595,7 +1596,7 @@ ms_status ms_model_finalize(ms_model* m) {
     s = s ? s : m->alloc(&m->ex_xfe, (size_t)(H / 32) * 4);
     s = s ? s : m->alloc(&m->ex_adig, (size_t)c.top_k * (c.inter / 32) * 256);
     s = s ? s : m->alloc(&m->ex_afe, (size_t)c.top_k * (c.inter / 32) * 4);
-    s = s ? s : m->alloc(&m->ex_cnt, (size_t)c.top_k * tc_gu_tiles(c.inter) * 4);
+    s = s ? s : m->alloc(&m->ex_cnt, (size_t)c.top_k * (tc_gu_tiles(c.inter) + tc_down_tiles(H)) * 4);
     s = s ? s : m->alloc(&m->xterm, (size_t)tc_bterm_bytes(H / 32));
     s = s ? s : m->alloc(&m->act_terms, (size_t)c.top_k * tc_bterm_bytes(c.inter / 32));
     s = s ? s : m->alloc(&m->tc_part, (size_t)2 * tc_max_items(H, c.inter, c.top_k) * kTcMaxSeg * 128 * 4);
