@@ -52,6 +52,14 @@ __device__ __forceinline__ double warp_reduce_scatter32(double (&v)[32], int lan
   return v[0];
 }
 
+// D += A B on the f64 tensor cores (m8n8k4): lane (g, t) = (lane >> 2, lane & 3) holds A[g][t],
+// B[t][g] and D[g][2t], D[g][2t + 1]
+__device__ __forceinline__ void dmma_884(double& d0, double& d1, double a, double b) {
+  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};\n"
+               : "+d"(d0), "+d"(d1)
+               : "d"(a), "d"(b));
+}
+
 template <int HD, int REP>
 __global__ void __launch_bounds__(kXThreads) exact_attn_kernel(AttnArgs a, uint32_t* err, int max_per_cta) {
   constexpr int DPL = HD / 32;
@@ -125,54 +133,96 @@ __global__ void __launch_bounds__(kXThreads) exact_attn_kernel(AttnArgs a, uint3
     __syncwarp();
   }
   __syncthreads();
-  // ---- scores: s = round(q . k) * scale (f64 dot), groups of G positions per warp ----
-  double qd[REP][DPL];
-#pragma unroll
-  for (int h = 0; h < REP; ++h)
-#pragma unroll
-    for (int d = 0; d < DPL; ++d) qd[h][d] = (double)qs[h * HD + lane + 32 * d];
+  // ---- scores: s = round(q . k) * scale (f64 dot) ----
   const int n_my = max(0, p1 - p0);
-  // the group's K rows (G positions, DPL values per lane); the next group's are loaded before this
-  // group's dots so the L2 reads overlap
-  auto load_k = [&](int gb, float (&kr)[G][DPL]) {
+  if constexpr (REP == 8) {
+    // f64 tensor cores: per 8 positions, A = K rows (8 x HD), B = the 8 queries; the k order is
+    // permuted so lane (g, t) holds dims t*KQ .. t*KQ + KQ - 1 of position g and of query g
+    constexpr int KQ = HD / 4;
+    const int g8 = lane >> 2, t4 = lane & 3;
+    double qf[KQ];
 #pragma unroll
-    for (int u = 0; u < G; ++u) {
-      const int p = p0 + gb + u;
-      if (gb + u < n_my) {
-        const float* krow = p == pos ? kn : kc + ((size_t)g * a.cap + slot_of(p)) * HD;
+    for (int kk = 0; kk < KQ; ++kk) qf[kk] = (double)qs[g8 * HD + t4 * KQ + kk];
+    auto load_k = [&](int pb, float (&kr)[KQ]) {
+      const int p = p0 + pb + g8;
+      if (pb + g8 < n_my) {
+        const float* krow = (p == pos ? kn : kc + ((size_t)g * a.cap + slot_of(p)) * HD) + t4 * KQ;
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) kr[u][d] = krow[lane + 32 * d];
+        for (int kk = 0; kk < KQ; kk += 4) {
+          const float4 v4 = *reinterpret_cast<const float4*>(krow + kk);
+          kr[kk] = v4.x; kr[kk + 1] = v4.y; kr[kk + 2] = v4.z; kr[kk + 3] = v4.w;
+        }
       } else {
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) kr[u][d] = 0.f;
+        for (int kk = 0; kk < KQ; ++kk) kr[kk] = 0.f;
       }
-    }
-  };
-  float kcur[G][DPL];
-  if (warp * G < n_my) load_k(warp * G, kcur);
-  for (int gb = warp * G; gb < n_my; gb += kXWarps * G) {
-    float knext[G][DPL];
-    if (gb + kXWarps * G < n_my) load_k(gb + kXWarps * G, knext);
-    double v[32];
+    };
+    float kcur[KQ];
+    if (warp * 8 < n_my) load_k(warp * 8, kcur);
+    for (int pb = warp * 8; pb < n_my; pb += kXWarps * 8) {
+      float knext[KQ];
+      if (pb + kXWarps * 8 < n_my) load_k(pb + kXWarps * 8, knext);
+      double c0 = 0.0, c1 = 0.0, e0 = 0.0, e1 = 0.0;   // two accumulation chains
 #pragma unroll
-    for (int u = 0; u < G; ++u) {
-#pragma unroll
-      for (int h = 0; h < REP; ++h) {
-        double t = 0.0;
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) t = fma(qd[h][d], (double)kcur[u][d], t);
-        v[u * REP + h] = t;
+      for (int kk = 0; kk < KQ; kk += 2) {
+        dmma_884(c0, c1, (double)kcur[kk], qf[kk]);
+        dmma_884(e0, e1, (double)kcur[kk + 1], qf[kk + 1]);
       }
+      if (pb + g8 < n_my) {   // D[position g][queries 2t, 2t + 1]
+        sc[(size_t)(2 * t4) * max_per_cta + pb + g8] = __fmul_rn((float)(c0 + e0), a.scale);
+        sc[(size_t)(2 * t4 + 1) * max_per_cta + pb + g8] = __fmul_rn((float)(c1 + e1), a.scale);
+      }
+#pragma unroll
+      for (int kk = 0; kk < KQ; ++kk) kcur[kk] = knext[kk];
     }
+  } else {
+    double qd[REP][DPL];
 #pragma unroll
-    for (int u = 0; u < G; ++u)
+    for (int h = 0; h < REP; ++h)
 #pragma unroll
-      for (int d = 0; d < DPL; ++d) kcur[u][d] = knext[u][d];
-    const double dot = warp_reduce_scatter32(v, lane);   // lane = u * REP + h
-    const int u = lane / REP, h = lane % REP;
-    if (gb + u < n_my) {
-      const float s = __fmul_rn((float)dot, a.scale);
-      sc[(size_t)h * max_per_cta + gb + u] = s;
+      for (int d = 0; d < DPL; ++d) qd[h][d] = (double)qs[h * HD + lane + 32 * d];
+    // the group's K rows (G positions, DPL values per lane); the next group's are loaded before this
+    // group's dots so the L2 reads overlap
+    auto load_k = [&](int gb, float (&kr)[G][DPL]) {
+#pragma unroll
+      for (int u = 0; u < G; ++u) {
+        const int p = p0 + gb + u;
+        if (gb + u < n_my) {
+          const float* krow = p == pos ? kn : kc + ((size_t)g * a.cap + slot_of(p)) * HD;
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) kr[u][d] = krow[lane + 32 * d];
+        } else {
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) kr[u][d] = 0.f;
+        }
+      }
+    };
+    float kcur[G][DPL];
+    if (warp * G < n_my) load_k(warp * G, kcur);
+    for (int gb = warp * G; gb < n_my; gb += kXWarps * G) {
+      float knext[G][DPL];
+      if (gb + kXWarps * G < n_my) load_k(gb + kXWarps * G, knext);
+      double v[32];
+#pragma unroll
+      for (int u = 0; u < G; ++u) {
+#pragma unroll
+        for (int h = 0; h < REP; ++h) {
+          double t = 0.0;
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) t = fma(qd[h][d], (double)kcur[u][d], t);
+          v[u * REP + h] = t;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < G; ++u)
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) kcur[u][d] = knext[u][d];
+      const double dot = warp_reduce_scatter32(v, lane);   // lane = u * REP + h
+      const int u = lane / REP, h = lane % REP;
+      if (gb + u < n_my) {
+        const float s = __fmul_rn((float)dot, a.scale);
+        sc[(size_t)h * max_per_cta + gb + u] = s;
+      }
     }
   }
   __syncthreads();
@@ -230,40 +280,82 @@ __global__ void __launch_bounds__(kXThreads) exact_attn_kernel(AttnArgs a, uint3
     sc[(size_t)h * max_per_cta + j] = __fdiv_rn(sc[(size_t)h * max_per_cta + j], s_den[h]);
   }
   __syncthreads();
-  // ---- P*V: weights p = e / den (f32), f64 accumulation over positions, lanes over dims ----
-  double o[REP][DPL];
+  // ---- P*V: weights p = e / den (f32), f64 accumulation over positions ----
+  if constexpr (REP == 8) {
+    // f64 tensor cores: per 4 positions, A = V^T (8 dims x 4 positions), B = P^T (4 positions x 8
+    // queries); lane (g, t) takes position t and dims g*MT .. g*MT + MT - 1 (m-tile mt = dim g*MT + mt)
+    constexpr int MT = HD / 8;
+    const int g8 = lane >> 2, t4 = lane & 3;
+    double o[MT][2];
 #pragma unroll
-  for (int h = 0; h < REP; ++h)
+    for (int mt = 0; mt < MT; ++mt) o[mt][0] = o[mt][1] = 0.0;
+    for (int j0 = warp * 8; j0 < n_my; j0 += kXWarps * 8) {   // two 4-position steps per round
+      float vr[2][MT];
+      double pw[2];
 #pragma unroll
-    for (int d = 0; d < DPL; ++d) o[h][d] = 0.0;
-  constexpr int U = DPL <= 2 ? 8 : 4;   // V rows per warp per round, loaded together
-  for (int j0 = warp * U; j0 < n_my; j0 += kXWarps * U) {
-    float vr[U][DPL];
+      for (int u = 0; u < 2; ++u) {
+        const int j = j0 + 4 * u + t4;
+        if (j < n_my) {
+          const int p = p0 + j;
+          const float* vrow = (p == pos ? vn : vc + ((size_t)g * a.cap + slot_of(p)) * HD) + g8 * MT;
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int p = p0 + j0 + u;
-      if (j0 + u < n_my) {
-        const float* vrow = p == pos ? vn : vc + ((size_t)g * a.cap + slot_of(p)) * HD;
+          for (int mt = 0; mt < MT; mt += 4) {
+            const float4 v4 = *reinterpret_cast<const float4*>(vrow + mt);
+            vr[u][mt] = v4.x; vr[u][mt + 1] = v4.y; vr[u][mt + 2] = v4.z; vr[u][mt + 3] = v4.w;
+          }
+          pw[u] = (double)sc[(size_t)g8 * max_per_cta + j];
+        } else {
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) vr[u][d] = vrow[lane + 32 * d];
+          for (int mt = 0; mt < MT; ++mt) vr[u][mt] = 0.f;
+          pw[u] = 0.0;
+        }
       }
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) dmma_884(o[mt][0], o[mt][1], (double)vr[u][mt], pw[u]);
     }
+    // D[dim g*MT + mt][queries 2t, 2t + 1]
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (j0 + u < n_my) {
+    for (int mt = 0; mt < MT; ++mt) {
+      wred[((size_t)warp * REP + 2 * t4) * HD + g8 * MT + mt] = o[mt][0];
+      wred[((size_t)warp * REP + 2 * t4 + 1) * HD + g8 * MT + mt] = o[mt][1];
+    }
+  } else {
+    double o[REP][DPL];
 #pragma unroll
-        for (int h = 0; h < REP; ++h) {
-          const float pw = sc[(size_t)h * max_per_cta + j0 + u];
+    for (int h = 0; h < REP; ++h)
 #pragma unroll
-          for (int d = 0; d < DPL; ++d) o[h][d] = fma((double)pw, (double)vr[u][d], o[h][d]);
+      for (int d = 0; d < DPL; ++d) o[h][d] = 0.0;
+    constexpr int U = DPL <= 2 ? 8 : 4;   // V rows per warp per round, loaded together
+    for (int j0 = warp * U; j0 < n_my; j0 += kXWarps * U) {
+      float vr[U][DPL];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int p = p0 + j0 + u;
+        if (j0 + u < n_my) {
+          const float* vrow = p == pos ? vn : vc + ((size_t)g * a.cap + slot_of(p)) * HD;
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) vr[u][d] = vrow[lane + 32 * d];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (j0 + u < n_my) {
+#pragma unroll
+          for (int h = 0; h < REP; ++h) {
+            const float pw = sc[(size_t)h * max_per_cta + j0 + u];
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) o[h][d] = fma((double)pw, (double)vr[u][d], o[h][d]);
+          }
         }
       }
     }
+#pragma unroll
+    for (int h = 0; h < REP; ++h)
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) wred[((size_t)warp * REP + h) * HD + lane + 32 * d] = o[h][d];
   }
-#pragma unroll
-  for (int h = 0; h < REP; ++h)
-#pragma unroll
-    for (int d = 0; d < DPL; ++d) wred[((size_t)warp * REP + h) * HD + lane + 32 * d] = o[h][d];
   __syncthreads();
   // every CTA's partial P*V to the rank that owns its slice of the outputs (32-element multiples)
   const int NS = min(C, REP * HD / 32), SL = REP * HD / NS;
