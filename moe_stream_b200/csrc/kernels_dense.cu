@@ -512,9 +512,11 @@ __global__ void __launch_bounds__(kTThreads) attn_tile_kernel(AttnArgs a, uint32
   } else {
     for (int h = threadIdx.x; h < REP; h += kTThreads) { part[h * (HD + 2)] = -INFINITY; part[h * (HD + 2) + 1] = 0.f; }
   }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) last = (atomicAdd(&a.cnt[kh], 1u) == (uint32_t)S - 1) ? 1u : 0u;
+  __syncthreads();   // every thread's stores, then (cumulative) thread 0's fence and count
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = (atomicAdd(&a.cnt[kh], 1u) == (uint32_t)S - 1) ? 1u : 0u;
+  }
   __syncthreads();
   if (!last) return;
   __threadfence();
@@ -825,9 +827,11 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
   } else {
     for (int h = threadIdx.x; h < REP; h += kAThreads) { part[h * (HD + 2)] = -INFINITY; part[h * (HD + 2) + 1] = 0.f; }
   }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) last = (atomicAdd(&a.cnt[vh], 1u) == (uint32_t)S - 1) ? 1u : 0u;
+  __syncthreads();   // every thread's stores, then (cumulative) thread 0's fence and count
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = (atomicAdd(&a.cnt[vh], 1u) == (uint32_t)S - 1) ? 1u : 0u;
+  }
   __syncthreads();
   if (!last) return;
   __threadfence();

@@ -603,9 +603,11 @@ __global__ void __launch_bounds__(kEThreads, 3) exact_gu_kernel(ExactMoeArgs a, 
     o[lane >> 2] = o0;
     o[8 + (lane >> 2)] = o1;
   }
-  __threadfence();
+  // the barrier orders every thread's stores before thread 0's fence (cumulative), which orders them
+  // before its count
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence();
     uint32_t* c = a.cnt + (size_t)k * a.gu_tiles + mt;
     last = atomicAdd(c, 1u) == (uint32_t)a.n_seg_gu - 1 ? 1u : 0u;
     if (last) *c = 0u;
@@ -662,9 +664,11 @@ __global__ void __launch_bounds__(kEThreads, 3) exact_down_kernel(ExactMoeArgs a
     dp[lane >> 2] = o0;
     dp[8 + (lane >> 2)] = o1;
   }
-  __threadfence();
+  // the barrier orders every thread's stores before thread 0's fence (cumulative), which orders them
+  // before its count
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence();
     uint32_t* c = a.cnt + (size_t)a.K * a.gu_tiles + (size_t)k * a.down_tiles + mt;
     last = atomicAdd(c, 1u) == (uint32_t)a.n_seg_down - 1 ? 1u : 0u;
     if (last) *c = 0u;
@@ -918,9 +922,9 @@ __global__ void __launch_bounds__(256) exact_argmax_refine_kernel(const uint16_t
       else atomicOr(err, EF_BAD_SHAPE);
     }
   }
-  __threadfence();
-  __syncthreads();
+  __syncthreads();   // every thread's stores, then (cumulative) thread 0's fence and count
   if (threadIdx.x == 0) {
+    __threadfence();
     last = (atomicAdd(done, 1u) == gridDim.x - 1) ? 1u : 0u;
     s_best = 0ull;
   }
