@@ -283,24 +283,36 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 }
 __device__ __forceinline__ float expcr(float x) { return (float)exp((double)x); }
 
-// Exact integer digits of one 32-element f32 block (one element per lane), the activation side of
-// the exact MXFP4 expert dots: X_j = round(x_j 2^F) with F = 180 - (the block's largest biased
-// exponent), so |X_j| < 2^54 and X keeps every bit of the block's larger elements; X is written as
-// 7 signed base-256 digits, dig[n * 32 + lane] = digit n of element lane (n = 0..6; row 7 is never
-// read).  *fexp = 1023 - 128 - F, the block's part of the double scale exponent.
-__device__ __forceinline__ void exact_digits_warp(float x, int lane, int8_t* dig, int* fexp) {
+// Exact base-4 terms of one 32-element f32 block (one element per lane), the B operand of the exact
+// MXFP4 expert dots on the tensor cores: X_j = round(|x_j| 2^F) with F = 180 - (the block's largest
+// biased exponent), so X_j < 2^54 and X keeps every bit of the block's larger elements; X is cut
+// into kExactDigits = 27 base-4 digits and term d of element j is the e2m1 code of sign(x_j) * d_d
+// (values 0, 1, 2, 3).  The chunk's 1 KB block holds 64 B columns of 32 codes (16 bytes, element 2i
+// in the low nibble of byte i); the block's terms are columns parity * 32 + d, where parity = the
+// chunk index & 1, and every other column stays zero, so one K = 64 MMA over two chunks keeps the
+// chunks' dots apart.  *fexp = 1023 - 127 - F, the block's part of the double scale exponent.
+constexpr int kExactDigits = 27;
+__device__ __forceinline__ void exact_bterm_warp(float x, int lane, uint8_t* blk, int parity, int* fexp) {
   int eb = (int)((__float_as_uint(x) >> 23) & 0xFFu);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) eb = max(eb, __shfl_xor_sync(0xffffffffu, eb, o));
   const int F = 180 - eb;
-  long long X = __double2ll_rn((double)x * __longlong_as_double((long long)(F + 1023) << 52));
+  const unsigned long long X =
+      (unsigned long long)__double2ll_rn(fabs((double)x) * __longlong_as_double((long long)(F + 1023) << 52));
+  const uint32_t sgn = (__float_as_uint(x) >> 31) << 3;
+  uint32_t* col = reinterpret_cast<uint32_t*>(blk + parity * 32 * 16) + (lane >> 3);
 #pragma unroll
-  for (int n = 0; n < 7; ++n) {
-    const int d = (int)(int8_t)(X & 255);   // the balanced digit in [-128, 127]
-    X = (X - d) >> 8;
-    dig[n * 32 + lane] = (int8_t)d;
+  for (int d = 0; d < kExactDigits; ++d) {
+    const uint32_t dig = (uint32_t)(X >> (2 * d)) & 3u;
+    uint32_t code = (0x5420u >> (4 * dig)) & 0xFu;   // e2m1 of 0, 1, 2, 3
+    code |= code ? sgn : 0u;
+    uint32_t w = code << (4 * (lane & 7));           // 8 lanes' codes -> one 32-bit word
+    w |= __shfl_xor_sync(0xffffffffu, w, 1);
+    w |= __shfl_xor_sync(0xffffffffu, w, 2);
+    w |= __shfl_xor_sync(0xffffffffu, w, 4);
+    if ((lane & 7) == 0) col[d * 4] = w;
   }
-  if (lane == 0) *fexp = 1023 - 128 - F;
+  if (lane == 0) *fexp = 1023 - 127 - F;
 }
 
 // inverse RMS with the reference's op sequence (ops/norm.rs:16-37): x.sqr() in f32, mean_keepdim =

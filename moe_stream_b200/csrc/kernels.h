@@ -131,8 +131,8 @@ struct RouterArgs {
   int softmax_weight = 1;         // GPT-OSS: softmax over the selected k logits
   int normalize = 0;              // renormalise top-k probabilities (norm_topk_prob)
   uint8_t* xterm = nullptr;       // optional: the normed x as MXFP4 B terms (tc_bterm_bytes(H/32))
-  int8_t* xdig = nullptr;         // optional: the normed x as exact digits ([H/32][256], exact_digits_warp)
-  int* xfe = nullptr;             //   and their scale exponents [H/32]
+  uint8_t* xbt = nullptr;         // optional: the normed x as exact B terms ([H/32][1024], exact_bterm_warp,
+  int* xfe = nullptr;             //   zeroed once) and their scale exponents [H/32]
   int batch = 1;                  // grid.y = tokens: h/xn + b*H, logits + b*E, idx/wts + b*K, counter + b
 };
 cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s);
@@ -314,14 +314,15 @@ struct ExactMoeArgs {
   double* gp = nullptr;             // [K][n_seg_gu][2 I]
   double* dp = nullptr;             // [K][n_seg_down][h_pad]
   int n_seg_gu = 0, n_seg_down = 0, h_pad = 0;
-  const int8_t* xdig = nullptr;     // [H/32][256] digits of x (exact_digits_warp), written by the router
-  const int* xfe = nullptr;         // [H/32] their scale exponents
-  int8_t* adig = nullptr;           // [K][I/32][256] digits of the activations (written by gate/up)
-  int* afe = nullptr;               // [K][I/32]
+  const uint8_t* xbt = nullptr;     // [H/32][1024] exact base-4 B terms of x (exact_bterm_warp), from the router
+  const int* xfe = nullptr;         // [H/32 + 4] their scale exponents (+ padding for 16-byte copies)
+  uint8_t* abt = nullptr;           // [K][I/32][1024] B terms of the activations (written by gate/up; zeroed once)
+  int* afe = nullptr;               // [K][I/32 rounded up to 4] (16-byte copies of 4 chunks' exponents)
   uint32_t* cnt = nullptr;          // [K][gate/up tiles] + [K][down tiles], zero-initialised, self-resetting
   const float* down_b = nullptr;    // [E_local, H] or null
   float* y = nullptr;               // [K][H] each slot's output (the combine's PendingCombine.partial)
   int gu_tiles = 0, down_tiles = 0;           // filled by launch_exact_moe
+  uint32_t* err = nullptr;                    // filled by launch_exact_moe
   int64_t gu_tile_bytes = 0, down_tile_bytes = 0;
 };
 int exact_seg_count(int kc);        // K segments over kc 32-element chunks

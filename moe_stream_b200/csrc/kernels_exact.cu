@@ -24,6 +24,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "umma.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -436,139 +437,34 @@ cudaError_t launch_exact_attn_hd(const AttnArgs& a, const DevCtx& c, int rep, in
   return cudaErrorInvalidValue;
 }
 
-// ============================ experts (MXFP4 tensor-core tiles) ============================
-constexpr int kEThreads = 256;    // 8 warps: one 16-row group of the 128-row tile each
-constexpr int kESegChunks = 8;    // 32-element chunks per K segment (within one 16-chunk slab)
+// ============================ experts (MXFP4 tiles on tcgen05) ============================
+// The expert rows are the packed MXFP4 tiles of the tensor-core path (128 rows; slabs of 16 chunk
+// columns, codes then 512-byte scale groups).  A unit is one K-word of one (slot, tile) item: 4
+// chunk columns (the last unit of a row may hold 2) and their scale group.  Per unit the tensor
+// core computes, with every block scale set to 1, D[row][parity * 32 + d] = sum over the 32
+// elements of chunk (2p + parity) of e2m1(w) * term_d(x) for each K = 64 pair p -- integer
+// multiples of 1/2 below 2^10, exact in f32.  The epilogue folds 7 digits at a time in f32 (still
+// exact: below 2^23 halves), then applies 2^(E_w - 127 - F) and accumulates in f64.  Warp roles:
+// warp 0 streams units with 1-D bulk copies (codes, scale group, B terms), warp 1 owns tensor
+// memory and issues the MMAs (one elected thread), warps 2-17 drain the accumulators (four warps
+// per TMEM lane quadrant, one chunk each).  The units of all (slot, tile) items are cut into equal
+// contiguous ranges, one per CTA; the last CTA to finish an item reduces its per-unit f64 partials.
+constexpr int kUC = 4;                          // chunk columns per unit
+constexpr int kUStA = kUC * 2048;               // A codes
+constexpr int kUStS = 512;                      // A scale group
+constexpr int kUStB = kUC * 1024;               // B terms: 64 columns x 16 bytes per chunk
+constexpr int kUStF = 16;                       // the 4 chunks' scale exponents of B (x / activation)
+constexpr int kUStage = kUStA + kUStS + kUStB + kUStF;
+constexpr int kUStages = 6;
+constexpr int kUAcc = 3;                        // accumulators of 128 columns (two K = 64 pairs)
+constexpr int kUEpiWarps = 16;
+constexpr int kUThreads = 64 + 32 * kUEpiWarps;
+constexpr int kUTmemCols = 512;
+constexpr uint32_t kUSfCol = kUAcc * 128;       // unit block scales: A at +0, B at +4
+constexpr int kUMaxSlots = 16;
+static_assert(kUSfCol + 8 <= kUTmemCols, "tensor memory budget");
 
-// one row's dot over chunks [c0, c1) of a packed tile (tile layout: slabs of 16 chunk columns,
-// codes [chunk][128 rows][16 B] then a 512-byte scale group per 4 chunks, element 2i / 2i+1 in the
-// low / high nibble of code byte i), x as doubles in shared memory
-// ---- exact dots of MXFP4 rows on the integer tensor cores ----
-// x (f32) is written per 32-element block as X_j = round(x_j 2^F) with F = 180 - (the block's largest
-// biased exponent), so |X_j| < 2^54 and X carries every bit of the block's larger elements (smaller
-// ones lose bits below 2^-54 of the block maximum, as a double accumulation would).  X is split into
-// 7 signed base-256 digits; the MXFP4 codes become doubled e2m1 integers n in [-12, 12].  One
-// mma.sync.m16n8k32.s8 per (16 rows, 32 elements) then yields, exactly in int32, the 7 digit dots of
-// 16 rows (B column = digit); each lane folds its two digits into a double scaled by
-// 2^(E_w - 128 - F + 16t) and accumulates in double.
-// four e2m1 codes (16 bits, element order low nibble first) -> four doubled values as int8
-__device__ __forceinline__ uint32_t e2m1x4_to_s8(uint32_t u) {
-  const uint32_t m7 = u & 0x7777u;
-  const uint32_t pos = __byte_perm(0x03020100u, 0x0C080604u, m7);   // 0 1 2 3 4 6 8 12
-  const uint32_t neg = __byte_perm(0xFDFEFF00u, 0xF4F8FAFCu, m7);   // their negatives
-  return __byte_perm(pos, neg, ((u >> 1) & 0x4444u) | 0x3210u);
-}
-
-__device__ __forceinline__ double i32_to_double(int v) {   // exact, on the FP64 pipe
-  const double magic = 6755399441055744.0;                   // 2^52 + 2^51
-  return __hiloint2double(0x43380000, v ^ 0x80000000) - (magic + 2147483648.0);
-}
-
-__device__ __forceinline__ void mma_s8_m16n8k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                                uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// Rows rb .. rb+15 of a packed tile over chunks [c0, c1) (inside one 16-chunk slab).  The MMA's k
-// order is permuted so each lane's A elements are contiguous: lane (g, t) takes code word t of rows
-// g and g + 8 (elements 8t .. 8t+7) as its k = 4t.. and k = 16 + 4t.. fragments, and the activation
-// digits are read in the same order.  The lane's code words and scale bytes are loaded as soon as
-// the expert is known ...
-struct Rows16 {
-  uint32_t w[kESegChunks][2];
-  uint32_t es[4];   // scale bytes: rows r0 / r1 (es[0..1] / es[2..3]) of the segment's two 4-chunk groups
-};
-static_assert(kESegChunks == 8, "a segment is two 4-chunk scale groups");
-// n = c1 - c0 chunks (c0 a multiple of 8); FULL: n == 8
-template <bool FULL>
-__device__ __forceinline__ void rows16_load(const uint8_t* tile, int kc, int rb, int c0, int n, int lane, Rows16& R) {
-  const int g = lane >> 2, t = lane & 3;
-  const int slab = c0 >> 4, nchs = min(16, kc - slab * 16), cl0 = c0 & 15;
-  const uint8_t* sb = tile + (size_t)slab * (16 * 2048 + 4 * 512);
-  const uint8_t* cb = sb + (size_t)cl0 * 2048 + (rb + g) * 16 + 4 * t;
-#pragma unroll
-  for (int i = 0; i < kESegChunks; ++i) {
-    if (FULL || i < n) {
-      R.w[i][0] = __ldcs(reinterpret_cast<const uint32_t*>(cb + i * 2048));
-      R.w[i][1] = __ldcs(reinterpret_cast<const uint32_t*>(cb + i * 2048 + 8 * 16));
-    } else {
-      R.w[i][0] = R.w[i][1] = 0u;
-    }
-  }
-  // the scale group of 4 chunks holds, per row r, the 4 chunks' scale bytes as one aligned word at
-  // 16 (r & 31) + 4 (r >> 5)
-  const int r0 = rb + g, r1 = rb + g + 8;
-  const uint8_t* sg = sb + nchs * 2048 + (cl0 >> 2) * 512;
-  R.es[0] = __ldcs(reinterpret_cast<const uint32_t*>(sg + 16 * (r0 & 31) + 4 * (r0 >> 5)));
-  R.es[2] = __ldcs(reinterpret_cast<const uint32_t*>(sg + 16 * (r1 & 31) + 4 * (r1 >> 5)));
-  if (FULL || n > 4) {
-    R.es[1] = __ldcs(reinterpret_cast<const uint32_t*>(sg + 512 + 16 * (r0 & 31) + 4 * (r0 >> 5)));
-    R.es[3] = __ldcs(reinterpret_cast<const uint32_t*>(sg + 512 + 16 * (r1 & 31) + 4 * (r1 >> 5)));
-  } else {
-    R.es[1] = R.es[3] = 0u;
-  }
-}
-
-// ... then, once the activation digits are written (dig: the segment's first chunk, 256 bytes per
-// chunk; fe: its scale exponents), the dots: returns, in lanes with (lane & 3) == 0, the f64 dots of
-// rows rb + (lane >> 2) (out0) and rb + 8 + (lane >> 2) (out1).  B column g of the MMA is digit g;
-// column 7 is zero.  The scale of a (row, chunk) term is 2^(E_w + fe + 16 t - 1023), built as the
-// high word (E_w + fe + 16 t) << 20 of a double.
-template <bool FULL>
-__device__ __forceinline__ void rows16_dot(const Rows16& R, int n, const int8_t* dig, const int* fe, int lane,
-                                           double& out0, double& out1) {
-  const int g = lane >> 2, t = lane & 3;
-  uint2 bv[kESegChunks];
-  int fx[kESegChunks];
-  const int8_t* lb = dig + g * 32 + 8 * t;
-#pragma unroll
-  for (int i = 0; i < kESegChunks; ++i) {
-    bv[i] = make_uint2(0u, 0u);
-    fx[i] = 0;
-    if (FULL || i < n) {
-      if (g < 7) bv[i] = __ldcg(reinterpret_cast<const uint2*>(lb + i * 256));   // digits of elements 8t .. 8t+7
-      fx[i] = (__ldcg(fe + i) + 16 * t) << 20;
-    }
-  }
-  double acc0 = 0.0, acc1 = 0.0;
-#pragma unroll
-  for (int i = 0; i < kESegChunks; ++i) {
-    if (FULL || i < n) {
-      int d[4] = {0, 0, 0, 0};
-      const uint32_t w0 = R.w[i][0], w1 = R.w[i][1];
-      mma_s8_m16n8k32(d, e2m1x4_to_s8(w0), e2m1x4_to_s8(w1), e2m1x4_to_s8(w0 >> 16), e2m1x4_to_s8(w1 >> 16), bv[i].x,
-                      bv[i].y);
-      const uint32_t e0 = __byte_perm(R.es[i >> 2], 0u, 0x4440u | (i & 3));       // E_w of row r0
-      const uint32_t e1 = __byte_perm(R.es[2 + (i >> 2)], 0u, 0x4440u | (i & 3)); // and of row r1
-      const double s0 = __hiloint2double((int)(e0 * (1u << 20) + (uint32_t)fx[i]), 0);
-      const double s1 = __hiloint2double((int)(e1 * (1u << 20) + (uint32_t)fx[i]), 0);
-      acc0 = fma(i32_to_double(d[0] + (d[1] << 8)), s0, acc0);   // digits 2t, 2t+1 of row r0
-      acc1 = fma(i32_to_double(d[2] + (d[3] << 8)), s1, acc1);
-    }
-  }
-  acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-  acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-  acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-  acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-  out0 = acc0;
-  out1 = acc1;
-}
-
-// both halves of a segment: the full fast path, or the guarded one for a slab's last segment
-__device__ __forceinline__ void rows16_seg(const uint8_t* tile, int kc, int rb, int c0, int n, const int8_t* dig,
-                                           const int* fe, int lane, double& o0, double& o1) {
-  Rows16 R;
-  if (n == kESegChunks) {
-    rows16_load<true>(tile, kc, rb, c0, n, lane, R);
-    rows16_dot<true>(R, n, dig, fe, lane, o0, o1);
-  } else {
-    rows16_load<false>(tile, kc, rb, c0, n, lane, R);
-    rows16_dot<false>(R, n, dig, fe, lane, o0, o1);
-  }
-}
+__host__ __device__ __forceinline__ int64_t ex_slab_off(int s) { return (int64_t)s * (16 * 2048 + 4 * 512); }
 
 __device__ __forceinline__ float act_exact(float g, float u, int oai) {
   if (oai) {   // ops/activation.rs:25-45 (clamp 7, alpha 1.702)
@@ -581,116 +477,295 @@ __device__ __forceinline__ float act_exact(float g, float u, int oai) {
   return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expcr(-g))), u);
 }
 
-// gate/up: grid (segments, gate_up tiles, slots); 8 warps = the 8 groups of 16 rows of a 128-row
-// tile (rows < 64 gate, >= 64 up).  The last CTA to finish a (tile, slot) sums its 64 gate and up
-// rows over the segments (in segment order, rounded once), adds the biases, applies the activation
-// and writes the 64 activations as exact digits for the down kernel.
-__global__ void __launch_bounds__(kEThreads, 3) exact_gu_kernel(ExactMoeArgs a, uint32_t* err) {
-  __shared__ uint32_t last;
-  const int seg = blockIdx.x, mt = blockIdx.y, k = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kc = a.H / 32, c0 = seg * kESegChunks, c1 = min(kc, c0 + kESegChunks);
-  pdl_wait_prior();
-  pdl_launch_dependents();
-  const int e = a.idx[k] - a.expert_base;
-  if (e < 0 || e >= a.n_local) return;   // another rank's expert (or out of range: the combine skips it)
-  const uint8_t* tile = a.gu + ((size_t)e * a.gu_tiles + mt) * (size_t)a.gu_tile_bytes;
-  double o0, o1;
-  rows16_seg(tile, kc, 16 * warp, c0, c1 - c0, a.xdig + (size_t)c0 * 256, a.xfe + c0, lane, o0, o1);
-  double* gp = a.gp + (size_t)k * a.n_seg_gu * (2 * a.I);
-  if ((lane & 3) == 0) {
-    double* o = gp + (size_t)seg * (2 * a.I) + (size_t)mt * 128 + 16 * warp;
-    o[lane >> 2] = o0;
-    o[8 + (lane >> 2)] = o1;
+// position of a unit: slot list entry i, tile mt, unit u (chunk columns 4u ..); advanced in order
+struct UnitCursor {
+  int u, mt, i;
+  __device__ void init(int q, int nu, int tiles) {
+    u = q % nu;
+    const int r = q / nu;
+    mt = r % tiles;
+    i = r / tiles;
   }
-  // the barrier orders every thread's stores before thread 0's fence (cumulative), which orders them
-  // before its count
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    uint32_t* c = a.cnt + (size_t)k * a.gu_tiles + mt;
-    last = atomicAdd(c, 1u) == (uint32_t)a.n_seg_gu - 1 ? 1u : 0u;
-    if (last) *c = 0u;
-  }
-  __syncthreads();
-  if (!last || warp >= 2) return;
-  __threadfence();
-  const int i = mt * 64 + 32 * warp + lane;           // activation index; its gate / up rows:
-  const int gr = mt * 128 + 32 * warp + lane, ur = gr + 64;
-  double gs = 0.0, us = 0.0;
-  for (int s0 = 0; s0 < a.n_seg_gu; s0 += 8) {   // 16 loads in flight, summed in segment order
-    double gl[8], ul[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const bool in = s0 + j < a.n_seg_gu;
-      gl[j] = in ? __ldcg(gp + (size_t)(s0 + j) * (2 * a.I) + gr) : 0.0;
-      ul[j] = in ? __ldcg(gp + (size_t)(s0 + j) * (2 * a.I) + ur) : 0.0;
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (s0 + j < a.n_seg_gu) {
-        gs += gl[j];
-        us += ul[j];
+  __device__ void next(int nu, int tiles) {
+    if (++u == nu) {
+      u = 0;
+      if (++mt == tiles) {
+        mt = 0;
+        ++i;
       }
     }
   }
-  float gv = (float)gs, uv = (float)us;
-  if (a.gate_b) gv = __fadd_rn(gv, a.gate_b[(size_t)e * a.I + i]);
-  if (a.up_b) uv = __fadd_rn(uv, a.up_b[(size_t)e * a.I + i]);
-  const size_t chunk = (size_t)k * (a.I / 32) + 2 * mt + warp;
-  exact_digits_warp(act_exact(gv, uv, a.oai_swiglu), lane, a.adig + (size_t)chunk * 256, a.afe + chunk);
-  (void)err;
-}
+};
 
-// down: grid (segments, down tiles, slots), over the activation digits written by gate/up.  The
-// last CTA to finish a (tile, slot) sums its 128 rows over the segments (in segment order, rounded
-// once), adds the bias and writes the slot's output rows y[k][r].
-__global__ void __launch_bounds__(kEThreads, 3) exact_down_kernel(ExactMoeArgs a, uint32_t* err) {
-  __shared__ uint32_t last;
-  const int seg = blockIdx.x, mt = blockIdx.y, k = blockIdx.z;
+// phase 0: gate/up (rows < 64 of a tile gate, >= 64 up; the last run of an item writes the
+// activation terms); phase 1: down (the last run writes the slot's output rows).  A CTA's
+// consecutive units of one item form a run: the epilogue warps accumulate the run in registers and
+// write one f64 partial per row at the run's first unit; the item's reducer finds the runs again
+// from the CTA ranges.
+template <int PHASE>
+__global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_constant__ ExactMoeArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kUStages], empty[kUStages], acc_full[kUAcc], acc_empty[kUAcc];
+  __shared__ uint32_t tmem_base;
+  __shared__ int s_slot[kUMaxSlots], s_exp[kUMaxSlots], s_n, s_abort, s_last;
+  __shared__ double red[2][kUC][128];
+  __shared__ __align__(16) uint8_t sf_one[512];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kc = a.I / 32, c0 = seg * kESegChunks, c1 = min(kc, c0 + kESegChunks);
+  const int kc = PHASE ? a.I / 32 : a.H / 32;
+  const int tiles = PHASE ? a.down_tiles : a.gu_tiles;
+  const int nu = (kc + kUC - 1) / kUC;
+  const int rows_out = PHASE ? a.h_pad : 2 * a.I;       // partial rows per (slot, run start)
+  const uint8_t* wbase = PHASE ? a.down : a.gu;
+  const int64_t tile_bytes = PHASE ? a.down_tile_bytes : a.gu_tile_bytes;
+  double* part = PHASE ? a.dp : a.gp;                  // [K][nu][rows_out]
+  uint32_t* err = a.err;
+
+  // barriers and the unit scales do not depend on the previous kernel
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kUStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1 + kUEpiWarps);   // the MMA commit and every epilogue warp (stage bytes read)
+    }
+    for (int q = 0; q < kUAcc; ++q) {
+      mbar_init(&acc_full[q], 1);
+      mbar_init(&acc_empty[q], kUEpiWarps);
+    }
+    fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < 512; i += kUThreads) sf_one[i] = 127;   // ue8m0 1.0
+  umma::fence_proxy_async_smem();
   pdl_wait_prior();
   pdl_launch_dependents();
-  const int e = a.idx[k] - a.expert_base;
-  if (e < 0 || e >= a.n_local) return;
-  const uint8_t* tile = a.down + ((size_t)e * a.down_tiles + mt) * (size_t)a.down_tile_bytes;
-  const size_t ch = (size_t)k * kc + c0;
-  double o0, o1;
-  rows16_seg(tile, kc, 16 * warp, c0, c1 - c0, a.adig + ch * 256, a.afe + ch, lane, o0, o1);
-  const double* dk = a.dp + (size_t)k * a.n_seg_down * a.h_pad;
-  if ((lane & 3) == 0) {
-    double* dp = const_cast<double*>(dk) + (size_t)seg * a.h_pad + (size_t)mt * 128 + 16 * warp;
-    dp[lane >> 2] = o0;
-    dp[8 + (lane >> 2)] = o1;
+  // all of tensor memory, taken only after the previous kernel has finished (so a kernel of the
+  // same kind launched ahead of time never waits on a CTA that is waiting on it)
+  if (warp == 1) {
+    umma::tmem_alloc(&tmem_base, kUTmemCols);
+    umma::tmem_relinquish();
   }
-  // the barrier orders every thread's stores before thread 0's fence (cumulative), which orders them
-  // before its count
-  __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
-    uint32_t* c = a.cnt + (size_t)a.K * a.gu_tiles + (size_t)k * a.down_tiles + mt;
-    last = atomicAdd(c, 1u) == (uint32_t)a.n_seg_down - 1 ? 1u : 0u;
-    if (last) *c = 0u;
+    int n = 0;
+    for (int k = 0; k < a.K && n < kUMaxSlots; ++k) {
+      const int e = a.idx[k] - a.expert_base;
+      if (e < 0 || e >= a.n_local) continue;   // another rank's expert (or out of range: the combine skips it)
+      s_slot[n] = k;
+      s_exp[n] = e;
+      ++n;
+    }
+    s_n = n;
+    s_abort = 0;
   }
+  umma::fence_before_sync();
   __syncthreads();
-  if (!last || threadIdx.x >= 128) return;
-  __threadfence();
-  const int r = mt * 128 + threadIdx.x;
-  if (r >= a.H) return;
-  double t = 0.0;
-  for (int s0 = 0; s0 < a.n_seg_down; s0 += 8) {   // 8 loads in flight, summed in segment order
-    double v[8];
+  umma::fence_after_sync();
+  const uint32_t tb = tmem_base;
+  const int U = s_n * tiles * nu, G = (int)gridDim.x;
+  auto range_lo = [&](int b) { return (int)((int64_t)b * U / G); };
+  const int q0 = range_lo(blockIdx.x), q1 = range_lo(blockIdx.x + 1);
+  const uint8_t* bt = PHASE ? a.abt : a.xbt;
+  const int64_t bt_stride = PHASE ? (int64_t)kc * 1024 : 0;
+  const int* fe_src = PHASE ? a.afe : a.xfe;
+  const int64_t fe_stride = PHASE ? (int64_t)((kc + 3) & ~3) : 0;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      UnitCursor C;
+      C.init(q0, nu, tiles);
+      int j = 0;
+      for (int q = q0; q < q1; ++q, ++j, C.next(nu, tiles)) {
+        if (*reinterpret_cast<volatile int*>(&s_abort)) break;
+        const int k = s_slot[C.i], e = s_exp[C.i], c0 = C.u * kUC, n = min(kUC, kc - c0);
+        const int s = j % kUStages, use = j / kUStages;
+        if (use > 0 && !mbar_wait(&empty[s], (uint32_t)((use - 1) & 1), err, EF_TIMEOUT_EMPTY)) {
+          s_abort = 1;
+          break;
+        }
+        const uint8_t* tile = wbase + ((int64_t)e * tiles + C.mt) * tile_bytes;
+        const int slab = c0 >> 4, sl0 = slab * 16, nch = min(16, kc - sl0);
+        const uint8_t* sb = tile + ex_slab_off(slab);
+        uint8_t* st = smem + (size_t)s * kUStage;
+        mbar_expect_tx(&full[s], (uint32_t)n * (2048u + 1024u) + 512u + 16u);
+        bulk_g2s_stream(st, sb + (int64_t)(c0 - sl0) * 2048, (uint32_t)n * 2048u, &full[s], pol);
+        bulk_g2s_stream(st + kUStA, sb + (int64_t)nch * 2048 + ((c0 - sl0) >> 2) * 512, 512u, &full[s], pol);
+        bulk_g2s(st + kUStA + kUStS, bt + (int64_t)k * bt_stride + (int64_t)c0 * 1024, (uint32_t)n * 1024u, &full[s]);
+        bulk_g2s(st + kUStA + kUStS + kUStB, fe_src + (int64_t)k * fe_stride + c0, 16u, &full[s]);
+      }
+      // no copy may still be landing in shared memory when the CTA exits
+      for (int q = max(0, j - kUStages); q < j; ++q)
+        mbar_wait(&full[q % kUStages], (uint32_t)((q / kUStages) & 1), err, EF_TIMEOUT_FULL);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      umma::cp_sf_group(tb + kUSfCol, sf_one);
+      umma::cp_sf_group(tb + kUSfCol + 4, sf_one);
+      constexpr uint32_t idesc = umma::idesc_mxf4(128, 64, 0, 0);
+      UnitCursor C;
+      C.init(q0, nu, tiles);
+      int j = 0;
+      for (int q = q0; q < q1; ++q, ++j, C.next(nu, tiles)) {
+        if (*reinterpret_cast<volatile int*>(&s_abort)) break;
+        const int n = min(kUC, kc - C.u * kUC);
+        const int s = j % kUStages, acc = j % kUAcc;
+        if (!mbar_wait(&full[s], (uint32_t)((j / kUStages) & 1), err, EF_TIMEOUT_FULL)) {
+          s_abort = 1;
+          break;
+        }
+        if (j >= kUAcc && !mbar_wait(&acc_empty[acc], (uint32_t)(((j / kUAcc) - 1) & 1), err, EF_TIMEOUT_EMPTY)) {
+          s_abort = 1;
+          break;
+        }
+        umma::fence_after_sync();
+        const uint8_t* st = smem + (size_t)s * kUStage;
+        for (int p = 0; p < n / 2; ++p) {
+          const uint64_t ad = umma::smem_desc(st + p * 4096, 2048, 128);
+          const uint64_t bd = umma::smem_desc(st + kUStA + kUStS + p * 2048, 1024, 128);
+          umma::mma_mxf4(tb + (uint32_t)(acc * 128 + p * 64), ad, bd, idesc, tb + kUSfCol, tb + kUSfCol + 4, false);
+        }
+        umma::commit(&empty[s]);
+        umma::commit(&acc_full[acc]);
+      }
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int ew = warp - 2, quad = warp & 3, jc = ew >> 2;   // this warp's TMEM lane quadrant and chunk
+    const int row = 32 * quad + lane;
+    UnitCursor C;
+    C.init(q0, nu, tiles);
+    int j = 0, run = 0, run_u0 = C.u, rp = 0;
+    double racc = 0.0;
+    for (int q = q0; q < q1; ++q, ++j, C.next(nu, tiles)) {
+      const int s = j % kUStages, acc = j % kUAcc;
+      const int n = min(kUC, kc - C.u * kUC);
+      const bool live = jc < n;
+      bool ok = mbar_wait(&acc_full[acc], (uint32_t)((j / kUAcc) & 1), err, EF_TIMEOUT_FULL);
+      ok = ok && mbar_wait(&full[s], (uint32_t)((j / kUStages) & 1), err, EF_TIMEOUT_FULL);
+      ok = __all_sync(0xffffffffu, ok);   // the accumulator load below is warp-collective
+      umma::fence_after_sync();
+      float v[32];
+      if (live && ok) {
+        umma::ld_32x32b_x32(tb + ((uint32_t)(32 * quad) << 16) + (uint32_t)(acc * 128 + jc * 32), v);
+      } else {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = s0 + j < a.n_seg_down ? __ldcg(dk + (size_t)(s0 + j) * a.h_pad + r) : 0.0;
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      umma::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      const uint8_t* st = smem + (size_t)s * kUStage;
+      const uint32_t ew_scale = st[kUStA + 16 * (row & 31) + 4 * (row >> 5) + jc];   // E_w of (row, chunk)
+      const uint32_t fe = (uint32_t)reinterpret_cast<const int*>(st + kUStA + kUStS + kUStB)[jc];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (live) {
+        // this chunk's 27 digit dots: columns (jc & 1) * 32 + d of the pair's accumulator
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (s0 + j < a.n_seg_down) t += v[j];
+        for (int g = 0; g < 4; ++g) {
+          const int d0 = 7 * g, d1 = min(kExactDigits, d0 + 7);
+          float f = v[d1 - 1];
+#pragma unroll
+          for (int d = d1 - 2; d >= d0; --d) f = fmaf(f, 4.0f, v[d]);   // exact: integers in halves below 2^23
+          const double sc = __hiloint2double((int)((ew_scale + fe + 14u * g) << 20), 0);
+          racc = fma((double)f, sc, racc);
+        }
+      }
+      ++run;
+      const bool run_end = q + 1 == q1 || C.u + 1 == nu;   // the next unit starts another item
+      if (!run_end) continue;
+      // ---- the run's partial: the four chunk warps of each row summed, written at the run's first unit ----
+      const int k = s_slot[C.i], e = s_exp[C.i], mt = C.mt;
+      red[rp][jc][row] = racc;
+      racc = 0.0;
+      named_bar(1, 32 * kUEpiWarps);
+      const int nrun = run, u_start = run_u0;
+      run = 0;
+      run_u0 = 0;   // a later run of this CTA starts an item at unit 0
+      const int rb = rp;
+      rp ^= 1;
+      if (jc != 0) continue;
+      const double t = ((red[rb][0][row] + red[rb][1][row]) + red[rb][2][row]) + red[rb][3][row];
+      double* pk = part + (size_t)k * nu * rows_out;
+      pk[(size_t)u_start * rows_out + (size_t)mt * 128 + row] = t;
+      named_bar(2, 128);
+      if (ew == 0 && lane == 0) {
+        __threadfence();   // the run's partials (ordered before by the barrier), then the count
+        uint32_t* cnt = a.cnt + (PHASE ? (size_t)a.K * a.gu_tiles : 0) + (size_t)k * tiles + mt;
+        s_last = atomicAdd(cnt, (uint32_t)nrun) + (uint32_t)nrun == (uint32_t)nu ? 1 : 0;
+        if (s_last) {
+          *cnt = 0u;
+          __threadfence();
+        }
+      }
+      named_bar(2, 128);
+      if (!s_last) continue;
+      // ---- the item's reduction: its runs in CTA order (the CTA ranges cut the unit sequence) ----
+      const int A0 = (C.i * tiles + mt) * nu;   // the item's first unit
+      int bnext = max(0, (int)((int64_t)A0 * G / (U > 0 ? U : 1)) - 1);
+      // up to 8 run starts at a time, so their loads are in flight together
+      auto next_runs = [&](int (&runs)[8]) {
+        int nr = 0;
+        for (; bnext < G && nr < 8; ++bnext) {
+          const int lo = range_lo(bnext), hi = range_lo(bnext + 1);
+          if (lo >= A0 + nu) {
+            bnext = G;
+            break;
+          }
+          if (hi > lo && hi > A0) runs[nr++] = max(lo, A0) - A0;
+        }
+        return nr;
+      };
+      const double* base = pk + (size_t)mt * 128;
+      int runs[8];
+      if (PHASE == 0) {
+        // the tile's 64 activations: gate row r and up row 64 + r, r = 32 * quad + lane for quads 0, 1
+        if (quad < 2) {
+          const int r = row, i = mt * 64 + r;
+          double gs = 0.0, us = 0.0;
+          for (int nr = next_runs(runs); nr > 0; nr = next_runs(runs)) {
+            double gl[8], ul[8];
+#pragma unroll
+            for (int q2 = 0; q2 < 8; ++q2) {
+              gl[q2] = q2 < nr ? __ldcg(base + (size_t)runs[q2] * rows_out + r) : 0.0;
+              ul[q2] = q2 < nr ? __ldcg(base + (size_t)runs[q2] * rows_out + 64 + r) : 0.0;
+            }
+#pragma unroll
+            for (int q2 = 0; q2 < 8; ++q2)
+              if (q2 < nr) {
+                gs += gl[q2];
+                us += ul[q2];
+              }
+          }
+          float gv = (float)gs, uv = (float)us;
+          if (a.gate_b) gv = __fadd_rn(gv, a.gate_b[(size_t)e * a.I + i]);
+          if (a.up_b) uv = __fadd_rn(uv, a.up_b[(size_t)e * a.I + i]);
+          const int ch = 2 * mt + quad;   // the down projection's chunk column of these 32 activations
+          const int kcd = a.I / 32;
+          exact_bterm_warp(act_exact(gv, uv, a.oai_swiglu), lane, a.abt + ((int64_t)k * kcd + ch) * 1024, ch & 1,
+                           a.afe + (int64_t)k * ((kcd + 3) & ~3) + ch);
+        }
+      } else {
+        const int r = mt * 128 + row;
+        if (r < a.H) {
+          double t2 = 0.0;
+          for (int nr = next_runs(runs); nr > 0; nr = next_runs(runs)) {
+            double vl[8];
+#pragma unroll
+            for (int q2 = 0; q2 < 8; ++q2) vl[q2] = q2 < nr ? __ldcg(base + (size_t)runs[q2] * rows_out + row) : 0.0;
+#pragma unroll
+            for (int q2 = 0; q2 < 8; ++q2)
+              if (q2 < nr) t2 += vl[q2];
+          }
+          float y = (float)t2;
+          if (a.down_b) y = __fadd_rn(y, a.down_b[(size_t)e * a.H + r]);
+          a.y[(size_t)k * a.H + r] = y;
+        }
+      }
+    }
   }
-  float y = (float)t;
-  if (a.down_b) y = __fadd_rn(y, a.down_b[(size_t)e * a.H + r]);
-  a.y[(size_t)k * a.H + r] = y;
-  (void)err;
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) umma::tmem_dealloc(tb, kUTmemCols);
 }
 
 // ============================ experts (K-quant native blocks) ============================
@@ -862,27 +937,41 @@ cudaError_t launch_exact_attention(const DevCtx& c, const AttnArgs& a, int range
   return cudaErrorInvalidValue;
 }
 
-int exact_seg_count(int kc) { return (kc + kESegChunks - 1) / kESegChunks; }
+int exact_seg_count(int kc) { return (kc + kUC - 1) / kUC; }
 
 cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a0, cudaStream_t s, int part) {
   ExactMoeArgs a = a0;
-  if (!tc_supported(a.H, a.I) || a.K < 1 || a.K > 16 || !a.gp || !a.dp || !a.xdig || !a.xfe || !a.adig || !a.afe ||
-      !a.cnt || !a.y || a.I % 64)
+  if (!tc_supported(a.H, a.I) || a.K < 1 || a.K > kUMaxSlots || !a.gp || !a.dp || !a.xbt || !a.xfe || !a.abt ||
+      !a.afe || !a.cnt || !a.y || a.I % 64)
     return cudaErrorInvalidValue;
   a.gu_tiles = tc_gu_tiles(a.I);
   a.down_tiles = tc_down_tiles(a.H);
   a.gu_tile_bytes = tc_tile_bytes(a.H / 32);
   a.down_tile_bytes = tc_tile_bytes(a.I / 32);
+  a.err = c.err;
   if (a.n_seg_gu != exact_seg_count(a.H / 32) || a.n_seg_down != exact_seg_count(a.I / 32) ||
       a.h_pad < tc_down_tiles(a.H) * 128)
     return cudaErrorInvalidValue;
-  if (part != 1) {
-    cudaError_t e = launch_pdl_x(exact_gu_kernel, dim3((unsigned)a.n_seg_gu, (unsigned)tc_gu_tiles(a.I), (unsigned)a.K),
-                                 dim3(kEThreads), 0, s, a, c.err);
-    if (e != cudaSuccess || part == 0) return e;
+  const size_t smem = (size_t)kUStages * kUStage;
+  for (int ph = 0; ph < 2; ++ph) {
+    if (part >= 0 && part != ph) continue;
+    auto kern = ph ? exact_tc_kernel<1> : exact_tc_kernel<0>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)c.sm_count);
+    cfg.blockDim = dim3(kUThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, a);
+    if (e != cudaSuccess) return e;
   }
-  return launch_pdl_x(exact_down_kernel, dim3((unsigned)a.n_seg_down, (unsigned)tc_down_tiles(a.H), (unsigned)a.K),
-                      dim3(kEThreads), 0, s, a, c.err);
+  return cudaSuccess;
 }
 
 namespace {

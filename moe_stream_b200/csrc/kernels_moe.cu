@@ -1120,12 +1120,12 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, ui
       umma::quantize_terms_warp(v, lane, a.xterm, nb, b);
     }
   }
-  if (a.xdig) {   // the same blocks as exact digits
+  if (a.xbt) {   // the same blocks as exact B terms
     const int nb = a.H / 32, nw = kRouterThreads / 32;
     for (int b = e * nw + warp; b < nb; b += (int)gridDim.x * nw) {
       const int i = 32 * b + lane;
       const float v = a.h ? __fmul_rn(__fmul_rn(a.h[i], inv), a.norm_w[i]) : a.xn[i];
-      exact_digits_warp(v, lane, a.xdig + (size_t)b * 256, a.xfe + b);
+      exact_bterm_warp(v, lane, a.xbt + (size_t)b * 1024, b & 1, a.xfe + b);
     }
   }
   __syncthreads();
@@ -1244,7 +1244,7 @@ cudaError_t launch_moe_combine(const DevCtx& c, const PendingCombine& pc, int H,
 
 cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s) {
   if (a.K < 1 || a.K > kMaxK || a.K > a.E || a.E > kRouterMaxE || !a.counter || a.batch < 1 ||
-      (a.batch > 1 && (a.xterm || a.xdig)) || (a.xdig && (a.H % 32 || !a.xfe)))
+      (a.batch > 1 && (a.xterm || a.xbt)) || (a.xbt && (a.H % 32 || !a.xfe)))
     return cudaErrorInvalidValue;
   if (a.batch > 1) {
     if (a.H % 4 || !a.h || reinterpret_cast<uintptr_t>(a.w) % 16) return cudaErrorInvalidValue;

@@ -262,10 +262,10 @@ struct ms_model {
   bool exact = true;
   double* ex_gp = nullptr;          // [K][segments][2 I] gate/up partial dots
   double* ex_dp = nullptr;          // [K][segments][h_pad] down partial dots
-  int8_t* ex_xdig = nullptr;        // [H/32][256] exact digits of the MoE input
+  uint8_t* ex_xbt = nullptr;        // [H/32][1024] exact B terms of the MoE input
   int* ex_xfe = nullptr;            // [H/32]
-  int8_t* ex_adig = nullptr;        // [K][I/32][256] exact digits of the activations
-  int* ex_afe = nullptr;            // [K][I/32]
+  uint8_t* ex_abt = nullptr;        // [K][I/32][1024] exact B terms of the activations
+  int* ex_afe = nullptr;            // [K][I/32 rounded up to 4]
   uint32_t* ex_cnt = nullptr;       // [K][gate/up tiles] per-tile arrival counters
   int ex_seg_gu = 0, ex_seg_down = 0, ex_hpad = 0;
   float* ex_kgu = nullptr;          // K-quant experts: gate / up outputs [K][2][I]
@@ -545,7 +545,7 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     ra.H = H; ra.E = c.experts; ra.K = c.top_k; ra.softmax_weight = c.arch == MS_ARCH_GPT_OSS;
     ra.normalize = c.norm_topk_prob;
     if (Lw.tc && m->exact) {
-      ra.xdig = m->ex_xdig;
+      ra.xbt = m->ex_xbt;
       ra.xfe = m->ex_xfe;
     } else if (Lw.tc) {
       ra.xterm = m->xterm;
@@ -580,7 +580,7 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
         ea.H = H; ea.I = c.inter; ea.K = c.top_k; ea.expert_base = m->expert_base; ea.n_local = m->n_local;
         ea.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ea.gp = m->ex_gp; ea.dp = m->ex_dp; ea.n_seg_gu = m->ex_seg_gu;
         ea.n_seg_down = m->ex_seg_down; ea.h_pad = m->ex_hpad;
-        ea.xdig = m->ex_xdig; ea.xfe = m->ex_xfe; ea.adig = m->ex_adig; ea.afe = m->ex_afe; ea.cnt = m->ex_cnt;
+        ea.xbt = m->ex_xbt; ea.xfe = m->ex_xfe; ea.abt = m->ex_abt; ea.afe = m->ex_afe; ea.cnt = m->ex_cnt;
         ea.down_b = Lw.down_b; ea.y = m->partial;
         LAUNCH(launch_exact_moe(dc, ea, s, 0));   // gate/up (+ activation digits)
         LAUNCH(launch_exact_moe(dc, ea, s, 1));   // down
@@ -1592,10 +1592,10 @@ ms_status ms_model_finalize(ms_model* m) {
     m->ex_hpad = tc_down_tiles(H) * 128;
     s = s ? s : m->alloc(&m->ex_gp, (size_t)c.top_k * m->ex_seg_gu * 2 * c.inter * 8);
     s = s ? s : m->alloc(&m->ex_dp, (size_t)c.top_k * m->ex_seg_down * m->ex_hpad * 8);
-    s = s ? s : m->alloc(&m->ex_xdig, (size_t)(H / 32) * 256);
-    s = s ? s : m->alloc(&m->ex_xfe, (size_t)(H / 32) * 4);
-    s = s ? s : m->alloc(&m->ex_adig, (size_t)c.top_k * (c.inter / 32) * 256);
-    s = s ? s : m->alloc(&m->ex_afe, (size_t)c.top_k * (c.inter / 32) * 4);
+    s = s ? s : m->alloc(&m->ex_xbt, (size_t)(H / 32) * 1024);
+    s = s ? s : m->alloc(&m->ex_xfe, (size_t)(H / 32 + 4) * 4);   // + the padding of a 16-byte copy
+    s = s ? s : m->alloc(&m->ex_abt, (size_t)c.top_k * (c.inter / 32) * 1024);
+    s = s ? s : m->alloc(&m->ex_afe, (size_t)c.top_k * ((c.inter / 32 + 3) & ~3) * 4 + 16);   // rows of 4-aligned stride
     s = s ? s : m->alloc(&m->ex_cnt, (size_t)c.top_k * (tc_gu_tiles(c.inter) + tc_down_tiles(H)) * 4);
     s = s ? s : m->alloc(&m->xterm, (size_t)tc_bterm_bytes(H / 32));
     s = s ? s : m->alloc(&m->act_terms, (size_t)c.top_k * tc_bterm_bytes(c.inter / 32));
