@@ -59,6 +59,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return false;
 }
 
+// Bounded wait that sleeps between polls, for warps that would otherwise take issue slots from
+// the producer / MMA threads of their SM sub-partition.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t bit,
+                                                uint32_t ns) {
+  for (uint32_t i = 0; i < kWaitLimit / 16; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    __nanosleep(ns);
+  }
+  if (err) atomicOr(err, bit);
+  return false;
+}
+
 // 1-D bulk copy global -> shared (TMA, no multicast); bytes % 16 == 0, both addresses 16-aligned.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -283,34 +295,40 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 }
 __device__ __forceinline__ float expcr(float x) { return (float)exp((double)x); }
 
-// Exact base-4 terms of one 32-element f32 block (one element per lane), the B operand of the exact
+// Exact base-8 terms of one 32-element f32 block (one element per lane), the B operand of the exact
 // MXFP4 expert dots on the tensor cores: X_j = round(|x_j| 2^F) with F = 180 - (the block's largest
-// biased exponent), so X_j < 2^54 and X keeps every bit of the block's larger elements; X is cut
-// into kExactDigits = 27 base-4 digits and term d of element j is the e2m1 code of sign(x_j) * d_d
-// (values 0, 1, 2, 3).  The chunk's 1 KB block holds 64 B columns of 32 codes (16 bytes, element 2i
-// in the low nibble of byte i); the block's terms are columns parity * 32 + d, where parity = the
-// chunk index & 1, and every other column stays zero, so one K = 64 MMA over two chunks keeps the
-// chunks' dots apart.  *fexp = 1023 - 127 - F, the block's part of the double scale exponent.
-constexpr int kExactDigits = 27;
+// biased exponent), so X_j < 2^54 and X keeps every bit of the block's larger elements.  X is written
+// in kExactDigits = 19 balanced base-8 digits d in [-4, 3] (19 because balanced digits reach only
+// 3/7 of 8^n), and term t of element j is the e2m1 code of sign(x_j) * d_t -- a value in [-4, 4],
+// every one of which e2m1 holds exactly.  The chunk's 768-byte block holds 48 B columns of 32 codes
+// (16 bytes, element 2i in the low nibble of byte i); the block's terms are columns parity * 24 + t,
+// parity = the chunk index & 1, and every other column stays zero, so one K = 64 MMA over two
+// chunks keeps the chunks' dots apart.  *fexp = 1023 - 127 - F, the block's part of the double
+// scale exponent.
+constexpr int kExactDigits = 19;
+constexpr int kExactCols = 48;          // B columns per chunk block (two parities of 24)
+constexpr int kExactBlock = kExactCols * 16;
 __device__ __forceinline__ void exact_bterm_warp(float x, int lane, uint8_t* blk, int parity, int* fexp) {
   int eb = (int)((__float_as_uint(x) >> 23) & 0xFFu);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) eb = max(eb, __shfl_xor_sync(0xffffffffu, eb, o));
   const int F = 180 - eb;
-  const unsigned long long X =
-      (unsigned long long)__double2ll_rn(fabs((double)x) * __longlong_as_double((long long)(F + 1023) << 52));
-  const uint32_t sgn = (__float_as_uint(x) >> 31) << 3;
-  uint32_t* col = reinterpret_cast<uint32_t*>(blk + parity * 32 * 16) + (lane >> 3);
+  long long X = __double2ll_rn(fabs((double)x) * __longlong_as_double((long long)(F + 1023) << 52));
+  const bool neg = (__float_as_uint(x) >> 31) != 0;
+  uint32_t* col = reinterpret_cast<uint32_t*>(blk + parity * 24 * 16) + (lane >> 3);
 #pragma unroll
-  for (int d = 0; d < kExactDigits; ++d) {
-    const uint32_t dig = (uint32_t)(X >> (2 * d)) & 3u;
-    uint32_t code = (0x5420u >> (4 * dig)) & 0xFu;   // e2m1 of 0, 1, 2, 3
-    code |= code ? sgn : 0u;
-    uint32_t w = code << (4 * (lane & 7));           // 8 lanes' codes -> one 32-bit word
+  for (int t = 0; t < kExactDigits; ++t) {
+    const int d = (int)((X + 4) & 7) - 4;   // balanced digit
+    X = (X - d) >> 3;
+    const int v = neg ? -d : d;             // in [-4, 4]
+    const uint32_t mag = (uint32_t)(v < 0 ? -v : v);
+    uint32_t code = (0x65420u >> (4 * mag)) & 0xFu;   // e2m1 of 0, 1, 2, 3, 4 (0x0, 0x2, 0x4, 0x5, 0x6)
+    code |= v < 0 ? 8u : 0u;
+    uint32_t w = code << (4 * (lane & 7));  // 8 lanes' codes -> one 32-bit word
     w |= __shfl_xor_sync(0xffffffffu, w, 1);
     w |= __shfl_xor_sync(0xffffffffu, w, 2);
     w |= __shfl_xor_sync(0xffffffffu, w, 4);
-    if ((lane & 7) == 0) col[d * 4] = w;
+    if ((lane & 7) == 0) col[t * 4] = w;
   }
   if (lane == 0) *fexp = 1023 - 127 - F;
 }

@@ -131,7 +131,7 @@ struct RouterArgs {
   int softmax_weight = 1;         // GPT-OSS: softmax over the selected k logits
   int normalize = 0;              // renormalise top-k probabilities (norm_topk_prob)
   uint8_t* xterm = nullptr;       // optional: the normed x as MXFP4 B terms (tc_bterm_bytes(H/32))
-  uint8_t* xbt = nullptr;         // optional: the normed x as exact B terms ([H/32][1024], exact_bterm_warp,
+  uint8_t* xbt = nullptr;         // optional: the normed x as exact B terms ([H/32][exact_term_block_bytes()],
   int* xfe = nullptr;             //   zeroed once) and their scale exponents [H/32]
   int batch = 1;                  // grid.y = tokens: h/xn + b*H, logits + b*E, idx/wts + b*K, counter + b
 };
@@ -314,10 +314,10 @@ struct ExactMoeArgs {
   double* gp = nullptr;             // [K][n_seg_gu][2 I]
   double* dp = nullptr;             // [K][n_seg_down][h_pad]
   int n_seg_gu = 0, n_seg_down = 0, h_pad = 0;
-  const uint8_t* xbt = nullptr;     // [H/32][1024] exact base-4 B terms of x (exact_bterm_warp), from the router
-  const int* xfe = nullptr;         // [H/32 + 4] their scale exponents (+ padding for 16-byte copies)
-  uint8_t* abt = nullptr;           // [K][I/32][1024] B terms of the activations (written by gate/up; zeroed once)
-  int* afe = nullptr;               // [K][I/32 rounded up to 4] (16-byte copies of 4 chunks' exponents)
+  const uint8_t* xbt = nullptr;     // [H/32][exact_term_block_bytes()] exact B terms of x (exact_bterm_warp), from the router
+  const int* xfe = nullptr;         // [H/32 + 8] their scale exponents (+ padding for 32-byte copies)
+  uint8_t* abt = nullptr;           // [K][I/32][exact_term_block_bytes()] B terms of the activations (from gate/up; zeroed once)
+  int* afe = nullptr;               // [K][I/32 rounded up to 8] (32-byte copies of 8 chunks' exponents)
   uint32_t* cnt = nullptr;          // [K][gate/up tiles] + [K][down tiles], zero-initialised, self-resetting
   const float* down_b = nullptr;    // [E_local, H] or null
   float* y = nullptr;               // [K][H] each slot's output (the combine's PendingCombine.partial)
@@ -325,7 +325,8 @@ struct ExactMoeArgs {
   uint32_t* err = nullptr;                    // filled by launch_exact_moe
   int64_t gu_tile_bytes = 0, down_tile_bytes = 0;
 };
-int exact_seg_count(int kc);        // K segments over kc 32-element chunks
+int exact_seg_count(int kc);
+int exact_term_block_bytes();     // bytes of one chunk's exact B-term block        // K segments over kc 32-element chunks
 // the same for K-quant experts in native blocks (Q4_K, or Q6_K repacked to 224-byte superblocks):
 // gate / up rows -> gu_out [K][2][I] (f32, rounded once, + bias), down rows -> y [K][H] (+ bias);
 // the consumer combines y (PendingCombine.partial) in ascending expert id

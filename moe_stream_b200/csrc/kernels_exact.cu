@@ -439,30 +439,32 @@ cudaError_t launch_exact_attn_hd(const AttnArgs& a, const DevCtx& c, int rep, in
 
 // ============================ experts (MXFP4 tiles on tcgen05) ============================
 // The expert rows are the packed MXFP4 tiles of the tensor-core path (128 rows; slabs of 16 chunk
-// columns, codes then 512-byte scale groups).  A unit is one K-word of one (slot, tile) item: 4
-// chunk columns (the last unit of a row may hold 2) and their scale group.  Per unit the tensor
-// core computes, with every block scale set to 1, D[row][parity * 32 + d] = sum over the 32
-// elements of chunk (2p + parity) of e2m1(w) * term_d(x) for each K = 64 pair p -- integer
-// multiples of 1/2 below 2^10, exact in f32.  The epilogue folds 7 digits at a time in f32 (still
-// exact: below 2^23 halves), then applies 2^(E_w - 127 - F) and accumulates in f64.  Warp roles:
-// warp 0 streams units with 1-D bulk copies (codes, scale group, B terms), warp 1 owns tensor
-// memory and issues the MMAs (one elected thread), warps 2-17 drain the accumulators (four warps
-// per TMEM lane quadrant, one chunk each).  The units of all (slot, tile) items are cut into equal
-// contiguous ranges, one per CTA; the last CTA to finish an item reduces its per-unit f64 partials.
-constexpr int kUC = 4;                          // chunk columns per unit
+// columns, codes then 512-byte scale groups).  A unit is half a slab of one (slot, tile) item: 8
+// chunk columns (the last unit of a row may hold fewer) and their two scale groups.  Per K = 64
+// pair of chunks the tensor core computes, with every block scale set to 1,
+// D[row][parity * 24 + t] = sum over the 32 elements of the pair's chunk `parity` of
+// e2m1(w) * term_t(x) -- multiples of 1/2 below 2^10, exact in f32.  The epilogue folds 5 base-8
+// digits at a time in f32 (still exact: below 2^23 halves), applies 2^(E_w - 127 - F + 15 g) and
+// accumulates in f64.  Warp roles: warp 0 streams units with 1-D bulk copies, warp 1 owns tensor
+// memory and issues the MMAs (one elected thread), warps 2-17 drain the accumulators (four warps per
+// TMEM lane quadrant, one chunk pair each).  The units of all (slot, tile) items are cut into equal
+// contiguous ranges, one per CTA; the last CTA to finish an item reduces the items' partials.
+constexpr int kUC = 8;                          // chunk columns per unit
 constexpr int kUStA = kUC * 2048;               // A codes
-constexpr int kUStS = 512;                      // A scale group
-constexpr int kUStB = kUC * 1024;               // B terms: 64 columns x 16 bytes per chunk
-constexpr int kUStF = 16;                       // the 4 chunks' scale exponents of B (x / activation)
+constexpr int kUStS = 2 * 512;                  // A scale groups
+constexpr int kUStB = kUC * kExactBlock;        // B terms
+constexpr int kUStF = 32;                       // the 8 chunks' scale exponents of B (x / activation)
 constexpr int kUStage = kUStA + kUStS + kUStB + kUStF;
-constexpr int kUStages = 6;
-constexpr int kUAcc = 3;                        // accumulators of 128 columns (two K = 64 pairs)
+constexpr int kUStages = 4;
+constexpr int kUAcc = 2;                        // accumulators of 4 pairs x 48 columns
+constexpr int kUAccCols = (kUC / 2) * kExactCols;
 constexpr int kUEpiWarps = 16;
 constexpr int kUThreads = 64 + 32 * kUEpiWarps;
 constexpr int kUTmemCols = 512;
-constexpr uint32_t kUSfCol = kUAcc * 128;       // unit block scales: A at +0, B at +4
+constexpr uint32_t kUSfCol = kUAcc * kUAccCols; // unit block scales: A at +0, B at +4
 constexpr int kUMaxSlots = 16;
 static_assert(kUSfCol + 8 <= kUTmemCols, "tensor memory budget");
+static_assert(kUStage % 16 == 0, "bulk-copy alignment");
 
 __host__ __device__ __forceinline__ int64_t ex_slab_off(int s) { return (int64_t)s * (16 * 2048 + 4 * 512); }
 
@@ -477,7 +479,7 @@ __device__ __forceinline__ float act_exact(float g, float u, int oai) {
   return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expcr(-g))), u);
 }
 
-// position of a unit: slot list entry i, tile mt, unit u (chunk columns 4u ..); advanced in order
+// position of a unit: slot list entry i, tile mt, unit u (chunk columns 8u ..); advanced in order
 struct UnitCursor {
   int u, mt, i;
   __device__ void init(int q, int nu, int tiles) {
@@ -501,14 +503,14 @@ struct UnitCursor {
 // activation terms); phase 1: down (the last run writes the slot's output rows).  A CTA's
 // consecutive units of one item form a run: the epilogue warps accumulate the run in registers and
 // write one f64 partial per row at the run's first unit; the item's reducer finds the runs again
-// from the CTA ranges.
+// from the CTA ranges.  xres (gate/up): x's B terms stay in shared memory for the whole kernel.
 template <int PHASE>
-__global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_constant__ ExactMoeArgs a) {
+__global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_constant__ ExactMoeArgs a, int xres) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ __align__(8) uint64_t full[kUStages], empty[kUStages], acc_full[kUAcc], acc_empty[kUAcc];
+  __shared__ __align__(8) uint64_t full[kUStages], empty[kUStages], acc_full[kUAcc], acc_empty[kUAcc], xb_full;
   __shared__ uint32_t tmem_base;
   __shared__ int s_slot[kUMaxSlots], s_exp[kUMaxSlots], s_n, s_abort, s_last;
-  __shared__ double red[2][kUC][128];
+  __shared__ double red[2][kUC / 2][128];
   __shared__ __align__(16) uint8_t sf_one[512];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kc = PHASE ? a.I / 32 : a.H / 32;
@@ -530,6 +532,7 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
       mbar_init(&acc_full[q], 1);
       mbar_init(&acc_empty[q], kUEpiWarps);
     }
+    mbar_init(&xb_full, 1);
     fence_mbar_init();
   }
   for (int i = threadIdx.x; i < 512; i += kUThreads) sf_one[i] = 127;   // ue8m0 1.0
@@ -562,45 +565,60 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
   auto range_lo = [&](int b) { return (int)((int64_t)b * U / G); };
   const int q0 = range_lo(blockIdx.x), q1 = range_lo(blockIdx.x + 1);
   const uint8_t* bt = PHASE ? a.abt : a.xbt;
-  const int64_t bt_stride = PHASE ? (int64_t)kc * 1024 : 0;
+  const int64_t bt_stride = PHASE ? (int64_t)kc * kExactBlock : 0;
   const int* fe_src = PHASE ? a.afe : a.xfe;
-  const int64_t fe_stride = PHASE ? (int64_t)((kc + 3) & ~3) : 0;
+  const int64_t fe_stride = PHASE ? (int64_t)((kc + 7) & ~7) : 0;
+  uint8_t* xb_s = smem + (size_t)kUStages * kUStage;   // xres: [kc][kExactBlock] terms, then kc exponents
+  const int* xfe_s = reinterpret_cast<const int*>(xb_s + (size_t)kc * kExactBlock);
 
   if (warp == 0) {
     // ---------------- producer ----------------
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
+      if (xres && q1 > q0) {
+        const uint32_t fb = (uint32_t)((kc + 7) & ~7) * 4u;
+        mbar_expect_tx(&xb_full, (uint32_t)kc * kExactBlock + fb);
+        bulk_g2s(xb_s, bt, (uint32_t)kc * kExactBlock, &xb_full);
+        bulk_g2s(xb_s + (size_t)kc * kExactBlock, fe_src, fb, &xb_full);
+      }
       UnitCursor C;
       C.init(q0, nu, tiles);
       int j = 0;
       for (int q = q0; q < q1; ++q, ++j, C.next(nu, tiles)) {
         if (*reinterpret_cast<volatile int*>(&s_abort)) break;
-        const int k = s_slot[C.i], e = s_exp[C.i], c0 = C.u * kUC, n = min(kUC, kc - c0);
+        const int c0 = C.u * kUC, n = min(kUC, kc - c0);
         const int s = j % kUStages, use = j / kUStages;
         if (use > 0 && !mbar_wait(&empty[s], (uint32_t)((use - 1) & 1), err, EF_TIMEOUT_EMPTY)) {
           s_abort = 1;
           break;
         }
-        const uint8_t* tile = wbase + ((int64_t)e * tiles + C.mt) * tile_bytes;
+        const int k = s_slot[C.i], e = s_exp[C.i];
         const int slab = c0 >> 4, sl0 = slab * 16, nch = min(16, kc - sl0);
-        const uint8_t* sb = tile + ex_slab_off(slab);
+        const uint8_t* sb = wbase + ((int64_t)e * tiles + C.mt) * tile_bytes + ex_slab_off(slab);
         uint8_t* st = smem + (size_t)s * kUStage;
-        mbar_expect_tx(&full[s], (uint32_t)n * (2048u + 1024u) + 512u + 16u);
+        const uint32_t sbytes = n > 4 ? 1024u : 512u;   // one or two scale groups
+        const uint32_t bytes = (uint32_t)n * 2048u + sbytes + (xres ? 0u : (uint32_t)n * kExactBlock + 32u);
+        mbar_expect_tx(&full[s], bytes);
         bulk_g2s_stream(st, sb + (int64_t)(c0 - sl0) * 2048, (uint32_t)n * 2048u, &full[s], pol);
-        bulk_g2s_stream(st + kUStA, sb + (int64_t)nch * 2048 + ((c0 - sl0) >> 2) * 512, 512u, &full[s], pol);
-        bulk_g2s(st + kUStA + kUStS, bt + (int64_t)k * bt_stride + (int64_t)c0 * 1024, (uint32_t)n * 1024u, &full[s]);
-        bulk_g2s(st + kUStA + kUStS + kUStB, fe_src + (int64_t)k * fe_stride + c0, 16u, &full[s]);
+        bulk_g2s_stream(st + kUStA, sb + (int64_t)nch * 2048 + ((c0 - sl0) >> 2) * 512, sbytes, &full[s], pol);
+        if (!xres) {
+          bulk_g2s(st + kUStA + kUStS, bt + (int64_t)k * bt_stride + (int64_t)c0 * kExactBlock,
+                   (uint32_t)n * kExactBlock, &full[s]);
+          bulk_g2s(st + kUStA + kUStS + kUStB, fe_src + (int64_t)k * fe_stride + c0, 32u, &full[s]);
+        }
       }
       // no copy may still be landing in shared memory when the CTA exits
       for (int q = max(0, j - kUStages); q < j; ++q)
         mbar_wait(&full[q % kUStages], (uint32_t)((q / kUStages) & 1), err, EF_TIMEOUT_FULL);
+      if (xres && q1 > q0) mbar_wait(&xb_full, 0u, err, EF_TIMEOUT_FULL);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       umma::cp_sf_group(tb + kUSfCol, sf_one);
       umma::cp_sf_group(tb + kUSfCol + 4, sf_one);
-      constexpr uint32_t idesc = umma::idesc_mxf4(128, 64, 0, 0);
+      constexpr uint32_t idesc = umma::idesc_mxf4(128, kExactCols, 0, 0);
+      if (xres && q1 > q0 && !mbar_wait(&xb_full, 0u, err, EF_TIMEOUT_FULL)) s_abort = 1;
       UnitCursor C;
       C.init(q0, nu, tiles);
       int j = 0;
@@ -618,64 +636,76 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
         }
         umma::fence_after_sync();
         const uint8_t* st = smem + (size_t)s * kUStage;
-        for (int p = 0; p < n / 2; ++p) {
-          const uint64_t ad = umma::smem_desc(st + p * 4096, 2048, 128);
-          const uint64_t bd = umma::smem_desc(st + kUStA + kUStS + p * 2048, 1024, 128);
-          umma::mma_mxf4(tb + (uint32_t)(acc * 128 + p * 64), ad, bd, idesc, tb + kUSfCol, tb + kUSfCol + 4, false);
-        }
+        const uint8_t* bsrc = xres ? xb_s + (size_t)C.u * kUC * kExactBlock : st + kUStA + kUStS;
+        const uint64_t ad0 = umma::smem_desc(st, 2048, 128), bd0 = umma::smem_desc(bsrc, kExactBlock, 128);
+        for (int p = 0; p < n / 2; ++p)   // descriptor start addresses in 16-byte units
+          umma::mma_mxf4(tb + (uint32_t)(acc * kUAccCols + p * kExactCols), ad0 + (uint64_t)(p * 4096 / 16),
+                         bd0 + (uint64_t)(p * 2 * kExactBlock / 16), idesc, tb + kUSfCol, tb + kUSfCol + 4, false);
         umma::commit(&empty[s]);
         umma::commit(&acc_full[acc]);
       }
     }
   } else {
     // ---------------- epilogue ----------------
-    const int ew = warp - 2, quad = warp & 3, jc = ew >> 2;   // this warp's TMEM lane quadrant and chunk
+    const int ew = warp - 2, quad = warp & 3, pr = ew >> 2;   // this warp's TMEM lane quadrant and chunk pair
     const int row = 32 * quad + lane;
     UnitCursor C;
     C.init(q0, nu, tiles);
     int j = 0, run = 0, run_u0 = C.u, rp = 0;
     double racc = 0.0;
+    if (xres && q1 > q0) mbar_wait_sleep(&xb_full, 0u, err, EF_TIMEOUT_FULL, 64);   // the resident scale exponents
     for (int q = q0; q < q1; ++q, ++j, C.next(nu, tiles)) {
       const int s = j % kUStages, acc = j % kUAcc;
       const int n = min(kUC, kc - C.u * kUC);
-      const bool live = jc < n;
-      bool ok = mbar_wait(&acc_full[acc], (uint32_t)((j / kUAcc) & 1), err, EF_TIMEOUT_FULL);
+      const bool live = 2 * pr < n;
+      bool ok = mbar_wait_sleep(&acc_full[acc], (uint32_t)((j / kUAcc) & 1), err, EF_TIMEOUT_FULL, 64);
       ok = ok && mbar_wait(&full[s], (uint32_t)((j / kUStages) & 1), err, EF_TIMEOUT_FULL);
-      ok = __all_sync(0xffffffffu, ok);   // the accumulator load below is warp-collective
+      ok = __all_sync(0xffffffffu, ok);   // the accumulator loads below are warp-collective
       umma::fence_after_sync();
-      float v[32];
+      float v[48];
       if (live && ok) {
-        umma::ld_32x32b_x32(tb + ((uint32_t)(32 * quad) << 16) + (uint32_t)(acc * 128 + jc * 32), v);
+        const uint32_t ta = tb + ((uint32_t)(32 * quad) << 16) + (uint32_t)(acc * kUAccCols + pr * kExactCols);
+        float* v0 = v;
+        umma::ld_32x32b_x32(ta, *reinterpret_cast<float(*)[32]>(v0));
+        umma::ld_32x32b_x16(ta + 32, *reinterpret_cast<float(*)[16]>(v0 + 32));
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        for (int i = 0; i < 48; ++i) v[i] = 0.f;
       }
       umma::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
       const uint8_t* st = smem + (size_t)s * kUStage;
-      const uint32_t ew_scale = st[kUStA + 16 * (row & 31) + 4 * (row >> 5) + jc];   // E_w of (row, chunk)
-      const uint32_t fe = (uint32_t)reinterpret_cast<const int*>(st + kUStA + kUStS + kUStB)[jc];
+      uint32_t ews[2], fes[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int jc = 2 * pr + h;   // chunk within the unit: scale group jc / 4, byte jc % 4
+        ews[h] = st[kUStA + (jc >> 2) * 512 + 16 * (row & 31) + 4 * (row >> 5) + (jc & 3)];
+        fes[h] = (uint32_t)(xres ? xfe_s[C.u * kUC + jc] : reinterpret_cast<const int*>(st + kUStA + kUStS + kUStB)[jc]);
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
       if (live) {
-        // this chunk's 27 digit dots: columns (jc & 1) * 32 + d of the pair's accumulator
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int d0 = 7 * g, d1 = min(kExactDigits, d0 + 7);
-          float f = v[d1 - 1];
+        for (int h = 0; h < 2; ++h) {
+          // chunk h of the pair: its 19 digit dots at columns h * 24 + t
 #pragma unroll
-          for (int d = d1 - 2; d >= d0; --d) f = fmaf(f, 4.0f, v[d]);   // exact: integers in halves below 2^23
-          const double sc = __hiloint2double((int)((ew_scale + fe + 14u * g) << 20), 0);
-          racc = fma((double)f, sc, racc);
+          for (int g = 0; g < 4; ++g) {
+            const int t0 = 5 * g, t1 = min(kExactDigits, t0 + 5);
+            float f = v[h * 24 + t1 - 1];
+#pragma unroll
+            for (int t = t1 - 2; t >= t0; --t) f = fmaf(f, 8.0f, v[h * 24 + t]);   // exact: halves below 2^23
+            const double sc = __hiloint2double((int)((ews[h] + fes[h] + 15u * g) << 20), 0);
+            racc = fma((double)f, sc, racc);
+          }
         }
       }
       ++run;
       const bool run_end = q + 1 == q1 || C.u + 1 == nu;   // the next unit starts another item
       if (!run_end) continue;
-      // ---- the run's partial: the four chunk warps of each row summed, written at the run's first unit ----
+      // ---- the run's partial: the four pair warps of each row summed, written at the run's first unit ----
       const int k = s_slot[C.i], e = s_exp[C.i], mt = C.mt;
-      red[rp][jc][row] = racc;
+      red[rp][pr][row] = racc;
       racc = 0.0;
       named_bar(1, 32 * kUEpiWarps);
       const int nrun = run, u_start = run_u0;
@@ -683,7 +713,7 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
       run_u0 = 0;   // a later run of this CTA starts an item at unit 0
       const int rb = rp;
       rp ^= 1;
-      if (jc != 0) continue;
+      if (pr != 0) continue;
       const double t = ((red[rb][0][row] + red[rb][1][row]) + red[rb][2][row]) + red[rb][3][row];
       double* pk = part + (size_t)k * nu * rows_out;
       pk[(size_t)u_start * rows_out + (size_t)mt * 128 + row] = t;
@@ -741,8 +771,8 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
           if (a.up_b) uv = __fadd_rn(uv, a.up_b[(size_t)e * a.I + i]);
           const int ch = 2 * mt + quad;   // the down projection's chunk column of these 32 activations
           const int kcd = a.I / 32;
-          exact_bterm_warp(act_exact(gv, uv, a.oai_swiglu), lane, a.abt + ((int64_t)k * kcd + ch) * 1024, ch & 1,
-                           a.afe + (int64_t)k * ((kcd + 3) & ~3) + ch);
+          exact_bterm_warp(act_exact(gv, uv, a.oai_swiglu), lane, a.abt + ((int64_t)k * kcd + ch) * kExactBlock,
+                           ch & 1, a.afe + (int64_t)k * ((kcd + 7) & ~7) + ch);
         }
       } else {
         const int r = mt * 128 + row;
@@ -938,6 +968,7 @@ cudaError_t launch_exact_attention(const DevCtx& c, const AttnArgs& a, int range
 }
 
 int exact_seg_count(int kc) { return (kc + kUC - 1) / kUC; }
+int exact_term_block_bytes() { return kExactBlock; }
 
 cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a0, cudaStream_t s, int part) {
   ExactMoeArgs a = a0;
@@ -952,10 +983,15 @@ cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a0, cudaStream
   if (a.n_seg_gu != exact_seg_count(a.H / 32) || a.n_seg_down != exact_seg_count(a.I / 32) ||
       a.h_pad < tc_down_tiles(a.H) * 128)
     return cudaErrorInvalidValue;
-  const size_t smem = (size_t)kUStages * kUStage;
   for (int ph = 0; ph < 2; ++ph) {
     if (part >= 0 && part != ph) continue;
     auto kern = ph ? exact_tc_kernel<1> : exact_tc_kernel<0>;
+    // gate/up keeps x's B terms resident in shared memory when they fit beside the stages
+    const int kc = ph ? a.I / 32 : a.H / 32;
+    const size_t stages = (size_t)kUStages * kUStage;
+    const size_t xb = (size_t)kc * kExactBlock + (size_t)((kc + 7) & ~7) * 4;
+    const int xres = (ph == 0 && stages + xb <= 200 * 1024) ? 1 : 0;
+    const size_t smem = stages + (xres ? xb : 0);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
@@ -968,7 +1004,7 @@ cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a0, cudaStream
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kern, a);
+    e = cudaLaunchKernelEx(&cfg, kern, a, xres);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

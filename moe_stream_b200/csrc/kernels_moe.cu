@@ -1125,7 +1125,7 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, ui
     for (int b = e * nw + warp; b < nb; b += (int)gridDim.x * nw) {
       const int i = 32 * b + lane;
       const float v = a.h ? __fmul_rn(__fmul_rn(a.h[i], inv), a.norm_w[i]) : a.xn[i];
-      exact_bterm_warp(v, lane, a.xbt + (size_t)b * 1024, b & 1, a.xfe + b);
+      exact_bterm_warp(v, lane, a.xbt + (size_t)b * kExactBlock, b & 1, a.xfe + b);
     }
   }
   __syncthreads();

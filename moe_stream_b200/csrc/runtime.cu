@@ -262,10 +262,10 @@ struct ms_model {
   bool exact = true;
   double* ex_gp = nullptr;          // [K][segments][2 I] gate/up partial dots
   double* ex_dp = nullptr;          // [K][segments][h_pad] down partial dots
-  uint8_t* ex_xbt = nullptr;        // [H/32][1024] exact B terms of the MoE input
+  uint8_t* ex_xbt = nullptr;        // [H/32][term block] exact B terms of the MoE input
   int* ex_xfe = nullptr;            // [H/32]
-  uint8_t* ex_abt = nullptr;        // [K][I/32][1024] exact B terms of the activations
-  int* ex_afe = nullptr;            // [K][I/32 rounded up to 4]
+  uint8_t* ex_abt = nullptr;        // [K][I/32][term block] exact B terms of the activations
+  int* ex_afe = nullptr;            // [K][I/32 rounded up to 8]
   uint32_t* ex_cnt = nullptr;       // [K][gate/up tiles] per-tile arrival counters
   int ex_seg_gu = 0, ex_seg_down = 0, ex_hpad = 0;
   float* ex_kgu = nullptr;          // K-quant experts: gate / up outputs [K][2][I]
@@ -1592,10 +1592,10 @@ ms_status ms_model_finalize(ms_model* m) {
     m->ex_hpad = tc_down_tiles(H) * 128;
     s = s ? s : m->alloc(&m->ex_gp, (size_t)c.top_k * m->ex_seg_gu * 2 * c.inter * 8);
     s = s ? s : m->alloc(&m->ex_dp, (size_t)c.top_k * m->ex_seg_down * m->ex_hpad * 8);
-    s = s ? s : m->alloc(&m->ex_xbt, (size_t)(H / 32) * 1024);
-    s = s ? s : m->alloc(&m->ex_xfe, (size_t)(H / 32 + 4) * 4);   // + the padding of a 16-byte copy
-    s = s ? s : m->alloc(&m->ex_abt, (size_t)c.top_k * (c.inter / 32) * 1024);
-    s = s ? s : m->alloc(&m->ex_afe, (size_t)c.top_k * ((c.inter / 32 + 3) & ~3) * 4 + 16);   // rows of 4-aligned stride
+    s = s ? s : m->alloc(&m->ex_xbt, (size_t)(H / 32) * exact_term_block_bytes());
+    s = s ? s : m->alloc(&m->ex_xfe, (size_t)(H / 32 + 8) * 4);   // + the padding of a 32-byte copy
+    s = s ? s : m->alloc(&m->ex_abt, (size_t)c.top_k * (c.inter / 32) * exact_term_block_bytes());
+    s = s ? s : m->alloc(&m->ex_afe, (size_t)c.top_k * ((c.inter / 32 + 7) & ~7) * 4 + 32);   // rows of 8-aligned stride
     s = s ? s : m->alloc(&m->ex_cnt, (size_t)c.top_k * (tc_gu_tiles(c.inter) + tc_down_tiles(H)) * 4);
     s = s ? s : m->alloc(&m->xterm, (size_t)tc_bterm_bytes(H / 32));
     s = s ? s : m->alloc(&m->act_terms, (size_t)c.top_k * tc_bterm_bytes(c.inter / 32));
