@@ -513,7 +513,11 @@ def run_case_qwen3(args):
         "workload": f"Qwen3-30B-A3B-shaped Q4_K/Q6_K greedy decode after a {prompt_len}-token prompt",
         "layers": spec.layers, "kv_context": prompt_len, "l2": "no flush: each step streams > 2 GB"},
         "steps": args.steps, "warmup": args.warmup}
-    for B in batches:
+    modes = ["exact", "fast"] if args.numerics == "both" else [args.numerics]
+    for mode, B in [(m, b) for m in modes for b in batches]:
+        # exact: the order-independent kernels (token-exact against the oracle); fast: f32 kernels
+        # in their own summation order (per-layer parity 1e-3, not token-exact over long runs)
+        eng.set_exact(mode == "exact")
         prompts = np.stack([synth.prompt_ids(spec, prompt_len, seed=b) for b in range(B)])
         t0 = time.time()
         if B == 1:
@@ -538,15 +542,16 @@ def run_case_qwen3(args):
         ctx.sync()
         nbytes, uniq = qwen3_step_bytes(spec, B, prompt_len + args.warmup + args.steps // 2)
         gbs = nbytes / (ms * 1e-3) / 1e9
-        out[f"bs{B}"] = {"tok_s": round(B / (ms * 1e-3), 1), "ms_per_step": round(ms, 4),
+        res = out.setdefault(mode, {})
+        res[f"bs{B}"] = {"tok_s": round(B / (ms * 1e-3), 1), "ms_per_step": round(ms, 4),
                          "kernels_per_step": eng.kernels_per_step if B == 1 else eng.batch_kernels_per_step,
                          "algorithmic_bytes_per_step": int(nbytes), "expected_unique_experts_per_layer": round(uniq, 1),
                          "achieved_gbs": round(gbs, 1), "hbm_frac": round(gbs / peak, 4), "peak_kind": peak_kind,
                          "clocks": clk.summary()}
         if not args.no_profile:
-            out[f"bs{B}"]["kernel_us_per_step"] = (eng.batch_profile_step() if B > 1 else
+            res[f"bs{B}"]["kernel_us_per_step"] = (eng.batch_profile_step() if B > 1 else
                                                    [round(v, 1) for v in eng.profile_step()])
-        log(f"bs{B}: {out[f'bs{B}']}")
+        log(f"{mode} bs{B}: {res[f'bs{B}']}")
         if B > 1:
             eng.batch_close()
     eng.close()
@@ -574,6 +579,8 @@ def main():
                     help="moe-layer: the decode expert FFN alone; prefill: config 4's MoE step; "
                          "qwen3: config 2 decode at the --batch sizes")
     ap.add_argument("--batch", default="1,32", help="qwen3 case: comma-separated batch sizes")
+    ap.add_argument("--numerics", default="both", choices=["exact", "fast", "both"],
+                    help="qwen3 case: order-independent kernels, f32 kernels, or both")
     ap.add_argument("--save-tokens", default=None, help="write the greedy tokens decoded after the prompt (npz)")
     args = ap.parse_args()
     if args.warmup < 3:

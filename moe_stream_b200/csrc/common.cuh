@@ -71,7 +71,7 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
   return false;
 }
 
-// 1-D bulk copy global -> shared (TMA, no multicast); bytes % 16 == 0, both addresses 16-aligned.
+// 1-D bulk copy global -> this CTA's shared memory; bytes % 16 == 0, both addresses 16-aligned.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),

@@ -7,18 +7,20 @@
 // discrete decision: the Q8_0 codes of the next projection's activation, the routed experts and the
 // greedy token.
 //
-//   exact_attn_kernel   decode attention (ops/attention.rs:178-280) for one token per sequence:
-//                       a thread-block cluster per (kv head, sequence) splits the positions; the
-//                       softmax needs the global max before any exp, so the CTAs exchange their
-//                       maxima, then their f64 denominator sums, then their f64 P*V partials
-//                       through distributed shared memory (three cluster barriers).
-//   exact_gu_kernel     expert gate/up rows of the selected experts (MXFP4 tensor-core tiles read
-//                       thread-per-row, coalesced 16-byte code loads) over a K segment -> f64
-//                       partial dots.
-//   exact_down_kernel   rebuilds its K segment of the activation from the gate/up partials
-//                       (bias, OAI SwiGLU or SiLU*up, model/layer.rs:1797-1845, ops/activation.rs)
-//                       and writes f64 partial dots of the down rows; the residual kernel sums the
-//                       segments, adds the bias and combines the experts in ascending id.
+//   exact_attn_kernel     decode attention (ops/attention.rs:178-280) for one token per sequence:
+//                         a thread-block cluster per (kv head, sequence) splits the positions; the
+//                         softmax needs the global max before any exp, so the CTAs exchange their
+//                         maxima, then their f64 denominator sums, then their f64 P*V partials
+//                         through distributed shared memory (three cluster barriers).  With 8
+//                         queries per kv head the dots run on the f64 tensor cores.
+//   exact_tc_kernel<0/1>  expert gate/up and down (model/layer.rs:1797-1847) over the packed MXFP4
+//                         tiles on tcgen05: x (or the activation) as exact base-8 digit terms, unit
+//                         block scales, f32 digit folds and f64 scaling in the epilogue; the last
+//                         CTA of an item writes the activation terms (gate/up) or the slot's output
+//                         row (down), which the residual kernel combines in ascending expert id.
+//   exact_kq_*_kernel     K-quant experts (Q4_K / Q6_K), dequantized in the reference's f32 op
+//                         order and dotted in double.
+//   exact_argmax_refine   the greedy token: f64 re-scoring of the ids near the approximate maximum.
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
