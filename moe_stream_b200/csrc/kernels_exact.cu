@@ -804,7 +804,9 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
 // A lane takes 64 elements of a row: group q (0..3) of a 256-element superblock -- Q4_K: the low
 // and high nibbles of 32 code bytes (sub-blocks 2q, 2q+1); Q6_K: element runs l and l + 64 (q even)
 // or l + 32 and l + 96 (q odd) of one half.  Element values are dequantized with the reference's
-// f32 op order (dequant.rs:218-262, 335-378), then dotted with x in double.
+// f32 op order (dequant.rs:218-262, 335-378), then dotted with x in double.  x sits in shared memory
+// as doubles with one padding double after every 64 elements (a superblock spans 260), so the 32
+// lanes of a warp -- 32 groups at once -- read from different banks.
 __device__ __forceinline__ double kq_group_dot(int fmt, const uint8_t* blk, int q, const double* xs) {
   double a0 = 0.0, a1 = 0.0;
   if (fmt == Q_Q4_K) {
@@ -822,7 +824,7 @@ __device__ __forceinline__ double kq_group_dot(int fmt, const uint8_t* blk, int 
     const uint4* qp = reinterpret_cast<const uint4*>(blk + 16 + 32 * q);
     const uint4 w0 = qp[0], w1 = qp[1];
     const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-    const double* xl = xs + 64 * q;
+    const double* xl = xs + 65 * q;   // 64-element group q (one padding double per group)
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
 #pragma unroll
@@ -841,7 +843,7 @@ __device__ __forceinline__ double kq_group_dot(int fmt, const uint8_t* blk, int 
     const int half = q >> 1, sub = q & 1;
     const uint8_t* ql = blk + half * 64 + 32 * sub;
     const uint8_t* qh = blk + 128 + half * 32;
-    const double* xl = xs + half * 128 + 32 * sub;
+    const double* xl = xs + half * 130 + 32 * sub;   // padded: groups 2 half and 2 half + 1
 #pragma unroll 8
     for (int l = 0; l < 32; ++l) {
       const uint32_t lb = ql[l], hb = qh[l];
@@ -851,7 +853,7 @@ __device__ __forceinline__ double kq_group_dot(int fmt, const uint8_t* blk, int 
       const float va = __fmul_rn(__fmul_rn(d, (float)scv[isa]), (float)qa);
       const float vb = __fmul_rn(__fmul_rn(d, (float)scv[isb]), (float)qb);
       a0 = fma((double)va, xl[l], a0);
-      a1 = fma((double)vb, xl[64 + l], a1);
+      a1 = fma((double)vb, xl[65 + l], a1);
     }
   }
   return a0 + a1;
@@ -871,7 +873,7 @@ __device__ __forceinline__ void kq_rows(int fmt, const uint8_t* w, int64_t rb, i
   double part = 0.0;
   if (sub < R && row < rows) {
     const uint8_t* wr = w + (int64_t)row * rb;
-    for (int gi = grp0; gi < G; gi += 32) part += kq_group_dot(fmt, wr + (gi >> 2) * sb_bytes, gi & 3, xs + 256 * (gi >> 2));
+    for (int gi = grp0; gi < G; gi += 32) part += kq_group_dot(fmt, wr + (gi >> 2) * sb_bytes, gi & 3, xs + 260 * (gi >> 2));
   }
   red[threadIdx.x] = part;
   __syncwarp();
@@ -889,7 +891,7 @@ __device__ __forceinline__ void kq_rows(int fmt, const uint8_t* w, int64_t rb, i
 }
 
 __global__ void __launch_bounds__(kKThreads) exact_kq_gu_kernel(ExactKqArgs a, uint32_t* err) {
-  extern __shared__ double xk[];   // [H]
+  extern __shared__ double xk[];   // [H + H/64]: element e at e + e/64
   __shared__ double red[kKThreads];
   const int which = blockIdx.z & 1, b = blockIdx.z >> 1;   // 0 gate, 1 up; token b
   const int k = b * a.K + blockIdx.y;                       // (token, slot)
@@ -897,7 +899,7 @@ __global__ void __launch_bounds__(kKThreads) exact_kq_gu_kernel(ExactKqArgs a, u
   pdl_launch_dependents();
   const int e = a.idx[k] - a.expert_base;
   if (e < 0 || e >= a.n_local) return;
-  for (int i = threadIdx.x; i < a.H; i += kKThreads) xk[i] = (double)a.x[(size_t)b * a.H + i];
+  for (int i = threadIdx.x; i < a.H; i += kKThreads) xk[i + (i >> 6)] = (double)a.x[(size_t)b * a.H + i];
   __syncthreads();
   const int G = a.H / 64, R = G >= 32 ? 1 : 32 / G;
   const int64_t rb = (int64_t)(a.H / 256) * (a.gate_fmt == Q_Q4_K ? 144 : kQ6PadBytes);
@@ -909,7 +911,7 @@ __global__ void __launch_bounds__(kKThreads) exact_kq_gu_kernel(ExactKqArgs a, u
 }
 
 __global__ void __launch_bounds__(kKThreads) exact_kq_down_kernel(ExactKqArgs a, uint32_t* err) {
-  extern __shared__ double ak[];   // [I] activations
+  extern __shared__ double ak[];   // [I + I/64] activations, element e at e + e/64
   __shared__ double red[kKThreads];
   const int k = blockIdx.z * a.K + blockIdx.y;               // (token, slot)
   pdl_wait_prior();
@@ -917,7 +919,7 @@ __global__ void __launch_bounds__(kKThreads) exact_kq_down_kernel(ExactKqArgs a,
   const int e = a.idx[k] - a.expert_base;
   if (e < 0 || e >= a.n_local) return;
   const float* g = a.gu_out + (size_t)k * 2 * a.I;
-  for (int i = threadIdx.x; i < a.I; i += kKThreads) ak[i] = (double)act_exact(g[i], g[a.I + i], a.oai_swiglu);
+  for (int i = threadIdx.x; i < a.I; i += kKThreads) ak[i + (i >> 6)] = (double)act_exact(g[i], g[a.I + i], a.oai_swiglu);
   __syncthreads();
   const int G = a.I / 64, R = G >= 32 ? 1 : 32 / G;
   const int64_t rb = (int64_t)(a.I / 256) * (a.down_fmt == Q_Q4_K ? 144 : kQ6PadBytes);
@@ -1113,10 +1115,10 @@ cudaError_t launch_exact_kq_moe(const DevCtx& c, const ExactKqArgs& a, cudaStrea
   const int rg = rows_per_cta(a.H), rd = rows_per_cta(a.I);
   if (a.B < 1) return cudaErrorInvalidValue;
   cudaError_t e = launch_pdl_x(exact_kq_gu_kernel, dim3((unsigned)((a.I + rg - 1) / rg), (unsigned)a.K, 2u * a.B),
-                               dim3(kKThreads), (size_t)a.H * 8, s, a, c.err);
+                               dim3(kKThreads), (size_t)(a.H + a.H / 64) * 8, s, a, c.err);
   if (e != cudaSuccess) return e;
   return launch_pdl_x(exact_kq_down_kernel, dim3((unsigned)((a.H + rd - 1) / rd), (unsigned)a.K, (unsigned)a.B),
-                      dim3(kKThreads), (size_t)a.I * 8, s, a, c.err);
+                      dim3(kKThreads), (size_t)(a.I + a.I / 64) * 8, s, a, c.err);
 }
 
 }  // namespace ms
