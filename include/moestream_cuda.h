@@ -119,6 +119,14 @@ MS_API ms_status ms_router_topk(ms_ctx* ctx, const float* d_h, const float* d_no
 MS_API ms_status ms_rope(ms_ctx* ctx, const float* d_x, const float* d_cos, const float* d_sin, int n_tokens,
                          int heads, int head_dim, int rot_dim, float* d_y);
 
+/* One token drawn from logits (SamplingParams::sample, engine.rs:124-208): d_logits [V] f32,
+ * d_counts [V] times each token was generated (repetition penalty; NULL = none), r the uniform
+ * draw in [0, 1), d_work [V] f32 scratch, *d_token the result (device memory).  Sums of
+ * probabilities are exact to 2^-109 and rounded to f32 once, so the result does not depend on
+ * summation order. */
+MS_API ms_status ms_sample(ms_ctx* ctx, const float* d_logits, int V, const uint32_t* d_counts, float temperature,
+                           float top_p, float repetition_penalty, float r, float* d_work, int32_t* d_token);
+
 /* One attention half-layer in device memory (layer.rs:511-749 for a single decode token). */
 typedef struct ms_attn_layer {
   int hidden, heads, kv_heads, head_dim, rot_dim;
@@ -305,9 +313,17 @@ MS_API ms_status ms_model_forward(ms_model* m, const int32_t* tokens, int n_toke
  * tokens, routed experts and the Q8_0 activation codes are reproducible bit for bit against a CPU
  * evaluation of the reference's ops (engine.rs:1869-2118) that rounds the same way.  0: the
  * pipelined f32 kernels (tensor-core experts, split-K attention), results within ~1e-6 relative
- * of 1 per op but not bit-identical.  MXFP4 experts and head dims 32/64/128 have order-independent
- * kernels; K-quant experts use the pipelined kernels in both modes. */
+ * of 1 per op but not bit-identical.  MXFP4 and K-quant experts and head dims 32/64/128 have
+ * order-independent kernels. */
 MS_API ms_status ms_model_set_exact(ms_model* m, int enable);
+/* Sampled decoding (SamplingParams::sample, engine.rs:124-208, as generate_sampled drives it,
+ * engine.rs:2222-2300).  enable != 0: from the next forward on, each step's token is drawn on the
+ * device (repetition penalty over the tokens drawn since this call, greedy when temperature == 0,
+ * temperature, softmax, top-p, then the draw) instead of the greedy argmax; the draws come from
+ * SplitMix64(seed, n) for the n-th draw (24 bits, as rand builds an f32), so a seed reproduces a
+ * sequence.  enable == 0 returns to greedy decoding.  temperature >= 0, 0 < top_p, penalty > 0. */
+MS_API ms_status ms_model_set_sampling(ms_model* m, int enable, float temperature, float top_p,
+                                       float repetition_penalty, uint64_t seed);
 /* How ms_model_forward runs more than one token (a prompt).  1 (default): batched passes of up to
  * 2048 tokens -- Q8_0 projections of all tokens, QK-norm + RoPE at absolute positions, causal
  * attention with the sliding-window mask and sinks over the cache and the chunk, the router of

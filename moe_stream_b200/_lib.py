@@ -88,6 +88,7 @@ _SIGS = {
     "ms_moe_mxfp4_prefill_packed": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i, _vp,
                                               _vp, _vp, _i]),
     "ms_rope": (C.c_int, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "ms_sample": (C.c_int, [_vp, _vp, _i, _vp, C.c_float, C.c_float, C.c_float, C.c_float, _vp, _vp]),
     "ms_attn_layer_decode": (C.c_int, [_vp, C.POINTER(AttnLayer), _i, _vp]),
     "ms_deltanet_decode": (C.c_int, [_vp, C.POINTER(DeltaNetLayer), _vp, _vp, _vp, _vp]),
     "ms_shared_expert": (C.c_int, [_vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _vp, _vp]),
@@ -124,6 +125,7 @@ _SIGS = {
     "ms_model_set_trace": (C.c_int, [_vp, _i]),
     "ms_model_set_prefill": (C.c_int, [_vp, _i]),
     "ms_model_set_exact": (C.c_int, [_vp, _i]),
+    "ms_model_set_sampling": (C.c_int, [_vp, _i, C.c_float, C.c_float, C.c_float, C.c_uint64]),
     "ms_model_layer_trace": (C.c_int, [_vp, _fp, _fp]),
     "ms_model_set_graph": (C.c_int, [_vp, _i]),
     "ms_model_kernels_per_step": (C.c_int, [_vp]),

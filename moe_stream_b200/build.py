@@ -9,7 +9,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "_build")
-SOURCES = ["kernels_dense.cu", "kernels_moe.cu", "kernels_moe_tc.cu", "kernels_prefill.cu", "kernels_prefill_attn.cu", "kernels_exact.cu", "kernels_ssm.cu", "kernels_batch.cu", "runtime.cu"]
+SOURCES = ["kernels_dense.cu", "kernels_moe.cu", "kernels_moe_tc.cu", "kernels_prefill.cu", "kernels_prefill_attn.cu", "kernels_exact.cu", "kernels_sample.cu", "kernels_ssm.cu", "kernels_batch.cu", "runtime.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr"]

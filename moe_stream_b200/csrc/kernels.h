@@ -468,6 +468,22 @@ cudaError_t launch_silu_mul(const float* g, const float* u, float* o, int n, cud
 cudaError_t launch_gated_accum(const float* x, const float* gate_inp, const float* v, float* y, int n, cudaStream_t s);
 
 // ---- step plumbing ----
+// ---- sampling (kernels_sample.cu): SamplingParams::sample (engine.rs:124-208) on the device ----
+struct SampleArgs {
+  const float* logits = nullptr;      // [V]
+  int V = 0;
+  const uint32_t* counts = nullptr;   // [V] times each token was generated (repetition penalty), or null
+  float temperature = 1.0f, top_p = 1.0f, penalty = 1.0f;
+  float r = 0.0f;                     // the draw in [0, 1) when rng is null
+  unsigned long long* rng = nullptr;  // optional [seed, n]: draw = SplitMix64(seed, n); n advances per call
+  float* work = nullptr;              // [V] scratch
+  int* token_out = nullptr;           // optional
+  unsigned long long* key_out = nullptr;   // optional: the token as a step key (StepState::key)
+  uint32_t* counts_rw = nullptr;      // optional: counts[token] += 1 after the draw
+  const int* draw = nullptr;          // optional: no draw at all while *draw == 0 (prompt positions)
+};
+cudaError_t launch_sample(const DevCtx& c, const SampleArgs& a, cudaStream_t s);
+
 struct StepState {
   int token_in;            // host-provided token
   int use_argmax;          // 1: take the token from the previous step's argmax key

@@ -117,6 +117,15 @@ class Context:
         check(lib().ms_rope(self.h, _ptr(x), _ptr(cos), _ptr(sin), n_tokens, heads, head_dim, rot_dim, _ptr(y)),
               self.h)
 
+    def sample(self, logits, counts, temperature: float, top_p: float, repetition_penalty: float, r: float,
+               work, token) -> None:
+        """token[0] = SamplingParams::sample (engine.rs:124-208) of device logits [V] (f32), with
+        counts [V] (uint32, times each token was generated; None = no penalty), draw r in [0, 1)
+        and work [V] f32 scratch."""
+        check(lib().ms_sample(self.h, _ptr(logits), int(logits.numel()), _ptr(counts) if counts is not None else None,
+                              float(temperature), float(top_p), float(repetition_penalty), float(r), _ptr(work),
+                              _ptr(token)), self.h)
+
     def attn_layer_decode(self, layer: dict, pos: int, h) -> None:
         """h += attention(RMSNorm(h)) for one token at `pos` (layer.rs:511-749).  layer: ints hidden,
         heads, kv_heads, head_dim, rot_dim, window, cap, float eps and device tensors attn_norm, wqkv,
@@ -363,6 +372,22 @@ class Engine:
         """Order-independent decode numerics (f64 reductions rounded once; default) or the
         pipelined f32 kernels."""
         check(lib().ms_model_set_exact(self.h, int(enable)), self.ctx.h)
+
+    def set_sampling(self, enable: bool, temperature: float = 1.0, top_p: float = 1.0,
+                     repetition_penalty: float = 1.0, seed: int = 0) -> None:
+        """Draw each step's token on the device (SamplingParams::sample, engine.rs:124-208) instead
+        of the greedy argmax; the n-th draw comes from SplitMix64(seed, n)."""
+        check(lib().ms_model_set_sampling(self.h, int(enable), float(temperature), float(top_p),
+                                          float(repetition_penalty), int(seed) & ((1 << 64) - 1)), self.ctx.h)
+
+    def generate_sampled(self, prompt: Sequence[int], max_new_tokens: int, temperature: float = 1.0,
+                         top_p: float = 1.0, repetition_penalty: float = 1.0, seed: int = 0) -> list:
+        """Engine::generate_sampled (engine.rs:2222-2300) with a seeded draw; leaves sampling off."""
+        self.set_sampling(True, temperature, top_p, repetition_penalty, seed)
+        try:
+            return self.generate(prompt, max_new_tokens)
+        finally:
+            self.set_sampling(False)
 
     def set_prefill(self, mode: int) -> None:
         """Prompt handling of forward(): 1 batched (bf16 hi/lo expert GEMM, default), 2 batched

@@ -1013,4 +1013,105 @@ int orc_shared_expert(int gu_q, const void* gate, const void* up, int down_q, co
   return 0;
 }
 
+// SamplingParams::sample (engine.rs:124-208).  The reference's f32 running sums of probabilities
+// become sums of 128-bit fixed-point integers (least significant bit 2^-109, probabilities below
+// 2^-85 truncated there) rounded to f32 where the reference holds an f32, so the result does not
+// depend on summation order; exp is the double exp rounded to f32.  r: the uniform draw in [0, 1).
+namespace {
+typedef unsigned __int128 u128;
+u128 fx_from_f32(float v) {
+  uint32_t b;
+  std::memcpy(&b, &v, 4);
+  const int E = (int)((b >> 23) & 0xFFu);
+  if (E == 0 || (b >> 31)) return 0;
+  const u128 M = (u128)((b & 0x7FFFFFu) | 0x800000u);
+  const int sh = E - 41;
+  if (sh >= 0) return M << sh;
+  if (sh > -24) return M >> (-sh);
+  return 0;
+}
+float fx_to_f32(u128 a) {   // nearest, ties to even (values below 2^18)
+  if (a == 0) return 0.f;
+  int msb = 127;
+  while (!((a >> msb) & 1)) --msb;
+  const int lsb = msb - 23;
+  uint64_t mant;
+  int round_bit = 0;
+  bool sticky = false;
+  if (lsb >= 0) {
+    mant = (uint64_t)((a >> lsb) & 0xFFFFFFu);
+    if (lsb >= 1) round_bit = (int)((a >> (lsb - 1)) & 1);
+    if (lsb >= 2) sticky = (a & (((u128)1 << (lsb - 1)) - 1)) != 0;
+  } else {
+    mant = (uint64_t)(a << (-lsb));
+  }
+  int e = msb;
+  if (round_bit && (sticky || (mant & 1))) {
+    ++mant;
+    if (mant == 0x1000000u) { mant >>= 1; ++e; }
+  }
+  const uint32_t bits = ((uint32_t)(e - 109 + 127) << 23) | (uint32_t)(mant & 0x7FFFFFu);
+  float f;
+  std::memcpy(&f, &bits, 4);
+  return f;
+}
+}  // namespace
+
+int orc_sample(const float* logits, int V, const uint32_t* counts, float temperature, float top_p, float penalty,
+               float r) {
+  std::vector<float> x(logits, logits + V);
+  // repetition penalty over the generated tokens (engine.rs:129-141): once per occurrence
+  if (penalty != 1.0f && counts)
+    for (int v = 0; v < V; ++v)
+      for (uint32_t j = 0; j < counts[v]; ++j) x[v] = x[v] > 0.0f ? x[v] / penalty : x[v] * penalty;
+  if (temperature == 0.0f) {   // Iterator::max_by: the last of equal maxima (engine.rs:143-151)
+    float best = -std::numeric_limits<float>::infinity();
+    int bi = -1;
+    for (int v = 0; v < V; ++v)
+      if (x[v] >= best) { best = x[v]; bi = v; }
+    return bi < 0 ? 0 : bi;
+  }
+  if (temperature != 1.0f) {   // engine.rs:154-159
+    const float inv_t = 1.0f / temperature;
+    for (float& v : x) v *= inv_t;
+  }
+  float mx = -std::numeric_limits<float>::infinity();   // engine.rs:162-168
+  for (float v : x) mx = std::max(mx, v);
+  std::vector<float> p(V);
+  u128 tot = 0;
+  for (int v = 0; v < V; ++v) {
+    p[v] = expcr(x[v] - mx);
+    tot += fx_from_f32(p[v]);
+  }
+  const float S = fx_to_f32(tot);
+  for (float& v : p) v = v / S;
+  if (top_p < 1.0f) {   // engine.rs:171-195: stable sort descending, shortest prefix exceeding top_p
+    std::vector<int> ord(V);
+    for (int v = 0; v < V; ++v) ord[v] = v;
+    std::stable_sort(ord.begin(), ord.end(), [&](int a, int b) { return p[a] > p[b]; });
+    u128 cum = 0;
+    int cutoff = V;
+    for (int i = 0; i < V; ++i) {
+      cum += fx_from_f32(p[ord[i]]);
+      if (fx_to_f32(cum) > top_p) { cutoff = i + 1; break; }
+    }
+    std::vector<char> keep(V, 0);
+    for (int i = 0; i < cutoff; ++i) keep[ord[i]] = 1;
+    u128 ks = 0;
+    for (int v = 0; v < V; ++v) {
+      if (!keep[v]) p[v] = 0.0f;
+      ks += fx_from_f32(p[v]);
+    }
+    const float S2 = fx_to_f32(ks);
+    if (S2 > 0.0f)
+      for (float& v : p) v = v / S2;
+  }
+  u128 cum = 0;   // engine.rs:197-207
+  for (int v = 0; v < V; ++v) {
+    cum += fx_from_f32(p[v]);
+    if (p[v] > 0.0f && r < fx_to_f32(cum)) return v;
+  }
+  return V - 1;
+}
+
 }  // extern "C"

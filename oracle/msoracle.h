@@ -51,6 +51,11 @@ void orc_sdpa(const float* q, const float* k, const float* v, int nh, int nkv, i
               double scale, int causal, const float* sinks, int sliding_window, float* out);
 /* RoPE of x [n_tok][heads][hd] with per-token tables cos/sin [n_tok][rot/2] (ops/attention.rs:96-164) */
 void orc_rope(const float* x, const float* cos_t, const float* sin_t, int n_tok, int heads, int hd, int rot, float* y);
+/* SamplingParams::sample (engine.rs:124-208) of logits [V]: counts [V] = times each token was
+ * generated (NULL: none), r = the uniform draw in [0, 1).  Sums of probabilities are exact to
+ * 2^-109 and rounded to f32 once. */
+int orc_sample(const float* logits, int V, const uint32_t* counts, float temperature, float top_p, float penalty,
+               float r);
 /* layer.rs:2346-2403; returns indices/weights [n_tok, k] */
 void orc_top_k_routing(const float* logits, int n_tok, int n_exp, int k, int normalize, int softmax_weight,
                        int32_t* idx, float* w);

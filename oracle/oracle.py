@@ -76,6 +76,8 @@ def lib():
         L.orc_moe_forward.argtypes = [C.POINTER(MoeLayer), _fp, C.c_int, _fp, _i32p, _fp]
         L.orc_moe_forward_range.argtypes = [C.POINTER(MoeLayer), _fp, C.c_int, _fp, C.c_int, C.c_int]
         L.orc_rope.argtypes = [_fp, _fp, _fp, C.c_int, C.c_int, C.c_int, C.c_int, _fp]
+        L.orc_sample.argtypes = [_fp, C.c_int, C.POINTER(C.c_uint32), C.c_float, C.c_float, C.c_float, C.c_float]
+        L.orc_sample.restype = C.c_int
         L.orc_attn_decode.argtypes = [C.POINTER(AttnLayer), _fp, _fp, C.c_int, _fp]
         L.orc_deltanet_step.argtypes = [C.POINTER(DeltaNetLayer), _fp, _fp, _fp, _fp]
         L.orc_shared_expert.argtypes = [C.c_int, _vp, _vp, C.c_int, _vp, _fp, C.c_int, C.c_int, _fp, _fp]
@@ -216,6 +218,16 @@ def moe_forward(layer: dict, x: np.ndarray, expert_range=None):
         return out, None, None
     lib().orc_moe_forward(C.byref(L), _f(x), n_tok, _f(out), _i(idx), _f(w))
     return out, idx, w
+
+
+def sample(logits, counts=None, temperature=1.0, top_p=1.0, penalty=1.0, r=0.5):
+    """SamplingParams::sample (engine.rs:124-208) with the draw r in [0, 1)."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    cp = None
+    if counts is not None:
+        cts = np.ascontiguousarray(counts, dtype=np.uint32)
+        cp = cts.ctypes.data_as(C.POINTER(C.c_uint32))
+    return int(lib().orc_sample(_f(lg), lg.size, cp, float(temperature), float(top_p), float(penalty), float(r)))
 
 
 def rope(x, cos, sin, n_tok, heads, hd, rot):

@@ -799,3 +799,55 @@ def test_prefill_then_decode_matches_stepwise(ctx, tiny_qwen_path):
     b = eng.generate(prompt, 10)
     assert a == b and eng.token_log() == la and eng.seq_len == len(prompt) + 9
     eng.close()
+
+
+# ---- sampling (SamplingParams::sample, engine.rs:124-208) ----
+def _sample_cases(V, n, seed):
+    rng = np.random.default_rng(seed)
+    for t in range(n):
+        lg = (rng.standard_normal(V) * [1.0, 3.0, 8.0][t % 3]).astype(np.float32)
+        if t % 4 == 1:
+            lg[rng.integers(0, V, 8)] = lg.max()                      # ties at the maximum
+        if t % 4 == 2:
+            lg[: V // 2] = np.float32(0.5)                             # ties inside the nucleus boundary
+        counts = rng.integers(0, 3, V).astype(np.uint32) if t % 3 == 0 else None
+        T = [0.0, 1.0, 0.7, 1.3][t % 4]
+        top_p = [1.0, 0.9, 0.5, 0.02, 0.999][t % 5]
+        pen = [1.0, 1.2][t % 2]
+        yield lg, counts, T, top_p, pen, float(rng.random())
+
+
+@pytest.mark.parametrize("V,n", [(50, 40), (3000, 40), (201088, 12)])
+def test_sample_matches_oracle(ctx, orc, V, n):
+    """ms_sample picks the oracle's token: penalty, greedy ties (last maximum), temperature, the
+    top-p nucleus with ties at its boundary in index order, the draw"""
+    work = torch.empty(V, dtype=torch.float32, device="cuda")
+    tok = torch.empty(1, dtype=torch.int32, device="cuda")
+    for i, (lg, counts, T, top_p, pen, r) in enumerate(_sample_cases(V, n, V)):
+        ctx.sample(dev(lg), dev(counts) if counts is not None else None, T, top_p, pen, r, work, tok)
+        torch.cuda.synchronize()
+        want = orc.sample(lg, counts, T, top_p, pen, r)
+        assert int(tok.item()) == want, (i, T, top_p, pen, r)
+    assert ctx.error_flags() == 0
+
+
+def test_model_sampled_generation(ctx, tiny_path):
+    """generate_sampled on the device: temperature 0 gives the greedy sequence, a seed reproduces its
+    sequence and another seed changes it, and the prompt positions draw nothing (the first draw
+    follows the last prompt token)"""
+    from moe_stream_b200.engine import Engine
+    f = np.load(os.path.join(GOLD, "tiny_models.npz"))
+    prompt = f["tiny_gpt_oss_prompt"]
+    eng = Engine.open(tiny_path, max_seq_len=256, ctx=ctx)
+    try:
+        greedy = eng.generate(prompt, 12)
+        assert eng.generate_sampled(prompt, 12, temperature=0.0) == greedy
+        a = eng.generate_sampled(prompt, 12, temperature=1.0, top_p=0.9, repetition_penalty=1.1, seed=5)
+        b = eng.generate_sampled(prompt, 12, temperature=1.0, top_p=0.9, repetition_penalty=1.1, seed=5)
+        c = eng.generate_sampled(prompt, 12, temperature=1.0, top_p=0.9, repetition_penalty=1.1, seed=6)
+        assert a == b and a != c
+        V = eng.config.vocab
+        assert all(0 <= t < V for t in a)
+        assert ctx.error_flags() == 0
+    finally:
+        eng.close()

@@ -186,3 +186,68 @@ def test_gguf_roundtrip(tmp_path):
     per = G.raw_size(G.MXFP4, 256 * 256)
     assert np.array_equal(e, m.tensors["blk.0.ffn_gate_exps.weight"].raw()[3 * per:4 * per])
     r.close()
+
+
+def _sample_reference_f32(lg, counts, T, top_p, pen, r):
+    """SamplingParams::sample (engine.rs:124-208) step by step in f32 with sequential sums"""
+    lg = lg.astype(np.float32).copy()
+    if pen != 1.0 and counts is not None:
+        for v in np.nonzero(counts)[0]:
+            for _ in range(int(counts[v])):
+                lg[v] = lg[v] / np.float32(pen) if lg[v] > 0 else lg[v] * np.float32(pen)
+    if T == 0:
+        return int(np.nonzero(lg == lg.max())[0][-1])   # Iterator::max_by: the last maximum
+    if T != 1:
+        lg = lg * (np.float32(1) / np.float32(T))
+    p = np.exp((lg - lg.max()).astype(np.float64)).astype(np.float32)
+    s = np.float32(0)
+    for v in p:
+        s = np.float32(s + v)
+    p = (p / s).astype(np.float32)
+    if top_p < 1:
+        order = np.argsort(-p, kind="stable")
+        c, cut = np.float32(0), len(p)
+        for i, j in enumerate(order):
+            c = np.float32(c + p[j])
+            if c > np.float32(top_p):
+                cut = i + 1
+                break
+        keep = np.zeros(len(p), bool)
+        keep[order[:cut]] = True
+        p = np.where(keep, p, np.float32(0)).astype(np.float32)
+        s = np.float32(0)
+        for v in p:
+            s = np.float32(s + v)
+        p = (p / s).astype(np.float32)
+    c = np.float32(0)
+    for i, v in enumerate(p):
+        c = np.float32(c + v)
+        if np.float32(r) < c:
+            return i
+    return len(p) - 1
+
+
+def test_sampler_follows_reference_algorithm(orc):  # model/engine.rs:124-208
+    """the oracle's sampler (sums exact to 2^-109, rounded once) picks the token the reference's
+    sequential-f32 algorithm picks: penalties, greedy ties, temperature, top-p, the draw"""
+    rng = np.random.default_rng(0)
+    for t in range(240):
+        V = int(rng.integers(2, 300))
+        lg = (rng.standard_normal(V) * 3).astype(np.float32)
+        if t % 5 == 0:
+            lg[rng.integers(0, V, 4)] = lg.max()   # ties at the maximum
+        counts = rng.integers(0, 3, V).astype(np.uint32) if t % 3 == 0 else None
+        T = [0.0, 1.0, 0.7, 1.5][t % 4]
+        top_p = [1.0, 0.9, 0.5, 0.05][(t // 4) % 4]
+        pen = [1.0, 1.3][(t // 16) % 2]
+        r = float(rng.random())
+        assert orc.sample(lg, counts, T, top_p, pen, r) == _sample_reference_f32(lg, counts, T, top_p, pen, r), t
+
+
+def test_sampler_edges(orc):
+    lg = np.array([1.0, 3.0, 3.0, -2.0], np.float32)
+    assert orc.sample(lg, None, 0.0) == 2                     # greedy: the last of equal maxima
+    assert orc.sample(lg, np.array([0, 0, 1, 0], np.uint32), 0.0, penalty=2.0) == 1   # 3 / 2 < 3
+    assert orc.sample(lg, None, 1.0, top_p=1e-6, r=0.999) == 1  # nucleus of one: the first of the tied maxima
+    assert orc.sample(np.zeros(10, np.float32), None, 1.0, top_p=0.35, r=0.99) == 3   # 4 equal tokens kept
+    assert orc.sample(lg, None, 1.0, r=0.0) == 0              # the first token with mass
