@@ -457,15 +457,15 @@ constexpr int kUStS = 2 * 512;                  // A scale groups
 constexpr int kUStB = kUC * kExactBlock;        // B terms
 constexpr int kUStF = 32;                       // the 8 chunks' scale exponents of B (x / activation)
 constexpr int kUStage = kUStA + kUStS + kUStB + kUStF;
-constexpr int kUStages = 4;
-constexpr int kUAcc = 2;                        // accumulators of 4 pairs x 48 columns
-constexpr int kUAccCols = (kUC / 2) * kExactCols;
-constexpr int kUEpiWarps = 16;
-constexpr int kUThreads = 64 + 32 * kUEpiWarps;
+constexpr int kUPipes = 2;                      // independent copy / MMA / epilogue pipelines per CTA
+constexpr int kUStages = 3;                     // stages per pipeline
+constexpr int kUAccCols = (kUC / 2) * kExactCols;   // one accumulator per pipeline: 4 pairs x 48 columns
+constexpr int kUEpiWarps = 8;                   // epilogue warps per pipeline (two per TMEM lane quadrant)
+constexpr int kUThreads = 32 * (2 * kUPipes + kUPipes * kUEpiWarps);
 constexpr int kUTmemCols = 512;
-constexpr uint32_t kUSfCol = kUAcc * kUAccCols; // unit block scales: A at +0, B at +4
+constexpr uint32_t kUSfCol = kUPipes * kUAccCols;   // unit block scales: pipeline p's A at +8p, B at +8p+4
 constexpr int kUMaxSlots = 16;
-static_assert(kUSfCol + 8 <= kUTmemCols, "tensor memory budget");
+static_assert(kUSfCol + 8 * kUPipes <= kUTmemCols, "tensor memory budget");
 static_assert(kUStage % 16 == 0, "bulk-copy alignment");
 
 __host__ __device__ __forceinline__ int64_t ex_slab_off(int s) { return (int64_t)s * (16 * 2048 + 4 * 512); }
@@ -502,17 +502,21 @@ struct UnitCursor {
 };
 
 // phase 0: gate/up (rows < 64 of a tile gate, >= 64 up; the last run of an item writes the
-// activation terms); phase 1: down (the last run writes the slot's output rows).  A CTA's
-// consecutive units of one item form a run: the epilogue warps accumulate the run in registers and
-// write one f64 partial per row at the run's first unit; the item's reducer finds the runs again
-// from the CTA ranges.  xres (gate/up): x's B terms stay in shared memory for the whole kernel.
+// activation terms); phase 1: down (the last run writes the slot's output rows).  Each CTA runs
+// kUPipes independent pipelines, each over its own contiguous range of units (a "virtual CTA":
+// the grid's unit sequence is cut into kUPipes x gridDim.x equal ranges).  A pipeline's
+// consecutive units of one item form a run: its epilogue warps accumulate the run in registers
+// and write one f64 partial per row at the run's first unit; the item's reducer finds the runs
+// again from the range boundaries.  xres (gate/up): x's B terms stay in shared memory for the
+// whole kernel, shared by the pipelines.
 template <int PHASE>
 __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_constant__ ExactMoeArgs a, int xres) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ __align__(8) uint64_t full[kUStages], empty[kUStages], acc_full[kUAcc], acc_empty[kUAcc], xb_full;
+  __shared__ __align__(8) uint64_t full[kUPipes][kUStages], empty[kUPipes][kUStages], acc_full[kUPipes],
+      acc_empty[kUPipes], xb_full;
   __shared__ uint32_t tmem_base;
-  __shared__ int s_slot[kUMaxSlots], s_exp[kUMaxSlots], s_n, s_abort, s_last;
-  __shared__ double red[2][kUC / 2][128];
+  __shared__ int s_slot[kUMaxSlots], s_exp[kUMaxSlots], s_n, s_abort, s_last[kUPipes];
+  __shared__ double red[kUPipes][2][2][128];
   __shared__ __align__(16) uint8_t sf_one[512];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kc = PHASE ? a.I / 32 : a.H / 32;
@@ -526,13 +530,13 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
 
   // barriers and the unit scales do not depend on the previous kernel
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kUStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1 + kUEpiWarps);   // the MMA commit and every epilogue warp (stage bytes read)
-    }
-    for (int q = 0; q < kUAcc; ++q) {
-      mbar_init(&acc_full[q], 1);
-      mbar_init(&acc_empty[q], kUEpiWarps);
+    for (int p = 0; p < kUPipes; ++p) {
+      for (int s = 0; s < kUStages; ++s) {
+        mbar_init(&full[p][s], 1);
+        mbar_init(&empty[p][s], 1 + kUEpiWarps);   // the MMA commit and every epilogue warp (stage bytes read)
+      }
+      mbar_init(&acc_full[p], 1);
+      mbar_init(&acc_empty[p], kUEpiWarps);
     }
     mbar_init(&xb_full, 1);
     fence_mbar_init();
@@ -543,7 +547,7 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
   pdl_launch_dependents();
   // all of tensor memory, taken only after the previous kernel has finished (so a kernel of the
   // same kind launched ahead of time never waits on a CTA that is waiting on it)
-  if (warp == 1) {
+  if (warp == 2) {
     umma::tmem_alloc(&tmem_base, kUTmemCols);
     umma::tmem_relinquish();
   }
@@ -563,21 +567,23 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tb = tmem_base;
-  const int U = s_n * tiles * nu, G = (int)gridDim.x;
+  const int U = s_n * tiles * nu, G = (int)gridDim.x * kUPipes;
   auto range_lo = [&](int b) { return (int)((int64_t)b * U / G); };
-  const int q0 = range_lo(blockIdx.x), q1 = range_lo(blockIdx.x + 1);
   const uint8_t* bt = PHASE ? a.abt : a.xbt;
   const int64_t bt_stride = PHASE ? (int64_t)kc * kExactBlock : 0;
   const int* fe_src = PHASE ? a.afe : a.xfe;
   const int64_t fe_stride = PHASE ? (int64_t)((kc + 7) & ~7) : 0;
-  uint8_t* xb_s = smem + (size_t)kUStages * kUStage;   // xres: [kc][kExactBlock] terms, then kc exponents
+  uint8_t* xb_s = smem + (size_t)kUPipes * kUStages * kUStage;   // xres: [kc][kExactBlock] terms, then exponents
   const int* xfe_s = reinterpret_cast<const int*>(xb_s + (size_t)kc * kExactBlock);
+  const bool any = U > 0;
 
-  if (warp == 0) {
-    // ---------------- producer ----------------
+  if (warp < kUPipes) {
+    // ---------------- producer of pipeline `warp` ----------------
+    const int pp = warp;
+    const int q0 = range_lo(kUPipes * blockIdx.x + pp), q1 = range_lo(kUPipes * blockIdx.x + pp + 1);
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
-      if (xres && q1 > q0) {
+      if (xres && pp == 0 && any) {
         const uint32_t fb = (uint32_t)((kc + 7) & ~7) * 4u;
         mbar_expect_tx(&xb_full, (uint32_t)kc * kExactBlock + fb);
         bulk_g2s(xb_s, bt, (uint32_t)kc * kExactBlock, &xb_full);
@@ -590,35 +596,38 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
         if (*reinterpret_cast<volatile int*>(&s_abort)) break;
         const int c0 = C.u * kUC, n = min(kUC, kc - c0);
         const int s = j % kUStages, use = j / kUStages;
-        if (use > 0 && !mbar_wait(&empty[s], (uint32_t)((use - 1) & 1), err, EF_TIMEOUT_EMPTY)) {
+        if (use > 0 && !mbar_wait(&empty[pp][s], (uint32_t)((use - 1) & 1), err, EF_TIMEOUT_EMPTY)) {
           s_abort = 1;
           break;
         }
         const int k = s_slot[C.i], e = s_exp[C.i];
         const int slab = c0 >> 4, sl0 = slab * 16, nch = min(16, kc - sl0);
         const uint8_t* sb = wbase + ((int64_t)e * tiles + C.mt) * tile_bytes + ex_slab_off(slab);
-        uint8_t* st = smem + (size_t)s * kUStage;
+        uint8_t* st = smem + (size_t)(pp * kUStages + s) * kUStage;
         const uint32_t sbytes = n > 4 ? 1024u : 512u;   // one or two scale groups
         const uint32_t bytes = (uint32_t)n * 2048u + sbytes + (xres ? 0u : (uint32_t)n * kExactBlock + 32u);
-        mbar_expect_tx(&full[s], bytes);
-        bulk_g2s_stream(st, sb + (int64_t)(c0 - sl0) * 2048, (uint32_t)n * 2048u, &full[s], pol);
-        bulk_g2s_stream(st + kUStA, sb + (int64_t)nch * 2048 + ((c0 - sl0) >> 2) * 512, sbytes, &full[s], pol);
+        mbar_expect_tx(&full[pp][s], bytes);
+        bulk_g2s_stream(st, sb + (int64_t)(c0 - sl0) * 2048, (uint32_t)n * 2048u, &full[pp][s], pol);
+        bulk_g2s_stream(st + kUStA, sb + (int64_t)nch * 2048 + ((c0 - sl0) >> 2) * 512, sbytes, &full[pp][s], pol);
         if (!xres) {
           bulk_g2s(st + kUStA + kUStS, bt + (int64_t)k * bt_stride + (int64_t)c0 * kExactBlock,
-                   (uint32_t)n * kExactBlock, &full[s]);
-          bulk_g2s(st + kUStA + kUStS + kUStB, fe_src + (int64_t)k * fe_stride + c0, 32u, &full[s]);
+                   (uint32_t)n * kExactBlock, &full[pp][s]);
+          bulk_g2s(st + kUStA + kUStS + kUStB, fe_src + (int64_t)k * fe_stride + c0, 32u, &full[pp][s]);
         }
       }
       // no copy may still be landing in shared memory when the CTA exits
       for (int q = max(0, j - kUStages); q < j; ++q)
-        mbar_wait(&full[q % kUStages], (uint32_t)((q / kUStages) & 1), err, EF_TIMEOUT_FULL);
-      if (xres && q1 > q0) mbar_wait(&xb_full, 0u, err, EF_TIMEOUT_FULL);
+        mbar_wait(&full[pp][q % kUStages], (uint32_t)((q / kUStages) & 1), err, EF_TIMEOUT_FULL);
+      if (xres && pp == 0 && any) mbar_wait(&xb_full, 0u, err, EF_TIMEOUT_FULL);
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp < 2 * kUPipes) {
+    // ---------------- MMA issuer of pipeline `warp - kUPipes` ----------------
+    const int pp = warp - kUPipes;
+    const int q0 = range_lo(kUPipes * blockIdx.x + pp), q1 = range_lo(kUPipes * blockIdx.x + pp + 1);
     if (lane == 0) {
-      umma::cp_sf_group(tb + kUSfCol, sf_one);
-      umma::cp_sf_group(tb + kUSfCol + 4, sf_one);
+      const uint32_t sfa = tb + kUSfCol + 8u * pp, sfb = sfa + 4u;
+      umma::cp_sf_group(sfa, sf_one);
+      umma::cp_sf_group(sfb, sf_one);
       constexpr uint32_t idesc = umma::idesc_mxf4(128, kExactCols, 0, 0);
       if (xres && q1 > q0 && !mbar_wait(&xb_full, 0u, err, EF_TIMEOUT_FULL)) s_abort = 1;
       UnitCursor C;
@@ -627,111 +636,120 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
       for (int q = q0; q < q1; ++q, ++j, C.next(nu, tiles)) {
         if (*reinterpret_cast<volatile int*>(&s_abort)) break;
         const int n = min(kUC, kc - C.u * kUC);
-        const int s = j % kUStages, acc = j % kUAcc;
-        if (!mbar_wait(&full[s], (uint32_t)((j / kUStages) & 1), err, EF_TIMEOUT_FULL)) {
+        const int s = j % kUStages;
+        if (!mbar_wait(&full[pp][s], (uint32_t)((j / kUStages) & 1), err, EF_TIMEOUT_FULL)) {
           s_abort = 1;
           break;
         }
-        if (j >= kUAcc && !mbar_wait(&acc_empty[acc], (uint32_t)(((j / kUAcc) - 1) & 1), err, EF_TIMEOUT_EMPTY)) {
+        if (j >= 1 && !mbar_wait(&acc_empty[pp], (uint32_t)((j - 1) & 1), err, EF_TIMEOUT_EMPTY)) {
           s_abort = 1;
           break;
         }
         umma::fence_after_sync();
-        const uint8_t* st = smem + (size_t)s * kUStage;
+        const uint8_t* st = smem + (size_t)(pp * kUStages + s) * kUStage;
         const uint8_t* bsrc = xres ? xb_s + (size_t)C.u * kUC * kExactBlock : st + kUStA + kUStS;
         const uint64_t ad0 = umma::smem_desc(st, 2048, 128), bd0 = umma::smem_desc(bsrc, kExactBlock, 128);
         for (int p = 0; p < n / 2; ++p)   // descriptor start addresses in 16-byte units
-          umma::mma_mxf4(tb + (uint32_t)(acc * kUAccCols + p * kExactCols), ad0 + (uint64_t)(p * 4096 / 16),
-                         bd0 + (uint64_t)(p * 2 * kExactBlock / 16), idesc, tb + kUSfCol, tb + kUSfCol + 4, false);
-        umma::commit(&empty[s]);
-        umma::commit(&acc_full[acc]);
+          umma::mma_mxf4(tb + (uint32_t)(pp * kUAccCols + p * kExactCols), ad0 + (uint64_t)(p * 4096 / 16),
+                         bd0 + (uint64_t)(p * 2 * kExactBlock / 16), idesc, sfa, sfb, false);
+        umma::commit(&empty[pp][s]);
+        umma::commit(&acc_full[pp]);
       }
     }
   } else {
-    // ---------------- epilogue ----------------
-    const int ew = warp - 2, quad = warp & 3, pr = ew >> 2;   // this warp's TMEM lane quadrant and chunk pair
+    // ---------------- epilogue of pipeline (warp - 2 kUPipes) / kUEpiWarps ----------------
+    const int ew = warp - 2 * kUPipes, pp = ew / kUEpiWarps, le = ew % kUEpiWarps;
+    const int quad = warp & 3, pg = le >> 2;   // TMEM lane quadrant; chunk pairs 2 pg, 2 pg + 1
     const int row = 32 * quad + lane;
+    const int q0 = range_lo(kUPipes * blockIdx.x + pp), q1 = range_lo(kUPipes * blockIdx.x + pp + 1);
     UnitCursor C;
     C.init(q0, nu, tiles);
     int j = 0, run = 0, run_u0 = C.u, rp = 0;
     double racc = 0.0;
     if (xres && q1 > q0) mbar_wait_sleep(&xb_full, 0u, err, EF_TIMEOUT_FULL, 64);   // the resident scale exponents
     for (int q = q0; q < q1; ++q, ++j, C.next(nu, tiles)) {
-      const int s = j % kUStages, acc = j % kUAcc;
+      const int s = j % kUStages;
       const int n = min(kUC, kc - C.u * kUC);
-      const bool live = 2 * pr < n;
-      bool ok = mbar_wait_sleep(&acc_full[acc], (uint32_t)((j / kUAcc) & 1), err, EF_TIMEOUT_FULL, 64);
-      ok = ok && mbar_wait(&full[s], (uint32_t)((j / kUStages) & 1), err, EF_TIMEOUT_FULL);
+      bool ok = mbar_wait_sleep(&acc_full[pp], (uint32_t)(j & 1), err, EF_TIMEOUT_FULL, 64);
+      ok = ok && mbar_wait(&full[pp][s], (uint32_t)((j / kUStages) & 1), err, EF_TIMEOUT_FULL);
       ok = __all_sync(0xffffffffu, ok);   // the accumulator loads below are warp-collective
       umma::fence_after_sync();
-      float v[48];
-      if (live && ok) {
-        const uint32_t ta = tb + ((uint32_t)(32 * quad) << 16) + (uint32_t)(acc * kUAccCols + pr * kExactCols);
-        float* v0 = v;
-        umma::ld_32x32b_x32(ta, *reinterpret_cast<float(*)[32]>(v0));
-        umma::ld_32x32b_x16(ta + 32, *reinterpret_cast<float(*)[16]>(v0 + 32));
-      } else {
+      const uint8_t* st = smem + (size_t)(pp * kUStages + s) * kUStage;
+      uint32_t ews[4], fes[4];
 #pragma unroll
-        for (int i = 0; i < 48; ++i) v[i] = 0.f;
-      }
-      umma::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
-      const uint8_t* st = smem + (size_t)s * kUStage;
-      uint32_t ews[2], fes[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int jc = 2 * pr + h;   // chunk within the unit: scale group jc / 4, byte jc % 4
+      for (int h = 0; h < 4; ++h) {
+        const int jc = 4 * pg + h;   // chunk within the unit: scale group jc / 4, byte jc % 4
         ews[h] = st[kUStA + (jc >> 2) * 512 + 16 * (row & 31) + 4 * (row >> 5) + (jc & 3)];
         fes[h] = (uint32_t)(xres ? xfe_s[C.u * kUC + jc] : reinterpret_cast<const int*>(st + kUStA + kUStS + kUStB)[jc]);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      if (live) {
+      if (lane == 0) mbar_arrive(&empty[pp][s]);
+      // the warp's two chunk pairs, one at a time: 48 accumulator columns each (chunk h of the
+      // pair: its 19 digit dots at columns h * 24 + t); the accumulator is released after the
+      // second pair's load
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int pr = 2 * pg + h2;
+        float v[48];
+        if (2 * pr < n && ok) {
+          const uint32_t ta = tb + ((uint32_t)(32 * quad) << 16) + (uint32_t)(pp * kUAccCols + pr * kExactCols);
+          umma::ld_32x32b_x32(ta, *reinterpret_cast<float(*)[32]>(&v[0]));
+          umma::ld_32x32b_x16(ta + 32, *reinterpret_cast<float(*)[16]>(&v[32]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 48; ++i) v[i] = 0.f;
+        }
+        if (h2 == 1) {
+          umma::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[pp]);
+        }
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          // chunk h of the pair: its 19 digit dots at columns h * 24 + t
+          if (2 * pr + h < n) {
+            const float* vv = &v[h * 24];
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int t0 = 5 * g, t1 = min(kExactDigits, t0 + 5);
-            float f = v[h * 24 + t1 - 1];
+            for (int g = 0; g < 4; ++g) {
+              const int t0 = 5 * g, t1 = min(kExactDigits, t0 + 5);
+              float f = vv[t1 - 1];
 #pragma unroll
-            for (int t = t1 - 2; t >= t0; --t) f = fmaf(f, 8.0f, v[h * 24 + t]);   // exact: halves below 2^23
-            const double sc = __hiloint2double((int)((ews[h] + fes[h] + 15u * g) << 20), 0);
-            racc = fma((double)f, sc, racc);
+              for (int t = t1 - 2; t >= t0; --t) f = fmaf(f, 8.0f, vv[t]);   // exact: halves below 2^23
+              const double sc = __hiloint2double((int)((ews[2 * h2 + h] + fes[2 * h2 + h] + 15u * g) << 20), 0);
+              racc = fma((double)f, sc, racc);
+            }
           }
         }
       }
       ++run;
       const bool run_end = q + 1 == q1 || C.u + 1 == nu;   // the next unit starts another item
       if (!run_end) continue;
-      // ---- the run's partial: the four pair warps of each row summed, written at the run's first unit ----
+      // ---- the run's partial: the two pair-group warps of each row summed, written at the run's first unit ----
       const int k = s_slot[C.i], e = s_exp[C.i], mt = C.mt;
-      red[rp][pr][row] = racc;
+      red[pp][rp][pg][row] = racc;
       racc = 0.0;
-      named_bar(1, 32 * kUEpiWarps);
+      named_bar(1 + pp, 32 * kUEpiWarps);
       const int nrun = run, u_start = run_u0;
       run = 0;
-      run_u0 = 0;   // a later run of this CTA starts an item at unit 0
+      run_u0 = 0;   // a later run of this pipeline starts an item at unit 0
       const int rb = rp;
       rp ^= 1;
-      if (pr != 0) continue;
-      const double t = ((red[rb][0][row] + red[rb][1][row]) + red[rb][2][row]) + red[rb][3][row];
+      if (pg != 0) continue;
+      const double t = red[pp][rb][0][row] + red[pp][rb][1][row];
       double* pk = part + (size_t)k * nu * rows_out;
       pk[(size_t)u_start * rows_out + (size_t)mt * 128 + row] = t;
-      named_bar(2, 128);
-      if (ew == 0 && lane == 0) {
+      named_bar(3 + pp, 128);
+      if (le == 0 && lane == 0) {
         __threadfence();   // the run's partials (ordered before by the barrier), then the count
         uint32_t* cnt = a.cnt + (PHASE ? (size_t)a.K * a.gu_tiles : 0) + (size_t)k * tiles + mt;
-        s_last = atomicAdd(cnt, (uint32_t)nrun) + (uint32_t)nrun == (uint32_t)nu ? 1 : 0;
-        if (s_last) {
+        s_last[pp] = atomicAdd(cnt, (uint32_t)nrun) + (uint32_t)nrun == (uint32_t)nu ? 1 : 0;
+        if (s_last[pp]) {
           *cnt = 0u;
           __threadfence();
         }
       }
-      named_bar(2, 128);
-      if (!s_last) continue;
-      // ---- the item's reduction: its runs in CTA order (the CTA ranges cut the unit sequence) ----
+      named_bar(3 + pp, 128);
+      if (!s_last[pp]) continue;
+      // ---- the item's reduction: its runs in range order (the ranges cut the unit sequence) ----
       const int A0 = (C.i * tiles + mt) * nu;   // the item's first unit
       int bnext = max(0, (int)((int64_t)A0 * G / (U > 0 ? U : 1)) - 1);
       // up to 8 run starts at a time, so their loads are in flight together
@@ -797,7 +815,7 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
   }
   umma::fence_before_sync();
   __syncthreads();
-  if (warp == 1) umma::tmem_dealloc(tb, kUTmemCols);
+  if (warp == 2) umma::tmem_dealloc(tb, kUTmemCols);
 }
 
 // ============================ experts (K-quant native blocks) ============================
@@ -992,9 +1010,9 @@ cudaError_t launch_exact_moe(const DevCtx& c, const ExactMoeArgs& a0, cudaStream
     auto kern = ph ? exact_tc_kernel<1> : exact_tc_kernel<0>;
     // gate/up keeps x's B terms resident in shared memory when they fit beside the stages
     const int kc = ph ? a.I / 32 : a.H / 32;
-    const size_t stages = (size_t)kUStages * kUStage;
+    const size_t stages = (size_t)kUPipes * kUStages * kUStage;
     const size_t xb = (size_t)kc * kExactBlock + (size_t)((kc + 7) & ~7) * 4;
-    const int xres = (ph == 0 && stages + xb <= 200 * 1024) ? 1 : 0;
+    const int xres = (ph == 0 && stages + xb <= 210 * 1024) ? 1 : 0;
     const size_t smem = stages + (xres ? xb : 0);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
