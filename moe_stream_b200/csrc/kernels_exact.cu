@@ -441,29 +441,31 @@ cudaError_t launch_exact_attn_hd(const AttnArgs& a, const DevCtx& c, int rep, in
 
 // ============================ experts (MXFP4 tiles on tcgen05) ============================
 // The expert rows are the packed MXFP4 tiles of the tensor-core path (128 rows; slabs of 16 chunk
-// columns, codes then 512-byte scale groups).  A unit is half a slab of one (slot, tile) item: 8
-// chunk columns (the last unit of a row may hold fewer) and their two scale groups.  Per K = 64
-// pair of chunks the tensor core computes, with every block scale set to 1,
+// columns, codes then 512-byte scale groups).  A unit is one K-word of one (slot, tile) item: 4
+// chunk columns (the last unit of a row may hold 2) and their scale group.  Per K = 64 pair of
+// chunks the tensor core computes, with every block scale set to 1,
 // D[row][parity * 24 + t] = sum over the 32 elements of the pair's chunk `parity` of
 // e2m1(w) * term_t(x) -- multiples of 1/2 below 2^10, exact in f32.  The epilogue folds 5 base-8
 // digits at a time in f32 (still exact: below 2^23 halves), applies 2^(E_w - 127 - F + 15 g) and
-// accumulates in f64.  Warp roles: warp 0 streams units with 1-D bulk copies, warp 1 owns tensor
-// memory and issues the MMAs (one elected thread), warps 2-17 drain the accumulators (four warps per
-// TMEM lane quadrant, one chunk pair each).  The units of all (slot, tile) items are cut into equal
-// contiguous ranges, one per CTA; the last CTA to finish an item reduces the items' partials.
-constexpr int kUC = 8;                          // chunk columns per unit
+// accumulates in f64.  A CTA runs two independent pipelines, each with its own warps: a producer
+// (1-D bulk copies into 4 stages), an MMA issuer (one elected thread; two accumulators of 96 TMEM
+// columns, so a unit's MMAs overlap the previous unit's drain) and 8 epilogue warps (two per TMEM
+// lane quadrant, one chunk pair each).  The units of all (slot, tile) items are cut into equal
+// contiguous ranges, one per pipeline; the last run of an item reduces the item's partials.
+constexpr int kUC = 4;                          // chunk columns per unit (one K-word, one scale group)
 constexpr int kUStA = kUC * 2048;               // A codes
-constexpr int kUStS = 2 * 512;                  // A scale groups
+constexpr int kUStS = 512;                      // A scale group
 constexpr int kUStB = kUC * kExactBlock;        // B terms
-constexpr int kUStF = 32;                       // the 8 chunks' scale exponents of B (x / activation)
+constexpr int kUStF = 16;                       // the 4 chunks' scale exponents of B (x / activation)
 constexpr int kUStage = kUStA + kUStS + kUStB + kUStF;
 constexpr int kUPipes = 2;                      // independent copy / MMA / epilogue pipelines per CTA
-constexpr int kUStages = 3;                     // stages per pipeline
-constexpr int kUAccCols = (kUC / 2) * kExactCols;   // one accumulator per pipeline: 4 pairs x 48 columns
+constexpr int kUStages = 4;                     // stages per pipeline
+constexpr int kUAcc = 2;                        // accumulators per pipeline (double-buffered)
+constexpr int kUAccCols = (kUC / 2) * kExactCols;   // one accumulator: 2 pairs x 48 columns
 constexpr int kUEpiWarps = 8;                   // epilogue warps per pipeline (two per TMEM lane quadrant)
 constexpr int kUThreads = 32 * (2 * kUPipes + kUPipes * kUEpiWarps);
 constexpr int kUTmemCols = 512;
-constexpr uint32_t kUSfCol = kUPipes * kUAccCols;   // unit block scales: pipeline p's A at +8p, B at +8p+4
+constexpr uint32_t kUSfCol = kUPipes * kUAcc * kUAccCols;   // unit block scales: pipeline p's A at +8p, B at +8p+4
 constexpr int kUMaxSlots = 16;
 static_assert(kUSfCol + 8 * kUPipes <= kUTmemCols, "tensor memory budget");
 static_assert(kUStage % 16 == 0, "bulk-copy alignment");
@@ -512,8 +514,8 @@ struct UnitCursor {
 template <int PHASE>
 __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_constant__ ExactMoeArgs a, int xres) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ __align__(8) uint64_t full[kUPipes][kUStages], empty[kUPipes][kUStages], acc_full[kUPipes],
-      acc_empty[kUPipes], xb_full;
+  __shared__ __align__(8) uint64_t full[kUPipes][kUStages], empty[kUPipes][kUStages], acc_full[kUPipes][kUAcc],
+      acc_empty[kUPipes][kUAcc], xb_full;
   __shared__ uint32_t tmem_base;
   __shared__ int s_slot[kUMaxSlots], s_exp[kUMaxSlots], s_n, s_abort, s_last[kUPipes];
   __shared__ double red[kUPipes][2][2][128];
@@ -535,8 +537,10 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
         mbar_init(&full[p][s], 1);
         mbar_init(&empty[p][s], 1 + kUEpiWarps);   // the MMA commit and every epilogue warp (stage bytes read)
       }
-      mbar_init(&acc_full[p], 1);
-      mbar_init(&acc_empty[p], kUEpiWarps);
+      for (int q = 0; q < kUAcc; ++q) {
+        mbar_init(&acc_full[p][q], 1);
+        mbar_init(&acc_empty[p][q], kUEpiWarps);
+      }
     }
     mbar_init(&xb_full, 1);
     fence_mbar_init();
@@ -604,15 +608,15 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
         const int slab = c0 >> 4, sl0 = slab * 16, nch = min(16, kc - sl0);
         const uint8_t* sb = wbase + ((int64_t)e * tiles + C.mt) * tile_bytes + ex_slab_off(slab);
         uint8_t* st = smem + (size_t)(pp * kUStages + s) * kUStage;
-        const uint32_t sbytes = n > 4 ? 1024u : 512u;   // one or two scale groups
-        const uint32_t bytes = (uint32_t)n * 2048u + sbytes + (xres ? 0u : (uint32_t)n * kExactBlock + 32u);
+        const uint32_t sbytes = 512u;   // the unit's scale group
+        const uint32_t bytes = (uint32_t)n * 2048u + sbytes + (xres ? 0u : (uint32_t)n * kExactBlock + 16u);
         mbar_expect_tx(&full[pp][s], bytes);
         bulk_g2s_stream(st, sb + (int64_t)(c0 - sl0) * 2048, (uint32_t)n * 2048u, &full[pp][s], pol);
         bulk_g2s_stream(st + kUStA, sb + (int64_t)nch * 2048 + ((c0 - sl0) >> 2) * 512, sbytes, &full[pp][s], pol);
         if (!xres) {
           bulk_g2s(st + kUStA + kUStS, bt + (int64_t)k * bt_stride + (int64_t)c0 * kExactBlock,
                    (uint32_t)n * kExactBlock, &full[pp][s]);
-          bulk_g2s(st + kUStA + kUStS + kUStB, fe_src + (int64_t)k * fe_stride + c0, 32u, &full[pp][s]);
+          bulk_g2s(st + kUStA + kUStS + kUStB, fe_src + (int64_t)k * fe_stride + c0, 16u, &full[pp][s]);
         }
       }
       // no copy may still be landing in shared memory when the CTA exits
@@ -636,12 +640,13 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
       for (int q = q0; q < q1; ++q, ++j, C.next(nu, tiles)) {
         if (*reinterpret_cast<volatile int*>(&s_abort)) break;
         const int n = min(kUC, kc - C.u * kUC);
-        const int s = j % kUStages;
+        const int s = j % kUStages, acc = j % kUAcc;
         if (!mbar_wait(&full[pp][s], (uint32_t)((j / kUStages) & 1), err, EF_TIMEOUT_FULL)) {
           s_abort = 1;
           break;
         }
-        if (j >= 1 && !mbar_wait(&acc_empty[pp], (uint32_t)((j - 1) & 1), err, EF_TIMEOUT_EMPTY)) {
+        if (j >= kUAcc &&
+            !mbar_wait(&acc_empty[pp][acc], (uint32_t)(((j / kUAcc) - 1) & 1), err, EF_TIMEOUT_EMPTY)) {
           s_abort = 1;
           break;
         }
@@ -650,16 +655,17 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
         const uint8_t* bsrc = xres ? xb_s + (size_t)C.u * kUC * kExactBlock : st + kUStA + kUStS;
         const uint64_t ad0 = umma::smem_desc(st, 2048, 128), bd0 = umma::smem_desc(bsrc, kExactBlock, 128);
         for (int p = 0; p < n / 2; ++p)   // descriptor start addresses in 16-byte units
-          umma::mma_mxf4(tb + (uint32_t)(pp * kUAccCols + p * kExactCols), ad0 + (uint64_t)(p * 4096 / 16),
-                         bd0 + (uint64_t)(p * 2 * kExactBlock / 16), idesc, sfa, sfb, false);
+          umma::mma_mxf4(tb + (uint32_t)((pp * kUAcc + acc) * kUAccCols + p * kExactCols),
+                         ad0 + (uint64_t)(p * 4096 / 16), bd0 + (uint64_t)(p * 2 * kExactBlock / 16), idesc, sfa, sfb,
+                         false);
         umma::commit(&empty[pp][s]);
-        umma::commit(&acc_full[pp]);
+        umma::commit(&acc_full[pp][acc]);
       }
     }
   } else {
     // ---------------- epilogue of pipeline (warp - 2 kUPipes) / kUEpiWarps ----------------
     const int ew = warp - 2 * kUPipes, pp = ew / kUEpiWarps, le = ew % kUEpiWarps;
-    const int quad = warp & 3, pg = le >> 2;   // TMEM lane quadrant; chunk pairs 2 pg, 2 pg + 1
+    const int quad = warp & 3, pg = le >> 2;   // TMEM lane quadrant; chunk pair pg
     const int row = 32 * quad + lane;
     const int q0 = range_lo(kUPipes * blockIdx.x + pp), q1 = range_lo(kUPipes * blockIdx.x + pp + 1);
     UnitCursor C;
@@ -668,62 +674,54 @@ __global__ void __launch_bounds__(kUThreads, 1) exact_tc_kernel(const __grid_con
     double racc = 0.0;
     if (xres && q1 > q0) mbar_wait_sleep(&xb_full, 0u, err, EF_TIMEOUT_FULL, 64);   // the resident scale exponents
     for (int q = q0; q < q1; ++q, ++j, C.next(nu, tiles)) {
-      const int s = j % kUStages;
+      const int s = j % kUStages, acc = j % kUAcc;
       const int n = min(kUC, kc - C.u * kUC);
-      bool ok = mbar_wait_sleep(&acc_full[pp], (uint32_t)(j & 1), err, EF_TIMEOUT_FULL, 64);
+      bool ok = mbar_wait_sleep(&acc_full[pp][acc], (uint32_t)((j / kUAcc) & 1), err, EF_TIMEOUT_FULL, 64);
       ok = ok && mbar_wait(&full[pp][s], (uint32_t)((j / kUStages) & 1), err, EF_TIMEOUT_FULL);
       ok = __all_sync(0xffffffffu, ok);   // the accumulator loads below are warp-collective
       umma::fence_after_sync();
       const uint8_t* st = smem + (size_t)(pp * kUStages + s) * kUStage;
-      uint32_t ews[4], fes[4];
+      uint32_t ews[2], fes[2];
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const int jc = 4 * pg + h;   // chunk within the unit: scale group jc / 4, byte jc % 4
-        ews[h] = st[kUStA + (jc >> 2) * 512 + 16 * (row & 31) + 4 * (row >> 5) + (jc & 3)];
+      for (int h = 0; h < 2; ++h) {
+        const int jc = 2 * pg + h;   // chunk within the unit: byte jc of the row's scale word
+        ews[h] = st[kUStA + 16 * (row & 31) + 4 * (row >> 5) + jc];
         fes[h] = (uint32_t)(xres ? xfe_s[C.u * kUC + jc] : reinterpret_cast<const int*>(st + kUStA + kUStS + kUStB)[jc]);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[pp][s]);
-      // the warp's two chunk pairs, one at a time: 48 accumulator columns each (chunk h of the
-      // pair: its 19 digit dots at columns h * 24 + t); the accumulator is released after the
-      // second pair's load
+      // the warp's chunk pair: 48 accumulator columns (chunk h: its 19 digit dots at h * 24 + t)
+      float v[48];
+      if (2 * pg < n && ok) {
+        const uint32_t ta = tb + ((uint32_t)(32 * quad) << 16) + (uint32_t)((pp * kUAcc + acc) * kUAccCols + pg * kExactCols);
+        umma::ld_32x32b_x32(ta, *reinterpret_cast<float(*)[32]>(&v[0]));
+        umma::ld_32x32b_x16(ta + 32, *reinterpret_cast<float(*)[16]>(&v[32]));
+      } else {
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const int pr = 2 * pg + h2;
-        float v[48];
-        if (2 * pr < n && ok) {
-          const uint32_t ta = tb + ((uint32_t)(32 * quad) << 16) + (uint32_t)(pp * kUAccCols + pr * kExactCols);
-          umma::ld_32x32b_x32(ta, *reinterpret_cast<float(*)[32]>(&v[0]));
-          umma::ld_32x32b_x16(ta + 32, *reinterpret_cast<float(*)[16]>(&v[32]));
-        } else {
+        for (int i = 0; i < 48; ++i) v[i] = 0.f;
+      }
+      umma::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[pp][acc]);
 #pragma unroll
-          for (int i = 0; i < 48; ++i) v[i] = 0.f;
-        }
-        if (h2 == 1) {
-          umma::fence_before_sync();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[pp]);
-        }
+      for (int h = 0; h < 2; ++h) {
+        if (2 * pg + h < n) {
+          const float* vv = &v[h * 24];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (2 * pr + h < n) {
-            const float* vv = &v[h * 24];
+          for (int g = 0; g < 4; ++g) {
+            const int t0 = 5 * g, t1 = min(kExactDigits, t0 + 5);
+            float f = vv[t1 - 1];
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              const int t0 = 5 * g, t1 = min(kExactDigits, t0 + 5);
-              float f = vv[t1 - 1];
-#pragma unroll
-              for (int t = t1 - 2; t >= t0; --t) f = fmaf(f, 8.0f, vv[t]);   // exact: halves below 2^23
-              const double sc = __hiloint2double((int)((ews[2 * h2 + h] + fes[2 * h2 + h] + 15u * g) << 20), 0);
-              racc = fma((double)f, sc, racc);
-            }
+            for (int t = t1 - 2; t >= t0; --t) f = fmaf(f, 8.0f, vv[t]);   // exact: halves below 2^23
+            const double sc = __hiloint2double((int)((ews[h] + fes[h] + 15u * g) << 20), 0);
+            racc = fma((double)f, sc, racc);
           }
         }
       }
       ++run;
       const bool run_end = q + 1 == q1 || C.u + 1 == nu;   // the next unit starts another item
       if (!run_end) continue;
-      // ---- the run's partial: the two pair-group warps of each row summed, written at the run's first unit ----
+      // ---- the run's partial: the two pair warps of each row summed, written at the run's first unit ----
       const int k = s_slot[C.i], e = s_exp[C.i], mt = C.mt;
       red[pp][rp][pg][row] = racc;
       racc = 0.0;
