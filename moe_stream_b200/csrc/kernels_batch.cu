@@ -41,17 +41,6 @@ __device__ __forceinline__ unsigned long long key_of(float v, int idx) {   // la
   return ((unsigned long long)b << 32) | (uint32_t)(0xffffffffu - (uint32_t)idx);
 }
 
-__device__ __forceinline__ float cta_sum(float v, float* red) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  v = warp_sum(v);
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = 0.f;
-  for (int k = 0; k < nw; ++k) t += red[k];
-  __syncthreads();
-  return t;
-}
-
 __global__ void batch_begin_kernel(BatchState* st, uint32_t* err) {
   pdl_wait_prior();
   pdl_launch_dependents();

@@ -32,17 +32,6 @@ int64_t row_bytes(int q, int64_t cols) {
 
 namespace {
 
-__device__ __forceinline__ float block_sum(float v, float* red) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  v = warp_sum(v);
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = 0.f;
-  for (int w = 0; w < nw; ++w) t += red[w];
-  return t;
-}
-
 // ============================ dequant (bit-exact) ============================
 __device__ __forceinline__ float e8m0_half(uint32_t e) {
   return e < 2 ? __uint_as_float(0x00200000u << e) : __uint_as_float((e - 1u) << 23);
@@ -145,7 +134,6 @@ __global__ void __launch_bounds__(kQThreads, 1) q8_gemv_kernel(Q8Params p) {
   float* xf = xd + ((p.cols / 32 + 3) & ~3);                                       // [cols]
   uint64_t* full = reinterpret_cast<uint64_t*>(xf + p.cols);
   uint64_t* empty = full + kQMaxStages;
-  __shared__ float red[256];
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -582,7 +570,7 @@ template <int HD, int REP, int PB, int MINB>
 __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a, uint32_t* err) {
   constexpr int DPL = HD / 32;                 // head dims per lane
   constexpr int GL = 32 / REP;                 // lanes per head after the reduce-scatter
-  extern __shared__ __align__(16) float dyn[];
+  extern __shared__ __align__(128) float dyn[];
   float* ow = dyn;                             // [kAWarps][REP][HD] per-warp outputs
   float* wsm = ow + kAWarps * REP * HD;        // [S][REP] split weights of the final merge
   __shared__ __align__(16) float qs[REP * HD];
@@ -907,7 +895,6 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
 template <int NCH>
 __global__ void __launch_bounds__(kLWarps * 32, 1) lmhead_kernel(LmHeadArgs a) {
   extern __shared__ __align__(16) float xs[];
-  __shared__ float red[kLWarps];
   __shared__ unsigned long long bestk[kLWarps];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_wait_prior();

@@ -970,18 +970,6 @@ int pick_group_stages(int stage_bytes, int gw) {
 constexpr int kRouterThreads = 256;
 constexpr int kRouterMaxE = 1024;
 
-__device__ __forceinline__ float router_block_sum(float v, float* red) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  v = warp_sum(v);
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = 0.f;
-#pragma unroll
-  for (int w = 0; w < kRouterThreads / 32; ++w) t += red[w];
-  __syncthreads();
-  return t;
-}
-
 // Top-k selection and routing weights of one token by one warp, after every logit is written.
 // Lane l holds logits l, l + 32, ... in registers (read once); ties go to the lower index, as a
 // stable descending sort does (layer.rs:2346-2403).
@@ -1067,7 +1055,6 @@ __device__ __forceinline__ void router_select(const RouterArgs& a, uint32_t* err
 // expert GEMVs' activation terms.  The last CTA to finish selects the top-k with one warp.
 __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, uint32_t* err, int row_async) {
   extern __shared__ __align__(16) float wrow[];   // [H] this expert's router row
-  __shared__ float red[kRouterThreads / 32];
   __shared__ __align__(8) uint64_t bar;
   __shared__ uint32_t last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1140,7 +1127,6 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, ui
 constexpr int kRBRows = 16;
 __global__ void __launch_bounds__(kRouterThreads) router_batch_kernel(RouterArgs a, uint32_t* err) {
   extern __shared__ __align__(16) float xs[];   // [H] normed input
-  __shared__ float red[kRouterThreads / 32];
   __shared__ uint32_t last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.y;
