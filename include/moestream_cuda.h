@@ -20,7 +20,7 @@
 extern "C" {
 #endif
 
-#define MS_ABI_VERSION 2
+#define MS_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define MS_API __attribute__((visibility("default")))
@@ -145,6 +145,9 @@ typedef struct ms_attn_layer {
   float* v_cache;
   const float* cos_t;         /* RoPE tables [max_seq][rot_dim / 2] */
   const float* sin_t;
+  int q_gate;                 /* 1 (hybrid models, layer.rs:620-635, 699-705): wqkv's first 2*heads*hd rows
+                                 (and bqkv's) hold [Q_h, gate_h] per head, and the attention output is
+                                 multiplied by sigmoid(gate) before the O projection; 0 otherwise */
 } ms_attn_layer;
 
 /* h += O(SDPA(RoPE(QKV(RMSNorm(h))))) for one token at position pos, appending its K/V to the

@@ -41,7 +41,8 @@ class AttnLayer(C.Structure):
                 ("rot_dim", C.c_int), ("eps", C.c_float), ("window", C.c_int), ("cap", C.c_int),
                 ("attn_norm", C.c_void_p), ("wqkv", C.c_void_p), ("bqkv", C.c_void_p), ("wo", C.c_void_p),
                 ("bo", C.c_void_p), ("sinks", C.c_void_p), ("q_norm", C.c_void_p), ("k_norm", C.c_void_p),
-                ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("cos_t", C.c_void_p), ("sin_t", C.c_void_p)]
+                ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("cos_t", C.c_void_p), ("sin_t", C.c_void_p),
+                ("q_gate", C.c_int)]
 
 
 class DeltaNetLayer(C.Structure):

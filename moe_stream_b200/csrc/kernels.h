@@ -35,6 +35,10 @@ cudaError_t launch_rms_norm(const DevCtx& c, const float* x, const float* w, flo
                             cudaStream_t s);
 // RoPE (NeoX half-rotation of the first rot dims) of x [n_tok][heads][hd] with per-token tables
 // cos/sin [n_tok][rot/2] -> y (y must not overlap x)
+// gated attention of hybrid models (layer.rs:620-635, 699-705): y [2 Dq + 2 Dkv] with [Q_h, gate_h]
+// per head -> qkv [Dq + 2 Dkv] and gate [Dq]; then att *= sigmoid(gate) and its Q8_0 blocks
+cudaError_t launch_gate_split(const float* y, int nh, int hd, int Dkv, float* qkv, float* gate, cudaStream_t s);
+cudaError_t launch_gate_apply_q8(float* att, const float* gate, int n, int8_t* oq, float* od, cudaStream_t s);
 cudaError_t launch_rope(const float* x, const float* cs, const float* sn, float* y, int n_tok, int heads, int hd,
                         int rot, cudaStream_t s);
 // *p = v on the stream (a capturable scalar upload)

@@ -881,6 +881,44 @@ __global__ void __launch_bounds__(kAThreads, MINB) attn_decode_kernel(AttnArgs a
   if (threadIdx.x == 0) a.cnt[vh] = 0u;
 }
 
+// ============================ gated attention (hybrid models, layer.rs:620-635, 699-705) ============================
+// The Q projection of a hybrid attention layer holds [Q_h, gate_h] per head: y [2 Dq + 2 Dkv] ->
+// the plain layout qkv [Dq + 2 Dkv] (q of every head, then k, v) and gate [Dq].
+__global__ void gate_split_kernel(const float* __restrict__ y, int nh, int hd, int Dkv, float* __restrict__ qkv,
+                                  float* __restrict__ gate) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int Dq = nh * hd;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < Dq + 2 * Dkv; i += gridDim.x * blockDim.x) {
+    if (i < Dq) {
+      const int h = i / hd, d = i - h * hd;
+      qkv[i] = y[(size_t)h * 2 * hd + d];
+      gate[i] = y[(size_t)h * 2 * hd + hd + d];
+    } else {
+      qkv[i] = y[Dq + i];   // k, v follow the 2 Dq gated query rows
+    }
+  }
+}
+
+// attn *= sigmoid(gate) with sigmoid = recip(exp(-x) + 1) (ops/activation.rs:41-45), then the
+// O projection's Q8_0 activation: one thread per 32-element block
+__global__ void gate_apply_q8_kernel(float* __restrict__ att, const float* __restrict__ gate, int n,
+                                     int8_t* __restrict__ oq, float* __restrict__ od) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < n / 32; b += gridDim.x * blockDim.x) {
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      const int i = 32 * b + k;
+      const float sg = __fdiv_rn(1.0f, __fadd_rn(expcr(-gate[i]), 1.0f));
+      v[k] = __fmul_rn(att[i], sg);
+      att[i] = v[k];
+    }
+    quantize_q8_block(v, oq + 32 * b, &od[b]);
+  }
+}
+
 // ============================ LM head (f16) + argmax ============================
 // Warp per row, 16-byte streaming loads; x (after the final RMSNorm) in registers.
 constexpr int kLWarps = 8;
@@ -1154,6 +1192,17 @@ __global__ void rope_kernel(const float* __restrict__ x, const float* __restrict
     }
     y[i] = v;
   }
+}
+
+cudaError_t launch_gate_split(const float* y, int nh, int hd, int Dkv, float* qkv, float* gate, cudaStream_t s) {
+  const int n = nh * hd + 2 * Dkv;
+  return launch_pdl(gate_split_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, y, nh, hd, Dkv, qkv, gate);
+}
+
+cudaError_t launch_gate_apply_q8(float* att, const float* gate, int n, int8_t* oq, float* od, cudaStream_t s) {
+  if (n % 32) return cudaErrorInvalidValue;
+  return launch_pdl(gate_apply_q8_kernel, dim3((unsigned)((n / 32 + 127) / 128)), dim3(128), 0, s, att, gate, n, oq,
+                    od);
 }
 
 cudaError_t launch_rope(const float* x, const float* cs, const float* sn, float* y, int n_tok, int heads, int hd,

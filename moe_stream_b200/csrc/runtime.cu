@@ -1405,10 +1405,13 @@ ms_status ms_attn_layer_decode(ms_ctx* c, const ms_attn_layer* L, int pos, float
   const int spl = hd <= 64 ? 0 : 256;
   const int range = L->cap;
   const int S = spl ? (range + spl - 1) / spl : attn_splits(range, hd);
+  const int gated = L->q_gate ? 1 : 0;
   auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
   const size_t o_qkv = 0, o_att = o_qkv + up((size_t)(Dq + 2 * Dkv) * 4), o_oq = o_att + up((size_t)Dq * 4),
                o_od = o_oq + up((size_t)Dq + 64), o_part = o_od + up((size_t)Dq / 32 * 4 + 64),
-               o_pos = o_part + up((size_t)nkv * S * rep * (hd + 2) * 4), total = o_pos + 256;
+               o_pos = o_part + up((size_t)nkv * S * rep * (hd + 2) * 4), o_raw = o_pos + 256,
+               o_gate = o_raw + (gated ? up((size_t)(2 * Dq + 2 * Dkv) * 4) : 0),
+               total = o_gate + (gated ? up((size_t)Dq * 4) : 0);
   // counter words [4096, 4096 + 4 nkv + 16) are this entry point's (self-resetting)
   ms_status st = ensure_scratch(c, total, 4096 + 4 * (size_t)nkv + 16);
   if (st != MS_OK) return st;
@@ -1416,16 +1419,22 @@ ms_status ms_attn_layer_decode(ms_ctx* c, const ms_attn_layer* L, int pos, float
   int* d_pos = (int*)(base + o_pos);
   MS_CUDA(c, launch_set_i32(d_pos, pos, c->stream));
   Q8GemvArgs qa;
-  qa.w = (const uint8_t*)L->wqkv; qa.rows = Dq + 2 * Dkv; qa.cols = H; qa.x = h; qa.norm_w = L->attn_norm;
-  qa.eps = L->eps; qa.bias = L->bqkv; qa.y = (float*)(base + o_qkv);
+  qa.w = (const uint8_t*)L->wqkv; qa.rows = (gated ? 2 : 1) * Dq + 2 * Dkv; qa.cols = H; qa.x = h;
+  qa.norm_w = L->attn_norm; qa.eps = L->eps; qa.bias = L->bqkv;
+  qa.y = (float*)(base + (gated ? o_raw : o_qkv));
   MS_CUDA(c, launch_q8_gemv(c->dc, qa, c->stream));
+  if (gated)   // [Q_h, gate_h] per head -> q rows, then k, v; and the gate
+    MS_CUDA(c, launch_gate_split((const float*)(base + o_raw), nh, hd, Dkv, (float*)(base + o_qkv),
+                                 (float*)(base + o_gate), c->stream));
   AttnArgs aa;
   aa.qkv = (const float*)(base + o_qkv); aa.q_norm = L->q_norm; aa.k_norm = L->k_norm; aa.eps = L->eps;
   aa.cos_t = L->cos_t; aa.sin_t = L->sin_t; aa.rot = L->rot_dim; aa.pos = d_pos; aa.kc = L->k_cache; aa.vc = L->v_cache;
   aa.cap = L->cap; aa.window = L->window > 0 ? L->window : 0; aa.sinks = L->sinks; aa.part = (float*)(base + o_part);
   aa.cnt = c->counters + 4096; aa.out = (float*)(base + o_att); aa.nh = nh; aa.nkv = nkv; aa.hd = hd; aa.S = S;
-  aa.spl = spl; aa.scale = (float)(1.0 / std::sqrt((double)hd)); aa.oq = (int8_t*)(base + o_oq);
-  aa.od = (float*)(base + o_od);
+  aa.spl = spl; aa.scale = (float)(1.0 / std::sqrt((double)hd));
+  // the O projection's Q8_0 activation comes from the attention kernel, or after the gate
+  aa.oq = gated ? nullptr : (int8_t*)(base + o_oq);
+  aa.od = gated ? nullptr : (float*)(base + o_od);
   if (spl && rep % 4 == 0) aa.head_split = 4;
   else if (spl && rep % 2 == 0 && rep >= 4) aa.head_split = 2;
   // order-independent attention (f64 reductions rounded once) where it has a kernel
@@ -1433,8 +1442,12 @@ ms_status ms_attn_layer_decode(ms_ctx* c, const ms_attn_layer* L, int pos, float
     MS_CUDA(c, launch_exact_attention(c->dc, aa, range, c->stream));
   else
     MS_CUDA(c, launch_attention(c->dc, aa, c->stream));
+  if (gated)   // attn_out *= sigmoid(gate) (layer.rs:699-705), then its Q8_0 blocks
+    MS_CUDA(c, launch_gate_apply_q8((float*)(base + o_att), (const float*)(base + o_gate), Dq, (int8_t*)(base + o_oq),
+                                    (float*)(base + o_od), c->stream));
   Q8GemvArgs oa;
-  oa.w = (const uint8_t*)L->wo; oa.rows = H; oa.cols = Dq; oa.xq_in = aa.oq; oa.xd_in = aa.od; oa.bias = L->bo;
+  oa.w = (const uint8_t*)L->wo; oa.rows = H; oa.cols = Dq; oa.xq_in = (const int8_t*)(base + o_oq);
+  oa.xd_in = (const float*)(base + o_od); oa.bias = L->bo;
   oa.residual = h;
   MS_CUDA(c, launch_q8_gemv(c->dc, oa, c->stream));
   return MS_OK;

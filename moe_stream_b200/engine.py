@@ -129,14 +129,14 @@ class Context:
     def attn_layer_decode(self, layer: dict, pos: int, h) -> None:
         """h += attention(RMSNorm(h)) for one token at `pos` (layer.rs:511-749).  layer: ints hidden,
         heads, kv_heads, head_dim, rot_dim, window, cap, float eps and device tensors attn_norm, wqkv,
-        wo, k_cache, v_cache, cos_t, sin_t (bqkv, bo, sinks, q_norm, k_norm optional)."""
+        wo, k_cache, v_cache, cos_t, sin_t (bqkv, bo, sinks, q_norm, k_norm, q_gate optional)."""
         from ._lib import AttnLayer
         d = layer
         L = AttnLayer(d["hidden"], d["heads"], d["kv_heads"], d["head_dim"], d["rot_dim"], d["eps"],
                       d.get("window", 0), d["cap"], _ptr(d["attn_norm"]), _ptr(d["wqkv"]), _ptr(d.get("bqkv")),
                       _ptr(d["wo"]), _ptr(d.get("bo")), _ptr(d.get("sinks")), _ptr(d.get("q_norm")),
                       _ptr(d.get("k_norm")), _ptr(d["k_cache"]), _ptr(d["v_cache"]), _ptr(d["cos_t"]),
-                      _ptr(d["sin_t"]))
+                      _ptr(d["sin_t"]), int(d.get("q_gate", 0)))
         check(lib().ms_attn_layer_decode(self.h, C.byref(L), pos, _ptr(h)), self.h)
 
     def deltanet_decode(self, layer: dict, x, conv_state, rec_state, y) -> None:

@@ -717,7 +717,7 @@ void orc_rope(const float* x, const float* cs, const float* sn, int n_tok, int h
 int orc_attn_decode(const orc_attn_layer* L, float* K, float* V, int pos, float* h) {
   const int H = L->hidden, nh = L->heads, nkv = L->kv_heads, hd = L->head_dim, Dq = nh * hd, Dkv = nkv * hd;
   const int th = hw_threads();
-  std::vector<float> xn(H), q(Dq), k(Dkv), v(Dkv), attn(Dq), o(H);
+  std::vector<float> xn(H), q(Dq), k(Dkv), v(Dkv), attn(Dq), o(H), gate;
   rms_norm(h, L->attn_norm, xn.data(), 1, H, L->eps);
   auto proj = [&](const uint8_t* w, int rows, int cols, const float* x, float* y) {
     if (L->attn_mode == 1) { q8_0_gemv_actq(w, rows, cols, x, y, th); return; }
@@ -725,8 +725,21 @@ int orc_attn_decode(const orc_attn_layer* L, float* K, float* V, int pos, float*
     dequant_matrix(ORC_Q8_0, w, rows, cols, Wf.data(), th);
     matmul_xwt(x, 1, Wf.data(), rows, cols, y, th);
   };
-  proj(L->wq, Dq, H, xn.data(), q.data()); proj(L->wk, Dkv, H, xn.data(), k.data()); proj(L->wv, Dkv, H, xn.data(), v.data());
-  if (L->bq) for (int i = 0; i < Dq; ++i) q[i] += L->bq[i];
+  if (L->q_gate) {   // hybrid models: per head [Q_h, gate_h] interleaved (layer.rs:620-635)
+    std::vector<float> qg(2 * (size_t)Dq);
+    proj(L->wq, 2 * Dq, H, xn.data(), qg.data());
+    if (L->bq) for (int i = 0; i < 2 * Dq; ++i) qg[i] += L->bq[i];
+    gate.resize(Dq);
+    for (int i = 0; i < nh; ++i)
+      for (int d = 0; d < hd; ++d) {
+        q[(size_t)i * hd + d] = qg[(size_t)i * 2 * hd + d];
+        gate[(size_t)i * hd + d] = qg[(size_t)i * 2 * hd + hd + d];
+      }
+  } else {
+    proj(L->wq, Dq, H, xn.data(), q.data());
+    if (L->bq) for (int i = 0; i < Dq; ++i) q[i] += L->bq[i];
+  }
+  proj(L->wk, Dkv, H, xn.data(), k.data()); proj(L->wv, Dkv, H, xn.data(), v.data());
   if (L->bk) for (int i = 0; i < Dkv; ++i) k[i] += L->bk[i];
   if (L->bv) for (int i = 0; i < Dkv; ++i) v[i] += L->bv[i];
   if (L->q_norm && L->k_norm) {
@@ -746,6 +759,8 @@ int orc_attn_decode(const orc_attn_layer* L, float* K, float* V, int pos, float*
   }
   const float scale = (float)(1.0 / std::sqrt((double)hd));
   sdpa(q.data(), K, V, nh, nkv, 1, Lk, hd, scale, false, L->sinks, L->window, attn.data(), th);
+  if (L->q_gate)   // attn_out *= sigmoid(gate), sigmoid = recip(exp(-x) + 1) (layer.rs:699-705, activation.rs:41-45)
+    for (int i = 0; i < Dq; ++i) attn[i] = attn[i] * (1.0f / (expcr(-gate[i]) + 1.0f));
   proj(L->wo, H, Dq, attn.data(), o.data());
   for (int i = 0; i < H; ++i) h[i] = h[i] + (L->bo ? o[i] + L->bo[i] : o[i]);
   return 0;

@@ -89,6 +89,8 @@ typedef struct {
   const float* attn_norm;
   const uint8_t *wq, *wk, *wv, *wo;  /* Q8_0 */
   const float *bq, *bk, *bv, *bo, *sinks, *q_norm, *k_norm;   /* or NULL */
+  int q_gate;                        /* 1: wq rows (and bq) hold [Q_h, gate_h] per head (hybrid models,
+                                        layer.rs:620-635); the output is multiplied by sigmoid(gate) */
 } orc_attn_layer;
 int orc_attn_decode(const orc_attn_layer* L, float* K, float* V, int pos, float* h);
 

@@ -37,7 +37,7 @@ class AttnLayer(C.Structure):
                 ("rot_dim", C.c_int), ("eps", C.c_float), ("rope_theta", C.c_float), ("window", C.c_int),
                 ("attn_mode", C.c_int), ("attn_norm", _fp), ("wq", _vp), ("wk", _vp), ("wv", _vp), ("wo", _vp),
                 ("bq", _fp), ("bk", _fp), ("bv", _fp), ("bo", _fp), ("sinks", _fp), ("q_norm", _fp),
-                ("k_norm", _fp)]
+                ("k_norm", _fp), ("q_gate", C.c_int)]
 
 
 class DeltaNetLayer(C.Structure):
@@ -255,7 +255,8 @@ class AttnState:
                            d["rope_theta"], d.get("window", 0), attn_mode, ptr(d["attn_norm"], True),
                            ptr(d["wq"]), ptr(d["wk"]), ptr(d["wv"]), ptr(d["wo"]), ptr(d.get("bq"), True),
                            ptr(d.get("bk"), True), ptr(d.get("bv"), True), ptr(d.get("bo"), True),
-                           ptr(d.get("sinks"), True), ptr(d.get("q_norm"), True), ptr(d.get("k_norm"), True))
+                           ptr(d.get("sinks"), True), ptr(d.get("q_norm"), True), ptr(d.get("k_norm"), True),
+                           int(d.get("q_gate", 0)))
         self.K = np.zeros((d["kv_heads"], 0, d["head_dim"]), np.float32)
         self.V = np.zeros_like(self.K)
 

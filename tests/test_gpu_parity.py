@@ -660,15 +660,17 @@ def test_rope_bit_exact(ctx, orc, heads, hd, rot, n_tok):
     assert np.array_equal(y.cpu().numpy().view(np.uint32), want.reshape(-1).view(np.uint32))
 
 
-def _attn_layer(seed, H, nh, nkv, hd, rot, window=0, sinks=False, bias=False, qk_norm=False, theta=150000.0):
+def _attn_layer(seed, H, nh, nkv, hd, rot, window=0, sinks=False, bias=False, qk_norm=False, theta=150000.0,
+                q_gate=False):
     rng = np.random.default_rng(seed)
     Dq, Dkv = nh * hd, nkv * hd
+    Dqw = 2 * Dq if q_gate else Dq   # hybrid models: [Q_h, gate_h] per head in the Q projection
     d = dict(hidden=H, heads=nh, kv_heads=nkv, head_dim=hd, rot_dim=rot, eps=1e-5, rope_theta=theta, window=window,
              attn_norm=(1 + 0.1 * rng.standard_normal(H)).astype(np.float32),
-             wq=synth.rand_q8_0(rng, Dq * H), wk=synth.rand_q8_0(rng, Dkv * H), wv=synth.rand_q8_0(rng, Dkv * H),
-             wo=synth.rand_q8_0(rng, H * Dq))
+             wq=synth.rand_q8_0(rng, Dqw * H), wk=synth.rand_q8_0(rng, Dkv * H), wv=synth.rand_q8_0(rng, Dkv * H),
+             wo=synth.rand_q8_0(rng, H * Dq), q_gate=int(q_gate))
     if bias:
-        for k, n in (("bq", Dq), ("bk", Dkv), ("bv", Dkv), ("bo", H)):
+        for k, n in (("bq", Dqw), ("bk", Dkv), ("bv", Dkv), ("bo", H)):
             d[k] = (rng.standard_normal(n) * 0.01).astype(np.float32)
     if sinks:
         d["sinks"] = rng.standard_normal(nh).astype(np.float32)
@@ -683,7 +685,9 @@ def _attn_layer(seed, H, nh, nkv, hd, rot, window=0, sinks=False, bias=False, qk
     dict(H=2880, nh=64, nkv=8, hd=64, rot=64, sinks=True, bias=True, steps=40),                 # GPT-OSS full layer
     dict(H=2048, nh=32, nkv=4, hd=128, rot=128, qk_norm=True, theta=1e6, steps=40),            # Qwen3-30B-A3B
     dict(H=2048, nh=16, nkv=2, hd=256, rot=64, qk_norm=True, theta=1e7, steps=24),             # head_dim 256, rotary 0.25
-], ids=["gpt-oss-swa", "gpt-oss-full", "qwen3", "hd256-partial-rope"])
+    dict(H=2048, nh=16, nkv=2, hd=256, rot=64, qk_norm=True, theta=1e7, q_gate=True, steps=24),  # hybrid: gated Q
+    dict(H=1024, nh=16, nkv=2, hd=64, rot=16, qk_norm=True, bias=True, q_gate=True, steps=40),   # gated, exact kernel
+], ids=["gpt-oss-swa", "gpt-oss-full", "qwen3", "hd256-partial-rope", "hybrid-gated-hd256", "gated-hd64"])
 def test_attn_layer_decode(ctx, orc, shape):
     """ms_attn_layer_decode step by step against the oracle's attention half-layer (fresh input each
     step; both keep their own K/V).  Head dims 32/64/128 run the order-independent kernel: every
@@ -707,7 +711,8 @@ def test_attn_layer_decode(ctx, orc, shape):
              cap=cap, attn_norm=dev(d["attn_norm"]), wqkv=dev(pad_rows(wqkv)), wo=dev(pad_rows(d["wo"])),
              bqkv=dev(bqkv) if bqkv is not None else None, bo=dev(d["bo"]) if "bo" in d else None,
              sinks=dev(d["sinks"]) if "sinks" in d else None, q_norm=dev(d["q_norm"]) if "q_norm" in d else None,
-             k_norm=dev(d["k_norm"]) if "k_norm" in d else None, k_cache=kc, v_cache=vc, cos_t=dev(cs), sin_t=dev(sn))
+             k_norm=dev(d["k_norm"]) if "k_norm" in d else None, k_cache=kc, v_cache=vc, cos_t=dev(cs), sin_t=dev(sn),
+             q_gate=d["q_gate"])
     rng = np.random.default_rng(5)
     exact = hd <= 128
     for pos in range(steps):
