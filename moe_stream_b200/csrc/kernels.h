@@ -302,7 +302,7 @@ int attn_split_positions(int range, int units, int sm_count);
 // decode attention for one token per sequence (AttnArgs as launch_attention; oq / od written when
 // set); `range` = the most positions a sequence can attend to (cache slots, or the window)
 cudaError_t launch_exact_attention(const DevCtx& c, const AttnArgs& a, int range, cudaStream_t s);
-int exact_attn_cluster(int range);
+int exact_attn_cluster(int range, int units, int sm_count);
 // the expert FFN of one token over packed MXFP4 tiles: f64 partial dots of gate/up rows per K
 // segment (gp), the activations as exact digits, f64 partial dots of the down rows (dp), and each
 // slot's output y = (segments summed in f64, rounded) + bias; the consumer (PendingCombine.partial

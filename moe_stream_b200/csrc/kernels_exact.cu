@@ -966,9 +966,12 @@ cudaError_t launch_pdl_x(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_
 
 }  // namespace
 
-int exact_attn_cluster(int range) {   // a power of two, so the output slices divide evenly
+// CTAs per (kv head, sequence) cluster: a power of two (the output slices divide evenly), at most
+// 16, at least 16 positions per CTA, and no more than needed for about two CTAs per SM over all
+// (kv head, sequence) units
+int exact_attn_cluster(int range, int units, int sm_count) {
   int C = 1;
-  while (C < 16 && C * 64 < range) C *= 2;
+  while (C < 16 && C * 16 < range && (long)units * C < 2L * sm_count) C *= 2;
   return C;
 }
 
@@ -977,7 +980,7 @@ cudaError_t launch_exact_attention(const DevCtx& c, const AttnArgs& a, int range
   if (a.batch > 1 && a.bs_out % 32) return cudaErrorInvalidValue;
   const int rep = a.nh / a.nkv;
   if (32 % rep) return cudaErrorInvalidValue;
-  const int C = exact_attn_cluster(range);
+  const int C = exact_attn_cluster(range, a.nkv * a.batch, c.sm_count);
   const int max_per = (range + C - 1) / C;
   switch (a.hd) {
     case 32: return launch_exact_attn_hd<32>(a, c, rep, C, max_per, s);
