@@ -20,7 +20,7 @@
 extern "C" {
 #endif
 
-#define MS_ABI_VERSION 3
+#define MS_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define MS_API __attribute__((visibility("default")))
@@ -276,6 +276,16 @@ typedef struct ms_model_config {
   int max_seq_len;      /* RoPE table and KV capacity */
   int ep_rank, ep_size; /* expert parallel placement (single GPU: 0, 1) */
   int attn_splits;      /* split-K factor of decode attention, 0 = automatic */
+  /* Gated DeltaNet hybrids (Qwen3-Next / Qwen3.5, config.rs:318-352, 446-494).  attn_interval > 0:
+   * layer l is gated attention (Q projection [Q_h, gate_h] per head, output x sigmoid(gate),
+   * layer.rs:620-635, 699-705) when (l + 1) % attn_interval == 0, else a Gated DeltaNet layer with
+   * ssm_groups key heads of ssm_state dims, ssm_dt_rank value heads of ssm_inner / ssm_dt_rank (= 128)
+   * dims and a causal conv of ssm_conv taps (tensors blk.N.attn_qkv / attn_gate / ssm_ba (or ssm_beta +
+   * ssm_alpha) / ssm_out / ssm_conv1d / ssm_a / ssm_dt.bias / ssm_norm, deltanet.rs:101-137, 204-543).
+   * 0: every layer is attention and the ssm fields are ignored.  Any model may also carry a shared
+   * expert per layer (blk.N.ffn_{gate,up,down}_shexp, ffn_gate_inp_shexp; layer.rs:910-922). */
+  int attn_interval;
+  int ssm_groups, ssm_state, ssm_dt_rank, ssm_inner, ssm_conv;
 } ms_model_config;
 
 /* Create an empty model; then ms_model_set_tensor for every tensor and ms_model_finalize. */

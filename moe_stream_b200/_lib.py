@@ -32,7 +32,9 @@ class ModelConfig(C.Structure):
                 ("kv_heads", C.c_int), ("head_dim", C.c_int), ("rot_dim", C.c_int), ("experts", C.c_int),
                 ("top_k", C.c_int), ("inter", C.c_int), ("vocab", C.c_int), ("rope_theta", C.c_float),
                 ("eps", C.c_float), ("sliding_window", C.c_int), ("norm_topk_prob", C.c_int),
-                ("max_seq_len", C.c_int), ("ep_rank", C.c_int), ("ep_size", C.c_int), ("attn_splits", C.c_int)]
+                ("max_seq_len", C.c_int), ("ep_rank", C.c_int), ("ep_size", C.c_int), ("attn_splits", C.c_int),
+                ("attn_interval", C.c_int), ("ssm_groups", C.c_int), ("ssm_state", C.c_int),
+                ("ssm_dt_rank", C.c_int), ("ssm_inner", C.c_int), ("ssm_conv", C.c_int)]
 
 
 class AttnLayer(C.Structure):

@@ -50,6 +50,9 @@ cudaError_t launch_set_i32(int* p, int v, cudaStream_t s);
 // or h[r] + dense[r] when the expert-parallel all-reduce already summed it.
 struct PendingCombine {
   const float* dense = nullptr;    // [H] summed MoE output, or null
+  // [H] or null: added to the routed experts' combined output before the residual add (the shared
+  // expert's output, layer.rs:910-922); read by the residual kernel only
+  const float* extra = nullptr;
   const float* partial = nullptr;  // [K, H] per-slot expert outputs (bias included)
   // or, from the tensor-core down projection: per-range partial sums [items][kTcMaxSeg][128] of
   // item = local slot (ascending expert) x 128-row tile, tc_splits(items, seg_kw, seg_grid) ranges each

@@ -1085,7 +1085,10 @@ __global__ void __launch_bounds__(kResidRows) resid_norm_q8_kernel(PendingCombin
   combine_prepare(pc, &co);
   __syncthreads();
   const int r = blockIdx.x * kResidRows + threadIdx.x;
-  if (r < H) h[r] = h[r] + combine_at(pc, co, H, r);
+  if (r < H) {
+    const float moe = combine_at(pc, co, H, r);
+    h[r] = h[r] + (pc.extra ? __fadd_rn(moe, pc.extra[r]) : moe);
+  }
   if (!norm_w) return;
   __syncthreads();
   if (threadIdx.x == 0) {

@@ -143,6 +143,18 @@ struct LayerW {
   uint8_t* down_tc = nullptr;
   bool have_gate = false, have_up = false, have_down = false;
   bool tc = false;
+  // Gated DeltaNet layer of a hybrid model (deltanet.rs:204-543); attention fields stay null
+  bool deltanet = false;
+  uint8_t *dn_qkv = nullptr, *dn_z = nullptr, *dn_ba = nullptr, *dn_out = nullptr;
+  int dn_qkv_q = -1, dn_z_q = -1, dn_ba_q = -1, dn_out_q = -1;
+  int dn_ba_parts = 0;              // ssm_ba, or ssm_beta + ssm_alpha
+  float *dn_conv_w = nullptr, *dn_a = nullptr, *dn_dt = nullptr, *dn_norm = nullptr;
+  float *dn_conv_state = nullptr, *dn_state = nullptr;   // [conv_dim][taps - 1], [v heads][hkd][hvd]
+  // shared expert (layer.rs:1898-1953, 2250-2293)
+  uint8_t *sh_gate = nullptr, *sh_up = nullptr, *sh_down = nullptr;
+  int sh_gate_q = -1, sh_up_q = -1, sh_down_q = -1;
+  float* sh_gate_inp = nullptr;
+  int sh_dims[3] = {0, 0, 0};       // gate rows, up rows, down cols (the shared expert's width)
 };
 
 // NCCL is resolved at run time (dlopen), so a process that already loaded libnccl (torch does)
@@ -279,6 +291,11 @@ struct ms_model {
   float* xn_final = nullptr;        // the LM head's input after the final norm [H]
   int head_start = 1;               // index of the step's first LM-head launch (profiling classes)
   int* ref_scratch = nullptr;       // exact greedy re-scoring: candidate ids, counters
+  // hybrid models: DeltaNet step scratch, gated attention's raw Q/gate projection, shared expert
+  float *dn_mixed = nullptr, *dn_conv = nullptr, *dn_zv = nullptr, *dn_bav = nullptr, *dn_o = nullptr;
+  float *q_raw = nullptr, *q_gate = nullptr;
+  float *sh_g = nullptr, *sh_u = nullptr, *sh_a = nullptr, *sh_o = nullptr, *sh_y = nullptr;
+  int sh_max = 0;                   // widest shared expert (0: none)
   struct Prefill {
     int cap = 0;                       // tokens the buffers hold
     std::vector<void*> allocs;
@@ -308,6 +325,13 @@ namespace {
 
 int q_dim(const ms_model_config& c) { return c.heads * c.head_dim; }
 int kv_dim(const ms_model_config& c) { return c.kv_heads * c.head_dim; }
+// DeltaNet hybrids (config.rs:446-458): gated attention every attn_interval-th layer, DeltaNet otherwise
+bool is_hybrid(const ms_model_config& c) { return c.attn_interval > 0; }
+bool is_attention_layer(const ms_model_config& c, int li) { return c.attn_interval <= 0 || (li + 1) % c.attn_interval == 0; }
+// rows of the Q projection: [Q_h, gate_h] per head in hybrid models (layer.rs:620-635)
+int q_rows(const ms_model_config& c) { return (is_hybrid(c) ? 2 : 1) * q_dim(c); }
+int dn_conv_dim(const ms_model_config& c) { return 2 * c.ssm_groups * c.ssm_state + c.ssm_inner; }
+int dn_hvd(const ms_model_config& c) { return c.ssm_dt_rank > 0 ? c.ssm_inner / c.ssm_dt_rank : 128; }
 
 ms_status upload(ms_model* m, void* dst, const void* src, size_t bytes) {
   cudaError_t e = cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
@@ -345,27 +369,30 @@ ms_status set_layer_tensor(ms_model* m, int li, const std::string& t, int q, con
   if (t == "attn_output.bias") return set_vec(m, &Lw.bo, nm, q, n, H, data);
   if (t == "ffn_gate_inp.bias") return set_vec(m, &Lw.router_b, nm, q, n, c.experts, data);
   if (t == "attn_q.weight" || t == "attn_k.weight" || t == "attn_v.weight") {
-    // q, k, v rows are concatenated into one [Dq + 2 Dkv, H] projection (row layout unchanged)
-    const int rows = t == "attn_q.weight" ? Dq : Dkv;
-    const int off = t == "attn_q.weight" ? 0 : (t == "attn_k.weight" ? Dq : Dq + Dkv);
+    // q, k, v rows are concatenated into one [Qr + 2 Dkv, H] projection (row layout unchanged);
+    // Qr = Dq, or 2 Dq with [Q_h, gate_h] per head in hybrid models
+    const int Qr = q_rows(c);
+    const int rows = t == "attn_q.weight" ? Qr : Dkv;
+    const int off = t == "attn_q.weight" ? 0 : (t == "attn_k.weight" ? Qr : Qr + Dkv);
     if (dims.size() != 2 || dims[0] != rows || dims[1] != H) return fail(m->ctx, MS_ERR_SHAPE, "%s: bad shape", nm);
     if (q != Q_Q8_0) return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: attention projections must be Q8_0", nm);
     if (Lw.attn_q >= 0 && Lw.attn_q != q) return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: mixed qtypes", nm);
     Lw.attn_q = q;
     const int64_t rb = row_bytes(q, H);
     if (!Lw.wqkv) {
-      ms_status s = m->alloc(&Lw.wqkv, padded((size_t)(Dq + 2 * Dkv) * rb));
+      ms_status s = m->alloc(&Lw.wqkv, padded((size_t)(Qr + 2 * Dkv) * rb));
       if (s != MS_OK) return s;
     }
     ++Lw.qkv_parts;
     return upload(m, Lw.wqkv + (size_t)off * rb, data, (size_t)rows * rb);
   }
   if (t == "attn_q.bias" || t == "attn_k.bias" || t == "attn_v.bias") {
-    const int rows = t == "attn_q.bias" ? Dq : Dkv;
-    const int off = t == "attn_q.bias" ? 0 : (t == "attn_k.bias" ? Dq : Dq + Dkv);
+    const int Qr = q_rows(c);
+    const int rows = t == "attn_q.bias" ? Qr : Dkv;
+    const int off = t == "attn_q.bias" ? 0 : (t == "attn_k.bias" ? Qr : Qr + Dkv);
     if (q != Q_F32 || n != rows) return fail(m->ctx, MS_ERR_SHAPE, "%s: bad bias", nm);
     if (!Lw.bqkv) {
-      ms_status s = m->alloc(&Lw.bqkv, (size_t)(Dq + 2 * Dkv) * 4);
+      ms_status s = m->alloc(&Lw.bqkv, (size_t)(Qr + 2 * Dkv) * 4);
       if (s != MS_OK) return s;
     }
     ++Lw.bqkv_parts;
@@ -377,6 +404,62 @@ ms_status set_layer_tensor(ms_model* m, int li, const std::string& t, int q, con
     ms_status s = m->alloc(&Lw.wo, padded(bytes));
     if (s != MS_OK) return s;
     return upload(m, Lw.wo, data, (size_t)raw_bytes(q, n));
+  }
+  // ---- Gated DeltaNet projections and tensors (deltanet.rs:101-137, 204-543) and the shared expert
+  // (layer.rs:2250-2293).  Projections run as f32-activation GEMVs over the native blocks, the
+  // reference's dequantize-then-matmul (Q8_0 would need the f32 activation too, so it is refused).
+  {
+    const int conv_dim = dn_conv_dim(c), vt = c.ssm_inner, nv = c.ssm_dt_rank;
+    struct Proj { const char* name; uint8_t** w; int* qt; int rows, cols; bool dn; };
+    const Proj projs[] = {
+        {"attn_qkv.weight", &Lw.dn_qkv, &Lw.dn_qkv_q, conv_dim, H, true},
+        {"attn_gate.weight", &Lw.dn_z, &Lw.dn_z_q, vt, H, true},
+        {"ssm_ba.weight", &Lw.dn_ba, &Lw.dn_ba_q, 2 * nv, H, true},
+        {"ssm_beta.weight", &Lw.dn_ba, &Lw.dn_ba_q, nv, H, true},
+        {"ssm_alpha.weight", &Lw.dn_ba, &Lw.dn_ba_q, nv, H, true},
+        {"ssm_out.weight", &Lw.dn_out, &Lw.dn_out_q, H, vt, true},
+        {"ffn_gate_shexp.weight", &Lw.sh_gate, &Lw.sh_gate_q, -1, H, false},
+        {"ffn_up_shexp.weight", &Lw.sh_up, &Lw.sh_up_q, -1, H, false},
+        {"ffn_down_shexp.weight", &Lw.sh_down, &Lw.sh_down_q, H, -1, false}};
+    for (const Proj& P : projs) {
+      if (t != P.name) continue;
+      if (P.dn && (!is_hybrid(c) || is_attention_layer(c, li)))
+        return fail(m->ctx, MS_ERR_STATE, "%s: layer %d is not a DeltaNet layer", nm, li);
+      if (q != Q_F32 && q != Q_Q4_K && q != Q_Q6_K && q != Q_MXFP4)
+        return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: qtype %d (F32, Q4_K, Q6_K or MXFP4 required)", nm, q);
+      if (dims.size() != 2) return fail(m->ctx, MS_ERR_SHAPE, "%s: 2-D tensor expected", nm);
+      const int rows = P.rows > 0 ? P.rows : (int)dims[0], cols = P.cols > 0 ? P.cols : (int)dims[1];
+      if (dims[0] != rows || dims[1] != cols || row_bytes(q, cols) <= 0)
+        return fail(m->ctx, MS_ERR_SHAPE, "%s: expected [%d, %d]", nm, rows, cols);
+      const int64_t rb = row_bytes(q, cols);
+      const bool split_ba = t == "ssm_beta.weight" || t == "ssm_alpha.weight";
+      if (*P.qt >= 0 && *P.qt != q) return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "%s: mixed qtypes", nm);
+      *P.qt = q;
+      if (P.w == &Lw.sh_gate) Lw.sh_dims[0] = rows;
+      if (P.w == &Lw.sh_up) Lw.sh_dims[1] = rows;
+      if (P.w == &Lw.sh_down) Lw.sh_dims[2] = cols;
+      const int alloc_rows = split_ba ? 2 * nv : rows;
+      if (!*P.w) {   // whole 16-row tiles for the GEMV's row streaming
+        ms_status s = m->alloc(P.w, padded((size_t)((alloc_rows + 15) / 16 * 16) * rb));
+        if (s != MS_OK) return s;
+      } else if (!split_ba) {
+        return fail(m->ctx, MS_ERR_STATE, "%s: set twice", nm);
+      }
+      if (t == "ssm_ba.weight" || split_ba) Lw.dn_ba_parts += split_ba ? 1 : 2;
+      // beta rows first, then alpha rows (deltanet.rs:118-125)
+      const size_t off = t == "ssm_alpha.weight" ? (size_t)nv * rb : 0;
+      return upload(m, *P.w + off, data, (size_t)rows * rb);
+    }
+    if (t == "ssm_conv1d.weight") {
+      if (!is_hybrid(c) || is_attention_layer(c, li)) return fail(m->ctx, MS_ERR_STATE, "%s: not a DeltaNet layer", nm);
+      if (q != Q_F32 || n != (int64_t)conv_dim * c.ssm_conv)
+        return fail(m->ctx, MS_ERR_SHAPE, "%s: expected F32 [%d, %d]", nm, conv_dim, c.ssm_conv);
+      return set_vec(m, &Lw.dn_conv_w, nm, q, n, n, data);
+    }
+    if (t == "ssm_a") return set_vec(m, &Lw.dn_a, nm, q, n, nv, data);
+    if (t == "ssm_dt.bias") return set_vec(m, &Lw.dn_dt, nm, q, n, nv, data);
+    if (t == "ssm_norm.weight") return set_vec(m, &Lw.dn_norm, nm, q, n, dn_hvd(c), data);
+    if (t == "ffn_gate_inp_shexp.weight") return set_vec(m, &Lw.sh_gate_inp, nm, q, n, H, data);
   }
   if (t == "ffn_gate_inp.weight") {
     if (q != Q_F32 || dims.size() != 2 || dims[0] != c.experts || dims[1] != H)
@@ -535,10 +618,33 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
                       m->xq_h, m->xd_h));
   for (int li = 0; li < c.layers; ++li) {
     LayerW& Lw = m->L[li];
+    if (Lw.deltanet) {
+      // Gated DeltaNet mixer (deltanet.rs:204-543): h += out(gated RMSNorm(delta rule(conv(qkv x)))),
+      // x = RMSNorm(h); f32-activation GEMVs over the native blocks, as the reference's dequantize + matmul
+      const int conv_dim = dn_conv_dim(c), vt = c.ssm_inner, nv = c.ssm_dt_rank;
+      LAUNCH(launch_rms_norm(dc, m->h, Lw.attn_norm, m->xn, 1, H, c.eps, s));
+      GemvArgs g;
+      g.qtype = Lw.dn_qkv_q; g.w = Lw.dn_qkv; g.rows = conv_dim; g.cols = H; g.x = m->xn; g.y = m->dn_mixed;
+      LAUNCH(launch_gemv(dc, g, s));
+      g.qtype = Lw.dn_z_q; g.w = Lw.dn_z; g.rows = vt; g.y = m->dn_zv;
+      LAUNCH(launch_gemv(dc, g, s));
+      g.qtype = Lw.dn_ba_q; g.w = Lw.dn_ba; g.rows = 2 * nv; g.y = m->dn_bav;
+      LAUNCH(launch_gemv(dc, g, s));
+      DeltaNetStep da;
+      da.nk = c.ssm_groups; da.hkd = c.ssm_state; da.nv = nv; da.hvd = dn_hvd(c); da.eps = c.eps;
+      da.scale = 1.0f / sqrtf((float)da.hvd); da.conv_out = m->dn_conv; da.ba = m->dn_bav; da.z = m->dn_zv;
+      da.ssm_a = Lw.dn_a; da.dt_bias = Lw.dn_dt; da.norm = Lw.dn_norm; da.state = Lw.dn_state; da.out = m->dn_o;
+      LAUNCH(launch_deltanet_core(dc, da, conv_dim, c.ssm_conv, m->dn_mixed, Lw.dn_conv_w, Lw.dn_conv_state, s));
+      ++nk;   // conv + delta rule
+      g.qtype = Lw.dn_out_q; g.w = Lw.dn_out; g.rows = H; g.cols = vt; g.x = m->dn_o; g.y = m->h; g.accumulate = 1;
+      LAUNCH(launch_gemv(dc, g, s));   // h = h + out (the residual add, layer.rs:455)
+    } else {
+    const bool gated = is_hybrid(c);   // [Q_h, gate_h] per head, output x sigmoid(gate) (layer.rs:620-635, 699-705)
     Q8GemvArgs qa;
-    qa.w = Lw.wqkv; qa.rows = Dq + 2 * Dkv; qa.cols = H; qa.xq_in = m->xq_h; qa.xd_in = m->xd_h;
-    qa.bias = Lw.bqkv; qa.y = m->qkv;
+    qa.w = Lw.wqkv; qa.rows = q_rows(c) + 2 * Dkv; qa.cols = H; qa.xq_in = m->xq_h; qa.xd_in = m->xd_h;
+    qa.bias = Lw.bqkv; qa.y = gated ? m->q_raw : m->qkv;
     LAUNCH(launch_q8_gemv(dc, qa, s));
+    if (gated) LAUNCH(launch_gate_split(m->q_raw, c.heads, c.head_dim, Dkv, m->qkv, m->q_gate, s));
     AttnArgs aa;
     aa.qkv = m->qkv; aa.q_norm = Lw.qn; aa.k_norm = Lw.kn; aa.eps = c.eps; aa.cos_t = m->cos_t; aa.sin_t = m->sin_t;
     aa.rot = c.rot_dim; aa.pos = &m->st->pos; aa.kc = Lw.kc; aa.vc = Lw.vc; aa.cap = Lw.cap; aa.window = Lw.window;
@@ -547,13 +653,18 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     // single sequence, streaming kernel: several CTAs per kv head (each a group of its query heads) fill the GPU
     if (m->attn_spl && (c.heads / c.kv_heads) % 4 == 0) aa.head_split = 4;
     else if (m->attn_spl && (c.heads / c.kv_heads) % 2 == 0 && c.heads / c.kv_heads >= 4) aa.head_split = 2;
-    aa.scale = (float)(1.0 / std::sqrt((double)c.head_dim)); aa.oq = m->xq_a; aa.od = m->xd_a;
+    aa.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
+    // the O projection's Q8_0 activation comes from the attention kernel, or after the gate
+    aa.oq = gated ? nullptr : m->xq_a;
+    aa.od = gated ? nullptr : m->xd_a;
     if (exact_attn_ok(m)) LAUNCH(launch_exact_attention(dc, aa, Lw.window ? Lw.cap : c.max_seq_len, s));
     else LAUNCH(launch_attention(dc, aa, s));
+    if (gated) LAUNCH(launch_gate_apply_q8(m->attn_out, m->q_gate, Dq, m->xq_a, m->xd_a, s));
     Q8GemvArgs oa;
     oa.w = Lw.wo; oa.rows = H; oa.cols = Dq; oa.xq_in = m->xq_a; oa.xd_in = m->xd_a; oa.bias = Lw.bo;
     oa.residual = m->h;
     LAUNCH(launch_q8_gemv(dc, oa, s));
+    }
     RouterArgs ra;
     ra.h = m->h; ra.norm_w = Lw.post_norm; ra.eps = c.eps; ra.xn = m->xn; ra.w = Lw.router_w; ra.b = Lw.router_b;
     ra.mask = Lw.mask; ra.logits = m->router_logits; ra.idx = Lw.idx; ra.wts = Lw.wts; ra.counter = m->router_cnt;
@@ -689,8 +800,28 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
         pc.expert_base = m->expert_base; pc.n_local = m->n_local;
       }
     }
-    // h += MoE (ascending expert order); quantize the next layer's attention input
-    const float* next_norm = li + 1 < c.layers ? m->L[li + 1].attn_norm : nullptr;
+    if (Lw.sh_gate) {
+      // shared expert (layer.rs:2250-2293): sigmoid(x . gate_inp) * down(silu(gate x) * up x) on the MoE
+      // input; the residual kernel adds it to the routed output before the residual add (layer.rs:910-922)
+      const int S = Lw.sh_dims[0];
+      GemvArgs g;
+      g.qtype = Lw.sh_gate_q; g.w = Lw.sh_gate; g.rows = S; g.cols = H; g.x = m->xn; g.y = m->sh_g;
+      LAUNCH(launch_gemv(dc, g, s));
+      g.qtype = Lw.sh_up_q; g.w = Lw.sh_up; g.y = m->sh_u;
+      LAUNCH(launch_gemv(dc, g, s));
+      LAUNCH(launch_silu_mul(m->sh_g, m->sh_u, m->sh_a, S, s));
+      g.qtype = Lw.sh_down_q; g.w = Lw.sh_down; g.rows = H; g.cols = S; g.x = m->sh_a; g.y = m->sh_o;
+      LAUNCH(launch_gemv(dc, g, s));
+      if (m->prof_class < 0) {
+        cudaError_t e_ = cudaMemsetAsync(m->sh_y, 0, (size_t)H * 4, s);
+        if (e_ != cudaSuccess) return cuda_fail(m->ctx, e_, "shared expert clear");
+      }
+      LAUNCH(launch_gated_accum(m->xn, Lw.sh_gate_inp, m->sh_o, m->sh_y, H, s));
+      pc.extra = m->sh_y;
+    }
+    // h += MoE (ascending expert order); quantize the next layer's attention input (none before a
+    // DeltaNet layer, which normalises in f32)
+    const float* next_norm = li + 1 < c.layers && !m->L[li + 1].deltanet ? m->L[li + 1].attn_norm : nullptr;
     LAUNCH(launch_resid_norm_q8(dc, pc, m->h, H, next_norm, c.eps, m->xq_h, m->xd_h, m->resid_cnt, s));
     if (m->trace && m->prof_class < 0) {
       cudaError_t e_ = cudaMemcpyAsync(m->trace_h + (size_t)li * H, m->h, (size_t)H * 4, cudaMemcpyDeviceToDevice, s);
@@ -801,6 +932,9 @@ bool pf_supported(const ms_model* m) {
   const ms_model_config& c = m->cfg;
   if (m->prefill_mode == 0) return false;
   if (c.ep_size > 1 && !m->comm) return false;   // the peer-mailbox exchange is sized for one token
+  // DeltaNet layers run token by token (layer.rs:435-452) and shared experts have no batched path:
+  // such models take one decode step per prompt token
+  if (is_hybrid(c) || m->sh_max > 0) return false;
   if (c.hidden % 32 || (c.heads * c.head_dim) % 32 || c.head_dim % 32 || c.head_dim > 256) return false;
   return true;
 }
@@ -1525,6 +1659,13 @@ ms_status ms_model_create(ms_ctx* c, const ms_model_config* cfg, ms_model** out)
       k.ep_rank < 0 || k.ep_rank >= k.ep_size || k.experts % k.ep_size)
     return fail(c, MS_ERR_INVALID_ARG, "invalid model config");
   if (k.hidden % 64 || k.inter % 32) return fail(c, MS_ERR_SHAPE, "hidden %% 64 and inter %% 32 required");
+  if (k.attn_interval < 0) return fail(c, MS_ERR_INVALID_ARG, "invalid model config: attn_interval < 0");
+  if (k.attn_interval > 0 &&
+      (k.ssm_groups <= 0 || k.ssm_state <= 0 || k.ssm_dt_rank <= 0 || k.ssm_inner <= 0 || k.ssm_conv < 1 ||
+       k.ssm_conv > 16 || k.ssm_dt_rank % k.ssm_groups || k.ssm_inner % k.ssm_dt_rank))
+    return fail(c, MS_ERR_INVALID_ARG, "invalid DeltaNet config (ssm fields)");
+  if (k.attn_interval > 0 && (k.ssm_inner / k.ssm_dt_rank != 128 || k.ssm_state > 128 || k.ssm_state % 2))
+    return fail(c, MS_ERR_SHAPE, "DeltaNet: value head dim 128 and an even key head dim <= 128 required");
   auto* m = new ms_model();
   m->ctx = c;
   c->models.push_back(m);
@@ -1582,12 +1723,22 @@ ms_status ms_model_finalize(ms_model* m) {
   cudaSetDevice(m->ctx->device);
   const ms_model_config& c = m->cfg;
   if (!m->embd || !m->out_w || !m->out_norm) return fail(m->ctx, MS_ERR_STATE, "missing token_embd/output/output_norm");
-  bool any_tc = false;
+  bool any_tc = false, any_dn = false;
   for (int li = 0; li < c.layers; ++li) {
     LayerW& Lw = m->L[li];
-    if (!Lw.attn_norm || !Lw.post_norm || Lw.qkv_parts != 3 || !Lw.wo || !Lw.router_w || !Lw.have_gate ||
-        !Lw.have_up || !Lw.have_down)
+    Lw.deltanet = !is_attention_layer(c, li);
+    if (!Lw.attn_norm || !Lw.post_norm || !Lw.router_w || !Lw.have_gate || !Lw.have_up || !Lw.have_down ||
+        (!Lw.deltanet && (Lw.qkv_parts != 3 || !Lw.wo)))
       return fail(m->ctx, MS_ERR_STATE, "layer %d: missing tensors", li);
+    if (Lw.deltanet && (!Lw.dn_qkv || !Lw.dn_z || Lw.dn_ba_parts != 2 || !Lw.dn_out || !Lw.dn_conv_w || !Lw.dn_a ||
+                        !Lw.dn_dt || !Lw.dn_norm))
+      return fail(m->ctx, MS_ERR_STATE, "layer %d: missing Gated DeltaNet tensors", li);
+    if (Lw.sh_gate || Lw.sh_up || Lw.sh_down) {
+      if (!Lw.sh_gate || !Lw.sh_up || !Lw.sh_down || Lw.sh_dims[0] != Lw.sh_dims[1] || Lw.sh_dims[0] != Lw.sh_dims[2] ||
+          Lw.sh_gate_q != Lw.sh_up_q)
+        return fail(m->ctx, MS_ERR_STATE, "layer %d: incomplete or inconsistent shared expert", li);
+      m->sh_max = std::max(m->sh_max, Lw.sh_dims[0]);
+    }
     Lw.tc = Lw.gu_tc && Lw.down_tc;
     if ((Lw.gu_tc || Lw.down_tc) && !Lw.tc)
       return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "layer %d: MXFP4 and K-quant experts mixed in one layer", li);
@@ -1597,9 +1748,16 @@ ms_status ms_model_finalize(ms_model* m) {
     Lw.window = (c.sliding_window > 0 && li % 2 == 0) ? c.sliding_window : 0;   // config.rs:463-465
     Lw.cap = Lw.window ? std::min(Lw.window, c.max_seq_len) : c.max_seq_len;
     if (Lw.window) Lw.cap = Lw.window;
-    const size_t kvb = (size_t)c.kv_heads * Lw.cap * c.head_dim * 4;
-    ms_status s = m->alloc(&Lw.kc, kvb, false);
-    if (s == MS_OK) s = m->alloc(&Lw.vc, kvb, false);
+    ms_status s = MS_OK;
+    if (Lw.deltanet) {   // DeltaNetState (deltanet.rs:139-196): zero at the start of a sequence
+      s = m->alloc(&Lw.dn_conv_state, (size_t)dn_conv_dim(c) * std::max(c.ssm_conv - 1, 1) * 4);
+      if (s == MS_OK) s = m->alloc(&Lw.dn_state, (size_t)c.ssm_dt_rank * c.ssm_state * dn_hvd(c) * 4);
+      any_dn = true;
+    } else {
+      const size_t kvb = (size_t)c.kv_heads * Lw.cap * c.head_dim * 4;
+      s = m->alloc(&Lw.kc, kvb, false);
+      if (s == MS_OK) s = m->alloc(&Lw.vc, kvb, false);
+    }
     if (s == MS_OK) s = m->alloc(&Lw.idx, 16 * 4);
     if (s == MS_OK) s = m->alloc(&Lw.wts, 16 * 4);
     if (s != MS_OK) return s;
@@ -1639,6 +1797,25 @@ ms_status ms_model_finalize(ms_model* m) {
   s = s ? s : m->alloc(&m->ex_kgu, (size_t)c.top_k * 2 * c.inter * 4);
   s = s ? s : m->alloc(&m->xn_final, (size_t)H * 4);
   s = s ? s : m->alloc(&m->ref_scratch, (size_t)exact_refine_scratch_ints(1) * 4);
+  if (is_hybrid(c)) {   // gated attention: [Q_h, gate_h] projection, then the gate
+    s = s ? s : m->alloc(&m->q_raw, (size_t)(q_rows(c) + 2 * Dkv) * 4);
+    s = s ? s : m->alloc(&m->q_gate, (size_t)Dq * 4);
+  }
+  if (any_dn) {
+    const int conv_dim = dn_conv_dim(c);
+    s = s ? s : m->alloc(&m->dn_mixed, (size_t)conv_dim * 4);
+    s = s ? s : m->alloc(&m->dn_conv, (size_t)conv_dim * 4);
+    s = s ? s : m->alloc(&m->dn_zv, (size_t)c.ssm_inner * 4);
+    s = s ? s : m->alloc(&m->dn_bav, (size_t)2 * c.ssm_dt_rank * 4);
+    s = s ? s : m->alloc(&m->dn_o, (size_t)c.ssm_inner * 4);
+  }
+  if (m->sh_max > 0) {
+    s = s ? s : m->alloc(&m->sh_g, (size_t)m->sh_max * 4);
+    s = s ? s : m->alloc(&m->sh_u, (size_t)m->sh_max * 4);
+    s = s ? s : m->alloc(&m->sh_a, (size_t)m->sh_max * 4);
+    s = s ? s : m->alloc(&m->sh_o, (size_t)H * 4);
+    s = s ? s : m->alloc(&m->sh_y, (size_t)H * 4);
+  }
   if (any_tc) {
     m->ex_seg_gu = exact_seg_count(H / 32);
     m->ex_seg_down = exact_seg_count(c.inter / 32);
@@ -1682,6 +1859,8 @@ ms_status ms_model_batch_open(ms_model* m, int B) {
   if (!m->finalized) return fail(m->ctx, MS_ERR_STATE, "batch before finalize");
   const ms_model_config& c = m->cfg;
   if (c.ep_size > 1) return fail(m->ctx, MS_ERR_STATE, "batched decode runs on one GPU (ep_size 1)");
+  if (is_hybrid(c) || m->sh_max > 0)
+    return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "batched decode covers attention + routed-expert layers only");
   for (int li = 0; li < c.layers; ++li)
     if (m->L[li].tc || !m->L[li].gate)
       return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE,
@@ -1938,6 +2117,15 @@ ms_status ms_model_clear_cache(ms_model* m) {
   memset(m->h_st, 0, sizeof(StepState));
   m->h_st->max_seq = m->cfg.max_seq_len;
   MS_CUDA(m->ctx, cudaMemcpy(m->st, m->h_st, sizeof(StepState), cudaMemcpyHostToDevice));
+  // DeltaNet recurrent and conv states start from zero for a new sequence (DeltaNetState::new)
+  const ms_model_config& c = m->cfg;
+  for (const LayerW& Lw : m->L)
+    if (Lw.deltanet) {
+      MS_CUDA(m->ctx, cudaMemsetAsync(Lw.dn_conv_state, 0, (size_t)dn_conv_dim(c) * std::max(c.ssm_conv - 1, 1) * 4,
+                                      m->ctx->stream));
+      MS_CUDA(m->ctx, cudaMemsetAsync(Lw.dn_state, 0, (size_t)c.ssm_dt_rank * c.ssm_state * dn_hvd(c) * 4,
+                                      m->ctx->stream));
+    }
   m->seq = 0;
   return MS_OK;
 }
@@ -2222,6 +2410,8 @@ ms_status ms_model_profile_step(ms_model* m, float* us, int max, int* n) {
   if (!m->finalized || m->kernels_per_step <= 0)
     return fail(m->ctx, MS_ERR_STATE, "profile after finalize and at least one decode step");
   if (m->cfg.ep_size > 1) return fail(m->ctx, MS_ERR_STATE, "profiling is single-device only");
+  if (is_hybrid(m->cfg) || m->sh_max > 0)   // the launch classes assume one launch pattern per layer
+    return fail(m->ctx, MS_ERR_STATE, "per-class profiling covers uniform layer stacks (no DeltaNet / shared expert)");
   cudaSetDevice(m->ctx->device);
   cudaStream_t s = m->ctx->stream, cs = m->ctx->own;
   // a pass that launches nothing, so the launch layout (head_start) is the current mode's
@@ -2328,9 +2518,16 @@ ms_status ms_model_open_gguf(ms_ctx* c, const char* path, int max_seq_len, int e
   std::map<std::string, GgufT> tm(ts.begin(), ts.end());
   // config.rs:253-434 keys and defaults
   const std::string a = gs("general.architecture", "qwen2moe");
-  if (tm.count("blk.0.ssm_a") || tm.count("blk.0.ssm_conv1d.weight"))
-    return fail(c, MS_ERR_UNSUPPORTED_QTYPE, "DeltaNet hybrid models are not supported by this build");
   ms_model_config cfg{};
+  // config.rs:318-352: SSM tensors make a DeltaNet hybrid, every 4th layer attention unless the
+  // file says otherwise; DeltaNet shape keys with the reference's defaults
+  const bool has_ssm = tm.count("blk.0.ssm_a") || tm.count("blk.0.ssm_conv1d.weight");
+  cfg.attn_interval = (int)gi(a + ".attention.full_attention_interval", has_ssm ? 4 : 0);
+  cfg.ssm_groups = (int)gi(a + ".ssm.group_count", 16);
+  cfg.ssm_state = (int)gi(a + ".ssm.state_size", 128);
+  cfg.ssm_dt_rank = (int)gi(a + ".ssm.time_step_rank", gi(a + ".ssm.dt_rank", 32));
+  cfg.ssm_inner = (int)gi(a + ".ssm.inner_size", 4096);
+  cfg.ssm_conv = (int)gi(a + ".ssm.conv_kernel", 4);
   cfg.arch = a == "gpt-oss" ? MS_ARCH_GPT_OSS : MS_ARCH_QWEN_MOE;
   cfg.hidden = (int)gi(a + ".embedding_length", 2048);
   cfg.layers = (int)gi(a + ".block_count", 48);

@@ -191,7 +191,20 @@ def config_from_model(m: G.Model, max_seq_len: int, ep_rank: int = 0, ep_size: i
     c.rope_theta = gf("rope.freq_base", 1e6)
     c.eps = gf("attention.layer_norm_rms_epsilon", 1e-6)
     c.sliding_window = gi("attention.sliding_window", 0)
-    c.rot_dim = c.head_dim
+    # partial rotary: rope.partial_rotary_factor, else rope.dimension_count / head_dim (config.rs:328-335)
+    prf = meta.get(f"{a}.rope.partial_rotary_factor")
+    if prf is None:
+        dc = meta.get(f"{a}.rope.dimension_count")
+        prf = float(np.float32(dc) / np.float32(c.head_dim)) if dc is not None else 1.0
+    c.rot_dim = int(np.float32(c.head_dim) * np.float32(prf))
+    # DeltaNet hybrids (config.rs:318-352): SSM tensors imply an attention interval of 4
+    has_ssm = "blk.0.ssm_a" in m.tensors or "blk.0.ssm_conv1d.weight" in m.tensors
+    c.attn_interval = gi("attention.full_attention_interval", 4 if has_ssm else 0)
+    c.ssm_groups = gi("ssm.group_count", 16)
+    c.ssm_state = gi("ssm.state_size", 128)
+    c.ssm_dt_rank = int(meta.get(f"{a}.ssm.time_step_rank", meta.get(f"{a}.ssm.dt_rank", 32)))
+    c.ssm_inner = gi("ssm.inner_size", 4096)
+    c.ssm_conv = gi("ssm.conv_kernel", 4)
     name = meta.get("general.name", "")
     c.norm_topk_prob = int(not ("Qwen1.5" in name or "Qwen2" in name))
     c.max_seq_len = max_seq_len

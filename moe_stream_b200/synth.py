@@ -51,6 +51,19 @@ class ModelSpec:
     router_bias: bool = True
     with_attention: bool = True     # False: MoE-only layer stack (config 0)
     with_lm: bool = True            # embedding / final norm / LM head present
+    # DeltaNet hybrids (Qwen3-Next): layer l is gated attention when (l + 1) % attn_interval == 0,
+    # else Gated DeltaNet with ssm_groups k heads of ssm_state dims, ssm_dt_rank v heads of
+    # ssm_inner / ssm_dt_rank dims and a causal conv of ssm_conv taps (config.rs:318-352, 446-494)
+    attn_interval: int = 0
+    ssm_groups: int = 16
+    ssm_state: int = 128
+    ssm_dt_rank: int = 32
+    ssm_inner: int = 4096
+    ssm_conv: int = 4
+    ssm_q: int = G.Q4_K             # DeltaNet projections (attn_qkv, attn_gate, ssm_ba, ssm_out)
+    shared_inter: int = 0           # > 0: one always-on shared expert of this width per layer
+    shared_q: int = G.Q4_K
+    rot_factor: float = 1.0         # rope.partial_rotary_factor (rotary dims = head_dim * factor)
 
     @property
     def q_dim(self) -> int:
@@ -59,6 +72,13 @@ class ModelSpec:
     @property
     def kv_dim(self) -> int:
         return self.kv_heads * self.head_dim
+
+    def is_attention_layer(self, layer: int) -> bool:
+        return self.attn_interval == 0 or (layer + 1) % self.attn_interval == 0
+
+    @property
+    def ssm_conv_dim(self) -> int:
+        return 2 * self.ssm_groups * self.ssm_state + self.ssm_inner
 
 
 # ---- named configurations -------------------------------------------------
@@ -77,8 +97,23 @@ TINY_GPT_OSS = replace(GPT_OSS_20B, name="tiny-gpt-oss", hidden=256, layers=2, h
 TINY_QWEN3 = replace(QWEN3_30B_A3B, name="tiny-qwen3", hidden=256, layers=2, heads=4, kv_heads=2,
                      head_dim=64, experts=16, top_k=4, inter=256, vocab=1024)
 
+# Qwen3-Coder-Next-80B shape.  Quantization of the non-expert tensors is not named by the
+# benchmark: DeltaNet projections and the shared expert in Q4_K, attention in Q8_0 (stated assumption);
+# rope theta is not named either (1e7 here).
+QWEN3_NEXT_80B = ModelSpec(arch="qwen3next", name="Qwen3-Coder-Next-80B-synthetic", hidden=2048, layers=48,
+                           heads=16, kv_heads=2, head_dim=256, experts=512, top_k=10, inter=512,
+                           vocab=151936, rope_theta=1e7, eps=1e-6, sliding_window=0,
+                           expert_gate_q=G.Q4_K, expert_down_q=G.Q4_K, attn_q=G.Q8_0,
+                           expert_bias=False, attn_bias=False, sinks=False, qk_norm=True,
+                           router_bias=False, attn_interval=4, ssm_groups=16, ssm_state=128,
+                           ssm_dt_rank=32, ssm_inner=4096, ssm_conv=4, shared_inter=512, rot_factor=0.25)
+TINY_QWEN3_NEXT = replace(QWEN3_NEXT_80B, name="tiny-qwen3-next", hidden=256, layers=8, experts=64,
+                          inter=256, vocab=1024, ssm_groups=2, ssm_state=64, ssm_dt_rank=4, ssm_inner=512,
+                          shared_inter=256)
+
 PRESETS = {"gpt-oss-20b": GPT_OSS_20B, "gpt-oss-moe-layer": GPT_OSS_MOE_LAYER,
-           "qwen3-30b-a3b": QWEN3_30B_A3B, "tiny-gpt-oss": TINY_GPT_OSS, "tiny-qwen3": TINY_QWEN3}
+           "qwen3-30b-a3b": QWEN3_30B_A3B, "tiny-gpt-oss": TINY_GPT_OSS, "tiny-qwen3": TINY_QWEN3,
+           "qwen3-next-80b": QWEN3_NEXT_80B, "tiny-qwen3-next": TINY_QWEN3_NEXT}
 
 
 # ---- random block generators ----------------------------------------------
@@ -188,9 +223,14 @@ def tensor_defs(spec: ModelSpec) -> Iterator[TensorDef]:
                lambda rng: _rand_quant(rng, spec.embed_q, spec.vocab * H))
     for L in range(spec.layers):
         p = f"blk.{L}"
-        if spec.with_attention:
+        if spec.with_attention and not spec.is_attention_layer(L):
             yield (f"{p}.attn_norm.weight", G.F32, (H,), ones(H))
-            for nm, rows in (("attn_q", spec.q_dim), ("attn_k", spec.kv_dim), ("attn_v", spec.kv_dim)):
+            yield from _deltanet_defs(spec, p)
+        elif spec.with_attention:
+            yield (f"{p}.attn_norm.weight", G.F32, (H,), ones(H))
+            # hybrid models: the Q projection holds [Q_h, gate_h] per head (layer.rs:620-635)
+            q_rows = spec.q_dim * (2 if spec.attn_interval else 1)
+            for nm, rows in (("attn_q", q_rows), ("attn_k", spec.kv_dim), ("attn_v", spec.kv_dim)):
                 yield (f"{p}.{nm}.weight", spec.attn_q, (rows, H),
                        (lambda r: lambda rng: _rand_quant(rng, spec.attn_q, r * H))(rows))
                 if spec.attn_bias:
@@ -220,6 +260,28 @@ def tensor_defs(spec: ModelSpec) -> Iterator[TensorDef]:
                 rows = shp[1]
                 yield (f"{p}.{nm}.bias", G.F32, (E, rows),
                        (lambda n_: lambda rng: rand_normal_f32(rng, n_, 0.01))(E * rows))
+        if spec.shared_inter:
+            S, q = spec.shared_inter, spec.shared_q
+            for nm, shp in (("ffn_gate_shexp", (S, H)), ("ffn_up_shexp", (S, H)), ("ffn_down_shexp", (H, S))):
+                yield (f"{p}.{nm}.weight", q, shp,
+                       (lambda n_: lambda rng: _rand_quant(rng, q, n_))(shp[0] * shp[1]))
+            yield (f"{p}.ffn_gate_inp_shexp.weight", G.F32, (H,), lambda rng: rand_normal_f32(rng, H, 0.05))
+
+
+def _deltanet_defs(spec: ModelSpec, p: str) -> Iterator[TensorDef]:
+    """One Gated DeltaNet layer in the split (Unsloth) format deltanet.rs:101-137 reads: attn_qkv
+    (flat Q, K, V rows), attn_gate (z), ssm_ba (flat beta, alpha rows), ssm_out, and the f32 conv1d
+    [conv_dim, taps], ssm_a (= -exp(A_log)), ssm_dt.bias and ssm_norm [head_v_dim]."""
+    H, nv, q = spec.hidden, spec.ssm_dt_rank, spec.ssm_q
+    C, V = spec.ssm_conv_dim, spec.ssm_inner
+    for nm, rows, cols in (("attn_qkv", C, H), ("attn_gate", V, H), ("ssm_ba", 2 * nv, H), ("ssm_out", H, V)):
+        yield (f"{p}.{nm}.weight", q, (rows, cols), (lambda n_: lambda rng: _rand_quant(rng, q, n_))(rows * cols))
+    ks = spec.ssm_conv
+    yield (f"{p}.ssm_conv1d.weight", G.F32, (C, ks), lambda rng: rand_normal_f32(rng, C * ks, 0.5))
+    yield (f"{p}.ssm_a", G.F32, (nv,), lambda rng: (-np.exp(rng.uniform(-1.0, 1.0, nv))).astype(np.float32))
+    yield (f"{p}.ssm_dt.bias", G.F32, (nv,), lambda rng: rng.uniform(-1.0, 1.0, nv).astype(np.float32))
+    hvd = V // nv
+    yield (f"{p}.ssm_norm.weight", G.F32, (hvd,), lambda rng: rng.uniform(0.5, 1.5, hvd).astype(np.float32))
 
 
 def metadata(spec: ModelSpec) -> Dict[str, Tuple[int, object]]:
@@ -242,6 +304,15 @@ def metadata(spec: ModelSpec) -> Dict[str, Tuple[int, object]]:
     }
     if spec.sliding_window:
         m[f"{a}.attention.sliding_window"] = (G.T_U32, spec.sliding_window)
+    if spec.rot_factor != 1.0:
+        m[f"{a}.rope.partial_rotary_factor"] = (G.T_F32, spec.rot_factor)
+    if spec.attn_interval:
+        m[f"{a}.attention.full_attention_interval"] = (G.T_U32, spec.attn_interval)
+        m[f"{a}.ssm.group_count"] = (G.T_U32, spec.ssm_groups)
+        m[f"{a}.ssm.state_size"] = (G.T_U32, spec.ssm_state)
+        m[f"{a}.ssm.time_step_rank"] = (G.T_U32, spec.ssm_dt_rank)
+        m[f"{a}.ssm.inner_size"] = (G.T_U32, spec.ssm_inner)
+        m[f"{a}.ssm.conv_kernel"] = (G.T_U32, spec.ssm_conv)
     return m
 
 

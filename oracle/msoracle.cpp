@@ -527,6 +527,7 @@ struct orc_model {
   int experts = 0, top_k = 0, inter = 0, vocab = 0, sliding_window = 0, max_seq = 0;
   float rope_theta = 0, eps = 0; bool norm_topk = true, oai = false;
   int attn_mode = 1, threads = 0;
+  int attn_interval = 0;   // full_attention_interval; > 0 = DeltaNet hybrid with gated attention
   std::vector<float> cos_t, sin_t;
   struct Layer {
     const float* attn_norm = nullptr; const float* post_norm = nullptr;
@@ -535,6 +536,14 @@ struct orc_model {
     orc_moe_layer moe{};
     std::vector<int> dummies;
     std::vector<float> K, V;   // [kv_heads][seq][hd] grown per step (kv_cache.rs:37-60)
+    // hybrid models (config.rs:446-458): a layer is attention or Gated DeltaNet
+    bool is_attn = true;
+    orc_deltanet_layer dn{};
+    std::vector<uint8_t> ba_cat;                     // split ssm_beta / ssm_alpha rows joined (beta first)
+    std::vector<float> conv_state, rec_state;        // DeltaNetState (deltanet.rs:139-196), zero at start
+    // shared expert (layer.rs:1898-1953, 2250-2293)
+    const GTensor *sh_gate = nullptr, *sh_up = nullptr, *sh_down = nullptr;
+    const float* sh_gate_inp = nullptr;
   };
   std::vector<Layer> L;
   const GTensor *embd = nullptr, *out = nullptr; const float* out_norm = nullptr; const float* out_bias = nullptr;
@@ -607,10 +616,26 @@ void sdpa(const float* q, const float* K, const float* V, int nh, int nkv, int n
 // layer.rs:511-749 for n tokens at positions [seq, seq+n)
 void attention(orc_model* m, orc_model::Layer& Ly, int li, const float* x, int n, float* out) {
   const int H = m->hidden, nh = m->heads, nkv = m->kv_heads, hd = m->head_dim;
-  std::vector<float> q((size_t)n * nh * hd), k((size_t)n * nkv * hd), v((size_t)n * nkv * hd);
-  project(m, Ly.q, x, n, q.data()); project(m, Ly.k, x, n, k.data()); project(m, Ly.v, x, n, v.data());
+  std::vector<float> q((size_t)n * nh * hd), k((size_t)n * nkv * hd), v((size_t)n * nkv * hd), gate;
+  const bool gated = m->attn_interval > 0;   // hybrid models: Q projection = [Q_h, gate_h] per head
+  if (gated) {                               // (layer.rs:620-635)
+    const size_t Dq = (size_t)nh * hd;
+    std::vector<float> qg((size_t)n * 2 * Dq);
+    project(m, Ly.q, x, n, qg.data());
+    if (Ly.qb) for (int t = 0; t < n; ++t) for (size_t i = 0; i < 2 * Dq; ++i) qg[t * 2 * Dq + i] += Ly.qb[i];
+    gate.resize((size_t)n * Dq);
+    for (int t = 0; t < n; ++t)
+      for (int i = 0; i < nh; ++i)
+        for (int d = 0; d < hd; ++d) {
+          q[t * Dq + (size_t)i * hd + d] = qg[t * 2 * Dq + (size_t)i * 2 * hd + d];
+          gate[t * Dq + (size_t)i * hd + d] = qg[t * 2 * Dq + (size_t)i * 2 * hd + hd + d];
+        }
+  } else {
+    project(m, Ly.q, x, n, q.data());
+  }
+  project(m, Ly.k, x, n, k.data()); project(m, Ly.v, x, n, v.data());
   for (int t = 0; t < n; ++t) {
-    if (Ly.qb) for (int i = 0; i < nh * hd; ++i) q[(size_t)t * nh * hd + i] += Ly.qb[i];
+    if (Ly.qb && !gated) for (int i = 0; i < nh * hd; ++i) q[(size_t)t * nh * hd + i] += Ly.qb[i];
     if (Ly.kb) for (int i = 0; i < nkv * hd; ++i) k[(size_t)t * nkv * hd + i] += Ly.kb[i];
     if (Ly.vb) for (int i = 0; i < nkv * hd; ++i) v[(size_t)t * nkv * hd + i] += Ly.vb[i];
   }
@@ -644,6 +669,8 @@ void attention(orc_model* m, orc_model::Layer& Ly, int li, const float* x, int n
   std::vector<float> attn((size_t)n * nh * hd);
   sdpa(q.data(), Ly.K.data(), Ly.V.data(), nh, nkv, n, Lk, hd, scale, n > 1, Ly.sinks, sw, attn.data(),
        m->threads ? m->threads : hw_threads());
+  if (gated)   // attn_out *= sigmoid(gate), sigmoid = recip(exp(-x) + 1) (layer.rs:699-705, activation.rs:41-45)
+    for (size_t i = 0; i < attn.size(); ++i) attn[i] = attn[i] * (1.0f / (expcr(-gate[i]) + 1.0f));
   project(m, Ly.o, attn.data(), n, out);                     // layer.rs:709-730
   if (Ly.ob) for (int t = 0; t < n; ++t) for (int i = 0; i < H; ++i) out[(size_t)t * H + i] += Ly.ob[i];
 }
@@ -801,7 +828,14 @@ orc_model* orc_model_open(const char* path, int max_seq_len, char* err, int err_
   std::string name = g.str("general.name", "");
   m->norm_topk = !(name.find("Qwen1.5") != std::string::npos || name.find("Qwen2") != std::string::npos);
   m->oai = (a == "gpt-oss");
-  if (g.get("blk.0.ssm_a") || g.get("blk.0.ssm_conv1d.weight")) return fail("DeltaNet hybrid models are not supported by this oracle build");
+  // config.rs:318-352: SSM tensors make a DeltaNet hybrid (every attn_interval-th layer attention)
+  const bool has_ssm = g.get("blk.0.ssm_a") || g.get("blk.0.ssm_conv1d.weight");
+  m->attn_interval = (int)g.u32(a + ".attention.full_attention_interval", has_ssm ? 4 : 0);
+  const int dn_nk = (int)g.u32(a + ".ssm.group_count", 16), dn_hkd = (int)g.u32(a + ".ssm.state_size", 128);
+  int dn_nv = (int)g.u32(a + ".ssm.time_step_rank", -1);
+  if (dn_nv < 0) dn_nv = (int)g.u32(a + ".ssm.dt_rank", 32);
+  const int dn_inner = (int)g.u32(a + ".ssm.inner_size", 4096), dn_ks = (int)g.u32(a + ".ssm.conv_kernel", 4);
+  const int dn_hvd = dn_nv == 0 ? 128 : dn_inner / dn_nv;   // config.rs:486-488
   m->max_seq = max_seq_len;
   m->cos_t.resize((size_t)max_seq_len * (m->rot_dim / 2)); m->sin_t.resize(m->cos_t.size());
   rope_tables(m->rot_dim, max_seq_len, (double)m->rope_theta, m->cos_t.data(), m->sin_t.data());
@@ -815,9 +849,41 @@ orc_model* orc_model_open(const char* path, int max_seq_len, char* err, int err_
     Ly.attn_norm = f32p(g.get(p + "attn_norm.weight"));
     Ly.post_norm = f32p(g.get(p + "post_attention_norm.weight"));
     if (!Ly.post_norm) Ly.post_norm = f32p(g.get(p + "ffn_norm.weight"));
-    Ly.q = g.get(p + "attn_q.weight"); Ly.k = g.get(p + "attn_k.weight");
-    Ly.v = g.get(p + "attn_v.weight"); Ly.o = g.get(p + "attn_output.weight");
-    if (!Ly.attn_norm || !Ly.post_norm || !Ly.q || !Ly.k || !Ly.v || !Ly.o) return fail("missing attention tensors in " + p);
+    if (!Ly.attn_norm || !Ly.post_norm) return fail("missing norm tensors in " + p);
+    // config.rs:452-458: with an interval, layer li is attention when (li + 1) % interval == 0
+    Ly.is_attn = m->attn_interval == 0 || (li + 1) % m->attn_interval == 0;
+    if (!Ly.is_attn) {   // Gated DeltaNet layer, split (Unsloth) tensor format (deltanet.rs:101-137)
+      auto& D = Ly.dn;
+      D.hidden = m->hidden; D.n_k_heads = dn_nk; D.head_k_dim = dn_hkd; D.n_v_heads = dn_nv; D.head_v_dim = dn_hvd;
+      D.conv_kernel = dn_ks; D.eps = m->eps;
+      const GTensor *qkv = g.get(p + "attn_qkv.weight"), *z = g.get(p + "attn_gate.weight"),
+                    *ba = g.get(p + "ssm_ba.weight"), *out = g.get(p + "ssm_out.weight");
+      if (!qkv || !z || !out) return fail("missing DeltaNet projections in " + p + " (the split attn_qkv format is required)");
+      D.qkv_q = qkv->qtype; D.qkv = qkv->data; D.gate_q = z->qtype; D.gate = z->data;
+      D.out_q = out->qtype; D.out = out->data;
+      if (ba) { D.ba_q = ba->qtype; D.ba = ba->data; }
+      else {   // ssm_beta + ssm_alpha rows, beta first (deltanet.rs:118-125)
+        const GTensor *bt = g.get(p + "ssm_beta.weight"), *at = g.get(p + "ssm_alpha.weight");
+        if (!bt || !at || bt->qtype != at->qtype) return fail("missing ssm_ba / ssm_beta + ssm_alpha in " + p);
+        Ly.ba_cat.assign(bt->data, bt->data + bt->nbytes);
+        Ly.ba_cat.insert(Ly.ba_cat.end(), at->data, at->data + at->nbytes);
+        D.ba_q = bt->qtype; D.ba = Ly.ba_cat.data();
+      }
+      D.conv1d = f32p(g.get(p + "ssm_conv1d.weight")); D.ssm_a = f32p(g.get(p + "ssm_a"));
+      D.dt_bias = f32p(g.get(p + "ssm_dt.bias")); D.norm = f32p(g.get(p + "ssm_norm.weight"));
+      if (!D.conv1d || !D.ssm_a || !D.dt_bias || !D.norm) return fail("missing DeltaNet f32 tensors in " + p);
+      const int conv_dim = 2 * dn_nk * dn_hkd + dn_nv * dn_hvd;   // config.rs:492-494
+      Ly.conv_state.assign((size_t)conv_dim * (dn_ks - 1), 0.0f);
+      Ly.rec_state.assign((size_t)dn_nv * dn_hkd * dn_hvd, 0.0f);
+    } else {
+      Ly.q = g.get(p + "attn_q.weight"); Ly.k = g.get(p + "attn_k.weight");
+      Ly.v = g.get(p + "attn_v.weight"); Ly.o = g.get(p + "attn_output.weight");
+      if (!Ly.q || !Ly.k || !Ly.v || !Ly.o) return fail("missing attention tensors in " + p);
+    }
+    Ly.sh_gate = g.get(p + "ffn_gate_shexp.weight"); Ly.sh_up = g.get(p + "ffn_up_shexp.weight");
+    Ly.sh_down = g.get(p + "ffn_down_shexp.weight"); Ly.sh_gate_inp = f32p(g.get(p + "ffn_gate_inp_shexp.weight"));
+    if ((Ly.sh_gate || Ly.sh_up || Ly.sh_down) && !(Ly.sh_gate && Ly.sh_up && Ly.sh_down))
+      return fail("incomplete shared expert in " + p);
     Ly.qb = f32p(g.get(p + "attn_q.bias")); Ly.kb = f32p(g.get(p + "attn_k.bias"));
     Ly.vb = f32p(g.get(p + "attn_v.bias")); Ly.ob = f32p(g.get(p + "attn_output.bias"));
     Ly.sinks = f32p(g.get(p + "attn_sinks.weight"));
@@ -848,7 +914,14 @@ void orc_model_set_threads(orc_model* m, int n) { m->threads = n; }
 int orc_model_vocab(const orc_model* m) { return m->vocab; }
 int orc_model_hidden(const orc_model* m) { return m->hidden; }
 int orc_model_seq_len(const orc_model* m) { return m->seq; }
-void orc_model_clear_cache(orc_model* m) { for (auto& l : m->L) { l.K.clear(); l.V.clear(); } m->seq = 0; }
+void orc_model_clear_cache(orc_model* m) {
+  for (auto& l : m->L) {
+    l.K.clear(); l.V.clear();
+    std::fill(l.conv_state.begin(), l.conv_state.end(), 0.0f);
+    std::fill(l.rec_state.begin(), l.rec_state.end(), 0.0f);
+  }
+  m->seq = 0;
+}
 void orc_model_destroy(orc_model* m) { delete m; }
 void orc_model_last_hidden(const orc_model* m, float* o) { std::memcpy(o, m->last_hidden.data(), m->last_hidden.size() * 4); }
 void orc_model_last_routing(const orc_model* m, int32_t* idx, float* w) {
@@ -898,11 +971,23 @@ int orc_model_forward(orc_model* m, const int32_t* tokens, int n, float* logits)
   for (int li = 0; li < m->layers; ++li) {  // layer.rs:393-503
     auto& Ly = m->L[li];
     rms_norm(h.data(), Ly.attn_norm, xn.data(), n, H, m->eps);
-    attention(m, Ly, li, xn.data(), n, tmp.data());
+    if (Ly.is_attn) {
+      attention(m, Ly, li, xn.data(), n, tmp.data());
+    } else {   // DeltaNet: one token after another through the recurrent state (layer.rs:435-452)
+      for (int t = 0; t < n; ++t)
+        if (orc_deltanet_step(&Ly.dn, &xn[(size_t)t * H], Ly.conv_state.data(), Ly.rec_state.data(),
+                              &tmp[(size_t)t * H]) != 0)
+          return -3;
+    }
     for (size_t i = 0; i < h.size(); ++i) h[i] = h[i] + tmp[i];
     rms_norm(h.data(), Ly.post_norm, xn.data(), n, H, m->eps);
     moe_forward(&Ly.moe, xn.data(), n, tmp.data(), idx.data(), w.data(), &Ly.dummies, th, 0, 1 << 30,
                 &m->layer_logits[(size_t)li * E]);
+    if (Ly.sh_gate)   // routed output + shared expert output (layer.rs:910-922), per token
+      for (int t = 0; t < n; ++t)
+        if (orc_shared_expert(Ly.sh_gate->qtype, Ly.sh_gate->data, Ly.sh_up->data, Ly.sh_down->qtype, Ly.sh_down->data,
+                              Ly.sh_gate_inp, H, (int)Ly.sh_gate->shape[0], &xn[(size_t)t * H], &tmp[(size_t)t * H]) != 0)
+          return -3;
     for (size_t i = 0; i < h.size(); ++i) h[i] = h[i] + tmp[i];
     std::memcpy(&m->layer_hidden[(size_t)li * H], &h[(size_t)(n - 1) * H], (size_t)H * 4);
     std::memcpy(&m->last_idx[(size_t)li * K], &idx[(size_t)(n - 1) * K], K * 4);

@@ -34,7 +34,7 @@ def test_static_library_built():
 
 
 def test_abi_version_and_status_strings(L):
-    assert L.ms_abi_version() == 3
+    assert L.ms_abi_version() == 4
     assert L.ms_status_string(0) == b"ok"
     assert L.ms_status_string(5) == b"device wait timed out"
     assert L.ms_status_string(99) == b"unknown status"
