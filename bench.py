@@ -577,6 +577,84 @@ def run_case_qwen3(args):
     print(json.dumps(out), flush=True)
 
 
+def qwen3next_step_bytes(spec, ctx_len):
+    """Algorithmic HBM bytes of one config-3 decode step (batch 1): the Q4_K DeltaNet projections and
+    the f32 recurrent state (read and written) of the DeltaNet layers, the Q8_0 gated-attention
+    projections and f32 KV at ctx_len positions of the attention layers, and in every layer the f32
+    router, the top-k routed Q4_K experts and the shared expert; plus the f16 LM head."""
+    H, E, k, I, S = spec.hidden, spec.experts, spec.top_k, spec.inter, spec.shared_inter
+    q4 = lambda rows, cols: rows * (cols // 256) * 144
+    q8 = lambda rows, cols: rows * (cols // 32) * 34
+    nv, hvd = spec.ssm_dt_rank, spec.ssm_inner // spec.ssm_dt_rank
+    dn = (q4(spec.ssm_conv_dim, H) + q4(spec.ssm_inner, H) + q4(2 * nv, H) + q4(H, spec.ssm_inner)
+          + 2 * nv * spec.ssm_state * hvd * 4 + 2 * spec.ssm_conv_dim * (spec.ssm_conv - 1) * 4)
+    attn = (q8(2 * spec.q_dim + 2 * spec.kv_dim, H) + q8(H, spec.q_dim)
+            + 2 * ctx_len * spec.kv_heads * spec.head_dim * 4)
+    moe = E * H * 4 + k * 3 * q4(I, H) + 3 * q4(S, H)
+    n_attn = sum(spec.is_attention_layer(li) for li in range(spec.layers))
+    return n_attn * attn + (spec.layers - n_attn) * dn + spec.layers * moe + spec.vocab * H * 2
+
+
+def run_case_qwen3next(args):
+    """Config 3: Qwen3-Coder-Next-80B-shaped DeltaNet hybrid (36 Gated DeltaNet + 12 gated-attention
+    layers, 512 Q4_K experts top-10 + a shared expert), greedy decode at batch 1 after a --prompt-token
+    prompt (one step per position), then K device-resident greedy steps timed with CUDA events.  The
+    43 GB of expert stacks are generated once and uploaded to every layer's own buffers (the routers,
+    and so the routing, differ per layer)."""
+    import re
+    import torch
+    from dataclasses import replace
+    from moe_stream_b200 import synth
+    from moe_stream_b200.engine import Context, Engine
+    spec = synth.QWEN3_NEXT_80B
+    if args.layers:
+        spec = replace(spec, layers=args.layers)
+    prompt_len = args.prompt
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx = Context(0)
+    ctx.set_stream(stream)
+    t0 = time.time()
+    share = lambda n: re.sub(r"^blk\.\d+\.(ffn_(gate|up|down)_exps\.weight)$", r"blk.0.\1", n) \
+        if re.match(r"^blk\.\d+\.ffn_(gate|up|down)_exps\.weight$", n) else None
+    eng = Engine.from_spec(spec, seed=0, max_seq_len=prompt_len + args.warmup + args.steps + 64, ctx=ctx,
+                           share=share)
+    log(f"qwen3-next model generated + uploaded in {time.time() - t0:.1f}s")
+    peak, peak_kind = peaks()
+    prompt = synth.prompt_ids(spec, prompt_len, seed=0)
+    t0 = time.time()
+    eng.clear_cache()
+    eng.forward(prompt)
+    torch.cuda.synchronize()
+    log(f"prompt of {prompt_len} positions in {time.time() - t0:.1f}s")
+    eng.decode_steps_device(args.warmup)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        s.record(stream)
+        eng.decode_steps_device(args.steps)
+        e.record(stream)
+        torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    ctx.sync()
+    nbytes = qwen3next_step_bytes(spec, prompt_len + args.warmup + args.steps // 2)
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    out = {"case": "qwen3-coder-next-80b", "metric": "decode tok/s (bs1)", "value": round(1e3 / ms, 1),
+           "unit": "tok/s", "ms_per_step": round(ms, 4), "steps": args.steps, "warmup": args.warmup,
+           "n_gpus": 1, "dtype": "f32 (Q4_K / Q8_0 weights)", "data": "synthetic",
+           "kernels_per_step": eng.kernels_per_step, "algorithmic_bytes_per_step": int(nbytes),
+           "achieved_gbs": round(gbs, 1), "hbm_frac": round(gbs / peak, 4), "peak_kind": peak_kind,
+           "clocks": clk.summary(),
+           "config": {"workload": f"Qwen3-Coder-Next-80B-shaped DeltaNet hybrid, greedy decode after a "
+                                  f"{prompt_len}-token prompt", "layers": spec.layers,
+                      "attention_layers": sum(spec.is_attention_layer(li) for li in range(spec.layers)),
+                      "experts": spec.experts, "top_k": spec.top_k, "kv_context": prompt_len,
+                      "expert_bytes": "one generated set uploaded to every layer",
+                      "l2": "no flush: each step streams > 2 GB"}}
+    eng.close()
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -595,7 +673,7 @@ def main():
                     help="expert-parallel MoE exchange: peer-memory stores (default) or NCCL all-reduce")
     ap.add_argument("--mode", default="ep", choices=["ep", "replicas"],
                     help="N > 1: expert parallel over one sequence (default) or N independent replicas")
-    ap.add_argument("--case", default=None, choices=[None, "moe-layer", "prefill", "qwen3"],
+    ap.add_argument("--case", default=None, choices=[None, "moe-layer", "prefill", "qwen3", "qwen3next"],
                     help="moe-layer: the decode expert FFN alone; prefill: config 4's MoE step; "
                          "qwen3: config 2 decode at the --batch sizes")
     ap.add_argument("--batch", default="1,32", help="qwen3 case: comma-separated batch sizes")
@@ -613,6 +691,10 @@ def main():
         if args.prompt == PROMPT:
             args.prompt = 4096
         run_case_qwen3(args)
+    elif args.case == "qwen3next":
+        if args.prompt == PROMPT:
+            args.prompt = 4096
+        run_case_qwen3next(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -472,7 +472,9 @@ struct DeltaNetStep {
 cudaError_t launch_deltanet_core(const DevCtx& c, const DeltaNetStep& a, int conv_dim, int ks, const float* mixed,
                                  const float* conv_w, float* conv_state, cudaStream_t s);
 cudaError_t launch_silu_mul(const float* g, const float* u, float* o, int n, cudaStream_t s);
-cudaError_t launch_gated_accum(const float* x, const float* gate_inp, const float* v, float* y, int n, cudaStream_t s);
+// y += sigmoid(x . gate_inp) * v (assign: y = ...); gate_inp null: factor 1
+cudaError_t launch_gated_accum(const float* x, const float* gate_inp, const float* v, float* y, int n, cudaStream_t s,
+                               int assign = 0);
 
 // ---- step plumbing ----
 // ---- sampling (kernels_sample.cu): SamplingParams::sample (engine.rs:124-208) on the device ----

@@ -117,7 +117,7 @@ __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __rest
 
 // y += sigmoid(x . gate_inp) * v (every CTA recomputes the gate dot, deterministic)
 __global__ void gated_accum_kernel(const float* __restrict__ x, const float* __restrict__ gate_inp,
-                                   const float* __restrict__ v, float* __restrict__ y, int n) {
+                                   const float* __restrict__ v, float* __restrict__ y, int n, int assign) {
   __shared__ float red[8];
   float sig = 1.0f;
   if (gate_inp) {
@@ -126,7 +126,8 @@ __global__ void gated_accum_kernel(const float* __restrict__ x, const float* __r
     d = block_sum_2w(d, red, blockDim.x / 32);
     sig = 1.0f / (1.0f + expf(-d));
   }
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) y[i] += v[i] * sig;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    y[i] = assign ? v[i] * sig : y[i] + v[i] * sig;
 }
 
 }  // namespace
@@ -146,8 +147,9 @@ cudaError_t launch_silu_mul(const float* g, const float* u, float* o, int n, cud
   return cudaGetLastError();
 }
 
-cudaError_t launch_gated_accum(const float* x, const float* gate_inp, const float* v, float* y, int n, cudaStream_t s) {
-  gated_accum_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, gate_inp, v, y, n);
+cudaError_t launch_gated_accum(const float* x, const float* gate_inp, const float* v, float* y, int n, cudaStream_t s,
+                               int assign) {
+  gated_accum_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, gate_inp, v, y, n, assign);
   return cudaGetLastError();
 }
 

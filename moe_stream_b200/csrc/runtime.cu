@@ -155,6 +155,12 @@ struct LayerW {
   int sh_gate_q = -1, sh_up_q = -1, sh_down_q = -1;
   float* sh_gate_inp = nullptr;
   int sh_dims[3] = {0, 0, 0};       // gate rows, up rows, down cols (the shared expert's width)
+  // one buffer for the DeltaNet input projections [qkv | z | ba rows] and one for the shared expert's
+  // [gate | up rows] when their qtypes agree, so each group is a single GEMV launch
+  uint8_t* dn_in = nullptr;
+  int dn_in_q = -1;
+  uint8_t* sh_gu = nullptr;
+  int sh_gu_q = -1, sh_gu_rows = 0;
 };
 
 // NCCL is resolved at run time (dlopen), so a process that already loaded libnccl (torch does)
@@ -294,7 +300,7 @@ struct ms_model {
   // hybrid models: DeltaNet step scratch, gated attention's raw Q/gate projection, shared expert
   float *dn_mixed = nullptr, *dn_conv = nullptr, *dn_zv = nullptr, *dn_bav = nullptr, *dn_o = nullptr;
   float *q_raw = nullptr, *q_gate = nullptr;
-  float *sh_g = nullptr, *sh_u = nullptr, *sh_a = nullptr, *sh_o = nullptr, *sh_y = nullptr;
+  float *sh_g = nullptr, *sh_a = nullptr, *sh_o = nullptr, *sh_y = nullptr;
   int sh_max = 0;                   // widest shared expert (0: none)
   struct Prefill {
     int cap = 0;                       // tokens the buffers hold
@@ -438,17 +444,36 @@ ms_status set_layer_tensor(ms_model* m, int li, const std::string& t, int q, con
       if (P.w == &Lw.sh_gate) Lw.sh_dims[0] = rows;
       if (P.w == &Lw.sh_up) Lw.sh_dims[1] = rows;
       if (P.w == &Lw.sh_down) Lw.sh_dims[2] = cols;
-      const int alloc_rows = split_ba ? 2 * nv : rows;
-      if (!*P.w) {   // whole 16-row tiles for the GEMV's row streaming
-        ms_status s = m->alloc(P.w, padded((size_t)((alloc_rows + 15) / 16 * 16) * rb));
-        if (s != MS_OK) return s;
-      } else if (!split_ba) {
-        return fail(m->ctx, MS_ERR_STATE, "%s: set twice", nm);
-      }
-      if (t == "ssm_ba.weight" || split_ba) Lw.dn_ba_parts += split_ba ? 1 : 2;
+      if (*P.w && !split_ba) return fail(m->ctx, MS_ERR_STATE, "%s: set twice", nm);
       // beta rows first, then alpha rows (deltanet.rs:118-125)
-      const size_t off = t == "ssm_alpha.weight" ? (size_t)nv * rb : 0;
-      return upload(m, *P.w + off, data, (size_t)rows * rb);
+      const size_t sub = t == "ssm_alpha.weight" ? (size_t)nv * rb : 0;
+      if (t == "ssm_ba.weight" || split_ba) Lw.dn_ba_parts += split_ba ? 1 : 2;
+      const bool dn_in = P.w == &Lw.dn_qkv || P.w == &Lw.dn_z || P.w == &Lw.dn_ba;
+      const bool sh_in = P.w == &Lw.sh_gate || P.w == &Lw.sh_up;
+      if (dn_in && !Lw.dn_in) {   // [qkv | z | ba] rows in one buffer, whole 16-row tiles
+        ms_status s = m->alloc(&Lw.dn_in, padded((size_t)((conv_dim + vt + 2 * nv + 15) / 16 * 16) * rb));
+        if (s != MS_OK) return s;
+        Lw.dn_in_q = q;
+      }
+      if (sh_in && !Lw.sh_gu) {   // [gate | up] rows in one buffer
+        ms_status s = m->alloc(&Lw.sh_gu, padded((size_t)((2 * rows + 15) / 16 * 16) * rb));
+        if (s != MS_OK) return s;
+        Lw.sh_gu_q = q;
+        Lw.sh_gu_rows = rows;
+      }
+      if (!*P.w) {
+        if (dn_in && Lw.dn_in_q == q) {
+          const int r0 = P.w == &Lw.dn_qkv ? 0 : (P.w == &Lw.dn_z ? conv_dim : conv_dim + vt);
+          *P.w = Lw.dn_in + (size_t)r0 * rb;
+        } else if (sh_in && Lw.sh_gu_q == q && Lw.sh_gu_rows == rows) {
+          *P.w = Lw.sh_gu + (P.w == &Lw.sh_up ? (size_t)rows * rb : 0);
+        } else {   // own buffer, whole 16-row tiles for the GEMV's row streaming
+          const int alloc_rows = split_ba ? 2 * nv : rows;
+          ms_status s = m->alloc(P.w, padded((size_t)((alloc_rows + 15) / 16 * 16) * rb));
+          if (s != MS_OK) return s;
+        }
+      }
+      return upload(m, *P.w + sub, data, (size_t)rows * rb);
     }
     if (t == "ssm_conv1d.weight") {
       if (!is_hybrid(c) || is_attention_layer(c, li)) return fail(m->ctx, MS_ERR_STATE, "%s: not a DeltaNet layer", nm);
@@ -625,11 +650,18 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
       LAUNCH(launch_rms_norm(dc, m->h, Lw.attn_norm, m->xn, 1, H, c.eps, s));
       GemvArgs g;
       g.qtype = Lw.dn_qkv_q; g.w = Lw.dn_qkv; g.rows = conv_dim; g.cols = H; g.x = m->xn; g.y = m->dn_mixed;
-      LAUNCH(launch_gemv(dc, g, s));
-      g.qtype = Lw.dn_z_q; g.w = Lw.dn_z; g.rows = vt; g.y = m->dn_zv;
-      LAUNCH(launch_gemv(dc, g, s));
-      g.qtype = Lw.dn_ba_q; g.w = Lw.dn_ba; g.rows = 2 * nv; g.y = m->dn_bav;
-      LAUNCH(launch_gemv(dc, g, s));
+      const int64_t rb_in = row_bytes(Lw.dn_qkv_q, H);
+      if (Lw.dn_z_q == Lw.dn_qkv_q && Lw.dn_ba_q == Lw.dn_qkv_q && Lw.dn_z == Lw.dn_qkv + (size_t)conv_dim * rb_in &&
+          Lw.dn_ba == Lw.dn_z + (size_t)vt * rb_in) {
+        g.rows = conv_dim + vt + 2 * nv;   // qkv, z, beta / alpha rows in one launch
+        LAUNCH(launch_gemv(dc, g, s));
+      } else {
+        LAUNCH(launch_gemv(dc, g, s));
+        g.qtype = Lw.dn_z_q; g.w = Lw.dn_z; g.rows = vt; g.y = m->dn_zv;
+        LAUNCH(launch_gemv(dc, g, s));
+        g.qtype = Lw.dn_ba_q; g.w = Lw.dn_ba; g.rows = 2 * nv; g.y = m->dn_bav;
+        LAUNCH(launch_gemv(dc, g, s));
+      }
       DeltaNetStep da;
       da.nk = c.ssm_groups; da.hkd = c.ssm_state; da.nv = nv; da.hvd = dn_hvd(c); da.eps = c.eps;
       da.scale = 1.0f / sqrtf((float)da.hvd); da.conv_out = m->dn_conv; da.ba = m->dn_bav; da.z = m->dn_zv;
@@ -804,19 +836,21 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
       // shared expert (layer.rs:2250-2293): sigmoid(x . gate_inp) * down(silu(gate x) * up x) on the MoE
       // input; the residual kernel adds it to the routed output before the residual add (layer.rs:910-922)
       const int S = Lw.sh_dims[0];
+      float* sh_u = m->sh_g + S;   // [gate | up] outputs back to back
       GemvArgs g;
       g.qtype = Lw.sh_gate_q; g.w = Lw.sh_gate; g.rows = S; g.cols = H; g.x = m->xn; g.y = m->sh_g;
-      LAUNCH(launch_gemv(dc, g, s));
-      g.qtype = Lw.sh_up_q; g.w = Lw.sh_up; g.y = m->sh_u;
-      LAUNCH(launch_gemv(dc, g, s));
-      LAUNCH(launch_silu_mul(m->sh_g, m->sh_u, m->sh_a, S, s));
+      if (Lw.sh_gate == Lw.sh_gu && Lw.sh_up == Lw.sh_gu + (size_t)S * row_bytes(Lw.sh_gate_q, H)) {
+        g.rows = 2 * S;   // gate and up rows in one launch
+        LAUNCH(launch_gemv(dc, g, s));
+      } else {
+        LAUNCH(launch_gemv(dc, g, s));
+        g.qtype = Lw.sh_up_q; g.w = Lw.sh_up; g.y = sh_u;
+        LAUNCH(launch_gemv(dc, g, s));
+      }
+      LAUNCH(launch_silu_mul(m->sh_g, sh_u, m->sh_a, S, s));
       g.qtype = Lw.sh_down_q; g.w = Lw.sh_down; g.rows = H; g.cols = S; g.x = m->sh_a; g.y = m->sh_o;
       LAUNCH(launch_gemv(dc, g, s));
-      if (m->prof_class < 0) {
-        cudaError_t e_ = cudaMemsetAsync(m->sh_y, 0, (size_t)H * 4, s);
-        if (e_ != cudaSuccess) return cuda_fail(m->ctx, e_, "shared expert clear");
-      }
-      LAUNCH(launch_gated_accum(m->xn, Lw.sh_gate_inp, m->sh_o, m->sh_y, H, s));
+      LAUNCH(launch_gated_accum(m->xn, Lw.sh_gate_inp, m->sh_o, m->sh_y, H, s, 1));   // sh_y = sigmoid(.) * o
       pc.extra = m->sh_y;
     }
     // h += MoE (ascending expert order); quantize the next layer's attention input (none before a
@@ -1803,15 +1837,17 @@ ms_status ms_model_finalize(ms_model* m) {
   }
   if (any_dn) {
     const int conv_dim = dn_conv_dim(c);
-    s = s ? s : m->alloc(&m->dn_mixed, (size_t)conv_dim * 4);
+    // the input projections' outputs back to back [mixed qkv | z | beta, alpha] (one GEMV writes all)
+    s = s ? s : m->alloc(&m->dn_mixed, ((size_t)conv_dim + c.ssm_inner + 2 * c.ssm_dt_rank) * 4);
+    if (s == MS_OK) {
+      m->dn_zv = m->dn_mixed + conv_dim;
+      m->dn_bav = m->dn_zv + c.ssm_inner;
+    }
     s = s ? s : m->alloc(&m->dn_conv, (size_t)conv_dim * 4);
-    s = s ? s : m->alloc(&m->dn_zv, (size_t)c.ssm_inner * 4);
-    s = s ? s : m->alloc(&m->dn_bav, (size_t)2 * c.ssm_dt_rank * 4);
     s = s ? s : m->alloc(&m->dn_o, (size_t)c.ssm_inner * 4);
   }
   if (m->sh_max > 0) {
-    s = s ? s : m->alloc(&m->sh_g, (size_t)m->sh_max * 4);
-    s = s ? s : m->alloc(&m->sh_u, (size_t)m->sh_max * 4);
+    s = s ? s : m->alloc(&m->sh_g, (size_t)2 * m->sh_max * 4);   // [gate | up] outputs of one layer
     s = s ? s : m->alloc(&m->sh_a, (size_t)m->sh_max * 4);
     s = s ? s : m->alloc(&m->sh_o, (size_t)H * 4);
     s = s ? s : m->alloc(&m->sh_y, (size_t)H * 4);

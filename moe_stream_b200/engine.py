@@ -257,9 +257,12 @@ class Engine:
     @classmethod
     def from_spec(cls, spec, seed: int = 0, max_seq_len: int = 4096, device: int = 0, ep_rank: int = 0,
                   ep_size: int = 1, ctx: Optional[Context] = None, attn_splits: int = 0,
-                  progress=None) -> "Engine":
+                  progress=None, share=None) -> "Engine":
         """Generate a seeded synthetic model tensor by tensor and upload each as it is made,
-        so host memory holds one tensor at a time (the benchmark's 13 GB GPT-OSS shape)."""
+        so host memory holds one tensor at a time (the benchmark's 13 GB GPT-OSS shape).
+        share(name) -> name or None: tensors mapped to the same name get the bytes generated once for
+        that name (each is still uploaded to its own device buffer), e.g. one set of expert stacks for
+        every layer of a 43 GB model whose generation would otherwise dominate the run."""
         from . import synth
         ctx = ctx or Context(device)
         meta = G.Model()
@@ -270,8 +273,15 @@ class Engine:
         h = C.c_void_p()
         check(lib().ms_model_create(ctx.h, C.byref(cfg), C.byref(h)), ctx.h)
         try:
+            shared = {}
             for name, q, shape, gen in synth.tensor_defs(spec):
-                raw = np.ascontiguousarray(gen(synth.tensor_rng(seed, name))).view(np.uint8).reshape(-1)
+                key = share(name) if share else None
+                if key is not None and key in shared:
+                    raw = shared[key]
+                else:
+                    raw = np.ascontiguousarray(gen(synth.tensor_rng(seed, key or name))).view(np.uint8).reshape(-1)
+                    if key is not None:
+                        shared[key] = raw
                 dims = (C.c_int64 * len(shape))(*shape)
                 check(lib().ms_model_set_tensor(h, name.encode(), q, len(shape), dims, raw.ctypes.data, raw.size),
                       ctx.h)
