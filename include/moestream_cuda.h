@@ -313,6 +313,22 @@ MS_API ms_status ms_model_ep_connect(ms_model* m, const void* handles, size_t by
 /* Parse a GGUF file (reader.rs:259-368, config.rs:253-434) and upload everything. */
 MS_API ms_status ms_model_open_gguf(ms_ctx* ctx, const char* path, int max_seq_len, int ep_rank, int ep_size,
                              ms_model** out);
+/* Host-tier expert streaming (the reference's SSD / mmap streaming mode with its per-layer expert LRU,
+ * gguf/reader.rs:631-858, model/layer.rs:1146-1152, 1777-1784, model/cache.rs:84-158).  Call after
+ * ms_model_create and before the expert tensors are set: every layer's K-quant expert stacks (Q4_K /
+ * Q6_K, still in their block format) are then kept in pinned host memory and HBM holds `slots`
+ * experts per layer (slots >= top_k; 0 turns the tier off).  At each layer the step waits for the
+ * router, copies the routed experts that are not cached into the least recently used slots not
+ * routed this step, and runs the same expert kernels on the slots, so logits and tokens are the same
+ * bits as with HBM-resident experts.  The step is then enqueued per call (no captured graph, one host
+ * synchronisation per layer); prompts run one decode step per token; the lockstep batch path and
+ * expert parallelism are not available.  Needs the order-independent numerics (ms_model_set_exact 1). */
+MS_API ms_status ms_model_set_expert_tier(ms_model* m, int slots);
+/* Expert-slot hits and misses since the model was created (ExpertCache::stats, cache.rs:144-158). */
+MS_API ms_status ms_model_expert_tier_stats(const ms_model* m, uint64_t* hits, uint64_t* misses);
+/* ms_model_open_gguf (one GPU) with host-tier experts of `expert_slots` HBM slots per layer. */
+MS_API ms_status ms_model_open_gguf_tiered(ms_ctx* ctx, const char* path, int max_seq_len, int expert_slots,
+                                           ms_model** out);
 MS_API ms_status ms_model_get_config(const ms_model* m, ms_model_config* cfg);
 MS_API ms_status ms_model_destroy(ms_model* m);
 

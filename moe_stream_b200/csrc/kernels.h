@@ -347,6 +347,10 @@ struct ExactKqArgs {
   const int* idx = nullptr;
   int H = 0, I = 0, K = 0, expert_base = 0, n_local = 0, oai_swiglu = 0;
   int B = 1;                        // tokens: x [B][H], idx [B][K], gu_out [B K][2][I], y [B K][H]
+  // [B K] or null: the weight slot of each (token, slot) in gate / up / down (host-tier expert
+  // streaming keeps only a cache of slots in HBM); null: the expert's own position.  Biases and the
+  // combine still follow idx.
+  const int* wslot = nullptr;
   float* gu_out = nullptr;
   float* y = nullptr;
 };

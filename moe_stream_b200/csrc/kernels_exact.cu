@@ -919,7 +919,8 @@ __global__ void __launch_bounds__(kKThreads) exact_kq_gu_kernel(ExactKqArgs a, u
   __syncthreads();
   const int G = a.H / 64, R = G >= 32 ? 1 : 32 / G;
   const int64_t rb = (int64_t)(a.H / 256) * (a.gate_fmt == Q_Q4_K ? 144 : kQ6PadBytes);
-  const uint8_t* w = (which ? a.up : a.gate) + (int64_t)e * a.I * rb;
+  const int we = a.wslot ? a.wslot[k] : e;   // weight slot (host-tier cache) or the expert itself
+  const uint8_t* w = (which ? a.up : a.gate) + (int64_t)we * a.I * rb;
   const float* bias = which ? (a.up_b ? a.up_b + (size_t)e * a.I : nullptr) : (a.gate_b ? a.gate_b + (size_t)e * a.I : nullptr);
   kq_rows(a.gate_fmt, w, rb, a.I, a.H, xk, blockIdx.x * (kKThreads / 32) * R, bias, a.gu_out + ((size_t)k * 2 + which) * a.I,
           red);
@@ -939,7 +940,7 @@ __global__ void __launch_bounds__(kKThreads) exact_kq_down_kernel(ExactKqArgs a,
   __syncthreads();
   const int G = a.I / 64, R = G >= 32 ? 1 : 32 / G;
   const int64_t rb = (int64_t)(a.I / 256) * (a.down_fmt == Q_Q4_K ? 144 : kQ6PadBytes);
-  const uint8_t* w = a.down + (int64_t)e * a.H * rb;
+  const uint8_t* w = a.down + (int64_t)(a.wslot ? a.wslot[k] : e) * a.H * rb;
   kq_rows(a.down_fmt, w, rb, a.H, a.I, ak, blockIdx.x * (kKThreads / 32) * R,
           a.down_b ? a.down_b + (size_t)e * a.H : nullptr, a.y + (size_t)k * a.H, red);
   (void)err;

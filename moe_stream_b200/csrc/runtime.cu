@@ -301,6 +301,20 @@ struct ms_model {
   float *dn_mixed = nullptr, *dn_conv = nullptr, *dn_zv = nullptr, *dn_bav = nullptr, *dn_o = nullptr;
   float *q_raw = nullptr, *q_gate = nullptr;
   float *sh_g = nullptr, *sh_a = nullptr, *sh_o = nullptr, *sh_y = nullptr;
+  // host-tier expert streaming (ms_model_set_expert_tier): every layer's K-quant expert stacks live
+  // in pinned host memory; HBM holds tier_slots experts per layer, least recently used evicted
+  struct TierLayer {
+    uint8_t* host[3] = {nullptr, nullptr, nullptr};   // gate, up, down stacks [E][rows][row bytes]
+    int64_t stride[3] = {0, 0, 0};                   // bytes per expert (Q6_K padded to 224-byte blocks)
+    std::vector<int> slot_expert;                     // expert held by each HBM slot (-1: empty)
+    std::vector<uint64_t> slot_used;                  // step of the slot's last use
+    int* wslot = nullptr;                             // device [16]: weight slot of each routed slot
+  };
+  int tier_slots = 0;
+  std::vector<TierLayer> tier;
+  uint64_t tier_hits = 0, tier_misses = 0, tier_clock = 0;
+  int* h_wslot = nullptr;           // pinned [layers][16] staging of the slot tables
+  int* h_tier_idx = nullptr;        // pinned [16] routed ids read back per layer
   int sh_max = 0;                   // widest shared expert (0: none)
   struct Prefill {
     int cap = 0;                       // tokens the buffers hold
@@ -356,6 +370,80 @@ ms_status set_vec(ms_model* m, float** slot, const char* name, int q, int64_t n,
 
 // weight allocations are padded so 16-row streaming tiles never read past the end
 size_t padded(size_t bytes) { return (bytes + 16 * 4352 + 255) & ~(size_t)255; }
+
+// Host-tier expert stack (gate 0 / up 1 / down 2) of layer li: the native blocks into pinned host
+// memory (Q6_K rows padded to 224-byte superblocks, as the HBM-resident layout), and an HBM cache of
+// tier_slots experts.  The reference streams expert slices from the mmap'ed GGUF into an LRU of
+// dequantized experts (gguf/reader.rs:631-858, model/cache.rs:84-158); here the slices stay in their
+// block format and the cache is device memory.
+ms_status tier_upload(ms_model* m, int li, int which, int q, int rows, int cols, const uint8_t* src, int64_t per,
+                      uint8_t** dev, int* qt) {
+  if (q != Q_Q4_K && q != Q_Q6_K)
+    return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "host-tier expert streaming covers Q4_K / Q6_K experts (qtype %d)", q);
+  if (*dev) return fail(m->ctx, MS_ERR_STATE, "expert stack of layer %d set twice", li);
+  const int E = m->n_local;
+  const bool q6 = q == Q_Q6_K;
+  const int64_t n_sb = (int64_t)rows * (cols / 256);
+  const int64_t stride = q6 ? n_sb * kQ6PadBytes : per;
+  ms_model::TierLayer& T = m->tier[li];
+  void* host = nullptr;
+  MS_CUDA(m->ctx, cudaHostAlloc(&host, (size_t)stride * E, cudaHostAllocDefault));
+  T.host[which] = (uint8_t*)host;
+  T.stride[which] = stride;
+  if (q6) {
+    for (int64_t b = 0; b < n_sb * E; ++b) {
+      std::memcpy(T.host[which] + b * kQ6PadBytes, src + b * 210, 210);
+      std::memset(T.host[which] + b * kQ6PadBytes + 210, 0, kQ6PadBytes - 210);
+    }
+  } else {
+    std::memcpy(host, src, (size_t)per * E);
+  }
+  *qt = q6 ? Q_Q6_K_PAD : q;
+  return m->alloc(dev, padded((size_t)stride * m->tier_slots));
+}
+
+// Before a host-tier layer's expert kernels: read the routed ids back (the router has run), bring
+// every routed expert missing from the layer's HBM slots in from host memory (evicting the least
+// recently used slot not routed this step), and upload the slot table the expert kernels read.
+// Stream-ordered: the copies and the table precede the expert kernels on `s`.
+ms_status tier_fetch(ms_model* m, int li, cudaStream_t s) {
+  const ms_model_config& c = m->cfg;
+  ms_model::TierLayer& T = m->tier[li];
+  LayerW& Lw = m->L[li];
+  const int K = c.top_k, C = m->tier_slots;
+  MS_CUDA(m->ctx, cudaMemcpyAsync(m->h_tier_idx, Lw.idx, (size_t)K * 4, cudaMemcpyDeviceToHost, s));
+  MS_CUDA(m->ctx, cudaStreamSynchronize(s));
+  const uint64_t now = ++m->tier_clock;
+  int* ws = m->h_wslot + (size_t)li * 16;
+  bool hit[16];
+  for (int k = 0; k < K; ++k) {
+    const int e = m->h_tier_idx[k];
+    if (e < 0 || e >= m->n_local) return fail(m->ctx, MS_ERR_DEVICE_INDEX, "layer %d: routed expert %d out of range", li, e);
+    hit[k] = false;
+    for (int j = 0; j < C; ++j)
+      if (T.slot_expert[j] == e) { ws[k] = j; T.slot_used[j] = now; hit[k] = true; ++m->tier_hits; break; }
+  }
+  uint8_t* dst[3] = {Lw.gate, Lw.up, Lw.down};
+  for (int k = 0; k < K; ++k) {
+    if (hit[k]) continue;
+    int best = -1;   // an empty slot first, else the least recently used slot not routed this step
+    for (int j = 0; j < C; ++j) {
+      if (T.slot_expert[j] < 0) { best = j; break; }
+      if (T.slot_used[j] != now && (best < 0 || T.slot_used[j] < T.slot_used[best])) best = j;
+    }
+    if (best < 0) return fail(m->ctx, MS_ERR_STATE, "layer %d: no free expert slot", li);
+    const int e = m->h_tier_idx[k];
+    for (int w = 0; w < 3; ++w)
+      MS_CUDA(m->ctx, cudaMemcpyAsync(dst[w] + (size_t)best * T.stride[w], T.host[w] + (size_t)e * T.stride[w],
+                                      (size_t)T.stride[w], cudaMemcpyHostToDevice, s));
+    T.slot_expert[best] = e;
+    T.slot_used[best] = now;
+    ws[k] = best;
+    ++m->tier_misses;
+  }
+  MS_CUDA(m->ctx, cudaMemcpyAsync(T.wslot, ws, (size_t)K * 4, cudaMemcpyHostToDevice, s));
+  return MS_OK;
+}
 
 ms_status set_layer_tensor(ms_model* m, int li, const std::string& t, int q, const std::vector<int64_t>& dims,
                            const void* data, size_t bytes) {
@@ -520,6 +608,9 @@ ms_status set_layer_tensor(ms_model* m, int li, const std::string& t, int q, con
       *x.qt = q;
       const bool is_down = x.w == &Lw.down;
       (is_down ? Lw.have_down : (x.w == &Lw.gate ? Lw.have_gate : Lw.have_up)) = true;
+      if (m->tier_slots > 0)
+        return tier_upload(m, li, is_down ? 2 : (x.w == &Lw.gate ? 0 : 1), q, x.rows, x.cols,
+                           (const uint8_t*)data + per * m->expert_base, per, x.w, x.qt);
       if (q == Q_MXFP4 && m->use_tc && tc_supported(H, c.inter)) {
         // repack this rank's experts into tensor-core tiles (gate rows 0-63 and up rows 64-127 of a
         // gate_up tile; 128 hidden rows per down tile); the native blocks are not kept
@@ -728,6 +819,8 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     PendingCombine pc;
     const bool exact_kq = m->exact && !Lw.tc && exact_kq_supported(Lw.gate_q, Lw.down_q, H, c.inter) &&
                           Lw.up_q == Lw.gate_q;
+    if (m->tier_slots > 0 && !exact_kq)   // the slot table is read by the order-independent K-quant kernels only
+      return fail(m->ctx, MS_ERR_STATE, "layer %d: host-tier experts need the order-independent K-quant kernels", li);
     if ((m->exact && Lw.tc) || exact_kq) {
       // order-independent experts: f64 partial dots; the combine (residual kernel, the peer-mailbox
       // send, or a combine kernel before the NCCL all-reduce) sums segments in ascending expert id
@@ -749,6 +842,11 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
         ka.gate_b = Lw.gate_b; ka.up_b = Lw.up_b; ka.down_b = Lw.down_b; ka.x = m->xn; ka.idx = Lw.idx; ka.H = H;
         ka.I = c.inter; ka.K = c.top_k; ka.expert_base = m->expert_base; ka.n_local = m->n_local;
         ka.oai_swiglu = c.arch == MS_ARCH_GPT_OSS; ka.gu_out = m->ex_kgu; ka.y = m->partial;
+        if (m->tier_slots > 0) {   // host tier: routed experts into this layer's HBM slots first
+          ms_status ts = tier_fetch(m, li, s);
+          if (ts != MS_OK) return ts;
+          ka.wslot = m->tier[li].wslot;
+        }
         LAUNCH(launch_exact_kq_moe(dc, ka, s));
         ++nk;   // gate/up, down
         lc.partial = m->partial;
@@ -882,7 +980,9 @@ ms_status run_step(ms_model* m) {
   cudaStream_t s = m->ctx->stream;
   if (m->cfg.ep_size > 1 && !m->comm && !m->ep_p2p)
     return fail(m->ctx, MS_ERR_STATE, "expert-parallel model: call ms_model_init_ep or ms_model_ep_connect first");
-  if (!m->use_graph) return enqueue_step(m, s);
+  // host-tier experts: the step stops at every layer's router for the host to fill the HBM slots,
+  // so it is enqueued directly (a captured graph cannot contain the host's decisions)
+  if (!m->use_graph || m->tier_slots > 0) return enqueue_step(m, s);
   if (!m->graph) {
     // capture on the context's private stream (the caller's stream may be the legacy default
     // stream, which cannot be captured); the graph is then launched on the caller's stream
@@ -969,6 +1069,7 @@ bool pf_supported(const ms_model* m) {
   // DeltaNet layers run token by token (layer.rs:435-452) and shared experts have no batched path:
   // such models take one decode step per prompt token
   if (is_hybrid(c) || m->sh_max > 0) return false;
+  if (m->tier_slots > 0) return false;   // host-tier experts: the expert kernels read HBM slots
   if (c.hidden % 32 || (c.heads * c.head_dim) % 32 || c.head_dim % 32 || c.head_dim > 256) return false;
   return true;
 }
@@ -1796,6 +1897,22 @@ ms_status ms_model_finalize(ms_model* m) {
     if (s == MS_OK) s = m->alloc(&Lw.wts, 16 * 4);
     if (s != MS_OK) return s;
   }
+  if (m->tier_slots > 0) {
+    for (int li = 0; li < c.layers; ++li) {
+      ms_model::TierLayer& T = m->tier[li];
+      if (!T.host[0] || !T.host[1] || !T.host[2])
+        return fail(m->ctx, MS_ERR_STATE, "layer %d: host-tier expert stacks missing", li);
+      if (!exact_kq_supported(m->L[li].gate_q, m->L[li].down_q, c.hidden, c.inter) || m->L[li].up_q != m->L[li].gate_q)
+        return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "layer %d: host-tier experts need Q4_K / Q6_K shapes the "
+                    "order-independent kernels cover", li);
+      T.slot_expert.assign(m->tier_slots, -1);
+      T.slot_used.assign(m->tier_slots, 0);
+      ms_status ts = m->alloc(&T.wslot, 16 * 4);
+      if (ts != MS_OK) return ts;
+    }
+    MS_CUDA(m->ctx, cudaMallocHost(&m->h_wslot, (size_t)c.layers * 16 * 4));
+    MS_CUDA(m->ctx, cudaMallocHost(&m->h_tier_idx, 16 * 4));
+  }
   const int H = c.hidden, Dq = q_dim(c), Dkv = kv_dim(c), rep = c.heads / c.kv_heads;
   // decode attention splits: 128 positions each, sized for the longest attended range
   // decode attention splits sized for the longest attended range of each layer kind: head_dim <= 64
@@ -1897,6 +2014,7 @@ ms_status ms_model_batch_open(ms_model* m, int B) {
   if (c.ep_size > 1) return fail(m->ctx, MS_ERR_STATE, "batched decode runs on one GPU (ep_size 1)");
   if (is_hybrid(c) || m->sh_max > 0)
     return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "batched decode covers attention + routed-expert layers only");
+  if (m->tier_slots > 0) return fail(m->ctx, MS_ERR_STATE, "batched decode needs HBM-resident experts (no host tier)");
   for (int li = 0; li < c.layers; ++li)
     if (m->L[li].tc || !m->L[li].gate)
       return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE,
@@ -2125,6 +2243,11 @@ ms_status ms_model_destroy(ms_model* m) {
   for (void* p : m->allocs) cudaFree(p);
   if (m->h_tok) cudaFreeHost(m->h_tok);
   if (m->h_st) cudaFreeHost(m->h_st);
+  for (auto& T : m->tier)
+    for (uint8_t* p : T.host)
+      if (p) cudaFreeHost(p);
+  if (m->h_wslot) cudaFreeHost(m->h_wslot);
+  if (m->h_tier_idx) cudaFreeHost(m->h_tier_idx);
   auto& v = m->ctx->models;
   v.erase(std::remove(v.begin(), v.end(), m), v.end());
   delete m;
@@ -2296,6 +2419,8 @@ ms_status ms_model_last_routing(ms_model* m, int layer, int32_t* idx, float* wts
 
 ms_status ms_model_set_exact(ms_model* m, int enable) {
   if (!m) return MS_ERR_INVALID_ARG;
+  if (!enable && m->tier_slots > 0)
+    return fail(m->ctx, MS_ERR_STATE, "host-tier experts run on the order-independent kernels only");
   cudaSetDevice(m->ctx->device);
   MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
   m->exact = enable != 0;
@@ -2446,6 +2571,7 @@ ms_status ms_model_profile_step(ms_model* m, float* us, int max, int* n) {
   if (!m->finalized || m->kernels_per_step <= 0)
     return fail(m->ctx, MS_ERR_STATE, "profile after finalize and at least one decode step");
   if (m->cfg.ep_size > 1) return fail(m->ctx, MS_ERR_STATE, "profiling is single-device only");
+  if (m->tier_slots > 0) return fail(m->ctx, MS_ERR_STATE, "per-class profiling needs HBM-resident experts");
   if (is_hybrid(m->cfg) || m->sh_max > 0)   // the launch classes assume one launch pattern per layer
     return fail(m->ctx, MS_ERR_STATE, "per-class profiling covers uniform layer stacks (no DeltaNet / shared expert)");
   cudaSetDevice(m->ctx->device);
@@ -2498,7 +2624,42 @@ ms_status ms_model_profile_step(ms_model* m, float* us, int max, int* n) {
   return st;
 }
 
+ms_status ms_model_set_expert_tier(ms_model* m, int slots) {
+  if (!m || slots < 0) return MS_ERR_INVALID_ARG;
+  const ms_model_config& c = m->cfg;
+  if (m->finalized) return fail(m->ctx, MS_ERR_STATE, "expert tier after finalize");
+  for (const LayerW& Lw : m->L)
+    if (Lw.have_gate || Lw.have_up || Lw.have_down)
+      return fail(m->ctx, MS_ERR_STATE, "expert tier must be chosen before the expert tensors are set");
+  if (slots == 0) { m->tier_slots = 0; m->tier.clear(); return MS_OK; }
+  if (c.ep_size > 1) return fail(m->ctx, MS_ERR_STATE, "host-tier experts run on one GPU (ep_size 1)");
+  if (slots < c.top_k) return fail(m->ctx, MS_ERR_INVALID_ARG, "expert slots %d < top_k %d", slots, c.top_k);
+  m->tier_slots = std::min(slots, m->n_local);
+  m->tier.assign(c.layers, ms_model::TierLayer{});
+  return MS_OK;
+}
+
+ms_status ms_model_expert_tier_stats(const ms_model* m, uint64_t* hits, uint64_t* misses) {
+  if (!m || !hits || !misses) return MS_ERR_INVALID_ARG;
+  *hits = m->tier_hits;
+  *misses = m->tier_misses;
+  return MS_OK;
+}
+
+static ms_status open_gguf(ms_ctx* c, const char* path, int max_seq_len, int ep_rank, int ep_size, int expert_slots,
+                           ms_model** out);
+
 ms_status ms_model_open_gguf(ms_ctx* c, const char* path, int max_seq_len, int ep_rank, int ep_size, ms_model** out) {
+  return open_gguf(c, path, max_seq_len, ep_rank, ep_size, 0, out);
+}
+
+ms_status ms_model_open_gguf_tiered(ms_ctx* c, const char* path, int max_seq_len, int expert_slots, ms_model** out) {
+  if (expert_slots <= 0) return MS_ERR_INVALID_ARG;
+  return open_gguf(c, path, max_seq_len, 0, 1, expert_slots, out);
+}
+
+static ms_status open_gguf(ms_ctx* c, const char* path, int max_seq_len, int ep_rank, int ep_size, int expert_slots,
+                           ms_model** out) {
   if (!c || !path || !out || max_seq_len <= 0) return MS_ERR_INVALID_ARG;
   *out = nullptr;
   int fd = ::open(path, O_RDONLY);
@@ -2593,6 +2754,7 @@ ms_status ms_model_open_gguf(ms_ctx* c, const char* path, int max_seq_len, int e
   ms_model* m = nullptr;
   ms_status s = ms_model_create(c, &cfg, &m);
   if (s != MS_OK) return s;
+  if (expert_slots > 0 && (s = ms_model_set_expert_tier(m, expert_slots)) != MS_OK) { ms_model_destroy(m); return s; }
   for (auto& kv : ts) {
     const GgufT& t = kv.second;
     if (t.nbytes < 0) continue;   // types outside the decode path are not indexed

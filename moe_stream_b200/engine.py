@@ -227,15 +227,28 @@ class Engine:
     # engine.rs:277 open_with_device
     @classmethod
     def open(cls, path: str, max_seq_len: int = 4096, device: int = 0, ep_rank: int = 0, ep_size: int = 1,
-             ctx: Optional[Context] = None) -> "Engine":
+             ctx: Optional[Context] = None, expert_slots: int = 0) -> "Engine":
+        """expert_slots > 0: host-tier experts (pinned host memory, an HBM LRU of that many experts per
+        layer; the reference's SSD-streaming mode)."""
         ctx = ctx or Context(device)
         h = C.c_void_p()
-        check(lib().ms_model_open_gguf(ctx.h, path.encode(), max_seq_len, ep_rank, ep_size, C.byref(h)), ctx.h)
+        if expert_slots > 0:
+            if ep_size != 1:
+                raise ValueError("host-tier experts run on one GPU")
+            check(lib().ms_model_open_gguf_tiered(ctx.h, path.encode(), max_seq_len, expert_slots, C.byref(h)), ctx.h)
+        else:
+            check(lib().ms_model_open_gguf(ctx.h, path.encode(), max_seq_len, ep_rank, ep_size, C.byref(h)), ctx.h)
         return cls(h, ctx)
+
+    def expert_tier_stats(self):
+        """(hits, misses) of the host-tier expert slots"""
+        hits, misses = C.c_uint64(), C.c_uint64()
+        check(lib().ms_model_expert_tier_stats(self.h, C.byref(hits), C.byref(misses)), self.ctx.h)
+        return hits.value, misses.value
 
     @classmethod
     def from_model(cls, m: G.Model, max_seq_len: int = 4096, device: int = 0, ep_rank: int = 0, ep_size: int = 1,
-                   ctx: Optional[Context] = None, attn_splits: int = 0) -> "Engine":
+                   ctx: Optional[Context] = None, attn_splits: int = 0, expert_slots: int = 0) -> "Engine":
         """Upload an in-memory GGUF model (native block layouts) without writing a file."""
         ctx = ctx or Context(device)
         cfg = config_from_model(m, max_seq_len, ep_rank, ep_size)
@@ -243,6 +256,8 @@ class Engine:
         h = C.c_void_p()
         check(lib().ms_model_create(ctx.h, C.byref(cfg), C.byref(h)), ctx.h)
         try:
+            if expert_slots:
+                check(lib().ms_model_set_expert_tier(h, expert_slots), ctx.h)
             for name, t in m.tensors.items():
                 raw = t.raw()
                 dims = (C.c_int64 * len(t.shape))(*t.shape)
