@@ -63,6 +63,7 @@ def test_host_tier_matches_resident_experts(ctx, tmp_path, spec_name, slots):
     prompt = synth.prompt_ids(spec, 6, seed=5)
     n_new = 16
     res = Engine.open(path, max_seq_len=64, ctx=ctx)
+    res.set_prefill(0)   # one decode step per prompt token, as the tiered model runs its prompt
     want = res.generate(prompt, n_new)
     res.clear_cache()
     want_logits = res.forward(prompt)
