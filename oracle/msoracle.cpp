@@ -368,21 +368,64 @@ void rope_apply(float* x, int rot_dim, const float* c, const float* s) {
 
 // ---------------------------------------------------------------------------
 // MoE FFN (layer.rs:756-1895, default f32 path)
+// Router entropy (layer.rs:2302-2325): Shannon entropy of softmax(logits) per token, averaged over
+// the tokens of the call; exp and ln rounded from double, sums in double rounded once.
+float router_entropy(const float* logits, int n_tok, int E) {
+  double total = 0.0;
+  for (int t = 0; t < n_tok; ++t) {
+    const float* row = logits + (size_t)t * E;
+    float mx = -INFINITY;
+    for (int e = 0; e < E; ++e) mx = std::max(mx, row[e]);
+    std::vector<float> ex(E);
+    double s64 = 0.0;
+    for (int e = 0; e < E; ++e) { ex[e] = expcr(row[e] - mx); s64 += ex[e]; }
+    const float s = round_f32(s64);
+    double h64 = 0.0;
+    for (int e = 0; e < E; ++e) {
+      const float p = ex[e] / s;
+      if (p > 0.0f) h64 += (double)(p * (float)std::log((double)p));
+    }
+    total += (double)(-round_f32(h64));
+  }
+  return round_f32(total) / (float)n_tok;
+}
+
+// entropy_to_k (layer.rs:2329-2334): linear map of entropy / ln(E) onto [k_min, k_max], rounded
+int entropy_to_k(float entropy, int E, int k_min, int k_max) {
+  const float h_max = (float)std::log((double)E);
+  const float norm = std::min(std::max(entropy / h_max, 0.0f), 1.0f);
+  const float k = (float)k_min + norm * (float)(k_max - k_min);
+  return std::min(std::max((int)std::round(k), k_min), k_max);
+}
+
 int moe_forward(const orc_moe_layer* L, const float* x, int n_tok, float* out, int32_t* idx_out, float* w_out,
                 const std::vector<int>* dummies, int threads, int e_begin = 0, int e_end = 1 << 30,
-                float* last_logits = nullptr) {
-  const int H = L->hidden, I = L->inter, E = L->n_experts, K = L->top_k;
+                float* last_logits = nullptr, int dk_min = 0, int dk_max = 0, float* ent_out = nullptr,
+                int* k_out = nullptr) {
+  const int H = L->hidden, I = L->inter, E = L->n_experts, Kslots = L->top_k;
   std::vector<float> logits((size_t)n_tok * E);
   matmul_xwt(x, n_tok, L->router_w, E, H, logits.data(), threads);       // layer.rs:818-820
   if (L->router_b)                                                       // layer.rs:832-837
     for (int t = 0; t < n_tok; ++t) for (int e = 0; e < E; ++e) logits[(size_t)t * E + e] += L->router_b[e];
+  // entropy before the dummy mask; dynamic K from it (layer.rs:980-1011): one K for the call
+  int K = Kslots;
+  if (ent_out || dk_max > 0) {
+    const float ent = router_entropy(logits.data(), n_tok, E);
+    if (ent_out) *ent_out = ent;
+    if (dk_max > 0) K = entropy_to_k(ent, E, dk_min, dk_max);
+  }
+  if (k_out) *k_out = K;
   if (dummies)                                                           // layer.rs:1016-1026
     for (int t = 0; t < n_tok; ++t) for (int d : *dummies) logits[(size_t)t * E + d] += -INFINITY;
   if (last_logits) std::memcpy(last_logits, &logits[(size_t)(n_tok - 1) * E], (size_t)E * 4);
   std::vector<int32_t> idx((size_t)n_tok * K); std::vector<float> wts((size_t)n_tok * K);
   top_k_routing(logits.data(), n_tok, E, K, L->norm_topk_prob != 0, L->oai_swiglu != 0, idx.data(), wts.data());
-  if (idx_out) std::memcpy(idx_out, idx.data(), idx.size() * 4);
-  if (w_out) std::memcpy(w_out, wts.data(), wts.size() * 4);
+  // [n_tok][slots] outputs; slots beyond a dynamic K hold expert id E (none) and weight 0
+  for (int t = 0; t < n_tok; ++t)
+    for (int j = 0; j < Kslots; ++j) {
+      if (idx_out) idx_out[(size_t)t * Kslots + j] = j < K ? idx[(size_t)t * K + j] : E;
+      if (w_out) w_out[(size_t)t * Kslots + j] = j < K ? wts[(size_t)t * K + j] : 0.0f;
+    }
   // expert -> [(token, weight)] in (t, k) order; unique experts ascending (layer.rs:1092-1106)
   std::map<int, std::vector<std::pair<int, float>>> assign;
   for (int t = 0; t < n_tok; ++t)
@@ -544,6 +587,7 @@ struct orc_model {
     // shared expert (layer.rs:1898-1953, 2250-2293)
     const GTensor *sh_gate = nullptr, *sh_up = nullptr, *sh_down = nullptr;
     const float* sh_gate_inp = nullptr;
+    int dk_lo = 0, dk_hi = 0;   // dynamic K range of this layer (0, 0: fixed top_k)
   };
   std::vector<Layer> L;
   const GTensor *embd = nullptr, *out = nullptr; const float* out_norm = nullptr; const float* out_bias = nullptr;
@@ -552,6 +596,9 @@ struct orc_model {
   // per layer, last position of the last forward: residual stream after the layer [layers][H]
   // and the router logits after bias and dummy mask [layers][E] (test diagnostics)
   std::vector<float> layer_hidden, layer_logits;
+  // router entropy and the K used, per layer, of the last forward (layer.rs:980-1011)
+  std::vector<float> last_entropy;
+  std::vector<int> last_k;
 };
 
 namespace {
@@ -910,6 +957,32 @@ orc_model* orc_model_open(const char* path, int max_seq_len, char* err, int err_
 }
 
 void orc_model_set_attn_mode(orc_model* m, int mode) { m->attn_mode = mode; }
+
+// Dynamic K (config.rs:183-192, 468-483; LayerTierConfig::default_for_k, config.rs:86-106): per layer
+// the range [k_min, k_max], or with layer_adaptive the depth tier's range for k_max.
+int orc_model_set_dynamic_k(orc_model* m, int enable, int k_min, int k_max, int layer_adaptive) {
+  if (!enable) { for (auto& l : m->L) l.dk_lo = l.dk_hi = 0; return 0; }
+  if (k_min < 1 || k_max < k_min || k_max > m->top_k) return -1;
+  const int two_thirds = std::min(std::max(k_max * 2 / 3, 4), k_max);
+  for (int li = 0; li < m->layers; ++li) {
+    int lo = k_min, hi = k_max;
+    if (layer_adaptive) {
+      const float depth = (float)li / (float)m->layers;
+      if (depth < 0.15f) { lo = k_max; hi = k_max; }
+      else if (depth < 0.85f) { lo = std::min(4, k_max); hi = two_thirds; }
+      else { lo = two_thirds; hi = k_max; }
+    }
+    m->L[li].dk_lo = lo; m->L[li].dk_hi = hi;
+  }
+  return 0;
+}
+
+void orc_model_router_stats(const orc_model* m, float* entropy, int32_t* k) {
+  for (int li = 0; li < m->layers; ++li) {
+    if (entropy) entropy[li] = m->last_entropy.empty() ? 0.0f : m->last_entropy[li];
+    if (k) k[li] = m->last_k.empty() ? 0 : m->last_k[li];
+  }
+}
 void orc_model_set_threads(orc_model* m, int n) { m->threads = n; }
 int orc_model_vocab(const orc_model* m) { return m->vocab; }
 int orc_model_hidden(const orc_model* m) { return m->hidden; }
@@ -967,6 +1040,7 @@ int orc_model_forward(orc_model* m, const int32_t* tokens, int n, float* logits)
   m->last_idx.assign((size_t)m->layers * K, 0); m->last_w.assign((size_t)m->layers * K, 0.0f);
   const int E = m->experts;
   m->layer_hidden.assign((size_t)m->layers * H, 0.0f); m->layer_logits.assign((size_t)m->layers * E, 0.0f);
+  m->last_entropy.assign(m->layers, 0.0f); m->last_k.assign(m->layers, 0);
   std::vector<int32_t> idx((size_t)n * K); std::vector<float> w((size_t)n * K);
   for (int li = 0; li < m->layers; ++li) {  // layer.rs:393-503
     auto& Ly = m->L[li];
@@ -982,7 +1056,7 @@ int orc_model_forward(orc_model* m, const int32_t* tokens, int n, float* logits)
     for (size_t i = 0; i < h.size(); ++i) h[i] = h[i] + tmp[i];
     rms_norm(h.data(), Ly.post_norm, xn.data(), n, H, m->eps);
     moe_forward(&Ly.moe, xn.data(), n, tmp.data(), idx.data(), w.data(), &Ly.dummies, th, 0, 1 << 30,
-                &m->layer_logits[(size_t)li * E]);
+                &m->layer_logits[(size_t)li * E], Ly.dk_lo, Ly.dk_hi, &m->last_entropy[li], &m->last_k[li]);
     if (Ly.sh_gate)   // routed output + shared expert output (layer.rs:910-922), per token
       for (int t = 0; t < n; ++t)
         if (orc_shared_expert(Ly.sh_gate->qtype, Ly.sh_gate->data, Ly.sh_up->data, Ly.sh_down->qtype, Ly.sh_down->data,

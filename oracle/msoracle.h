@@ -138,6 +138,12 @@ void orc_model_last_routing(const orc_model* m, int32_t* idx, float* w);
 void orc_model_layer_trace(const orc_model* m, float* hidden, float* logits);
 /* final norm + LM head of one hidden vector [hidden] -> logits [vocab] (timing / tests) */
 void orc_model_lm_head(orc_model* m, const float* hidden, float* logits);
+/* dynamic K (layer.rs:947-1011, config.rs:183-192, 468-483): per-token K from router entropy in
+ * [k_min, k_max] (or the depth tier's range when layer_adaptive), k_max <= the model's top_k; slots
+ * beyond K report expert id n_experts.  Returns 0, or -1 for an invalid range. */
+int orc_model_set_dynamic_k(orc_model* m, int enable, int k_min, int k_max, int layer_adaptive);
+/* router entropy and the K used per layer of the last forward [layers] (either may be NULL) */
+void orc_model_router_stats(const orc_model* m, float* entropy, int32_t* k);
 void orc_model_destroy(orc_model* m);
 
 #ifdef __cplusplus

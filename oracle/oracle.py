@@ -84,6 +84,9 @@ def lib():
         L.orc_model_open.restype = _vp
         L.orc_model_open.argtypes = [C.c_char_p, C.c_int, C.c_char_p, C.c_int]
         L.orc_model_set_attn_mode.argtypes = [_vp, C.c_int]
+        L.orc_model_set_dynamic_k.argtypes = [_vp, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.orc_model_set_dynamic_k.restype = C.c_int
+        L.orc_model_router_stats.argtypes = [_vp, _fp, _i32p]
         L.orc_model_set_threads.argtypes = [_vp, C.c_int]
         L.orc_model_forward.argtypes = [_vp, _i32p, C.c_int, _fp]
         L.orc_model_generate.argtypes = [_vp, _i32p, C.c_int, C.c_int, _i32p]
@@ -347,6 +350,17 @@ class Model:
         w = np.empty(layers * k, np.float32)
         lib().orc_model_last_routing(self.h, _i(idx), _f(w))
         return idx.reshape(layers, k), w.reshape(layers, k)
+
+    def set_dynamic_k(self, enable: bool, k_min: int = 2, k_max: int = 0, layer_adaptive: bool = False):
+        if lib().orc_model_set_dynamic_k(self.h, int(enable), k_min, k_max, int(layer_adaptive)) != 0:
+            raise ValueError("invalid dynamic-K range")
+
+    def router_stats(self, layers: int):
+        """(router entropy [layers] f32, K used [layers]) of the last forward"""
+        ent = np.empty(layers, np.float32)
+        k = np.empty(layers, np.int32)
+        lib().orc_model_router_stats(self.h, _f(ent), _i(k))
+        return ent, k
 
     def layer_trace(self, layers: int, experts: int):
         """(hidden after each layer [layers, H], router logits per layer [layers, E]), last position"""
