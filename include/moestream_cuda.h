@@ -313,6 +313,21 @@ MS_API ms_status ms_model_ep_connect(ms_model* m, const void* handles, size_t by
 /* Parse a GGUF file (reader.rs:259-368, config.rs:253-434) and upload everything. */
 MS_API ms_status ms_model_open_gguf(ms_ctx* ctx, const char* path, int max_seq_len, int ep_rank, int ep_size,
                              ms_model** out);
+/* Dynamic K (layer.rs:947-1011, entropy_to_k layer.rs:2329-2334; config.rs:183-192, 468-483): each
+ * decode step's router computes the entropy H of softmax(router logits) per layer and routes
+ * K = round(k_lo + clamp(H / ln E, 0, 1) (k_hi - k_lo)) experts, k_lo / k_hi = [k_min, k_max], or with
+ * layer_adaptive the depth tier of LayerTierConfig::default_for_k(k_max) (first 15 % of layers
+ * [k_max, k_max], up to 85 % [min(4, k_max), max(4, 2 k_max / 3)], then [max(4, 2 k_max / 3), k_max]).
+ * 1 <= k_min <= k_max <= top_k; slots past K report expert id n_experts and weight 0.  Every prompt
+ * token is then its own step (the reference takes one K per forward call from the mean entropy of
+ * its tokens, which is the same for one-token calls).  Not with the lockstep batch. */
+MS_API ms_status ms_model_set_dynamic_k(ms_model* m, int enable, int k_min, int k_max, int layer_adaptive);
+/* Router statistics (the entropy_out / routing_stats_out of LayerForward::forward, layer.rs:393-503):
+ * enable != 0 makes every later step record each layer's router entropy and the K it routed;
+ * ms_model_router_stats reads those of the last step, entropy [layers] and k [layers] (either may be
+ * NULL).  The routed ids and weights themselves come from ms_model_last_routing. */
+MS_API ms_status ms_model_set_router_stats(ms_model* m, int enable);
+MS_API ms_status ms_model_router_stats(ms_model* m, float* entropy, int32_t* k);
 /* Host-tier expert streaming (the reference's SSD / mmap streaming mode with its per-layer expert LRU,
  * gguf/reader.rs:631-858, model/layer.rs:1146-1152, 1777-1784, model/cache.rs:84-158).  Call after
  * ms_model_create and before the expert tensors are set: every layer's K-quant expert stacks (Q4_K /

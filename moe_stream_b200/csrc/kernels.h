@@ -141,6 +141,15 @@ struct RouterArgs {
   uint8_t* xbt = nullptr;         // optional: the normed x as exact B terms ([H/32][exact_term_block_bytes()],
   int* xfe = nullptr;             //   zeroed once) and their scale exponents [H/32]
   int batch = 1;                  // grid.y = tokens: h/xn + b*H, logits + b*E, idx/wts + b*K, counter + b
+  // router statistics and dynamic K (layer.rs:947-1011, 2302-2334; one token, batch 1 only):
+  // with `raw` set every CTA also stores its logit before the dummy mask, and the selecting warp
+  // writes the entropy of softmax(raw) to *entropy; k_hi > 0 then routes only
+  // K' = round(k_lo + clamp(H / ln E, 0, 1) (k_hi - k_lo)) experts (k_hi <= K), the other slots
+  // get expert id E (none) and weight 0; *k_used = the K routed
+  float* raw = nullptr;           // [E]
+  float* entropy = nullptr;
+  int* k_used = nullptr;
+  int k_lo = 0, k_hi = 0;
 };
 cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s);
 

@@ -981,10 +981,48 @@ __device__ __forceinline__ void router_select_t(const RouterArgs& a, uint32_t* e
     const int i = lane + 32 * j;
     lv[j] = i < a.E ? __ldcg(&a.logits[i]) : -INFINITY;
   }
+  // router entropy over the unmasked logits, and the dynamic K it selects (layer.rs:980-1011,
+  // 2302-2334): exp and ln rounded from double, sums in double rounded once
+  int K = a.K;
+  if (a.raw) {
+    float rv[kPer];
+    float rmx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = lane + 32 * j;
+      rv[j] = i < a.E ? __ldcg(&a.raw[i]) : -INFINITY;
+      rmx = fmaxf(rmx, rv[j]);
+    }
+    rmx = warp_max(rmx);
+    double es = 0.0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      rv[j] = lane + 32 * j < a.E ? expcr(__fsub_rn(rv[j], rmx)) : 0.f;
+      es += (double)rv[j];
+    }
+    const float s32 = (float)warp_sum_d(es);
+    double hs = 0.0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const float p = __fdiv_rn(rv[j], s32);
+      if (p > 0.f) hs += (double)__fmul_rn(p, (float)log((double)p));
+    }
+    const float ent = -(float)warp_sum_d(hs);
+    if (a.k_hi > 0) {   // entropy_to_k
+      const float hmax = (float)log((double)a.E);
+      const float nrm = fminf(fmaxf(__fdiv_rn(ent, hmax), 0.f), 1.f);
+      const float kf = __fadd_rn((float)a.k_lo, __fmul_rn(nrm, (float)(a.k_hi - a.k_lo)));
+      K = min(max((int)roundf(kf), a.k_lo), a.k_hi);
+    }
+    if (lane == 0) {
+      if (a.entropy) *a.entropy = ent;
+      if (a.k_used) *a.k_used = K;
+    }
+  }
   uint32_t taken = 0u;
   float sel_v[kMaxK];
   int sel_i[kMaxK];
-  for (int k = 0; k < a.K; ++k) {
+  for (int k = 0; k < K; ++k) {
     float best = -INFINITY;
     int bidx = 0x7fffffff;
 #pragma unroll
@@ -1011,12 +1049,12 @@ __device__ __forceinline__ void router_select_t(const RouterArgs& a, uint32_t* e
   float w[kMaxK];
   if (a.softmax_weight) {              // layer.rs:2361-2372: softmax over the selected logits
     float mx = -INFINITY;
-    for (int k = 0; k < a.K; ++k) mx = fmaxf(mx, sel_v[k]);
+    for (int k = 0; k < K; ++k) mx = fmaxf(mx, sel_v[k]);
     double sum = 0.0;
-    for (int k = 0; k < a.K; ++k) { w[k] = expcr(__fsub_rn(sel_v[k], mx)); }
-    for (int k = 0; k < a.K; ++k) sum += (double)w[k];
+    for (int k = 0; k < K; ++k) { w[k] = expcr(__fsub_rn(sel_v[k], mx)); }
+    for (int k = 0; k < K; ++k) sum += (double)w[k];
     const float s32 = (float)sum;
-    for (int k = 0; k < a.K; ++k) w[k] = __fdiv_rn(w[k], s32);
+    for (int k = 0; k < K; ++k) w[k] = __fdiv_rn(w[k], s32);
   } else {                              // layer.rs:2374-2394: softmax over all, then (re)normalise
     float mx = -INFINITY;
 #pragma unroll
@@ -1028,13 +1066,14 @@ __device__ __forceinline__ void router_select_t(const RouterArgs& a, uint32_t* e
       if (lane + 32 * j < a.E) sum += (double)expcr(__fsub_rn(lv[j], mx));
     const float s32 = (float)warp_sum_d(sum);
     double ts = 0.0;
-    for (int k = 0; k < a.K; ++k) { w[k] = __fdiv_rn(expcr(__fsub_rn(sel_v[k], mx)), s32); }
-    for (int k = 0; k < a.K; ++k) ts += (double)w[k];
+    for (int k = 0; k < K; ++k) { w[k] = __fdiv_rn(expcr(__fsub_rn(sel_v[k], mx)), s32); }
+    for (int k = 0; k < K; ++k) ts += (double)w[k];
     const float t32 = (float)ts;
-    if (a.normalize) for (int k = 0; k < a.K; ++k) w[k] = __fdiv_rn(w[k], t32);
+    if (a.normalize) for (int k = 0; k < K; ++k) w[k] = __fdiv_rn(w[k], t32);
   }
   if (lane == 0) {
-    for (int k = 0; k < a.K; ++k) { a.idx[k] = sel_i[k]; a.wts[k] = w[k]; }
+    for (int k = 0; k < K; ++k) { a.idx[k] = sel_i[k]; a.wts[k] = w[k]; }
+    for (int k = K; k < a.K; ++k) { a.idx[k] = a.E; a.wts[k] = 0.f; }   // slots past a dynamic K: none
     *a.counter = 0u;
   }
 }
@@ -1092,6 +1131,7 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, ui
     for (int w = 0; w < kRouterThreads / 32; ++w) t += redd[w];
     float v = (float)t;
     if (a.b) v = __fadd_rn(v, a.b[e]);
+    if (a.raw) a.raw[e] = v;   // before the dummy mask (the reference's entropy sees these)
     if (a.mask && a.mask[e]) v = -INFINITY;
     a.logits[e] = v;
     __threadfence();
@@ -1229,6 +1269,8 @@ cudaError_t launch_moe_combine(const DevCtx& c, const PendingCombine& pc, int H,
 }
 
 cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s) {
+  if (a.raw && (a.batch != 1 || (a.k_hi > 0 && (a.k_lo < 1 || a.k_lo > a.k_hi || a.k_hi > a.K))))
+    return cudaErrorInvalidValue;
   if (a.K < 1 || a.K > kMaxK || a.K > a.E || a.E > kRouterMaxE || !a.counter || a.batch < 1 ||
       (a.batch > 1 && (a.xterm || a.xbt)) || (a.xbt && (a.H % 32 || !a.xfe)))
     return cudaErrorInvalidValue;

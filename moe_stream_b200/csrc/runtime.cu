@@ -161,6 +161,7 @@ struct LayerW {
   int dn_in_q = -1;
   uint8_t* sh_gu = nullptr;
   int sh_gu_q = -1, sh_gu_rows = 0;
+  int dk_lo = 0, dk_hi = 0;         // dynamic K range of this layer (ms_model_set_dynamic_k), 0: off
 };
 
 // NCCL is resolved at run time (dlopen), so a process that already loaded libnccl (torch does)
@@ -315,6 +316,11 @@ struct ms_model {
   uint64_t tier_hits = 0, tier_misses = 0, tier_clock = 0;
   int* h_wslot = nullptr;           // pinned [layers][16] staging of the slot tables
   int* h_tier_idx = nullptr;        // pinned [16] routed ids read back per layer
+  // router statistics / dynamic K: unmasked logits [E], per-layer entropy and K of the last step
+  bool router_stats = false, dyn_k = false;
+  float* r_raw = nullptr;
+  float* r_entropy = nullptr;
+  int* r_k = nullptr;
   int sh_max = 0;                   // widest shared expert (0: none)
   struct Prefill {
     int cap = 0;                       // tokens the buffers hold
@@ -418,6 +424,7 @@ ms_status tier_fetch(ms_model* m, int li, cudaStream_t s) {
   bool hit[16];
   for (int k = 0; k < K; ++k) {
     const int e = m->h_tier_idx[k];
+    if (e == c.experts) { hit[k] = true; ws[k] = 0; continue; }   // a slot past a dynamic K: no expert
     if (e < 0 || e >= m->n_local) return fail(m->ctx, MS_ERR_DEVICE_INDEX, "layer %d: routed expert %d out of range", li, e);
     hit[k] = false;
     for (int j = 0; j < C; ++j)
@@ -793,6 +800,10 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     ra.mask = Lw.mask; ra.logits = m->router_logits; ra.idx = Lw.idx; ra.wts = Lw.wts; ra.counter = m->router_cnt;
     ra.H = H; ra.E = c.experts; ra.K = c.top_k; ra.softmax_weight = c.arch == MS_ARCH_GPT_OSS;
     ra.normalize = c.norm_topk_prob;
+    if (m->router_stats || m->dyn_k) {   // entropy of the routing (and dynamic K), layer.rs:980-1011
+      ra.raw = m->r_raw; ra.entropy = m->r_entropy + li; ra.k_used = m->r_k + li;
+      if (m->dyn_k) { ra.k_lo = Lw.dk_lo; ra.k_hi = Lw.dk_hi; }
+    }
     if (Lw.tc && m->exact) {
       ra.xbt = m->ex_xbt;
       ra.xfe = m->ex_xfe;
@@ -1070,6 +1081,7 @@ bool pf_supported(const ms_model* m) {
   // such models take one decode step per prompt token
   if (is_hybrid(c) || m->sh_max > 0) return false;
   if (m->tier_slots > 0) return false;   // host-tier experts: the expert kernels read HBM slots
+  if (m->dyn_k || m->router_stats) return false;   // the batched router has no entropy / dynamic K
   if (c.hidden % 32 || (c.heads * c.head_dim) % 32 || c.head_dim % 32 || c.head_dim > 256) return false;
   return true;
 }
@@ -1948,6 +1960,9 @@ ms_status ms_model_finalize(ms_model* m) {
   s = s ? s : m->alloc(&m->ex_kgu, (size_t)c.top_k * 2 * c.inter * 4);
   s = s ? s : m->alloc(&m->xn_final, (size_t)H * 4);
   s = s ? s : m->alloc(&m->ref_scratch, (size_t)exact_refine_scratch_ints(1) * 4);
+  s = s ? s : m->alloc(&m->r_raw, (size_t)c.experts * 4);
+  s = s ? s : m->alloc(&m->r_entropy, (size_t)c.layers * 4);
+  s = s ? s : m->alloc(&m->r_k, (size_t)c.layers * 4);
   if (is_hybrid(c)) {   // gated attention: [Q_h, gate_h] projection, then the gate
     s = s ? s : m->alloc(&m->q_raw, (size_t)(q_rows(c) + 2 * Dkv) * 4);
     s = s ? s : m->alloc(&m->q_gate, (size_t)Dq * 4);
@@ -2015,6 +2030,7 @@ ms_status ms_model_batch_open(ms_model* m, int B) {
   if (is_hybrid(c) || m->sh_max > 0)
     return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE, "batched decode covers attention + routed-expert layers only");
   if (m->tier_slots > 0) return fail(m->ctx, MS_ERR_STATE, "batched decode needs HBM-resident experts (no host tier)");
+  if (m->dyn_k || m->router_stats) return fail(m->ctx, MS_ERR_STATE, "batched decode has no dynamic K / router statistics");
   for (int li = 0; li < c.layers; ++li)
     if (m->L[li].tc || !m->L[li].gate)
       return fail(m->ctx, MS_ERR_UNSUPPORTED_QTYPE,
@@ -2637,6 +2653,51 @@ ms_status ms_model_set_expert_tier(ms_model* m, int slots) {
   m->tier_slots = std::min(slots, m->n_local);
   m->tier.assign(c.layers, ms_model::TierLayer{});
   return MS_OK;
+}
+
+ms_status ms_model_set_dynamic_k(ms_model* m, int enable, int k_min, int k_max, int layer_adaptive) {
+  if (!m) return MS_ERR_INVALID_ARG;
+  const ms_model_config& c = m->cfg;
+  if (!m->finalized) return fail(m->ctx, MS_ERR_STATE, "dynamic K after finalize");
+  if (enable && (k_min < 1 || k_max < k_min || k_max > c.top_k))
+    return fail(m->ctx, MS_ERR_INVALID_ARG, "dynamic K range [%d, %d] must lie in [1, top_k %d]", k_min, k_max, c.top_k);
+  if (enable && m->bt) return fail(m->ctx, MS_ERR_STATE, "dynamic K with an open batch");
+  MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+  m->dyn_k = enable != 0;
+  // LayerTierConfig::default_for_k (config.rs:86-106) and get_layer_k_range (config.rs:473-483)
+  const int two_thirds = std::min(std::max(k_max * 2 / 3, 4), k_max);
+  for (int li = 0; li < c.layers; ++li) {
+    int lo = k_min, hi = k_max;
+    if (layer_adaptive) {
+      const float depth = (float)li / (float)c.layers;
+      if (depth < 0.15f) { lo = k_max; hi = k_max; }
+      else if (depth < 0.85f) { lo = std::min(4, k_max); hi = two_thirds; }
+      else { lo = two_thirds; hi = k_max; }
+    }
+    m->L[li].dk_lo = enable ? lo : 0;
+    m->L[li].dk_hi = enable ? hi : 0;
+  }
+  if (m->graph) { cudaGraphExecDestroy(m->graph); m->graph = nullptr; }
+  return MS_OK;
+}
+
+ms_status ms_model_set_router_stats(ms_model* m, int enable) {
+  if (!m) return MS_ERR_INVALID_ARG;
+  if (!m->finalized) return fail(m->ctx, MS_ERR_STATE, "router statistics after finalize");
+  if (enable && m->bt) return fail(m->ctx, MS_ERR_STATE, "router statistics with an open batch");
+  MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
+  m->router_stats = enable != 0;
+  if (m->graph) { cudaGraphExecDestroy(m->graph); m->graph = nullptr; }
+  return MS_OK;
+}
+
+ms_status ms_model_router_stats(ms_model* m, float* entropy, int32_t* k) {
+  if (!m || (!entropy && !k)) return MS_ERR_INVALID_ARG;
+  if (!m->router_stats && !m->dyn_k) return fail(m->ctx, MS_ERR_STATE, "router statistics are off");
+  cudaStream_t s = m->ctx->stream;
+  if (entropy) MS_CUDA(m->ctx, cudaMemcpyAsync(entropy, m->r_entropy, (size_t)m->cfg.layers * 4, cudaMemcpyDeviceToHost, s));
+  if (k) MS_CUDA(m->ctx, cudaMemcpyAsync(k, m->r_k, (size_t)m->cfg.layers * 4, cudaMemcpyDeviceToHost, s));
+  return ms_sync(m->ctx);
 }
 
 ms_status ms_model_expert_tier_stats(const ms_model* m, uint64_t* hits, uint64_t* misses) {

@@ -240,6 +240,23 @@ class Engine:
             check(lib().ms_model_open_gguf(ctx.h, path.encode(), max_seq_len, ep_rank, ep_size, C.byref(h)), ctx.h)
         return cls(h, ctx)
 
+    def set_dynamic_k(self, enable: bool, k_min: int = 2, k_max: int = 0, layer_adaptive: bool = False) -> None:
+        """per-step K from router entropy (layer.rs:947-1011); k_max 0 = the model's top_k"""
+        check(lib().ms_model_set_dynamic_k(self.h, int(enable), k_min, k_max or self.config.top_k,
+                                           int(layer_adaptive)), self.ctx.h)
+
+    def set_router_stats(self, enable: bool) -> None:
+        check(lib().ms_model_set_router_stats(self.h, int(enable)), self.ctx.h)
+
+    def router_stats(self):
+        """(router entropy [layers], K routed [layers]) of the last step"""
+        n = self.config.layers
+        ent = np.empty(n, np.float32)
+        k = np.empty(n, np.int32)
+        check(lib().ms_model_router_stats(self.h, ent.ctypes.data_as(C.POINTER(C.c_float)),
+                                          k.ctypes.data_as(C.POINTER(C.c_int32))), self.ctx.h)
+        return ent, k
+
     def expert_tier_stats(self):
         """(hits, misses) of the host-tier expert slots"""
         hits, misses = C.c_uint64(), C.c_uint64()
