@@ -70,7 +70,7 @@ def test_ep_decomposition_gloo(orc, tmp_path):
     assert np.abs(got - full).max() / np.abs(full).max() < 1e-5
 
 
-def _gpu_rank(rank, world, port, path, prompt, out_dir, exchange):
+def _gpu_rank(rank, world, port, path, prompt, out_dir, exchange, n_new=16):
     import torch
     import torch.distributed as dist
     from moe_stream_b200.engine import Context, Engine
@@ -85,7 +85,7 @@ def _gpu_rank(rank, world, port, path, prompt, out_dir, exchange):
         dist.broadcast_object_list(uid, src=0)
         eng.init_ep(uid[0])
     eng.set_prefill(0)   # the prompt through the decode step, as on one device
-    toks = eng.generate(prompt, 16)
+    toks = eng.generate(prompt, n_new)
     np.save(os.path.join(out_dir, f"tok{rank}.npy"), np.array(toks, np.int32))
     eng.close()
     ctx.close()
@@ -106,3 +106,21 @@ def test_ep_two_gpus_greedy_tokens(tmp_path, exchange):
              join=True)
     for r in range(2):
         assert np.load(str(tmp_path / f"tok{r}.npy")).tolist() == f["tiny_gpt_oss_tokens"].tolist()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+def test_ep_two_gpus_hybrid_model(tmp_path, exchange):
+    """configs[3]'s partition at small scale: the tiny Qwen3-Next hybrid (64 experts top-10, shared
+    expert, DeltaNet and gated-attention layers replicated) split 32 + 32 experts over two GPUs
+    decodes the one-device oracle's greedy tokens (tests/golden/tiny_qwen3_next.npz)"""
+    import torch
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    f = np.load(os.path.join(GOLD, "tiny_qwen3_next.npz"))
+    path = str(tmp_path / "hyb.gguf")
+    synth.write_model(path, synth.TINY_QWEN3_NEXT, seed=11)
+    mp.spawn(_gpu_rank, args=(2, _free_port(), path, f["prompt"], str(tmp_path), exchange, 16), nprocs=2, join=True)
+    for r in range(2):
+        assert np.load(str(tmp_path / f"tok{r}.npy")).tolist() == f["tokens"][:16].tolist()
