@@ -13,6 +13,7 @@ from moe_stream_b200 import gguf as G
 from moe_stream_b200 import synth
 
 from . import hybrid_synth as hs
+from .moe_ref import moe_with_routing
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -187,6 +188,8 @@ def test_router_and_moe_layer(ctx, orc, spec):
         assert got_idx.tolist() == want_idx[0].tolist()
         np.testing.assert_allclose(wts.cpu().numpy(), want_w[0], rtol=1e-5)
         assert rel_err(out.cpu().numpy(), want[0]) < REL_TOL
+    else:   # a near-tie: the layer on the GPU's own routing against the float64 restatement
+        assert rel_err(out.cpu().numpy(), moe_with_routing(orc, L, x, got_idx, wts.cpu().numpy())) < REL_TOL
     del h0, d_h, ones
 
 
@@ -259,6 +262,8 @@ def test_moe_packed_scale_range_and_residual(ctx, orc):
                          dev(x), dev(idx), dev(wts), ref)
     ctx.sync()
     assert rel_err(d_h.cpu().numpy() - h, ref.cpu().numpy() - h) < 1e-5
+    # and against the float64 restatement: the repeated expert counts once per slot (layer.rs:1415, 1822)
+    assert rel_err(d_h.cpu().numpy() - h, moe_with_routing(orc, L, x, idx, wts)) < REL_TOL
     assert ctx.error_flags() == 0
 
 
