@@ -70,6 +70,57 @@ def test_ep_decomposition_gloo(orc, tmp_path):
     assert np.abs(got - full).max() / np.abs(full).max() < 1e-5
 
 
+def _hybrid_layer(seed):
+    spec = synth.TINY_QWEN3_NEXT
+    m = synth.build_model(spec, seed, only=lambda n: n.startswith("blk.0.ffn"))
+    t = lambda n: m.tensors["blk.0." + n]
+    L = dict(hidden=spec.hidden, inter=spec.inter, n_experts=spec.experts, top_k=spec.top_k,
+             gate_q=spec.expert_gate_q, up_q=spec.expert_gate_q, down_q=spec.expert_down_q,
+             gate=t("ffn_gate_exps.weight").raw(), up=t("ffn_up_exps.weight").raw(),
+             down=t("ffn_down_exps.weight").raw(), router_w=t("ffn_gate_inp.weight").data.astype(np.float32),
+             oai_swiglu=0, norm_topk_prob=1)
+    sh = (t("ffn_gate_shexp.weight"), t("ffn_up_shexp.weight"), t("ffn_down_shexp.weight"),
+          t("ffn_gate_inp_shexp.weight").data.astype(np.float32))
+    return spec, L, sh
+
+
+def _shared(orc, spec, sh, x, y):
+    g, u, d, gi = sh
+    return orc.shared_expert(g.qtype, g.raw(), u.raw(), d.qtype, d.raw(), gi, spec.hidden, spec.shared_inter, x, y)
+
+
+def _cpu_rank_hybrid(rank, world, port, out_path):
+    import torch
+    import torch.distributed as dist
+    from oracle import oracle
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    spec, L, sh = _hybrid_layer(6)
+    x = np.random.default_rng(9).standard_normal(spec.hidden).astype(np.float32)
+    per = spec.experts // world
+    local, _, _ = oracle.moe_forward(L, x, expert_range=(rank * per, (rank + 1) * per))
+    t = torch.from_numpy(local.reshape(-1).copy())
+    dist.all_reduce(t)                                       # the routed experts' exchange
+    out = _shared(oracle, spec, sh, x, t.numpy().copy())     # the replicated shared expert, on every rank
+    np.save(out_path.replace(".npy", f"{rank}.npy"), out)
+    dist.destroy_process_group()
+
+
+def test_ep_decomposition_hybrid_gloo(orc, tmp_path):
+    """configs[3]'s partition on CPU ranks: 64 experts top-10 split over 2 ranks, shared expert
+    replicated and added after the routed exchange; every rank ends with the one-device layer"""
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "hy.npy")
+    mp.spawn(_cpu_rank_hybrid, args=(2, _free_port(), out), nprocs=2, join=True)
+    spec, L, sh = _hybrid_layer(6)
+    x = np.random.default_rng(9).standard_normal(spec.hidden).astype(np.float32)
+    full, idx, _ = orc.moe_forward(L, x)
+    assert len(set(idx[0].tolist()) & set(range(spec.experts // 2))) not in (0, spec.top_k)   # both ranks work
+    want = _shared(orc, spec, sh, x, full.reshape(-1).copy())
+    for r in range(2):
+        got = np.load(str(tmp_path / f"hy{r}.npy"))
+        assert np.abs(got - want).max() / np.abs(want).max() < 1e-5
+
+
 def _gpu_rank(rank, world, port, path, prompt, out_dir, exchange, n_new=16):
     import torch
     import torch.distributed as dist

@@ -163,3 +163,23 @@ def test_hybrid_layer_dispatch_matches_numpy(orc, hybrid):
         h = h + moe + hs.shared_expert_np(orc, sh, x.astype(np.float32))
         assert rel_err(o_hid[li], h) < 1e-4, f"layer {li}"
     assert [spec.is_attention_layer(li) for li in range(spec.layers)] == [False, False, False, True] * 2
+
+
+def test_engine_config_reads_hybrid_keys():
+    """host-side GGUF config of the Python binding (config.rs:318-352): interval, ssm shape, partial
+    rotary; and the defaults a file without the interval key but with SSM tensors gets"""
+    from moe_stream_b200.engine import config_from_model
+    spec = synth.TINY_QWEN3_NEXT
+    m = synth.build_model(spec, seed=1, only=lambda n: n.startswith("blk.0.") or n == "token_embd.weight")
+    c = config_from_model(m, max_seq_len=32)
+    assert (c.attn_interval, c.ssm_groups, c.ssm_state, c.ssm_dt_rank, c.ssm_inner, c.ssm_conv) == \
+        (4, spec.ssm_groups, spec.ssm_state, spec.ssm_dt_rank, spec.ssm_inner, spec.ssm_conv)
+    assert c.rot_dim == int(spec.head_dim * spec.rot_factor) == 64
+    del m.metadata[f"{spec.arch}.attention.full_attention_interval"]
+    del m.metadata[f"{spec.arch}.rope.partial_rotary_factor"]
+    m.add_meta(f"{spec.arch}.rope.dimension_count", G.T_U32, 128)
+    c = config_from_model(m, max_seq_len=32)
+    assert c.attn_interval == 4 and c.rot_dim == 128   # SSM tensors present: every 4th layer attention
+    plain = synth.build_model(synth.TINY_QWEN3, seed=1, only=lambda n: n == "token_embd.weight")
+    c = config_from_model(plain, max_seq_len=32)
+    assert c.attn_interval == 0 and c.rot_dim == synth.TINY_QWEN3.head_dim
