@@ -328,6 +328,15 @@ MS_API ms_status ms_model_set_dynamic_k(ms_model* m, int enable, int k_min, int 
  * NULL).  The routed ids and weights themselves come from ms_model_last_routing. */
 MS_API ms_status ms_model_set_router_stats(ms_model* m, int enable);
 MS_API ms_status ms_model_router_stats(ms_model* m, float* entropy, int32_t* k);
+/* Running totals since router statistics were last enabled (RoutingStatsCollector and EntropyProfiler,
+ * model/cache.rs:404-580, kept on the device and updated by every step's router): counts
+ * [layers][n_experts] times each expert was routed, weight_sums [layers][n_experts] the sum of its
+ * routing weights (f64, in step order), tokens [layers] steps seen, and entropy_log
+ * [min(steps, max_steps)][layers] each step's router entropy (the log holds max_seq_len steps);
+ * *n_steps = steps logged.  Any pointer may be NULL.  frequency = count / tokens, mean gate weight =
+ * weight_sum / count and importance = frequency x mean gate weight follow on the host. */
+MS_API ms_status ms_model_router_totals(ms_model* m, uint64_t* counts, double* weight_sums, uint64_t* tokens,
+                                        float* entropy_log, int max_steps, int* n_steps);
 /* Host-tier expert streaming (the reference's SSD / mmap streaming mode with its per-layer expert LRU,
  * gguf/reader.rs:631-858, model/layer.rs:1146-1152, 1777-1784, model/cache.rs:84-158).  Call after
  * ms_model_create and before the expert tensors are set: every layer's K-quant expert stacks (Q4_K /

@@ -108,6 +108,7 @@ _SIGS = {
     "ms_model_set_dynamic_k": (C.c_int, [_vp, _i, _i, _i, _i]),
     "ms_model_set_router_stats": (C.c_int, [_vp, _i]),
     "ms_model_router_stats": (C.c_int, [_vp, _fp, _ip]),
+    "ms_model_router_totals": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _i, C.POINTER(C.c_int)]),
     "ms_model_expert_tier_stats": (C.c_int, [_vp, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
     "ms_model_get_config": (C.c_int, [_vp, C.POINTER(ModelConfig)]),
     "ms_model_destroy": (C.c_int, [_vp]),

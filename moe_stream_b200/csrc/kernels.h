@@ -150,6 +150,16 @@ struct RouterArgs {
   float* entropy = nullptr;
   int* k_used = nullptr;
   int k_lo = 0, k_hi = 0;
+  // running totals of this layer (RoutingStatsCollector::record / EntropyProfiler::record,
+  // model/cache.rs:404-580), updated by the selecting lane once per step when cnt is set (needs raw):
+  // per expert the times routed and the sum of its routing weights, the tokens seen, and the entropy
+  // appended to a log of ent_cap entries with stride ent_stride
+  unsigned long long* cnt = nullptr;   // [E]
+  double* wsum = nullptr;              // [E]
+  unsigned long long* tokens = nullptr;
+  float* ent_log = nullptr;
+  uint32_t* ent_n = nullptr;
+  int ent_cap = 0, ent_stride = 1;
 };
 cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s);
 

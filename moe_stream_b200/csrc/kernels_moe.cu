@@ -984,6 +984,7 @@ __device__ __forceinline__ void router_select_t(const RouterArgs& a, uint32_t* e
   // router entropy over the unmasked logits, and the dynamic K it selects (layer.rs:980-1011,
   // 2302-2334): exp and ln rounded from double, sums in double rounded once
   int K = a.K;
+  float ent = 0.f;
   if (a.raw) {
     float rv[kPer];
     float rmx = -INFINITY;
@@ -1007,7 +1008,7 @@ __device__ __forceinline__ void router_select_t(const RouterArgs& a, uint32_t* e
       const float p = __fdiv_rn(rv[j], s32);
       if (p > 0.f) hs += (double)__fmul_rn(p, (float)log((double)p));
     }
-    const float ent = -(float)warp_sum_d(hs);
+    ent = -(float)warp_sum_d(hs);
     if (a.k_hi > 0) {   // entropy_to_k
       const float hmax = (float)log((double)a.E);
       const float nrm = fminf(fmaxf(__fdiv_rn(ent, hmax), 0.f), 1.f);
@@ -1074,6 +1075,18 @@ __device__ __forceinline__ void router_select_t(const RouterArgs& a, uint32_t* e
   if (lane == 0) {
     for (int k = 0; k < K; ++k) { a.idx[k] = sel_i[k]; a.wts[k] = w[k]; }
     for (int k = K; k < a.K; ++k) { a.idx[k] = a.E; a.wts[k] = 0.f; }   // slots past a dynamic K: none
+    if (a.cnt) {   // running routing and entropy statistics, in step order (one thread)
+      *a.tokens += 1ull;
+      for (int k = 0; k < K; ++k) {
+        a.cnt[sel_i[k]] += 1ull;
+        a.wsum[sel_i[k]] += (double)w[k];
+      }
+      const uint32_t n = *a.ent_n;
+      if ((int)n < a.ent_cap) {
+        a.ent_log[(size_t)n * a.ent_stride] = ent;
+        *a.ent_n = n + 1u;
+      }
+    }
     *a.counter = 0u;
   }
 }
@@ -1270,6 +1283,8 @@ cudaError_t launch_moe_combine(const DevCtx& c, const PendingCombine& pc, int H,
 
 cudaError_t launch_router(const DevCtx& c, const RouterArgs& a, cudaStream_t s) {
   if (a.raw && (a.batch != 1 || (a.k_hi > 0 && (a.k_lo < 1 || a.k_lo > a.k_hi || a.k_hi > a.K))))
+    return cudaErrorInvalidValue;
+  if (a.cnt && (!a.raw || !a.wsum || !a.tokens || !a.ent_log || !a.ent_n || a.ent_stride < 1))
     return cudaErrorInvalidValue;
   if (a.K < 1 || a.K > kMaxK || a.K > a.E || a.E > kRouterMaxE || !a.counter || a.batch < 1 ||
       (a.batch > 1 && (a.xterm || a.xbt)) || (a.xbt && (a.H % 32 || !a.xfe)))

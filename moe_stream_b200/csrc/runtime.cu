@@ -321,6 +321,13 @@ struct ms_model {
   float* r_raw = nullptr;
   float* r_entropy = nullptr;
   int* r_k = nullptr;
+  // running totals while router statistics are on: per layer and expert the times routed and the
+  // sum of routing weights, tokens per layer, and the entropy log [max_seq_len][layers]
+  unsigned long long* st_cnt = nullptr;
+  double* st_wsum = nullptr;
+  unsigned long long* st_tok = nullptr;
+  float* st_log = nullptr;
+  uint32_t* st_n = nullptr;
   int sh_max = 0;                   // widest shared expert (0: none)
   struct Prefill {
     int cap = 0;                       // tokens the buffers hold
@@ -803,6 +810,11 @@ ms_status enqueue_step(ms_model* m, cudaStream_t s) {
     if (m->router_stats || m->dyn_k) {   // entropy of the routing (and dynamic K), layer.rs:980-1011
       ra.raw = m->r_raw; ra.entropy = m->r_entropy + li; ra.k_used = m->r_k + li;
       if (m->dyn_k) { ra.k_lo = Lw.dk_lo; ra.k_hi = Lw.dk_hi; }
+    }
+    if (m->router_stats) {   // running totals (RoutingStatsCollector, EntropyProfiler)
+      ra.cnt = m->st_cnt + (size_t)li * c.experts; ra.wsum = m->st_wsum + (size_t)li * c.experts;
+      ra.tokens = m->st_tok + li; ra.ent_log = m->st_log + li; ra.ent_n = m->st_n + li;
+      ra.ent_cap = c.max_seq_len; ra.ent_stride = c.layers;
     }
     if (Lw.tc && m->exact) {
       ra.xbt = m->ex_xbt;
@@ -1963,6 +1975,11 @@ ms_status ms_model_finalize(ms_model* m) {
   s = s ? s : m->alloc(&m->r_raw, (size_t)c.experts * 4);
   s = s ? s : m->alloc(&m->r_entropy, (size_t)c.layers * 4);
   s = s ? s : m->alloc(&m->r_k, (size_t)c.layers * 4);
+  s = s ? s : m->alloc(&m->st_cnt, (size_t)c.layers * c.experts * 8);
+  s = s ? s : m->alloc(&m->st_wsum, (size_t)c.layers * c.experts * 8);
+  s = s ? s : m->alloc(&m->st_tok, (size_t)c.layers * 8);
+  s = s ? s : m->alloc(&m->st_log, (size_t)c.max_seq_len * c.layers * 4);
+  s = s ? s : m->alloc(&m->st_n, (size_t)c.layers * 4);
   if (is_hybrid(c)) {   // gated attention: [Q_h, gate_h] projection, then the gate
     s = s ? s : m->alloc(&m->q_raw, (size_t)(q_rows(c) + 2 * Dkv) * 4);
     s = s ? s : m->alloc(&m->q_gate, (size_t)Dq * 4);
@@ -2687,7 +2704,39 @@ ms_status ms_model_set_router_stats(ms_model* m, int enable) {
   if (enable && m->bt) return fail(m->ctx, MS_ERR_STATE, "router statistics with an open batch");
   MS_CUDA(m->ctx, cudaStreamSynchronize(m->ctx->stream));
   m->router_stats = enable != 0;
+  if (enable) {   // the running totals start from zero
+    const ms_model_config& c = m->cfg;
+    cudaStream_t s = m->ctx->stream;
+    MS_CUDA(m->ctx, cudaMemsetAsync(m->st_cnt, 0, (size_t)c.layers * c.experts * 8, s));
+    MS_CUDA(m->ctx, cudaMemsetAsync(m->st_wsum, 0, (size_t)c.layers * c.experts * 8, s));
+    MS_CUDA(m->ctx, cudaMemsetAsync(m->st_tok, 0, (size_t)c.layers * 8, s));
+    MS_CUDA(m->ctx, cudaMemsetAsync(m->st_n, 0, (size_t)c.layers * 4, s));
+  }
   if (m->graph) { cudaGraphExecDestroy(m->graph); m->graph = nullptr; }
+  return MS_OK;
+}
+
+ms_status ms_model_router_totals(ms_model* m, uint64_t* counts, double* weight_sums, uint64_t* tokens,
+                                 float* entropy_log, int max_steps, int* n_steps) {
+  if (!m) return MS_ERR_INVALID_ARG;
+  if (!m->router_stats) return fail(m->ctx, MS_ERR_STATE, "router statistics are off");
+  const ms_model_config& c = m->cfg;
+  cudaStream_t s = m->ctx->stream;
+  const size_t le = (size_t)c.layers * c.experts;
+  if (counts) MS_CUDA(m->ctx, cudaMemcpyAsync(counts, m->st_cnt, le * 8, cudaMemcpyDeviceToHost, s));
+  if (weight_sums) MS_CUDA(m->ctx, cudaMemcpyAsync(weight_sums, m->st_wsum, le * 8, cudaMemcpyDeviceToHost, s));
+  if (tokens) MS_CUDA(m->ctx, cudaMemcpyAsync(tokens, m->st_tok, (size_t)c.layers * 8, cudaMemcpyDeviceToHost, s));
+  uint32_t n = 0;
+  MS_CUDA(m->ctx, cudaMemcpyAsync(&n, m->st_n, 4, cudaMemcpyDeviceToHost, s));
+  ms_status st = ms_sync(m->ctx);
+  if (st != MS_OK) return st;
+  const int rows = entropy_log ? std::min((int)n, std::max(max_steps, 0)) : 0;
+  if (rows > 0) {
+    MS_CUDA(m->ctx, cudaMemcpyAsync(entropy_log, m->st_log, (size_t)rows * c.layers * 4, cudaMemcpyDeviceToHost, s));
+    st = ms_sync(m->ctx);
+    if (st != MS_OK) return st;
+  }
+  if (n_steps) *n_steps = (int)n;
   return MS_OK;
 }
 

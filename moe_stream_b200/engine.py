@@ -257,6 +257,45 @@ class Engine:
                                           k.ctypes.data_as(C.POINTER(C.c_int32))), self.ctx.h)
         return ent, k
 
+    def router_totals(self, max_steps: int = 4096) -> dict:
+        """Running routing statistics since set_router_stats(True), with the reference's summaries
+        (RoutingStatsCollector::summary and EntropyProfiler::summary, model/cache.rs:404-580):
+        counts / weight_sums [layers, experts], tokens [layers], entropy_log [steps, layers],
+        frequency, mean_gate_weight, importance [layers, experts] (f64) and per-layer entropy
+        mean / std / min / max (f32, as the reference accumulates them)."""
+        c = self.config
+        counts = np.zeros((c.layers, c.experts), np.uint64)
+        wsum = np.zeros((c.layers, c.experts), np.float64)
+        tokens = np.zeros(c.layers, np.uint64)
+        log = np.zeros((max_steps, c.layers), np.float32)
+        n = C.c_int()
+        check(lib().ms_model_router_totals(self.h, counts.ctypes.data, wsum.ctypes.data, tokens.ctypes.data,
+                                           log.ctypes.data, max_steps, C.byref(n)), self.ctx.h)
+        log = log[:min(n.value, max_steps)]
+        freq = np.where(tokens[:, None] > 0, counts / np.maximum(tokens[:, None], 1).astype(np.float64), 0.0)
+        mean_w = np.where(counts > 0, wsum / np.maximum(counts, 1).astype(np.float64), 0.0)
+        ent = {"mean": [], "std": [], "min": [], "max": []}
+        for li in range(c.layers):
+            v = log[:, li]
+            if v.size == 0:
+                for key in ent:
+                    ent[key].append(0.0)
+                continue
+            nf = np.float32(v.size)
+            mean = np.float32(0.0)
+            for x in v:   # f32 running sums, as the reference's iterator sums
+                mean = np.float32(mean + x)
+            mean = np.float32(mean / nf)
+            var = np.float32(0.0)
+            for x in v:
+                var = np.float32(var + np.float32(np.float32(x - mean) ** 2))
+            ent["mean"].append(float(mean))
+            ent["std"].append(float(np.sqrt(np.float32(var / nf))))
+            ent["min"].append(float(v.min()))
+            ent["max"].append(float(v.max()))
+        return dict(counts=counts, weight_sums=wsum, tokens=tokens, entropy_log=log, frequency=freq,
+                    mean_gate_weight=mean_w, importance=freq * mean_w, entropy=ent, steps=n.value)
+
     def expert_tier_stats(self):
         """(hits, misses) of the host-tier expert slots"""
         hits, misses = C.c_uint64(), C.c_uint64()

@@ -92,3 +92,35 @@ def test_router_stats_without_dynamic_k(ctx, orc, model_path):
     assert np.abs(ent - w_ent).max() <= 1e-6 * max(1.0, float(np.abs(w_ent).max()))
     eng.close()
     om.close()
+
+
+def test_router_totals_accumulate_on_device(ctx, model_path):
+    """RoutingStatsCollector / EntropyProfiler totals kept by the router on the device equal the
+    per-step routing and entropy read back after every step; re-enabling starts from zero"""
+    from moe_stream_b200.engine import Engine
+    L, E, K = SPEC.layers, SPEC.experts, SPEC.top_k
+    eng = Engine.open(model_path, max_seq_len=64, ctx=ctx)
+    eng.set_dynamic_k(True, 1, K)
+    eng.set_router_stats(True)
+    cnt = np.zeros((L, E), np.uint64)
+    wsum = np.zeros((L, E), np.float64)
+    ents = []
+    tokens = list(synth.prompt_ids(SPEC, 12, seed=4))
+    for t in tokens:
+        eng.forward([t])
+        e, k = eng.router_stats()
+        ents.append(e)
+        for li in range(L):
+            gi, gw = eng.last_routing(li)
+            for j in range(int(k[li])):
+                cnt[li, gi[j]] += 1
+                wsum[li, gi[j]] += float(gw[j])
+    tot = eng.router_totals()
+    assert tot["steps"] == len(tokens) and (tot["tokens"] == len(tokens)).all()
+    assert np.array_equal(tot["counts"], cnt)
+    assert np.array_equal(tot["weight_sums"], wsum)   # f64 sums in the same (step) order
+    assert np.array_equal(tot["entropy_log"], np.stack(ents))
+    assert np.allclose(tot["importance"], cnt / len(tokens) * np.where(cnt > 0, wsum / np.maximum(cnt, 1), 0))
+    eng.set_router_stats(True)
+    assert eng.router_totals()["steps"] == 0
+    eng.close()
