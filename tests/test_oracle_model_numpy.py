@@ -1,6 +1,7 @@
 """One token through the oracle's GPT-OSS-shaped model (the benchmark's architecture: sinks, sliding
 window on even layers, biases, softmax over the selected top-k, OAI SwiGLU, f16 embedding and LM
-head) against a float64 numpy composition of the reference's steps (engine.rs:1869-2006,
+head) and its Qwen3-shaped model (QK-norm, softmax over all experts then renormalised top-k, SiLU,
+Q4_K / Q6_K experts) against a float64 numpy composition of the reference's steps (engine.rs:1869-2006,
 layer.rs:393-503), per layer within 1e-4.  The oracle runs its projections in exact-f32 mode here, so
 the comparison measures the model wiring rather than Q8_0 activation rounding."""
 import numpy as np
@@ -12,8 +13,12 @@ from .moe_ref import moe_with_routing
 from .test_oracle_attention import _attn_np
 
 
-def test_gpt_oss_model_one_token_matches_numpy(orc, tmp_path):
-    spec = synth.TINY_GPT_OSS
+import pytest
+
+
+@pytest.mark.parametrize("spec", [synth.TINY_GPT_OSS, synth.TINY_QWEN3], ids=["gpt-oss", "qwen3"])
+def test_model_one_token_matches_numpy(orc, tmp_path, spec):
+    oai = spec.arch == "gpt-oss"
     m = synth.build_model(spec, seed=13)
     path = str(tmp_path / "g.gguf")
     G.write_gguf(path, m)
@@ -28,29 +33,34 @@ def test_gpt_oss_model_one_token_matches_numpy(orc, tmp_path):
     h = T["token_embd.weight"].data.reshape(spec.vocab, H)[token].astype(np.float64)
     for li in range(spec.layers):
         p = f"blk.{li}."
-        f32 = lambda n: T[p + n].data.astype(np.float32)
+        f32 = lambda n: T[p + n].data.astype(np.float32) if p + n in T else None
         d = dict(hidden=H, heads=spec.heads, kv_heads=spec.kv_heads, head_dim=spec.head_dim, rot_dim=spec.head_dim,
                  eps=spec.eps, rope_theta=spec.rope_theta, window=spec.sliding_window if li % 2 == 0 else 0,
                  attn_norm=f32("attn_norm.weight"), wq=T[p + "attn_q.weight"].raw(), wk=T[p + "attn_k.weight"].raw(),
                  wv=T[p + "attn_v.weight"].raw(), wo=T[p + "attn_output.weight"].raw(), bq=f32("attn_q.bias"),
                  bk=f32("attn_k.bias"), bv=f32("attn_v.bias"), bo=f32("attn_output.bias"),
-                 sinks=f32("attn_sinks.weight"))
+                 sinks=f32("attn_sinks.weight"), q_norm=f32("attn_q_norm.weight"), k_norm=f32("attn_k_norm.weight"))
         h = _attn_np(orc, d, h, [], [], 0)
-        x = h / np.sqrt((h * h).mean() + spec.eps) * f32("post_attention_norm.weight")
-        logits = f32("ffn_gate_inp.weight").reshape(E, H).astype(np.float64) @ x + f32("ffn_gate_inp.bias")
+        x = h / np.sqrt((h * h).mean() + spec.eps) * f32("post_attention_norm.weight" if oai else "ffn_norm.weight")
+        logits = f32("ffn_gate_inp.weight").reshape(E, H).astype(np.float64) @ x
+        if f32("ffn_gate_inp.bias") is not None:
+            logits = logits + f32("ffn_gate_inp.bias")
         assert np.abs(o_lg[li] - logits).max() / np.abs(logits).max() < 1e-5
-        order = np.argsort(-logits, kind="stable")[:K]   # top-k by raw logits, then softmax over them
         srt = np.sort(logits)[::-1]
         assert srt[K - 1] - srt[K] > 1e-5, "seed has a near-tie at the top-k boundary"
+        order = np.argsort(-logits, kind="stable")[:K]
         assert order.tolist() == o_idx[li].tolist()
-        w = np.exp(logits[order] - logits[order].max())
+        if oai:   # softmax over the selected logits (layer.rs:2361-2372)
+            w = np.exp(logits[order] - logits[order].max())
+        else:     # softmax over all, then renormalised over the selected (layer.rs:2374-2394)
+            w = np.exp(logits - logits.max())[order]
         w /= w.sum()
         np.testing.assert_allclose(o_w[li], w, rtol=1e-5)
         L = dict(hidden=H, inter=spec.inter, n_experts=E, top_k=K, gate_q=spec.expert_gate_q, up_q=spec.expert_gate_q,
                  down_q=spec.expert_down_q, gate=T[p + "ffn_gate_exps.weight"].raw(),
                  up=T[p + "ffn_up_exps.weight"].raw(), down=T[p + "ffn_down_exps.weight"].raw(),
                  gate_bias=f32("ffn_gate_exps.bias"), up_bias=f32("ffn_up_exps.bias"),
-                 down_bias=f32("ffn_down_exps.bias"), oai_swiglu=1)
+                 down_bias=f32("ffn_down_exps.bias"), oai_swiglu=int(oai))
         h = h + moe_with_routing(orc, L, x, order, w)
         assert np.abs(o_hid[li] - h).max() / np.abs(h).max() < 1e-4, f"layer {li}"
     xf = h / np.sqrt((h * h).mean() + spec.eps) * T["output_norm.weight"].data
