@@ -67,3 +67,25 @@ def test_model_one_token_matches_numpy(orc, tmp_path, spec):
     logits = T["output.weight"].data.reshape(spec.vocab, H).astype(np.float64) @ xf
     assert np.abs(o_logits - logits).max() / np.abs(logits).max() < 1e-4
     assert int(np.argmax(o_logits)) == int(np.argmax(logits))
+
+
+@pytest.mark.parametrize("spec", [synth.TINY_GPT_OSS, synth.TINY_QWEN3, synth.TINY_QWEN3_NEXT],
+                         ids=["gpt-oss", "qwen3", "qwen3-next"])
+def test_multi_token_forward_equals_token_by_token(orc, tmp_path, spec):
+    """the oracle's prompt forward (causal attention over the call's positions, layer.rs:393-503 with
+    seq_len > 1; DeltaNet token by token) gives the logits and per-layer residuals of feeding the same
+    tokens one call at a time -- the reference the batched GPU prefill is compared with"""
+    path = str(tmp_path / "m.gguf")
+    synth.write_model(path, spec, seed=17)
+    prompt = synth.prompt_ids(spec, 11, seed=17)
+    a = orc.Model(path, max_seq_len=32)
+    la = a.forward(prompt)
+    ha, _ = a.layer_trace(spec.layers, spec.experts)
+    b = orc.Model(path, max_seq_len=32)
+    for t in prompt:
+        lb = b.forward(np.array([t], np.int32))
+    hb, _ = b.layer_trace(spec.layers, spec.experts)
+    assert np.abs(la - lb).max() / np.abs(lb).max() < 1e-5
+    assert np.abs(ha - hb).max() / np.abs(hb).max() < 1e-5
+    a.close()
+    b.close()
